@@ -1,0 +1,497 @@
+"""Full-chain forward+backward throughput (Mpixels/s) of the differentiable
+rasterization chain on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg4] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+A step is one pass of the configuration's chain (rasterize -> interpolate ->
+texture -> antialias -> MSE, then every VJP) over the rank's views, plus the
+NCCL all-reduce of the shared-parameter gradients when N > 1.  Rank 0 prints
+one JSON line.  The default workload is configuration 4 of the benchmark
+(1M-triangle soup, 32 views at 1024^2, two depth-peeled layers with rast_db,
+8-channel interpolation with diffAttrs=.all, antialias with the topology hash),
+the configuration the throughput target is stated on.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mlx-swift-diffrast_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "full-chain fwd+bwd Mpixels/s"
+
+WORKLOADS = {
+    "cfg1": "tier-1 colour fit: 1 triangle, N=1, 256^2, rasterize->interpolate(RGB)->antialias->MSE, bwd d_pos/d_rgb",
+    "cfg2": "icosphere L4 (2562 v / 5120 t), 8 views 512^2, RGB+UV interpolate, bilinear clamp 512^2x3 texture, "
+            "antialias, MSE; bwd d_pos/d_attr/d_tex",
+    "cfg3": "icosphere L4, 16 views 1024^2, rast_db, UV diffAttrs=.all, trilinear 2048^2x4 wrap texture with per-pixel "
+            "mip bias, MSE; bwd d_tex(all levels)/d_uv/d_uvDA->d_pos",
+    "cfg4": "1M-triangle soup (20% in edge-sharing strips), 32 views/GPU at 1024^2, 2 depth-peeled layers with rast_db, "
+            "interpolate A=8 diffAttrs=.all, antialias+topology hash, MSE; bwd d_pos(->shared verts)/d_attr",
+    "cfg5": "geodesic sphere 499,280 tris, 256 views 2048^2 sharded over GPUs, cube 6x1024^2x3 (.linear), antialias, "
+            "MSE; bwd d_verts/d_tex",
+}
+# Configurations whose per-GPU work is fixed as N grows (each rank renders the
+# configuration's full view count); cfg5 splits its 256 views over the ranks.
+WEAK = {"cfg1", "cfg2", "cfg3", "cfg4"}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------- algorithmic bytes
+
+def algorithmic_bytes(cfg: str, chain) -> dict:
+    """Compulsory HBM bytes per step for each library kernel (each input read
+    once, each output written once; intermediates such as setup records, tile
+    lists and scan buffers count zero).  Returns {kernel: bytes per step}."""
+    import torch  # noqa: F401
+    i = chain.info
+    n = i.n_views
+    H, W = i.res
+    P = n * H * W
+    k = {}
+
+    def add(name, b):
+        k[name] = k.get(name, 0) + b
+
+    if cfg == "cfg4":
+        V, T, A = chain.base.shape[0], chain.tri.shape[0], 8
+        for layer in (0, 1):
+            add("raster_setup", n * V * 16 + T * 12)
+            add("raster_tiles", P * 16 + P * 16 + (P * 16 if layer else 0))
+            add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A))
+            # out_da never reaches the loss: the VJP runs without the DA terms.
+            add("interp_bwd", 2 * V * A * 4 + T * 12 + P * (16 + 16 + 4 * A))
+            add("raster_bwd", 2 * n * V * 16 + T * 12 + P * 32 + P * 16)
+        add("aa_fwd", P * (8 * A + 16) + n * V * 16 + 2 * T * 12)
+        add("aa_bwd", P * (12 * A + 16) + 2 * n * V * 16 + 2 * T * 12)
+        add("mse", 2 * P * 12 * A)
+    elif cfg == "cfg1":
+        V, T, C = 3, 1, 3
+        add("raster_setup", V * 16 + T * 12)
+        add("raster_tiles", P * 16)
+        add("interp_fwd", V * C * 4 + T * 12 + P * (16 + 4 * C))
+        add("interp_bwd", 2 * V * C * 4 + T * 12 + P * (32 + 4 * C))
+        add("raster_bwd", 2 * V * 16 + T * 12 + P * 32)
+        add("aa_fwd", P * (8 * C + 16) + V * 16 + 2 * T * 12)
+        add("aa_bwd", P * (12 * C + 16) + 2 * V * 16 + 2 * T * 12)
+        add("mse", P * 12 * C)
+    elif cfg == "cfg2":
+        V, T = chain.pos.shape[1], chain.tri.shape[0]
+        S = 512 * 512 * 3 * 4
+        add("raster_setup", n * V * 16 + T * 12)
+        add("raster_tiles", P * 16)
+        add("interp_fwd", V * 3 * 4 + V * 2 * 4 + 2 * T * 12 + P * (16 + 12) + P * (16 + 8))
+        add("interp_bwd", 2 * V * 5 * 4 + 2 * T * 12 + P * (32 + 12) + P * (32 + 8))
+        add("tex_linear_fwd", S + P * (8 + 12))
+        add("tex_linear_bwd", 2 * S + P * (16 + 12))
+        add("raster_bwd", 2 * n * V * 16 + T * 12 + P * 32)
+        add("aa_fwd", P * (8 * 3 + 16) + n * V * 16 + 2 * T * 12)
+        add("aa_bwd", P * (12 * 3 + 16) + 2 * n * V * 16 + 2 * T * 12)
+        add("mse", P * 12 * 3)
+    elif cfg == "cfg3":
+        V, T = chain.pos.shape[1], chain.tri.shape[0]
+        S0 = 2048 * 2048 * 4 * 4
+        S_all = S0 * 4 // 3
+        add("raster_setup", n * V * 16 + T * 12)
+        add("raster_tiles", P * 32)
+        add("interp_fwd", V * 2 * 4 + T * 12 + P * (16 + 16 + 8 + 16))
+        add("interp_bwd", 2 * V * 2 * 4 + T * 12 + P * (32 + 32 + 8 + 16))
+        add("mip_down", S0 + S0 // 3)
+        add("tex_mip_fwd", S_all + P * (8 + 16 + 4 + 16))
+        add("tex_mip_bwd", 2 * S_all + P * (16 + 32 + 4 + 16))
+        add("mip_fold", S_all + S0)
+        add("raster_bwd", 2 * n * V * 16 + T * 12 + P * 32 + P * 16)
+        add("mse", P * 12 * 4)
+    elif cfg == "cfg5":
+        V, T = chain.verts.shape[0], chain.tri.shape[0]
+        S = 6 * 1024 * 1024 * 3 * 4
+        micro = -(-n // chain.micro)
+        add("raster_setup", n * V * 16 + micro * T * 12)
+        add("raster_tiles", P * 16)
+        add("interp_fwd", micro * (V * 12 + T * 12) + P * (16 + 12))
+        add("interp_bwd", micro * (2 * V * 12 + T * 12) + P * (32 + 12))
+        add("tex_cube_fwd", micro * S + P * (12 + 12))
+        add("tex_cube_bwd", micro * 2 * S + P * (12 + 12 + 12))
+        add("raster_bwd", 2 * n * V * 16 + micro * T * 12 + P * 32)
+        add("aa_fwd", P * (8 * 3 + 16) + n * V * 16 + micro * 2 * T * 12)
+        add("aa_bwd", P * (12 * 3 + 16) + 2 * n * V * 16 + micro * 2 * T * 12)
+        add("mse", P * 12 * 3)
+    return k
+
+
+# --------------------------------------------------------- CPU baseline
+
+def cpu_chain_sample(cfg: str, nthreads: int):
+    """Build a bounded sample of the configuration for the CPU oracle chain.
+    Returns (callable, pixels, description)."""
+    import numpy as np
+
+    import oracle
+    import oracle.chains as OC
+    from diffrast import scenes
+
+    if cfg == "cfg4":
+        s = scenes.scene_cfg4(n_views=1)
+        pos = np.einsum("nij,vj->nvi", s["sim"], s["base"]).astype(np.float32)
+        g = np.random.default_rng(13)
+        H, W = s["res"]
+        t0 = g.normal(size=(1, H, W, 8)).astype(np.float32)
+        t1 = g.normal(size=(1, H, W, 8)).astype(np.float32)
+        topo = oracle.topology_hash(s["tri"])
+        f = lambda: OC.cfg4(pos, s["tri"], s["attr"], t0, t1, s["res"], topo, nthreads)  # noqa: E731
+        return f, H * W, "1 of 32 views of cfg4 at full size (1M triangles, 1024^2, 2 layers, A=8, aa)"
+    if cfg == "cfg1":
+        s = scenes.scene_cfg1()
+        topo = oracle.topology_hash(s["tri"])
+        f = lambda: OC.cfg1(s["pos"], s["tri"], s["attr"], s["target"], s["res"], topo, nthreads)  # noqa: E731
+        return f, 256 * 256, "full cfg1 step"
+    if cfg == "cfg2":
+        s = scenes.scene_cfg2()
+        topo = oracle.topology_hash(s["tri"])
+        f = lambda: OC.cfg2(s["pos"][:2], s["tri"], s["rgb"], s["uv"], s["tex"], s["target"][:2], s["res"], topo,  # noqa: E731
+                            nthreads)
+        return f, 2 * 512 * 512, "2 of 8 views of cfg2"
+    if cfg == "cfg3":
+        s = scenes.scene_cfg3()
+        f = lambda: OC.cfg3(s["pos"][:1], s["tri"], s["uv"], s["tex"], s["bias_map"][:1], s["target"][:1],  # noqa: E731
+                            s["res"], nthreads)
+        return f, 1024 * 1024, "1 of 16 views of cfg3"
+    s = scenes.scene_cfg5(n_views=1)
+    pos = scenes.clip_positions(s["verts"], s["mvps"][:1])
+    g = np.random.default_rng(16)
+    tgt = g.random((1,) + s["res"] + (3,)).astype(np.float32)
+    topo = oracle.topology_hash(s["tri"])
+    f = lambda: OC.cfg5(pos, s["tri"], s["unit"], s["cube"], tgt, s["res"], topo, nthreads)  # noqa: E731
+    return f, s["res"][0] * s["res"][1], "1 of 256 views of cfg5"
+
+
+def time_cpu(cfg: str, reps: int = 2):
+    nthreads = os.cpu_count() or 1
+    f, pixels, desc = cpu_chain_sample(cfg, nthreads)
+    f()  # warm-up (oracle scratch pool, page faults)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        f()
+        ts.append(time.perf_counter() - t0)
+    dt = statistics.median(ts)
+    return {"value": pixels / dt / 1e6, "unit": "Mpx/s", "cores": nthreads, "kind": "port",
+            "sample": f"{desc}; median of {reps} runs after 1 warm-up, {dt:.2f} s each"}
+
+
+# ------------------------------------------------------------------ main
+
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1 and not dist.is_initialized():
+        import datetime
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    return ws, rank, local
+
+
+def run_reference(args, ws, rank):
+    """The reference's path on the host: the oracle's restatement of the
+    reference kernels (the reference itself is Swift + Metal and cannot run on
+    this machine), with every host thread, each step a bounded sample."""
+    if rank != 0:
+        return
+    nthreads = os.cpu_count() or 1
+    f, pixels, desc = cpu_chain_sample(args.config, nthreads)
+    for _ in range(args.warmup):
+        f()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        f()
+    dt = (time.perf_counter() - t0) / args.steps
+    v = pixels / dt / 1e6
+    line = {"metric": METRIC, "value": v, "unit": "Mpx/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak" if args.config in WEAK else "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded PCG64 scenes)", "impl": "reference",
+            "config": {"workload": f"{args.config}: {WORKLOADS[args.config]}", "sample_per_step": desc},
+            "cpu_baseline": {"value": v, "unit": "Mpx/s", "cores": nthreads, "kind": "port",
+                             "sample": desc + " per step; CPU oracle restatement of the reference kernels"},
+            "e2e": {"value": v, "unit": "Mpx/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="cfg4", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--views", type=int, default=0, help="override views per GPU (profiling runs)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+
+    ws, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import diffrast
+    from diffrast import _lib, chains
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = args.config
+    total = chains.TOTAL_VIEWS[cfg]
+    if cfg in WEAK:
+        per = args.views or total
+        lo, hi, tot = rank * per, (rank + 1) * per, per * ws
+    else:
+        per = args.views or total // ws
+        lo, hi, tot = rank * per, (rank + 1) * per, per * ws
+    kw = {}
+    if cfg == "cfg4":
+        kw = dict(view_lo=lo, view_hi=hi, total_views=tot)
+    elif cfg == "cfg1":
+        kw = {}
+    else:
+        kw = dict(view_lo=lo, view_hi=hi)
+    chain = chains.CHAINS[cfg](dev, **kw)
+    torch.cuda.synchronize()
+
+    flat_buf = {}
+
+    def allreduce():
+        if ws == 1:
+            return
+        gs = chain.shared_grads()
+        flat = torch._utils._flatten_dense_tensors(gs)
+        dist.all_reduce(flat)
+        for g, f in zip(gs, torch._utils._unflatten_dense_tensors(flat, gs)):
+            g.copy_(f)
+
+    def one_step():
+        chain.zero_grad()
+        loss = chain.step()
+        allreduce()
+        return loss
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    diffrast.sync(local)
+    if ws > 1:
+        dist.barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.4)
+    _lib.set_timing(True, local)
+    launches0 = diffrast.launch_count(local)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        loss = one_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = diffrast.launch_count(local) - launches0
+    report = _lib.timing_report(local)
+    _lib.set_timing(False, local)
+    clk = clocks.stop()
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    diffrast.sync(local)
+
+    pixels_all = chain.info.pixels * ws
+    value = pixels_all / (ms_max * 1e-3) / 1e6
+
+    peak, peak_kind = load_peaks()
+    algo = algorithmic_bytes(cfg, chain)
+    kernels = {}
+    for name, (cnt, tot_ms) in sorted(report.items(), key=lambda kv: -kv[1][1]):
+        b = algo.get(name, 0) * args.steps
+        ach = b / (tot_ms * 1e-3) / 1e9 if (b and tot_ms > 0) else None
+        kernels[name] = {"launches": cnt, "ms_per_launch": tot_ms / cnt, "share": tot_ms / (ms * args.steps),
+                         "algo_bytes_per_launch": (b / cnt) if b else 0,
+                         "gbs": ach, "frac": (ach / peak) if ach else None}
+    dom = next((n for n in kernels if kernels[n]["gbs"]), None)
+    roof = None
+    if dom:
+        kd = kernels[dom]
+        roof = {"kernel": dom, "bound": "hbm", "achieved": kd["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": kd["frac"], "peak_source": f"{peak_kind} hbm_gbs", "traffic": None}
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(chain, cfg, args, ws, dev, allreduce)
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        try:
+            cpu = time_cpu(cfg)
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"error": str(ex)[:200]}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "Mpx/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+                "scaling": "weak" if cfg in WEAK else "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded PCG64 scenes, seeded torch targets)",
+                "config": {"workload": f"{cfg}: {WORKLOADS[cfg]}", "views_per_gpu": chain.info.n_views,
+                           "resolution": list(chain.info.res), "pixels_per_step": pixels_all,
+                           "parallelism": f"dp{ws} (views sharded, grads all-reduced)" if ws > 1 else "single GPU",
+                           "l2": "inputs larger than L2 (per-step tensors are GBs; no flush needed)"},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+                "gpu_launches_per_step": launches / args.steps, "clocks": clk, "kernels": kernels,
+                "loss": float(loss)}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(chain, cfg, args, ws, dev, allreduce):
+    """Same step through the public API with host inputs: every step copies its
+    per-view inputs (targets and view transforms) from pinned host memory and
+    reads the loss back, inside the timed region."""
+    import torch
+
+    ins = [t for t in chain_inputs(chain, cfg) if t is not None]
+    host = [t.detach().cpu().pin_memory() for t in ins]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    out = torch.empty((), dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(2):
+        for d, h in zip(ins, host):
+            d.copy_(h, non_blocking=True)
+        chain.zero_grad()
+        loss = chain.step()
+        allreduce()
+        out.copy_(loss.detach(), non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        for d, h in zip(ins, host):
+            d.copy_(h, non_blocking=True)
+        chain.zero_grad()
+        loss = chain.step()
+        allreduce()
+        out.copy_(loss.detach(), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": chain.info.pixels * ws / (ms * 1e-3) / 1e6, "unit": "Mpx/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+            "inputs": "per-step targets and view transforms from pinned host memory; loss read back"}
+
+
+def chain_inputs(chain, cfg):
+    if cfg == "cfg4":
+        return [chain.tgt0, chain.tgt1, chain.sim]
+    if cfg == "cfg5":
+        return [chain.target, chain.mvp]
+    if cfg == "cfg3":
+        return [chain.target, chain.bias]
+    return [chain.target]
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,251 @@
+/*
+ * diffrast.h — C ABI of the B200-native differentiable rasterization chain.
+ *
+ * This is the drop-in boundary under the Swift `DiffRast.*` operator surface of
+ * mlx-swift-diffrast (Sources/MLXDiffRast/*.swift).  Every forward op is paired
+ * with an explicit VJP ("_bwd") entry point; the Swift wrapper (or any other
+ * host language) owns autograd and calls these two halves.
+ *
+ * Conventions (identical to the reference):
+ *   - Layouts are NHWC, fp32; indices are int32.
+ *   - pos is clip space (x*w, y*w, z*w, w).
+ *   - Pixel (h=0, w=0) is the top-left pixel; NDC +y is up.
+ *   - rast channels are (u, v, z/w, tri_id+1) with u = w1, v = w2 (the
+ *     barycentric weights of vertices 1 and 2; w0 = 1-u-v).
+ *   - rast_db channels are (du/dx, du/dy, dv/dx, dv/dy) in pixel units.
+ *
+ * Memory: every tensor pointer is a DEVICE pointer on the context's device,
+ * except `diff_idx`, which is a host array (it is a Swift [Int32] in the
+ * reference).  Outputs are caller-allocated and fully overwritten; gradient
+ * accumulators are zeroed by the callee.  All calls are asynchronous on the
+ * context's stream and return a status; device-side index errors (a triangle
+ * that names a vertex >= V, a rast tri_id > T) are skipped by the kernels and
+ * reported by the next dr_ctx_sync().
+ *
+ * Threading: a context is not re-entrant; use one context per host thread /
+ * stream.  Contexts on different devices are independent.
+ */
+#ifndef DIFFRAST_H
+#define DIFFRAST_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DR_API __attribute__((visibility("default")))
+#else
+#define DR_API
+#endif
+
+#define DR_ABI_VERSION 1
+#define DR_MAX_MIP_LEVELS 32
+#define DR_MAX_DIFF_ATTRS 1024
+
+typedef enum dr_status {
+  DR_OK = 0,
+  DR_EINVAL = 1,     /* bad shape / argument (reference: `precondition` failure) */
+  DR_ENOMEM = 2,     /* workspace allocation failed */
+  DR_ECUDA = 3,      /* CUDA runtime error (launch or earlier asynchronous fault) */
+  DR_EOVERFLOW = 4,  /* a fixed capacity was exceeded (no-drop guarantee) */
+  DR_EDEVICE = 5     /* a kernel saw out-of-range indices in its inputs */
+} dr_status;
+
+/* Texture filter modes: DiffRast.FilterMode (Texture.swift:35-40). */
+typedef enum dr_filter {
+  DR_FILTER_NEAREST = 0,
+  DR_FILTER_LINEAR = 1,
+  DR_FILTER_LINEAR_MIPMAP_NEAREST = 2,
+  DR_FILTER_LINEAR_MIPMAP_LINEAR = 3
+} dr_filter;
+
+/* Boundary modes: DiffRast.BoundaryMode raw values (Texture.swift:8-17). */
+typedef enum dr_boundary {
+  DR_BOUNDARY_WRAP = 0,
+  DR_BOUNDARY_CLAMP = 1,
+  DR_BOUNDARY_ZERO = 2,
+  DR_BOUNDARY_CUBE = 3
+} dr_boundary;
+
+typedef struct dr_ctx dr_ctx;
+
+/* ---- context ----------------------------------------------------------- */
+
+DR_API int dr_abi_version(void);
+
+/* Create a context on `device`.  It owns a grow-only device workspace
+ * (setup records, tile bins, mip pyramids, hash tables) and uses the legacy
+ * default stream until dr_ctx_set_stream() is called. */
+DR_API dr_status dr_ctx_create(int device, dr_ctx** out);
+DR_API void dr_ctx_destroy(dr_ctx* ctx);
+/* `stream` is a cudaStream_t. */
+DR_API dr_status dr_ctx_set_stream(dr_ctx* ctx, void* stream);
+DR_API void* dr_ctx_get_stream(const dr_ctx* ctx);
+/* Message describing the last non-OK status on this context. */
+DR_API const char* dr_last_error(const dr_ctx* ctx);
+/* Synchronize the context's stream and report DR_EDEVICE if any kernel since
+ * the previous sync saw out-of-range indices (the flag is then cleared). */
+DR_API dr_status dr_ctx_sync(dr_ctx* ctx);
+/* Number of kernels this context has launched (for launch accounting). */
+DR_API uint64_t dr_ctx_launch_count(const dr_ctx* ctx);
+DR_API size_t dr_ctx_workspace_bytes(const dr_ctx* ctx);
+/* Instrumentation (no counterpart in the reference, which has no tracing):
+ * when enabled, every kernel launch is bracketed by CUDA events on the
+ * context's stream.  Enabling (or disabling) clears the records.  The report
+ * synchronizes the stream and writes one line per kernel name,
+ * "<name> <launches> <total_ms>\n", into buf. */
+DR_API dr_status dr_ctx_set_timing(dr_ctx* ctx, int enable);
+DR_API dr_status dr_ctx_timing_report(dr_ctx* ctx, char* buf, size_t n);
+
+/* ---- rasterize (Rasterize.swift:44-144) -------------------------------- */
+
+/* Forward.  Replaces DiffRast.rasterize (Rasterize.swift:44) and its kernels
+ * diffrast_rasterize_precompute/_bin/_fwd/_fwd_db (Rasterize.swift:280-609).
+ *   Instanced mode: ranges == NULL, pos is [N, V, 4].
+ *   Range mode:     ranges is [N, 2] int32 (start, count), pos is [V, 4].
+ *   peel_layer: NULL, or a previous rast [N, H, W, 4] to peel through.
+ *   rast: [N, H, W, 4] out.  rast_db: [N, H, W, 4] out, or NULL (gradDB=false).
+ * Unlike the reference (MAX_PER_TILE=128, overflow dropped) no triangle is ever
+ * dropped, and depth ties resolve to the lowest triangle index. */
+DR_API dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V,
+                           const int32_t* tri, int T, const int32_t* ranges,
+                           int N, int H, int W, const float* peel_layer,
+                           float* rast, float* rast_db);
+
+/* VJP.  Replaces the rasterize VJP closures (Rasterize.swift:109-117,
+ * 129-138) and diffrast_rasterize_bwd (Rasterize.swift:637-812).
+ *   d_rast: [N, H, W, 4] (channel 3 ignored); d_rast_db: [N, H, W, 4] or NULL.
+ *   d_pos: out, [N, V, 4] instanced or [V, 4] in range mode (summed over the
+ *   batch, as MLX's broadcast-backward does). */
+DR_API dr_status dr_rasterize_bwd(dr_ctx* ctx, const float* pos, int V,
+                           const int32_t* tri, int T, const int32_t* ranges,
+                           int N, int H, int W, const float* rast,
+                           const float* d_rast, const float* d_rast_db,
+                           float* d_pos);
+
+/* ---- interpolate (Interpolate.swift:43-132) ---------------------------- */
+
+/* Forward.  Replaces DiffRast.interpolate and diffrast_interp_fwd/_fwd_da
+ * (Interpolate.swift:137-228).
+ *   attr: [attr_batch, V, A] with attr_batch == 1 (broadcast; also the
+ *         reference's [V, A] range-mode form) or attr_batch == N.
+ *   rast: [N, H, W, 4]; tri: [T, 3].
+ *   K == 0: no pixel derivatives (diffAttrs == nil); rast_db/out_da ignored.
+ *   K  > 0: rast_db [N, H, W, 4]; diff_idx = HOST array of K attribute
+ *           indices (.indices), or NULL with K == A (.all);
+ *           out_da: [N, H, W, 2K].
+ *   out: [N, H, W, A]. */
+DR_API dr_status dr_interpolate_fwd(dr_ctx* ctx, const float* attr, int attr_batch,
+                             int V, int A, const float* rast, int N, int H,
+                             int W, const int32_t* tri, int T,
+                             const float* rast_db, const int32_t* diff_idx,
+                             int K, float* out, float* out_da);
+
+/* VJP.  Replaces diffrast_interp_grad_attr/_grad_attr_da/_grad_rast/
+ * _grad_rast_db (Interpolate.swift:231-417, 502-541).
+ *   d_attr: out, [attr_batch, V, A] (summed over the batch when attr_batch==1).
+ *   d_rast: out, [N, H, W, 4] (channels 2, 3 are zero).
+ *   d_rast_db: out, [N, H, W, 4] when K > 0, else ignored. */
+DR_API dr_status dr_interpolate_bwd(dr_ctx* ctx, const float* attr, int attr_batch,
+                             int V, int A, const float* rast, int N, int H,
+                             int W, const int32_t* tri, int T,
+                             const float* rast_db, const int32_t* diff_idx,
+                             int K, const float* d_out, const float* d_out_da,
+                             float* d_attr, float* d_rast, float* d_rast_db);
+
+/* ---- texture (Texture.swift:62-1313) ----------------------------------- */
+
+/* Host-only: the mip pyramid layout textureConstructMip (Texture.swift:144-161)
+ * produces for a [Nt, Ht, Wt, C] texture.  Level 0 is the texture itself; the
+ * pyramid buffer holds levels 1..num_levels-1 back to back, level k as
+ * [Nt, level_h[k], level_w[k], C] starting at float offset level_offset[k]
+ * (level_offset[0] = -1).  max_level < 0 means "no limit". */
+DR_API dr_status dr_texture_mip_layout(int Nt, int Ht, int Wt, int C, int max_level,
+                                int* num_levels, int64_t* level_offset,
+                                int* level_h, int* level_w,
+                                int64_t* pyramid_floats);
+
+/* textureConstructMip (Texture.swift:144-161): 2x2 box-filter levels 1.. into
+ * `pyramid` (size from dr_texture_mip_layout). */
+DR_API dr_status dr_texture_construct_mip(dr_ctx* ctx, const float* tex, int Nt,
+                                   int Ht, int Wt, int C, int max_level,
+                                   float* pyramid);
+
+/* Forward.  Replaces DiffRast.texture (Texture.swift:62-131) and kernels
+ * diffrast_texture_fwd / _nearest_fwd / _cube_fwd / _trilinear_fwd.
+ *   tex: [Nt, Ht, Wt, C] (Nt == 1 broadcasts) or, for DR_BOUNDARY_CUBE,
+ *        [Nt, 6, Ht, Wt, C] (cube requires DR_FILTER_LINEAR, as the reference).
+ *   pyramid: mip levels >= 1 from dr_texture_construct_mip, or NULL to build
+ *        them internally (mipmap filters only).  max_level as in the layout.
+ *   uv: [N, Hi, Wi, 2] ([N, Hi, Wi, 3] direction for cube).
+ *   uv_da: [N, Hi, Wi, 4], required for the mipmap filters.
+ *   mip_level_bias / mip_level_bias_map ([N, Hi, Wi] or NULL): scale uv_da by
+ *        2^bias * 2^map before the LOD, as Texture.swift:104-126.
+ *   out: [N, Hi, Wi, C]. */
+DR_API dr_status dr_texture_fwd(dr_ctx* ctx, int filter, int boundary,
+                         const float* tex, int Nt, int Ht, int Wt, int C,
+                         const float* pyramid, int max_level, const float* uv,
+                         const float* uv_da, float mip_level_bias,
+                         const float* mip_level_bias_map, int N, int Hi,
+                         int Wi, float* out);
+
+/* VJP.  Replaces the texture VJP closures and kernels _grad_tex, _grad_uv,
+ * _nearest_grad_tex, _cube_grad_tex, _trilinear_grad_pyramid/_grad_uv/
+ * _grad_uvda (Texture.swift:405-521, 574-605, 686-738, 865-1102), plus the
+ * MLX autograd of the pyramid build (folded into level 0 here).
+ *   d_tex: out, same shape as tex (pyramid gradients folded in).
+ *   d_uv: out, shape of uv (zero for nearest; zero d_dir for cube, as
+ *         Texture.swift:196-197).
+ *   d_uv_da: out [N, Hi, Wi, 4] for mipmap filters, or NULL.
+ *   d_bias_map: out [N, Hi, Wi] gradient of the bias map, or NULL. */
+DR_API dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary,
+                         const float* tex, int Nt, int Ht, int Wt, int C,
+                         const float* pyramid, int max_level, const float* uv,
+                         const float* uv_da, float mip_level_bias,
+                         const float* mip_level_bias_map, int N, int Hi,
+                         int Wi, const float* d_out, float* d_tex,
+                         float* d_uv, float* d_uv_da, float* d_bias_map);
+
+/* ---- antialias (Antialias.swift:19-601) -------------------------------- */
+
+/* antialiasConstructTopologyHash (Antialias.swift:19-66), on the GPU.
+ *   tri: [T, 3]; topo: out [T, 3] (neighbour tri, -1 boundary, -2 non-manifold).
+ * Bit-identical to the reference's sort-based construction. */
+DR_API dr_status dr_antialias_construct_topology_hash(dr_ctx* ctx,
+                                               const int32_t* tri, int T,
+                                               int32_t* topo);
+
+/* Forward.  Replaces DiffRast.antialias (Antialias.swift:90-131) and
+ * diffrast_antialias_fwd (Antialias.swift:333-358).
+ *   color: [N, H, W, C]; rast: [N, H, W, 4]; pos: [N, V, 4] (instanced, as the
+ *   reference requires); tri: [T, 3]; topo: [T, 3]; out: [N, H, W, C]. */
+DR_API dr_status dr_antialias_fwd(dr_ctx* ctx, const float* color, int N, int H,
+                           int W, int C, const float* rast, const float* pos,
+                           int V, const int32_t* tri, int T,
+                           const int32_t* topo, float* out);
+
+/* VJP.  Replaces diffrast_antialias_bwd_color / _bwd_pos
+ * (Antialias.swift:388-524).  d_color: out [N, H, W, C]; d_pos: out [N, V, 4]. */
+DR_API dr_status dr_antialias_bwd(dr_ctx* ctx, const float* color, int N, int H,
+                           int W, int C, const float* rast, const float* pos,
+                           int V, const int32_t* tri, int T,
+                           const int32_t* topo, const float* d_out,
+                           float* d_color, float* d_pos);
+
+/* ---- loss helper (the MSE of the reference's examples) ------------------ */
+
+/* loss += scale * sum((pred - target)^2) into the device scalar `loss`
+ * (zeroed by the callee when zero_loss != 0) and
+ * d_pred = 2 * scale * (pred - target).  n elements. */
+DR_API dr_status dr_mse_fwd_bwd(dr_ctx* ctx, const float* pred, const float* target,
+                         int64_t n, float scale, float* d_pred, float* loss,
+                         int zero_loss);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIFFRAST_H */

@@ -1,0 +1,408 @@
+// antialias.cu — topology hash on the GPU, silhouette antialiasing forward and
+// backward.
+//
+// Reference: Sources/MLXDiffRast/Antialias.swift.
+//   antialiasConstructTopologyHash (19-66) runs on the CPU in the reference
+//   (device->host copy, sort of 3T edges, run classification).  Here it is an
+//   open-addressing hash table on the GPU: every edge (min, max) is inserted
+//   with a 64-bit CAS; the slot counts its users and keeps the first two
+//   (triangle, edge) references.  A second pass classifies each reference:
+//   count 1 -> -1 (boundary), 2 -> the other triangle, >= 3 -> -2
+//   (non-manifold).  The classification is order independent, so the table is
+//   bit-identical to the reference's sort-based result.
+//
+//   silhouetteBlock (168-326) is evaluated per (pixel, direction) by sil_dir().
+//   Forward = diffrast_antialias_fwd (333-358).  Backward fuses _bwd_color
+//   (498-524) and _bwd_pos (388-496): d_color is computed in gather form — each
+//   pixel adds its own g*(1 - sum beta) and the beta*g its four neighbours
+//   would have scattered toward it — so it needs no atomics and is
+//   deterministic; only d_pos uses (float) atomics.
+#include "common.cuh"
+
+namespace {
+
+constexpr unsigned long long EMPTY_KEY = 0xFFFFFFFF00000000ull;  // lo > hi: never a real edge
+
+__device__ __forceinline__ unsigned long long edge_key(int a, int b) {
+  const int lo = min(a, b), hi = max(a, b);
+  return ((unsigned long long)((unsigned)lo ^ 0x80000000u) << 32) | (unsigned)((unsigned)hi ^ 0x80000000u);
+}
+
+__device__ __forceinline__ uint32_t hash64(unsigned long long k) {
+  k ^= k >> 33;
+  k *= 0xff51afd7ed558ccdull;
+  k ^= k >> 33;
+  k *= 0xc4ceb9fe1a85ec53ull;
+  k ^= k >> 33;
+  return (uint32_t)k;
+}
+
+// Edge k of triangle t joins vertices (k+1)%3 and (k+2)%3 (Antialias.swift:33).
+__global__ void k_topo_insert(const int32_t* __restrict__ tri, int T, unsigned long long* __restrict__ keys,
+                              uint32_t* __restrict__ cnt, int32_t* __restrict__ ref_a,
+                              int32_t* __restrict__ ref_b, uint32_t* __restrict__ ref_slot, uint32_t mask,
+                              unsigned* err) {
+  const int64_t ref = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (ref >= (int64_t)T * 3) return;
+  const int t = (int)(ref / 3), k = (int)(ref % 3);
+  const int va = __ldg(tri + 3 * t + (k + 1) % 3), vb = __ldg(tri + 3 * t + (k + 2) % 3);
+  const unsigned long long key = edge_key(va, vb);
+  uint32_t slot = hash64(key) & mask;
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    const unsigned long long prev = atomicCAS(keys + slot, EMPTY_KEY, key);
+    if (prev == EMPTY_KEY || prev == key) {
+      const uint32_t c = atomicAdd(cnt + slot, 1u);
+      if (c == 0) ref_a[slot] = (int32_t)ref;
+      else if (c == 1) ref_b[slot] = (int32_t)ref;
+      ref_slot[ref] = slot;
+      return;
+    }
+    slot = (slot + 1) & mask;
+  }
+  dr_flag(err, DR_DEVERR_CAPACITY);  // unreachable at load factor <= 1/2
+  ref_slot[ref] = 0xFFFFFFFFu;
+}
+
+__global__ void k_topo_classify(int T, const uint32_t* __restrict__ cnt, const int32_t* __restrict__ ref_a,
+                                const int32_t* __restrict__ ref_b, const uint32_t* __restrict__ ref_slot,
+                                int32_t* __restrict__ topo) {
+  const int64_t ref = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (ref >= (int64_t)T * 3) return;
+  const uint32_t slot = ref_slot[ref];
+  if (slot == 0xFFFFFFFFu) { topo[ref] = -1; return; }
+  const uint32_t c = cnt[slot];
+  int32_t v = -1;
+  if (c == 2) {
+    const int32_t a = ref_a[slot], b = ref_b[slot];
+    v = (a == (int32_t)ref ? b : a) / 3;
+  } else if (c > 2) {
+    v = -2;
+  }
+  topo[ref] = v;
+}
+
+// ------------------------------------------------------------ silhouettes
+
+struct SilDir {
+  bool active;
+  float beta;
+  int ie0, ie1;
+  float e0x, e0y, e1x, e1y, t, denom, dbeta;
+  bool horiz;
+};
+
+__device__ __forceinline__ int rast_tri(const float4* __restrict__ rast, int64_t pix, int T, unsigned* err) {
+  const int t = (int)__ldg(&rast[pix].w) - 1;
+  if (t >= T) { dr_flag(err, DR_DEVERR_TRI_ID); return -1; }
+  return t;
+}
+
+// One direction of silhouetteBlock (Antialias.swift:189-325) for pixel
+// (pn, ph, pw) whose triangle is tri_p.  dir: 0 +x, 1 +y, 2 -x, 3 -y.
+__device__ SilDir sil_dir(const float4* __restrict__ rast, const float* __restrict__ pos,
+                          const int32_t* __restrict__ tri, const int32_t* __restrict__ topo, int H, int W,
+                          int V, int T, int pn, int ph, int pw, int tri_p, int dir, unsigned* err) {
+  SilDir s;
+  s.active = false;
+  s.beta = 0.0f;
+  const int dw = dir == 0 ? 1 : (dir == 2 ? -1 : 0);
+  const int dh = dir == 1 ? 1 : (dir == 3 ? -1 : 0);
+  const int nh = ph + dh, nw = pw + dw;
+  if (nh < 0 || nh >= H || nw < 0 || nw >= W) return s;
+  const int tri_n = rast_tri(rast, ((int64_t)pn * H + nh) * W + nw, T, err);
+  if (tri_p == tri_n) return s;
+  if (tri_p < 0 && tri_n < 0) return s;
+  int fg, target;
+  if (tri_p >= 0 && tri_n >= 0) {
+    const int n0 = __ldg(topo + 3 * tri_p), n1 = __ldg(topo + 3 * tri_p + 1), n2 = __ldg(topo + 3 * tri_p + 2);
+    if (!(n0 == tri_n || n1 == tri_n || n2 == tri_n)) return s;
+    fg = tri_p; target = tri_n;
+  } else if (tri_p >= 0) {
+    fg = tri_p; target = -1;
+  } else {
+    fg = tri_n; target = -1;
+  }
+  const float* pb = pos + (int64_t)pn * V * 4;
+  const float pcx = (float)pw + 0.5f, pcy = (float)ph + 0.5f;
+  const float ncx = (float)nw + 0.5f, ncy = (float)nh + 0.5f;
+  int k_sel = -1, ie0 = -1, ie1 = -1;
+  float e0x = 0.f, e0y = 0.f, e1x = 0.f, e1y = 0.f;
+  for (int kk = 0; kk < 3; ++kk) {
+    if (__ldg(topo + 3 * fg + kk) != target) continue;
+    const int a = __ldg(tri + 3 * fg + (kk + 1) % 3), b = __ldg(tri + 3 * fg + (kk + 2) % 3);
+    if (a < 0 || a >= V || b < 0 || b >= V) { dr_flag(err, DR_DEVERR_VERTEX); continue; }
+    const float4 pa = ldg4(pb + (int64_t)a * 4), pq = ldg4(pb + (int64_t)b * 4);
+    const float E0x = (pa.x / pa.w + 1.0f) * (float)W * 0.5f;
+    const float E0y = (1.0f - pa.y / pa.w) * (float)H * 0.5f;
+    const float E1x = (pq.x / pq.w + 1.0f) * (float)W * 0.5f;
+    const float E1y = (1.0f - pq.y / pq.w) * (float)H * 0.5f;
+    const float ex = E1x - E0x, ey = E1y - E0y;
+    const float side_p = ex * (pcy - E0y) - ey * (pcx - E0x);
+    const float side_n = ex * (ncy - E0y) - ey * (ncx - E0x);
+    if (side_p * side_n < 0.0f) {
+      k_sel = kk; ie0 = a; ie1 = b;
+      e0x = E0x; e0y = E0y; e1x = E1x; e1y = E1y;
+      break;
+    }
+  }
+  if (k_sel < 0) return s;
+  float beta = 0.0f, t_val = 0.0f, denom = 0.0f, dbeta = 0.0f;
+  const bool horiz = (dh == 0);
+  if (horiz) {
+    const float dyv = e1y - e0y;
+    denom = dyv;
+    if (fabsf(dyv) >= 1e-7f) {
+      const float tval = (pcy - e0y) / dyv;
+      t_val = tval;
+      if (tval >= 0.0f && tval <= 1.0f) {
+        const float xe = e0x + tval * (e1x - e0x);
+        if (xe > (float)pw && xe < (float)(pw + 1)) {
+          const float d = xe - pcx;
+          beta = 0.5f - fabsf(d);
+          dbeta = (d > 0.0f) ? -1.0f : 1.0f;
+        }
+      }
+    }
+  } else {
+    const float dxv = e1x - e0x;
+    denom = dxv;
+    if (fabsf(dxv) >= 1e-7f) {
+      const float tval = (pcx - e0x) / dxv;
+      t_val = tval;
+      if (tval >= 0.0f && tval <= 1.0f) {
+        const float ye = e0y + tval * (e1y - e0y);
+        if (ye > (float)ph && ye < (float)(ph + 1)) {
+          const float d = ye - pcy;
+          beta = 0.5f - fabsf(d);
+          dbeta = (d > 0.0f) ? -1.0f : 1.0f;
+        }
+      }
+    }
+  }
+  if (beta <= 0.0f) return s;
+  s.active = true;
+  s.beta = beta;
+  s.ie0 = ie0; s.ie1 = ie1;
+  s.e0x = e0x; s.e0y = e0y; s.e1x = e1x; s.e1y = e1y;
+  s.t = t_val; s.denom = denom; s.dbeta = dbeta; s.horiz = horiz;
+  return s;
+}
+
+__device__ __forceinline__ int64_t nbr_pix(int pn, int ph, int pw, int dir, int H, int W) {
+  const int dw = dir == 0 ? 1 : (dir == 2 ? -1 : 0);
+  const int dh = dir == 1 ? 1 : (dir == 3 ? -1 : 0);
+  return ((int64_t)pn * H + (ph + dh)) * W + (pw + dw);
+}
+
+__global__ void k_aa_fwd(const float* __restrict__ color, int N, int H, int W, int C,
+                         const float4* __restrict__ rast, const float* __restrict__ pos, int V,
+                         const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
+                         float* __restrict__ out, unsigned* err) {
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= (int64_t)N * H * W) return;
+  const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+  const int tri_p = rast_tri(rast, pix, T, err);
+  float beta[4];
+  int64_t nb[4];
+  bool any = false;
+#pragma unroll
+  for (int d = 0; d < 4; ++d) {
+    const SilDir s = sil_dir(rast, pos, tri, topo, H, W, V, T, pn, ph, pw, tri_p, d, err);
+    beta[d] = s.active ? s.beta : 0.0f;
+    nb[d] = s.active ? nbr_pix(pn, ph, pw, d, H, W) : -1;
+    any |= s.active;
+  }
+  const float* cp = color + pix * C;
+  float* o = out + pix * C;
+  if (!any) {
+    for (int c = 0; c < C; ++c) o[c] = __ldg(cp + c);
+    return;
+  }
+  for (int c = 0; c < C; ++c) {
+    const float p = __ldg(cp + c);
+    float acc = p;
+#pragma unroll
+    for (int d = 0; d < 4; ++d)
+      if (nb[d] >= 0) acc += beta[d] * (__ldg(color + nb[d] * C + c) - p);
+    o[c] = acc;
+  }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void add_pos(float* p, float x, float y, float w) {
+  if (VEC) {
+    atomicAdd(reinterpret_cast<float4*>(p), make_float4(x, y, 0.0f, w));
+  } else {
+    atomicAdd(p + 0, x);
+    atomicAdd(p + 1, y);
+    atomicAdd(p + 3, w);
+  }
+}
+
+template <bool VEC>
+__global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, int C,
+                         const float4* __restrict__ rast, const float* __restrict__ pos, int V,
+                         const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
+                         const float* __restrict__ d_out, float* __restrict__ d_color, float* __restrict__ d_pos,
+                         unsigned* err) {
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= (int64_t)N * H * W) return;
+  const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+  const int tri_p = rast_tri(rast, pix, T, err);
+  const float* g = d_out + pix * C;
+  const float halfW = (float)W * 0.5f, halfH = (float)H * 0.5f;
+  float alpha_sum = 0.0f;
+  // Own silhouettes: the (1 - sum beta) factor and d_pos (Antialias.swift:405-495).
+#pragma unroll 1
+  for (int dir = 0; dir < 4; ++dir) {
+    const SilDir s = sil_dir(rast, pos, tri, topo, H, W, V, T, pn, ph, pw, tri_p, dir, err);
+    if (!s.active) continue;
+    alpha_sum += s.beta;
+    if (s.beta <= 0.0f || s.beta >= 1.0f) continue;
+    const int64_t nb = nbr_pix(pn, ph, pw, dir, H, W);
+    float d_alpha = 0.0f;
+    for (int c = 0; c < C; ++c) {
+      const float cp = __ldg(color + pix * C + c), cn = __ldg(color + nb * C + c);
+      d_alpha += __ldg(g + c) * (cn - cp);
+    }
+    if (d_alpha == 0.0f) continue;
+    float dade0x, dade0y, dade1x, dade1y;
+    const float inv_denom_sq = 1.0f / (s.denom * s.denom);
+    if (s.horiz) {
+      const float row_y = (float)ph + 0.5f;
+      const float ex_diff = s.e1x - s.e0x;
+      dade0x = s.dbeta * (1.0f - s.t);
+      dade1x = s.dbeta * s.t;
+      dade0y = s.dbeta * ex_diff * (row_y - s.e1y) * inv_denom_sq;
+      dade1y = s.dbeta * (-ex_diff) * (row_y - s.e0y) * inv_denom_sq;
+    } else {
+      const float col_x = (float)pw + 0.5f;
+      const float ey_diff = s.e1y - s.e0y;
+      dade0y = s.dbeta * (1.0f - s.t);
+      dade1y = s.dbeta * s.t;
+      dade0x = s.dbeta * ey_diff * (col_x - s.e1x) * inv_denom_sq;
+      dade1x = s.dbeta * (-ey_diff) * (col_x - s.e0x) * inv_denom_sq;
+    }
+    const int64_t pb = (int64_t)pn * V * 4;
+    {
+      const float4 pv = ldg4(pos + pb + (int64_t)s.ie0 * 4);
+      const float inv_w = 1.0f / pv.w;
+      const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
+      add_pos<VEC>(d_pos + pb + (int64_t)s.ie0 * 4, d_alpha * dade0x * halfW * inv_w,
+                   d_alpha * dade0y * (-halfH) * inv_w,
+                   d_alpha * (dade0x * (-halfW * nd_x) + dade0y * (halfH * nd_y)) * inv_w);
+    }
+    {
+      const float4 pv = ldg4(pos + pb + (int64_t)s.ie1 * 4);
+      const float inv_w = 1.0f / pv.w;
+      const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
+      add_pos<VEC>(d_pos + pb + (int64_t)s.ie1 * 4, d_alpha * dade1x * halfW * inv_w,
+                   d_alpha * dade1y * (-halfH) * inv_w,
+                   d_alpha * (dade1x * (-halfW * nd_x) + dade1y * (halfH * nd_y)) * inv_w);
+    }
+  }
+  // Neighbours' betas toward this pixel: neighbour p = q - dir_d sees q in
+  // direction d.
+  float nbeta[4];
+  int64_t nsrc[4];
+#pragma unroll 1
+  for (int d = 0; d < 4; ++d) {
+    nbeta[d] = 0.0f;
+    nsrc[d] = -1;
+    const int sw = pw - (d == 0 ? 1 : (d == 2 ? -1 : 0));
+    const int sh = ph - (d == 1 ? 1 : (d == 3 ? -1 : 0));
+    if (sw < 0 || sw >= W || sh < 0 || sh >= H) continue;
+    const int64_t p = ((int64_t)pn * H + sh) * W + sw;
+    const int tri_s = rast_tri(rast, p, T, err);
+    if (tri_s == tri_p) continue;  // no silhouette between equal ids
+    const SilDir s = sil_dir(rast, pos, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
+    if (s.active) { nbeta[d] = s.beta; nsrc[d] = p; }
+  }
+  for (int c = 0; c < C; ++c) {
+    float v = __ldg(g + c) * (1.0f - alpha_sum);
+#pragma unroll
+    for (int d = 0; d < 4; ++d)
+      if (nsrc[d] >= 0) v += __ldg(d_out + nsrc[d] * C + c) * nbeta[d];
+    d_color[pix * C + c] = v;
+  }
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+dr_status check_aa(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
+                   const float* pos, int V, const int32_t* tri, int T, const int32_t* topo) {
+  DR_REQUIRE(ctx, color && rast && pos && tri && topo, "antialias: null input");
+  DR_REQUIRE(ctx, N > 0 && H > 0 && W > 0 && C > 0 && V > 0 && T >= 0, "antialias: bad sizes");
+  DR_REQUIRE(ctx, aligned16(rast) && aligned16(pos), "antialias: rast / pos must be 16-byte aligned");
+  return DR_OK;
+}
+
+}  // namespace
+
+using namespace dr;
+
+extern "C" dr_status dr_antialias_construct_topology_hash(dr_ctx* ctx, const int32_t* tri, int T, int32_t* topo) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, tri && topo && T >= 0, "antialiasConstructTopologyHash: bad arguments");
+  DR_REQUIRE(ctx, T < (1 << 29), "antialiasConstructTopologyHash: T too large");
+  if (T == 0) return DR_OK;
+  const int64_t E = (int64_t)T * 3;
+  uint64_t cap = 1024;
+  while (cap < (uint64_t)(2 * E)) cap <<= 1;
+  const size_t bytes = cap * (8 + 4 + 4 + 4) + (size_t)E * 4 + 256;
+  char* w = (char*)ws_get(ctx, WS_HASH, bytes);
+  if (!w) return DR_ENOMEM;
+  unsigned long long* keys = (unsigned long long*)w;
+  uint32_t* cnt = (uint32_t*)(keys + cap);
+  int32_t* ra = (int32_t*)(cnt + cap);
+  int32_t* rb = ra + cap;
+  uint32_t* rs = (uint32_t*)(rb + cap);
+  cudaMemsetAsync(keys, 0xFF, cap * 8, ctx->stream);
+  // EMPTY_KEY's low word is 0: clear it after the 0xFF fill.
+  cudaMemset2DAsync(keys, 8, 0, 4, cap, ctx->stream);
+  cudaMemsetAsync(cnt, 0, cap * 4, ctx->stream);
+  DR_TB(ctx);
+  k_topo_insert<<<grid_for(E, 256), 256, 0, ctx->stream>>>(tri, T, keys, cnt, ra, rb, rs, (uint32_t)(cap - 1),
+                                                            ctx->d_err);
+  DR_LAUNCHED(ctx, "topo_insert");
+  DR_TB(ctx);
+  k_topo_classify<<<grid_for(E, 256), 256, 0, ctx->stream>>>(T, cnt, ra, rb, rs, topo);
+  DR_LAUNCHED(ctx, "topo_classify");
+  return DR_OK;
+}
+
+extern "C" dr_status dr_antialias_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                      const float* rast, const float* pos, int V, const int32_t* tri, int T,
+                                      const int32_t* topo, float* out) {
+  DR_ENTER(ctx);
+  dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
+  if (st != DR_OK) return st;
+  DR_REQUIRE(ctx, out, "antialias: out required");
+  const int64_t P = (int64_t)N * H * W;
+  DR_TB(ctx);
+  k_aa_fwd<<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, reinterpret_cast<const float4*>(rast),
+                                                       pos, V, tri, T, topo, out, ctx->d_err);
+  DR_LAUNCHED(ctx, "aa_fwd");
+  return DR_OK;
+}
+
+extern "C" dr_status dr_antialias_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                      const float* rast, const float* pos, int V, const int32_t* tri, int T,
+                                      const int32_t* topo, const float* d_out, float* d_color, float* d_pos) {
+  DR_ENTER(ctx);
+  dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
+  if (st != DR_OK) return st;
+  DR_REQUIRE(ctx, d_out && d_color && d_pos, "antialias_bwd: d_out, d_color, d_pos required");
+  cudaMemsetAsync(d_pos, 0, sizeof(float) * (size_t)N * V * 4, ctx->stream);
+  const int64_t P = (int64_t)N * H * W;
+  const float4* r4 = reinterpret_cast<const float4*>(rast);
+  DR_TB(ctx);
+  if (aligned16(d_pos))
+    k_aa_bwd<true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, V, tri, T, topo, d_out,
+                                                               d_color, d_pos, ctx->d_err);
+  else
+    k_aa_bwd<false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, V, tri, T, topo,
+                                                                d_out, d_color, d_pos, ctx->d_err);
+  DR_LAUNCHED(ctx, "aa_bwd");
+  return DR_OK;
+}

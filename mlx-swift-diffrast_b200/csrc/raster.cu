@@ -1,0 +1,500 @@
+// raster.cu — rasterize forward (setup, binning, per-tile fine raster, rast_db,
+// depth peeling) and backward (d_pos).
+//
+// Reference: Sources/MLXDiffRast/Rasterize.swift.  The reference rasterizes one
+// thread per pixel over a capped (128) tile bin list; this implementation is
+// triangle-centric inside each 16x16 tile:
+//   1. k_raster_setup    one thread per (view, triangle): range / w<=0 reject,
+//                        perspective divide, signed area (Rasterize.swift:280-328),
+//                        the EXACT pixel rectangle of the NDC AABB test the
+//                        reference applies per pixel (Rasterize.swift:426-433),
+//                        and a count per touched tile.
+//   2. scan               exclusive scan of the per-tile counts (no cap, no drop).
+//   3. k_raster_scatter   per-tile candidate lists (order irrelevant, see 4).
+//   4. k_raster_tiles     one CTA per (view, tile): every candidate visits the
+//                        pixels of its rectangle inside the tile, runs the
+//                        reference's edge / inside / z / peel tests with the same
+//                        IEEE operations, and folds (z, tri) into a per-pixel
+//                        64-bit shared-memory atomicMin.  The minimum of the
+//                        packed key is the lexicographic minimum of (z, tri) — the
+//                        winner the reference's ascending strict-< loop picks — so
+//                        the result does not depend on list order.  The winner's
+//                        (u, v, z) and rast_db are then recomputed bit-identically.
+// All coverage-critical arithmetic uses explicit round-to-nearest intrinsics
+// (never contracted into FMA), so tri_id, u, v and z match the CPU oracle bit for
+// bit.
+#include "common.cuh"
+
+namespace {
+
+constexpr int TILE = 16;
+constexpr int TILE_PIX = TILE * TILE;
+
+#define FM(a, b) __fmul_rn((a), (b))
+#define FA(a, b) __fadd_rn((a), (b))
+#define FS(a, b) __fsub_rn((a), (b))
+#define FD(a, b) __fdiv_rn((a), (b))
+
+// Pixel-centre NDC exactly as Rasterize.swift:381-382 computes it.
+__device__ __forceinline__ float ndc_x_of(int pw, int W) {
+  return FS(FD(FM(2.0f, FA((float)pw, 0.5f)), (float)W), 1.0f);
+}
+__device__ __forceinline__ float ndc_y_of(int ph, int H) {
+  return FS(1.0f, FD(FM(2.0f, FA((float)ph, 0.5f)), (float)H));
+}
+
+// Setup record: 48 bytes.
+//   r0 = (sx0, sy0, sz0, sx1)   r1 = (sy1, sz1, sx2, sy2)
+//   r2 = (sz2, area, bits(x0 | x1 << 16), bits(y0 | y1 << 16))
+// area == 0 marks a triangle that can cover no pixel.
+struct Rec {
+  float sx0, sy0, sz0, sx1, sy1, sz1, sx2, sy2, sz2, area;
+  int x0, x1, y0, y1;
+};
+
+__device__ __forceinline__ Rec load_rec(const float4* __restrict__ rec, int64_t i) {
+  float4 a = __ldg(rec + 3 * i + 0), b = __ldg(rec + 3 * i + 1), c = __ldg(rec + 3 * i + 2);
+  Rec r;
+  r.sx0 = a.x; r.sy0 = a.y; r.sz0 = a.z; r.sx1 = a.w;
+  r.sy1 = b.x; r.sz1 = b.y; r.sx2 = b.z; r.sy2 = b.w;
+  r.sz2 = c.x; r.area = c.y;
+  unsigned xs = __float_as_uint(c.z), ys = __float_as_uint(c.w);
+  r.x0 = (int)(xs & 0xffffu); r.x1 = (int)(xs >> 16);
+  r.y0 = (int)(ys & 0xffffu); r.y1 = (int)(ys >> 16);
+  return r;
+}
+
+__device__ __forceinline__ float clampf_safe(float x, float lo, float hi) {
+  return fminf(fmaxf(x, lo), hi);  // NaN never reaches here (records are finite)
+}
+
+// Smallest / largest pixel column whose centre NDC lies in [minx, maxx].  The
+// float estimate is refined against the exact ndc_x_of, which is monotone in pw.
+__device__ void exact_cols(float minx, float maxx, int W, int& lo, int& hi) {
+  float fl = clampf_safe((minx + 1.0f) * 0.5f * (float)W - 0.5f, -2.0f, (float)W + 1.0f);
+  float fh = clampf_safe((maxx + 1.0f) * 0.5f * (float)W - 0.5f, -2.0f, (float)W + 1.0f);
+  lo = min(max((int)floorf(fl), 0), W);
+  while (lo > 0 && ndc_x_of(lo - 1, W) >= minx) --lo;
+  while (lo < W && ndc_x_of(lo, W) < minx) ++lo;
+  hi = min(max((int)ceilf(fh), -1), W - 1);
+  while (hi < W - 1 && ndc_x_of(hi + 1, W) <= maxx) ++hi;
+  while (hi >= 0 && ndc_x_of(hi, W) > maxx) --hi;
+}
+
+// Rows whose centre NDC y lies in [miny, maxy] (ndc_y_of decreases with ph).
+__device__ void exact_rows(float miny, float maxy, int H, int& lo, int& hi) {
+  float gl = clampf_safe((1.0f - maxy) * 0.5f * (float)H - 0.5f, -2.0f, (float)H + 1.0f);
+  float gh = clampf_safe((1.0f - miny) * 0.5f * (float)H - 0.5f, -2.0f, (float)H + 1.0f);
+  lo = min(max((int)floorf(gl), 0), H);
+  while (lo > 0 && ndc_y_of(lo - 1, H) <= maxy) --lo;
+  while (lo < H && ndc_y_of(lo, H) > maxy) ++lo;
+  hi = min(max((int)ceilf(gh), -1), H - 1);
+  while (hi < H - 1 && ndc_y_of(hi + 1, H) >= miny) ++hi;
+  while (hi >= 0 && ndc_y_of(hi, H) < miny) --hi;
+}
+
+__device__ __forceinline__ bool finite3(float a, float b, float c) {
+  return isfinite(a) && isfinite(b) && isfinite(c);
+}
+
+__global__ void k_raster_setup(const float* __restrict__ pos, int V, const int32_t* __restrict__ tri,
+                               int T, const int32_t* __restrict__ ranges, int N, int H, int W,
+                               int ntx, int nty, float4* __restrict__ rec,
+                               uint32_t* __restrict__ tile_count, unsigned* err) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)N * T) return;
+  int t = (int)(idx % T);
+  int n = (int)(idx / T);
+  float4* out = rec + 3 * idx;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  bool ok = true;
+  int64_t pos_n_base = 0;
+  if (ranges) {
+    int rs = __ldg(ranges + 2 * n), rc = __ldg(ranges + 2 * n + 1);
+    ok = !(t < rs || t >= rs + rc);
+  } else {
+    pos_n_base = (int64_t)n * V * 4;
+  }
+  int i0 = 0, i1 = 0, i2 = 0;
+  if (ok) {
+    i0 = __ldg(tri + 3 * t); i1 = __ldg(tri + 3 * t + 1); i2 = __ldg(tri + 3 * t + 2);
+    if (i0 < 0 || i0 >= V || i1 < 0 || i1 >= V || i2 < 0 || i2 >= V) {
+      dr_flag(err, DR_DEVERR_VERTEX);
+      ok = false;
+    }
+  }
+  float4 p0, p1, p2;
+  if (ok) {
+    p0 = ldg4(pos + pos_n_base + (int64_t)i0 * 4);
+    p1 = ldg4(pos + pos_n_base + (int64_t)i1 * 4);
+    p2 = ldg4(pos + pos_n_base + (int64_t)i2 * 4);
+    ok = !(p0.w <= 0.0f || p1.w <= 0.0f || p2.w <= 0.0f);
+  }
+  if (!ok) {
+    out[0] = zero; out[1] = zero; out[2] = zero;
+    return;
+  }
+  float sx0 = FD(p0.x, p0.w), sy0 = FD(p0.y, p0.w), sz0 = FD(p0.z, p0.w);
+  float sx1 = FD(p1.x, p1.w), sy1 = FD(p1.y, p1.w), sz1 = FD(p1.z, p1.w);
+  float sx2 = FD(p2.x, p2.w), sy2 = FD(p2.y, p2.w), sz2 = FD(p2.z, p2.w);
+  float area = FS(FM(FS(sx1, sx0), FS(sy2, sy0)), FM(FS(sx2, sx0), FS(sy1, sy0)));
+  ok = finite3(sx0, sy0, sz0) && finite3(sx1, sy1, sz1) && finite3(sx2, sy2, sz2) &&
+       isfinite(area) && area != 0.0f;
+  int x0 = 0, x1 = -1, y0 = 0, y1 = -1;
+  if (ok) {
+    float minx = fminf(sx0, fminf(sx1, sx2)), maxx = fmaxf(sx0, fmaxf(sx1, sx2));
+    float miny = fminf(sy0, fminf(sy1, sy2)), maxy = fmaxf(sy0, fmaxf(sy1, sy2));
+    exact_cols(minx, maxx, W, x0, x1);
+    exact_rows(miny, maxy, H, y0, y1);
+    ok = (x0 <= x1) && (y0 <= y1);
+  }
+  if (!ok) {
+    out[0] = zero; out[1] = zero; out[2] = zero;
+    return;
+  }
+  out[0] = make_float4(sx0, sy0, sz0, sx1);
+  out[1] = make_float4(sy1, sz1, sx2, sy2);
+  out[2] = make_float4(sz2, area, __uint_as_float((unsigned)x0 | ((unsigned)x1 << 16)),
+                       __uint_as_float((unsigned)y0 | ((unsigned)y1 << 16)));
+  uint32_t* tc = tile_count + (int64_t)n * ntx * nty;
+  for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
+    for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) atomicAdd(tc + ty * ntx + tx, 1u);
+}
+
+// Scatter every valid (view, triangle) into the lists of the tiles it touches.
+// tile_cur starts as the exclusive offsets; atomicAdd hands out list slots.
+__global__ void k_raster_scatter(const float4* __restrict__ rec, int N, int T, int ntx, int nty,
+                                 uint32_t* __restrict__ tile_cur, int32_t* __restrict__ list) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)N * T) return;
+  float4 c = __ldg(rec + 3 * idx + 2);
+  if (c.y == 0.0f) return;  // area == 0: invalid
+  int t = (int)(idx % T);
+  int n = (int)(idx / T);
+  unsigned xs = __float_as_uint(c.z), ys = __float_as_uint(c.w);
+  int x0 = (int)(xs & 0xffffu), x1 = (int)(xs >> 16), y0 = (int)(ys & 0xffffu), y1 = (int)(ys >> 16);
+  uint32_t* tc = tile_cur + (int64_t)n * ntx * nty;
+  for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
+    for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) {
+      uint32_t slot = atomicAdd(tc + ty * ntx + tx, 1u);
+      list[slot] = t;
+    }
+}
+
+// Total order on (z, tri): z mapped to an order-preserving uint32 in the high
+// word (-0 canonicalised to +0, which compares equal to it), tri in the low word.
+__device__ __forceinline__ unsigned long long pack_key(float z, int t) {
+  unsigned u = __float_as_uint(FA(z, 0.0f));
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned)t;
+}
+
+template <bool PEEL, bool DB>
+__global__ void __launch_bounds__(TILE_PIX)
+k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int nty,
+               const uint32_t* __restrict__ tile_off, const uint32_t* __restrict__ tile_count,
+               const int32_t* __restrict__ list, const float* __restrict__ peel,
+               float4* __restrict__ rast, float4* __restrict__ rast_db) {
+  __shared__ unsigned long long s_key[TILE_PIX];
+  __shared__ float s_peel[TILE_PIX];
+  __shared__ float s_ndcx[TILE], s_ndcy[TILE];
+
+  const int ntiles = ntx * nty;
+  const int n = blockIdx.x / ntiles;
+  const int tile = blockIdx.x - n * ntiles;
+  const int tx0 = (tile % ntx) * TILE, ty0 = (tile / ntx) * TILE;
+  const int tid = threadIdx.x;
+  const int px = tx0 + (tid & (TILE - 1)), py = ty0 + (tid >> 4);
+  const bool inside_img = (px < W) && (py < H);
+  const int64_t pix = ((int64_t)n * H + py) * W + px;
+
+  s_key[tid] = ~0ull;
+  if (PEEL) {
+    float pz = -1e30f;
+    if (inside_img) {
+      float4 pl = ldg4(peel + 4 * pix);
+      if (pl.w > 0.0f) pz = pl.z;
+    }
+    s_peel[tid] = pz;
+  }
+  if (tid < TILE) s_ndcx[tid] = ndc_x_of(tx0 + tid, W);
+  else if (tid < 2 * TILE) s_ndcy[tid - TILE] = ndc_y_of(ty0 + tid - TILE, H);
+  __syncthreads();
+
+  const uint32_t gt = (uint32_t)blockIdx.x;
+  const uint32_t begin = __ldg(tile_off + gt), cnt = __ldg(tile_count + gt);
+  const int64_t rec_view = (int64_t)n * T;
+  for (uint32_t i = tid; i < cnt; i += TILE_PIX) {
+    const int t = __ldg(list + begin + i);
+    const Rec r = load_rec(rec, rec_view + t);
+    const float inv_area = FD(1.0f, r.area);
+    const int cx0 = max(r.x0, tx0), cx1 = min(r.x1, tx0 + TILE - 1);
+    const int cy0 = max(r.y0, ty0), cy1 = min(r.y1, ty0 + TILE - 1);
+    for (int yy = cy0; yy <= cy1; ++yy) {
+      const float y = s_ndcy[yy - ty0];
+      const float dy0 = FS(r.sy0, y), dy1 = FS(r.sy1, y), dy2 = FS(r.sy2, y);
+      for (int xx = cx0; xx <= cx1; ++xx) {
+        const float x = s_ndcx[xx - tx0];
+        const float dx0 = FS(r.sx0, x), dx1 = FS(r.sx1, x), dx2 = FS(r.sx2, x);
+        const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));
+        const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
+        const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
+        if (FM(e0, r.area) < 0.0f || FM(e1, r.area) < 0.0f || FM(e2, r.area) < 0.0f) continue;
+        const float bw = FM(e0, inv_area), u = FM(e1, inv_area), v = FM(e2, inv_area);
+        const float z = FA(FA(FM(bw, r.sz0), FM(u, r.sz1)), FM(v, r.sz2));
+        if (z < -1.0f || z > 1.0f) continue;
+        const int p = (yy - ty0) * TILE + (xx - tx0);
+        if (PEEL && z <= s_peel[p]) continue;
+        const unsigned long long key = pack_key(z, t);
+        if (key < s_key[p]) atomicMin(&s_key[p], key);
+      }
+    }
+  }
+  __syncthreads();
+  if (!inside_img) return;
+  const unsigned long long key = s_key[tid];
+  if (key == ~0ull) {
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    rast[pix] = z4;
+    if (DB) rast_db[pix] = z4;
+    return;
+  }
+  const int t = (int)(unsigned)(key & 0xffffffffull);
+  const Rec r = load_rec(rec, rec_view + t);
+  const float inv_area = FD(1.0f, r.area);
+  const float x = s_ndcx[px - tx0], y = s_ndcy[py - ty0];
+  const float dx0 = FS(r.sx0, x), dx1 = FS(r.sx1, x), dx2 = FS(r.sx2, x);
+  const float dy0 = FS(r.sy0, y), dy1 = FS(r.sy1, y), dy2 = FS(r.sy2, y);
+  const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));
+  const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
+  const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
+  const float bw = FM(e0, inv_area), u = FM(e1, inv_area), v = FM(e2, inv_area);
+  const float z = FA(FA(FM(bw, r.sz0), FM(u, r.sz1)), FM(v, r.sz2));
+  rast[pix] = make_float4(u, v, z, (float)(t + 1));
+  if (DB) {
+    // Rasterize.swift:586-598
+    const float k_x = FD(2.0f, (float)W), k_y = FD(-2.0f, (float)H);
+    rast_db[pix] = make_float4(FM(FM(FS(r.sy2, r.sy0), inv_area), k_x),
+                               FM(FM(FS(r.sx0, r.sx2), inv_area), k_y),
+                               FM(FM(FS(r.sy0, r.sy1), inv_area), k_x),
+                               FM(FM(FS(r.sx1, r.sx0), inv_area), k_y));
+  }
+}
+
+// d_pos: Rasterize.swift:637-812, one thread per pixel, float4 atomics.
+template <bool DB, bool VEC>
+__global__ void k_raster_bwd(const float* __restrict__ pos, int V, const int32_t* __restrict__ tri,
+                             int T, bool shared_pos, int N, int H, int W,
+                             const float4* __restrict__ rast, const float4* __restrict__ d_rast,
+                             const float4* __restrict__ d_rast_db, float* __restrict__ d_pos,
+                             unsigned* err) {
+  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= (int64_t)N * H * W) return;
+  const float4 r = __ldg(rast + pix);
+  const int t = (int)r.w - 1;
+  if (t < 0) return;
+  if (t >= T) { dr_flag(err, DR_DEVERR_TRI_ID); return; }
+  const int pw = (int)(pix % W);
+  const int ph = (int)((pix / W) % H);
+  const int pn = (int)(pix / ((int64_t)H * W));
+  const float u_val = r.x, v_val = r.y;
+  const float bw_val = 1.0f - u_val - v_val;
+  const float4 g = __ldg(d_rast + pix);
+  const float d_u = g.x, d_v = g.y, d_z = g.z;
+  float d_db0 = 0.f, d_db1 = 0.f, d_db2 = 0.f, d_db3 = 0.f;
+  if (DB) {
+    const float4 gd = __ldg(d_rast_db + pix);
+    d_db0 = gd.x; d_db1 = gd.y; d_db2 = gd.z; d_db3 = gd.w;
+  }
+  const float Px = 2.0f * ((float)pw + 0.5f) / (float)W - 1.0f;
+  const float Py = 1.0f - 2.0f * ((float)ph + 0.5f) / (float)H;
+  const int64_t pos_n_base = shared_pos ? 0 : (int64_t)pn * V * 4;
+  const int i0 = __ldg(tri + 3 * t), i1 = __ldg(tri + 3 * t + 1), i2 = __ldg(tri + 3 * t + 2);
+  if (i0 < 0 || i0 >= V || i1 < 0 || i1 >= V || i2 < 0 || i2 >= V) {
+    dr_flag(err, DR_DEVERR_VERTEX);
+    return;
+  }
+  const float4 q0 = ldg4(pos + pos_n_base + (int64_t)i0 * 4);
+  const float4 q1 = ldg4(pos + pos_n_base + (int64_t)i1 * 4);
+  const float4 q2 = ldg4(pos + pos_n_base + (int64_t)i2 * 4);
+  const float w0 = q0.w, w1 = q1.w, w2 = q2.w;
+  const float sx0 = q0.x / w0, sy0 = q0.y / w0, sz0 = q0.z / w0;
+  const float sx1 = q1.x / w1, sy1 = q1.y / w1, sz1 = q1.z / w1;
+  const float sx2 = q2.x / w2, sy2 = q2.y / w2, sz2 = q2.z / w2;
+  const float area = (sx1 - sx0) * (sy2 - sy0) - (sx2 - sx0) * (sy1 - sy0);
+  const float inv_area = 1.0f / area;
+  const float dadsx0 = sy1 - sy2, dadsx1 = sy2 - sy0, dadsx2 = sy0 - sy1;
+  const float dadsy0 = sx2 - sx1, dadsy1 = sx0 - sx2, dadsy2 = sx1 - sx0;
+  const float de1dsx0 = Py - sy2, de1dsx2 = sy0 - Py, de1dsy0 = sx2 - Px, de1dsy2 = Px - sx0;
+  const float de2dsx0 = sy1 - Py, de2dsx1 = Py - sy0, de2dsy0 = Px - sx1, de2dsy1 = sx0 - Px;
+  const float dudsx0 = (de1dsx0 - u_val * dadsx0) * inv_area;
+  const float dudsx1 = (0.0f - u_val * dadsx1) * inv_area;
+  const float dudsx2 = (de1dsx2 - u_val * dadsx2) * inv_area;
+  const float dudsy0 = (de1dsy0 - u_val * dadsy0) * inv_area;
+  const float dudsy1 = (0.0f - u_val * dadsy1) * inv_area;
+  const float dudsy2 = (de1dsy2 - u_val * dadsy2) * inv_area;
+  const float dvdsx0 = (de2dsx0 - v_val * dadsx0) * inv_area;
+  const float dvdsx1 = (de2dsx1 - v_val * dadsx1) * inv_area;
+  const float dvdsx2 = (0.0f - v_val * dadsx2) * inv_area;
+  const float dvdsy0 = (de2dsy0 - v_val * dadsy0) * inv_area;
+  const float dvdsy1 = (de2dsy1 - v_val * dadsy1) * inv_area;
+  const float dvdsy2 = (0.0f - v_val * dadsy2) * inv_area;
+  const float dsz10 = sz1 - sz0, dsz20 = sz2 - sz0;
+  float dsx0 = d_u * dudsx0 + d_v * dvdsx0 + d_z * (dudsx0 * dsz10 + dvdsx0 * dsz20);
+  float dsx1 = d_u * dudsx1 + d_v * dvdsx1 + d_z * (dudsx1 * dsz10 + dvdsx1 * dsz20);
+  float dsx2 = d_u * dudsx2 + d_v * dvdsx2 + d_z * (dudsx2 * dsz10 + dvdsx2 * dsz20);
+  float dsy0 = d_u * dudsy0 + d_v * dvdsy0 + d_z * (dudsy0 * dsz10 + dvdsy0 * dsz20);
+  float dsy1 = d_u * dudsy1 + d_v * dvdsy1 + d_z * (dudsy1 * dsz10 + dvdsy1 * dsz20);
+  float dsy2 = d_u * dudsy2 + d_v * dvdsy2 + d_z * (dudsy2 * dsz10 + dvdsy2 * dsz20);
+  const float dsz0_s = d_z * bw_val, dsz1_s = d_z * u_val, dsz2_s = d_z * v_val;
+  if (DB) {
+    const float Kx = 2.0f / (float)W, Ky = -2.0f / (float)H;
+    const float rdb0 = (sy2 - sy0) * Kx * inv_area;
+    const float rdb1 = (sx0 - sx2) * Ky * inv_area;
+    const float rdb2 = (sy0 - sy1) * Kx * inv_area;
+    const float rdb3 = (sx1 - sx0) * Ky * inv_area;
+    const float s = d_db0 * rdb0 + d_db1 * rdb1 + d_db2 * rdb2 + d_db3 * rdb3;
+    dsx0 += (-s * dadsx0) * inv_area;
+    dsx1 += (-s * dadsx1) * inv_area;
+    dsx2 += (-s * dadsx2) * inv_area;
+    dsy0 += (-s * dadsy0) * inv_area;
+    dsy1 += (-s * dadsy1) * inv_area;
+    dsy2 += (-s * dadsy2) * inv_area;
+    dsy0 += d_db0 * (-Kx) * inv_area;
+    dsy2 += d_db0 * (Kx) * inv_area;
+    dsx0 += d_db1 * (Ky) * inv_area;
+    dsx2 += d_db1 * (-Ky) * inv_area;
+    dsy0 += d_db2 * (Kx) * inv_area;
+    dsy1 += d_db2 * (-Kx) * inv_area;
+    dsx0 += d_db3 * (-Ky) * inv_area;
+    dsx1 += d_db3 * (Ky) * inv_area;
+  }
+  const float inv_w0 = 1.0f / w0, inv_w1 = 1.0f / w1, inv_w2 = 1.0f / w2;
+  const float4 g0 = make_float4(dsx0 * inv_w0, dsy0 * inv_w0, dsz0_s * inv_w0,
+                                -(sx0 * dsx0 + sy0 * dsy0 + sz0 * dsz0_s) * inv_w0);
+  const float4 g1 = make_float4(dsx1 * inv_w1, dsy1 * inv_w1, dsz1_s * inv_w1,
+                                -(sx1 * dsx1 + sy1 * dsy1 + sz1 * dsz1_s) * inv_w1);
+  const float4 g2 = make_float4(dsx2 * inv_w2, dsy2 * inv_w2, dsz2_s * inv_w2,
+                                -(sx2 * dsx2 + sy2 * dsy2 + sz2 * dsz2_s) * inv_w2);
+  float* b0 = d_pos + pos_n_base + (int64_t)i0 * 4;
+  float* b1 = d_pos + pos_n_base + (int64_t)i1 * 4;
+  float* b2 = d_pos + pos_n_base + (int64_t)i2 * 4;
+  if (VEC) {
+    atomicAdd(reinterpret_cast<float4*>(b0), g0);
+    atomicAdd(reinterpret_cast<float4*>(b1), g1);
+    atomicAdd(reinterpret_cast<float4*>(b2), g2);
+  } else {
+    atomicAdd(b0 + 0, g0.x); atomicAdd(b0 + 1, g0.y); atomicAdd(b0 + 2, g0.z); atomicAdd(b0 + 3, g0.w);
+    atomicAdd(b1 + 0, g1.x); atomicAdd(b1 + 1, g1.y); atomicAdd(b1 + 2, g1.z); atomicAdd(b1 + 3, g1.w);
+    atomicAdd(b2 + 0, g2.x); atomicAdd(b2 + 1, g2.y); atomicAdd(b2 + 2, g2.z); atomicAdd(b2 + 3, g2.w);
+  }
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+}  // namespace
+
+using namespace dr;
+
+extern "C" dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V, const int32_t* tri,
+                                      int T, const int32_t* ranges, int N, int H, int W,
+                                      const float* peel_layer, float* rast, float* rast_db) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, pos && tri && rast, "rasterize: pos, tri and rast are required");
+  DR_REQUIRE(ctx, N > 0 && V > 0 && T >= 0 && H > 0 && W > 0,
+             "rasterize: bad sizes N=%d V=%d T=%d H=%d W=%d", N, V, T, H, W);
+  DR_REQUIRE(ctx, H <= 32768 && W <= 32768, "rasterize: resolution above 32768 is not supported");
+  DR_REQUIRE(ctx, T < (1 << 24), "rasterize: T must be < 2^24 (tri_id+1 is stored as float)");
+  DR_REQUIRE(ctx, aligned16(pos) && aligned16(rast) && (!rast_db || aligned16(rast_db)) &&
+                      (!peel_layer || aligned16(peel_layer)),
+             "rasterize: pos/rast/rast_db/peel_layer must be 16-byte aligned");
+  const int ntx = (W + TILE - 1) / TILE, nty = (H + TILE - 1) / TILE;
+  const int64_t ntiles_all = (int64_t)N * ntx * nty;
+  const int64_t NT = (int64_t)N * T;
+  DR_REQUIRE(ctx, ntiles_all < (1ll << 31), "rasterize: too many tiles");
+
+  float4* rec = (float4*)ws_get(ctx, WS_RASTER_REC, sizeof(float4) * 3 * (size_t)(NT > 0 ? NT : 1));
+  uint32_t* tc = (uint32_t*)ws_get(ctx, WS_TILE_COUNT, sizeof(uint32_t) * (size_t)(3 * ntiles_all + 4));
+  if (!rec || !tc) return DR_ENOMEM;
+  uint32_t* tile_count = tc;
+  uint32_t* tile_off = tc + ntiles_all;
+  uint32_t* tile_cur = tc + 2 * ntiles_all;
+  uint32_t* total = tc + 3 * ntiles_all;
+
+  cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * (size_t)ntiles_all, ctx->stream);
+  if (NT > 0) {
+    DR_TB(ctx);
+    k_raster_setup<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(pos, V, tri, T, ranges, N, H, W, ntx,
+                                                               nty, rec, tile_count, ctx->d_err);
+    DR_LAUNCHED(ctx, "raster_setup");
+  }
+  dr_status st = scan_u32(ctx, tile_count, tile_off, ntiles_all, total);
+  if (st != DR_OK) return st;
+  // The list length is data dependent: read it back (one small sync) and size
+  // the list buffer exactly, so no candidate is ever dropped.
+  cudaMemcpyAsync(ctx->h_pinned, total, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream);
+  cudaMemcpyAsync(tile_cur, tile_off, sizeof(uint32_t) * (size_t)ntiles_all,
+                  cudaMemcpyDeviceToDevice, ctx->stream);
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return fail(ctx, DR_ECUDA, "rasterize: %s", cudaGetErrorString(e));
+  const uint32_t n_pairs = (uint32_t)ctx->h_pinned[0];
+  int32_t* list = (int32_t*)ws_get(ctx, WS_TILE_LIST, sizeof(int32_t) * (size_t)(n_pairs + 1));
+  if (!list) return DR_ENOMEM;
+  if (NT > 0 && n_pairs > 0) {
+    DR_TB(ctx);
+    k_raster_scatter<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(rec, N, T, ntx, nty, tile_cur, list);
+    DR_LAUNCHED(ctx, "raster_scatter");
+  }
+  const unsigned grid = (unsigned)ntiles_all;
+  const float4* rec_c = rec;
+  float4* r4 = reinterpret_cast<float4*>(rast);
+  float4* d4 = reinterpret_cast<float4*>(rast_db);
+  DR_TB(ctx);
+  if (peel_layer) {
+    if (rast_db)
+      k_raster_tiles<true, true><<<grid, TILE_PIX, 0, ctx->stream>>>(rec_c, T, H, W, ntx, nty, tile_off,
+                                                                      tile_count, list, peel_layer, r4, d4);
+    else
+      k_raster_tiles<true, false><<<grid, TILE_PIX, 0, ctx->stream>>>(rec_c, T, H, W, ntx, nty, tile_off,
+                                                                       tile_count, list, peel_layer, r4, d4);
+  } else {
+    if (rast_db)
+      k_raster_tiles<false, true><<<grid, TILE_PIX, 0, ctx->stream>>>(rec_c, T, H, W, ntx, nty, tile_off,
+                                                                       tile_count, list, nullptr, r4, d4);
+    else
+      k_raster_tiles<false, false><<<grid, TILE_PIX, 0, ctx->stream>>>(rec_c, T, H, W, ntx, nty, tile_off,
+                                                                        tile_count, list, nullptr, r4, d4);
+  }
+  DR_LAUNCHED(ctx, "raster_tiles");
+  return DR_OK;
+}
+
+extern "C" dr_status dr_rasterize_bwd(dr_ctx* ctx, const float* pos, int V, const int32_t* tri, int T,
+                                      const int32_t* ranges, int N, int H, int W, const float* rast,
+                                      const float* d_rast, const float* d_rast_db, float* d_pos) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, pos && tri && rast && d_rast && d_pos, "rasterize_bwd: null pointer");
+  DR_REQUIRE(ctx, N > 0 && V > 0 && T >= 0 && H > 0 && W > 0, "rasterize_bwd: bad sizes");
+  DR_REQUIRE(ctx, aligned16(pos) && aligned16(rast) && aligned16(d_rast) &&
+                      (!d_rast_db || aligned16(d_rast_db)),
+             "rasterize_bwd: pos/rast/d_rast/d_rast_db must be 16-byte aligned");
+  const bool shared_pos = ranges != nullptr;
+  const size_t npos = (size_t)(shared_pos ? 1 : N) * V * 4;
+  cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream);
+  const int64_t P = (int64_t)N * H * W;
+  const bool vec = aligned16(d_pos);
+  const float4* r4 = reinterpret_cast<const float4*>(rast);
+  const float4* g4 = reinterpret_cast<const float4*>(d_rast);
+  const float4* gd4 = reinterpret_cast<const float4*>(d_rast_db);
+  const unsigned grid = grid_for(P, 256);
+  DR_TB(ctx);
+  if (d_rast_db) {
+    if (vec) k_raster_bwd<true, true><<<grid, 256, 0, ctx->stream>>>(pos, V, tri, T, shared_pos, N, H, W, r4, g4, gd4, d_pos, ctx->d_err);
+    else k_raster_bwd<true, false><<<grid, 256, 0, ctx->stream>>>(pos, V, tri, T, shared_pos, N, H, W, r4, g4, gd4, d_pos, ctx->d_err);
+  } else {
+    if (vec) k_raster_bwd<false, true><<<grid, 256, 0, ctx->stream>>>(pos, V, tri, T, shared_pos, N, H, W, r4, g4, gd4, d_pos, ctx->d_err);
+    else k_raster_bwd<false, false><<<grid, 256, 0, ctx->stream>>>(pos, V, tri, T, shared_pos, N, H, W, r4, g4, gd4, d_pos, ctx->d_err);
+  }
+  DR_LAUNCHED(ctx, "raster_bwd");
+  return DR_OK;
+}

@@ -1,0 +1,636 @@
+// texture.cu — texture sampling forward / backward for every filter and
+// boundary mode, mip pyramid construction and the pyramid-gradient fold.
+//
+// Reference: Sources/MLXDiffRast/Texture.swift.
+//   bilinear       diffrast_texture_fwd / _grad_tex / _grad_uv  (359-521)
+//   nearest        _nearest_fwd / _nearest_grad_tex             (545-605)
+//   cube           _cube_fwd / _cube_grad_tex                   (616-738)
+//   mipmap         _trilinear_fwd / _grad_pyramid / _grad_uv / _grad_uvda
+//                  (764-1102), pyramid = textureConstructMip (144-161)
+// Each backward here is ONE kernel (d_tex scatter + d_uv + d_uvDA together)
+// instead of the reference's two or three passes.  A texture with batch 1 is
+// sampled directly (the reference broadcasts it to N copies and builds N
+// pyramids, Texture.swift:282-285); gradients accumulate into the one copy.
+// Pyramid gradients of levels >= 1 are folded into d_tex level 0 by one kernel,
+// which is what MLX's autograd of reshape/mean/concatenate computes.
+#include "common.cuh"
+
+using dr::grid_for;
+
+namespace {
+
+struct MipDesc {
+  int L;                       // number of levels, level 0 = tex
+  int h[DR_MAX_MIP_LEVELS];
+  int w[DR_MAX_MIP_LEVELS];
+  int64_t off[DR_MAX_MIP_LEVELS];  // float offset of level k (k >= 1) in the pyramid
+};
+
+MipDesc mip_desc(int Nt, int Ht, int Wt, int C, int max_level, int64_t* total) {
+  MipDesc m{};
+  m.L = 1;
+  m.h[0] = Ht; m.w[0] = Wt; m.off[0] = -1;
+  int64_t tot = 0;
+  int H = Ht, W = Wt;
+  // Texture.swift:153-159: halve while both dims are even and >= 2.
+  while (H >= 2 && W >= 2 && (H % 2) == 0 && (W % 2) == 0) {
+    if (max_level >= 0 && m.L > max_level) break;
+    if (m.L >= DR_MAX_MIP_LEVELS) break;
+    H /= 2; W /= 2;
+    m.h[m.L] = H; m.w[m.L] = W; m.off[m.L] = tot;
+    tot += (int64_t)Nt * H * W * C;
+    m.L++;
+  }
+  *total = tot;
+  return m;
+}
+
+// apply_boundary (Texture.swift:336-354).  MODE 0 wrap, 1 clamp, 2 zero.
+template <int MODE>
+__device__ __forceinline__ int apply_boundary(int t, int size, float& oob) {
+  if (MODE == 2) {
+    if (t < 0 || t >= size) { oob = 1.0f; return 0; }
+    oob = 0.0f;
+    return t;
+  }
+  oob = 0.0f;
+  if (MODE == 1) return t < 0 ? 0 : (t >= size ? size - 1 : t);
+  int r = t % size;
+  if (r < 0) r += size;
+  return r;
+}
+
+struct Taps {
+  int64_t a00, a10, a01, a11;  // texel index (times C added by caller)
+  float fx, fy;
+  float w00, w10, w01, w11;
+  float m00, m10, m01, m11;
+};
+
+// Bilinear taps with texel centres at tx = u*W - 0.5 (Texture.swift:372-391).
+template <int MODE>
+__device__ __forceinline__ Taps bilin_taps(float u, float v, int Wk, int Hk) {
+  Taps q;
+  const float tx = u * (float)Wk - 0.5f;
+  const float ty = v * (float)Hk - 0.5f;
+  const int tx0 = dr_floor_i(tx), ty0 = dr_floor_i(ty);
+  const int tx1 = (int)((unsigned)tx0 + 1u), ty1 = (int)((unsigned)ty0 + 1u);
+  q.fx = tx - (float)tx0;
+  q.fy = ty - (float)ty0;
+  float ox0, ox1, oy0, oy1;
+  const int ix0 = apply_boundary<MODE>(tx0, Wk, ox0), ix1 = apply_boundary<MODE>(tx1, Wk, ox1);
+  const int iy0 = apply_boundary<MODE>(ty0, Hk, oy0), iy1 = apply_boundary<MODE>(ty1, Hk, oy1);
+  const float fx = q.fx, fy = q.fy;
+  q.w00 = (1.0f - fx) * (1.0f - fy) * (1.0f - ox0) * (1.0f - oy0);
+  q.w10 = (fx) * (1.0f - fy) * (1.0f - ox1) * (1.0f - oy0);
+  q.w01 = (1.0f - fx) * (fy) * (1.0f - ox0) * (1.0f - oy1);
+  q.w11 = (fx) * (fy) * (1.0f - ox1) * (1.0f - oy1);
+  q.m00 = (1.0f - ox0) * (1.0f - oy0);
+  q.m10 = (1.0f - ox1) * (1.0f - oy0);
+  q.m01 = (1.0f - ox0) * (1.0f - oy1);
+  q.m11 = (1.0f - ox1) * (1.0f - oy1);
+  q.a00 = (int64_t)iy0 * Wk + ix0;
+  q.a10 = (int64_t)iy0 * Wk + ix1;
+  q.a01 = (int64_t)iy1 * Wk + ix0;
+  q.a11 = (int64_t)iy1 * Wk + ix1;
+  return q;
+}
+
+__device__ __forceinline__ float sample4(const float* __restrict__ b, const Taps& q, int C, int c) {
+  const float t00 = __ldg(b + q.a00 * C + c), t10 = __ldg(b + q.a10 * C + c);
+  const float t01 = __ldg(b + q.a01 * C + c), t11 = __ldg(b + q.a11 * C + c);
+  return q.w00 * t00 + q.w10 * t10 + q.w01 * t01 + q.w11 * t11;
+}
+
+// ---------------------------------------------------------------- bilinear
+
+template <int MODE>
+__global__ void k_tex_linear_fwd(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
+                                 const float2* __restrict__ uv, int64_t P, int64_t HWi,
+                                 float* __restrict__ out) {
+  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= P) return;
+  const float2 t = __ldg(uv + pix);
+  const Taps q = bilin_taps<MODE>(t.x, t.y, Wt, Ht);
+  const float* b = tex + (tex_shared ? 0 : (pix / HWi) * Ht * Wt * C);
+  float* o = out + pix * C;
+  for (int c = 0; c < C; ++c) o[c] = sample4(b, q, C, c);
+}
+
+// d_tex scatter (Texture.swift:407-459) and d_uv (472-521) in one pass.
+template <int MODE>
+__global__ void k_tex_linear_bwd(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
+                                 const float2* __restrict__ uv, int64_t P, int64_t HWi,
+                                 const float* __restrict__ d_out, float* __restrict__ d_tex,
+                                 float2* __restrict__ d_uv) {
+  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= P) return;
+  const float2 t = __ldg(uv + pix);
+  const Taps q = bilin_taps<MODE>(t.x, t.y, Wt, Ht);
+  const int64_t base = tex_shared ? 0 : (pix / HWi) * Ht * Wt * C;
+  const float* b = tex + base;
+  float* db = d_tex + base;
+  const float fx = q.fx, fy = q.fy;
+  float dfx_sum = 0.0f, dfy_sum = 0.0f;
+  for (int c = 0; c < C; ++c) {
+    const float g = __ldg(d_out + pix * C + c);
+    atomicAdd(db + q.a00 * C + c, q.w00 * g);
+    atomicAdd(db + q.a10 * C + c, q.w10 * g);
+    atomicAdd(db + q.a01 * C + c, q.w01 * g);
+    atomicAdd(db + q.a11 * C + c, q.w11 * g);
+    const float t00 = __ldg(b + q.a00 * C + c) * q.m00, t10 = __ldg(b + q.a10 * C + c) * q.m10;
+    const float t01 = __ldg(b + q.a01 * C + c) * q.m01, t11 = __ldg(b + q.a11 * C + c) * q.m11;
+    dfx_sum += g * ((1.0f - fy) * (t10 - t00) + fy * (t11 - t01));
+    dfy_sum += g * ((1.0f - fx) * (t01 - t00) + fx * (t11 - t10));
+  }
+  d_uv[pix] = make_float2(dfx_sum * (float)Wt, dfy_sum * (float)Ht);
+}
+
+// ----------------------------------------------------------------- nearest
+
+template <int MODE>
+__global__ void k_tex_nearest(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
+                              const float2* __restrict__ uv, int64_t P, int64_t HWi,
+                              float* __restrict__ out, const float* __restrict__ d_out,
+                              float* __restrict__ d_tex, float2* __restrict__ d_uv) {
+  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= P) return;
+  const float2 t = __ldg(uv + pix);
+  const int tx = dr_floor_i(t.x * (float)Wt), ty = dr_floor_i(t.y * (float)Ht);
+  float ox, oy;
+  const int ix = apply_boundary<MODE>(tx, Wt, ox), iy = apply_boundary<MODE>(ty, Ht, oy);
+  const float mask = (1.0f - ox) * (1.0f - oy);
+  const int64_t base = (tex_shared ? 0 : (pix / HWi) * Ht * Wt * C) + ((int64_t)iy * Wt + ix) * C;
+  if (out) {
+    for (int c = 0; c < C; ++c) out[pix * C + c] = __ldg(tex + base + c) * mask;
+  } else {
+    for (int c = 0; c < C; ++c) atomicAdd(d_tex + base + c, __ldg(d_out + pix * C + c) * mask);
+    d_uv[pix] = make_float2(0.0f, 0.0f);
+  }
+}
+
+// -------------------------------------------------------------------- cube
+
+// Cube projection (Texture.swift:616-636), face order +X,-X,+Y,-Y,+Z,-Z.
+__device__ __forceinline__ void cube_project(float x, float y, float z, int& face, float& u, float& v) {
+  const float ax = fabsf(x), ay = fabsf(y), az = fabsf(z);
+  float sc, tc, ma;
+  if (ax >= ay && ax >= az) {
+    ma = ax;
+    if (x > 0.0f) { face = 0; sc = -z; tc = -y; } else { face = 1; sc = z; tc = -y; }
+  } else if (ay >= az) {
+    ma = ay;
+    if (y > 0.0f) { face = 2; sc = x; tc = z; } else { face = 3; sc = x; tc = -z; }
+  } else {
+    ma = az;
+    if (z > 0.0f) { face = 4; sc = x; tc = -y; } else { face = 5; sc = -x; tc = -y; }
+  }
+  const float inv_ma = 1.0f / ma;
+  u = (sc * inv_ma + 1.0f) * 0.5f;
+  v = (tc * inv_ma + 1.0f) * 0.5f;
+}
+
+__global__ void k_tex_cube(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
+                           const float* __restrict__ dir, int64_t P, int64_t HWi, float* __restrict__ out,
+                           const float* __restrict__ d_out, float* __restrict__ d_tex,
+                           float* __restrict__ d_dir) {
+  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= P) return;
+  const float x = __ldg(dir + 3 * pix), y = __ldg(dir + 3 * pix + 1), z = __ldg(dir + 3 * pix + 2);
+  int face;
+  float u, v;
+  cube_project(x, y, z, face, u, v);
+  // Per-face clamp bilinear (Texture.swift:656-672): weights carry no OOB mask.
+  Taps q = bilin_taps<1>(u, v, Wt, Ht);
+  const float fx = q.fx, fy = q.fy;
+  const float w00 = (1.0f - fx) * (1.0f - fy), w10 = fx * (1.0f - fy);
+  const float w01 = (1.0f - fx) * fy, w11 = fx * fy;
+  const int64_t fb = ((tex_shared ? 0 : (pix / HWi)) * 6 + face) * (int64_t)Ht * Wt * C;
+  if (out) {
+    for (int c = 0; c < C; ++c) {
+      const float t00 = __ldg(tex + fb + q.a00 * C + c), t10 = __ldg(tex + fb + q.a10 * C + c);
+      const float t01 = __ldg(tex + fb + q.a01 * C + c), t11 = __ldg(tex + fb + q.a11 * C + c);
+      out[pix * C + c] = w00 * t00 + w10 * t10 + w01 * t01 + w11 * t11;
+    }
+  } else {
+    for (int c = 0; c < C; ++c) {
+      const float g = __ldg(d_out + pix * C + c);
+      atomicAdd(d_tex + fb + q.a00 * C + c, w00 * g);
+      atomicAdd(d_tex + fb + q.a10 * C + c, w10 * g);
+      atomicAdd(d_tex + fb + q.a01 * C + c, w01 * g);
+      atomicAdd(d_tex + fb + q.a11 * C + c, w11 * g);
+    }
+    // d_dir is identically zero in the reference (Texture.swift:196-197).
+    d_dir[3 * pix] = 0.0f; d_dir[3 * pix + 1] = 0.0f; d_dir[3 * pix + 2] = 0.0f;
+  }
+}
+
+// ------------------------------------------------------------------ mipmap
+
+// 2x2 box filter of one level: ((t00 + t01) + (t10 + t11)) / 4.
+__global__ void k_mip_down(const float* __restrict__ src, int Hs, int Ws, float* __restrict__ dst, int Hd,
+                           int Wd, int C, int64_t n_out) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_out) return;
+  const int c = (int)(i % C);
+  const int x = (int)((i / C) % Wd);
+  const int64_t ny = i / ((int64_t)C * Wd);  // n * Hd + y
+  const int y = (int)(ny % Hd);
+  const int64_t n = ny / Hd;
+  const float* s = src + n * Hs * Ws * C;
+  const float a = __ldg(s + ((int64_t)(2 * y) * Ws + 2 * x) * C + c);
+  const float b = __ldg(s + ((int64_t)(2 * y) * Ws + 2 * x + 1) * C + c);
+  const float cc = __ldg(s + ((int64_t)(2 * y + 1) * Ws + 2 * x) * C + c);
+  const float d = __ldg(s + ((int64_t)(2 * y + 1) * Ws + 2 * x + 1) * C + c);
+  dst[i] = ((a + b) + (cc + d)) * 0.25f;
+}
+
+// Effective uvDA = uvDA * 2^map * 2^bias (Texture.swift:104-126).
+__device__ __forceinline__ float4 effective_da(const float4 da, int64_t pix, float bias,
+                                               const float* __restrict__ bias_map, float& s) {
+  s = 1.0f;
+  bool scaled = false;
+  if (bias_map) {
+    s = exp2f(__ldg(bias_map + pix));
+    if (bias != 0.0f) s = s * exp2f(bias);
+    scaled = true;
+  } else if (bias != 0.0f) {
+    s = exp2f(bias);
+    scaled = true;
+  }
+  if (!scaled) return da;
+  return make_float4(da.x * s, da.y * s, da.z * s, da.w * s);
+}
+
+struct LodSel {
+  int k0, k1;
+  float frac;
+};
+
+// Texture.swift:764-790.
+template <bool MIP_LINEAR>
+__device__ __forceinline__ LodSel lod_select(const float4 e, int Ht, int Wt, int L) {
+  const float sx = e.x * (float)Wt, sy = e.y * (float)Wt;
+  const float tx = e.z * (float)Ht, ty = e.w * (float)Ht;
+  const float rho_sq = fmaxf(sx * sx + tx * tx, sy * sy + ty * ty);
+  float lod = 0.5f * log2f(fmaxf(rho_sq, 1e-20f));
+  lod = fmaxf(0.0f, fminf((float)(L - 1), lod));
+  LodSel s;
+  if (MIP_LINEAR) {
+    s.k0 = dr_floor_i(lod);
+    s.k1 = s.k0 + 1;
+    if (s.k1 >= L) s.k1 = L - 1;
+    s.frac = lod - (float)s.k0;
+  } else {
+    s.k0 = dr_floor_i(lod + 0.5f);
+    if (s.k0 >= L) s.k0 = L - 1;
+    s.k1 = s.k0;
+    s.frac = 0.0f;
+  }
+  return s;
+}
+
+__device__ __forceinline__ const float* level_ptr(const float* tex, const float* pyr, const MipDesc& m, int k,
+                                                  int64_t nt, int C) {
+  const float* b = (k == 0) ? tex : pyr + m.off[k];
+  return b + nt * (int64_t)m.h[k] * m.w[k] * C;
+}
+
+template <int MODE, bool MIP_LINEAR>
+__global__ void k_tex_mip_fwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+                              bool tex_shared, int C, const float2* __restrict__ uv,
+                              const float4* __restrict__ uv_da, float bias, const float* __restrict__ bias_map,
+                              int64_t P, int64_t HWi, float* __restrict__ out) {
+  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= P) return;
+  const int64_t nt = tex_shared ? 0 : pix / HWi;
+  float s;
+  const float4 e = effective_da(__ldg(uv_da + pix), pix, bias, bias_map, s);
+  const LodSel ls = lod_select<MIP_LINEAR>(e, m.h[0], m.w[0], m.L);
+  const float2 t = __ldg(uv + pix);
+  const Taps q0 = bilin_taps<MODE>(t.x, t.y, m.w[ls.k0], m.h[ls.k0]);
+  const Taps q1 = bilin_taps<MODE>(t.x, t.y, m.w[ls.k1], m.h[ls.k1]);
+  const float* b0 = level_ptr(tex, pyr, m, ls.k0, nt, C);
+  const float* b1 = level_ptr(tex, pyr, m, ls.k1, nt, C);
+  float* o = out + pix * C;
+  for (int c = 0; c < C; ++c) {
+    // out = (1-frac)*s0, then += frac*s1 (Texture.swift:853-859)
+    const float o0 = (1.0f - ls.frac) * sample4(b0, q0, C, c);
+    o[c] = o0 + ls.frac * sample4(b1, q1, C, c);
+  }
+}
+
+// Fused mipmap VJP: d_tex / d_pyramid scatter (K20), d_uv (K21), d_uvDA (K22)
+// and the optional gradient of the bias map.
+template <int MODE, bool MIP_LINEAR>
+__global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+                              bool tex_shared, int C, const float2* __restrict__ uv,
+                              const float4* __restrict__ uv_da, float bias, const float* __restrict__ bias_map,
+                              int64_t P, int64_t HWi, const float* __restrict__ d_out,
+                              float* __restrict__ d_tex, float* __restrict__ d_pyr, float2* __restrict__ d_uv,
+                              float4* __restrict__ d_uv_da, float* __restrict__ d_bias_map) {
+  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= P) return;
+  const int64_t nt = tex_shared ? 0 : pix / HWi;
+  float s;
+  const float4 e = effective_da(__ldg(uv_da + pix), pix, bias, bias_map, s);
+  const int Ht = m.h[0], Wt = m.w[0], L = m.L;
+  const LodSel ls = lod_select<MIP_LINEAR>(e, Ht, Wt, L);
+  const float2 t = __ldg(uv + pix);
+  const float* g = d_out + pix * C;
+  float dfx_total = 0.0f, dfy_total = 0.0f;
+#pragma unroll
+  for (int li = 0; li < 2; ++li) {
+    const int k = li == 0 ? ls.k0 : ls.k1;
+    const float scale = li == 0 ? (1.0f - ls.frac) : ls.frac;
+    const Taps q = bilin_taps<MODE>(t.x, t.y, m.w[k], m.h[k]);
+    const float* b = level_ptr(tex, pyr, m, k, nt, C);
+    float* db = (k == 0 ? d_tex : d_pyr + m.off[k]) + nt * (int64_t)m.h[k] * m.w[k] * C;
+    float dfx = 0.0f, dfy = 0.0f;
+    const float fx = q.fx, fy = q.fy;
+    for (int c = 0; c < C; ++c) {
+      const float gc = __ldg(g + c) * scale;
+      if (gc != 0.0f) {
+        atomicAdd(db + q.a00 * C + c, q.w00 * gc);
+        atomicAdd(db + q.a10 * C + c, q.w10 * gc);
+        atomicAdd(db + q.a01 * C + c, q.w01 * gc);
+        atomicAdd(db + q.a11 * C + c, q.w11 * gc);
+      }
+      const float t00 = __ldg(b + q.a00 * C + c) * q.m00, t10 = __ldg(b + q.a10 * C + c) * q.m10;
+      const float t01 = __ldg(b + q.a01 * C + c) * q.m01, t11 = __ldg(b + q.a11 * C + c) * q.m11;
+      dfx += gc * ((1.0f - fy) * (t10 - t00) + fy * (t11 - t01));
+      dfy += gc * ((1.0f - fx) * (t01 - t00) + fx * (t11 - t10));
+    }
+    dfx_total += dfx * (float)m.w[k];
+    dfy_total += dfy * (float)m.h[k];
+  }
+  d_uv[pix] = make_float2(dfx_total, dfy_total);
+
+  if (!d_uv_da && !d_bias_map) return;
+  // K22 (Texture.swift:1011-1102): independent of MIP_LINEAR.
+  const float sx = e.x * (float)Wt, sy = e.y * (float)Wt;
+  const float tx_ = e.z * (float)Ht, ty_ = e.w * (float)Ht;
+  const float Asq = sx * sx + tx_ * tx_, Bsq = sy * sy + ty_ * ty_;
+  const float rho_sq = fmaxf(Asq, Bsq);
+  const float lod_raw = 0.5f * log2f(fmaxf(rho_sq, 1e-20f));
+  float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (!(lod_raw <= 0.0f || lod_raw >= (float)(L - 1))) {
+    const int k0 = dr_floor_i(lod_raw);
+    int k1 = k0 + 1;
+    if (k1 >= L) k1 = L - 1;
+    float d_lod = 0.0f;
+    for (int li = 0; li < 2; ++li) {
+      const int k = li == 0 ? k0 : k1;
+      const float sign = li == 0 ? -1.0f : 1.0f;
+      const Taps q = bilin_taps<MODE>(t.x, t.y, m.w[k], m.h[k]);
+      const float* b = level_ptr(tex, pyr, m, k, nt, C);
+      for (int c = 0; c < C; ++c) d_lod += sign * sample4(b, q, C, c) * __ldg(g + c);
+    }
+    const float ln2 = 0.6931471805599453f;
+    const float dlod_drho_sq = 1.0f / (2.0f * rho_sq * ln2);
+    const float A_is_max = (Asq >= Bsq) ? 1.0f : 0.0f;
+    const float B_is_max = 1.0f - A_is_max;
+    g4.x = d_lod * dlod_drho_sq * A_is_max * 2.0f * sx * (float)Wt;
+    g4.y = d_lod * dlod_drho_sq * B_is_max * 2.0f * sy * (float)Wt;
+    g4.z = d_lod * dlod_drho_sq * A_is_max * 2.0f * tx_ * (float)Ht;
+    g4.w = d_lod * dlod_drho_sq * B_is_max * 2.0f * ty_ * (float)Ht;
+  }
+  // Backward of eff = uvDA * s: d_uvDA = g * s, d_map = ln2 * sum(g * eff).
+  if (d_uv_da) d_uv_da[pix] = make_float4(g4.x * s, g4.y * s, g4.z * s, g4.w * s);
+  if (d_bias_map) {
+    const float acc = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
+    d_bias_map[pix] = bias_map ? acc * 0.6931471805599453f : 0.0f;
+  }
+}
+
+// d_tex[level 0] += sum_k d_pyr_k[y >> k, x >> k] / 4^k: the adjoint of the
+// 2x2 mean pyramid, evaluated in one pass over level 0.
+__global__ void k_mip_fold(float* __restrict__ d_tex, const float* __restrict__ d_pyr, const MipDesc m, int C,
+                           int64_t n0) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n0) return;
+  const int c = (int)(i % C);
+  const int x = (int)((i / C) % m.w[0]);
+  const int64_t ny = i / ((int64_t)C * m.w[0]);
+  const int y = (int)(ny % m.h[0]);
+  const int64_t n = ny / m.h[0];
+  float acc = 0.0f, w = 1.0f;
+  for (int k = 1; k < m.L; ++k) {
+    w *= 0.25f;
+    const float* lk = d_pyr + m.off[k] + n * (int64_t)m.h[k] * m.w[k] * C;
+    acc += w * __ldg(lk + ((int64_t)(y >> k) * m.w[k] + (x >> k)) * C + c);
+  }
+  d_tex[i] += acc;
+}
+
+inline bool aligned(const void* p, unsigned a) { return ((uintptr_t)p & (a - 1)) == 0; }
+
+dr_status build_pyramid(dr_ctx* ctx, const float* tex, int Nt, int C, const MipDesc& m, float* pyr) {
+  for (int k = 1; k < m.L; ++k) {
+    const float* src = (k == 1) ? tex : pyr + m.off[k - 1];
+    const int64_t n_out = (int64_t)Nt * m.h[k] * m.w[k] * C;
+    DR_TB(ctx);
+    k_mip_down<<<grid_for(n_out, 256), 256, 0, ctx->stream>>>(src, m.h[k - 1], m.w[k - 1], pyr + m.off[k],
+                                                               m.h[k], m.w[k], C, n_out);
+    DR_LAUNCHED(ctx, "mip_down");
+  }
+  return DR_OK;
+}
+
+struct TexArgs {
+  bool cube, mip, mip_linear;
+  int64_t P, HWi;
+  MipDesc m;
+  int64_t pyr_floats;
+};
+
+dr_status check_tex(dr_ctx* ctx, int filter, int boundary, const float* tex, int Nt, int Ht, int Wt, int C,
+                    int max_level, const float* uv, const float* uv_da, int N, int Hi, int Wi, TexArgs& a) {
+  DR_REQUIRE(ctx, tex && uv, "texture: tex and uv are required");
+  DR_REQUIRE(ctx, filter >= 0 && filter <= 3, "texture: bad filter mode %d", filter);
+  DR_REQUIRE(ctx, boundary >= 0 && boundary <= 3, "texture: bad boundary mode %d", boundary);
+  DR_REQUIRE(ctx, Nt > 0 && Ht > 0 && Wt > 0 && C > 0 && N > 0 && Hi > 0 && Wi > 0, "texture: bad sizes");
+  DR_REQUIRE(ctx, Nt == 1 || Nt == N, "texture: tex batch dim %d incompatible with uv batch %d", Nt, N);
+  a.cube = boundary == DR_BOUNDARY_CUBE;
+  if (a.cube)
+    DR_REQUIRE(ctx, filter == DR_FILTER_LINEAR, "texture: cube textures currently support filterMode .linear only");
+  a.mip = filter == DR_FILTER_LINEAR_MIPMAP_NEAREST || filter == DR_FILTER_LINEAR_MIPMAP_LINEAR;
+  a.mip_linear = filter == DR_FILTER_LINEAR_MIPMAP_LINEAR;
+  if (a.mip) {
+    DR_REQUIRE(ctx, uv_da != nullptr, "texture: mipmap filterModes require uvDA");
+    DR_REQUIRE(ctx, aligned(uv_da, 16), "texture: uvDA must be 16-byte aligned");
+  }
+  if (!a.cube) DR_REQUIRE(ctx, aligned(uv, 8), "texture: uv must be 8-byte aligned");
+  a.P = (int64_t)N * Hi * Wi;
+  a.HWi = (int64_t)Hi * Wi;
+  a.m = mip_desc(Nt, Ht, Wt, C, a.mip ? max_level : 0, &a.pyr_floats);
+  return DR_OK;
+}
+
+}  // namespace
+
+using namespace dr;
+
+extern "C" dr_status dr_texture_mip_layout(int Nt, int Ht, int Wt, int C, int max_level, int* num_levels,
+                                           int64_t* level_offset, int* level_h, int* level_w,
+                                           int64_t* pyramid_floats) {
+  if (Nt <= 0 || Ht <= 0 || Wt <= 0 || C <= 0 || !num_levels) return DR_EINVAL;
+  int64_t tot;
+  MipDesc m = mip_desc(Nt, Ht, Wt, C, max_level, &tot);
+  *num_levels = m.L;
+  for (int k = 0; k < m.L; ++k) {
+    if (level_offset) level_offset[k] = m.off[k];
+    if (level_h) level_h[k] = m.h[k];
+    if (level_w) level_w[k] = m.w[k];
+  }
+  if (pyramid_floats) *pyramid_floats = tot;
+  return DR_OK;
+}
+
+extern "C" dr_status dr_texture_construct_mip(dr_ctx* ctx, const float* tex, int Nt, int Ht, int Wt, int C,
+                                              int max_level, float* pyramid) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, tex && Nt > 0 && Ht > 0 && Wt > 0 && C > 0, "textureConstructMip: bad arguments");
+  int64_t tot;
+  MipDesc m = mip_desc(Nt, Ht, Wt, C, max_level, &tot);
+  if (m.L > 1) DR_REQUIRE(ctx, pyramid != nullptr, "textureConstructMip: pyramid buffer required");
+  return build_pyramid(ctx, tex, Nt, C, m, pyramid);
+}
+
+#define DR_MODE_SWITCH(MODE_VAR, ...)                 \
+  switch (MODE_VAR) {                                 \
+    case 0: { constexpr int MODE = 0; __VA_ARGS__; } break; \
+    case 1: { constexpr int MODE = 1; __VA_ARGS__; } break; \
+    default: { constexpr int MODE = 2; __VA_ARGS__; } break; \
+  }
+
+extern "C" dr_status dr_texture_fwd(dr_ctx* ctx, int filter, int boundary, const float* tex, int Nt, int Ht,
+                                    int Wt, int C, const float* pyramid, int max_level, const float* uv,
+                                    const float* uv_da, float mip_level_bias, const float* mip_level_bias_map,
+                                    int N, int Hi, int Wi, float* out) {
+  DR_ENTER(ctx);
+  TexArgs a;
+  dr_status st = check_tex(ctx, filter, boundary, tex, Nt, Ht, Wt, C, max_level, uv, uv_da, N, Hi, Wi, a);
+  if (st != DR_OK) return st;
+  DR_REQUIRE(ctx, out, "texture: out required");
+  const unsigned grid = grid_for(a.P, 256);
+  const bool shared = Nt == 1;
+  if (a.cube) {
+    DR_TB(ctx);
+    k_tex_cube<<<grid, 256, 0, ctx->stream>>>(tex, shared, Ht, Wt, C, uv, a.P, a.HWi, out, nullptr, nullptr,
+                                              nullptr);
+    DR_LAUNCHED(ctx, "tex_cube_fwd");
+    return DR_OK;
+  }
+  const float2* uv2 = reinterpret_cast<const float2*>(uv);
+  if (filter == DR_FILTER_NEAREST) {
+    DR_TB(ctx);
+    DR_MODE_SWITCH(boundary, (k_tex_nearest<MODE><<<grid, 256, 0, ctx->stream>>>(
+                                 tex, shared, Ht, Wt, C, uv2, a.P, a.HWi, out, nullptr, nullptr, nullptr)));
+    DR_LAUNCHED(ctx, "tex_nearest_fwd");
+    return DR_OK;
+  }
+  if (filter == DR_FILTER_LINEAR) {
+    DR_TB(ctx);
+    DR_MODE_SWITCH(boundary, (k_tex_linear_fwd<MODE><<<grid, 256, 0, ctx->stream>>>(tex, shared, Ht, Wt, C,
+                                                                                    uv2, a.P, a.HWi, out)));
+    DR_LAUNCHED(ctx, "tex_linear_fwd");
+    return DR_OK;
+  }
+  const float* pyr = pyramid;
+  if (!pyr && a.m.L > 1) {
+    float* w = (float*)ws_get(ctx, WS_MIP, sizeof(float) * (size_t)a.pyr_floats);
+    if (!w) return DR_ENOMEM;
+    st = build_pyramid(ctx, tex, Nt, C, a.m, w);
+    if (st != DR_OK) return st;
+    pyr = w;
+  }
+  const float4* da4 = reinterpret_cast<const float4*>(uv_da);
+  DR_TB(ctx);
+  if (a.mip_linear) {
+    DR_MODE_SWITCH(boundary, (k_tex_mip_fwd<MODE, true><<<grid, 256, 0, ctx->stream>>>(
+                                 tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P,
+                                 a.HWi, out)));
+  } else {
+    DR_MODE_SWITCH(boundary, (k_tex_mip_fwd<MODE, false><<<grid, 256, 0, ctx->stream>>>(
+                                 tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P,
+                                 a.HWi, out)));
+  }
+  DR_LAUNCHED(ctx, "tex_mip_fwd");
+  return DR_OK;
+}
+
+extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const float* tex, int Nt, int Ht,
+                                    int Wt, int C, const float* pyramid, int max_level, const float* uv,
+                                    const float* uv_da, float mip_level_bias, const float* mip_level_bias_map,
+                                    int N, int Hi, int Wi, const float* d_out, float* d_tex, float* d_uv,
+                                    float* d_uv_da, float* d_bias_map) {
+  DR_ENTER(ctx);
+  TexArgs a;
+  dr_status st = check_tex(ctx, filter, boundary, tex, Nt, Ht, Wt, C, max_level, uv, uv_da, N, Hi, Wi, a);
+  if (st != DR_OK) return st;
+  DR_REQUIRE(ctx, d_out && d_tex && d_uv, "texture_bwd: d_out, d_tex and d_uv are required");
+  if (d_uv_da) DR_REQUIRE(ctx, aligned(d_uv_da, 16), "texture_bwd: d_uv_da must be 16-byte aligned");
+  const unsigned grid = grid_for(a.P, 256);
+  const bool shared = Nt == 1;
+  const int64_t n_tex = (int64_t)Nt * (a.cube ? 6 : 1) * Ht * Wt * C;
+  cudaMemsetAsync(d_tex, 0, sizeof(float) * (size_t)n_tex, ctx->stream);
+  if (a.cube) {
+    DR_TB(ctx);
+    k_tex_cube<<<grid, 256, 0, ctx->stream>>>(tex, shared, Ht, Wt, C, uv, a.P, a.HWi, nullptr, d_out, d_tex,
+                                              d_uv);
+    DR_LAUNCHED(ctx, "tex_cube_bwd");
+    return DR_OK;
+  }
+  const float2* uv2 = reinterpret_cast<const float2*>(uv);
+  float2* duv2 = reinterpret_cast<float2*>(d_uv);
+  DR_REQUIRE(ctx, aligned(d_uv, 8), "texture_bwd: d_uv must be 8-byte aligned");
+  if (filter == DR_FILTER_NEAREST) {
+    DR_TB(ctx);
+    DR_MODE_SWITCH(boundary, (k_tex_nearest<MODE><<<grid, 256, 0, ctx->stream>>>(
+                                 tex, shared, Ht, Wt, C, uv2, a.P, a.HWi, nullptr, d_out, d_tex, duv2)));
+    DR_LAUNCHED(ctx, "tex_nearest_bwd");
+    return DR_OK;
+  }
+  if (filter == DR_FILTER_LINEAR) {
+    DR_TB(ctx);
+    DR_MODE_SWITCH(boundary, (k_tex_linear_bwd<MODE><<<grid, 256, 0, ctx->stream>>>(
+                                 tex, shared, Ht, Wt, C, uv2, a.P, a.HWi, d_out, d_tex, duv2)));
+    DR_LAUNCHED(ctx, "tex_linear_bwd");
+    return DR_OK;
+  }
+  const float* pyr = pyramid;
+  if (!pyr && a.m.L > 1) {
+    float* w = (float*)ws_get(ctx, WS_MIP, sizeof(float) * (size_t)a.pyr_floats);
+    if (!w) return DR_ENOMEM;
+    st = build_pyramid(ctx, tex, Nt, C, a.m, w);
+    if (st != DR_OK) return st;
+    pyr = w;
+  }
+  float* dpyr = nullptr;
+  if (a.m.L > 1) {
+    dpyr = (float*)ws_get(ctx, WS_DMIP, sizeof(float) * (size_t)a.pyr_floats);
+    if (!dpyr) return DR_ENOMEM;
+    cudaMemsetAsync(dpyr, 0, sizeof(float) * (size_t)a.pyr_floats, ctx->stream);
+  }
+  const float4* da4 = reinterpret_cast<const float4*>(uv_da);
+  float4* dda4 = reinterpret_cast<float4*>(d_uv_da);
+  DR_TB(ctx);
+  if (a.mip_linear) {
+    DR_MODE_SWITCH(boundary, (k_tex_mip_bwd<MODE, true><<<grid, 256, 0, ctx->stream>>>(
+                                 tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P,
+                                 a.HWi, d_out, d_tex, dpyr, duv2, dda4, d_bias_map)));
+  } else {
+    DR_MODE_SWITCH(boundary, (k_tex_mip_bwd<MODE, false><<<grid, 256, 0, ctx->stream>>>(
+                                 tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P,
+                                 a.HWi, d_out, d_tex, dpyr, duv2, dda4, d_bias_map)));
+  }
+  DR_LAUNCHED(ctx, "tex_mip_bwd");
+  if (a.m.L > 1) {
+    const int64_t n0 = (int64_t)Nt * Ht * Wt * C;
+    DR_TB(ctx);
+    k_mip_fold<<<grid_for(n0, 256), 256, 0, ctx->stream>>>(d_tex, dpyr, a.m, C, n0);
+    DR_LAUNCHED(ctx, "mip_fold");
+  }
+  return DR_OK;
+}

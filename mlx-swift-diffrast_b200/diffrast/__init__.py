@@ -1,0 +1,29 @@
+"""diffrast — B200-native differentiable rasterization (rasterize -> interpolate ->
+texture -> antialias, each with an explicit VJP), the drop-in for
+mlx-swift-diffrast's `DiffRast.*` operators.
+
+All compute runs in libdiffrast.so (hand-written sm_100a CUDA behind the C ABI
+of include/diffrast.h); this package binds it for torch tensors.
+"""
+from ._lib import DiffRastError, launch_count, sync, workspace_bytes  # noqa: F401
+from .ops import (  # noqa: F401
+    BoundaryMode,
+    DiffAttrs,
+    FilterMode,
+    antialias,
+    antialias_construct_topology_hash,
+    antialiasConstructTopologyHash,
+    interpolate,
+    mse_loss,
+    rasterize,
+    texture,
+    texture_construct_mip,
+    textureConstructMip,
+)
+
+__all__ = [
+    "BoundaryMode", "DiffAttrs", "FilterMode", "DiffRastError",
+    "rasterize", "interpolate", "texture", "texture_construct_mip", "textureConstructMip",
+    "antialias_construct_topology_hash", "antialiasConstructTopologyHash", "antialias",
+    "mse_loss", "launch_count", "sync", "workspace_bytes",
+]

@@ -1,0 +1,482 @@
+"""The DiffRast operator surface over libdiffrast's C ABI, for torch tensors.
+
+Each op mirrors the Swift `DiffRast.*` function of mlx-swift-diffrast
+(Sources/MLXDiffRast/*.swift): same argument names and meaning, same layouts
+and conventions, same `precondition` checks (raised here as ValueError /
+DiffRastError).  Forward and VJP are the explicit dr_*_fwd / dr_*_bwd pairs of
+include/diffrast.h, bound into torch.autograd.Function; torch provides device
+memory and the stream, every FLOP runs in the CUDA library.
+
+Two small differences from the reference's host glue, both about avoiding work:
+  * rasterize's VJP reuses the forward's rast instead of re-rasterizing
+    (Rasterize.swift:109-116 re-runs the forward because MLX does not cache it);
+  * broadcast inputs (attr [V,A] / [1,V,A], a batch-1 texture, range-mode pos)
+    are read and accumulated in place instead of materialising N copies.
+"""
+from __future__ import annotations
+
+import enum
+from typing import Optional, Sequence, Union
+
+import torch
+
+from . import _lib as L
+
+
+class BoundaryMode(enum.IntEnum):
+    """DiffRast.BoundaryMode (Texture.swift:8-17)."""
+    wrap = 0
+    clamp = 1
+    zero = 2
+    cube = 3
+
+
+class FilterMode(enum.IntEnum):
+    """DiffRast.FilterMode (Texture.swift:35-40)."""
+    nearest = 0
+    linear = 1
+    linearMipmapNearest = 2
+    linearMipmapLinear = 3
+
+
+class DiffAttrs:
+    """DiffRast.DiffAttrs (Interpolate.swift:15-18): `.all` or `.indices([...])`."""
+
+    def __init__(self, indices: Optional[Sequence[int]] = None):
+        self._indices = None if indices is None else [int(i) for i in indices]
+
+    @classmethod
+    def indices(cls, idx: Sequence[int]) -> "DiffAttrs":
+        return cls(list(idx))
+
+    @property
+    def is_all(self) -> bool:
+        return self._indices is None
+
+    def resolve(self, A: int):
+        if self._indices is None:
+            return None, A
+        if len(self._indices) == 0:
+            raise ValueError("interpolate: diffAttrs.indices must be non-empty")
+        if not all(0 <= i < A for i in self._indices):
+            raise ValueError(f"interpolate: diffAttrs.indices values must be in [0, A) (A={A})")
+        return list(self._indices), len(self._indices)
+
+    def __eq__(self, o):
+        return isinstance(o, DiffAttrs) and self._indices == o._indices
+
+    def __repr__(self):
+        return "DiffAttrs.all" if self._indices is None else f"DiffAttrs.indices({self._indices})"
+
+
+DiffAttrs.all = DiffAttrs(None)
+
+
+def _as_diff(d) -> Optional[DiffAttrs]:
+    if d is None or isinstance(d, DiffAttrs):
+        return d
+    if isinstance(d, str):
+        if d == "all":
+            return DiffAttrs.all
+        raise ValueError(f"unknown diffAttrs {d!r}")
+    return DiffAttrs.indices(d)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _f32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the library has no CPU path)")
+    t = t.detach() if t.requires_grad else t
+    if t.dtype != torch.float32:
+        t = t.float()
+    return t.contiguous()
+
+
+def _i32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the library has no CPU path)")
+    if t.dtype != torch.int32:
+        t = t.to(torch.int32)
+    return t.contiguous()
+
+
+def _ctx(t: torch.Tensor):
+    dev = t.device.index if t.device.index is not None else torch.cuda.current_device()
+    c = L.ctx_for(dev)
+    L.lib().dr_ctx_set_stream(c, torch.cuda.current_stream(dev).cuda_stream)
+    return c
+
+
+# --------------------------------------------------------------- rasterize
+
+class _Rasterize(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pos, tri, ranges, peel, H, W, grad_db):
+        posc = _f32(pos, "pos")
+        if ranges is not None:
+            N, V = ranges.shape[0], posc.shape[0]
+        else:
+            N, V = posc.shape[0], posc.shape[1]
+        T = tri.shape[0]
+        rast = torch.empty((N, H, W, 4), device=posc.device, dtype=torch.float32)
+        db = torch.empty((N, H, W, 4), device=posc.device, dtype=torch.float32) if grad_db else None
+        c = _ctx(posc)
+        L.check(L.lib().dr_rasterize_fwd(c, _ptr(posc), V, _ptr(tri), T, _ptr(ranges), N, H, W,
+                                         _ptr(peel), _ptr(rast), _ptr(db)), c, "rasterize")
+        ctx.save_for_backward(posc, tri, ranges, rast)
+        ctx.dims = (N, V, T, H, W, grad_db)
+        if db is None:
+            db = torch.zeros((N, H, W, 0), device=posc.device, dtype=torch.float32)
+        return rast, db
+
+    @staticmethod
+    def backward(ctx, d_rast, d_db):
+        posc, tri, ranges, rast = ctx.saved_tensors
+        N, V, T, H, W, grad_db = ctx.dims
+        if d_rast is None:
+            d_rast = torch.zeros_like(rast)
+        d_rast = d_rast.contiguous().float()
+        d_db = d_db.contiguous().float() if (grad_db and d_db is not None) else None
+        d_pos = torch.empty_like(posc)
+        c = _ctx(posc)
+        L.check(L.lib().dr_rasterize_bwd(c, _ptr(posc), V, _ptr(tri), T, _ptr(ranges), N, H, W,
+                                         _ptr(rast), _ptr(d_rast), _ptr(d_db), _ptr(d_pos)),
+                c, "rasterize_bwd")
+        return d_pos, None, None, None, None, None, None
+
+
+def rasterize(pos: torch.Tensor, tri: torch.Tensor, resolution, grad_db: bool = True,
+              ranges: Optional[torch.Tensor] = None, peel_layer: Optional[torch.Tensor] = None):
+    """DiffRast.rasterize (Rasterize.swift:44-144) -> (rast, rast_db).
+
+    Instanced mode: pos [N, V, 4].  Range mode: pos [V, 4] and ranges [N, 2]
+    int32 (start, count).  rast_db is [N, H, W, 0] when grad_db is False.
+    """
+    if tri.dim() != 2 or tri.shape[1] != 3:
+        raise ValueError(f"rasterize: tri must be [T, 3] (got {tuple(tri.shape)})")
+    H, W = int(resolution[0]), int(resolution[1])
+    if ranges is not None:
+        if pos.dim() != 2 or pos.shape[1] != 4:
+            raise ValueError(f"rasterize: with `ranges`, pos must be [V, 4] (got {tuple(pos.shape)})")
+        if ranges.dim() != 2 or ranges.shape[1] != 2:
+            raise ValueError(f"rasterize: ranges must be [N, 2] (got {tuple(ranges.shape)})")
+        ranges = _i32(ranges, "ranges")
+        N = ranges.shape[0]
+    else:
+        if pos.dim() != 3 or pos.shape[2] != 4:
+            raise ValueError(f"rasterize: pos must be [N, V, 4] (got {tuple(pos.shape)})")
+        N = pos.shape[0]
+    if peel_layer is not None:
+        if tuple(peel_layer.shape) != (N, H, W, 4):
+            raise ValueError("rasterize: peelLayer must match rast shape [N, H, W, 4] "
+                             f"(got {tuple(peel_layer.shape)})")
+        peel_layer = _f32(peel_layer, "peel_layer")
+    return _Rasterize.apply(pos, _i32(tri, "tri"), ranges, peel_layer, H, W, bool(grad_db))
+
+
+# ------------------------------------------------------------- interpolate
+
+class _Interpolate(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, attr, rast, rast_db, tri, idx, K):
+        attr_c = _f32(attr, "attr")
+        a3 = attr_c if attr_c.dim() == 3 else attr_c.unsqueeze(0)
+        rast_c = _f32(rast, "rast")
+        db_c = _f32(rast_db, "rast_db") if K > 0 else None
+        N, H, W = rast_c.shape[:3]
+        Na, V, A = a3.shape
+        out = torch.empty((N, H, W, A), device=rast_c.device, dtype=torch.float32)
+        out_da = torch.empty((N, H, W, 2 * K), device=rast_c.device, dtype=torch.float32)
+        arr = (ctypes_int_array(idx) if idx is not None else None)
+        c = _ctx(rast_c)
+        L.check(L.lib().dr_interpolate_fwd(c, _ptr(a3), Na, V, A, _ptr(rast_c), N, H, W, _ptr(tri),
+                                           tri.shape[0], _ptr(db_c), arr, K, _ptr(out),
+                                           _ptr(out_da) if K > 0 else None), c, "interpolate")
+        ctx.save_for_backward(a3, rast_c, db_c, tri)
+        ctx.meta = (idx, K, tuple(attr.shape))
+        return out, out_da
+
+    @staticmethod
+    def backward(ctx, d_out, d_out_da):
+        a3, rast_c, db_c, tri = ctx.saved_tensors
+        idx, K, attr_shape = ctx.meta
+        N, H, W = rast_c.shape[:3]
+        Na, V, A = a3.shape
+        d_out = torch.zeros((N, H, W, A), device=rast_c.device) if d_out is None else d_out.contiguous().float()
+        if K > 0 and d_out_da is None:
+            # out_da did not reach the loss: its cotangent is zero, so the DA
+            # terms of every gradient vanish; run the plain VJP.
+            K, idx = 0, None
+        d_out_da = d_out_da.contiguous().float() if K > 0 else None
+        d_attr = torch.empty_like(a3)
+        d_rast = torch.empty_like(rast_c)
+        d_db = torch.empty_like(rast_c) if K > 0 else None
+        arr = (ctypes_int_array(idx) if idx is not None else None)
+        c = _ctx(rast_c)
+        L.check(L.lib().dr_interpolate_bwd(c, _ptr(a3), Na, V, A, _ptr(rast_c), N, H, W, _ptr(tri),
+                                           tri.shape[0], _ptr(db_c), arr, K, _ptr(d_out),
+                                           _ptr(d_out_da), _ptr(d_attr), _ptr(d_rast), _ptr(d_db)),
+                c, "interpolate_bwd")
+        return d_attr.reshape(attr_shape), d_rast, d_db, None, None, None
+
+
+def ctypes_int_array(values):
+    import ctypes
+    arr = (ctypes.c_int * len(values))(*values)
+    return ctypes.cast(arr, ctypes.c_void_p)
+
+
+def interpolate(attr: torch.Tensor, rast: torch.Tensor, tri: torch.Tensor,
+                rast_db: Optional[torch.Tensor] = None,
+                diff_attrs: Union[None, DiffAttrs, str, Sequence[int]] = None):
+    """DiffRast.interpolate (Interpolate.swift:43-132) -> (out, out_da)."""
+    if rast.dim() != 4 or rast.shape[3] != 4:
+        raise ValueError(f"interpolate: rast must be [N, H, W, 4] (got {tuple(rast.shape)})")
+    if tri.dim() != 2 or tri.shape[1] != 3:
+        raise ValueError(f"interpolate: tri must be [T, 3] (got {tuple(tri.shape)})")
+    if attr.dim() not in (2, 3):
+        raise ValueError(f"interpolate: attr must be [V, A] or [N, V, A] (got {tuple(attr.shape)})")
+    diff = _as_diff(diff_attrs)
+    N = rast.shape[0]
+    Na = 1 if attr.dim() == 2 else attr.shape[0]
+    if Na != 1 and Na != N:
+        raise ValueError(f"interpolate: attr batch dim {Na} incompatible with rast batch {N}")
+    A = attr.shape[-1]
+    if diff is not None:
+        if rast_db is None:
+            raise ValueError("interpolate: rastDB is required when diffAttrs is set")
+        if tuple(rast_db.shape) != tuple(rast.shape):
+            raise ValueError(f"interpolate: rastDB must match rast shape (got {tuple(rast_db.shape)} "
+                             f"vs {tuple(rast.shape)})")
+        idx, K = diff.resolve(A)
+    else:
+        idx, K, rast_db = None, 0, None
+    return _Interpolate.apply(attr, rast, rast_db, _i32(tri, "tri"), idx, K)
+
+
+# ----------------------------------------------------------------- texture
+
+def _mip_layout(Nt, Ht, Wt, C, max_level):
+    import ctypes
+    n = ctypes.c_int()
+    off = (ctypes.c_int64 * 32)()
+    hh = (ctypes.c_int * 32)()
+    ww = (ctypes.c_int * 32)()
+    tot = ctypes.c_int64()
+    st = L.lib().dr_texture_mip_layout(Nt, Ht, Wt, C, max_level, ctypes.byref(n), off, hh, ww,
+                                       ctypes.byref(tot))
+    if st != L.DR_OK:
+        raise ValueError("textureConstructMip: bad texture shape")
+    k = n.value
+    return k, list(off[:k]), list(hh[:k]), list(ww[:k]), tot.value
+
+
+def _build_pyramid(tex_c: torch.Tensor, max_level: int):
+    Nt, Ht, Wt, C = tex_c.shape
+    n, off, hh, ww, tot = _mip_layout(Nt, Ht, Wt, C, max_level)
+    pyr = torch.empty(max(tot, 1), device=tex_c.device, dtype=torch.float32)
+    c = _ctx(tex_c)
+    L.check(L.lib().dr_texture_construct_mip(c, _ptr(tex_c), Nt, Ht, Wt, C, max_level, _ptr(pyr)),
+            c, "textureConstructMip")
+    return pyr, (n, off, hh, ww)
+
+
+class _Texture(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, tex, uv, uv_da, bias_map, filt, bnd, bias):
+        tex_c = _f32(tex, "tex")
+        uv_c = _f32(uv, "uv")
+        da_c = _f32(uv_da, "uvDA") if uv_da is not None else None
+        map_c = _f32(bias_map, "mipLevelBiasMap") if bias_map is not None else None
+        cube = bnd == BoundaryMode.cube
+        if cube:
+            Nt, _, Ht, Wt, C = tex_c.shape
+        else:
+            Nt, Ht, Wt, C = tex_c.shape
+        N, Hi, Wi = uv_c.shape[:3]
+        mip = filt in (FilterMode.linearMipmapNearest, FilterMode.linearMipmapLinear)
+        pyr = None
+        if mip:
+            pyr, _ = _build_pyramid(tex_c, -1)
+        out = torch.empty((N, Hi, Wi, C), device=uv_c.device, dtype=torch.float32)
+        c = _ctx(uv_c)
+        L.check(L.lib().dr_texture_fwd(c, int(filt), int(bnd), _ptr(tex_c), Nt, Ht, Wt, C, _ptr(pyr), -1,
+                                       _ptr(uv_c), _ptr(da_c), float(bias), _ptr(map_c), N, Hi, Wi,
+                                       _ptr(out)), c, "texture")
+        ctx.save_for_backward(tex_c, uv_c, da_c, map_c, pyr)
+        ctx.meta = (int(filt), int(bnd), float(bias), (Nt, Ht, Wt, C, N, Hi, Wi), tuple(map_c.shape) if map_c is not None else None)
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        tex_c, uv_c, da_c, map_c, pyr = ctx.saved_tensors
+        filt, bnd, bias, (Nt, Ht, Wt, C, N, Hi, Wi), map_shape = ctx.meta
+        d_out = d_out.contiguous().float()
+        d_tex = torch.empty_like(tex_c)
+        d_uv = torch.empty_like(uv_c)
+        mip = filt in (2, 3)
+        d_da = torch.empty_like(da_c) if (mip and ctx.needs_input_grad[2]) else None
+        d_map = (torch.empty((N, Hi, Wi), device=uv_c.device, dtype=torch.float32)
+                 if (mip and map_c is not None and ctx.needs_input_grad[3]) else None)
+        c = _ctx(uv_c)
+        L.check(L.lib().dr_texture_bwd(c, filt, bnd, _ptr(tex_c), Nt, Ht, Wt, C, _ptr(pyr), -1, _ptr(uv_c),
+                                       _ptr(da_c), float(bias), _ptr(map_c), N, Hi, Wi, _ptr(d_out),
+                                       _ptr(d_tex), _ptr(d_uv), _ptr(d_da), _ptr(d_map)),
+                c, "texture_bwd")
+        if d_map is not None:
+            d_map = d_map.reshape(map_shape)
+        return d_tex, d_uv, d_da, d_map, None, None, None
+
+
+def texture(tex: torch.Tensor, uv: torch.Tensor, uv_da: Optional[torch.Tensor] = None,
+            filter_mode: FilterMode = FilterMode.linear, boundary_mode: BoundaryMode = BoundaryMode.wrap,
+            mip_level_bias: float = 0.0, mip_level_bias_map: Optional[torch.Tensor] = None):
+    """DiffRast.texture (Texture.swift:62-131)."""
+    filt, bnd = FilterMode(filter_mode), BoundaryMode(boundary_mode)
+    if bnd == BoundaryMode.cube:
+        if filt != FilterMode.linear:
+            raise ValueError("texture: cube textures currently support filterMode .linear only")
+        if tex.dim() != 5 or tex.shape[1] != 6:
+            raise ValueError(f"texture: cube tex must be [N, 6, H, W, C] (got {tuple(tex.shape)})")
+        if uv.dim() != 4 or uv.shape[3] != 3:
+            raise ValueError("texture: cube uv must be [N, H_img, W_img, 3] direction vector "
+                             f"(got {tuple(uv.shape)})")
+        if tex.shape[0] not in (1, uv.shape[0]):
+            raise ValueError("texture: tex batch dim incompatible with uv batch")
+        return _Texture.apply(tex, uv, None, None, filt, bnd, 0.0)
+    if tex.dim() != 4:
+        raise ValueError(f"texture: tex must be [N, H_tex, W_tex, C] (got {tuple(tex.shape)})")
+    if uv.dim() != 4 or uv.shape[3] != 2:
+        raise ValueError(f"texture: uv must be [N, H_img, W_img, 2] (got {tuple(uv.shape)})")
+    if tex.shape[0] != 1 and tex.shape[0] != uv.shape[0]:
+        raise ValueError(f"texture: tex batch dim {tex.shape[0]} incompatible with uv batch {uv.shape[0]}")
+    if filt in (FilterMode.nearest, FilterMode.linear):
+        return _Texture.apply(tex, uv, None, None, filt, bnd, 0.0)
+    if uv_da is None:
+        raise ValueError("texture: mipmap filterModes require uvDA")
+    if tuple(uv_da.shape) != tuple(uv.shape[:3]) + (4,):
+        raise ValueError(f"texture: uvDA must be [N, H_img, W_img, 4] (got {tuple(uv_da.shape)})")
+    if mip_level_bias_map is not None:
+        m = mip_level_bias_map
+        if tuple(m.shape[:3]) != tuple(uv.shape[:3]) or not (m.dim() == 3 or (m.dim() == 4 and m.shape[3] == 1)):
+            raise ValueError("texture: mipLevelBiasMap must be [N, H_img, W_img] or [N, H_img, W_img, 1] "
+                             f"(got {tuple(m.shape)})")
+    return _Texture.apply(tex, uv, uv_da, mip_level_bias_map, filt, bnd, float(mip_level_bias))
+
+
+def texture_construct_mip(tex: torch.Tensor, max_level: Optional[int] = None):
+    """DiffRast.textureConstructMip (Texture.swift:144-161): [level0 = tex, level1, ...].
+
+    Forward only (the levels are views of one pyramid buffer); gradients of
+    mipmapped sampling flow through `texture`, which folds them into the texture.
+    """
+    if tex.dim() != 4:
+        raise ValueError(f"textureConstructMip: tex must be [N, H, W, C] (got {tuple(tex.shape)})")
+    tex_c = _f32(tex, "tex")
+    ml = -1 if max_level is None else int(max_level)
+    pyr, (n, off, hh, ww) = _build_pyramid(tex_c, ml)
+    Nt, _, _, C = tex_c.shape
+    levels = [tex]
+    for k in range(1, n):
+        cnt = Nt * hh[k] * ww[k] * C
+        levels.append(pyr[off[k]:off[k] + cnt].view(Nt, hh[k], ww[k], C))
+    return levels
+
+
+# --------------------------------------------------------------- antialias
+
+def antialias_construct_topology_hash(tri: torch.Tensor) -> torch.Tensor:
+    """DiffRast.antialiasConstructTopologyHash (Antialias.swift:19-66), on the GPU."""
+    if tri.dim() != 2 or tri.shape[1] != 3:
+        raise ValueError(f"antialiasConstructTopologyHash: tri must be [T, 3] (got {tuple(tri.shape)})")
+    tri_c = _i32(tri, "tri")
+    topo = torch.empty_like(tri_c)
+    c = _ctx(tri_c)
+    L.check(L.lib().dr_antialias_construct_topology_hash(c, _ptr(tri_c), tri_c.shape[0], _ptr(topo)),
+            c, "antialiasConstructTopologyHash")
+    return topo
+
+
+class _Antialias(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, color, pos, rast, tri, topo):
+        color_c = _f32(color, "color")
+        pos_c = _f32(pos, "pos")
+        rast_c = _f32(rast, "rast")
+        N, H, W, C = color_c.shape
+        V, T = pos_c.shape[1], tri.shape[0]
+        out = torch.empty_like(color_c)
+        c = _ctx(color_c)
+        L.check(L.lib().dr_antialias_fwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(tri),
+                                         T, _ptr(topo), _ptr(out)), c, "antialias")
+        ctx.save_for_backward(color_c, pos_c, rast_c, tri, topo)
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        color_c, pos_c, rast_c, tri, topo = ctx.saved_tensors
+        N, H, W, C = color_c.shape
+        V, T = pos_c.shape[1], tri.shape[0]
+        d_out = d_out.contiguous().float()
+        d_color = torch.empty_like(color_c)
+        d_pos = torch.empty_like(pos_c)
+        c = _ctx(color_c)
+        L.check(L.lib().dr_antialias_bwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(tri),
+                                         T, _ptr(topo), _ptr(d_out), _ptr(d_color), _ptr(d_pos)),
+                c, "antialias_bwd")
+        return d_color, d_pos, None, None, None
+
+
+def antialias(color: torch.Tensor, rast: torch.Tensor, pos: torch.Tensor, tri: torch.Tensor,
+              topology_hash: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """DiffRast.antialias (Antialias.swift:90-131); differentiable w.r.t. color and pos."""
+    if color.dim() != 4:
+        raise ValueError(f"antialias: color must be [N, H, W, C] (got {tuple(color.shape)})")
+    if rast.dim() != 4 or rast.shape[3] != 4 or tuple(rast.shape[:3]) != tuple(color.shape[:3]):
+        raise ValueError("antialias: rast must match color in [N, H, W] and have 4 channels")
+    if pos.dim() != 3 or pos.shape[2] != 4:
+        raise ValueError(f"antialias: pos must be [N, V, 4] (got {tuple(pos.shape)})")
+    if pos.shape[0] != color.shape[0]:
+        raise ValueError("antialias: pos batch must match color batch")
+    if tri.dim() != 2 or tri.shape[1] != 3:
+        raise ValueError(f"antialias: tri must be [T, 3] (got {tuple(tri.shape)})")
+    tri_c = _i32(tri, "tri")
+    topo = antialias_construct_topology_hash(tri_c) if topology_hash is None else _i32(topology_hash, "topologyHash")
+    return _Antialias.apply(color, pos, rast.detach(), tri_c, topo)
+
+
+# -------------------------------------------------------------------- loss
+
+class _MSE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pred, target):
+        p = _f32(pred, "pred")
+        t = _f32(target, "target")
+        n = p.numel()
+        d = torch.empty_like(p)
+        loss = torch.empty((), device=p.device, dtype=torch.float32)
+        c = _ctx(p)
+        L.check(L.lib().dr_mse_fwd_bwd(c, _ptr(p), _ptr(t), n, 1.0 / max(n, 1), _ptr(d), _ptr(loss), 1),
+                c, "mse")
+        ctx.save_for_backward(d)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        (d,) = ctx.saved_tensors
+        return d * g, None
+
+
+def mse_loss(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+    """mean((pred - target)^2) with its gradient computed in the same kernel."""
+    return _MSE.apply(pred, target)
+
+
+# Swift-style aliases of the reference's names.
+textureConstructMip = texture_construct_mip
+antialiasConstructTopologyHash = antialias_construct_topology_hash

@@ -1,0 +1,217 @@
+"""CUDA library vs CPU oracle on seeded synthetic scenes (the configurations'
+meshes at sizes the oracle finishes in seconds, plus full-resolution views of
+the 1M-triangle soup).  Tolerances:
+  tri_id / coverage / topology: bit-exact
+  barycentrics, z, rast_db, interpolated values, textures: <= 1e-5 relative
+  (in practice bit-exact where no atomics are involved)
+  gradients with atomic accumulation: <= 1e-4 relative L2
+"""
+import numpy as np
+import pytest
+
+import backends
+from diffrast import scenes
+from helpers import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+O = backends.OracleBackend()
+
+
+@pytest.fixture(scope="module")
+def cu():
+    return backends.CudaBackend()
+
+
+def _rel_max(a, b):
+    a = np.asarray(a, np.float64); b = np.asarray(b, np.float64)
+    return np.max(np.abs(a - b) / np.maximum(np.abs(b), 1e-6)) if a.size else 0.0
+
+
+@pytest.fixture(scope="module")
+def ico():
+    return scenes.scene_icosphere_views(4, 256)
+
+
+@pytest.fixture(scope="module")
+def soup():
+    base, tri = scenes.triangle_soup(20000, 1000, 10, seed=21)
+    M = scenes.similarity_matrices(3, seed=22)
+    pos = np.einsum("nij,vj->nvi", M, base).astype(np.float32)
+    return pos, tri
+
+
+def test_rasterize_bit_exact_icosphere(cu, ico):
+    for db in (False, True):
+        r_c, d_c = cu.rasterize(ico["pos"], ico["tri"], ico["res"], grad_db=db)
+        r_o, d_o = O.rasterize(ico["pos"], ico["tri"], ico["res"], grad_db=db)
+        assert np.array_equal(r_c, r_o)
+        if db:
+            assert np.array_equal(d_c, d_o)
+
+
+def test_rasterize_bit_exact_soup_with_peel(cu, soup):
+    pos, tri = soup
+    r0c, d0c = cu.rasterize(pos, tri, (320, 288))
+    r0o, d0o = O.rasterize(pos, tri, (320, 288))
+    assert np.array_equal(r0c, r0o) and np.array_equal(d0c, d0o)
+    r1c, _ = cu.rasterize(pos, tri, (320, 288), peel=r0o)
+    r1o, _ = O.rasterize(pos, tri, (320, 288), peel=r0o)
+    assert np.array_equal(r1c, r1o)
+    assert (r1c[..., 3] > 0).sum() > 0.3 * (r0c[..., 3] > 0).sum()
+
+
+def test_rasterize_range_mode_bit_exact(cu, soup):
+    pos, tri = soup
+    T = tri.shape[0]
+    ranges = np.array([[0, T // 2], [T // 3, T // 2], [0, T]], np.int32)
+    r_c, _ = cu.rasterize(pos[0], tri, (128, 200), ranges=ranges)
+    r_o, _ = O.rasterize(pos[0], tri, (128, 200), ranges=ranges)
+    assert np.array_equal(r_c, r_o)
+
+
+def test_rasterize_full_size_soup_views_bit_exact(cu):
+    # Two full 1024^2 views of the 1M-triangle cfg4 soup (depth complexity ~13).
+    s = scenes.scene_cfg4(n_views=2)
+    pos = np.einsum("nij,vj->nvi", s["sim"], s["base"]).astype(np.float32)
+    r_c, d_c = cu.rasterize(pos, s["tri"], s["res"])
+    r_o, d_o = O.rasterize(pos, s["tri"], s["res"])
+    assert np.array_equal(r_c[..., 3], r_o[..., 3])
+    assert np.array_equal(r_c, r_o) and np.array_equal(d_c, d_o)
+
+
+def test_rasterize_bwd_matches_oracle(cu, ico):
+    g = np.random.default_rng(1)
+    N, (H, W) = ico["pos"].shape[0], ico["res"]
+    d_r = g.normal(size=(N, H, W, 4)).astype(np.float32)
+    d_db = g.normal(size=(N, H, W, 4)).astype(np.float32)
+    for db in (None, d_db):
+        a = cu.rasterize_bwd(ico["pos"], ico["tri"], ico["res"], d_r, db)
+        b = O.rasterize_bwd(ico["pos"], ico["tri"], ico["res"], d_r, db)
+        assert rel_l2(a, b) < 1e-4
+
+
+def test_rasterize_bwd_range_mode(cu, soup):
+    pos, tri = soup
+    T = tri.shape[0]
+    ranges = np.array([[0, T], [T // 4, T // 2]], np.int32)
+    d_r = np.random.default_rng(2).normal(size=(2, 96, 96, 4)).astype(np.float32)
+    a = cu.rasterize_bwd(pos[0], tri, (96, 96), d_r, ranges=ranges)
+    b = O.rasterize_bwd(pos[0], tri, (96, 96), d_r, ranges=ranges)
+    assert a.shape == pos[0].shape and rel_l2(a, b) < 1e-4
+
+
+@pytest.mark.parametrize("A,diff", [(3, None), (8, "all"), (5, [4, 0, 2]), (2, "all")])
+@pytest.mark.parametrize("shared", [True, False])
+def test_interpolate_matches_oracle(cu, ico, A, diff, shared):
+    rast, db = O.rasterize(ico["pos"], ico["tri"], ico["res"])
+    N, V = ico["pos"].shape[:2]
+    g = np.random.default_rng(A)
+    attr = g.normal(size=((V, A) if shared else (N, V, A))).astype(np.float32)
+    o_c, oda_c = cu.interpolate(attr, rast, ico["tri"], db, diff)
+    o_o, oda_o = O.interpolate(attr, rast, ico["tri"], db, diff)
+    assert _rel_max(o_c, o_o) <= 1e-5 and _rel_max(oda_c, oda_o) <= 1e-5
+    K = 0 if diff is None else (A if diff == "all" else len(diff))
+    d_out = g.normal(size=o_o.shape).astype(np.float32)
+    d_da = g.normal(size=(N,) + ico["res"] + (2 * K,)).astype(np.float32) if K else None
+    ga = cu.interpolate_bwd(attr, rast, ico["tri"], d_out, db, diff, d_da)
+    gb = O.interpolate_bwd(attr, rast, ico["tri"], d_out, db, diff, d_da)
+    assert rel_l2(ga[0], gb[0]) < 1e-4
+    np.testing.assert_allclose(ga[1], gb[1], rtol=1e-5, atol=1e-6)
+    if K:
+        np.testing.assert_allclose(ga[2], gb[2], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("boundary", ["wrap", "clamp", "zero"])
+@pytest.mark.parametrize("filt", ["nearest", "linear", "linear-mipmap-nearest", "linear-mipmap-linear"])
+def test_texture_matches_oracle(cu, filt, boundary):
+    g = np.random.default_rng(11)
+    tex = g.random((1, 64, 128, 3)).astype(np.float32)
+    uv = g.uniform(-0.3, 1.3, size=(2, 48, 40, 2)).astype(np.float32)
+    da = (g.normal(size=(2, 48, 40, 4)) * 0.02).astype(np.float32)
+    bmap = g.uniform(-1, 1, size=(2, 48, 40)).astype(np.float32)
+    mip = filt.startswith("linear-mipmap")
+    kw = dict(uv_da=da if mip else None, filter_mode=filt, boundary_mode=boundary,
+              bias=0.5 if mip else 0.0, bias_map=bmap if mip else None)
+    a = cu.texture(tex, uv, **kw)
+    b = O.texture(tex, uv, **kw)
+    assert _rel_max(a, b) <= 1e-5
+    d_out = g.normal(size=a.shape).astype(np.float32)
+    ga = cu.texture_bwd(tex, uv, d_out, **kw)
+    gb = O.texture_bwd(tex, uv, d_out, **kw)
+    assert rel_l2(ga[0], gb[0]) < 1e-4
+    assert rel_l2(ga[1], gb[1]) < 1e-4 if np.any(gb[1]) else np.all(ga[1] == 0)
+    if mip:
+        assert rel_l2(ga[2], gb[2]) < 1e-4
+        assert rel_l2(ga[3], gb[3]) < 1e-4
+
+
+def test_texture_cube_matches_oracle(cu):
+    g = np.random.default_rng(12)
+    tex = g.random((2, 6, 32, 32, 3)).astype(np.float32)
+    d = g.normal(size=(2, 40, 24, 3)).astype(np.float32)
+    a = cu.texture(tex, d, boundary_mode="cube")
+    b = O.texture(tex, d, boundary_mode="cube")
+    assert _rel_max(a, b) <= 1e-5
+    d_out = g.normal(size=a.shape).astype(np.float32)
+    ga = cu.texture_bwd(tex, d, d_out, boundary_mode="cube")
+    gb = O.texture_bwd(tex, d, d_out, boundary_mode="cube")
+    assert rel_l2(ga[0], gb[0]) < 1e-4 and np.all(ga[1] == 0)
+
+
+def test_texture_mip_large_pyramid(cu):
+    # A 1024^2 x 4 texture (11 levels) sampled at mixed LODs.
+    g = np.random.default_rng(13)
+    tex = scenes.value_noise(1024, 1024, 4, seed=8)[None]
+    uv = g.uniform(0, 1, size=(1, 64, 64, 2)).astype(np.float32)
+    da = (np.exp(g.uniform(-9, 0, size=(1, 64, 64, 1))) * g.normal(size=(1, 64, 64, 4))).astype(np.float32)
+    kw = dict(uv_da=da, filter_mode="linear-mipmap-linear", boundary_mode="wrap")
+    a = cu.texture(tex, uv, **kw)
+    b = O.texture(tex, uv, **kw)
+    assert _rel_max(a, b) <= 1e-5
+    d_out = g.normal(size=a.shape).astype(np.float32)
+    ga, gb = cu.texture_bwd(tex, uv, d_out, **kw), O.texture_bwd(tex, uv, d_out, **kw)
+    assert rel_l2(ga[0], gb[0]) < 1e-4 and rel_l2(ga[1], gb[1]) < 1e-4 and rel_l2(ga[2], gb[2]) < 1e-4
+
+
+def test_construct_mip_matches_oracle(cu):
+    tex = np.random.default_rng(14).random((2, 256, 128, 3)).astype(np.float32)
+    for a, b in zip(cu.construct_mip(tex), O.construct_mip(tex)):
+        assert np.array_equal(a, b)
+
+
+def test_topology_hash_bit_exact_on_scenes(cu, ico, soup):
+    for tri in (ico["tri"], soup[1]):
+        assert np.array_equal(cu.topology_hash(tri), O.topology_hash(tri))
+
+
+def test_antialias_matches_oracle(cu, ico):
+    rast, _ = O.rasterize(ico["pos"], ico["tri"], ico["res"], grad_db=False)
+    g = np.random.default_rng(15)
+    N, (H, W) = ico["pos"].shape[0], ico["res"]
+    color = g.random((N, H, W, 3)).astype(np.float32)
+    topo = O.topology_hash(ico["tri"])
+    a = cu.antialias(color, rast, ico["pos"], ico["tri"], topo)
+    b = O.antialias(color, rast, ico["pos"], ico["tri"], topo)
+    assert _rel_max(a, b) <= 1e-5
+    assert np.any(a != color)
+    d_out = g.normal(size=a.shape).astype(np.float32)
+    ga = cu.antialias_bwd(color, rast, ico["pos"], ico["tri"], d_out, topo)
+    gb = O.antialias_bwd(color, rast, ico["pos"], ico["tri"], d_out, topo)
+    assert rel_l2(ga[0], gb[0]) < 1e-5
+    assert rel_l2(ga[1], gb[1]) < 1e-4
+
+
+def test_antialias_soup_with_strips(cu, soup):
+    pos, tri = soup
+    rast, _ = O.rasterize(pos, tri, (256, 256), grad_db=False)
+    g = np.random.default_rng(16)
+    color = g.normal(size=(pos.shape[0], 256, 256, 8)).astype(np.float32)
+    topo = O.topology_hash(tri)
+    a = cu.antialias(color, rast, pos, tri, topo)
+    b = O.antialias(color, rast, pos, tri, topo)
+    assert _rel_max(a, b) <= 1e-5
+    d_out = g.normal(size=a.shape).astype(np.float32)
+    ga = cu.antialias_bwd(color, rast, pos, tri, d_out, topo)
+    gb = O.antialias_bwd(color, rast, pos, tri, d_out, topo)
+    assert rel_l2(ga[0], gb[0]) < 1e-5 and rel_l2(ga[1], gb[1]) < 1e-4
