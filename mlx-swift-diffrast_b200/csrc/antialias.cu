@@ -37,6 +37,13 @@ __device__ __forceinline__ uint32_t hash64(unsigned long long k) {
   return (uint32_t)k;
 }
 
+__global__ void k_topo_init(unsigned long long* __restrict__ keys, uint32_t* __restrict__ cnt, uint32_t cap) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= cap) return;
+  keys[i] = EMPTY_KEY;
+  cnt[i] = 0u;
+}
+
 // Edge k of triangle t joins vertices (k+1)%3 and (k+2)%3 (Antialias.swift:33).
 __global__ void k_topo_insert(const int32_t* __restrict__ tri, int T, unsigned long long* __restrict__ keys,
                               uint32_t* __restrict__ cnt, int32_t* __restrict__ ref_a,
@@ -357,10 +364,9 @@ extern "C" dr_status dr_antialias_construct_topology_hash(dr_ctx* ctx, const int
   int32_t* ra = (int32_t*)(cnt + cap);
   int32_t* rb = ra + cap;
   uint32_t* rs = (uint32_t*)(rb + cap);
-  cudaMemsetAsync(keys, 0xFF, cap * 8, ctx->stream);
-  // EMPTY_KEY's low word is 0: clear it after the 0xFF fill.
-  cudaMemset2DAsync(keys, 8, 0, 4, cap, ctx->stream);
-  cudaMemsetAsync(cnt, 0, cap * 4, ctx->stream);
+  DR_TB(ctx);
+  k_topo_init<<<grid_for((int64_t)cap, 256), 256, 0, ctx->stream>>>(keys, cnt, (uint32_t)cap);
+  DR_LAUNCHED(ctx, "topo_init");
   DR_TB(ctx);
   k_topo_insert<<<grid_for(E, 256), 256, 0, ctx->stream>>>(tri, T, keys, cnt, ra, rb, rs, (uint32_t)(cap - 1),
                                                             ctx->d_err);
@@ -393,7 +399,7 @@ extern "C" dr_status dr_antialias_bwd(dr_ctx* ctx, const float* color, int N, in
   dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
   if (st != DR_OK) return st;
   DR_REQUIRE(ctx, d_out && d_color && d_pos, "antialias_bwd: d_out, d_color, d_pos required");
-  cudaMemsetAsync(d_pos, 0, sizeof(float) * (size_t)N * V * 4, ctx->stream);
+  DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * (size_t)N * V * 4, ctx->stream), "antialias_bwd memset");
   const int64_t P = (int64_t)N * H * W;
   const float4* r4 = reinterpret_cast<const float4*>(rast);
   DR_TB(ctx);

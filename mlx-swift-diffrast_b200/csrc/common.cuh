@@ -89,6 +89,16 @@ inline unsigned grid_for(int64_t n, int block) {
 
 #define DR_TB(ctx) dr::timing_begin(ctx)
 
+// Check a CUDA runtime call (memset / memcpy / sync); non-success -> DR_ECUDA.
+#define DR_CUDA(ctx, call, what)                                        \
+  do {                                                                  \
+    cudaError_t _e = (call);                                            \
+    if (_e != cudaSuccess) {                                            \
+      cudaGetLastError();                                               \
+      return dr::fail((ctx), DR_ECUDA, "%s: %s", (what), cudaGetErrorString(_e)); \
+    }                                                                   \
+  } while (0)
+
 #define DR_LAUNCHED(ctx, what)                          \
   do {                                                  \
     dr_status _st = dr::after_launch((ctx), (what));    \

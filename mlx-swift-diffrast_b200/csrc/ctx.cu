@@ -343,7 +343,7 @@ dr_status dr_mse_fwd_bwd(dr_ctx* ctx, const float* pred, const float* target, in
                          float scale, float* d_pred, float* loss, int zero_loss) {
   DR_ENTER(ctx);
   DR_REQUIRE(ctx, n >= 0 && pred && target && d_pred && loss, "mse: null pointer or n < 0");
-  if (zero_loss) cudaMemsetAsync(loss, 0, sizeof(float), ctx->stream);
+  if (zero_loss) DR_CUDA(ctx, cudaMemsetAsync(loss, 0, sizeof(float), ctx->stream), "mse memset");
   if (n == 0) return DR_OK;
   int blocks = (int)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)ctx->num_sms * 8);
   DR_TB(ctx);

@@ -246,7 +246,8 @@ extern "C" dr_status dr_interpolate_bwd(dr_ctx* ctx, const float* attr, int attr
              "interpolate_bwd: d_out, d_attr, d_rast (and d_out_da, d_rast_db with diffAttrs) required");
   DR_REQUIRE(ctx, aligned16(d_rast) && (K == 0 || aligned16(d_rast_db)),
              "interpolate_bwd: d_rast / d_rast_db must be 16-byte aligned");
-  cudaMemsetAsync(d_attr, 0, sizeof(float) * (size_t)attr_batch * V * A, ctx->stream);
+  DR_CUDA(ctx, cudaMemsetAsync(d_attr, 0, sizeof(float) * (size_t)attr_batch * V * A, ctx->stream),
+          "interpolate_bwd memset");
   const int64_t P = (int64_t)N * H * W;
   const bool vec = (A % 4 == 0) && aligned16(attr) && aligned16(d_out) && aligned16(d_attr);
   const bool use_idx = diff_idx != nullptr;

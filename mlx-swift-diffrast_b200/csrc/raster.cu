@@ -421,7 +421,8 @@ extern "C" dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V, cons
   uint32_t* tile_cur = tc + 2 * ntiles_all;
   uint32_t* total = tc + 3 * ntiles_all;
 
-  cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * (size_t)ntiles_all, ctx->stream);
+  DR_CUDA(ctx, cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * (size_t)ntiles_all, ctx->stream),
+          "rasterize memset");
   if (NT > 0) {
     DR_TB(ctx);
     k_raster_setup<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(pos, V, tri, T, ranges, N, H, W, ntx,
@@ -432,9 +433,10 @@ extern "C" dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V, cons
   if (st != DR_OK) return st;
   // The list length is data dependent: read it back (one small sync) and size
   // the list buffer exactly, so no candidate is ever dropped.
-  cudaMemcpyAsync(ctx->h_pinned, total, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream);
-  cudaMemcpyAsync(tile_cur, tile_off, sizeof(uint32_t) * (size_t)ntiles_all,
-                  cudaMemcpyDeviceToDevice, ctx->stream);
+  DR_CUDA(ctx, cudaMemcpyAsync(ctx->h_pinned, total, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream),
+          "rasterize readback");
+  DR_CUDA(ctx, cudaMemcpyAsync(tile_cur, tile_off, sizeof(uint32_t) * (size_t)ntiles_all,
+                               cudaMemcpyDeviceToDevice, ctx->stream), "rasterize copy");
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return fail(ctx, DR_ECUDA, "rasterize: %s", cudaGetErrorString(e));
   const uint32_t n_pairs = (uint32_t)ctx->h_pinned[0];
@@ -480,7 +482,7 @@ extern "C" dr_status dr_rasterize_bwd(dr_ctx* ctx, const float* pos, int V, cons
              "rasterize_bwd: pos/rast/d_rast/d_rast_db must be 16-byte aligned");
   const bool shared_pos = ranges != nullptr;
   const size_t npos = (size_t)(shared_pos ? 1 : N) * V * 4;
-  cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream);
+  DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream), "rasterize_bwd memset");
   const int64_t P = (int64_t)N * H * W;
   const bool vec = aligned16(d_pos);
   const float4* r4 = reinterpret_cast<const float4*>(rast);

@@ -574,7 +574,7 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   const unsigned grid = grid_for(a.P, 256);
   const bool shared = Nt == 1;
   const int64_t n_tex = (int64_t)Nt * (a.cube ? 6 : 1) * Ht * Wt * C;
-  cudaMemsetAsync(d_tex, 0, sizeof(float) * (size_t)n_tex, ctx->stream);
+  DR_CUDA(ctx, cudaMemsetAsync(d_tex, 0, sizeof(float) * (size_t)n_tex, ctx->stream), "texture_bwd memset");
   if (a.cube) {
     DR_TB(ctx);
     k_tex_cube<<<grid, 256, 0, ctx->stream>>>(tex, shared, Ht, Wt, C, uv, a.P, a.HWi, nullptr, d_out, d_tex,
@@ -611,7 +611,8 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   if (a.m.L > 1) {
     dpyr = (float*)ws_get(ctx, WS_DMIP, sizeof(float) * (size_t)a.pyr_floats);
     if (!dpyr) return DR_ENOMEM;
-    cudaMemsetAsync(dpyr, 0, sizeof(float) * (size_t)a.pyr_floats, ctx->stream);
+    DR_CUDA(ctx, cudaMemsetAsync(dpyr, 0, sizeof(float) * (size_t)a.pyr_floats, ctx->stream),
+            "texture_bwd memset");
   }
   const float4* da4 = reinterpret_cast<const float4*>(uv_da);
   float4* dda4 = reinterpret_cast<float4*>(d_uv_da);

@@ -52,7 +52,7 @@ SIGNATURES = {
 }
 
 _lib = None
-_lock = threading.Lock()
+_lock = threading.RLock()
 _ctx = {}
 
 
@@ -82,6 +82,7 @@ def ctx_for(device_index: int):
     """Per-device context (created on first use, kept for the process)."""
     c = _ctx.get(device_index)
     if c is None:
+        lib()
         with _lock:
             c = _ctx.get(device_index)
             if c is None:

@@ -1,0 +1,198 @@
+// DiffRast.swift — the `DiffRast.*` operator surface of mlx-swift-diffrast
+// (Sources/MLXDiffRast/*.swift) over the C ABI of libdiffrast (include/diffrast.h).
+//
+// SOURCE ONLY: this wrapper has not been compiled or run (it was written on a
+// machine without a Swift toolchain).  It is a mechanical 1:1 mapping onto the
+// C entry points: each forward returns its outputs, each `...VJP` function is
+// the explicit backward the reference obtained from MLX's CustomFunction.
+// Tensors are `DeviceTensor`s (a CUDA device pointer + shape) instead of
+// MLXArray; a caller that keeps MLX on the host side copies in and out.
+
+import CDiffRast
+import Foundation
+
+public struct DeviceTensor {
+    public let pointer: UnsafeMutableRawPointer
+    public let shape: [Int]
+    public init(pointer: UnsafeMutableRawPointer, shape: [Int]) {
+        self.pointer = pointer
+        self.shape = shape
+    }
+    public var count: Int { shape.reduce(1, *) }
+    var f: UnsafeMutablePointer<Float> { pointer.assumingMemoryBound(to: Float.self) }
+    var i: UnsafeMutablePointer<Int32> { pointer.assumingMemoryBound(to: Int32.self) }
+}
+
+/// Allocator the wrapper uses for outputs (e.g. cudaMalloc via the caller's runtime).
+public protocol DeviceAllocator {
+    func allocate(bytes: Int) -> UnsafeMutableRawPointer
+}
+
+public enum DiffRast {
+    public enum BoundaryMode: Int32 { case wrap = 0, clamp = 1, zero = 2, cube = 3 }
+    public enum FilterMode: Int32 { case nearest = 0, linear = 1, linearMipmapNearest = 2, linearMipmapLinear = 3 }
+    public enum DiffAttrs: Equatable { case all; case indices([Int32]) }
+
+    /// One context per device/thread, as the C ABI requires.
+    public final class Context {
+        let raw: OpaquePointer
+        public init(device: Int32 = 0) {
+            var p: OpaquePointer? = nil
+            let st = dr_ctx_create(device, &p)
+            precondition(st == DR_OK, "dr_ctx_create failed (\(st))")
+            raw = p!
+        }
+        deinit { dr_ctx_destroy(raw) }
+        public func setStream(_ s: UnsafeMutableRawPointer?) { _ = dr_ctx_set_stream(raw, s) }
+        func check(_ st: dr_status, _ what: String) {
+            // The reference crashes on misuse with `precondition`; keep that.
+            precondition(st == DR_OK, "\(what): \(String(cString: dr_last_error(raw)))")
+        }
+    }
+
+    // MARK: rasterize (Rasterize.swift:44-144)
+
+    public static func rasterize(_ ctx: Context, _ alloc: DeviceAllocator, _ pos: DeviceTensor,
+                                 tri: DeviceTensor, resolution: (height: Int, width: Int),
+                                 gradDB: Bool = true, ranges: DeviceTensor? = nil,
+                                 peelLayer: DeviceTensor? = nil) -> (rast: DeviceTensor, rastDB: DeviceTensor) {
+        let (N, V) = ranges != nil ? (ranges!.shape[0], pos.shape[0]) : (pos.shape[0], pos.shape[1])
+        let H = resolution.height, W = resolution.width
+        let rast = DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * 16), shape: [N, H, W, 4])
+        let db = DeviceTensor(pointer: alloc.allocate(bytes: gradDB ? N * H * W * 16 : 16),
+                              shape: gradDB ? [N, H, W, 4] : [N, H, W, 0])
+        ctx.check(dr_rasterize_fwd(ctx.raw, pos.f, Int32(V), tri.i, Int32(tri.shape[0]), ranges?.i,
+                                   Int32(N), Int32(H), Int32(W), peelLayer?.f, rast.f, gradDB ? db.f : nil),
+                  "rasterize")
+        return (rast, db)
+    }
+
+    public static func rasterizeVJP(_ ctx: Context, _ alloc: DeviceAllocator, _ pos: DeviceTensor,
+                                    tri: DeviceTensor, ranges: DeviceTensor?, rast: DeviceTensor,
+                                    dRast: DeviceTensor, dRastDB: DeviceTensor?) -> DeviceTensor {
+        let N = rast.shape[0], H = rast.shape[1], W = rast.shape[2]
+        let V = ranges != nil ? pos.shape[0] : pos.shape[1]
+        let dPos = DeviceTensor(pointer: alloc.allocate(bytes: pos.count * 4), shape: pos.shape)
+        ctx.check(dr_rasterize_bwd(ctx.raw, pos.f, Int32(V), tri.i, Int32(tri.shape[0]), ranges?.i, Int32(N),
+                                   Int32(H), Int32(W), rast.f, dRast.f, dRastDB?.f, dPos.f), "rasterize VJP")
+        return dPos
+    }
+
+    // MARK: interpolate (Interpolate.swift:43-132)
+
+    static func resolve(_ d: DiffAttrs?, _ A: Int) -> ([Int32]?, Int) {
+        guard let d = d else { return (nil, 0) }
+        switch d {
+        case .all: return (nil, A)
+        case .indices(let idx):
+            precondition(!idx.isEmpty, "interpolate: diffAttrs.indices must be non-empty")
+            return (idx, idx.count)
+        }
+    }
+
+    public static func interpolate(_ ctx: Context, _ alloc: DeviceAllocator, _ attr: DeviceTensor,
+                                   rast: DeviceTensor, tri: DeviceTensor, rastDB: DeviceTensor? = nil,
+                                   diffAttrs: DiffAttrs? = nil) -> (out: DeviceTensor, outDA: DeviceTensor) {
+        let N = rast.shape[0], H = rast.shape[1], W = rast.shape[2]
+        let Na = attr.shape.count == 2 ? 1 : attr.shape[0]
+        let V = attr.shape[attr.shape.count - 2], A = attr.shape[attr.shape.count - 1]
+        let (idx, K) = resolve(diffAttrs, A)
+        let out = DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * A * 4), shape: [N, H, W, A])
+        let oda = DeviceTensor(pointer: alloc.allocate(bytes: max(16, N * H * W * 2 * K * 4)), shape: [N, H, W, 2 * K])
+        let st: dr_status = (idx ?? []).withUnsafeBufferPointer { ib in
+            dr_interpolate_fwd(ctx.raw, attr.f, Int32(Na), Int32(V), Int32(A), rast.f, Int32(N), Int32(H),
+                               Int32(W), tri.i, Int32(tri.shape[0]), rastDB?.f, idx == nil ? nil : ib.baseAddress,
+                               Int32(K), out.f, K > 0 ? oda.f : nil)
+        }
+        ctx.check(st, "interpolate")
+        return (out, oda)
+    }
+
+    public static func interpolateVJP(_ ctx: Context, _ alloc: DeviceAllocator, _ attr: DeviceTensor,
+                                      rast: DeviceTensor, tri: DeviceTensor, rastDB: DeviceTensor?,
+                                      diffAttrs: DiffAttrs?, dOut: DeviceTensor, dOutDA: DeviceTensor?)
+        -> (dAttr: DeviceTensor, dRast: DeviceTensor, dRastDB: DeviceTensor?) {
+        let N = rast.shape[0], H = rast.shape[1], W = rast.shape[2]
+        let Na = attr.shape.count == 2 ? 1 : attr.shape[0]
+        let V = attr.shape[attr.shape.count - 2], A = attr.shape[attr.shape.count - 1]
+        let (idx, K) = resolve(diffAttrs, A)
+        let dAttr = DeviceTensor(pointer: alloc.allocate(bytes: attr.count * 4), shape: attr.shape)
+        let dRast = DeviceTensor(pointer: alloc.allocate(bytes: rast.count * 4), shape: rast.shape)
+        let dDB = K > 0 ? DeviceTensor(pointer: alloc.allocate(bytes: rast.count * 4), shape: rast.shape) : nil
+        let st: dr_status = (idx ?? []).withUnsafeBufferPointer { ib in
+            dr_interpolate_bwd(ctx.raw, attr.f, Int32(Na), Int32(V), Int32(A), rast.f, Int32(N), Int32(H),
+                               Int32(W), tri.i, Int32(tri.shape[0]), rastDB?.f, idx == nil ? nil : ib.baseAddress,
+                               Int32(K), dOut.f, dOutDA?.f, dAttr.f, dRast.f, dDB?.f)
+        }
+        ctx.check(st, "interpolate VJP")
+        return (dAttr, dRast, dDB)
+    }
+
+    // MARK: texture (Texture.swift:62-161)
+
+    public static func texture(_ ctx: Context, _ alloc: DeviceAllocator, _ tex: DeviceTensor, uv: DeviceTensor,
+                               uvDA: DeviceTensor? = nil, filterMode: FilterMode = .linear,
+                               boundaryMode: BoundaryMode = .wrap, mipLevelBias: Float = 0,
+                               mipLevelBiasMap: DeviceTensor? = nil) -> DeviceTensor {
+        let cube = boundaryMode == .cube
+        let Nt = tex.shape[0], Ht = tex.shape[cube ? 2 : 1], Wt = tex.shape[cube ? 3 : 2]
+        let C = tex.shape[cube ? 4 : 3]
+        let N = uv.shape[0], Hi = uv.shape[1], Wi = uv.shape[2]
+        let out = DeviceTensor(pointer: alloc.allocate(bytes: N * Hi * Wi * C * 4), shape: [N, Hi, Wi, C])
+        ctx.check(dr_texture_fwd(ctx.raw, filterMode.rawValue, boundaryMode.rawValue, tex.f, Int32(Nt), Int32(Ht),
+                                 Int32(Wt), Int32(C), nil, -1, uv.f, uvDA?.f, mipLevelBias, mipLevelBiasMap?.f,
+                                 Int32(N), Int32(Hi), Int32(Wi), out.f), "texture")
+        return out
+    }
+
+    public static func textureVJP(_ ctx: Context, _ alloc: DeviceAllocator, _ tex: DeviceTensor, uv: DeviceTensor,
+                                  uvDA: DeviceTensor?, filterMode: FilterMode, boundaryMode: BoundaryMode,
+                                  mipLevelBias: Float, mipLevelBiasMap: DeviceTensor?, dOut: DeviceTensor)
+        -> (dTex: DeviceTensor, dUV: DeviceTensor, dUVDA: DeviceTensor?) {
+        let cube = boundaryMode == .cube
+        let Nt = tex.shape[0], Ht = tex.shape[cube ? 2 : 1], Wt = tex.shape[cube ? 3 : 2]
+        let C = tex.shape[cube ? 4 : 3]
+        let N = uv.shape[0], Hi = uv.shape[1], Wi = uv.shape[2]
+        let dTex = DeviceTensor(pointer: alloc.allocate(bytes: tex.count * 4), shape: tex.shape)
+        let dUV = DeviceTensor(pointer: alloc.allocate(bytes: uv.count * 4), shape: uv.shape)
+        let mip = filterMode == .linearMipmapLinear || filterMode == .linearMipmapNearest
+        let dDA = mip ? DeviceTensor(pointer: alloc.allocate(bytes: N * Hi * Wi * 16), shape: [N, Hi, Wi, 4]) : nil
+        ctx.check(dr_texture_bwd(ctx.raw, filterMode.rawValue, boundaryMode.rawValue, tex.f, Int32(Nt), Int32(Ht),
+                                 Int32(Wt), Int32(C), nil, -1, uv.f, uvDA?.f, mipLevelBias, mipLevelBiasMap?.f,
+                                 Int32(N), Int32(Hi), Int32(Wi), dOut.f, dTex.f, dUV.f, dDA?.f, nil),
+                  "texture VJP")
+        return (dTex, dUV, dDA)
+    }
+
+    // MARK: antialias (Antialias.swift:19-131)
+
+    public static func antialiasConstructTopologyHash(_ ctx: Context, _ alloc: DeviceAllocator,
+                                                      _ tri: DeviceTensor) -> DeviceTensor {
+        let topo = DeviceTensor(pointer: alloc.allocate(bytes: tri.count * 4), shape: tri.shape)
+        ctx.check(dr_antialias_construct_topology_hash(ctx.raw, tri.i, Int32(tri.shape[0]), topo.i),
+                  "antialiasConstructTopologyHash")
+        return topo
+    }
+
+    public static func antialias(_ ctx: Context, _ alloc: DeviceAllocator, color: DeviceTensor, rast: DeviceTensor,
+                                 pos: DeviceTensor, tri: DeviceTensor, topologyHash: DeviceTensor? = nil) -> DeviceTensor {
+        let topo = topologyHash ?? antialiasConstructTopologyHash(ctx, alloc, tri)
+        let N = color.shape[0], H = color.shape[1], W = color.shape[2], C = color.shape[3]
+        let out = DeviceTensor(pointer: alloc.allocate(bytes: color.count * 4), shape: color.shape)
+        ctx.check(dr_antialias_fwd(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f, pos.f,
+                                   Int32(pos.shape[1]), tri.i, Int32(tri.shape[0]), topo.i, out.f), "antialias")
+        return out
+    }
+
+    public static func antialiasVJP(_ ctx: Context, _ alloc: DeviceAllocator, color: DeviceTensor, rast: DeviceTensor,
+                                    pos: DeviceTensor, tri: DeviceTensor, topologyHash: DeviceTensor,
+                                    dOut: DeviceTensor) -> (dColor: DeviceTensor, dPos: DeviceTensor) {
+        let N = color.shape[0], H = color.shape[1], W = color.shape[2], C = color.shape[3]
+        let dColor = DeviceTensor(pointer: alloc.allocate(bytes: color.count * 4), shape: color.shape)
+        let dPos = DeviceTensor(pointer: alloc.allocate(bytes: pos.count * 4), shape: pos.shape)
+        ctx.check(dr_antialias_bwd(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f, pos.f,
+                                   Int32(pos.shape[1]), tri.i, Int32(tri.shape[0]), topologyHash.i, dOut.f,
+                                   dColor.f, dPos.f), "antialias VJP")
+        return (dColor, dPos)
+    }
+}

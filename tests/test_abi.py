@@ -84,3 +84,16 @@ def test_ops_refuse_cpu_tensors():
     tri = torch.zeros(1, 3, dtype=torch.int32)
     with pytest.raises(ValueError, match="CUDA"):
         diffrast.rasterize(pos, tri, (4, 4))
+
+
+def test_first_call_path_does_not_deadlock():
+    # The first op of a process creates the context before anything else has
+    # loaded the library; that path must return (an error without a GPU).
+    import sys
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "from diffrast import _lib\n"
+            "try:\n    _lib.ctx_for(0)\n    print('ctx')\n"
+            "except _lib.DiffRastError as e:\n    print('err', e)\n") % os.path.join(ROOT, "mlx-swift-diffrast_b200")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.startswith(("ctx", "err"))
