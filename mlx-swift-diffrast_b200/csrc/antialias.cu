@@ -338,7 +338,7 @@ inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 dr_status check_aa(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
                    const float* pos, int V, const int32_t* tri, int T, const int32_t* topo) {
-  DR_REQUIRE(ctx, color && rast && pos && tri && topo, "antialias: null input");
+  DR_REQUIRE(ctx, color && rast && pos && ((tri && topo) || T == 0), "antialias: null input");
   DR_REQUIRE(ctx, N > 0 && H > 0 && W > 0 && C > 0 && V > 0 && T >= 0, "antialias: bad sizes");
   DR_REQUIRE(ctx, aligned16(rast) && aligned16(pos), "antialias: rast / pos must be 16-byte aligned");
   return DR_OK;
@@ -350,7 +350,7 @@ using namespace dr;
 
 extern "C" dr_status dr_antialias_construct_topology_hash(dr_ctx* ctx, const int32_t* tri, int T, int32_t* topo) {
   DR_ENTER(ctx);
-  DR_REQUIRE(ctx, tri && topo && T >= 0, "antialiasConstructTopologyHash: bad arguments");
+  DR_REQUIRE(ctx, T >= 0 && (T == 0 || (tri && topo)), "antialiasConstructTopologyHash: bad arguments");
   DR_REQUIRE(ctx, T < (1 << 29), "antialiasConstructTopologyHash: T too large");
   if (T == 0) return DR_OK;
   const int64_t E = (int64_t)T * 3;

@@ -170,7 +170,7 @@ inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 dr_status check_common(dr_ctx* ctx, const float* attr, int attr_batch, int V, int A,
                        const float* rast, int N, int H, int W, const int32_t* tri, int T,
                        const float* rast_db, const int32_t* diff_idx, int K, DiffIdx& idx) {
-  DR_REQUIRE(ctx, attr && rast && tri, "interpolate: attr, rast and tri are required");
+  DR_REQUIRE(ctx, attr && rast && (tri || T == 0), "interpolate: attr, rast and tri are required");
   DR_REQUIRE(ctx, N > 0 && H > 0 && W > 0 && V > 0 && A > 0 && T >= 0,
              "interpolate: bad sizes N=%d H=%d W=%d V=%d A=%d T=%d", N, H, W, V, A, T);
   DR_REQUIRE(ctx, attr_batch == 1 || attr_batch == N,

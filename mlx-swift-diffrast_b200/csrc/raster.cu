@@ -400,7 +400,7 @@ extern "C" dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V, cons
                                       int T, const int32_t* ranges, int N, int H, int W,
                                       const float* peel_layer, float* rast, float* rast_db) {
   DR_ENTER(ctx);
-  DR_REQUIRE(ctx, pos && tri && rast, "rasterize: pos, tri and rast are required");
+  DR_REQUIRE(ctx, pos && (tri || T == 0) && rast, "rasterize: pos, tri and rast are required");
   DR_REQUIRE(ctx, N > 0 && V > 0 && T >= 0 && H > 0 && W > 0,
              "rasterize: bad sizes N=%d V=%d T=%d H=%d W=%d", N, V, T, H, W);
   DR_REQUIRE(ctx, H <= 32768 && W <= 32768, "rasterize: resolution above 32768 is not supported");
@@ -475,7 +475,7 @@ extern "C" dr_status dr_rasterize_bwd(dr_ctx* ctx, const float* pos, int V, cons
                                       const int32_t* ranges, int N, int H, int W, const float* rast,
                                       const float* d_rast, const float* d_rast_db, float* d_pos) {
   DR_ENTER(ctx);
-  DR_REQUIRE(ctx, pos && tri && rast && d_rast && d_pos, "rasterize_bwd: null pointer");
+  DR_REQUIRE(ctx, pos && (tri || T == 0) && rast && d_rast && d_pos, "rasterize_bwd: null pointer");
   DR_REQUIRE(ctx, N > 0 && V > 0 && T >= 0 && H > 0 && W > 0, "rasterize_bwd: bad sizes");
   DR_REQUIRE(ctx, aligned16(pos) && aligned16(rast) && aligned16(d_rast) &&
                       (!d_rast_db || aligned16(d_rast_db)),

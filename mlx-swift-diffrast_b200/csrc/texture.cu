@@ -245,17 +245,24 @@ __global__ void k_mip_down(const float* __restrict__ src, int Hs, int Ws, float*
   dst[i] = ((a + b) + (cc + d)) * 0.25f;
 }
 
+// 2^x and log2(x) evaluated in double and rounded once to float, so the CPU
+// oracle (which does the same with the C library) agrees to the bit in all but
+// vanishingly rare rounding ties; the float versions differ by an ulp between
+// CUDA and glibc, which moves the LOD.
+__device__ __forceinline__ float exp2_rn(float x) { return (float)exp2((double)x); }
+__device__ __forceinline__ float log2_rn(float x) { return (float)log2((double)x); }
+
 // Effective uvDA = uvDA * 2^map * 2^bias (Texture.swift:104-126).
 __device__ __forceinline__ float4 effective_da(const float4 da, int64_t pix, float bias,
                                                const float* __restrict__ bias_map, float& s) {
   s = 1.0f;
   bool scaled = false;
   if (bias_map) {
-    s = exp2f(__ldg(bias_map + pix));
-    if (bias != 0.0f) s = s * exp2f(bias);
+    s = exp2_rn(__ldg(bias_map + pix));
+    if (bias != 0.0f) s = s * exp2_rn(bias);
     scaled = true;
   } else if (bias != 0.0f) {
-    s = exp2f(bias);
+    s = exp2_rn(bias);
     scaled = true;
   }
   if (!scaled) return da;
@@ -273,7 +280,7 @@ __device__ __forceinline__ LodSel lod_select(const float4 e, int Ht, int Wt, int
   const float sx = e.x * (float)Wt, sy = e.y * (float)Wt;
   const float tx = e.z * (float)Ht, ty = e.w * (float)Ht;
   const float rho_sq = fmaxf(sx * sx + tx * tx, sy * sy + ty * ty);
-  float lod = 0.5f * log2f(fmaxf(rho_sq, 1e-20f));
+  float lod = 0.5f * log2_rn(fmaxf(rho_sq, 1e-20f));
   lod = fmaxf(0.0f, fminf((float)(L - 1), lod));
   LodSel s;
   if (MIP_LINEAR) {
@@ -372,7 +379,7 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
   const float tx_ = e.z * (float)Ht, ty_ = e.w * (float)Ht;
   const float Asq = sx * sx + tx_ * tx_, Bsq = sy * sy + ty_ * ty_;
   const float rho_sq = fmaxf(Asq, Bsq);
-  const float lod_raw = 0.5f * log2f(fmaxf(rho_sq, 1e-20f));
+  const float lod_raw = 0.5f * log2_rn(fmaxf(rho_sq, 1e-20f));
   float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f);
   if (!(lod_raw <= 0.0f || lod_raw >= (float)(L - 1))) {
     const int k0 = dr_floor_i(lod_raw);

@@ -582,6 +582,12 @@ MipLayout mip_layout(int Nt, int Ht, int Wt, int C, int max_level) {
   return m;
 }
 
+// 2^x and log2(x) in double, rounded once to float (the CUDA path does the
+// same): the reference's float pow / log2 are not observable here, and the float
+// library versions differ by an ulp between libraries.
+inline float exp2_rn(float x) { return (float)std::exp2((double)x); }
+inline float log2_rn(float x) { return (float)std::log2((double)x); }
+
 // Per-pixel LOD block (Texture.swift:764-790).
 struct Lod { int k0, k1; float frac; };
 inline Lod lod_of(const float* da, int Ht, int Wt, int L, bool mip_linear) {
@@ -589,7 +595,7 @@ inline Lod lod_of(const float* da, int Ht, int Wt, int L, bool mip_linear) {
   float sx = du_dx * (float)Wt, sy = du_dy * (float)Wt;
   float tx = dv_dx * (float)Ht, ty = dv_dy * (float)Ht;
   float rho_sq = std::fmax(sx * sx + tx * tx, sy * sy + ty * ty);
-  float lod = 0.5f * std::log2(std::fmax(rho_sq, 1e-20f));
+  float lod = 0.5f * log2_rn(std::fmax(rho_sq, 1e-20f));
   lod = std::fmax(0.0f, std::fmin((float)(L - 1), lod));
   Lod r;
   if (mip_linear) {
@@ -613,11 +619,11 @@ inline void effective_da(const float* uv_da, int64_t pix, float bias, const floa
   float s = 1.0f;
   bool scaled = false;
   if (bias_map) {
-    s = std::pow(2.0f, bias_map[pix]);
-    if (bias != 0.0f) s = s * std::pow(2.0f, bias);
+    s = exp2_rn(bias_map[pix]);
+    if (bias != 0.0f) s = s * exp2_rn(bias);
     scaled = true;
   } else if (bias != 0.0f) {
-    s = std::pow(2.0f, bias);
+    s = exp2_rn(bias);
     scaled = true;
   }
   for (int c = 0; c < 4; ++c) eff[c] = scaled ? uv_da[pix * 4 + c] * s : uv_da[pix * 4 + c];
@@ -929,7 +935,7 @@ extern "C" int orc_texture_bwd(int filter, int boundary, const float* tex, int N
       float tx_ = dv_dx * (float)Ht, ty_ = dv_dy * (float)Ht;
       float Asq = sx * sx + tx_ * tx_, Bsq = sy * sy + ty_ * ty_;
       float rho_sq = std::fmax(Asq, Bsq);
-      float lod_raw = 0.5f * std::log2(std::fmax(rho_sq, 1e-20f));
+      float lod_raw = 0.5f * log2_rn(std::fmax(rho_sq, 1e-20f));
       float g4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       if (!(lod_raw <= 0.0f || lod_raw >= (float)(m.L - 1))) {
         int k0 = floor_to_int(lod_raw);
