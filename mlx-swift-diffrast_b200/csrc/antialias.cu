@@ -222,7 +222,11 @@ __global__ void k_aa_fwd(const float* __restrict__ color, int N, int H, int W, i
   const float* cp = color + pix * C;
   float* o = out + pix * C;
   if (!any) {
-    for (int c = 0; c < C; ++c) o[c] = __ldg(cp + c);
+    if ((C & 3) == 0 && ((((uintptr_t)color) | ((uintptr_t)out)) & 15) == 0) {
+      for (int c = 0; c < C; c += 4) *reinterpret_cast<float4*>(o + c) = ldg4(cp + c);
+    } else {
+      for (int c = 0; c < C; ++c) o[c] = __ldg(cp + c);
+    }
     return;
   }
   for (int c = 0; c < C; ++c) {
@@ -325,8 +329,24 @@ __global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, i
     const SilDir s = sil_dir(rast, pos, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
     if (s.active) { nbeta[d] = s.beta; nsrc[d] = p; }
   }
+  const float keep = 1.0f - alpha_sum;
+  if ((C & 3) == 0 && ((((uintptr_t)d_out) | ((uintptr_t)d_color)) & 15) == 0) {
+    for (int c = 0; c < C; c += 4) {
+      const float4 gs = ldg4(g + c);
+      float4 v = make_float4(gs.x * keep, gs.y * keep, gs.z * keep, gs.w * keep);
+#pragma unroll
+      for (int d = 0; d < 4; ++d)
+        if (nsrc[d] >= 0) {
+          const float4 gn = ldg4(d_out + nsrc[d] * C + c);
+          const float b = nbeta[d];
+          v.x += gn.x * b; v.y += gn.y * b; v.z += gn.z * b; v.w += gn.w * b;
+        }
+      *reinterpret_cast<float4*>(d_color + pix * C + c) = v;
+    }
+    return;
+  }
   for (int c = 0; c < C; ++c) {
-    float v = __ldg(g + c) * (1.0f - alpha_sum);
+    float v = __ldg(g + c) * keep;
 #pragma unroll
     for (int d = 0; d < 4; ++d)
       if (nsrc[d] >= 0) v += __ldg(d_out + nsrc[d] * C + c) * nbeta[d];

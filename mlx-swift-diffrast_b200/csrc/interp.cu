@@ -48,8 +48,13 @@ __global__ void k_interp_fwd(const float* __restrict__ attr, bool attr_shared, i
     } else {
       for (int a = 0; a < A; ++a) o[a] = 0.0f;
     }
-    if (DA)
-      for (int k = 0; k < 2 * K; ++k) od[k] = 0.0f;
+    if (DA) {
+      if (VEC4 && !IDX) {
+        for (int k = 0; k < 2 * K; k += 4) *reinterpret_cast<float4*>(od + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else {
+        for (int k = 0; k < 2 * K; ++k) od[k] = 0.0f;
+      }
+    }
     return;
   }
   const float u = r.x, v = r.y;
@@ -59,6 +64,29 @@ __global__ void k_interp_fwd(const float* __restrict__ attr, bool attr_shared, i
   const float* a0p = an + (int64_t)i0 * A;
   const float* a1p = an + (int64_t)i1 * A;
   const float* a2p = an + (int64_t)i2 * A;
+  if (VEC4 && DA && !IDX) {
+    // .all with A % 4 == 0: out and out_da from the same float4 gathers;
+    // out_da rows are 2A floats, so every store is a float4.
+    const float4 db = __ldg(rast_db + pix);
+    for (int a = 0; a < A; a += 4) {
+      const float4 x0 = ldg4(a0p + a), x1 = ldg4(a1p + a), x2 = ldg4(a2p + a);
+      float4 y;
+      y.x = bw * x0.x + u * x1.x + v * x2.x;
+      y.y = bw * x0.y + u * x1.y + v * x2.y;
+      y.z = bw * x0.z + u * x1.z + v * x2.z;
+      y.w = bw * x0.w + u * x1.w + v * x2.w;
+      *reinterpret_cast<float4*>(o + a) = y;
+      const float4 d01 = make_float4(x1.x - x0.x, x1.y - x0.y, x1.z - x0.z, x1.w - x0.w);
+      const float4 d02 = make_float4(x2.x - x0.x, x2.y - x0.y, x2.z - x0.z, x2.w - x0.w);
+      *reinterpret_cast<float4*>(od + 2 * a) =
+          make_float4(d01.x * db.x + d02.x * db.z, d01.x * db.y + d02.x * db.w,
+                      d01.y * db.x + d02.y * db.z, d01.y * db.y + d02.y * db.w);
+      *reinterpret_cast<float4*>(od + 2 * a + 4) =
+          make_float4(d01.z * db.x + d02.z * db.z, d01.z * db.y + d02.z * db.w,
+                      d01.w * db.x + d02.w * db.z, d01.w * db.y + d02.w * db.w);
+    }
+    return;
+  }
   if (VEC4) {
     for (int a = 0; a < A; a += 4) {
       const float4 x0 = ldg4(a0p + a), x1 = ldg4(a1p + a), x2 = ldg4(a2p + a);

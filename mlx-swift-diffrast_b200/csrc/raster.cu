@@ -189,6 +189,14 @@ __device__ __forceinline__ unsigned long long pack_key(float z, int t) {
   return ((unsigned long long)u << 32) | (unsigned)t;
 }
 
+// Per-tile fine raster.  Each warp takes 32 candidates at a time, stages their
+// records in shared memory, and flattens their (candidate, pixel) work items
+// (pixels of the candidate's rectangle inside the tile) with a warp prefix
+// sum, so all 32 lanes test one pixel each per round regardless of how the
+// rectangle sizes vary (1 to 256 pixels).
+constexpr int WARPS = TILE_PIX / 32;
+constexpr int SSTRIDE = 5;  // float4 per staged candidate (80 B: conflict-free 128-bit phases)
+
 template <bool PEEL, bool DB>
 __global__ void __launch_bounds__(TILE_PIX)
 k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int nty,
@@ -198,6 +206,8 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   __shared__ unsigned long long s_key[TILE_PIX];
   __shared__ float s_peel[TILE_PIX];
   __shared__ float s_ndcx[TILE], s_ndcy[TILE];
+  __shared__ float4 s_stage[WARPS][32 * SSTRIDE];
+  __shared__ int s_pre[WARPS][32];
 
   const int ntiles = ntx * nty;
   const int n = blockIdx.x / ntiles;
@@ -224,31 +234,69 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   const uint32_t gt = (uint32_t)blockIdx.x;
   const uint32_t begin = __ldg(tile_off + gt), cnt = __ldg(tile_count + gt);
   const int64_t rec_view = (int64_t)n * T;
-  for (uint32_t i = tid; i < cnt; i += TILE_PIX) {
-    const int t = __ldg(list + begin + i);
-    const Rec r = load_rec(rec, rec_view + t);
-    const float inv_area = FD(1.0f, r.area);
-    const int cx0 = max(r.x0, tx0), cx1 = min(r.x1, tx0 + TILE - 1);
-    const int cy0 = max(r.y0, ty0), cy1 = min(r.y1, ty0 + TILE - 1);
-    for (int yy = cy0; yy <= cy1; ++yy) {
-      const float y = s_ndcy[yy - ty0];
-      const float dy0 = FS(r.sy0, y), dy1 = FS(r.sy1, y), dy2 = FS(r.sy2, y);
-      for (int xx = cx0; xx <= cx1; ++xx) {
-        const float x = s_ndcx[xx - tx0];
-        const float dx0 = FS(r.sx0, x), dx1 = FS(r.sx1, x), dx2 = FS(r.sx2, x);
-        const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));
-        const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
-        const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
-        if (FM(e0, r.area) < 0.0f || FM(e1, r.area) < 0.0f || FM(e2, r.area) < 0.0f) continue;
-        const float bw = FM(e0, inv_area), u = FM(e1, inv_area), v = FM(e2, inv_area);
-        const float z = FA(FA(FM(bw, r.sz0), FM(u, r.sz1)), FM(v, r.sz2));
-        if (z < -1.0f || z > 1.0f) continue;
-        const int p = (yy - ty0) * TILE + (xx - tx0);
-        if (PEEL && z <= s_peel[p]) continue;
-        const unsigned long long key = pack_key(z, t);
-        if (key < s_key[p]) atomicMin(&s_key[p], key);
+  const int warp = tid >> 5, lane = tid & 31;
+  float4* st = s_stage[warp];
+  int* sp = s_pre[warp];
+  for (uint32_t base = (uint32_t)warp * 32u; base < cnt; base += TILE_PIX) {
+    const uint32_t i = base + lane;
+    int n_items = 0;
+    if (i < cnt) {
+      const int t = __ldg(list + begin + i);
+      const float4 a = __ldg(rec + 3 * (rec_view + t) + 0);
+      const float4 b = __ldg(rec + 3 * (rec_view + t) + 1);
+      const float4 c = __ldg(rec + 3 * (rec_view + t) + 2);
+      const unsigned xs = __float_as_uint(c.z), ys = __float_as_uint(c.w);
+      const int cx0 = max((int)(xs & 0xffffu), tx0), cx1 = min((int)(xs >> 16), tx0 + TILE - 1);
+      const int cy0 = max((int)(ys & 0xffffu), ty0), cy1 = min((int)(ys >> 16), ty0 + TILE - 1);
+      const int wc = cx1 - cx0 + 1, hc = cy1 - cy0 + 1;
+      if (wc > 0 && hc > 0) {
+        n_items = wc * hc;
+        const int magic = (65536 + wc - 1) / wc;  // (k * magic) >> 16 == k / wc for k < 256
+        const int pk = (cx0 - tx0) | ((cy0 - ty0) << 4) | ((wc - 1) << 8) | (magic << 12);
+        st[lane * SSTRIDE + 0] = a;
+        st[lane * SSTRIDE + 1] = b;
+        st[lane * SSTRIDE + 2] = make_float4(c.x, c.y, FD(1.0f, c.y), __int_as_float(t));
+        st[lane * SSTRIDE + 3] = make_float4(__int_as_float(pk), 0.f, 0.f, 0.f);
       }
     }
+    int incl = n_items;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    sp[lane] = incl - n_items;
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();
+    for (int item = lane; item < total; item += 32) {
+      int j = 0;
+#pragma unroll
+      for (int step = 16; step > 0; step >>= 1)
+        if (sp[j + step] <= item) j += step;
+      const int k = item - sp[j];
+      const float4 f0 = st[j * SSTRIDE + 0], f1 = st[j * SSTRIDE + 1], f2 = st[j * SSTRIDE + 2];
+      const int pk = __float_as_int(st[j * SSTRIDE + 3].x);
+      const int wc = ((pk >> 8) & 15) + 1;
+      const int row = (k * (pk >> 12)) >> 16;
+      const int lx = (pk & 15) + (k - row * wc), ly = ((pk >> 4) & 15) + row;
+      const float x = s_ndcx[lx], y = s_ndcy[ly];
+      // f0 = (sx0, sy0, sz0, sx1), f1 = (sy1, sz1, sx2, sy2), f2 = (sz2, area, 1/area, t)
+      const float dx0 = FS(f0.x, x), dx1 = FS(f0.w, x), dx2 = FS(f1.z, x);
+      const float dy0 = FS(f0.y, y), dy1 = FS(f1.x, y), dy2 = FS(f1.w, y);
+      const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));
+      const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
+      const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
+      const float area = f2.y;
+      if (FM(e0, area) < 0.0f || FM(e1, area) < 0.0f || FM(e2, area) < 0.0f) continue;
+      const float bw = FM(e0, f2.z), u = FM(e1, f2.z), v = FM(e2, f2.z);
+      const float z = FA(FA(FM(bw, f0.z), FM(u, f1.y)), FM(v, f2.x));
+      if (z < -1.0f || z > 1.0f) continue;
+      const int p = ly * TILE + lx;
+      if (PEEL && z <= s_peel[p]) continue;
+      const unsigned long long key = pack_key(z, __float_as_int(f2.w));
+      if (key < s_key[p]) atomicMin(&s_key[p], key);
+    }
+    __syncwarp();
   }
   __syncthreads();
   if (!inside_img) return;
