@@ -129,15 +129,16 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
 
     if cfg == "cfg4":
         V, T, A = chain.base.shape[0], chain.tri.shape[0], 8
+        # Vertices are the shared [V, 4] soup (Nv = 1) transformed per view in-kernel.
+        add("raster_setup", V * 16 + T * 12)  # both layers share setup and tile lists
         for layer in (0, 1):
-            add("raster_setup", n * V * 16 + T * 12)
             add("raster_tiles", P * 16 + P * 16 + (P * 16 if layer else 0))
             add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A))
             # out_da never reaches the loss: the VJP runs without the DA terms.
             add("interp_bwd", 2 * V * A * 4 + T * 12 + P * (16 + 16 + 4 * A))
-            add("raster_bwd", 2 * n * V * 16 + T * 12 + P * 32 + P * 16)
-        add("aa_fwd", P * (8 * A + 16) + n * V * 16 + 2 * T * 12)
-        add("aa_bwd", P * (12 * A + 16) + 2 * n * V * 16 + 2 * T * 12)
+            add("raster_bwd", 2 * V * 16 + T * 12 + P * 32 + P * 16)
+        add("aa_fwd", P * (8 * A + 16) + V * 16 + 2 * T * 12)
+        add("aa_bwd", P * (12 * A + 16) + 2 * V * 16 + 2 * T * 12)
         add("mse", 2 * P * 12 * A)
     elif cfg == "cfg1":
         V, T, C = 3, 1, 3

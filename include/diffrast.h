@@ -126,6 +126,44 @@ DR_API dr_status dr_rasterize_bwd(dr_ctx* ctx, const float* pos, int V,
                            const float* d_rast, const float* d_rast_db,
                            float* d_pos);
 
+/* Depth peeling of num_layers layers in one call: layer 0 is the front-most
+ * surface, layer l peels layer l-1 exactly as chained rasterize(peelLayer:)
+ * calls do (Rasterize.swift:36-42, 384-392), and the results are identical to
+ * those calls.  Setup and tile binning run once for all layers.
+ *   rast[l]: [N, H, W, 4] out; rast_db: NULL or an array whose entries are
+ *   [N, H, W, 4] outputs or NULL.  The arrays are host arrays of device pointers. */
+DR_API dr_status dr_rasterize_layers_fwd(dr_ctx* ctx, const float* pos, int V,
+                                  const int32_t* tri, int T, const int32_t* ranges,
+                                  int N, int H, int W, int num_layers,
+                                  float* const* rast, float* const* rast_db);
+
+/* VJP of dr_rasterize_layers_fwd: d_pos = sum over layers of the per-layer
+ * rasterize VJP (a layer with d_rast[l] == NULL contributes nothing). */
+DR_API dr_status dr_rasterize_layers_bwd(dr_ctx* ctx, const float* pos, int V,
+                                  const int32_t* tri, int T, const int32_t* ranges,
+                                  int N, int H, int W, int num_layers,
+                                  const float* const* rast,
+                                  const float* const* d_rast,
+                                  const float* const* d_rast_db, float* d_pos);
+
+/* Per-view vertex transform ("xf") mode — no counterpart in the reference,
+ * which takes pre-transformed clip positions.  The clip position of vertex v
+ * in view n is M_n · verts[v] with xform = M [N, 4, 4] row-major, evaluated as
+ *   clip_r = ((M[r][0]·x + M[r][1]·y) + M[r][2]·z) + M[r][3]·w
+ * (each product and sum rounded separately), i.e. instanced mode with
+ * pos = einsum('nij,vj->nvi', M, verts) but without materialising [N, V, 4].
+ * Layers as in dr_rasterize_layers_fwd.  The VJP writes d_verts [V, 4], the
+ * gradient of the shared vertices summed over views (M_n^T applied). */
+DR_API dr_status dr_rasterize_xf_fwd(dr_ctx* ctx, const float* verts, int V,
+                              const float* xform, const int32_t* tri, int T,
+                              int N, int H, int W, int num_layers,
+                              float* const* rast, float* const* rast_db);
+DR_API dr_status dr_rasterize_xf_bwd(dr_ctx* ctx, const float* verts, int V,
+                              const float* xform, const int32_t* tri, int T,
+                              int N, int H, int W, int num_layers,
+                              const float* const* rast, const float* const* d_rast,
+                              const float* const* d_rast_db, float* d_verts);
+
 /* ---- interpolate (Interpolate.swift:43-132) ---------------------------- */
 
 /* Forward.  Replaces DiffRast.interpolate and diffrast_interp_fwd/_fwd_da
@@ -234,6 +272,18 @@ DR_API dr_status dr_antialias_bwd(dr_ctx* ctx, const float* color, int N, int H,
                            int V, const int32_t* tri, int T,
                            const int32_t* topo, const float* d_out,
                            float* d_color, float* d_pos);
+
+/* Antialias with per-view transformed vertices (see dr_rasterize_xf_fwd);
+ * no counterpart in the reference.  d_verts: out [V, 4]. */
+DR_API dr_status dr_antialias_xf_fwd(dr_ctx* ctx, const float* color, int N, int H,
+                              int W, int C, const float* rast, const float* verts,
+                              int V, const float* xform, const int32_t* tri, int T,
+                              const int32_t* topo, float* out);
+DR_API dr_status dr_antialias_xf_bwd(dr_ctx* ctx, const float* color, int N, int H,
+                              int W, int C, const float* rast, const float* verts,
+                              int V, const float* xform, const int32_t* tri, int T,
+                              const int32_t* topo, const float* d_out,
+                              float* d_color, float* d_verts);
 
 /* ---- loss helper (the MSE of the reference's examples) ------------------ */
 

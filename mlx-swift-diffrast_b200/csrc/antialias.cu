@@ -104,9 +104,17 @@ __device__ __forceinline__ int rast_tri(const float4* __restrict__ rast, int64_t
   return t;
 }
 
+// Clip position of vertex a in view pn: pos[pn, a] (instanced) or M_pn verts[a].
+template <bool XF>
+__device__ __forceinline__ float4 vpos(const float* __restrict__ pos, const Mat4& M, int V, int pn, int a) {
+  if (XF) return mat4_apply(M, ldg4(pos + (int64_t)a * 4));
+  return ldg4(pos + ((int64_t)pn * V + a) * 4);
+}
+
 // One direction of silhouetteBlock (Antialias.swift:189-325) for pixel
 // (pn, ph, pw) whose triangle is tri_p.  dir: 0 +x, 1 +y, 2 -x, 3 -y.
-__device__ SilDir sil_dir(const float4* __restrict__ rast, const float* __restrict__ pos,
+template <bool XF>
+__device__ SilDir sil_dir(const float4* __restrict__ rast, const float* __restrict__ pos, const Mat4& M,
                           const int32_t* __restrict__ tri, const int32_t* __restrict__ topo, int H, int W,
                           int V, int T, int pn, int ph, int pw, int tri_p, int dir, unsigned* err) {
   SilDir s;
@@ -129,7 +137,6 @@ __device__ SilDir sil_dir(const float4* __restrict__ rast, const float* __restri
   } else {
     fg = tri_n; target = -1;
   }
-  const float* pb = pos + (int64_t)pn * V * 4;
   const float pcx = (float)pw + 0.5f, pcy = (float)ph + 0.5f;
   const float ncx = (float)nw + 0.5f, ncy = (float)nh + 0.5f;
   int k_sel = -1, ie0 = -1, ie1 = -1;
@@ -138,7 +145,7 @@ __device__ SilDir sil_dir(const float4* __restrict__ rast, const float* __restri
     if (__ldg(topo + 3 * fg + kk) != target) continue;
     const int a = __ldg(tri + 3 * fg + (kk + 1) % 3), b = __ldg(tri + 3 * fg + (kk + 2) % 3);
     if (a < 0 || a >= V || b < 0 || b >= V) { dr_flag(err, DR_DEVERR_VERTEX); continue; }
-    const float4 pa = ldg4(pb + (int64_t)a * 4), pq = ldg4(pb + (int64_t)b * 4);
+    const float4 pa = vpos<XF>(pos, M, V, pn, a), pq = vpos<XF>(pos, M, V, pn, b);
     const float E0x = (pa.x / pa.w + 1.0f) * (float)W * 0.5f;
     const float E0y = (1.0f - pa.y / pa.w) * (float)H * 0.5f;
     const float E1x = (pq.x / pq.w + 1.0f) * (float)W * 0.5f;
@@ -201,20 +208,24 @@ __device__ __forceinline__ int64_t nbr_pix(int pn, int ph, int pw, int dir, int 
   return ((int64_t)pn * H + (ph + dh)) * W + (pw + dw);
 }
 
+template <bool XF>
 __global__ void k_aa_fwd(const float* __restrict__ color, int N, int H, int W, int C,
-                         const float4* __restrict__ rast, const float* __restrict__ pos, int V,
+                         const float4* __restrict__ rast, const float* __restrict__ pos,
+                         const float* __restrict__ xform, int V,
                          const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
                          float* __restrict__ out, unsigned* err) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (pix >= (int64_t)N * H * W) return;
   const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
   const int tri_p = rast_tri(rast, pix, T, err);
+  Mat4 M;
+  if (XF) M = load_mat4(xform + (int64_t)pn * 16);
   float beta[4];
   int64_t nb[4];
   bool any = false;
 #pragma unroll
   for (int d = 0; d < 4; ++d) {
-    const SilDir s = sil_dir(rast, pos, tri, topo, H, W, V, T, pn, ph, pw, tri_p, d, err);
+    const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, d, err);
     beta[d] = s.active ? s.beta : 0.0f;
     nb[d] = s.active ? nbr_pix(pn, ph, pw, d, H, W) : -1;
     any |= s.active;
@@ -239,9 +250,11 @@ __global__ void k_aa_fwd(const float* __restrict__ color, int N, int H, int W, i
   }
 }
 
-template <bool VEC>
-__device__ __forceinline__ void add_pos(float* p, float x, float y, float w) {
-  if (VEC) {
+template <bool VEC, bool XF>
+__device__ __forceinline__ void add_pos(float* p, const Mat4& M, float x, float y, float w) {
+  if (XF) {
+    atomicAdd(reinterpret_cast<float4*>(p), mat4_apply_t(M, make_float4(x, y, 0.0f, w)));
+  } else if (VEC) {
     atomicAdd(reinterpret_cast<float4*>(p), make_float4(x, y, 0.0f, w));
   } else {
     atomicAdd(p + 0, x);
@@ -250,9 +263,10 @@ __device__ __forceinline__ void add_pos(float* p, float x, float y, float w) {
   }
 }
 
-template <bool VEC>
+template <bool VEC, bool XF>
 __global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, int C,
-                         const float4* __restrict__ rast, const float* __restrict__ pos, int V,
+                         const float4* __restrict__ rast, const float* __restrict__ pos,
+                         const float* __restrict__ xform, int V,
                          const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
                          const float* __restrict__ d_out, float* __restrict__ d_color, float* __restrict__ d_pos,
                          unsigned* err) {
@@ -260,13 +274,15 @@ __global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, i
   if (pix >= (int64_t)N * H * W) return;
   const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
   const int tri_p = rast_tri(rast, pix, T, err);
+  Mat4 M;
+  if (XF) M = load_mat4(xform + (int64_t)pn * 16);
   const float* g = d_out + pix * C;
   const float halfW = (float)W * 0.5f, halfH = (float)H * 0.5f;
   float alpha_sum = 0.0f;
   // Own silhouettes: the (1 - sum beta) factor and d_pos (Antialias.swift:405-495).
 #pragma unroll 1
   for (int dir = 0; dir < 4; ++dir) {
-    const SilDir s = sil_dir(rast, pos, tri, topo, H, W, V, T, pn, ph, pw, tri_p, dir, err);
+    const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, dir, err);
     if (!s.active) continue;
     alpha_sum += s.beta;
     if (s.beta <= 0.0f || s.beta >= 1.0f) continue;
@@ -294,22 +310,22 @@ __global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, i
       dade0x = s.dbeta * ey_diff * (col_x - s.e1x) * inv_denom_sq;
       dade1x = s.dbeta * (-ey_diff) * (col_x - s.e0x) * inv_denom_sq;
     }
-    const int64_t pb = (int64_t)pn * V * 4;
+    const int64_t pb = XF ? 0 : (int64_t)pn * V * 4;
     {
-      const float4 pv = ldg4(pos + pb + (int64_t)s.ie0 * 4);
+      const float4 pv = vpos<XF>(pos, M, V, pn, s.ie0);
       const float inv_w = 1.0f / pv.w;
       const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
-      add_pos<VEC>(d_pos + pb + (int64_t)s.ie0 * 4, d_alpha * dade0x * halfW * inv_w,
-                   d_alpha * dade0y * (-halfH) * inv_w,
-                   d_alpha * (dade0x * (-halfW * nd_x) + dade0y * (halfH * nd_y)) * inv_w);
+      add_pos<VEC, XF>(d_pos + pb + (int64_t)s.ie0 * 4, M, d_alpha * dade0x * halfW * inv_w,
+                       d_alpha * dade0y * (-halfH) * inv_w,
+                       d_alpha * (dade0x * (-halfW * nd_x) + dade0y * (halfH * nd_y)) * inv_w);
     }
     {
-      const float4 pv = ldg4(pos + pb + (int64_t)s.ie1 * 4);
+      const float4 pv = vpos<XF>(pos, M, V, pn, s.ie1);
       const float inv_w = 1.0f / pv.w;
       const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
-      add_pos<VEC>(d_pos + pb + (int64_t)s.ie1 * 4, d_alpha * dade1x * halfW * inv_w,
-                   d_alpha * dade1y * (-halfH) * inv_w,
-                   d_alpha * (dade1x * (-halfW * nd_x) + dade1y * (halfH * nd_y)) * inv_w);
+      add_pos<VEC, XF>(d_pos + pb + (int64_t)s.ie1 * 4, M, d_alpha * dade1x * halfW * inv_w,
+                       d_alpha * dade1y * (-halfH) * inv_w,
+                       d_alpha * (dade1x * (-halfW * nd_x) + dade1y * (halfH * nd_y)) * inv_w);
     }
   }
   // Neighbours' betas toward this pixel: neighbour p = q - dir_d sees q in
@@ -326,7 +342,7 @@ __global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, i
     const int64_t p = ((int64_t)pn * H + sh) * W + sw;
     const int tri_s = rast_tri(rast, p, T, err);
     if (tri_s == tri_p) continue;  // no silhouette between equal ids
-    const SilDir s = sil_dir(rast, pos, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
+    const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
     if (s.active) { nbeta[d] = s.beta; nsrc[d] = p; }
   }
   const float keep = 1.0f - alpha_sum;
@@ -397,38 +413,82 @@ extern "C" dr_status dr_antialias_construct_topology_hash(dr_ctx* ctx, const int
   return DR_OK;
 }
 
-extern "C" dr_status dr_antialias_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
-                                      const float* rast, const float* pos, int V, const int32_t* tri, int T,
-                                      const int32_t* topo, float* out) {
-  DR_ENTER(ctx);
+namespace {
+
+dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
+                 const float* pos, const float* xform, int V, const int32_t* tri, int T, const int32_t* topo,
+                 float* out) {
   dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
   if (st != DR_OK) return st;
   DR_REQUIRE(ctx, out, "antialias: out required");
   const int64_t P = (int64_t)N * H * W;
+  const float4* r4 = reinterpret_cast<const float4*>(rast);
   DR_TB(ctx);
-  k_aa_fwd<<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, reinterpret_cast<const float4*>(rast),
-                                                       pos, V, tri, T, topo, out, ctx->d_err);
+  if (xform)
+    k_aa_fwd<true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, xform, V, tri, T, topo,
+                                                                out, ctx->d_err);
+  else
+    k_aa_fwd<false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, nullptr, V, tri, T,
+                                                                 topo, out, ctx->d_err);
   DR_LAUNCHED(ctx, "aa_fwd");
   return DR_OK;
+}
+
+dr_status aa_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
+                 const float* pos, const float* xform, int V, const int32_t* tri, int T, const int32_t* topo,
+                 const float* d_out, float* d_color, float* d_pos) {
+  dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
+  if (st != DR_OK) return st;
+  DR_REQUIRE(ctx, d_out && d_color && d_pos, "antialias_bwd: d_out, d_color, d_pos required");
+  const size_t npos = (size_t)(xform ? 1 : N) * V * 4;
+  DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream), "antialias_bwd memset");
+  const int64_t P = (int64_t)N * H * W;
+  const float4* r4 = reinterpret_cast<const float4*>(rast);
+  DR_TB(ctx);
+  if (xform) {
+    DR_REQUIRE(ctx, aligned16(d_pos), "antialias_xf_bwd: d_verts must be 16-byte aligned");
+    k_aa_bwd<true, true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, xform, V, tri, T,
+                                                                     topo, d_out, d_color, d_pos, ctx->d_err);
+  } else if (aligned16(d_pos)) {
+    k_aa_bwd<true, false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, nullptr, V, tri,
+                                                                      T, topo, d_out, d_color, d_pos, ctx->d_err);
+  } else {
+    k_aa_bwd<false, false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, nullptr, V, tri,
+                                                                       T, topo, d_out, d_color, d_pos, ctx->d_err);
+  }
+  DR_LAUNCHED(ctx, "aa_bwd");
+  return DR_OK;
+}
+
+}  // namespace
+
+extern "C" dr_status dr_antialias_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                      const float* rast, const float* pos, int V, const int32_t* tri, int T,
+                                      const int32_t* topo, float* out) {
+  DR_ENTER(ctx);
+  return aa_fwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, out);
 }
 
 extern "C" dr_status dr_antialias_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
                                       const float* rast, const float* pos, int V, const int32_t* tri, int T,
                                       const int32_t* topo, const float* d_out, float* d_color, float* d_pos) {
   DR_ENTER(ctx);
-  dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
-  if (st != DR_OK) return st;
-  DR_REQUIRE(ctx, d_out && d_color && d_pos, "antialias_bwd: d_out, d_color, d_pos required");
-  DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * (size_t)N * V * 4, ctx->stream), "antialias_bwd memset");
-  const int64_t P = (int64_t)N * H * W;
-  const float4* r4 = reinterpret_cast<const float4*>(rast);
-  DR_TB(ctx);
-  if (aligned16(d_pos))
-    k_aa_bwd<true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, V, tri, T, topo, d_out,
-                                                               d_color, d_pos, ctx->d_err);
-  else
-    k_aa_bwd<false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, V, tri, T, topo,
-                                                                d_out, d_color, d_pos, ctx->d_err);
-  DR_LAUNCHED(ctx, "aa_bwd");
-  return DR_OK;
+  return aa_bwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, d_out, d_color, d_pos);
+}
+
+extern "C" dr_status dr_antialias_xf_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                         const float* rast, const float* verts, int V, const float* xform,
+                                         const int32_t* tri, int T, const int32_t* topo, float* out) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, xform && aligned16(xform), "antialias_xf: xform [N,4,4] must be given and 16-byte aligned");
+  return aa_fwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, out);
+}
+
+extern "C" dr_status dr_antialias_xf_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                         const float* rast, const float* verts, int V, const float* xform,
+                                         const int32_t* tri, int T, const int32_t* topo, const float* d_out,
+                                         float* d_color, float* d_verts) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, xform && aligned16(xform), "antialias_xf_bwd: xform [N,4,4] must be given and 16-byte aligned");
+  return aa_bwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, d_out, d_color, d_verts);
 }

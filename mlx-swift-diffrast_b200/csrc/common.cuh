@@ -119,3 +119,56 @@ __device__ __forceinline__ int dr_floor_i(float x) { return __float2int_rd(x); }
 __device__ __forceinline__ float4 ldg4(const float* p) {
   return __ldg(reinterpret_cast<const float4*>(p));
 }
+
+// Per-view vertex transform (the "xf" entry points): clip position of vertex v
+// in view n is M_n v with M_n a row-major 4x4, evaluated in this fixed order
+// (each product and sum rounded separately):
+//   out_r = ((M[r][0] vx + M[r][1] vy) + M[r][2] vz) + M[r][3] vw
+struct Mat4 {
+  float4 r0, r1, r2, r3;
+};
+
+__device__ __forceinline__ Mat4 load_mat4(const float* m) {
+  Mat4 M;
+  M.r0 = ldg4(m); M.r1 = ldg4(m + 4); M.r2 = ldg4(m + 8); M.r3 = ldg4(m + 12);
+  return M;
+}
+
+__device__ __forceinline__ float dot4_ordered(float4 a, float4 v) {
+  return __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(a.x, v.x), __fmul_rn(a.y, v.y)), __fmul_rn(a.z, v.z)),
+                   __fmul_rn(a.w, v.w));
+}
+
+__device__ __forceinline__ float4 mat4_apply(const Mat4& M, float4 v) {
+  return make_float4(dot4_ordered(M.r0, v), dot4_ordered(M.r1, v), dot4_ordered(M.r2, v), dot4_ordered(M.r3, v));
+}
+
+// M^T g: the gradient of M v with respect to v.
+__device__ __forceinline__ float4 mat4_apply_t(const Mat4& M, float4 g) {
+  return make_float4(M.r0.x * g.x + M.r1.x * g.y + M.r2.x * g.z + M.r3.x * g.w,
+                     M.r0.y * g.x + M.r1.y * g.y + M.r2.y * g.z + M.r3.y * g.w,
+                     M.r0.z * g.x + M.r1.z * g.y + M.r2.z * g.z + M.r3.z * g.w,
+                     M.r0.w * g.x + M.r1.w * g.y + M.r2.w * g.z + M.r3.w * g.w);
+}
+
+// Warp-level segmented suffix sum over runs of equal keys: after the call the
+// first lane of each run holds the run's total.  seg_end is one past the
+// caller's run.  All 32 lanes must call it.
+__device__ __forceinline__ float warp_seg_sum(float v, int lane, int seg_end) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_down_sync(0xffffffffu, v, o);
+    if (lane + o < seg_end) v += y;
+  }
+  return v;
+}
+
+// Run structure of a per-lane key in a warp: returns seg_end and whether this
+// lane is the run's head.
+__device__ __forceinline__ int warp_runs(long long key, int lane, bool& head) {
+  const long long key_up = __shfl_up_sync(0xffffffffu, key, 1);
+  const unsigned heads = __ballot_sync(0xffffffffu, lane == 0 || key != key_up);
+  const unsigned after = lane == 31 ? 0u : (heads >> (lane + 1));
+  head = (heads >> lane) & 1u;
+  return after ? lane + __ffs(after) : 32;
+}

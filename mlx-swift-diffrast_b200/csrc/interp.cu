@@ -112,7 +112,10 @@ __global__ void k_interp_fwd(const float* __restrict__ attr, bool attr_shared, i
   }
 }
 
-// Fused VJP: d_attr (atomics), d_rast, d_rast_db.
+// Fused VJP: d_attr, d_rast, d_rast_db in one pass.  Pixels of a warp that hit
+// the same triangle (runs along the row) first sum their d_attr contributions
+// with warp shuffles, so each run issues one set of atomics instead of one per
+// pixel.  Channels go in groups of four (float4 atomics when VEC4).
 template <bool VEC4, bool DA, bool IDX>
 __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, int V, int A,
                              const float4* __restrict__ rast, int64_t P, int64_t HW,
@@ -121,22 +124,24 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
                              const float* __restrict__ d_out, const float* __restrict__ d_out_da,
                              float* __restrict__ d_attr, float4* __restrict__ d_rast,
                              float4* __restrict__ d_rast_db, unsigned* err) {
-  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= P) return;
-  const float4 r = __ldg(rast + pix);
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const bool in = pix < P;
+  float4 r = make_float4(0.f, 0.f, 0.f, -1.f);
+  if (in) r = __ldg(rast + pix);
   int t = (int)r.w - 1;
-  int i0, i1, i2;
-  bool hit = t >= 0;
+  int i0 = 0, i1 = 0, i2 = 0;
+  bool hit = in && t >= 0;
   if (hit && t >= T) { dr_flag(err, DR_DEVERR_TRI_ID); hit = false; }
   if (hit && !tri_verts(tri, t, V, i0, i1, i2)) { dr_flag(err, DR_DEVERR_VERTEX); hit = false; }
-  if (!hit) {
-    d_rast[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (DA) d_rast_db[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
-    return;
-  }
+  const int n = in ? (int)(pix / HW) : 0;
+  // Run key: the triangle, and the view when every view has its own attributes.
+  const long long key = hit ? ((attr_shared ? 0ll : (long long)n * T) + t) : -1ll - (long long)lane;
+  bool head;
+  const int seg_end = warp_runs(key, lane, head);
+
   const float u = r.x, v = r.y;
   const float bw = 1.0f - u - v;
-  const int n = (int)(pix / HW);
   const int64_t nb = attr_shared ? 0 : (int64_t)n * V * A;
   const float* a0p = attr + nb + (int64_t)i0 * A;
   const float* a1p = attr + nb + (int64_t)i1 * A;
@@ -145,49 +150,105 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
   float* g1p = d_attr + nb + (int64_t)i1 * A;
   float* g2p = d_attr + nb + (int64_t)i2 * A;
   const float* g = d_out + pix * A;
+  const float* gd = DA ? d_out_da + pix * 2 * K : nullptr;
+  float4 db = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (DA && hit) db = __ldg(rast_db + pix);
   float du = 0.0f, dv = 0.0f;
-  if (VEC4) {
-    for (int a = 0; a < A; a += 4) {
-      const float4 ga = ldg4(g + a);
-      const float4 x0 = ldg4(a0p + a), x1 = ldg4(a1p + a), x2 = ldg4(a2p + a);
-      atomicAdd(reinterpret_cast<float4*>(g0p + a), make_float4(bw * ga.x, bw * ga.y, bw * ga.z, bw * ga.w));
-      atomicAdd(reinterpret_cast<float4*>(g1p + a), make_float4(u * ga.x, u * ga.y, u * ga.z, u * ga.w));
-      atomicAdd(reinterpret_cast<float4*>(g2p + a), make_float4(v * ga.x, v * ga.y, v * ga.z, v * ga.w));
-      du += (x1.x - x0.x) * ga.x; dv += (x2.x - x0.x) * ga.x;
-      du += (x1.y - x0.y) * ga.y; dv += (x2.y - x0.y) * ga.y;
-      du += (x1.z - x0.z) * ga.z; dv += (x2.z - x0.z) * ga.z;
-      du += (x1.w - x0.w) * ga.w; dv += (x2.w - x0.w) * ga.w;
+  float d_udx = 0.0f, d_udy = 0.0f, d_vdx = 0.0f, d_vdy = 0.0f;
+  for (int a = 0; a < A; a += 4) {
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+    if (hit) {
+      float ga[4], x0[4], x1[4], x2[4];
+      if (VEC4) {
+        const float4 q = ldg4(g + a), p0 = ldg4(a0p + a), p1 = ldg4(a1p + a), p2 = ldg4(a2p + a);
+        ga[0] = q.x; ga[1] = q.y; ga[2] = q.z; ga[3] = q.w;
+        x0[0] = p0.x; x0[1] = p0.y; x0[2] = p0.z; x0[3] = p0.w;
+        x1[0] = p1.x; x1[1] = p1.y; x1[2] = p1.z; x1[3] = p1.w;
+        x2[0] = p2.x; x2[1] = p2.y; x2[2] = p2.z; x2[3] = p2.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const bool ok = a + j < A;
+          ga[j] = ok ? __ldg(g + a + j) : 0.f;
+          x0[j] = ok ? __ldg(a0p + a + j) : 0.f;
+          x1[j] = ok ? __ldg(a1p + a + j) : 0.f;
+          x2[j] = ok ? __ldg(a2p + a + j) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        c0[j] = bw * ga[j];
+        c1[j] = u * ga[j];
+        c2[j] = v * ga[j];
+        du += (x1[j] - x0[j]) * ga[j];
+        dv += (x2[j] - x0[j]) * ga[j];
+      }
+      if (DA && !IDX) {
+        // .all: channel a + j has its (d/dx, d/dy) cotangent at 2(a + j).
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (!VEC4 && a + j >= A) break;
+          const float gx = __ldg(gd + 2 * (a + j)), gy = __ldg(gd + 2 * (a + j) + 1);
+          const float u_term = gx * db.x + gy * db.y;
+          const float v_term = gx * db.z + gy * db.w;
+          c0[j] += -u_term - v_term;
+          c1[j] += u_term;
+          c2[j] += v_term;
+          const float d01 = x1[j] - x0[j], d02 = x2[j] - x0[j];
+          d_udx += d01 * gx;
+          d_udy += d01 * gy;
+          d_vdx += d02 * gx;
+          d_vdy += d02 * gy;
+        }
+      }
     }
-  } else {
-    for (int a = 0; a < A; ++a) {
-      const float ga = __ldg(g + a);
-      atomicAdd(g0p + a, bw * ga);
-      atomicAdd(g1p + a, u * ga);
-      atomicAdd(g2p + a, v * ga);
-      const float x0 = __ldg(a0p + a), x1 = __ldg(a1p + a), x2 = __ldg(a2p + a);
-      du += (x1 - x0) * ga;
-      dv += (x2 - x0) * ga;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      c0[j] = warp_seg_sum(c0[j], lane, seg_end);
+      c1[j] = warp_seg_sum(c1[j], lane, seg_end);
+      c2[j] = warp_seg_sum(c2[j], lane, seg_end);
     }
+    if (hit && head) {
+      if (VEC4) {
+        atomicAdd(reinterpret_cast<float4*>(g0p + a), make_float4(c0[0], c0[1], c0[2], c0[3]));
+        atomicAdd(reinterpret_cast<float4*>(g1p + a), make_float4(c1[0], c1[1], c1[2], c1[3]));
+        atomicAdd(reinterpret_cast<float4*>(g2p + a), make_float4(c2[0], c2[1], c2[2], c2[3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (a + j >= A) break;
+          atomicAdd(g0p + a + j, c0[j]);
+          atomicAdd(g1p + a + j, c1[j]);
+          atomicAdd(g2p + a + j, c2[j]);
+        }
+      }
+    }
+  }
+  if (!in) return;
+  if (!hit) {
+    d_rast[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (DA) d_rast_db[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
   }
   d_rast[pix] = make_float4(du, dv, 0.0f, 0.0f);
   if (DA) {
-    const float4 db = __ldg(rast_db + pix);
-    const float* gd = d_out_da + pix * 2 * K;
-    float d_udx = 0.0f, d_udy = 0.0f, d_vdx = 0.0f, d_vdy = 0.0f;
-    for (int k = 0; k < K; ++k) {
-      const int a = IDX ? idx.k[k] : k;
-      const float gx = __ldg(gd + 2 * k), gy = __ldg(gd + 2 * k + 1);
-      const float u_term = gx * db.x + gy * db.y;
-      const float v_term = gx * db.z + gy * db.w;
-      atomicAdd(g0p + a, -u_term - v_term);
-      atomicAdd(g1p + a, u_term);
-      atomicAdd(g2p + a, v_term);
-      const float x0 = __ldg(a0p + a), x1 = __ldg(a1p + a), x2 = __ldg(a2p + a);
-      const float d01 = x1 - x0, d02 = x2 - x0;
-      d_udx += d01 * gx;
-      d_udy += d01 * gy;
-      d_vdx += d02 * gx;
-      d_vdy += d02 * gy;
+    if (IDX) {
+      // .indices: arbitrary (possibly repeated) attribute indices.
+      for (int k = 0; k < K; ++k) {
+        const int a = idx.k[k];
+        const float gx = __ldg(gd + 2 * k), gy = __ldg(gd + 2 * k + 1);
+        const float u_term = gx * db.x + gy * db.y;
+        const float v_term = gx * db.z + gy * db.w;
+        atomicAdd(g0p + a, -u_term - v_term);
+        atomicAdd(g1p + a, u_term);
+        atomicAdd(g2p + a, v_term);
+        const float x0 = __ldg(a0p + a), x1 = __ldg(a1p + a), x2 = __ldg(a2p + a);
+        const float d01 = x1 - x0, d02 = x2 - x0;
+        d_udx += d01 * gx;
+        d_udy += d01 * gy;
+        d_vdx += d02 * gx;
+        d_vdy += d02 * gy;
+      }
     }
     d_rast_db[pix] = make_float4(d_udx, d_udy, d_vdx, d_vdy);
   }

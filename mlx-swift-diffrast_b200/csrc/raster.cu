@@ -97,7 +97,8 @@ __device__ __forceinline__ bool finite3(float a, float b, float c) {
   return isfinite(a) && isfinite(b) && isfinite(c);
 }
 
-__global__ void k_raster_setup(const float* __restrict__ pos, int V, const int32_t* __restrict__ tri,
+__global__ void k_raster_setup(const float* __restrict__ pos, const float* __restrict__ xform, int V,
+                               const int32_t* __restrict__ tri,
                                int T, const int32_t* __restrict__ ranges, int N, int H, int W,
                                int ntx, int nty, float4* __restrict__ rec,
                                uint32_t* __restrict__ tile_count, unsigned* err) {
@@ -112,7 +113,7 @@ __global__ void k_raster_setup(const float* __restrict__ pos, int V, const int32
   if (ranges) {
     int rs = __ldg(ranges + 2 * n), rc = __ldg(ranges + 2 * n + 1);
     ok = !(t < rs || t >= rs + rc);
-  } else {
+  } else if (!xform) {
     pos_n_base = (int64_t)n * V * 4;
   }
   int i0 = 0, i1 = 0, i2 = 0;
@@ -128,6 +129,12 @@ __global__ void k_raster_setup(const float* __restrict__ pos, int V, const int32
     p0 = ldg4(pos + pos_n_base + (int64_t)i0 * 4);
     p1 = ldg4(pos + pos_n_base + (int64_t)i1 * 4);
     p2 = ldg4(pos + pos_n_base + (int64_t)i2 * 4);
+    if (xform) {
+      const Mat4 M = load_mat4(xform + (int64_t)n * 16);
+      p0 = mat4_apply(M, p0);
+      p1 = mat4_apply(M, p1);
+      p2 = mat4_apply(M, p2);
+    }
     ok = !(p0.w <= 0.0f || p1.w <= 0.0f || p2.w <= 0.0f);
   }
   if (!ok) {
@@ -207,7 +214,7 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   __shared__ float s_peel[TILE_PIX];
   __shared__ float s_ndcx[TILE], s_ndcy[TILE];
   __shared__ float4 s_stage[WARPS][32 * SSTRIDE];
-  __shared__ int s_pre[WARPS][32];
+  __shared__ unsigned s_next;
 
   const int ntiles = ntx * nty;
   const int n = blockIdx.x / ntiles;
@@ -229,6 +236,7 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   }
   if (tid < TILE) s_ndcx[tid] = ndc_x_of(tx0 + tid, W);
   else if (tid < 2 * TILE) s_ndcy[tid - TILE] = ndc_y_of(ty0 + tid - TILE, H);
+  if (tid == 0) s_next = 0u;
   __syncthreads();
 
   const uint32_t gt = (uint32_t)blockIdx.x;
@@ -236,28 +244,32 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   const int64_t rec_view = (int64_t)n * T;
   const int warp = tid >> 5, lane = tid & 31;
   float4* st = s_stage[warp];
-  int* sp = s_pre[warp];
-  for (uint32_t base = (uint32_t)warp * 32u; base < cnt; base += TILE_PIX) {
+  const unsigned below = (1u << lane) - 1u;  // lanes 0 .. lane-1
+  for (;;) {
+    // Batches of 32 candidates are handed out dynamically, so warps finish together.
+    unsigned b = 0;
+    if (lane == 0) b = atomicAdd(&s_next, 1u);
+    const uint32_t base = __shfl_sync(0xffffffffu, b, 0) * 32u;
+    if (base >= cnt) break;
     const uint32_t i = base + lane;
     int n_items = 0;
     if (i < cnt) {
       const int t = __ldg(list + begin + i);
       const float4 a = __ldg(rec + 3 * (rec_view + t) + 0);
-      const float4 b = __ldg(rec + 3 * (rec_view + t) + 1);
+      const float4 bb = __ldg(rec + 3 * (rec_view + t) + 1);
       const float4 c = __ldg(rec + 3 * (rec_view + t) + 2);
       const unsigned xs = __float_as_uint(c.z), ys = __float_as_uint(c.w);
       const int cx0 = max((int)(xs & 0xffffu), tx0), cx1 = min((int)(xs >> 16), tx0 + TILE - 1);
       const int cy0 = max((int)(ys & 0xffffu), ty0), cy1 = min((int)(ys >> 16), ty0 + TILE - 1);
-      const int wc = cx1 - cx0 + 1, hc = cy1 - cy0 + 1;
-      if (wc > 0 && hc > 0) {
-        n_items = wc * hc;
-        const int magic = (65536 + wc - 1) / wc;  // (k * magic) >> 16 == k / wc for k < 256
-        const int pk = (cx0 - tx0) | ((cy0 - ty0) << 4) | ((wc - 1) << 8) | (magic << 12);
-        st[lane * SSTRIDE + 0] = a;
-        st[lane * SSTRIDE + 1] = b;
-        st[lane * SSTRIDE + 2] = make_float4(c.x, c.y, FD(1.0f, c.y), __int_as_float(t));
-        st[lane * SSTRIDE + 3] = make_float4(__int_as_float(pk), 0.f, 0.f, 0.f);
-      }
+      // A listed candidate's rectangle always meets its tile (it was binned by it).
+      const int wc = max(cx1 - cx0 + 1, 1), hc = max(cy1 - cy0 + 1, 1);
+      n_items = wc * hc;
+      const int magic = (65536 + wc - 1) / wc;  // (k * magic) >> 16 == k / wc for k < 256
+      const int pk = (cx0 - tx0) | ((cy0 - ty0) << 4) | ((wc - 1) << 8) | (magic << 12);
+      st[lane * SSTRIDE + 0] = a;
+      st[lane * SSTRIDE + 1] = bb;
+      st[lane * SSTRIDE + 2] = make_float4(c.x, c.y, FD(1.0f, c.y), __int_as_float(t));
+      st[lane * SSTRIDE + 3] = make_float4(__int_as_float(pk), 0.f, 0.f, 0.f);
     }
     int incl = n_items;
 #pragma unroll
@@ -265,15 +277,24 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
       const int y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    sp[lane] = incl - n_items;
+    const int excl = incl - n_items;
     const int total = __shfl_sync(0xffffffffu, incl, 31);
     __syncwarp();
-    for (int item = lane; item < total; item += 32) {
-      int j = 0;
-#pragma unroll
-      for (int step = 16; step > 0; step >>= 1)
-        if (sp[j + step] <= item) j += step;
-      const int k = item - sp[j];
+    // Round r covers items [32r, 32r + 32).  Every active candidate owns >= 1
+    // item, so lane L's candidate is the one covering item 32r (c0) plus the
+    // number of candidates that start at positions 1..L of the round.
+    int c0 = 0;
+    for (int r0 = 0; r0 < total; r0 += 32) {
+      const unsigned pos_bit = (n_items > 0 && excl >= r0 && excl < r0 + 32) ? (1u << (excl - r0)) : 0u;
+      const unsigned starts = __reduce_or_sync(0xffffffffu, pos_bit) & ~1u;
+      const int j = c0 + __popc(starts & (below | (1u << lane)));
+      const int j31 = c0 + __popc(starts);
+      const int end31 = __shfl_sync(0xffffffffu, incl, j31 & 31);
+      const int sj = __shfl_sync(0xffffffffu, excl, j & 31);
+      c0 = j31 + (end31 == r0 + 32 ? 1 : 0);
+      const int item = r0 + lane;
+      if (item >= total) continue;
+      const int k = item - sj;
       const float4 f0 = st[j * SSTRIDE + 0], f1 = st[j * SSTRIDE + 1], f2 = st[j * SSTRIDE + 2];
       const int pk = __float_as_int(st[j * SSTRIDE + 3].x);
       const int wc = ((pk >> 8) & 15) + 1;
@@ -329,101 +350,136 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   }
 }
 
-// d_pos: Rasterize.swift:637-812, one thread per pixel, float4 atomics.
-template <bool DB, bool VEC>
-__global__ void k_raster_bwd(const float* __restrict__ pos, int V, const int32_t* __restrict__ tri,
-                             int T, bool shared_pos, int N, int H, int W,
+// d_pos: Rasterize.swift:637-812, one thread per pixel.  Pixels of a warp that
+// hit the same (view, triangle) first sum their 12 vertex gradients with warp
+// shuffles; the first pixel of each run issues the float4 atomics.  With a
+// per-view transform (XF) the clip-space gradient g of vertex v is mapped to
+// the shared vertex buffer as M_n^T g.
+template <bool DB, bool VEC, bool XF>
+__global__ void k_raster_bwd(const float* __restrict__ pos, const float* __restrict__ xform, int V,
+                             const int32_t* __restrict__ tri, int T, bool shared_pos, int N, int H, int W,
                              const float4* __restrict__ rast, const float4* __restrict__ d_rast,
                              const float4* __restrict__ d_rast_db, float* __restrict__ d_pos,
                              unsigned* err) {
-  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= (int64_t)N * H * W) return;
-  const float4 r = __ldg(rast + pix);
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t P = (int64_t)N * H * W;
+  const bool in = pix < P;
+  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (in) r = __ldg(rast + pix);
   const int t = (int)r.w - 1;
-  if (t < 0) return;
-  if (t >= T) { dr_flag(err, DR_DEVERR_TRI_ID); return; }
-  const int pw = (int)(pix % W);
-  const int ph = (int)((pix / W) % H);
-  const int pn = (int)(pix / ((int64_t)H * W));
-  const float u_val = r.x, v_val = r.y;
-  const float bw_val = 1.0f - u_val - v_val;
-  const float4 g = __ldg(d_rast + pix);
-  const float d_u = g.x, d_v = g.y, d_z = g.z;
-  float d_db0 = 0.f, d_db1 = 0.f, d_db2 = 0.f, d_db3 = 0.f;
-  if (DB) {
-    const float4 gd = __ldg(d_rast_db + pix);
-    d_db0 = gd.x; d_db1 = gd.y; d_db2 = gd.z; d_db3 = gd.w;
+  bool hit = in && t >= 0;
+  if (hit && t >= T) { dr_flag(err, DR_DEVERR_TRI_ID); hit = false; }
+  int i0 = 0, i1 = 0, i2 = 0;
+  if (hit) {
+    i0 = __ldg(tri + 3 * t); i1 = __ldg(tri + 3 * t + 1); i2 = __ldg(tri + 3 * t + 2);
+    if (i0 < 0 || i0 >= V || i1 < 0 || i1 >= V || i2 < 0 || i2 >= V) {
+      dr_flag(err, DR_DEVERR_VERTEX);
+      hit = false;
+    }
   }
-  const float Px = 2.0f * ((float)pw + 0.5f) / (float)W - 1.0f;
-  const float Py = 1.0f - 2.0f * ((float)ph + 0.5f) / (float)H;
-  const int64_t pos_n_base = shared_pos ? 0 : (int64_t)pn * V * 4;
-  const int i0 = __ldg(tri + 3 * t), i1 = __ldg(tri + 3 * t + 1), i2 = __ldg(tri + 3 * t + 2);
-  if (i0 < 0 || i0 >= V || i1 < 0 || i1 >= V || i2 < 0 || i2 >= V) {
-    dr_flag(err, DR_DEVERR_VERTEX);
-    return;
+  const int pn = in ? (int)(pix / ((int64_t)H * W)) : 0;
+  const int64_t pos_n_base = (shared_pos || XF) ? 0 : (int64_t)pn * V * 4;
+  float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0, g2 = g0;
+  Mat4 M;
+  if (XF && hit) M = load_mat4(xform + (int64_t)pn * 16);
+  if (hit) {
+    const int pw = (int)(pix % W);
+    const int ph = (int)((pix / W) % H);
+    const float u_val = r.x, v_val = r.y;
+    const float bw_val = 1.0f - u_val - v_val;
+    const float4 g = __ldg(d_rast + pix);
+    const float d_u = g.x, d_v = g.y, d_z = g.z;
+    float d_db0 = 0.f, d_db1 = 0.f, d_db2 = 0.f, d_db3 = 0.f;
+    if (DB) {
+      const float4 gd = __ldg(d_rast_db + pix);
+      d_db0 = gd.x; d_db1 = gd.y; d_db2 = gd.z; d_db3 = gd.w;
+    }
+    const float Px = 2.0f * ((float)pw + 0.5f) / (float)W - 1.0f;
+    const float Py = 1.0f - 2.0f * ((float)ph + 0.5f) / (float)H;
+    float4 q0 = ldg4(pos + pos_n_base + (int64_t)i0 * 4);
+    float4 q1 = ldg4(pos + pos_n_base + (int64_t)i1 * 4);
+    float4 q2 = ldg4(pos + pos_n_base + (int64_t)i2 * 4);
+    if (XF) {
+      q0 = mat4_apply(M, q0);
+      q1 = mat4_apply(M, q1);
+      q2 = mat4_apply(M, q2);
+    }
+    const float w0 = q0.w, w1 = q1.w, w2 = q2.w;
+    const float sx0 = q0.x / w0, sy0 = q0.y / w0, sz0 = q0.z / w0;
+    const float sx1 = q1.x / w1, sy1 = q1.y / w1, sz1 = q1.z / w1;
+    const float sx2 = q2.x / w2, sy2 = q2.y / w2, sz2 = q2.z / w2;
+    const float area = (sx1 - sx0) * (sy2 - sy0) - (sx2 - sx0) * (sy1 - sy0);
+    const float inv_area = 1.0f / area;
+    const float dadsx0 = sy1 - sy2, dadsx1 = sy2 - sy0, dadsx2 = sy0 - sy1;
+    const float dadsy0 = sx2 - sx1, dadsy1 = sx0 - sx2, dadsy2 = sx1 - sx0;
+    const float de1dsx0 = Py - sy2, de1dsx2 = sy0 - Py, de1dsy0 = sx2 - Px, de1dsy2 = Px - sx0;
+    const float de2dsx0 = sy1 - Py, de2dsx1 = Py - sy0, de2dsy0 = Px - sx1, de2dsy1 = sx0 - Px;
+    const float dudsx0 = (de1dsx0 - u_val * dadsx0) * inv_area;
+    const float dudsx1 = (0.0f - u_val * dadsx1) * inv_area;
+    const float dudsx2 = (de1dsx2 - u_val * dadsx2) * inv_area;
+    const float dudsy0 = (de1dsy0 - u_val * dadsy0) * inv_area;
+    const float dudsy1 = (0.0f - u_val * dadsy1) * inv_area;
+    const float dudsy2 = (de1dsy2 - u_val * dadsy2) * inv_area;
+    const float dvdsx0 = (de2dsx0 - v_val * dadsx0) * inv_area;
+    const float dvdsx1 = (de2dsx1 - v_val * dadsx1) * inv_area;
+    const float dvdsx2 = (0.0f - v_val * dadsx2) * inv_area;
+    const float dvdsy0 = (de2dsy0 - v_val * dadsy0) * inv_area;
+    const float dvdsy1 = (de2dsy1 - v_val * dadsy1) * inv_area;
+    const float dvdsy2 = (0.0f - v_val * dadsy2) * inv_area;
+    const float dsz10 = sz1 - sz0, dsz20 = sz2 - sz0;
+    float dsx0 = d_u * dudsx0 + d_v * dvdsx0 + d_z * (dudsx0 * dsz10 + dvdsx0 * dsz20);
+    float dsx1 = d_u * dudsx1 + d_v * dvdsx1 + d_z * (dudsx1 * dsz10 + dvdsx1 * dsz20);
+    float dsx2 = d_u * dudsx2 + d_v * dvdsx2 + d_z * (dudsx2 * dsz10 + dvdsx2 * dsz20);
+    float dsy0 = d_u * dudsy0 + d_v * dvdsy0 + d_z * (dudsy0 * dsz10 + dvdsy0 * dsz20);
+    float dsy1 = d_u * dudsy1 + d_v * dvdsy1 + d_z * (dudsy1 * dsz10 + dvdsy1 * dsz20);
+    float dsy2 = d_u * dudsy2 + d_v * dvdsy2 + d_z * (dudsy2 * dsz10 + dvdsy2 * dsz20);
+    const float dsz0_s = d_z * bw_val, dsz1_s = d_z * u_val, dsz2_s = d_z * v_val;
+    if (DB) {
+      const float Kx = 2.0f / (float)W, Ky = -2.0f / (float)H;
+      const float rdb0 = (sy2 - sy0) * Kx * inv_area;
+      const float rdb1 = (sx0 - sx2) * Ky * inv_area;
+      const float rdb2 = (sy0 - sy1) * Kx * inv_area;
+      const float rdb3 = (sx1 - sx0) * Ky * inv_area;
+      const float s = d_db0 * rdb0 + d_db1 * rdb1 + d_db2 * rdb2 + d_db3 * rdb3;
+      dsx0 += (-s * dadsx0) * inv_area;
+      dsx1 += (-s * dadsx1) * inv_area;
+      dsx2 += (-s * dadsx2) * inv_area;
+      dsy0 += (-s * dadsy0) * inv_area;
+      dsy1 += (-s * dadsy1) * inv_area;
+      dsy2 += (-s * dadsy2) * inv_area;
+      dsy0 += d_db0 * (-Kx) * inv_area;
+      dsy2 += d_db0 * (Kx) * inv_area;
+      dsx0 += d_db1 * (Ky) * inv_area;
+      dsx2 += d_db1 * (-Ky) * inv_area;
+      dsy0 += d_db2 * (Kx) * inv_area;
+      dsy1 += d_db2 * (-Kx) * inv_area;
+      dsx0 += d_db3 * (-Ky) * inv_area;
+      dsx1 += d_db3 * (Ky) * inv_area;
+    }
+    const float inv_w0 = 1.0f / w0, inv_w1 = 1.0f / w1, inv_w2 = 1.0f / w2;
+    g0 = make_float4(dsx0 * inv_w0, dsy0 * inv_w0, dsz0_s * inv_w0,
+                     -(sx0 * dsx0 + sy0 * dsy0 + sz0 * dsz0_s) * inv_w0);
+    g1 = make_float4(dsx1 * inv_w1, dsy1 * inv_w1, dsz1_s * inv_w1,
+                     -(sx1 * dsx1 + sy1 * dsy1 + sz1 * dsz1_s) * inv_w1);
+    g2 = make_float4(dsx2 * inv_w2, dsy2 * inv_w2, dsz2_s * inv_w2,
+                     -(sx2 * dsx2 + sy2 * dsy2 + sz2 * dsz2_s) * inv_w2);
   }
-  const float4 q0 = ldg4(pos + pos_n_base + (int64_t)i0 * 4);
-  const float4 q1 = ldg4(pos + pos_n_base + (int64_t)i1 * 4);
-  const float4 q2 = ldg4(pos + pos_n_base + (int64_t)i2 * 4);
-  const float w0 = q0.w, w1 = q1.w, w2 = q2.w;
-  const float sx0 = q0.x / w0, sy0 = q0.y / w0, sz0 = q0.z / w0;
-  const float sx1 = q1.x / w1, sy1 = q1.y / w1, sz1 = q1.z / w1;
-  const float sx2 = q2.x / w2, sy2 = q2.y / w2, sz2 = q2.z / w2;
-  const float area = (sx1 - sx0) * (sy2 - sy0) - (sx2 - sx0) * (sy1 - sy0);
-  const float inv_area = 1.0f / area;
-  const float dadsx0 = sy1 - sy2, dadsx1 = sy2 - sy0, dadsx2 = sy0 - sy1;
-  const float dadsy0 = sx2 - sx1, dadsy1 = sx0 - sx2, dadsy2 = sx1 - sx0;
-  const float de1dsx0 = Py - sy2, de1dsx2 = sy0 - Py, de1dsy0 = sx2 - Px, de1dsy2 = Px - sx0;
-  const float de2dsx0 = sy1 - Py, de2dsx1 = Py - sy0, de2dsy0 = Px - sx1, de2dsy1 = sx0 - Px;
-  const float dudsx0 = (de1dsx0 - u_val * dadsx0) * inv_area;
-  const float dudsx1 = (0.0f - u_val * dadsx1) * inv_area;
-  const float dudsx2 = (de1dsx2 - u_val * dadsx2) * inv_area;
-  const float dudsy0 = (de1dsy0 - u_val * dadsy0) * inv_area;
-  const float dudsy1 = (0.0f - u_val * dadsy1) * inv_area;
-  const float dudsy2 = (de1dsy2 - u_val * dadsy2) * inv_area;
-  const float dvdsx0 = (de2dsx0 - v_val * dadsx0) * inv_area;
-  const float dvdsx1 = (de2dsx1 - v_val * dadsx1) * inv_area;
-  const float dvdsx2 = (0.0f - v_val * dadsx2) * inv_area;
-  const float dvdsy0 = (de2dsy0 - v_val * dadsy0) * inv_area;
-  const float dvdsy1 = (de2dsy1 - v_val * dadsy1) * inv_area;
-  const float dvdsy2 = (0.0f - v_val * dadsy2) * inv_area;
-  const float dsz10 = sz1 - sz0, dsz20 = sz2 - sz0;
-  float dsx0 = d_u * dudsx0 + d_v * dvdsx0 + d_z * (dudsx0 * dsz10 + dvdsx0 * dsz20);
-  float dsx1 = d_u * dudsx1 + d_v * dvdsx1 + d_z * (dudsx1 * dsz10 + dvdsx1 * dsz20);
-  float dsx2 = d_u * dudsx2 + d_v * dvdsx2 + d_z * (dudsx2 * dsz10 + dvdsx2 * dsz20);
-  float dsy0 = d_u * dudsy0 + d_v * dvdsy0 + d_z * (dudsy0 * dsz10 + dvdsy0 * dsz20);
-  float dsy1 = d_u * dudsy1 + d_v * dvdsy1 + d_z * (dudsy1 * dsz10 + dvdsy1 * dsz20);
-  float dsy2 = d_u * dudsy2 + d_v * dvdsy2 + d_z * (dudsy2 * dsz10 + dvdsy2 * dsz20);
-  const float dsz0_s = d_z * bw_val, dsz1_s = d_z * u_val, dsz2_s = d_z * v_val;
-  if (DB) {
-    const float Kx = 2.0f / (float)W, Ky = -2.0f / (float)H;
-    const float rdb0 = (sy2 - sy0) * Kx * inv_area;
-    const float rdb1 = (sx0 - sx2) * Ky * inv_area;
-    const float rdb2 = (sy0 - sy1) * Kx * inv_area;
-    const float rdb3 = (sx1 - sx0) * Ky * inv_area;
-    const float s = d_db0 * rdb0 + d_db1 * rdb1 + d_db2 * rdb2 + d_db3 * rdb3;
-    dsx0 += (-s * dadsx0) * inv_area;
-    dsx1 += (-s * dadsx1) * inv_area;
-    dsx2 += (-s * dadsx2) * inv_area;
-    dsy0 += (-s * dadsy0) * inv_area;
-    dsy1 += (-s * dadsy1) * inv_area;
-    dsy2 += (-s * dadsy2) * inv_area;
-    dsy0 += d_db0 * (-Kx) * inv_area;
-    dsy2 += d_db0 * (Kx) * inv_area;
-    dsx0 += d_db1 * (Ky) * inv_area;
-    dsx2 += d_db1 * (-Ky) * inv_area;
-    dsy0 += d_db2 * (Kx) * inv_area;
-    dsy1 += d_db2 * (-Kx) * inv_area;
-    dsx0 += d_db3 * (-Ky) * inv_area;
-    dsx1 += d_db3 * (Ky) * inv_area;
+  bool head;
+  const long long key = hit ? (long long)pn * T + t : -1ll - (long long)lane;
+  const int seg_end = warp_runs(key, lane, head);
+  g0.x = warp_seg_sum(g0.x, lane, seg_end); g0.y = warp_seg_sum(g0.y, lane, seg_end);
+  g0.z = warp_seg_sum(g0.z, lane, seg_end); g0.w = warp_seg_sum(g0.w, lane, seg_end);
+  g1.x = warp_seg_sum(g1.x, lane, seg_end); g1.y = warp_seg_sum(g1.y, lane, seg_end);
+  g1.z = warp_seg_sum(g1.z, lane, seg_end); g1.w = warp_seg_sum(g1.w, lane, seg_end);
+  g2.x = warp_seg_sum(g2.x, lane, seg_end); g2.y = warp_seg_sum(g2.y, lane, seg_end);
+  g2.z = warp_seg_sum(g2.z, lane, seg_end); g2.w = warp_seg_sum(g2.w, lane, seg_end);
+  if (!(hit && head)) return;
+  if (XF) {
+    g0 = mat4_apply_t(M, g0);
+    g1 = mat4_apply_t(M, g1);
+    g2 = mat4_apply_t(M, g2);
   }
-  const float inv_w0 = 1.0f / w0, inv_w1 = 1.0f / w1, inv_w2 = 1.0f / w2;
-  const float4 g0 = make_float4(dsx0 * inv_w0, dsy0 * inv_w0, dsz0_s * inv_w0,
-                                -(sx0 * dsx0 + sy0 * dsy0 + sz0 * dsz0_s) * inv_w0);
-  const float4 g1 = make_float4(dsx1 * inv_w1, dsy1 * inv_w1, dsz1_s * inv_w1,
-                                -(sx1 * dsx1 + sy1 * dsy1 + sz1 * dsz1_s) * inv_w1);
-  const float4 g2 = make_float4(dsx2 * inv_w2, dsy2 * inv_w2, dsz2_s * inv_w2,
-                                -(sx2 * dsx2 + sy2 * dsy2 + sz2 * dsz2_s) * inv_w2);
   float* b0 = d_pos + pos_n_base + (int64_t)i0 * 4;
   float* b1 = d_pos + pos_n_base + (int64_t)i1 * 4;
   float* b2 = d_pos + pos_n_base + (int64_t)i2 * 4;
@@ -444,18 +500,26 @@ inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 using namespace dr;
 
-extern "C" dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V, const int32_t* tri,
-                                      int T, const int32_t* ranges, int N, int H, int W,
-                                      const float* peel_layer, float* rast, float* rast_db) {
-  DR_ENTER(ctx);
-  DR_REQUIRE(ctx, pos && (tri || T == 0) && rast, "rasterize: pos, tri and rast are required");
+namespace {
+
+struct Prepared {
+  const float4* rec;
+  const uint32_t* tile_off;
+  const uint32_t* tile_count;
+  const int32_t* list;
+  int ntx, nty;
+  int64_t ntiles_all;
+};
+
+// Setup, tile counts, scan, one readback of the list length, scatter.
+dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int V, const int32_t* tri, int T,
+                         const int32_t* ranges, int N, int H, int W, Prepared& pr) {
+  DR_REQUIRE(ctx, pos && (tri || T == 0), "rasterize: pos and tri are required");
   DR_REQUIRE(ctx, N > 0 && V > 0 && T >= 0 && H > 0 && W > 0,
              "rasterize: bad sizes N=%d V=%d T=%d H=%d W=%d", N, V, T, H, W);
   DR_REQUIRE(ctx, H <= 32768 && W <= 32768, "rasterize: resolution above 32768 is not supported");
   DR_REQUIRE(ctx, T < (1 << 24), "rasterize: T must be < 2^24 (tri_id+1 is stored as float)");
-  DR_REQUIRE(ctx, aligned16(pos) && aligned16(rast) && (!rast_db || aligned16(rast_db)) &&
-                      (!peel_layer || aligned16(peel_layer)),
-             "rasterize: pos/rast/rast_db/peel_layer must be 16-byte aligned");
+  DR_REQUIRE(ctx, aligned16(pos), "rasterize: pos must be 16-byte aligned");
   const int ntx = (W + TILE - 1) / TILE, nty = (H + TILE - 1) / TILE;
   const int64_t ntiles_all = (int64_t)N * ntx * nty;
   const int64_t NT = (int64_t)N * T;
@@ -473,7 +537,7 @@ extern "C" dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V, cons
           "rasterize memset");
   if (NT > 0) {
     DR_TB(ctx);
-    k_raster_setup<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(pos, V, tri, T, ranges, N, H, W, ntx,
+    k_raster_setup<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(pos, xform, V, tri, T, ranges, N, H, W, ntx,
                                                                nty, rec, tile_count, ctx->d_err);
     DR_LAUNCHED(ctx, "raster_setup");
   }
@@ -495,42 +559,102 @@ extern "C" dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V, cons
     k_raster_scatter<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(rec, N, T, ntx, nty, tile_cur, list);
     DR_LAUNCHED(ctx, "raster_scatter");
   }
-  const unsigned grid = (unsigned)ntiles_all;
-  const float4* rec_c = rec;
+  pr.rec = rec;
+  pr.tile_off = tile_off;
+  pr.tile_count = tile_count;
+  pr.list = list;
+  pr.ntx = ntx;
+  pr.nty = nty;
+  pr.ntiles_all = ntiles_all;
+  return DR_OK;
+}
+
+// One depth layer over prepared tile lists (peel: previous layer or NULL).
+dr_status raster_layer(dr_ctx* ctx, const Prepared& pr, int T, int H, int W, const float* peel_layer,
+                       float* rast, float* rast_db) {
+  DR_REQUIRE(ctx, rast != nullptr, "rasterize: rast output is required");
+  DR_REQUIRE(ctx, aligned16(rast) && (!rast_db || aligned16(rast_db)) && (!peel_layer || aligned16(peel_layer)),
+             "rasterize: rast/rast_db/peel_layer must be 16-byte aligned");
+  const unsigned grid = (unsigned)pr.ntiles_all;
   float4* r4 = reinterpret_cast<float4*>(rast);
   float4* d4 = reinterpret_cast<float4*>(rast_db);
+  const int ntx = pr.ntx, nty = pr.nty;
   DR_TB(ctx);
   if (peel_layer) {
     if (rast_db)
-      k_raster_tiles<true, true><<<grid, TILE_PIX, 0, ctx->stream>>>(rec_c, T, H, W, ntx, nty, tile_off,
-                                                                      tile_count, list, peel_layer, r4, d4);
+      k_raster_tiles<true, true><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,
+                                                                      pr.tile_count, pr.list, peel_layer, r4, d4);
     else
-      k_raster_tiles<true, false><<<grid, TILE_PIX, 0, ctx->stream>>>(rec_c, T, H, W, ntx, nty, tile_off,
-                                                                       tile_count, list, peel_layer, r4, d4);
+      k_raster_tiles<true, false><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,
+                                                                       pr.tile_count, pr.list, peel_layer, r4, d4);
   } else {
     if (rast_db)
-      k_raster_tiles<false, true><<<grid, TILE_PIX, 0, ctx->stream>>>(rec_c, T, H, W, ntx, nty, tile_off,
-                                                                       tile_count, list, nullptr, r4, d4);
+      k_raster_tiles<false, true><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,
+                                                                       pr.tile_count, pr.list, nullptr, r4, d4);
     else
-      k_raster_tiles<false, false><<<grid, TILE_PIX, 0, ctx->stream>>>(rec_c, T, H, W, ntx, nty, tile_off,
-                                                                        tile_count, list, nullptr, r4, d4);
+      k_raster_tiles<false, false><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,
+                                                                        pr.tile_count, pr.list, nullptr, r4, d4);
   }
   DR_LAUNCHED(ctx, "raster_tiles");
   return DR_OK;
 }
 
-extern "C" dr_status dr_rasterize_bwd(dr_ctx* ctx, const float* pos, int V, const int32_t* tri, int T,
-                                      const int32_t* ranges, int N, int H, int W, const float* rast,
-                                      const float* d_rast, const float* d_rast_db, float* d_pos) {
+}  // namespace
+
+extern "C" dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V, const int32_t* tri,
+                                      int T, const int32_t* ranges, int N, int H, int W,
+                                      const float* peel_layer, float* rast, float* rast_db) {
   DR_ENTER(ctx);
-  DR_REQUIRE(ctx, pos && (tri || T == 0) && rast && d_rast && d_pos, "rasterize_bwd: null pointer");
-  DR_REQUIRE(ctx, N > 0 && V > 0 && T >= 0 && H > 0 && W > 0, "rasterize_bwd: bad sizes");
-  DR_REQUIRE(ctx, aligned16(pos) && aligned16(rast) && aligned16(d_rast) &&
-                      (!d_rast_db || aligned16(d_rast_db)),
-             "rasterize_bwd: pos/rast/d_rast/d_rast_db must be 16-byte aligned");
-  const bool shared_pos = ranges != nullptr;
-  const size_t npos = (size_t)(shared_pos ? 1 : N) * V * 4;
-  DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream), "rasterize_bwd memset");
+  DR_REQUIRE(ctx, pos && (tri || T == 0) && rast, "rasterize: pos, tri and rast are required");
+  Prepared pr;
+  dr_status st = raster_prepare(ctx, pos, nullptr, V, tri, T, ranges, N, H, W, pr);
+  if (st != DR_OK) return st;
+  return raster_layer(ctx, pr, T, H, W, peel_layer, rast, rast_db);
+}
+
+namespace {
+
+dr_status layers_fwd(dr_ctx* ctx, const float* pos, const float* xform, int V, const int32_t* tri, int T,
+                     const int32_t* ranges, int N, int H, int W, int num_layers, float* const* rast,
+                     float* const* rast_db) {
+  DR_REQUIRE(ctx, num_layers >= 1 && rast, "rasterize_layers: num_layers >= 1 and rast[] required");
+  for (int l = 0; l < num_layers; ++l) DR_REQUIRE(ctx, rast[l] != nullptr, "rasterize_layers: rast[%d] is NULL", l);
+  Prepared pr;
+  dr_status st = raster_prepare(ctx, pos, xform, V, tri, T, ranges, N, H, W, pr);
+  if (st != DR_OK) return st;
+  for (int l = 0; l < num_layers; ++l) {
+    st = raster_layer(ctx, pr, T, H, W, l ? rast[l - 1] : nullptr, rast[l], rast_db ? rast_db[l] : nullptr);
+    if (st != DR_OK) return st;
+  }
+  return DR_OK;
+}
+
+}  // namespace
+
+extern "C" dr_status dr_rasterize_layers_fwd(dr_ctx* ctx, const float* pos, int V, const int32_t* tri, int T,
+                                             const int32_t* ranges, int N, int H, int W, int num_layers,
+                                             float* const* rast, float* const* rast_db) {
+  DR_ENTER(ctx);
+  return layers_fwd(ctx, pos, nullptr, V, tri, T, ranges, N, H, W, num_layers, rast, rast_db);
+}
+
+extern "C" dr_status dr_rasterize_xf_fwd(dr_ctx* ctx, const float* verts, int V, const float* xform,
+                                         const int32_t* tri, int T, int N, int H, int W, int num_layers,
+                                         float* const* rast, float* const* rast_db) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, xform != nullptr && ((uintptr_t)xform & 15) == 0,
+             "rasterize_xf: xform [N,4,4] must be given and 16-byte aligned");
+  return layers_fwd(ctx, verts, xform, V, tri, T, nullptr, N, H, W, num_layers, rast, rast_db);
+}
+
+namespace {
+
+dr_status raster_bwd_launch(dr_ctx* ctx, const float* pos, const float* xform, int V, const int32_t* tri, int T,
+                            bool shared_pos, int N, int H, int W, const float* rast, const float* d_rast,
+                            const float* d_rast_db, float* d_pos) {
+  DR_REQUIRE(ctx, rast && d_rast, "rasterize_bwd: rast and d_rast are required");
+  DR_REQUIRE(ctx, aligned16(rast) && aligned16(d_rast) && (!d_rast_db || aligned16(d_rast_db)),
+             "rasterize_bwd: rast/d_rast/d_rast_db must be 16-byte aligned");
   const int64_t P = (int64_t)N * H * W;
   const bool vec = aligned16(d_pos);
   const float4* r4 = reinterpret_cast<const float4*>(rast);
@@ -538,13 +662,74 @@ extern "C" dr_status dr_rasterize_bwd(dr_ctx* ctx, const float* pos, int V, cons
   const float4* gd4 = reinterpret_cast<const float4*>(d_rast_db);
   const unsigned grid = grid_for(P, 256);
   DR_TB(ctx);
-  if (d_rast_db) {
-    if (vec) k_raster_bwd<true, true><<<grid, 256, 0, ctx->stream>>>(pos, V, tri, T, shared_pos, N, H, W, r4, g4, gd4, d_pos, ctx->d_err);
-    else k_raster_bwd<true, false><<<grid, 256, 0, ctx->stream>>>(pos, V, tri, T, shared_pos, N, H, W, r4, g4, gd4, d_pos, ctx->d_err);
+#define DR_RB(DBV, VECV, XFV) \
+  k_raster_bwd<DBV, VECV, XFV><<<grid, 256, 0, ctx->stream>>>(pos, xform, V, tri, T, shared_pos, N, H, W, r4, g4, \
+                                                              gd4, d_pos, ctx->d_err)
+  const bool db = d_rast_db != nullptr, xf = xform != nullptr;
+  if (xf) {
+    if (db) { if (vec) DR_RB(true, true, true); else DR_RB(true, false, true); }
+    else { if (vec) DR_RB(false, true, true); else DR_RB(false, false, true); }
   } else {
-    if (vec) k_raster_bwd<false, true><<<grid, 256, 0, ctx->stream>>>(pos, V, tri, T, shared_pos, N, H, W, r4, g4, gd4, d_pos, ctx->d_err);
-    else k_raster_bwd<false, false><<<grid, 256, 0, ctx->stream>>>(pos, V, tri, T, shared_pos, N, H, W, r4, g4, gd4, d_pos, ctx->d_err);
+    if (db) { if (vec) DR_RB(true, true, false); else DR_RB(true, false, false); }
+    else { if (vec) DR_RB(false, true, false); else DR_RB(false, false, false); }
   }
+#undef DR_RB
   DR_LAUNCHED(ctx, "raster_bwd");
   return DR_OK;
+}
+
+}  // namespace
+
+extern "C" dr_status dr_rasterize_bwd(dr_ctx* ctx, const float* pos, int V, const int32_t* tri, int T,
+                                      const int32_t* ranges, int N, int H, int W, const float* rast,
+                                      const float* d_rast, const float* d_rast_db, float* d_pos) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, pos && (tri || T == 0) && rast && d_rast && d_pos, "rasterize_bwd: null pointer");
+  DR_REQUIRE(ctx, N > 0 && V > 0 && T >= 0 && H > 0 && W > 0, "rasterize_bwd: bad sizes");
+  DR_REQUIRE(ctx, aligned16(pos), "rasterize_bwd: pos must be 16-byte aligned");
+  const bool shared_pos = ranges != nullptr;
+  const size_t npos = (size_t)(shared_pos ? 1 : N) * V * 4;
+  DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream), "rasterize_bwd memset");
+  return raster_bwd_launch(ctx, pos, nullptr, V, tri, T, shared_pos, N, H, W, rast, d_rast, d_rast_db, d_pos);
+}
+
+namespace {
+
+dr_status layers_bwd(dr_ctx* ctx, const float* pos, const float* xform, int V, const int32_t* tri, int T,
+                     const int32_t* ranges, int N, int H, int W, int num_layers, const float* const* rast,
+                     const float* const* d_rast, const float* const* d_rast_db, float* d_pos) {
+  DR_REQUIRE(ctx, pos && (tri || T == 0) && rast && d_rast && d_pos && num_layers >= 1,
+             "rasterize_layers_bwd: null pointer");
+  DR_REQUIRE(ctx, N > 0 && V > 0 && T >= 0 && H > 0 && W > 0, "rasterize_layers_bwd: bad sizes");
+  DR_REQUIRE(ctx, aligned16(pos), "rasterize_layers_bwd: pos must be 16-byte aligned");
+  const bool shared_pos = ranges != nullptr;
+  const size_t npos = (size_t)((shared_pos || xform) ? 1 : N) * V * 4;
+  DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream), "rasterize_layers_bwd memset");
+  for (int l = 0; l < num_layers; ++l) {
+    if (!d_rast[l]) continue;  // a layer whose outputs did not reach the loss
+    dr_status st = raster_bwd_launch(ctx, pos, xform, V, tri, T, shared_pos, N, H, W, rast[l], d_rast[l],
+                                     d_rast_db ? d_rast_db[l] : nullptr, d_pos);
+    if (st != DR_OK) return st;
+  }
+  return DR_OK;
+}
+
+}  // namespace
+
+extern "C" dr_status dr_rasterize_layers_bwd(dr_ctx* ctx, const float* pos, int V, const int32_t* tri, int T,
+                                             const int32_t* ranges, int N, int H, int W, int num_layers,
+                                             const float* const* rast, const float* const* d_rast,
+                                             const float* const* d_rast_db, float* d_pos) {
+  DR_ENTER(ctx);
+  return layers_bwd(ctx, pos, nullptr, V, tri, T, ranges, N, H, W, num_layers, rast, d_rast, d_rast_db, d_pos);
+}
+
+extern "C" dr_status dr_rasterize_xf_bwd(dr_ctx* ctx, const float* verts, int V, const float* xform,
+                                         const int32_t* tri, int T, int N, int H, int W, int num_layers,
+                                         const float* const* rast, const float* const* d_rast,
+                                         const float* const* d_rast_db, float* d_verts) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, xform != nullptr && ((uintptr_t)xform & 15) == 0,
+             "rasterize_xf_bwd: xform [N,4,4] must be given and 16-byte aligned");
+  return layers_bwd(ctx, verts, xform, V, tri, T, nullptr, N, H, W, num_layers, rast, d_rast, d_rast_db, d_verts);
 }

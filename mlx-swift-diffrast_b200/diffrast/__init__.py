@@ -16,6 +16,7 @@ from .ops import (  # noqa: F401
     interpolate,
     mse_loss,
     rasterize,
+    rasterize_layers,
     texture,
     texture_construct_mip,
     textureConstructMip,
@@ -23,7 +24,7 @@ from .ops import (  # noqa: F401
 
 __all__ = [
     "BoundaryMode", "DiffAttrs", "FilterMode", "DiffRastError",
-    "rasterize", "interpolate", "texture", "texture_construct_mip", "textureConstructMip",
+    "rasterize", "rasterize_layers", "interpolate", "texture", "texture_construct_mip", "textureConstructMip",
     "antialias_construct_topology_hash", "antialiasConstructTopologyHash", "antialias",
     "mse_loss", "launch_count", "sync", "workspace_bytes",
 ]

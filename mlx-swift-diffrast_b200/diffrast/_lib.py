@@ -38,6 +38,10 @@ SIGNATURES = {
     "dr_ctx_timing_report": (I, [P, ctypes.c_char_p, ctypes.c_size_t]),
     "dr_rasterize_fwd": (I, [P, P, I, P, I, P, I, I, I, P, P, P]),
     "dr_rasterize_bwd": (I, [P, P, I, P, I, P, I, I, I, P, P, P, P]),
+    "dr_rasterize_layers_fwd": (I, [P, P, I, P, I, P, I, I, I, I, P, P]),
+    "dr_rasterize_layers_bwd": (I, [P, P, I, P, I, P, I, I, I, I, P, P, P, P]),
+    "dr_rasterize_xf_fwd": (I, [P, P, I, P, P, I, I, I, I, I, P, P]),
+    "dr_rasterize_xf_bwd": (I, [P, P, I, P, P, I, I, I, I, I, P, P, P, P]),
     "dr_interpolate_fwd": (I, [P, P, I, I, I, P, I, I, I, P, I, P, P, I, P, P]),
     "dr_interpolate_bwd": (I, [P, P, I, I, I, P, I, I, I, P, I, P, P, I, P, P, P, P, P]),
     "dr_texture_mip_layout": (I, [I, I, I, I, I, ctypes.POINTER(I), ctypes.POINTER(I64),
@@ -48,6 +52,8 @@ SIGNATURES = {
     "dr_antialias_construct_topology_hash": (I, [P, P, I, P]),
     "dr_antialias_fwd": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P]),
     "dr_antialias_bwd": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P, P, P]),
+    "dr_antialias_xf_fwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P]),
+    "dr_antialias_xf_bwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P, P]),
     "dr_mse_fwd_bwd": (I, [P, P, P, I64, F, P, P, I]),
 }
 

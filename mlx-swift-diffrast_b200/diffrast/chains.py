@@ -162,9 +162,10 @@ class Cfg4(Chain):
     diffAttrs=.all on both, antialias (topology hash) on layer 0; loss =
     MSE(aa0) + MSE(interp1); backward to the soup vertices and attributes.
 
-    The views are per-view 2-D similarity transforms of the shared soup, applied
-    in clip space (pos_n = base @ M_n^T), so d_pos of every view lands on the
-    shared [V, 4] vertex buffer."""
+    The views are per-view 2-D similarity transforms M_n of the shared soup in
+    clip space (pos_n = M_n @ base), evaluated inside the rasterize and antialias
+    kernels (the library's per-view transform mode), so no [N, V, 4] tensor is
+    materialised and every view's gradient lands on the shared [V, 4] buffer."""
 
     def __init__(self, dev, view_lo=0, view_hi=32, total_views=32, res=1024, n_isolated=800_000,
                  n_strips=20_000):
@@ -193,12 +194,11 @@ class Cfg4(Chain):
         return torch.einsum("nij,vj->nvi", self.sim, self.base)
 
     def step(self):
-        pos = self.positions()
-        rast0, db0 = ops.rasterize(pos, self.tri, self.res, grad_db=True)
-        rast1, db1 = ops.rasterize(pos, self.tri, self.res, grad_db=True, peel_layer=rast0.detach())
+        (rast0, db0), (rast1, db1) = ops.rasterize_layers(self.base, self.tri, self.res, 2, grad_db=True,
+                                                          xform=self.sim)
         out0, _ = ops.interpolate(self.attr, rast0, self.tri, db0, ops.DiffAttrs.all)
         out1, _ = ops.interpolate(self.attr, rast1, self.tri, db1, ops.DiffAttrs.all)
-        aa0 = ops.antialias(out0, rast0, pos, self.tri, self.topo)
+        aa0 = ops.antialias(out0, rast0, self.base, self.tri, self.topo, xform=self.sim)
         loss = ops.mse_loss(aa0, self.tgt0) + ops.mse_loss(out1, self.tgt1)
         loss.backward()
         return loss
@@ -241,11 +241,11 @@ class Cfg5(Chain):
         tot = None
         for a in range(0, n, self.micro):
             b = min(n, a + self.micro)
-            pos = torch.einsum("nij,vj->nvi", self.mvp[a:b], self.verts)
-            rast, _ = ops.rasterize(pos, self.tri, self.res, grad_db=False)
+            xf = self.mvp[a:b]
+            ((rast, _),) = ops.rasterize_layers(self.verts, self.tri, self.res, 1, grad_db=False, xform=xf)
             nrm, _ = ops.interpolate(self.nrm, rast, self.tri)
             col = ops.texture(self.cube, nrm, boundary_mode=ops.BoundaryMode.cube)
-            aa = ops.antialias(col, rast, pos, self.tri, self.topo)
+            aa = ops.antialias(col, rast, self.verts, self.tri, self.topo, xform=xf)
             loss = ops.mse_loss(aa, self.target[a:b]) * ((b - a) / n)
             loss.backward()
             tot = loss.detach() if tot is None else tot + loss.detach()

@@ -179,6 +179,94 @@ def rasterize(pos: torch.Tensor, tri: torch.Tensor, resolution, grad_db: bool = 
     return _Rasterize.apply(pos, _i32(tri, "tri"), ranges, peel_layer, H, W, bool(grad_db))
 
 
+class _RasterizeLayers(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pos, xform, tri, ranges, H, W, grad_db, nl):
+        import ctypes
+        posc = _f32(pos, "pos")
+        xf = _f32(xform, "xform") if xform is not None else None
+        if xf is not None:
+            N, V = xf.shape[0], posc.shape[0]
+        elif ranges is not None:
+            N, V = ranges.shape[0], posc.shape[0]
+        else:
+            N, V = posc.shape[0], posc.shape[1]
+        T = tri.shape[0]
+        rasts = [torch.empty((N, H, W, 4), device=posc.device, dtype=torch.float32) for _ in range(nl)]
+        dbs = ([torch.empty((N, H, W, 4), device=posc.device, dtype=torch.float32) for _ in range(nl)]
+               if grad_db else None)
+        rp = (ctypes.c_void_p * nl)(*[r.data_ptr() for r in rasts])
+        dp = (ctypes.c_void_p * nl)(*[d.data_ptr() for d in dbs]) if grad_db else None
+        rpp = ctypes.cast(rp, ctypes.c_void_p)
+        dpp = ctypes.cast(dp, ctypes.c_void_p) if dp is not None else None
+        c = _ctx(posc)
+        if xf is not None:
+            L.check(L.lib().dr_rasterize_xf_fwd(c, _ptr(posc), V, _ptr(xf), _ptr(tri), T, N, H, W, nl, rpp, dpp),
+                    c, "rasterize_xf")
+        else:
+            L.check(L.lib().dr_rasterize_layers_fwd(c, _ptr(posc), V, _ptr(tri), T, _ptr(ranges), N, H, W, nl,
+                                                    rpp, dpp), c, "rasterize_layers")
+        ctx.save_for_backward(posc, xf, tri, ranges, *rasts)
+        ctx.dims = (N, V, T, H, W, grad_db, nl)
+        if not grad_db:
+            dbs = [torch.zeros((N, H, W, 0), device=posc.device, dtype=torch.float32) for _ in range(nl)]
+        out = []
+        for r, d in zip(rasts, dbs):
+            out += [r, d]
+        return tuple(out)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        import ctypes
+        posc, xf, tri, ranges, *rasts = ctx.saved_tensors
+        N, V, T, H, W, grad_db, nl = ctx.dims
+        d_r = [g.contiguous().float() if g is not None else None for g in grads[0::2]]
+        d_d = [g.contiguous().float() if (grad_db and g is not None) else None for g in grads[1::2]]
+        d_pos = torch.empty_like(posc)
+        rp = ctypes.cast((ctypes.c_void_p * nl)(*[r.data_ptr() for r in rasts]), ctypes.c_void_p)
+        gp = ctypes.cast((ctypes.c_void_p * nl)(*[(g.data_ptr() if g is not None else None) for g in d_r]),
+                         ctypes.c_void_p)
+        dp = ctypes.cast((ctypes.c_void_p * nl)(*[(g.data_ptr() if g is not None else None) for g in d_d]),
+                         ctypes.c_void_p)
+        c = _ctx(posc)
+        if xf is not None:
+            L.check(L.lib().dr_rasterize_xf_bwd(c, _ptr(posc), V, _ptr(xf), _ptr(tri), T, N, H, W, nl, rp, gp, dp,
+                                                _ptr(d_pos)), c, "rasterize_xf_bwd")
+        else:
+            L.check(L.lib().dr_rasterize_layers_bwd(c, _ptr(posc), V, _ptr(tri), T, _ptr(ranges), N, H, W, nl,
+                                                    rp, gp, dp, _ptr(d_pos)), c, "rasterize_layers_bwd")
+        return d_pos, None, None, None, None, None, None, None
+
+
+def rasterize_layers(pos: torch.Tensor, tri: torch.Tensor, resolution, num_layers: int, grad_db: bool = True,
+                     ranges: Optional[torch.Tensor] = None, xform: Optional[torch.Tensor] = None):
+    """Depth peeling of `num_layers` layers in one call: the same results as
+    rasterize(...) followed by rasterize(..., peel_layer=previous) calls, with
+    triangle setup and tile binning done once.  Returns [(rast, rast_db), ...].
+
+    With `xform` [N, 4, 4], `pos` is a shared vertex buffer [V, 4] and view n
+    rasterizes M_n @ pos (no [N, V, 4] tensor is materialised); the gradient
+    flows to the shared vertices."""
+    if tri.dim() != 2 or tri.shape[1] != 3:
+        raise ValueError(f"rasterize: tri must be [T, 3] (got {tuple(tri.shape)})")
+    if int(num_layers) < 1:
+        raise ValueError("rasterize_layers: num_layers must be >= 1")
+    H, W = int(resolution[0]), int(resolution[1])
+    if xform is not None:
+        if pos.dim() != 2 or pos.shape[1] != 4 or xform.dim() != 3 or tuple(xform.shape[1:]) != (4, 4):
+            raise ValueError("rasterize: with `xform` [N, 4, 4], pos must be [V, 4]")
+        if ranges is not None:
+            raise ValueError("rasterize: `xform` and `ranges` are exclusive")
+    elif ranges is not None:
+        if pos.dim() != 2 or pos.shape[1] != 4:
+            raise ValueError(f"rasterize: with `ranges`, pos must be [V, 4] (got {tuple(pos.shape)})")
+        ranges = _i32(ranges, "ranges")
+    elif pos.dim() != 3 or pos.shape[2] != 4:
+        raise ValueError(f"rasterize: pos must be [N, V, 4] (got {tuple(pos.shape)})")
+    outs = _RasterizeLayers.apply(pos, xform, _i32(tri, "tri"), ranges, H, W, bool(grad_db), int(num_layers))
+    return [(outs[2 * l], outs[2 * l + 1]) for l in range(int(num_layers))]
+
+
 # ------------------------------------------------------------- interpolate
 
 class _Interpolate(torch.autograd.Function):
@@ -404,50 +492,67 @@ def antialias_construct_topology_hash(tri: torch.Tensor) -> torch.Tensor:
 
 class _Antialias(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, color, pos, rast, tri, topo):
+    def forward(ctx, color, pos, xform, rast, tri, topo):
         color_c = _f32(color, "color")
         pos_c = _f32(pos, "pos")
+        xf = _f32(xform, "xform") if xform is not None else None
         rast_c = _f32(rast, "rast")
         N, H, W, C = color_c.shape
-        V, T = pos_c.shape[1], tri.shape[0]
+        V, T = (pos_c.shape[0] if xf is not None else pos_c.shape[1]), tri.shape[0]
         out = torch.empty_like(color_c)
         c = _ctx(color_c)
-        L.check(L.lib().dr_antialias_fwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(tri),
-                                         T, _ptr(topo), _ptr(out)), c, "antialias")
-        ctx.save_for_backward(color_c, pos_c, rast_c, tri, topo)
+        if xf is not None:
+            L.check(L.lib().dr_antialias_xf_fwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(xf),
+                                                _ptr(tri), T, _ptr(topo), _ptr(out)), c, "antialias_xf")
+        else:
+            L.check(L.lib().dr_antialias_fwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(tri),
+                                             T, _ptr(topo), _ptr(out)), c, "antialias")
+        ctx.save_for_backward(color_c, pos_c, xf, rast_c, tri, topo)
         return out
 
     @staticmethod
     def backward(ctx, d_out):
-        color_c, pos_c, rast_c, tri, topo = ctx.saved_tensors
+        color_c, pos_c, xf, rast_c, tri, topo = ctx.saved_tensors
         N, H, W, C = color_c.shape
-        V, T = pos_c.shape[1], tri.shape[0]
+        V, T = (pos_c.shape[0] if xf is not None else pos_c.shape[1]), tri.shape[0]
         d_out = d_out.contiguous().float()
         d_color = torch.empty_like(color_c)
         d_pos = torch.empty_like(pos_c)
         c = _ctx(color_c)
-        L.check(L.lib().dr_antialias_bwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(tri),
-                                         T, _ptr(topo), _ptr(d_out), _ptr(d_color), _ptr(d_pos)),
-                c, "antialias_bwd")
-        return d_color, d_pos, None, None, None
+        if xf is not None:
+            L.check(L.lib().dr_antialias_xf_bwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(xf),
+                                                _ptr(tri), T, _ptr(topo), _ptr(d_out), _ptr(d_color), _ptr(d_pos)),
+                    c, "antialias_xf_bwd")
+        else:
+            L.check(L.lib().dr_antialias_bwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(tri),
+                                             T, _ptr(topo), _ptr(d_out), _ptr(d_color), _ptr(d_pos)),
+                    c, "antialias_bwd")
+        return d_color, d_pos, None, None, None, None
 
 
 def antialias(color: torch.Tensor, rast: torch.Tensor, pos: torch.Tensor, tri: torch.Tensor,
-              topology_hash: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """DiffRast.antialias (Antialias.swift:90-131); differentiable w.r.t. color and pos."""
+              topology_hash: Optional[torch.Tensor] = None, xform: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """DiffRast.antialias (Antialias.swift:90-131); differentiable w.r.t. color and pos.
+
+    With `xform` [N, 4, 4], `pos` is the shared vertex buffer [V, 4] and view n
+    uses M_n @ pos (as rasterize_layers(xform=...))."""
     if color.dim() != 4:
         raise ValueError(f"antialias: color must be [N, H, W, C] (got {tuple(color.shape)})")
     if rast.dim() != 4 or rast.shape[3] != 4 or tuple(rast.shape[:3]) != tuple(color.shape[:3]):
         raise ValueError("antialias: rast must match color in [N, H, W] and have 4 channels")
-    if pos.dim() != 3 or pos.shape[2] != 4:
-        raise ValueError(f"antialias: pos must be [N, V, 4] (got {tuple(pos.shape)})")
-    if pos.shape[0] != color.shape[0]:
-        raise ValueError("antialias: pos batch must match color batch")
+    if xform is not None:
+        if pos.dim() != 2 or pos.shape[1] != 4 or tuple(xform.shape) != (color.shape[0], 4, 4):
+            raise ValueError("antialias: with `xform` [N, 4, 4], pos must be [V, 4]")
+    else:
+        if pos.dim() != 3 or pos.shape[2] != 4:
+            raise ValueError(f"antialias: pos must be [N, V, 4] (got {tuple(pos.shape)})")
+        if pos.shape[0] != color.shape[0]:
+            raise ValueError("antialias: pos batch must match color batch")
     if tri.dim() != 2 or tri.shape[1] != 3:
         raise ValueError(f"antialias: tri must be [T, 3] (got {tuple(tri.shape)})")
     tri_c = _i32(tri, "tri")
     topo = antialias_construct_topology_hash(tri_c) if topology_hash is None else _i32(topology_hash, "topologyHash")
-    return _Antialias.apply(color, pos, rast.detach(), tri_c, topo)
+    return _Antialias.apply(color, pos, xform, rast.detach(), tri_c, topo)
 
 
 # -------------------------------------------------------------------- loss

@@ -251,3 +251,28 @@ def mse_fwd_bwd(pred, target, scale, nthreads=0):
                                  ctypes.c_float(scale), _p(d),
                                  _nt(nthreads))
     return loss, d
+
+
+# ------------------------------------------------- per-view vertex transforms
+
+def xf_positions(verts, xform):
+    """Clip positions of the "xf" entry points: pos[n, v, r] =
+    ((M[n,r,0] x + M[n,r,1] y) + M[n,r,2] z) + M[n,r,3] w, every product and
+    sum rounded to float32 (the order include/diffrast.h specifies)."""
+    v = np.ascontiguousarray(verts, np.float32)
+    M = np.ascontiguousarray(xform, np.float32)
+    out = np.empty((M.shape[0], v.shape[0], 4), np.float32)
+    for r in range(4):
+        acc = M[:, None, r, 0] * v[None, :, 0]
+        acc = acc + M[:, None, r, 1] * v[None, :, 1]
+        acc = acc + M[:, None, r, 2] * v[None, :, 2]
+        acc = acc + M[:, None, r, 3] * v[None, :, 3]
+        out[..., r] = acc
+    return out
+
+
+def xf_vertex_grad(d_pos, xform):
+    """Gradient of the shared vertices from per-view clip gradients:
+    d_verts[v] = sum_n M_n^T d_pos[n, v] (float64 accumulation)."""
+    return np.einsum("nri,nvr->vi", np.asarray(xform, np.float64),
+                     np.asarray(d_pos, np.float64)).astype(np.float32)

@@ -215,3 +215,87 @@ def test_antialias_soup_with_strips(cu, soup):
     ga = cu.antialias_bwd(color, rast, pos, tri, d_out, topo)
     gb = O.antialias_bwd(color, rast, pos, tri, d_out, topo)
     assert rel_l2(ga[0], gb[0]) < 1e-5 and rel_l2(ga[1], gb[1]) < 1e-4
+
+
+def test_rasterize_layers_equals_chained_peeling(cu, soup):
+    import torch
+
+    import diffrast
+    pos, tri = soup
+    p = torch.from_numpy(pos).cuda().requires_grad_(True)
+    t = torch.from_numpy(tri).cuda()
+    layers = diffrast.rasterize_layers(p, t, (200, 256), 3)
+    r_prev = None
+    for l, (r, db) in enumerate(layers):
+        rc, dc = diffrast.rasterize(p.detach(), t, (200, 256), peel_layer=r_prev)
+        assert torch.equal(r, rc) and torch.equal(db, dc), l
+        r_prev = rc
+    # VJP of the layered call == sum of the per-layer VJPs
+    g = np.random.default_rng(3)
+    w = [torch.from_numpy(g.normal(size=(3, 200, 256, 4)).astype(np.float32)).cuda() for _ in range(6)]
+    loss = sum((r * w[2 * l]).sum() + (db * w[2 * l + 1]).sum() for l, (r, db) in enumerate(layers))
+    loss.backward()
+    import oracle
+    ref = np.zeros_like(pos)
+    r_prev = None
+    for l in range(3):
+        r_o, _ = oracle.rasterize(pos, tri, (200, 256), peel_layer=r_prev)
+        ref += oracle.rasterize_bwd(pos, tri, r_o, w[2 * l].cpu().numpy(), w[2 * l + 1].cpu().numpy())
+        r_prev = r_o
+    assert rel_l2(p.grad.cpu().numpy(), ref) < 1e-4
+
+
+@pytest.mark.parametrize("diff", [None, "all"])
+def test_interpolate_bwd_soup_short_runs(cu, soup, diff):
+    # Tiny triangles: pixel runs of equal triangle are short, exercising the
+    # warp-aggregated d_attr path with many heads per warp.
+    pos, tri = soup
+    rast, db = O.rasterize(pos, tri, (256, 256))
+    V = pos.shape[1]
+    g = np.random.default_rng(17)
+    attr = g.normal(size=(V, 8)).astype(np.float32)
+    d_out = g.normal(size=(3, 256, 256, 8)).astype(np.float32)
+    d_da = g.normal(size=(3, 256, 256, 16)).astype(np.float32) if diff else None
+    ga = cu.interpolate_bwd(attr, rast, tri, d_out, db, diff, d_da)
+    gb = O.interpolate_bwd(attr, rast, tri, d_out, db, diff, d_da)
+    assert rel_l2(ga[0], gb[0]) < 1e-4
+    np.testing.assert_allclose(ga[1], gb[1], rtol=1e-5, atol=1e-5)
+    if diff:
+        np.testing.assert_allclose(ga[2], gb[2], rtol=1e-5, atol=1e-5)
+
+
+def test_xf_mode_matches_instanced_on_transformed_positions(cu, soup):
+    # Per-view transform entry points: identical rasterization to instanced mode
+    # on the positions the transform defines; d_verts = sum_n M_n^T d_pos_n.
+    import torch
+
+    import diffrast
+    import oracle
+    base, tri = scenes.triangle_soup(20000, 1000, 10, seed=21)
+    M = scenes.similarity_matrices(3, seed=22).astype(np.float32)
+    M[1, 3, 2] = 0.01  # a non-affine row, so w depends on z
+    pos = oracle.xf_positions(base, M)
+    vb = torch.from_numpy(base).cuda().requires_grad_(True)
+    xf = torch.from_numpy(M).cuda()
+    t = torch.from_numpy(tri).cuda()
+    layers = diffrast.rasterize_layers(vb, t, (160, 192), 2, xform=xf)
+    r0o, d0o = O.rasterize(pos, tri, (160, 192))
+    r1o, d1o = O.rasterize(pos, tri, (160, 192), peel=r0o)
+    assert np.array_equal(layers[0][0].cpu().numpy(), r0o) and np.array_equal(layers[0][1].cpu().numpy(), d0o)
+    assert np.array_equal(layers[1][0].cpu().numpy(), r1o) and np.array_equal(layers[1][1].cpu().numpy(), d1o)
+    g = np.random.default_rng(4)
+    w = [g.normal(size=(3, 160, 192, 4)).astype(np.float32) for _ in range(4)]
+    col = torch.from_numpy(g.normal(size=(3, 160, 192, 3)).astype(np.float32)).cuda()
+    wa = g.normal(size=(3, 160, 192, 3)).astype(np.float32)
+    aa = diffrast.antialias(col, layers[0][0], vb, t, xform=xf)
+    topo = oracle.topology_hash(tri)
+    np.testing.assert_allclose(aa.detach().cpu().numpy(), oracle.antialias(col.cpu().numpy(), r0o, pos, tri, topo), rtol=1e-5,
+                               atol=1e-6)
+    loss = sum((layers[l][0] * torch.from_numpy(w[2 * l]).cuda()).sum()
+               + (layers[l][1] * torch.from_numpy(w[2 * l + 1]).cuda()).sum() for l in range(2))
+    loss = loss + (aa * torch.from_numpy(wa).cuda()).sum()
+    loss.backward()
+    d_pos = (oracle.rasterize_bwd(pos, tri, r0o, w[0], w[1]) + oracle.rasterize_bwd(pos, tri, r1o, w[2], w[3])
+             + oracle.antialias_bwd(col.cpu().numpy(), r0o, pos, tri, wa, topo)[1])
+    ref = oracle.xf_vertex_grad(d_pos, M)
+    assert rel_l2(vb.grad.cpu().numpy(), ref) < 1e-4
