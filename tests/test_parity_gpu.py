@@ -281,8 +281,10 @@ def test_xf_mode_matches_instanced_on_transformed_positions(cu, soup):
     layers = diffrast.rasterize_layers(vb, t, (160, 192), 2, xform=xf)
     r0o, d0o = O.rasterize(pos, tri, (160, 192))
     r1o, d1o = O.rasterize(pos, tri, (160, 192), peel=r0o)
-    assert np.array_equal(layers[0][0].cpu().numpy(), r0o) and np.array_equal(layers[0][1].cpu().numpy(), d0o)
-    assert np.array_equal(layers[1][0].cpu().numpy(), r1o) and np.array_equal(layers[1][1].cpu().numpy(), d1o)
+    assert np.array_equal(layers[0][0].detach().cpu().numpy(), r0o)
+    assert np.array_equal(layers[0][1].detach().cpu().numpy(), d0o)
+    assert np.array_equal(layers[1][0].detach().cpu().numpy(), r1o)
+    assert np.array_equal(layers[1][1].detach().cpu().numpy(), d1o)
     g = np.random.default_rng(4)
     w = [g.normal(size=(3, 160, 192, 4)).astype(np.float32) for _ in range(4)]
     col = torch.from_numpy(g.normal(size=(3, 160, 192, 3)).astype(np.float32)).cuda()
