@@ -256,6 +256,22 @@ DR_API dr_status dr_antialias_construct_topology_hash(dr_ctx* ctx,
                                                const int32_t* tri, int T,
                                                int32_t* topo);
 
+/* Allocation-free variant of dr_antialias_construct_topology_hash — no
+ * counterpart in the reference.  For callers that cannot allocate device
+ * memory (their host owns the GPU's memory through its own pool, or they must
+ * avoid the device-wide synchronisation of cudaMalloc): it needs no context and
+ * allocates nothing, using a fixed hash table compiled into the library (about
+ * 10.8 MB on every GPU that loads it, held until the process exits).
+ *   tri: [T, 3] device; topo: out [T, 3] device; stream: a cudaStream_t.
+ *   T must be <= DR_STATIC_TOPO_MAX_TRIS, else DR_EINVAL (nothing launched).
+ * The first call on a device looks up the table's device address (with that
+ * device current), so make it before any stream capture.  Every call reuses the
+ * same table and clears what it uses; calls that overlap on the GPU race. */
+#define DR_STATIC_TOPO_MAX_TRIS 65536
+DR_API dr_status dr_antialias_construct_topology_hash_static(const int32_t* tri,
+                                                             int T, int32_t* topo,
+                                                             void* stream);
+
 /* Forward.  Replaces DiffRast.antialias (Antialias.swift:90-131) and
  * diffrast_antialias_fwd (Antialias.swift:333-358).
  *   color: [N, H, W, C]; rast: [N, H, W, 4]; pos: [N, V, 4] (instanced, as the

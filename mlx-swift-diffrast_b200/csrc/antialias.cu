@@ -17,6 +17,8 @@
 //   pixel adds its own g*(1 - sum beta) and the beta*g its four neighbours
 //   would have scattered toward it — so it needs no atomics and is
 //   deterministic; only d_pos uses (float) atomics.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -491,4 +493,81 @@ extern "C" dr_status dr_antialias_xf_bwd(dr_ctx* ctx, const float* color, int N,
   DR_ENTER(ctx);
   DR_REQUIRE(ctx, xform && aligned16(xform), "antialias_xf_bwd: xform [N,4,4] must be given and 16-byte aligned");
   return aa_bwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, d_out, d_color, d_verts);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free topology hash.
+//
+// Some callers cannot allocate device memory: a host that owns every byte of
+// the GPU through its own pool (a game engine or inference server), or code that
+// must not trigger the device-wide synchronisation cudaMalloc implies.  For
+// them dr_antialias_construct_topology_hash_static takes no context and
+// allocates nothing: its hash table lives in the fixed array below, which every
+// GPU that loads this library holds until the process exits.
+//
+// The table is sized for DR_STATIC_TOPO_MAX_TRIS triangles (3 edges each, load
+// factor <= 1/2): 2^19 slots of (key 8 B, count 4 B, two references 4 B each)
+// plus one slot index per edge, about 10.8 MB.  Every call clears the part it
+// uses before inserting.  All calls share the one array, so calls whose work
+// overlaps on the GPU (different streams, or threads sharing a device) race and
+// must be serialised by the caller.
+
+namespace {
+
+constexpr uint32_t kStaticCap = 1u << 19;
+constexpr size_t kStaticEdges = 3 * (size_t)DR_STATIC_TOPO_MAX_TRIS;
+constexpr size_t kStaticBytes = (size_t)kStaticCap * (8 + 4 + 4 + 4) + kStaticEdges * 4;
+static_assert(2 * kStaticEdges <= kStaticCap, "static topology table below load factor 1/2");
+
+static __device__ __align__(256) unsigned char g_topo_scratch[kStaticBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+unsigned char* g_static_base[kMaxDevices] = {};
+
+// Device address of g_topo_scratch on the current device.  Host code only sees
+// the array's host-side shadow; the device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+dr_status static_scratch(unsigned char** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return DR_ECUDA;
+  }
+  std::lock_guard<std::mutex> g(g_static_mu);
+  if (!g_static_base[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_topo_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return DR_ECUDA;
+    }
+    g_static_base[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_static_base[dev];
+  return DR_OK;
+}
+
+}  // namespace
+
+extern "C" dr_status dr_antialias_construct_topology_hash_static(const int32_t* tri, int T, int32_t* topo,
+                                                                 void* stream) {
+  if (T < 0 || T > DR_STATIC_TOPO_MAX_TRIS) return DR_EINVAL;
+  if (T == 0) return DR_OK;
+  if (!tri || !topo) return DR_EINVAL;
+  unsigned char* base = nullptr;
+  dr_status st = static_scratch(&base);
+  if (st != DR_OK) return st;
+  const int64_t E = (int64_t)T * 3;
+  uint32_t cap = 1024;
+  while (cap < (uint32_t)(2 * E)) cap <<= 1;
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(base);
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(keys + kStaticCap);
+  int32_t* ra = reinterpret_cast<int32_t*>(cnt + kStaticCap);
+  int32_t* rb = ra + kStaticCap;
+  uint32_t* rs = reinterpret_cast<uint32_t*>(rb + kStaticCap);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  k_topo_init<<<dr::grid_for((int64_t)cap, 256), 256, 0, s>>>(keys, cnt, cap);
+  k_topo_insert<<<dr::grid_for(E, 256), 256, 0, s>>>(tri, T, keys, cnt, ra, rb, rs, cap - 1, nullptr);
+  k_topo_classify<<<dr::grid_for(E, 256), 256, 0, s>>>(T, cnt, ra, rb, rs, topo);
+  return cudaGetLastError() == cudaSuccess ? DR_OK : DR_ECUDA;
 }

@@ -50,6 +50,7 @@ SIGNATURES = {
     "dr_texture_fwd": (I, [P, I, I, P, I, I, I, I, P, I, P, P, F, P, I, I, I, P]),
     "dr_texture_bwd": (I, [P, I, I, P, I, I, I, I, P, I, P, P, F, P, I, I, I, P, P, P, P, P]),
     "dr_antialias_construct_topology_hash": (I, [P, P, I, P]),
+    "dr_antialias_construct_topology_hash_static": (I, [P, I, P, P]),
     "dr_antialias_fwd": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P]),
     "dr_antialias_bwd": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P, P, P]),
     "dr_antialias_xf_fwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P]),
