@@ -257,18 +257,8 @@ def time_cpu(cfg: str, reps: int = 2):
 # ------------------------------------------------------------------ main
 
 def dist_setup(args):
-    import torch
-    import torch.distributed as dist
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if ws > 1 and not dist.is_initialized():
-        import datetime
-        backend = "nccl" if torch.cuda.is_available() else "gloo"
-        if torch.cuda.is_available():
-            torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
-    return ws, rank, local
+    from diffrast import dist as D
+    return D.init_from_env(timeout_s=300.0)
 
 
 def run_reference(args, ws, rank):
@@ -327,33 +317,20 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     cfg = args.config
-    total = chains.TOTAL_VIEWS[cfg]
-    if cfg in WEAK:
-        per = args.views or total
-        lo, hi, tot = rank * per, (rank + 1) * per, per * ws
-    else:
-        per = args.views or total // ws
-        lo, hi, tot = rank * per, (rank + 1) * per, per * ws
+    from diffrast import dist as D
+    total = args.views or chains.TOTAL_VIEWS[cfg]
+    lo, hi, tot = D.view_range(total, rank, ws, weak=cfg in WEAK)
     kw = {}
     if cfg == "cfg4":
         kw = dict(view_lo=lo, view_hi=hi, total_views=tot)
-    elif cfg == "cfg1":
-        kw = {}
-    else:
+    elif cfg != "cfg1":
         kw = dict(view_lo=lo, view_hi=hi)
     chain = chains.CHAINS[cfg](dev, **kw)
     torch.cuda.synchronize()
 
-    flat_buf = {}
-
     def allreduce():
-        if ws == 1:
-            return
-        gs = chain.shared_grads()
-        flat = torch._utils._flatten_dense_tensors(gs)
-        dist.all_reduce(flat)
-        for g, f in zip(gs, torch._utils._unflatten_dense_tensors(flat, gs)):
-            g.copy_(f)
+        if ws > 1:
+            D.allreduce_grads(chain.shared_grads())
 
     def one_step():
         chain.zero_grad()
@@ -389,10 +366,7 @@ def main():
     report = _lib.timing_report(local)
     _lib.set_timing(False, local)
     clk = clocks.stop()
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = D.max_over_ranks(ms, device=dev)
     diffrast.sync(local)
 
     pixels_all = chain.info.pixels * ws
@@ -473,12 +447,8 @@ def run_e2e(chain, cfg, args, ws, dev, allreduce):
         out.copy_(loss.detach(), non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if ws > 1:
-        import torch.distributed as dist
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    from diffrast import dist as D
+    ms = D.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
     return {"value": chain.info.pixels * ws / (ms * 1e-3) / 1e6, "unit": "Mpx/s", "ms_per_step": ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
             "inputs": "per-step targets and view transforms from pinned host memory; loss read back"}

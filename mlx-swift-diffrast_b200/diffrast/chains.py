@@ -89,8 +89,8 @@ class Cfg2(Chain):
     """Icosphere L4, 8 views at 512^2: RGB and spherical-UV interpolation, bilinear
     clamp texture 512^2x3, shade = rgb * tex, antialias, MSE; d_pos, d_attr, d_tex."""
 
-    def __init__(self, dev, view_lo=0, view_hi=8):
-        s = scenes.scene_cfg2()
+    def __init__(self, dev, view_lo=0, view_hi=8, res=512, tex=512):
+        s = scenes.scene_cfg2(n_views=view_hi, res=res, tex=tex)
         self.pos = _t(s["pos"][view_lo:view_hi], dev, True)
         self.tri = _t(s["tri"], dev)
         self.rgb = _t(s["rgb"], dev, True)
@@ -126,8 +126,8 @@ class Cfg3(Chain):
     trilinear 2048^2x4 noise texture, wrap, per-pixel mip bias ~U[-1,1]; MSE;
     backward d_tex (all levels folded), d_uv, d_uvDA -> d_rast/d_rast_db -> d_pos."""
 
-    def __init__(self, dev, view_lo=0, view_hi=16):
-        s = scenes.scene_cfg3()
+    def __init__(self, dev, view_lo=0, view_hi=16, res=1024, tex=2048):
+        s = scenes.scene_cfg3(n_views=view_hi, res=res, tex=tex)
         self.pos = _t(s["pos"][view_lo:view_hi], dev, True)
         self.tri = _t(s["tri"], dev)
         self.uv = _t(s["uv"], dev, True)
@@ -212,8 +212,8 @@ class Cfg5(Chain):
     reference's cube mode), antialias, MSE; backward d_verts and d_tex.  The
     rank's views run as micro-batches with gradient accumulation."""
 
-    def __init__(self, dev, view_lo=0, view_hi=256, micro=16, res=2048, freq=158):
-        s = scenes.scene_cfg5(n_views=view_hi, res=res, freq=freq)
+    def __init__(self, dev, view_lo=0, view_hi=256, micro=16, res=2048, freq=158, cube=1024):
+        s = scenes.scene_cfg5(n_views=view_hi, res=res, freq=freq, cube=cube)
         self.verts = _t(np.concatenate([s["verts"], np.ones((s["verts"].shape[0], 1), np.float32)], 1),
                         dev, True)
         self.tri = _t(s["tri"], dev)
@@ -227,6 +227,7 @@ class Cfg5(Chain):
         g.manual_seed(s["target_seed"] * 1000 + view_lo)
         self.target = torch.rand((n, H, W, 3), generator=g, device=dev)
         self.topo = ops.antialias_construct_topology_hash(self.tri)
+        self.bg_dir = torch.tensor([0.0, 0.0, 1.0], device=dev)
         self.micro = micro
         self.info = ChainInfo("cfg5", n, self.res, n * H * W)
 
@@ -244,6 +245,9 @@ class Cfg5(Chain):
             xf = self.mvp[a:b]
             ((rast, _),) = ops.rasterize_layers(self.verts, self.tri, self.res, 1, grad_db=False, xform=xf)
             nrm, _ = ops.interpolate(self.nrm, rast, self.tri)
+            # Background pixels interpolate a zero normal, which has no cube face
+            # (the projection divides by max|dir| = 0): look them up along +z.
+            nrm = nrm + (rast[..., 3:] == 0).float() * self.bg_dir
             col = ops.texture(self.cube, nrm, boundary_mode=ops.BoundaryMode.cube)
             aa = ops.antialias(col, rast, self.verts, self.tri, self.topo, xform=xf)
             loss = ops.mse_loss(aa, self.target[a:b]) * ((b - a) / n)

@@ -1,0 +1,67 @@
+"""Data parallelism over views: one process per GPU.
+
+The chain partitions over the view batch: every kernel indexes by view, so
+ranks render disjoint views with no collective in the data path.  The only
+exchange per step is the sum of the shared-parameter gradients (mesh vertices,
+attribute table, texture), done as one flattened all-reduce (NCCL over
+NVLink on GPUs; gloo in the CPU tests).
+"""
+from __future__ import annotations
+
+import datetime
+import os
+from typing import List, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def view_range(total_views: int, rank: int, world: int, weak: bool) -> Tuple[int, int, int]:
+    """Views [lo, hi) of `rank` and the job's total view count.
+
+    weak:   every rank renders `total_views` views of its own (views are numbered
+            globally, rank r owns [r*total, (r+1)*total)); per-GPU work is fixed.
+    strong: the job's `total_views` are split into equal contiguous blocks.
+    """
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} / world {world}")
+    if weak:
+        return rank * total_views, (rank + 1) * total_views, total_views * world
+    if total_views % world:
+        raise ValueError(f"{total_views} views do not split evenly over {world} ranks")
+    per = total_views // world
+    return rank * per, (rank + 1) * per, total_views
+
+
+def allreduce_grads(grads: Sequence[torch.Tensor], group=None) -> None:
+    """Sum `grads` across ranks in place with one flattened all-reduce."""
+    grads = [g for g in grads if g is not None]
+    if not grads or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return
+    flat = torch._utils._flatten_dense_tensors(grads)
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    for g, f in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
+        g.copy_(f)
+
+
+def init_from_env(timeout_s: float = 300.0) -> Tuple[int, int, int]:
+    """Initialise the process group from torchrun's environment; returns
+    (world, rank, local_rank).  NCCL when CUDA is present, gloo otherwise."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
+    return world, rank, local
+
+
+def max_over_ranks(value: float, device=None) -> float:
+    """Maximum of a per-rank scalar (step times are reported as the max)."""
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())

@@ -218,22 +218,22 @@ def scene_icosphere_views(n_views: int, res: int, jitter: float = 0.02, level: i
                 mvps=mvps.astype(np.float32), pos=pos, res=(res, res))
 
 
-def scene_cfg2():
-    s = scene_icosphere_views(8, 512)
+def scene_cfg2(n_views: int = 8, res: int = 512, tex: int = 512, level: int = 4):
+    s = scene_icosphere_views(n_views, res, level=level)
     V = s["pos"].shape[1]
     s["rgb"] = rng(5).random((V, 3)).astype(np.float32)
     s["uv"] = spherical_uv(s["unit"])
-    s["tex"] = rng(6).random((1, 512, 512, 3)).astype(np.float32)
-    s["target"] = rng(7).random((8, 512, 512, 3)).astype(np.float32)
+    s["tex"] = rng(6).random((1, tex, tex, 3)).astype(np.float32)
+    s["target"] = rng(7).random((n_views, res, res, 3)).astype(np.float32)
     return s
 
 
-def scene_cfg3():
-    s = scene_icosphere_views(16, 1024)
+def scene_cfg3(n_views: int = 16, res: int = 1024, tex: int = 2048, level: int = 4):
+    s = scene_icosphere_views(n_views, res, level=level)
     s["uv"] = spherical_uv(s["unit"])
-    s["tex"] = value_noise(2048, 2048, 4, seed=8)[None]
-    s["bias_map"] = rng(9).uniform(-1, 1, (16, 1024, 1024)).astype(np.float32)
-    s["target"] = rng(10).random((16, 1024, 1024, 4)).astype(np.float32)
+    s["tex"] = value_noise(tex, tex, 4, seed=8)[None]
+    s["bias_map"] = rng(9).uniform(-1, 1, (n_views, res, res)).astype(np.float32)
+    s["target"] = rng(10).random((n_views, res, res, 4)).astype(np.float32)
     return s
 
 
@@ -247,10 +247,10 @@ def scene_cfg4(n_views: int = 32, res: int = 1024, n_isolated: int = 800_000, n_
                 n_views=n_views, target_seed=13)
 
 
-def scene_cfg5(n_views: int = 256, res: int = 2048, freq: int = 158):
+def scene_cfg5(n_views: int = 256, res: int = 2048, freq: int = 158, cube: int = 1024):
     unit, tri = geodesic_sphere(freq)
     verts = jitter_radial(unit, 0.01, 13)
     mvps = view_mvps(n_views, 14)
-    cube = rng(15).random((1, 6, 1024, 1024, 3)).astype(np.float32)
+    cube_tex = rng(15).random((1, 6, cube, cube, 3)).astype(np.float32)
     return dict(unit=unit.astype(np.float32), verts=verts.astype(np.float32), tri=tri,
-                mvps=mvps.astype(np.float32), cube=cube, res=(res, res), n_views=n_views, target_seed=16)
+                mvps=mvps.astype(np.float32), cube=cube_tex, res=(res, res), n_views=n_views, target_seed=16)

@@ -89,6 +89,8 @@ def cfg5(pos, tri, nrm, cube, target, res, topo=None, nthreads=0):
     topo = topology_hash(tri) if topo is None else topo
     rast, _ = rasterize(pos, tri, res, grad_db=False, nthreads=nthreads)
     d, _ = interpolate(nrm, rast, tri, nthreads=nthreads)
+    # background pixels have a zero normal: look them up along +z
+    d = (d + (rast[..., 3:] == 0).astype(np.float32) * np.array([0, 0, 1], np.float32)).astype(np.float32)
     col = texture(cube, d, boundary_mode="cube", nthreads=nthreads)
     aa = antialias(col, rast, pos, tri, topo, nthreads=nthreads)
     loss, d_aa = _mse(aa, target, nthreads)
