@@ -131,8 +131,9 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         V, T, A = chain.base.shape[0], chain.tri.shape[0], 8
         # Vertices are the shared [V, 4] soup (Nv = 1) transformed per view in-kernel.
         add("raster_setup", V * 16 + T * 12)  # both layers share setup and tile lists
+        # One tile pass writes both layers (rast + rast_db each); layer 0 is never re-read.
+        add("raster_tiles", 2 * (P * 16 + P * 16))
         for layer in (0, 1):
-            add("raster_tiles", P * 16 + P * 16 + (P * 16 if layer else 0))
             add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A))
             # out_da never reaches the loss: the VJP runs without the DA terms.
             add("interp_bwd", 2 * V * A * 4 + T * 12 + P * (16 + 16 + 4 * A))

@@ -18,6 +18,7 @@ enum : unsigned {
   DR_DEVERR_VERTEX = 1u,    // a triangle names a vertex outside [0, V)
   DR_DEVERR_TRI_ID = 2u,    // a rast pixel names a triangle outside [0, T)
   DR_DEVERR_CAPACITY = 4u,  // a fixed-capacity buffer would have overflowed
+  DR_DEVERR_RETRY = 8u,     // a compare-and-swap loop hit its iteration bound
 };
 
 // Workspace slots: each is an independent grow-only device buffer.

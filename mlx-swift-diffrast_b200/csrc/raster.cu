@@ -196,22 +196,92 @@ __device__ __forceinline__ unsigned long long pack_key(float z, int t) {
   return ((unsigned long long)u << 32) | (unsigned)t;
 }
 
+// Two depth layers in one candidate pass.  Per pixel the pair (k0, k1) holds
+// k0 = the minimum key of all fragments seen and k1 = the minimum key among
+// those whose z is strictly greater than z(k0) — exactly what a second pass
+// peeling at layer 0's depth selects (Rasterize.swift:465-470: z <= peel_z is
+// rejected).  A fragment f updates the pair as
+//   z_f <  z(k0): (k0, k1) <- (f, k0)        every earlier fragment lies behind f
+//   z_f == z(k0): (k0, k1) <- (min(k0, f), k1)
+//   z_f >  z(k0): (k0, k1) <- (k0, min(k1, f))
+// through a 128-bit compare-and-swap.  Both halves only ever decrease and
+// k0 <= k1, so f can change nothing once key_f >= k1: a 64-bit read of k1
+// filters almost every fragment before the CAS.
+struct __align__(16) KeyPair {
+  unsigned long long k0, k1;
+};
+
+__device__ __forceinline__ void fold_pair(KeyPair* slot, unsigned long long key, unsigned* err) {
+  KeyPair cur;
+  cur.k0 = slot->k0;  // a possibly stale start; only CAS results are trusted
+  cur.k1 = slot->k1;
+  // Every failed CAS means another lane lowered the pair, which can happen at
+  // most a few times per fragment in flight; the bound only guards the loop.
+  for (int it = 0; it < (1 << 16); ++it) {
+    const unsigned zf = (unsigned)(key >> 32), z0 = (unsigned)(cur.k0 >> 32);
+    KeyPair nw;
+    if (zf < z0) { nw.k0 = key; nw.k1 = cur.k0; }
+    else if (zf == z0) { nw.k0 = key < cur.k0 ? key : cur.k0; nw.k1 = cur.k1; }
+    else { nw.k0 = cur.k0; nw.k1 = key < cur.k1 ? key : cur.k1; }
+    const KeyPair prev = atomicCAS_block(slot, cur, nw);
+    if (prev.k0 == cur.k0 && prev.k1 == cur.k1) return;
+    cur = prev;
+  }
+  dr_flag(err, DR_DEVERR_RETRY);
+}
+
+// Recompute the winner's (u, v, z) and rast_db bit-identically from its record
+// and write one output pixel (zeros where the key is empty).
+template <bool DB>
+__device__ __forceinline__ void write_pixel(const float4* __restrict__ rec, int64_t rec_view,
+                                            unsigned long long key, float x, float y, int H, int W,
+                                            float4* __restrict__ rast, float4* __restrict__ rast_db, int64_t pix) {
+  if (key == ~0ull) {
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    rast[pix] = z4;
+    if (DB) rast_db[pix] = z4;
+    return;
+  }
+  const int t = (int)(unsigned)(key & 0xffffffffull);
+  const Rec r = load_rec(rec, rec_view + t);
+  const float inv_area = FD(1.0f, r.area);
+  const float dx0 = FS(r.sx0, x), dx1 = FS(r.sx1, x), dx2 = FS(r.sx2, x);
+  const float dy0 = FS(r.sy0, y), dy1 = FS(r.sy1, y), dy2 = FS(r.sy2, y);
+  const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));
+  const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
+  const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
+  const float bw = FM(e0, inv_area), u = FM(e1, inv_area), v = FM(e2, inv_area);
+  const float z = FA(FA(FM(bw, r.sz0), FM(u, r.sz1)), FM(v, r.sz2));
+  rast[pix] = make_float4(u, v, z, (float)(t + 1));
+  if (DB) {
+    // Rasterize.swift:586-598
+    const float k_x = FD(2.0f, (float)W), k_y = FD(-2.0f, (float)H);
+    rast_db[pix] = make_float4(FM(FM(FS(r.sy2, r.sy0), inv_area), k_x),
+                               FM(FM(FS(r.sx0, r.sx2), inv_area), k_y),
+                               FM(FM(FS(r.sy0, r.sy1), inv_area), k_x),
+                               FM(FM(FS(r.sx1, r.sx0), inv_area), k_y));
+  }
+}
+
 // Per-tile fine raster.  Each warp takes 32 candidates at a time, stages their
 // records in shared memory, and flattens their (candidate, pixel) work items
 // (pixels of the candidate's rectangle inside the tile) with a warp prefix
 // sum, so all 32 lanes test one pixel each per round regardless of how the
 // rectangle sizes vary (1 to 256 pixels).
+// MODE: 0 = one layer, 1 = one layer peeled at `peel`, 2 = layers 0 and 1 at once.
 constexpr int WARPS = TILE_PIX / 32;
 constexpr int SSTRIDE = 5;  // float4 per staged candidate (80 B: conflict-free 128-bit phases)
 
-template <bool PEEL, bool DB>
-__global__ void __launch_bounds__(TILE_PIX)
+template <int MODE, bool DB>
+__global__ void __launch_bounds__(TILE_PIX, 5)
 k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int nty,
                const uint32_t* __restrict__ tile_off, const uint32_t* __restrict__ tile_count,
                const int32_t* __restrict__ list, const float* __restrict__ peel,
-               float4* __restrict__ rast, float4* __restrict__ rast_db) {
-  __shared__ unsigned long long s_key[TILE_PIX];
-  __shared__ float s_peel[TILE_PIX];
+               float4* __restrict__ rast, float4* __restrict__ rast_db,
+               float4* __restrict__ rast1, float4* __restrict__ rast_db1, unsigned* err) {
+  constexpr bool PEEL = MODE == 1, TWO = MODE == 2;
+  __shared__ KeyPair s_key[TILE_PIX];  // k1 unused unless TWO
+  __shared__ float s_peel[PEEL ? TILE_PIX : 1];
   __shared__ float s_ndcx[TILE], s_ndcy[TILE];
   __shared__ float4 s_stage[WARPS][32 * SSTRIDE];
   __shared__ unsigned s_next;
@@ -225,7 +295,8 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   const bool inside_img = (px < W) && (py < H);
   const int64_t pix = ((int64_t)n * H + py) * W + px;
 
-  s_key[tid] = ~0ull;
+  s_key[tid].k0 = ~0ull;
+  s_key[tid].k1 = ~0ull;
   if (PEEL) {
     float pz = -1e30f;
     if (inside_img) {
@@ -238,7 +309,6 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   else if (tid < 2 * TILE) s_ndcy[tid - TILE] = ndc_y_of(ty0 + tid - TILE, H);
   if (tid == 0) s_next = 0u;
   __syncthreads();
-
   const uint32_t gt = (uint32_t)blockIdx.x;
   const uint32_t begin = __ldg(tile_off + gt), cnt = __ldg(tile_count + gt);
   const int64_t rec_view = (int64_t)n * T;
@@ -311,43 +381,24 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
       if (FM(e0, area) < 0.0f || FM(e1, area) < 0.0f || FM(e2, area) < 0.0f) continue;
       const float bw = FM(e0, f2.z), u = FM(e1, f2.z), v = FM(e2, f2.z);
       const float z = FA(FA(FM(bw, f0.z), FM(u, f1.y)), FM(v, f2.x));
-      if (z < -1.0f || z > 1.0f) continue;
+      // NaN never wins in the reference (its strict z < best_z is false).
+      if (!(z >= -1.0f && z <= 1.0f)) continue;
       const int p = ly * TILE + lx;
       if (PEEL && z <= s_peel[p]) continue;
       const unsigned long long key = pack_key(z, __float_as_int(f2.w));
-      if (key < s_key[p]) atomicMin(&s_key[p], key);
+      if (TWO) {
+        if (key < s_key[p].k1) fold_pair(&s_key[p], key, err);
+      } else if (key < s_key[p].k0) {
+        atomicMin(&s_key[p].k0, key);
+      }
     }
     __syncwarp();
   }
   __syncthreads();
   if (!inside_img) return;
-  const unsigned long long key = s_key[tid];
-  if (key == ~0ull) {
-    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    rast[pix] = z4;
-    if (DB) rast_db[pix] = z4;
-    return;
-  }
-  const int t = (int)(unsigned)(key & 0xffffffffull);
-  const Rec r = load_rec(rec, rec_view + t);
-  const float inv_area = FD(1.0f, r.area);
   const float x = s_ndcx[px - tx0], y = s_ndcy[py - ty0];
-  const float dx0 = FS(r.sx0, x), dx1 = FS(r.sx1, x), dx2 = FS(r.sx2, x);
-  const float dy0 = FS(r.sy0, y), dy1 = FS(r.sy1, y), dy2 = FS(r.sy2, y);
-  const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));
-  const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
-  const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
-  const float bw = FM(e0, inv_area), u = FM(e1, inv_area), v = FM(e2, inv_area);
-  const float z = FA(FA(FM(bw, r.sz0), FM(u, r.sz1)), FM(v, r.sz2));
-  rast[pix] = make_float4(u, v, z, (float)(t + 1));
-  if (DB) {
-    // Rasterize.swift:586-598
-    const float k_x = FD(2.0f, (float)W), k_y = FD(-2.0f, (float)H);
-    rast_db[pix] = make_float4(FM(FM(FS(r.sy2, r.sy0), inv_area), k_x),
-                               FM(FM(FS(r.sx0, r.sx2), inv_area), k_y),
-                               FM(FM(FS(r.sy0, r.sy1), inv_area), k_x),
-                               FM(FM(FS(r.sx1, r.sx0), inv_area), k_y));
-  }
+  write_pixel<DB>(rec, rec_view, s_key[tid].k0, x, y, H, W, rast, rast_db, pix);
+  if (TWO) write_pixel<DB>(rec, rec_view, s_key[tid].k1, x, y, H, W, rast1, rast_db1, pix);
 }
 
 // d_pos: Rasterize.swift:637-812, one thread per pixel.  Pixels of a warp that
@@ -569,32 +620,33 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
   return DR_OK;
 }
 
-// One depth layer over prepared tile lists (peel: previous layer or NULL).
+// One depth layer over prepared tile lists (peel: previous layer or NULL), or
+// layers 0 and 1 together when rast1 is given (then peel must be NULL).
 dr_status raster_layer(dr_ctx* ctx, const Prepared& pr, int T, int H, int W, const float* peel_layer,
-                       float* rast, float* rast_db) {
+                       float* rast, float* rast_db, float* rast1 = nullptr, float* rast_db1 = nullptr) {
   DR_REQUIRE(ctx, rast != nullptr, "rasterize: rast output is required");
-  DR_REQUIRE(ctx, aligned16(rast) && (!rast_db || aligned16(rast_db)) && (!peel_layer || aligned16(peel_layer)),
+  DR_REQUIRE(ctx, aligned16(rast) && (!rast_db || aligned16(rast_db)) && (!peel_layer || aligned16(peel_layer)) &&
+                      (!rast1 || aligned16(rast1)) && (!rast_db1 || aligned16(rast_db1)),
              "rasterize: rast/rast_db/peel_layer must be 16-byte aligned");
   const unsigned grid = (unsigned)pr.ntiles_all;
   float4* r4 = reinterpret_cast<float4*>(rast);
   float4* d4 = reinterpret_cast<float4*>(rast_db);
+  float4* r41 = reinterpret_cast<float4*>(rast1);
+  float4* d41 = reinterpret_cast<float4*>(rast_db1);
   const int ntx = pr.ntx, nty = pr.nty;
   DR_TB(ctx);
-  if (peel_layer) {
-    if (rast_db)
-      k_raster_tiles<true, true><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,
-                                                                      pr.tile_count, pr.list, peel_layer, r4, d4);
-    else
-      k_raster_tiles<true, false><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,
-                                                                       pr.tile_count, pr.list, peel_layer, r4, d4);
+#define DR_RT(MODEV, DBV, PEELP)                                                                               \
+  k_raster_tiles<MODEV, DBV><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,        \
+                                                                 pr.tile_count, pr.list, PEELP, r4, d4, r41, d41, \
+                                                                 ctx->d_err)
+  if (rast1) {
+    if (rast_db) DR_RT(2, true, nullptr); else DR_RT(2, false, nullptr);
+  } else if (peel_layer) {
+    if (rast_db) DR_RT(1, true, peel_layer); else DR_RT(1, false, peel_layer);
   } else {
-    if (rast_db)
-      k_raster_tiles<false, true><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,
-                                                                       pr.tile_count, pr.list, nullptr, r4, d4);
-    else
-      k_raster_tiles<false, false><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,
-                                                                        pr.tile_count, pr.list, nullptr, r4, d4);
+    if (rast_db) DR_RT(0, true, nullptr); else DR_RT(0, false, nullptr);
   }
+#undef DR_RT
   DR_LAUNCHED(ctx, "raster_tiles");
   return DR_OK;
 }
@@ -622,8 +674,16 @@ dr_status layers_fwd(dr_ctx* ctx, const float* pos, const float* xform, int V, c
   Prepared pr;
   dr_status st = raster_prepare(ctx, pos, xform, V, tri, T, ranges, N, H, W, pr);
   if (st != DR_OK) return st;
-  for (int l = 0; l < num_layers; ++l) {
-    st = raster_layer(ctx, pr, T, H, W, l ? rast[l - 1] : nullptr, rast[l], rast_db ? rast_db[l] : nullptr);
+  auto db_of = [&](int l) { return rast_db ? rast_db[l] : nullptr; };
+  int l = 0;
+  // Layers 0 and 1 come out of one candidate pass when both or neither carry rast_db.
+  if (num_layers >= 2 && ((db_of(0) == nullptr) == (db_of(1) == nullptr))) {
+    st = raster_layer(ctx, pr, T, H, W, nullptr, rast[0], db_of(0), rast[1], db_of(1));
+    if (st != DR_OK) return st;
+    l = 2;
+  }
+  for (; l < num_layers; ++l) {
+    st = raster_layer(ctx, pr, T, H, W, l ? rast[l - 1] : nullptr, rast[l], db_of(l));
     if (st != DR_OK) return st;
   }
   return DR_OK;

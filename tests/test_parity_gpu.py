@@ -301,3 +301,43 @@ def test_xf_mode_matches_instanced_on_transformed_positions(cu, soup):
              + oracle.antialias_bwd(col.cpu().numpy(), r0o, pos, tri, wa, topo)[1])
     ref = oracle.xf_vertex_grad(d_pos, M)
     assert rel_l2(vb.grad.cpu().numpy(), ref) < 1e-4
+
+
+def test_layers_fused_pass_depth_ties(cu, soup):
+    # Every triangle appears three times: twice at its own depth (an exact z
+    # tie, broken by the lower index) and once pushed back.  Layer 1 must skip
+    # the tied copy (z <= layer-0 z is peeled) and find the pushed-back one or a
+    # deeper triangle — the z == z(k0) branch of the fused two-layer pass.
+    import torch
+
+    import diffrast
+    pos, tri = soup
+    pos = pos[:, :, :].copy()
+    V = pos.shape[1]
+    back = pos.copy()
+    back[..., 2] += 0.05 * back[..., 3]
+    p = np.concatenate([pos, back], axis=1)
+    t = np.concatenate([tri, tri, tri + V]).astype(np.int32)
+    layers = diffrast.rasterize_layers(torch.from_numpy(p).cuda(), torch.from_numpy(t).cuda(), (192, 160), 3)
+    r_prev = None
+    for l in range(3):
+        r_o, d_o = O.rasterize(p, t, (192, 160), peel=r_prev)
+        assert np.array_equal(layers[l][0].cpu().numpy(), r_o), l
+        assert np.array_equal(layers[l][1].cpu().numpy(), d_o), l
+        r_prev = r_o
+    ids0 = layers[0][0][..., 3].cpu().numpy()
+    assert ids0.max() <= tri.shape[0]  # ties resolve to the first copy
+
+
+def test_layers_full_size_soup_two_views(cu):
+    # Both depth layers of two full 1024^2 cfg4 views from the fused pass.
+    import torch
+
+    import diffrast
+    s = scenes.scene_cfg4(n_views=2)
+    pos = np.einsum("nij,vj->nvi", s["sim"], s["base"]).astype(np.float32)
+    layers = diffrast.rasterize_layers(torch.from_numpy(pos).cuda(), torch.from_numpy(s["tri"]).cuda(), s["res"], 2)
+    r0o, d0o = O.rasterize(pos, s["tri"], s["res"])
+    r1o, d1o = O.rasterize(pos, s["tri"], s["res"], peel=r0o)
+    assert np.array_equal(layers[0][0].cpu().numpy(), r0o) and np.array_equal(layers[0][1].cpu().numpy(), d0o)
+    assert np.array_equal(layers[1][0].cpu().numpy(), r1o) and np.array_equal(layers[1][1].cpu().numpy(), d1o)
