@@ -41,7 +41,7 @@ extern "C" {
 #define DR_API
 #endif
 
-#define DR_ABI_VERSION 1
+#define DR_ABI_VERSION 2
 #define DR_MAX_MIP_LEVELS 32
 #define DR_MAX_DIFF_ATTRS 1024
 
@@ -275,31 +275,42 @@ DR_API dr_status dr_antialias_construct_topology_hash_static(const int32_t* tri,
 /* Forward.  Replaces DiffRast.antialias (Antialias.swift:90-131) and
  * diffrast_antialias_fwd (Antialias.swift:333-358).
  *   color: [N, H, W, C]; rast: [N, H, W, 4]; pos: [N, V, 4] (instanced, as the
- *   reference requires); tri: [T, 3]; topo: [T, 3]; out: [N, H, W, C]. */
+ *   reference requires); tri: [T, 3]; topo: [T, 3]; out: [N, H, W, C].
+ *   aa_work: NULL, or dr_antialias_work_bytes(N, H, W) bytes (16-byte aligned)
+ *   that receive each pixel's silhouette record for the VJP.  It has no
+ *   counterpart in the reference, whose VJP re-runs the silhouette search;
+ *   passing it to dr_antialias_bwd gives the same gradients faster. */
 DR_API dr_status dr_antialias_fwd(dr_ctx* ctx, const float* color, int N, int H,
                            int W, int C, const float* rast, const float* pos,
                            int V, const int32_t* tri, int T,
-                           const int32_t* topo, float* out);
+                           const int32_t* topo, float* out, void* aa_work);
 
 /* VJP.  Replaces diffrast_antialias_bwd_color / _bwd_pos
- * (Antialias.swift:388-524).  d_color: out [N, H, W, C]; d_pos: out [N, V, 4]. */
+ * (Antialias.swift:388-524).  d_color: out [N, H, W, C]; d_pos: out [N, V, 4].
+ *   aa_work: NULL (the silhouettes are searched again, as the reference does)
+ *   or the buffer the forward filled for this same rast / pos / tri / topo. */
 DR_API dr_status dr_antialias_bwd(dr_ctx* ctx, const float* color, int N, int H,
                            int W, int C, const float* rast, const float* pos,
                            int V, const int32_t* tri, int T,
                            const int32_t* topo, const float* d_out,
-                           float* d_color, float* d_pos);
+                           float* d_color, float* d_pos, const void* aa_work);
+
+/* Size of the aa_work buffer for N views of H x W pixels: 17 bytes per pixel
+ * (a float4 of per-direction betas, then one byte of selected edges), rounded
+ * up to 16.  No counterpart in the reference. */
+DR_API size_t dr_antialias_work_bytes(int N, int H, int W);
 
 /* Antialias with per-view transformed vertices (see dr_rasterize_xf_fwd);
- * no counterpart in the reference.  d_verts: out [V, 4]. */
+ * no counterpart in the reference.  d_verts: out [V, 4].  aa_work as above. */
 DR_API dr_status dr_antialias_xf_fwd(dr_ctx* ctx, const float* color, int N, int H,
                               int W, int C, const float* rast, const float* verts,
                               int V, const float* xform, const int32_t* tri, int T,
-                              const int32_t* topo, float* out);
+                              const int32_t* topo, float* out, void* aa_work);
 DR_API dr_status dr_antialias_xf_bwd(dr_ctx* ctx, const float* color, int N, int H,
                               int W, int C, const float* rast, const float* verts,
                               int V, const float* xform, const int32_t* tri, int T,
                               const int32_t* topo, const float* d_out,
-                              float* d_color, float* d_verts);
+                              float* d_color, float* d_verts, const void* aa_work);
 
 /* ---- loss helper (the MSE of the reference's examples) ------------------ */
 

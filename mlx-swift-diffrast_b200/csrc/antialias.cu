@@ -95,7 +95,7 @@ __global__ void k_topo_classify(int T, const uint32_t* __restrict__ cnt, const i
 struct SilDir {
   bool active;
   float beta;
-  int ie0, ie1;
+  int kk, ie0, ie1;
   float e0x, e0y, e1x, e1y, t, denom, dbeta;
   bool horiz;
 };
@@ -111,6 +111,53 @@ template <bool XF>
 __device__ __forceinline__ float4 vpos(const float* __restrict__ pos, const Mat4& M, int V, int pn, int a) {
   if (XF) return mat4_apply(M, ldg4(pos + (int64_t)a * 4));
   return ldg4(pos + ((int64_t)pn * V + a) * 4);
+}
+
+// Pixel-space projection E = ((x/w + 1) W/2, (1 - y/w) H/2) (Antialias.swift:240-247).
+__device__ __forceinline__ void screen_of(const float4& p, int H, int W, float& ex, float& ey) {
+  ex = (p.x / p.w + 1.0f) * (float)W * 0.5f;
+  ey = (1.0f - p.y / p.w) * (float)H * 0.5f;
+}
+
+// Where the edge (e0, e1) crosses the segment between the centres of pixel
+// (ph, pw) and its neighbour (Antialias.swift:264-325): beta > 0 iff the
+// crossing lies inside this pixel's cell.  Shared by the forward's search and
+// the backward's replay, so both produce the same bits.
+__device__ __forceinline__ void crossing(bool horiz, int ph, int pw, float e0x, float e0y, float e1x, float e1y,
+                                         float& beta, float& t_val, float& denom, float& dbeta) {
+  const float pcx = (float)pw + 0.5f, pcy = (float)ph + 0.5f;
+  beta = 0.0f; t_val = 0.0f; dbeta = 0.0f;
+  if (horiz) {
+    const float dyv = e1y - e0y;
+    denom = dyv;
+    if (fabsf(dyv) >= 1e-7f) {
+      const float tval = (pcy - e0y) / dyv;
+      t_val = tval;
+      if (tval >= 0.0f && tval <= 1.0f) {
+        const float xe = e0x + tval * (e1x - e0x);
+        if (xe > (float)pw && xe < (float)(pw + 1)) {
+          const float d = xe - pcx;
+          beta = 0.5f - fabsf(d);
+          dbeta = (d > 0.0f) ? -1.0f : 1.0f;
+        }
+      }
+    }
+  } else {
+    const float dxv = e1x - e0x;
+    denom = dxv;
+    if (fabsf(dxv) >= 1e-7f) {
+      const float tval = (pcx - e0x) / dxv;
+      t_val = tval;
+      if (tval >= 0.0f && tval <= 1.0f) {
+        const float ye = e0y + tval * (e1y - e0y);
+        if (ye > (float)ph && ye < (float)(ph + 1)) {
+          const float d = ye - pcy;
+          beta = 0.5f - fabsf(d);
+          dbeta = (d > 0.0f) ? -1.0f : 1.0f;
+        }
+      }
+    }
+  }
 }
 
 // One direction of silhouetteBlock (Antialias.swift:189-325) for pixel
@@ -147,11 +194,9 @@ __device__ SilDir sil_dir(const float4* __restrict__ rast, const float* __restri
     if (__ldg(topo + 3 * fg + kk) != target) continue;
     const int a = __ldg(tri + 3 * fg + (kk + 1) % 3), b = __ldg(tri + 3 * fg + (kk + 2) % 3);
     if (a < 0 || a >= V || b < 0 || b >= V) { dr_flag(err, DR_DEVERR_VERTEX); continue; }
-    const float4 pa = vpos<XF>(pos, M, V, pn, a), pq = vpos<XF>(pos, M, V, pn, b);
-    const float E0x = (pa.x / pa.w + 1.0f) * (float)W * 0.5f;
-    const float E0y = (1.0f - pa.y / pa.w) * (float)H * 0.5f;
-    const float E1x = (pq.x / pq.w + 1.0f) * (float)W * 0.5f;
-    const float E1y = (1.0f - pq.y / pq.w) * (float)H * 0.5f;
+    float E0x, E0y, E1x, E1y;
+    screen_of(vpos<XF>(pos, M, V, pn, a), H, W, E0x, E0y);
+    screen_of(vpos<XF>(pos, M, V, pn, b), H, W, E1x, E1y);
     const float ex = E1x - E0x, ey = E1y - E0y;
     const float side_p = ex * (pcy - E0y) - ey * (pcx - E0x);
     const float side_n = ex * (ncy - E0y) - ey * (ncx - E0x);
@@ -162,45 +207,48 @@ __device__ SilDir sil_dir(const float4* __restrict__ rast, const float* __restri
     }
   }
   if (k_sel < 0) return s;
-  float beta = 0.0f, t_val = 0.0f, denom = 0.0f, dbeta = 0.0f;
   const bool horiz = (dh == 0);
-  if (horiz) {
-    const float dyv = e1y - e0y;
-    denom = dyv;
-    if (fabsf(dyv) >= 1e-7f) {
-      const float tval = (pcy - e0y) / dyv;
-      t_val = tval;
-      if (tval >= 0.0f && tval <= 1.0f) {
-        const float xe = e0x + tval * (e1x - e0x);
-        if (xe > (float)pw && xe < (float)(pw + 1)) {
-          const float d = xe - pcx;
-          beta = 0.5f - fabsf(d);
-          dbeta = (d > 0.0f) ? -1.0f : 1.0f;
-        }
-      }
-    }
-  } else {
-    const float dxv = e1x - e0x;
-    denom = dxv;
-    if (fabsf(dxv) >= 1e-7f) {
-      const float tval = (pcx - e0x) / dxv;
-      t_val = tval;
-      if (tval >= 0.0f && tval <= 1.0f) {
-        const float ye = e0y + tval * (e1y - e0y);
-        if (ye > (float)ph && ye < (float)(ph + 1)) {
-          const float d = ye - pcy;
-          beta = 0.5f - fabsf(d);
-          dbeta = (d > 0.0f) ? -1.0f : 1.0f;
-        }
-      }
-    }
-  }
+  float beta, t_val, denom, dbeta;
+  crossing(horiz, ph, pw, e0x, e0y, e1x, e1y, beta, t_val, denom, dbeta);
   if (beta <= 0.0f) return s;
   s.active = true;
   s.beta = beta;
+  s.kk = k_sel;
   s.ie0 = ie0; s.ie1 = ie1;
   s.e0x = e0x; s.e0y = e0y; s.e1x = e1x; s.e1y = e1y;
   s.t = t_val; s.denom = denom; s.dbeta = dbeta; s.horiz = horiz;
+  return s;
+}
+
+// The forward's per-pixel record for the VJP (the optional `aa_work` buffer):
+// beta[P] float4 (one beta per direction, 0 where inactive), then code[P]
+// bytes, 2 bits per direction: 0 inactive, else the selected edge kk + 1.
+__host__ __device__ __forceinline__ size_t aa_work_bytes(int64_t P) {
+  return (size_t)P * 16 + (((size_t)P + 15) & ~(size_t)15);
+}
+
+// Rebuild an active direction's edge from the recorded kk: the same vertex
+// loads, projection and crossing arithmetic the search ran, minus the search.
+template <bool XF>
+__device__ SilDir sil_replay(const float4* __restrict__ rast, const float* __restrict__ pos, const Mat4& M,
+                             const int32_t* __restrict__ tri, int H, int W, int V, int T, int pn, int ph,
+                             int pw, int tri_p, int dir, int kk, unsigned* err) {
+  SilDir s;
+  s.active = false;
+  const int dw = dir == 0 ? 1 : (dir == 2 ? -1 : 0);
+  const int dh = dir == 1 ? 1 : (dir == 3 ? -1 : 0);
+  const int nh = ph + dh, nw = pw + dw;
+  if (nh < 0 || nh >= H || nw < 0 || nw >= W) return s;  // a record from another rast
+  const int fg = tri_p >= 0 ? tri_p : rast_tri(rast, ((int64_t)pn * H + nh) * W + nw, T, err);
+  if (fg < 0) return s;
+  const int a = __ldg(tri + 3 * fg + (kk + 1) % 3), b = __ldg(tri + 3 * fg + (kk + 2) % 3);
+  if (a < 0 || a >= V || b < 0 || b >= V) { dr_flag(err, DR_DEVERR_VERTEX); return s; }
+  screen_of(vpos<XF>(pos, M, V, pn, a), H, W, s.e0x, s.e0y);
+  screen_of(vpos<XF>(pos, M, V, pn, b), H, W, s.e1x, s.e1y);
+  s.horiz = (dh == 0);
+  crossing(s.horiz, ph, pw, s.e0x, s.e0y, s.e1x, s.e1y, s.beta, s.t, s.denom, s.dbeta);
+  s.active = s.beta > 0.0f;
+  s.kk = kk; s.ie0 = a; s.ie1 = b;
   return s;
 }
 
@@ -210,12 +258,13 @@ __device__ __forceinline__ int64_t nbr_pix(int pn, int ph, int pw, int dir, int 
   return ((int64_t)pn * H + (ph + dh)) * W + (pw + dw);
 }
 
-template <bool XF>
+template <bool XF, bool WORK>
 __global__ void k_aa_fwd(const float* __restrict__ color, int N, int H, int W, int C,
                          const float4* __restrict__ rast, const float* __restrict__ pos,
                          const float* __restrict__ xform, int V,
                          const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
-                         float* __restrict__ out, unsigned* err) {
+                         float* __restrict__ out, float4* __restrict__ work_beta,
+                         uint8_t* __restrict__ work_code, unsigned* err) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (pix >= (int64_t)N * H * W) return;
   const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
@@ -225,12 +274,18 @@ __global__ void k_aa_fwd(const float* __restrict__ color, int N, int H, int W, i
   float beta[4];
   int64_t nb[4];
   bool any = false;
+  unsigned code = 0;
 #pragma unroll
   for (int d = 0; d < 4; ++d) {
     const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, d, err);
     beta[d] = s.active ? s.beta : 0.0f;
     nb[d] = s.active ? nbr_pix(pn, ph, pw, d, H, W) : -1;
     any |= s.active;
+    if (s.active) code |= (unsigned)(s.kk + 1) << (2 * d);
+  }
+  if (WORK) {
+    work_beta[pix] = make_float4(beta[0], beta[1], beta[2], beta[3]);
+    work_code[pix] = (uint8_t)code;
   }
   const float* cp = color + pix * C;
   float* o = out + pix * C;
@@ -265,12 +320,15 @@ __device__ __forceinline__ void add_pos(float* p, const Mat4& M, float x, float 
   }
 }
 
-template <bool VEC, bool XF>
+// WORK: the forward's record supplies every beta and each active direction's
+// edge, so no silhouette search runs (neighbour betas are plain loads).
+template <bool VEC, bool XF, bool WORK>
 __global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, int C,
                          const float4* __restrict__ rast, const float* __restrict__ pos,
                          const float* __restrict__ xform, int V,
                          const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
                          const float* __restrict__ d_out, float* __restrict__ d_color, float* __restrict__ d_pos,
+                         const float4* __restrict__ work_beta, const uint8_t* __restrict__ work_code,
                          unsigned* err) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (pix >= (int64_t)N * H * W) return;
@@ -282,9 +340,18 @@ __global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, i
   const float halfW = (float)W * 0.5f, halfH = (float)H * 0.5f;
   float alpha_sum = 0.0f;
   // Own silhouettes: the (1 - sum beta) factor and d_pos (Antialias.swift:405-495).
+  unsigned code = 0;
+  if (WORK) code = __ldg(work_code + pix);
 #pragma unroll 1
   for (int dir = 0; dir < 4; ++dir) {
-    const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, dir, err);
+    SilDir s;
+    if (WORK) {
+      const int kk = (int)((code >> (2 * dir)) & 3u) - 1;
+      if (kk < 0) continue;
+      s = sil_replay<XF>(rast, pos, M, tri, H, W, V, T, pn, ph, pw, tri_p, dir, kk, err);
+    } else {
+      s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, dir, err);
+    }
     if (!s.active) continue;
     alpha_sum += s.beta;
     if (s.beta <= 0.0f || s.beta >= 1.0f) continue;
@@ -334,18 +401,32 @@ __global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, i
   // direction d.
   float nbeta[4];
   int64_t nsrc[4];
+  if (WORK) {
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+      nbeta[d] = 0.0f;
+      nsrc[d] = -1;
+      const int sw = pw - (d == 0 ? 1 : (d == 2 ? -1 : 0));
+      const int sh = ph - (d == 1 ? 1 : (d == 3 ? -1 : 0));
+      if (sw < 0 || sw >= W || sh < 0 || sh >= H) continue;
+      const int64_t p = ((int64_t)pn * H + sh) * W + sw;
+      const float b = __ldg(reinterpret_cast<const float*>(work_beta + p) + d);
+      if (b > 0.0f) { nbeta[d] = b; nsrc[d] = p; }
+    }
+  } else {
 #pragma unroll 1
-  for (int d = 0; d < 4; ++d) {
-    nbeta[d] = 0.0f;
-    nsrc[d] = -1;
-    const int sw = pw - (d == 0 ? 1 : (d == 2 ? -1 : 0));
-    const int sh = ph - (d == 1 ? 1 : (d == 3 ? -1 : 0));
-    if (sw < 0 || sw >= W || sh < 0 || sh >= H) continue;
-    const int64_t p = ((int64_t)pn * H + sh) * W + sw;
-    const int tri_s = rast_tri(rast, p, T, err);
-    if (tri_s == tri_p) continue;  // no silhouette between equal ids
-    const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
-    if (s.active) { nbeta[d] = s.beta; nsrc[d] = p; }
+    for (int d = 0; d < 4; ++d) {
+      nbeta[d] = 0.0f;
+      nsrc[d] = -1;
+      const int sw = pw - (d == 0 ? 1 : (d == 2 ? -1 : 0));
+      const int sh = ph - (d == 1 ? 1 : (d == 3 ? -1 : 0));
+      if (sw < 0 || sw >= W || sh < 0 || sh >= H) continue;
+      const int64_t p = ((int64_t)pn * H + sh) * W + sw;
+      const int tri_s = rast_tri(rast, p, T, err);
+      if (tri_s == tri_p) continue;  // no silhouette between equal ids
+      const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
+      if (s.active) { nbeta[d] = s.beta; nsrc[d] = p; }
+    }
   }
   const float keep = 1.0f - alpha_sum;
   if ((C & 3) == 0 && ((((uintptr_t)d_out) | ((uintptr_t)d_color)) & 15) == 0) {
@@ -419,80 +500,98 @@ namespace {
 
 dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
                  const float* pos, const float* xform, int V, const int32_t* tri, int T, const int32_t* topo,
-                 float* out) {
+                 float* out, void* work) {
   dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
   if (st != DR_OK) return st;
   DR_REQUIRE(ctx, out, "antialias: out required");
+  DR_REQUIRE(ctx, !work || aligned16(work), "antialias: aa_work must be 16-byte aligned");
   const int64_t P = (int64_t)N * H * W;
   const float4* r4 = reinterpret_cast<const float4*>(rast);
+  float4* wb = reinterpret_cast<float4*>(work);
+  uint8_t* wc = work ? reinterpret_cast<uint8_t*>(work) + (size_t)P * 16 : nullptr;
   DR_TB(ctx);
-  if (xform)
-    k_aa_fwd<true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, xform, V, tri, T, topo,
-                                                                out, ctx->d_err);
-  else
-    k_aa_fwd<false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, nullptr, V, tri, T,
-                                                                 topo, out, ctx->d_err);
+#define DR_AF(XFV, WV, XP)                                                                                   \
+  k_aa_fwd<XFV, WV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T, topo, \
+                                                               out, wb, wc, ctx->d_err)
+  if (xform) {
+    if (work) DR_AF(true, true, xform); else DR_AF(true, false, xform);
+  } else {
+    if (work) DR_AF(false, true, nullptr); else DR_AF(false, false, nullptr);
+  }
+#undef DR_AF
   DR_LAUNCHED(ctx, "aa_fwd");
   return DR_OK;
 }
 
 dr_status aa_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
                  const float* pos, const float* xform, int V, const int32_t* tri, int T, const int32_t* topo,
-                 const float* d_out, float* d_color, float* d_pos) {
+                 const float* d_out, float* d_color, float* d_pos, const void* work) {
   dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
   if (st != DR_OK) return st;
   DR_REQUIRE(ctx, d_out && d_color && d_pos, "antialias_bwd: d_out, d_color, d_pos required");
+  DR_REQUIRE(ctx, !work || aligned16(work), "antialias_bwd: aa_work must be 16-byte aligned");
   const size_t npos = (size_t)(xform ? 1 : N) * V * 4;
   DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream), "antialias_bwd memset");
   const int64_t P = (int64_t)N * H * W;
   const float4* r4 = reinterpret_cast<const float4*>(rast);
+  const float4* wb = reinterpret_cast<const float4*>(work);
+  const uint8_t* wc = work ? reinterpret_cast<const uint8_t*>(work) + (size_t)P * 16 : nullptr;
+  if (xform) DR_REQUIRE(ctx, aligned16(d_pos), "antialias_xf_bwd: d_verts must be 16-byte aligned");
   DR_TB(ctx);
+#define DR_AB(VECV, XFV, WV, XP)                                                                             \
+  k_aa_bwd<VECV, XFV, WV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T, \
+                                                                     topo, d_out, d_color, d_pos, wb, wc,        \
+                                                                     ctx->d_err)
   if (xform) {
-    DR_REQUIRE(ctx, aligned16(d_pos), "antialias_xf_bwd: d_verts must be 16-byte aligned");
-    k_aa_bwd<true, true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, xform, V, tri, T,
-                                                                     topo, d_out, d_color, d_pos, ctx->d_err);
+    if (work) DR_AB(true, true, true, xform); else DR_AB(true, true, false, xform);
   } else if (aligned16(d_pos)) {
-    k_aa_bwd<true, false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, nullptr, V, tri,
-                                                                      T, topo, d_out, d_color, d_pos, ctx->d_err);
+    if (work) DR_AB(true, false, true, nullptr); else DR_AB(true, false, false, nullptr);
   } else {
-    k_aa_bwd<false, false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, nullptr, V, tri,
-                                                                       T, topo, d_out, d_color, d_pos, ctx->d_err);
+    if (work) DR_AB(false, false, true, nullptr); else DR_AB(false, false, false, nullptr);
   }
+#undef DR_AB
   DR_LAUNCHED(ctx, "aa_bwd");
   return DR_OK;
 }
 
 }  // namespace
 
+extern "C" size_t dr_antialias_work_bytes(int N, int H, int W) {
+  if (N <= 0 || H <= 0 || W <= 0) return 0;
+  return aa_work_bytes((int64_t)N * H * W);
+}
+
 extern "C" dr_status dr_antialias_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
                                       const float* rast, const float* pos, int V, const int32_t* tri, int T,
-                                      const int32_t* topo, float* out) {
+                                      const int32_t* topo, float* out, void* aa_work) {
   DR_ENTER(ctx);
-  return aa_fwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, out);
+  return aa_fwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, out, aa_work);
 }
 
 extern "C" dr_status dr_antialias_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
                                       const float* rast, const float* pos, int V, const int32_t* tri, int T,
-                                      const int32_t* topo, const float* d_out, float* d_color, float* d_pos) {
+                                      const int32_t* topo, const float* d_out, float* d_color, float* d_pos,
+                                      const void* aa_work) {
   DR_ENTER(ctx);
-  return aa_bwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, d_out, d_color, d_pos);
+  return aa_bwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, d_out, d_color, d_pos, aa_work);
 }
 
 extern "C" dr_status dr_antialias_xf_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
                                          const float* rast, const float* verts, int V, const float* xform,
-                                         const int32_t* tri, int T, const int32_t* topo, float* out) {
+                                         const int32_t* tri, int T, const int32_t* topo, float* out,
+                                         void* aa_work) {
   DR_ENTER(ctx);
   DR_REQUIRE(ctx, xform && aligned16(xform), "antialias_xf: xform [N,4,4] must be given and 16-byte aligned");
-  return aa_fwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, out);
+  return aa_fwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, out, aa_work);
 }
 
 extern "C" dr_status dr_antialias_xf_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
                                          const float* rast, const float* verts, int V, const float* xform,
                                          const int32_t* tri, int T, const int32_t* topo, const float* d_out,
-                                         float* d_color, float* d_verts) {
+                                         float* d_color, float* d_verts, const void* aa_work) {
   DR_ENTER(ctx);
   DR_REQUIRE(ctx, xform && aligned16(xform), "antialias_xf_bwd: xform [N,4,4] must be given and 16-byte aligned");
-  return aa_bwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, d_out, d_color, d_verts);
+  return aa_bwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, d_out, d_color, d_verts, aa_work);
 }
 
 // ---------------------------------------------------------------------------

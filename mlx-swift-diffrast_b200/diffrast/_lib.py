@@ -51,10 +51,11 @@ SIGNATURES = {
     "dr_texture_bwd": (I, [P, I, I, P, I, I, I, I, P, I, P, P, F, P, I, I, I, P, P, P, P, P]),
     "dr_antialias_construct_topology_hash": (I, [P, P, I, P]),
     "dr_antialias_construct_topology_hash_static": (I, [P, I, P, P]),
-    "dr_antialias_fwd": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P]),
-    "dr_antialias_bwd": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P, P, P]),
-    "dr_antialias_xf_fwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P]),
-    "dr_antialias_xf_bwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P, P]),
+    "dr_antialias_fwd": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P, P]),
+    "dr_antialias_bwd": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P, P, P, P]),
+    "dr_antialias_work_bytes": (ctypes.c_size_t, [I, I, I]),
+    "dr_antialias_xf_fwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P]),
+    "dr_antialias_xf_bwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P, P, P]),
     "dr_mse_fwd_bwd": (I, [P, P, P, I64, F, P, P, I]),
 }
 

@@ -501,18 +501,23 @@ class _Antialias(torch.autograd.Function):
         V, T = (pos_c.shape[0] if xf is not None else pos_c.shape[1]), tri.shape[0]
         out = torch.empty_like(color_c)
         c = _ctx(color_c)
+        # The forward records each pixel's silhouettes for the VJP (17 B/px)
+        # when a gradient will be asked for; the VJP then skips the search.
+        work = None
+        if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
+            work = torch.empty(L.lib().dr_antialias_work_bytes(N, H, W), dtype=torch.uint8, device=color_c.device)
         if xf is not None:
             L.check(L.lib().dr_antialias_xf_fwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(xf),
-                                                _ptr(tri), T, _ptr(topo), _ptr(out)), c, "antialias_xf")
+                                                _ptr(tri), T, _ptr(topo), _ptr(out), _ptr(work)), c, "antialias_xf")
         else:
             L.check(L.lib().dr_antialias_fwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(tri),
-                                             T, _ptr(topo), _ptr(out)), c, "antialias")
-        ctx.save_for_backward(color_c, pos_c, xf, rast_c, tri, topo)
+                                             T, _ptr(topo), _ptr(out), _ptr(work)), c, "antialias")
+        ctx.save_for_backward(color_c, pos_c, xf, rast_c, tri, topo, work)
         return out
 
     @staticmethod
     def backward(ctx, d_out):
-        color_c, pos_c, xf, rast_c, tri, topo = ctx.saved_tensors
+        color_c, pos_c, xf, rast_c, tri, topo, work = ctx.saved_tensors
         N, H, W, C = color_c.shape
         V, T = (pos_c.shape[0] if xf is not None else pos_c.shape[1]), tri.shape[0]
         d_out = d_out.contiguous().float()
@@ -521,11 +526,11 @@ class _Antialias(torch.autograd.Function):
         c = _ctx(color_c)
         if xf is not None:
             L.check(L.lib().dr_antialias_xf_bwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(xf),
-                                                _ptr(tri), T, _ptr(topo), _ptr(d_out), _ptr(d_color), _ptr(d_pos)),
-                    c, "antialias_xf_bwd")
+                                                _ptr(tri), T, _ptr(topo), _ptr(d_out), _ptr(d_color), _ptr(d_pos),
+                                                _ptr(work)), c, "antialias_xf_bwd")
         else:
             L.check(L.lib().dr_antialias_bwd(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V, _ptr(tri),
-                                             T, _ptr(topo), _ptr(d_out), _ptr(d_color), _ptr(d_pos)),
+                                             T, _ptr(topo), _ptr(d_out), _ptr(d_color), _ptr(d_pos), _ptr(work)),
                     c, "antialias_bwd")
         return d_color, d_pos, None, None, None, None
 

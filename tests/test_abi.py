@@ -40,7 +40,16 @@ def test_library_exports_every_declared_symbol():
 def test_binding_types_every_symbol():
     from diffrast import _lib
     assert set(_lib.SIGNATURES) == set(declared())
-    assert _lib.lib().dr_abi_version() == 1
+    assert _lib.lib().dr_abi_version() == 2
+
+
+def test_antialias_work_bytes():
+    # 16 B of betas + 1 B of edge codes per pixel, the code bytes rounded up to 16.
+    from diffrast import _lib
+    f = _lib.lib().dr_antialias_work_bytes
+    assert f(2, 3, 5) == 30 * 16 + 32
+    assert f(32, 1024, 1024) == 32 * 1024 * 1024 * 17
+    assert f(0, 4, 4) == 0 and f(1, -1, 4) == 0
 
 
 def test_mip_layout_matches_oracle():

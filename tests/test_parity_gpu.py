@@ -341,3 +341,69 @@ def test_layers_full_size_soup_two_views(cu):
     r1o, d1o = O.rasterize(pos, s["tri"], s["res"], peel=r0o)
     assert np.array_equal(layers[0][0].cpu().numpy(), r0o) and np.array_equal(layers[0][1].cpu().numpy(), d0o)
     assert np.array_equal(layers[1][0].cpu().numpy(), r1o) and np.array_equal(layers[1][1].cpu().numpy(), d1o)
+
+
+@pytest.mark.parametrize("xf", [False, True])
+def test_antialias_vjp_from_forward_record_equals_search(cu, soup, xf):
+    # The VJP with the forward's per-pixel record (aa_work) and the VJP that
+    # searches the silhouettes again give the same d_color bit for bit and the
+    # same d_pos up to float atomic order.
+    import ctypes
+
+    import torch
+
+    from diffrast import _lib as L
+    pos, tri = soup
+    N, H, W, C = pos.shape[0], 256, 224, 8
+    base, Ms = None, None
+    if xf:
+        import oracle
+        base, _ = scenes.triangle_soup(20000, 1000, 10, seed=21)
+        Ms = scenes.similarity_matrices(N, seed=22).astype(np.float32)
+        pos = oracle.xf_positions(base, Ms)
+    rast, _ = O.rasterize(pos, tri, (H, W), grad_db=False)
+    g = np.random.default_rng(23)
+    dev = torch.device("cuda", 0)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    color, d_out = t(g.normal(size=(N, H, W, C)).astype(np.float32)), t(g.normal(size=(N, H, W, C)).astype(np.float32))
+    r, tr = t(rast), t(tri)
+    topo = t(O.topology_hash(tri))
+    from diffrast import ops
+    lib = L.lib()
+    c = ops._ctx(color)
+    V = (base if xf else pos).shape[-2]
+    p = t(base) if xf else t(pos)
+    xfm = t(Ms) if xf else None
+    work = torch.empty(lib.dr_antialias_work_bytes(N, H, W), dtype=torch.uint8, device=dev)
+    outs = []
+    for w in (None, work):
+        out = torch.empty_like(color)
+        dc, dp = torch.empty_like(color), torch.empty_like(p)
+        P = lambda x: None if x is None else x.data_ptr()
+        if xf:
+            L.check(lib.dr_antialias_xf_fwd(c, P(color), N, H, W, C, P(r), P(p), V, P(xfm), P(tr), tri.shape[0],
+                                            P(topo), P(out), P(w)), c, "aa_xf_fwd")
+            L.check(lib.dr_antialias_xf_bwd(c, P(color), N, H, W, C, P(r), P(p), V, P(xfm), P(tr), tri.shape[0],
+                                            P(topo), P(d_out), P(dc), P(dp), P(w)), c, "aa_xf_bwd")
+        else:
+            L.check(lib.dr_antialias_fwd(c, P(color), N, H, W, C, P(r), P(p), V, P(tr), tri.shape[0], P(topo),
+                                         P(out), P(w)), c, "aa_fwd")
+            L.check(lib.dr_antialias_bwd(c, P(color), N, H, W, C, P(r), P(p), V, P(tr), tri.shape[0], P(topo),
+                                         P(d_out), P(dc), P(dp), P(w)), c, "aa_bwd")
+        torch.cuda.synchronize()
+        outs.append((out.cpu().numpy(), dc.cpu().numpy(), dp.cpu().numpy()))
+    (o0, c0, p0), (o1, c1, p1) = outs
+    assert np.array_equal(o0, o1) and np.array_equal(c0, c1)
+    assert rel_l2(p1, p0) < 1e-5
+    wb = work[: N * H * W * 16].view(torch.float32).view(N, H, W, 4).cpu().numpy()
+    assert (wb > 0).any() and (wb <= 0.5).all()
+    # and against the oracle's VJP
+    gb = O.antialias_bwd(color.cpu().numpy(), rast, pos, tri, d_out.cpu().numpy(), topo.cpu().numpy())
+    assert rel_l2(c1, gb[0]) < 1e-5
+    ref_p = oracle_vertex_grad(gb[1], Ms) if xf else gb[1]
+    assert rel_l2(p1, ref_p) < 1e-4
+
+
+def oracle_vertex_grad(d_pos, Ms):
+    import oracle
+    return oracle.xf_vertex_grad(d_pos, Ms)
