@@ -23,6 +23,8 @@
 // All coverage-critical arithmetic uses explicit round-to-nearest intrinsics
 // (never contracted into FMA), so tri_id, u, v and z match the CPU oracle bit for
 // bit.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace {
@@ -97,16 +99,13 @@ __device__ __forceinline__ bool finite3(float a, float b, float c) {
   return isfinite(a) && isfinite(b) && isfinite(c);
 }
 
-__global__ void k_raster_setup(const float* __restrict__ pos, const float* __restrict__ xform, int V,
-                               const int32_t* __restrict__ tri,
-                               int T, const int32_t* __restrict__ ranges, int N, int H, int W,
-                               int ntx, int nty, float4* __restrict__ rec,
-                               uint32_t* __restrict__ tile_count, unsigned* err) {
-  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (int64_t)N * T) return;
-  int t = (int)(idx % T);
-  int n = (int)(idx / T);
-  float4* out = rec + 3 * idx;
+// Setup of triangle t in view n: writes its record and returns its exact pixel
+// rectangle, or false (record zeroed) when it can cover no pixel.
+__device__ __forceinline__ bool setup_one(const float* __restrict__ pos, const float* __restrict__ xform, int V,
+                                          const int32_t* __restrict__ tri, int T,
+                                          const int32_t* __restrict__ ranges, int H, int W, int n, int t,
+                                          float4* __restrict__ out, int& x0, int& x1, int& y0, int& y1,
+                                          unsigned* err) {
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   bool ok = true;
   int64_t pos_n_base = 0;
@@ -139,7 +138,7 @@ __global__ void k_raster_setup(const float* __restrict__ pos, const float* __res
   }
   if (!ok) {
     out[0] = zero; out[1] = zero; out[2] = zero;
-    return;
+    return false;
   }
   float sx0 = FD(p0.x, p0.w), sy0 = FD(p0.y, p0.w), sz0 = FD(p0.z, p0.w);
   float sx1 = FD(p1.x, p1.w), sy1 = FD(p1.y, p1.w), sz1 = FD(p1.z, p1.w);
@@ -147,7 +146,7 @@ __global__ void k_raster_setup(const float* __restrict__ pos, const float* __res
   float area = FS(FM(FS(sx1, sx0), FS(sy2, sy0)), FM(FS(sx2, sx0), FS(sy1, sy0)));
   ok = finite3(sx0, sy0, sz0) && finite3(sx1, sy1, sz1) && finite3(sx2, sy2, sz2) &&
        isfinite(area) && area != 0.0f;
-  int x0 = 0, x1 = -1, y0 = 0, y1 = -1;
+  x0 = 0; x1 = -1; y0 = 0; y1 = -1;
   if (ok) {
     float minx = fminf(sx0, fminf(sx1, sx2)), maxx = fmaxf(sx0, fmaxf(sx1, sx2));
     float miny = fminf(sy0, fminf(sy1, sy2)), maxy = fmaxf(sy0, fmaxf(sy1, sy2));
@@ -157,12 +156,78 @@ __global__ void k_raster_setup(const float* __restrict__ pos, const float* __res
   }
   if (!ok) {
     out[0] = zero; out[1] = zero; out[2] = zero;
-    return;
+    return false;
   }
   out[0] = make_float4(sx0, sy0, sz0, sx1);
   out[1] = make_float4(sy1, sz1, sx2, sy2);
   out[2] = make_float4(sz2, area, __uint_as_float((unsigned)x0 | ((unsigned)x1 << 16)),
                        __uint_as_float((unsigned)y0 | ((unsigned)y1 << 16)));
+  return true;
+}
+
+// Binned setup: CTA (c, n) owns triangles [c*chunk, (c+1)*chunk) of view n and
+// counts their tiles in a shared-memory histogram of the view's tiles, then
+// writes the histogram to cnt[(n*ntiles + tile)*cpv + c].  The exclusive scan
+// of cnt (tile-major, chunk-minor) gives every (tile, chunk) its list segment,
+// so neither this kernel nor the scatter issues a global atomic.
+__global__ void __launch_bounds__(256)
+k_raster_setup_binned(const float* __restrict__ pos, const float* __restrict__ xform, int V,
+                      const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ ranges, int H, int W,
+                      int ntx, int nty, int chunk, int cpv, float4* __restrict__ rec,
+                      uint32_t* __restrict__ cnt, unsigned* err) {
+  extern __shared__ uint32_t s_hist[];
+  const int c = blockIdx.x, n = blockIdx.y;
+  const int ntiles = ntx * nty;
+  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) s_hist[i] = 0u;
+  __syncthreads();
+  const int t0 = c * chunk, t1 = min(T, t0 + chunk);
+  for (int t = t0 + (int)threadIdx.x; t < t1; t += blockDim.x) {
+    int x0, x1, y0, y1;
+    if (!setup_one(pos, xform, V, tri, T, ranges, H, W, n, t, rec + 3 * ((int64_t)n * T + t), x0, x1, y0, y1, err))
+      continue;
+    for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
+      for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) atomicAdd(&s_hist[ty * ntx + tx], 1u);
+  }
+  __syncthreads();
+  uint32_t* col = cnt + (int64_t)n * ntiles * cpv + c;
+  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) col[(int64_t)i * cpv] = s_hist[i];
+}
+
+// Binned scatter: the same CTA-to-chunk map as the setup; each (tile, chunk)
+// segment start comes from the scan, and slots within it from shared atomics.
+__global__ void __launch_bounds__(256)
+k_raster_scatter_binned(const float4* __restrict__ rec, int T, int ntx, int nty, int chunk, int cpv,
+                        const uint32_t* __restrict__ off, int32_t* __restrict__ list) {
+  extern __shared__ uint32_t s_base[];
+  const int c = blockIdx.x, n = blockIdx.y;
+  const int ntiles = ntx * nty;
+  const uint32_t* col = off + (int64_t)n * ntiles * cpv + c;
+  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) s_base[i] = __ldg(col + (int64_t)i * cpv);
+  __syncthreads();
+  const int t0 = c * chunk, t1 = min(T, t0 + chunk);
+  for (int t = t0 + (int)threadIdx.x; t < t1; t += blockDim.x) {
+    const float4 r2 = __ldg(rec + 3 * ((int64_t)n * T + t) + 2);
+    if (r2.y == 0.0f) continue;  // area == 0: invalid
+    const unsigned xs = __float_as_uint(r2.z), ys = __float_as_uint(r2.w);
+    const int x0 = (int)(xs & 0xffffu), x1 = (int)(xs >> 16), y0 = (int)(ys & 0xffffu), y1 = (int)(ys >> 16);
+    for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
+      for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) list[atomicAdd(&s_base[ty * ntx + tx], 1u)] = t;
+  }
+}
+
+// Unbinned setup (views with more tiles than a shared histogram holds): one
+// thread per (view, triangle), global atomics on the per-tile counts.
+__global__ void k_raster_setup(const float* __restrict__ pos, const float* __restrict__ xform, int V,
+                               const int32_t* __restrict__ tri,
+                               int T, const int32_t* __restrict__ ranges, int N, int H, int W,
+                               int ntx, int nty, float4* __restrict__ rec,
+                               uint32_t* __restrict__ tile_count, unsigned* err) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)N * T) return;
+  int t = (int)(idx % T);
+  int n = (int)(idx / T);
+  int x0, x1, y0, y1;
+  if (!setup_one(pos, xform, V, tri, T, ranges, H, W, n, t, rec + 3 * idx, x0, x1, y0, y1, err)) return;
   uint32_t* tc = tile_count + (int64_t)n * ntx * nty;
   for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
     for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) atomicAdd(tc + ty * ntx + tx, 1u);
@@ -275,7 +340,7 @@ constexpr int SSTRIDE = 5;  // float4 per staged candidate (80 B: conflict-free 
 template <int MODE, bool DB>
 __global__ void __launch_bounds__(TILE_PIX, 5)
 k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int nty,
-               const uint32_t* __restrict__ tile_off, const uint32_t* __restrict__ tile_count,
+               const uint32_t* __restrict__ tile_off, int off_stride,
                const int32_t* __restrict__ list, const float* __restrict__ peel,
                float4* __restrict__ rast, float4* __restrict__ rast_db,
                float4* __restrict__ rast1, float4* __restrict__ rast_db1, unsigned* err) {
@@ -310,7 +375,8 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   if (tid == 0) s_next = 0u;
   __syncthreads();
   const uint32_t gt = (uint32_t)blockIdx.x;
-  const uint32_t begin = __ldg(tile_off + gt), cnt = __ldg(tile_count + gt);
+  const uint32_t begin = __ldg(tile_off + (int64_t)gt * off_stride);
+  const uint32_t cnt = __ldg(tile_off + (int64_t)(gt + 1) * off_stride) - begin;
   const int64_t rec_view = (int64_t)n * T;
   const int warp = tid >> 5, lane = tid & 31;
   float4* st = s_stage[warp];
@@ -555,12 +621,16 @@ namespace {
 
 struct Prepared {
   const float4* rec;
-  const uint32_t* tile_off;
-  const uint32_t* tile_count;
+  const uint32_t* tile_off;  // tile gt's list is [tile_off[gt*off_stride], tile_off[(gt+1)*off_stride])
+  int off_stride;
   const int32_t* list;
   int ntx, nty;
   int64_t ntiles_all;
 };
+
+// Largest per-view tile count whose histogram (4 B per tile) the binned
+// setup / scatter keep in shared memory.
+constexpr int kMaxHistTiles = 40960;
 
 // Setup, tile counts, scan, one readback of the list length, scatter.
 dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int V, const int32_t* tri, int T,
@@ -572,34 +642,67 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
   DR_REQUIRE(ctx, T < (1 << 24), "rasterize: T must be < 2^24 (tri_id+1 is stored as float)");
   DR_REQUIRE(ctx, aligned16(pos), "rasterize: pos must be 16-byte aligned");
   const int ntx = (W + TILE - 1) / TILE, nty = (H + TILE - 1) / TILE;
-  const int64_t ntiles_all = (int64_t)N * ntx * nty;
+  const int ntiles = ntx * nty;
+  const int64_t ntiles_all = (int64_t)N * ntiles;
   const int64_t NT = (int64_t)N * T;
   DR_REQUIRE(ctx, ntiles_all < (1ll << 31), "rasterize: too many tiles");
 
-  float4* rec = (float4*)ws_get(ctx, WS_RASTER_REC, sizeof(float4) * 3 * (size_t)(NT > 0 ? NT : 1));
-  uint32_t* tc = (uint32_t*)ws_get(ctx, WS_TILE_COUNT, sizeof(uint32_t) * (size_t)(3 * ntiles_all + 4));
-  if (!rec || !tc) return DR_ENOMEM;
-  uint32_t* tile_count = tc;
-  uint32_t* tile_off = tc + ntiles_all;
-  uint32_t* tile_cur = tc + 2 * ntiles_all;
-  uint32_t* total = tc + 3 * ntiles_all;
-
-  DR_CUDA(ctx, cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * (size_t)ntiles_all, ctx->stream),
-          "rasterize memset");
-  if (NT > 0) {
-    DR_TB(ctx);
-    k_raster_setup<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(pos, xform, V, tri, T, ranges, N, H, W, ntx,
-                                                               nty, rec, tile_count, ctx->d_err);
-    DR_LAUNCHED(ctx, "raster_setup");
+  // Binned mode: cpv CTAs per view, each with a chunk of at least max(1024,
+  // ntiles) triangles (so its histogram flush is amortised), about 8 CTAs per
+  // SM in total.
+  const bool binned = ntiles <= kMaxHistTiles && T > 0 && N <= 65535;  // views on grid.y
+  int cpv = 1, chunk = T;
+  if (binned) {
+    const int64_t by_size = ((int64_t)T + std::max(1024, ntiles) - 1) / std::max(1024, ntiles);
+    const int64_t by_grid = ((int64_t)8 * ctx->num_sms + N - 1) / N;
+    cpv = (int)std::max<int64_t>(1, std::min<int64_t>(std::min(by_size, by_grid), 65535));
+    chunk = (int)(((int64_t)T + cpv - 1) / cpv);
   }
-  dr_status st = scan_u32(ctx, tile_count, tile_off, ntiles_all, total);
+  const int64_t ncnt = ntiles_all * cpv;
+  DR_REQUIRE(ctx, ncnt < (1ll << 31), "rasterize: too many tile segments");
+
+  float4* rec = (float4*)ws_get(ctx, WS_RASTER_REC, sizeof(float4) * 3 * (size_t)(NT > 0 ? NT : 1));
+  // cnt[ncnt] | off[ncnt + 1] | cur[ntiles_all] (unbinned only) | total
+  uint32_t* tc = (uint32_t*)ws_get(ctx, WS_TILE_COUNT, sizeof(uint32_t) * (size_t)(2 * ncnt + ntiles_all + 4));
+  if (!rec || !tc) return DR_ENOMEM;
+  uint32_t* cnt = tc;
+  uint32_t* off = tc + ncnt;
+  uint32_t* cur = off + ncnt + 1;
+  uint32_t* total = cur + ntiles_all;
+  const size_t hist_bytes = sizeof(uint32_t) * (size_t)ntiles;
+
+  if (binned) {
+    if (hist_bytes > 48 * 1024) {
+      DR_CUDA(ctx, cudaFuncSetAttribute(k_raster_setup_binned, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)hist_bytes), "rasterize smem");
+      DR_CUDA(ctx, cudaFuncSetAttribute(k_raster_scatter_binned, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)hist_bytes), "rasterize smem");
+    }
+    DR_TB(ctx);
+    k_raster_setup_binned<<<dim3(cpv, N), 256, hist_bytes, ctx->stream>>>(pos, xform, V, tri, T, ranges, H, W, ntx,
+                                                                         nty, chunk, cpv, rec, cnt, ctx->d_err);
+    DR_LAUNCHED(ctx, "raster_setup");
+  } else {
+    DR_CUDA(ctx, cudaMemsetAsync(cnt, 0, sizeof(uint32_t) * (size_t)ncnt, ctx->stream), "rasterize memset");
+    if (NT > 0) {
+      DR_TB(ctx);
+      k_raster_setup<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(pos, xform, V, tri, T, ranges, N, H, W, ntx,
+                                                                 nty, rec, cnt, ctx->d_err);
+      DR_LAUNCHED(ctx, "raster_setup");
+    }
+  }
+  dr_status st = scan_u32(ctx, cnt, off, ncnt, total);
   if (st != DR_OK) return st;
+  // off[ncnt] = total closes the last tile's range.
+  DR_CUDA(ctx, cudaMemcpyAsync(off + ncnt, total, sizeof(uint32_t), cudaMemcpyDeviceToDevice, ctx->stream),
+          "rasterize copy");
   // The list length is data dependent: read it back (one small sync) and size
   // the list buffer exactly, so no candidate is ever dropped.
   DR_CUDA(ctx, cudaMemcpyAsync(ctx->h_pinned, total, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream),
           "rasterize readback");
-  DR_CUDA(ctx, cudaMemcpyAsync(tile_cur, tile_off, sizeof(uint32_t) * (size_t)ntiles_all,
-                               cudaMemcpyDeviceToDevice, ctx->stream), "rasterize copy");
+  if (!binned)
+    DR_CUDA(ctx, cudaMemcpyAsync(cur, off, sizeof(uint32_t) * (size_t)ntiles_all, cudaMemcpyDeviceToDevice,
+                                 ctx->stream), "rasterize copy");
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return fail(ctx, DR_ECUDA, "rasterize: %s", cudaGetErrorString(e));
   const uint32_t n_pairs = (uint32_t)ctx->h_pinned[0];
@@ -607,12 +710,16 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
   if (!list) return DR_ENOMEM;
   if (NT > 0 && n_pairs > 0) {
     DR_TB(ctx);
-    k_raster_scatter<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(rec, N, T, ntx, nty, tile_cur, list);
+    if (binned)
+      k_raster_scatter_binned<<<dim3(cpv, N), 256, hist_bytes, ctx->stream>>>(rec, T, ntx, nty, chunk, cpv, off,
+                                                                              list);
+    else
+      k_raster_scatter<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(rec, N, T, ntx, nty, cur, list);
     DR_LAUNCHED(ctx, "raster_scatter");
   }
   pr.rec = rec;
-  pr.tile_off = tile_off;
-  pr.tile_count = tile_count;
+  pr.tile_off = off;
+  pr.off_stride = cpv;
   pr.list = list;
   pr.ntx = ntx;
   pr.nty = nty;
@@ -637,7 +744,7 @@ dr_status raster_layer(dr_ctx* ctx, const Prepared& pr, int T, int H, int W, con
   DR_TB(ctx);
 #define DR_RT(MODEV, DBV, PEELP)                                                                               \
   k_raster_tiles<MODEV, DBV><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,        \
-                                                                 pr.tile_count, pr.list, PEELP, r4, d4, r41, d41, \
+                                                                 pr.off_stride, pr.list, PEELP, r4, d4, r41, d41,  \
                                                                  ctx->d_err)
   if (rast1) {
     if (rast_db) DR_RT(2, true, nullptr); else DR_RT(2, false, nullptr);

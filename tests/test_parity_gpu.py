@@ -407,3 +407,13 @@ def test_antialias_vjp_from_forward_record_equals_search(cu, soup, xf):
 def oracle_vertex_grad(d_pos, Ms):
     import oracle
     return oracle.xf_vertex_grad(d_pos, Ms)
+
+
+def test_rasterize_unbinned_setup_at_large_resolution(cu, ico):
+    # 3328 x 3328 has 43,264 tiles per view, more than the binned setup's
+    # shared histogram holds, so tile lists are built by the per-triangle
+    # global-atomic setup; the result is the same bit for bit.
+    pos, tri = ico["pos"][:1], ico["tri"]
+    r_c, d_c = cu.rasterize(pos, tri, (3328, 3328))
+    r_o, d_o = O.rasterize(pos, tri, (3328, 3328))
+    assert np.array_equal(r_c, r_o) and np.array_equal(d_c, d_o)
