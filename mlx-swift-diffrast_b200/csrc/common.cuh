@@ -18,7 +18,6 @@ enum : unsigned {
   DR_DEVERR_VERTEX = 1u,    // a triangle names a vertex outside [0, V)
   DR_DEVERR_TRI_ID = 2u,    // a rast pixel names a triangle outside [0, T)
   DR_DEVERR_CAPACITY = 4u,  // a fixed-capacity buffer would have overflowed
-  DR_DEVERR_RETRY = 8u,     // a compare-and-swap loop hit its iteration bound
 };
 
 // Workspace slots: each is an independent grow-only device buffer.
@@ -154,10 +153,12 @@ __device__ __forceinline__ float4 mat4_apply_t(const Mat4& M, float4 g) {
 
 // Warp-level segmented suffix sum over runs of equal keys: after the call the
 // first lane of each run holds the run's total.  seg_end is one past the
-// caller's run.  All 32 lanes must call it.
-__device__ __forceinline__ float warp_seg_sum(float v, int lane, int seg_end) {
+// caller's run; span (warp-uniform) bounds the longest run in the warp, so
+// only ceil(log2(span)) shuffle steps run.  All 32 lanes must call it.
+__device__ __forceinline__ float warp_seg_sum(float v, int lane, int seg_end, int span = 32) {
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
+    if (o >= span) break;
     const float y = __shfl_down_sync(0xffffffffu, v, o);
     if (lane + o < seg_end) v += y;
   }
@@ -172,4 +173,10 @@ __device__ __forceinline__ int warp_runs(long long key, int lane, bool& head) {
   const unsigned after = lane == 31 ? 0u : (heads >> (lane + 1));
   head = (heads >> lane) & 1u;
   return after ? lane + __ffs(after) : 32;
+}
+
+// Length of the longest run in the warp (warp-uniform), the span bound of
+// warp_seg_sum.
+__device__ __forceinline__ int warp_max_run(int lane, int seg_end, bool head) {
+  return (int)__reduce_max_sync(0xffffffffu, head ? (unsigned)(seg_end - lane) : 0u);
 }

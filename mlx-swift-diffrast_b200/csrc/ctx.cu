@@ -285,11 +285,10 @@ dr_status dr_ctx_sync(dr_ctx* ctx) {
   if (bits) {
     cudaMemsetAsync(ctx->d_err, 0, sizeof(unsigned), ctx->stream);
     cudaStreamSynchronize(ctx->stream);
-    return fail(ctx, DR_EDEVICE, "device-side input error bits 0x%x (%s%s%s%s)", bits,
+    return fail(ctx, DR_EDEVICE, "device-side input error bits 0x%x (%s%s%s)", bits,
                 (bits & DR_DEVERR_VERTEX) ? "vertex index out of range; " : "",
                 (bits & DR_DEVERR_TRI_ID) ? "rast tri_id out of range; " : "",
-                (bits & DR_DEVERR_CAPACITY) ? "capacity exceeded; " : "",
-                (bits & DR_DEVERR_RETRY) ? "retry bound reached; " : "");
+                (bits & DR_DEVERR_CAPACITY) ? "capacity exceeded; " : "");
   }
   return DR_OK;
 }

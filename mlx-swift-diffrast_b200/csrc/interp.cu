@@ -139,6 +139,7 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
   const long long key = hit ? ((attr_shared ? 0ll : (long long)n * T) + t) : -1ll - (long long)lane;
   bool head;
   const int seg_end = warp_runs(key, lane, head);
+  const int span = warp_max_run(lane, seg_end, head);
 
   const float u = r.x, v = r.y;
   const float bw = 1.0f - u - v;
@@ -204,9 +205,9 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      c0[j] = warp_seg_sum(c0[j], lane, seg_end);
-      c1[j] = warp_seg_sum(c1[j], lane, seg_end);
-      c2[j] = warp_seg_sum(c2[j], lane, seg_end);
+      c0[j] = warp_seg_sum(c0[j], lane, seg_end, span);
+      c1[j] = warp_seg_sum(c1[j], lane, seg_end, span);
+      c2[j] = warp_seg_sum(c2[j], lane, seg_end, span);
     }
     if (hit && head) {
       if (VEC4) {

@@ -261,38 +261,26 @@ __device__ __forceinline__ unsigned long long pack_key(float z, int t) {
   return ((unsigned long long)u << 32) | (unsigned)t;
 }
 
-// Two depth layers in one candidate pass.  Per pixel the pair (k0, k1) holds
-// k0 = the minimum key of all fragments seen and k1 = the minimum key among
-// those whose z is strictly greater than z(k0) — exactly what a second pass
-// peeling at layer 0's depth selects (Rasterize.swift:465-470: z <= peel_z is
-// rejected).  A fragment f updates the pair as
-//   z_f <  z(k0): (k0, k1) <- (f, k0)        every earlier fragment lies behind f
-//   z_f == z(k0): (k0, k1) <- (min(k0, f), k1)
-//   z_f >  z(k0): (k0, k1) <- (k0, min(k1, f))
-// through a 128-bit compare-and-swap.  Both halves only ever decrease and
-// k0 <= k1, so f can change nothing once key_f >= k1: a 64-bit read of k1
-// filters almost every fragment before the CAS.
-struct __align__(16) KeyPair {
-  unsigned long long k0, k1;
-};
-
-__device__ __forceinline__ void fold_pair(KeyPair* slot, unsigned long long key, unsigned* err) {
-  KeyPair cur;
-  cur.k0 = slot->k0;  // a possibly stale start; only CAS results are trusted
-  cur.k1 = slot->k1;
-  // Every failed CAS means another lane lowered the pair, which can happen at
-  // most a few times per fragment in flight; the bound only guards the loop.
-  for (int it = 0; it < (1 << 16); ++it) {
-    const unsigned zf = (unsigned)(key >> 32), z0 = (unsigned)(cur.k0 >> 32);
-    KeyPair nw;
-    if (zf < z0) { nw.k0 = key; nw.k1 = cur.k0; }
-    else if (zf == z0) { nw.k0 = key < cur.k0 ? key : cur.k0; nw.k1 = cur.k1; }
-    else { nw.k0 = cur.k0; nw.k1 = key < cur.k1 ? key : cur.k1; }
-    const KeyPair prev = atomicCAS_block(slot, cur, nw);
-    if (prev.k0 == cur.k0 && prev.k1 == cur.k1) return;
-    cur = prev;
-  }
-  dr_flag(err, DR_DEVERR_RETRY);
+// Two depth layers in one candidate pass.  Per pixel, k0 = the minimum key of
+// all fragments and k1 = the minimum key among those whose z is strictly
+// greater than z(k0) — exactly what a second pass peeling at layer 0's depth
+// selects (Rasterize.swift:465-470: z <= peel_z is rejected).  Both are
+// maintained with 64-bit atomicMin only: a fragment f exchanges with k0
+// (old = atomicMin(k0, f)); of f and old, the larger key lost, and it is
+// offered to k1 when its z is strictly greater than the winner's.
+//   Every offered key is eligible (its z exceeds a k0 that can only fall).
+//   The smallest eligible key m is offered: if m lost its own exchange, the
+//   winner has a smaller key, hence (m being the smallest eligible) a smaller
+//   z, so m was offered; if m won, a later fragment with z <= z(k0 final) <
+//   z(m) displaced it and offered it.  A loser whose z ties the winner's is
+//   dropped safely: the winner has the same z and a smaller key.
+// Since k1 > k0 always, a fragment with key >= k1 changes neither: one 64-bit
+// read of k1 filters almost every fragment.
+__device__ __forceinline__ void fold_two(unsigned long long* k0, unsigned long long* k1,
+                                         unsigned long long key) {
+  const unsigned long long old = atomicMin(k0, key);
+  const unsigned long long win = key < old ? key : old, lose = key < old ? old : key;
+  if (lose != ~0ull && (lose >> 32) > (win >> 32)) atomicMin(k1, lose);
 }
 
 // Recompute the winner's (u, v, z) and rast_db bit-identically from its record
@@ -328,28 +316,32 @@ __device__ __forceinline__ void write_pixel(const float4* __restrict__ rec, int6
   }
 }
 
-// Per-tile fine raster.  Each warp takes 32 candidates at a time, stages their
-// records in shared memory, and flattens their (candidate, pixel) work items
-// (pixels of the candidate's rectangle inside the tile) with a warp prefix
-// sum, so all 32 lanes test one pixel each per round regardless of how the
-// rectangle sizes vary (1 to 256 pixels).
+// Per-tile fine raster.  The CTA stages up to 256 candidates at a time (one per
+// thread) in shared memory and block-scans their work-item counts (the pixels
+// of each candidate's rectangle inside the tile).  Every thread then takes an
+// equal contiguous range of the batch's items, finds the candidate holding its
+// first item by binary search, and walks (row, col) of that rectangle
+// incrementally, reloading a staged record only when its range crosses into
+// the next candidate.  Work is balanced to within one item per thread, and
+// the per-item cost is the reference's pixel test plus a counter step.
 // MODE: 0 = one layer, 1 = one layer peeled at `peel`, 2 = layers 0 and 1 at once.
 constexpr int WARPS = TILE_PIX / 32;
-constexpr int SSTRIDE = 5;  // float4 per staged candidate (80 B: conflict-free 128-bit phases)
+constexpr int SSTRIDE = 5;  // float4 per staged candidate (80 B)
 
 template <int MODE, bool DB>
-__global__ void __launch_bounds__(TILE_PIX, 5)
+__global__ void __launch_bounds__(TILE_PIX, 4)
 k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int nty,
                const uint32_t* __restrict__ tile_off, int off_stride,
                const int32_t* __restrict__ list, const float* __restrict__ peel,
                float4* __restrict__ rast, float4* __restrict__ rast_db,
                float4* __restrict__ rast1, float4* __restrict__ rast_db1, unsigned* err) {
   constexpr bool PEEL = MODE == 1, TWO = MODE == 2;
-  __shared__ KeyPair s_key[TILE_PIX];  // k1 unused unless TWO
+  __shared__ unsigned long long s_k0[TILE_PIX], s_k1[TWO ? TILE_PIX : 1];
   __shared__ float s_peel[PEEL ? TILE_PIX : 1];
   __shared__ float s_ndcx[TILE], s_ndcy[TILE];
-  __shared__ float4 s_stage[WARPS][32 * SSTRIDE];
-  __shared__ unsigned s_next;
+  __shared__ float4 s_stage[TILE_PIX * SSTRIDE];
+  __shared__ int s_excl[TILE_PIX + 1];
+  __shared__ int s_wsum[WARPS];
 
   const int ntiles = ntx * nty;
   const int n = blockIdx.x / ntiles;
@@ -360,8 +352,8 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   const bool inside_img = (px < W) && (py < H);
   const int64_t pix = ((int64_t)n * H + py) * W + px;
 
-  s_key[tid].k0 = ~0ull;
-  s_key[tid].k1 = ~0ull;
+  s_k0[tid] = ~0ull;
+  if (TWO) s_k1[tid] = ~0ull;
   if (PEEL) {
     float pz = -1e30f;
     if (inside_img) {
@@ -372,22 +364,45 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   }
   if (tid < TILE) s_ndcx[tid] = ndc_x_of(tx0 + tid, W);
   else if (tid < 2 * TILE) s_ndcy[tid - TILE] = ndc_y_of(ty0 + tid - TILE, H);
-  if (tid == 0) s_next = 0u;
-  __syncthreads();
+
   const uint32_t gt = (uint32_t)blockIdx.x;
   const uint32_t begin = __ldg(tile_off + (int64_t)gt * off_stride);
   const uint32_t cnt = __ldg(tile_off + (int64_t)(gt + 1) * off_stride) - begin;
   const int64_t rec_view = (int64_t)n * T;
   const int warp = tid >> 5, lane = tid & 31;
-  float4* st = s_stage[warp];
-  const unsigned below = (1u << lane) - 1u;  // lanes 0 .. lane-1
-  for (;;) {
-    // Batches of 32 candidates are handed out dynamically, so warps finish together.
-    unsigned b = 0;
-    if (lane == 0) b = atomicAdd(&s_next, 1u);
-    const uint32_t base = __shfl_sync(0xffffffffu, b, 0) * 32u;
-    if (base >= cnt) break;
-    const uint32_t i = base + lane;
+
+  // One pixel test (Rasterize.swift:426-470) of the staged candidate: true
+  // when the fragment may lower the pixel's key(s), with its key and pixel.
+  // f0 = (sx0, sy0, sz0, sx1), f1 = (sy1, sz1, sx2, sy2), f2 = (sz2, area, 1/area, t)
+  auto test = [&](const float4& f0, const float4& f1, const float4& f2, int lx, int ly,
+                  unsigned long long& key, int& p) -> bool {
+    const float x = s_ndcx[lx], y = s_ndcy[ly];
+    const float dx0 = FS(f0.x, x), dx1 = FS(f0.w, x), dx2 = FS(f1.z, x);
+    const float dy0 = FS(f0.y, y), dy1 = FS(f1.x, y), dy2 = FS(f1.w, y);
+    const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));
+    const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
+    const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
+    const float area = f2.y;
+    if (FM(e0, area) < 0.0f || FM(e1, area) < 0.0f || FM(e2, area) < 0.0f) return false;
+    const float bw = FM(e0, f2.z), u = FM(e1, f2.z), v = FM(e2, f2.z);
+    const float z = FA(FA(FM(bw, f0.z), FM(u, f1.y)), FM(v, f2.x));
+    // NaN never wins in the reference (its strict z < best_z is false).
+    if (!(z >= -1.0f && z <= 1.0f)) return false;
+    p = ly * TILE + lx;
+    if (PEEL && z <= s_peel[p]) return false;
+    key = pack_key(z, __float_as_int(f2.w));
+    return TWO ? key < s_k1[p] : key < s_k0[p];
+  };
+  auto fold = [&](unsigned long long key, int p) {
+    if (TWO) {
+      if (key < s_k1[p]) fold_two(&s_k0[p], &s_k1[p], key);
+    } else if (key < s_k0[p]) {
+      atomicMin(&s_k0[p], key);
+    }
+  };
+  for (uint32_t base = 0; base < cnt; base += TILE_PIX) {
+    __syncthreads();  // the previous batch's readers are done with the stage
+    const uint32_t i = base + tid;
     int n_items = 0;
     if (i < cnt) {
       const int t = __ldg(list + begin + i);
@@ -400,71 +415,73 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
       // A listed candidate's rectangle always meets its tile (it was binned by it).
       const int wc = max(cx1 - cx0 + 1, 1), hc = max(cy1 - cy0 + 1, 1);
       n_items = wc * hc;
-      const int magic = (65536 + wc - 1) / wc;  // (k * magic) >> 16 == k / wc for k < 256
-      const int pk = (cx0 - tx0) | ((cy0 - ty0) << 4) | ((wc - 1) << 8) | (magic << 12);
-      st[lane * SSTRIDE + 0] = a;
-      st[lane * SSTRIDE + 1] = bb;
-      st[lane * SSTRIDE + 2] = make_float4(c.x, c.y, FD(1.0f, c.y), __int_as_float(t));
-      st[lane * SSTRIDE + 3] = make_float4(__int_as_float(pk), 0.f, 0.f, 0.f);
+      const int pk = (cx0 - tx0) | ((cy0 - ty0) << 4) | (wc << 8) | (hc << 16);
+      s_stage[tid * SSTRIDE + 0] = a;
+      s_stage[tid * SSTRIDE + 1] = bb;
+      s_stage[tid * SSTRIDE + 2] = make_float4(c.x, c.y, FD(1.0f, c.y), __int_as_float(t));
+      s_stage[tid * SSTRIDE + 3] = make_float4(__int_as_float(pk), 0.f, 0.f, 0.f);
     }
+    // Block exclusive scan of the item counts.
     int incl = n_items;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    const int excl = incl - n_items;
-    const int total = __shfl_sync(0xffffffffu, incl, 31);
-    __syncwarp();
-    // Round r covers items [32r, 32r + 32).  Every active candidate owns >= 1
-    // item, so lane L's candidate is the one covering item 32r (c0) plus the
-    // number of candidates that start at positions 1..L of the round.
-    int c0 = 0;
-    for (int r0 = 0; r0 < total; r0 += 32) {
-      const unsigned pos_bit = (n_items > 0 && excl >= r0 && excl < r0 + 32) ? (1u << (excl - r0)) : 0u;
-      const unsigned starts = __reduce_or_sync(0xffffffffu, pos_bit) & ~1u;
-      const int j = c0 + __popc(starts & (below | (1u << lane)));
-      const int j31 = c0 + __popc(starts);
-      const int end31 = __shfl_sync(0xffffffffu, incl, j31 & 31);
-      const int sj = __shfl_sync(0xffffffffu, excl, j & 31);
-      c0 = j31 + (end31 == r0 + 32 ? 1 : 0);
-      const int item = r0 + lane;
-      if (item >= total) continue;
-      const int k = item - sj;
-      const float4 f0 = st[j * SSTRIDE + 0], f1 = st[j * SSTRIDE + 1], f2 = st[j * SSTRIDE + 2];
-      const int pk = __float_as_int(st[j * SSTRIDE + 3].x);
-      const int wc = ((pk >> 8) & 15) + 1;
-      const int row = (k * (pk >> 12)) >> 16;
-      const int lx = (pk & 15) + (k - row * wc), ly = ((pk >> 4) & 15) + row;
-      const float x = s_ndcx[lx], y = s_ndcy[ly];
-      // f0 = (sx0, sy0, sz0, sx1), f1 = (sy1, sz1, sx2, sy2), f2 = (sz2, area, 1/area, t)
-      const float dx0 = FS(f0.x, x), dx1 = FS(f0.w, x), dx2 = FS(f1.z, x);
-      const float dy0 = FS(f0.y, y), dy1 = FS(f1.x, y), dy2 = FS(f1.w, y);
-      const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));
-      const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
-      const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
-      const float area = f2.y;
-      if (FM(e0, area) < 0.0f || FM(e1, area) < 0.0f || FM(e2, area) < 0.0f) continue;
-      const float bw = FM(e0, f2.z), u = FM(e1, f2.z), v = FM(e2, f2.z);
-      const float z = FA(FA(FM(bw, f0.z), FM(u, f1.y)), FM(v, f2.x));
-      // NaN never wins in the reference (its strict z < best_z is false).
-      if (!(z >= -1.0f && z <= 1.0f)) continue;
-      const int p = ly * TILE + lx;
-      if (PEEL && z <= s_peel[p]) continue;
-      const unsigned long long key = pack_key(z, __float_as_int(f2.w));
-      if (TWO) {
-        if (key < s_key[p].k1) fold_pair(&s_key[p], key, err);
-      } else if (key < s_key[p].k0) {
-        atomicMin(&s_key[p].k0, key);
+    if (lane == 31) s_wsum[warp] = incl;
+    __syncthreads();
+    int before = 0;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w)
+      if (w < warp) before += s_wsum[w];
+    s_excl[tid] = before + incl - n_items;
+    if (tid == TILE_PIX - 1) s_excl[TILE_PIX] = before + incl;
+    __syncthreads();
+    const int total = s_excl[TILE_PIX];
+    const int nc = (int)min(cnt - base, (uint32_t)TILE_PIX);
+    const int lo = (int)(((long long)tid * total) / TILE_PIX);
+    const int nmine = (int)(((long long)(tid + 1) * total) / TILE_PIX) - lo;
+    float4 f0 = make_float4(0.f, 0.f, 0.f, 0.f), f1 = f0, f2 = f0;
+    int j = 0, pk = 0, wc = 1, hc = 1, row = 0, col = 0;
+    if (nmine > 0) {
+      // The candidate holding item lo: the last j with s_excl[j] <= lo (every
+      // candidate owns >= 1 item, so s_excl is strictly increasing over [0, nc)).
+      int jh = nc - 1;
+      while (j < jh) {
+        const int mid = (j + jh + 1) >> 1;
+        if (s_excl[mid] <= lo) j = mid; else jh = mid - 1;
+      }
+      f0 = s_stage[j * SSTRIDE + 0]; f1 = s_stage[j * SSTRIDE + 1]; f2 = s_stage[j * SSTRIDE + 2];
+      pk = __float_as_int(s_stage[j * SSTRIDE + 3].x);
+      wc = (pk >> 8) & 31; hc = (pk >> 16) & 31;
+      const int k = lo - s_excl[j];
+      row = k / wc;
+      col = k - row * wc;
+    }
+    for (int r = 0; r < nmine; ++r) {
+      unsigned long long key = 0;
+      int p = 0;
+      if (test(f0, f1, f2, (pk & 15) + col, ((pk >> 4) & 15) + row, key, p)) fold(key, p);
+      if (++col == wc) {
+        col = 0;
+        if (++row == hc && r + 1 < nmine) {
+          row = 0;
+          ++j;
+          f0 = s_stage[j * SSTRIDE + 0];
+          f1 = s_stage[j * SSTRIDE + 1];
+          f2 = s_stage[j * SSTRIDE + 2];
+          pk = __float_as_int(s_stage[j * SSTRIDE + 3].x);
+          wc = (pk >> 8) & 31;
+          hc = (pk >> 16) & 31;
+        }
       }
     }
-    __syncwarp();
   }
   __syncthreads();
   if (!inside_img) return;
   const float x = s_ndcx[px - tx0], y = s_ndcy[py - ty0];
-  write_pixel<DB>(rec, rec_view, s_key[tid].k0, x, y, H, W, rast, rast_db, pix);
-  if (TWO) write_pixel<DB>(rec, rec_view, s_key[tid].k1, x, y, H, W, rast1, rast_db1, pix);
+  write_pixel<DB>(rec, rec_view, s_k0[tid], x, y, H, W, rast, rast_db, pix);
+  if (TWO) write_pixel<DB>(rec, rec_view, s_k1[tid], x, y, H, W, rast1, rast_db1, pix);
 }
 
 // d_pos: Rasterize.swift:637-812, one thread per pixel.  Pixels of a warp that
