@@ -323,7 +323,7 @@ __device__ __forceinline__ void add_pos(float* p, const Mat4& M, float x, float 
 // WORK: the forward's record supplies every beta and each active direction's
 // edge, so no silhouette search runs (neighbour betas are plain loads).
 template <bool VEC, bool XF, bool WORK>
-__global__ void k_aa_bwd(const float* __restrict__ color, int N, int H, int W, int C,
+__global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd(const float* __restrict__ color, int N, int H, int W, int C,
                          const float4* __restrict__ rast, const float* __restrict__ pos,
                          const float* __restrict__ xform, int V,
                          const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,

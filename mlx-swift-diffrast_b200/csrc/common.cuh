@@ -20,6 +20,17 @@ enum : unsigned {
   DR_DEVERR_CAPACITY = 4u,  // a fixed-capacity buffer would have overflowed
 };
 
+// Minimum resident 256-thread blocks per SM requested from the compiler for
+// two register-heavy per-pixel kernels (caps them at 65536 / (256 * n)
+// registers; measured faster than the uncapped build on cfg4).  The other
+// per-pixel kernels measured fastest with no bound.
+#ifndef DR_MINB_RASTER_BWD
+#define DR_MINB_RASTER_BWD 5
+#endif
+#ifndef DR_MINB_AA_BWD
+#define DR_MINB_AA_BWD 5
+#endif
+
 // Workspace slots: each is an independent grow-only device buffer.
 enum WsSlot {
   WS_RASTER_REC = 0,   // per-(view, triangle) setup records

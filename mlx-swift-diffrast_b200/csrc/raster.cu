@@ -490,7 +490,7 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
 // per-view transform (XF) the clip-space gradient g of vertex v is mapped to
 // the shared vertex buffer as M_n^T g.
 template <bool DB, bool VEC, bool XF>
-__global__ void k_raster_bwd(const float* __restrict__ pos, const float* __restrict__ xform, int V,
+__global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const float* __restrict__ pos, const float* __restrict__ xform, int V,
                              const int32_t* __restrict__ tri, int T, bool shared_pos, int N, int H, int W,
                              const float4* __restrict__ rast, const float4* __restrict__ d_rast,
                              const float4* __restrict__ d_rast_db, float* __restrict__ d_pos,
