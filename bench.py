@@ -137,10 +137,12 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
             add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A))
             # out_da never reaches the loss: the VJP runs without the DA terms.
             add("interp_bwd", 2 * V * A * 4 + T * 12 + P * (16 + 16 + 4 * A))
-            add("raster_bwd", 2 * V * 16 + T * 12 + P * 32 + P * 16)
+            # rast_db's cotangent is zero (out_da is off the loss path): not read.
+            add("raster_bwd", 2 * V * 16 + T * 12 + P * 32)
         add("aa_fwd", P * (8 * A + 16) + V * 16 + 2 * T * 12)
         add("aa_bwd", P * (12 * A + 16) + 2 * V * 16 + 2 * T * 12)
-        add("mse", 2 * P * 12 * A)
+        add("mse", 2 * P * 8 * A)  # loss: read pred and target
+        add("mse_bwd", 2 * P * 12 * A)  # read pred and target, write d_pred
     elif cfg == "cfg1":
         V, T, C = 3, 1, 3
         add("raster_setup", V * 16 + T * 12)
@@ -150,7 +152,8 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         add("raster_bwd", 2 * V * 16 + T * 12 + P * 32)
         add("aa_fwd", P * (8 * C + 16) + V * 16 + 2 * T * 12)
         add("aa_bwd", P * (12 * C + 16) + 2 * V * 16 + 2 * T * 12)
-        add("mse", P * 12 * C)
+        add("mse", P * 8 * C)  # loss: read pred and target
+        add("mse_bwd", P * 12 * C)  # read pred and target, write d_pred
     elif cfg == "cfg2":
         V, T = chain.pos.shape[1], chain.tri.shape[0]
         S = 512 * 512 * 3 * 4
@@ -163,7 +166,8 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         add("raster_bwd", 2 * n * V * 16 + T * 12 + P * 32)
         add("aa_fwd", P * (8 * 3 + 16) + n * V * 16 + 2 * T * 12)
         add("aa_bwd", P * (12 * 3 + 16) + 2 * n * V * 16 + 2 * T * 12)
-        add("mse", P * 12 * 3)
+        add("mse", P * 8 * 3)  # loss: read pred and target
+        add("mse_bwd", P * 12 * 3)  # read pred and target, write d_pred
     elif cfg == "cfg3":
         V, T = chain.pos.shape[1], chain.tri.shape[0]
         S0 = 2048 * 2048 * 4 * 4
@@ -177,7 +181,8 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         add("tex_mip_bwd", 2 * S_all + P * (16 + 32 + 4 + 16))
         add("mip_fold", S_all + S0)
         add("raster_bwd", 2 * n * V * 16 + T * 12 + P * 32 + P * 16)
-        add("mse", P * 12 * 4)
+        add("mse", P * 8 * 4)  # loss: read pred and target
+        add("mse_bwd", P * 12 * 4)  # read pred and target, write d_pred
     elif cfg == "cfg5":
         V, T = chain.verts.shape[0], chain.tri.shape[0]
         S = 6 * 1024 * 1024 * 3 * 4
@@ -191,7 +196,8 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         add("raster_bwd", 2 * n * V * 16 + micro * T * 12 + P * 32)
         add("aa_fwd", P * (8 * 3 + 16) + n * V * 16 + micro * 2 * T * 12)
         add("aa_bwd", P * (12 * 3 + 16) + 2 * n * V * 16 + micro * 2 * T * 12)
-        add("mse", P * 12 * 3)
+        add("mse", P * 8 * 3)  # loss: read pred and target
+        add("mse_bwd", P * 12 * 3)  # read pred and target, write d_pred
     return k
 
 

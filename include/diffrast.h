@@ -315,11 +315,17 @@ DR_API dr_status dr_antialias_xf_bwd(dr_ctx* ctx, const float* color, int N, int
 /* ---- loss helper (the MSE of the reference's examples) ------------------ */
 
 /* loss += scale * sum((pred - target)^2) into the device scalar `loss`
- * (zeroed by the callee when zero_loss != 0) and
+ * (zeroed by the callee when zero_loss != 0) and, when d_pred is not NULL,
  * d_pred = 2 * scale * (pred - target).  n elements. */
 DR_API dr_status dr_mse_fwd_bwd(dr_ctx* ctx, const float* pred, const float* target,
                          int64_t n, float scale, float* d_pred, float* loss,
                          int zero_loss);
+
+/* VJP of the loss alone: d_pred = (2 * scale * (pred - target)) * d_loss[0],
+ * with the cotangent d_loss read on the device (NULL means 1). */
+DR_API dr_status dr_mse_bwd(dr_ctx* ctx, const float* pred, const float* target,
+                     int64_t n, float scale, const float* d_loss, float* d_pred);
+
 
 #ifdef __cplusplus
 }

@@ -176,13 +176,17 @@ dr_status scan_u32(dr_ctx* ctx, const uint32_t* in, uint32_t* out, int64_t n, ui
 }
 
 // ---------------------------------------------------------------------------
-// MSE: loss += scale * sum((p - t)^2); d = 2 * scale * (p - t).
-
+// MSE: loss += scale * sum((p - t)^2) (when loss is given) and
+// d = (2 * scale * (p - t)) * g (when d is given; g = *d_loss, or 1).
+template <bool LOSS, bool GRAD>
 __global__ void k_mse(const float* __restrict__ p, const float* __restrict__ t, int64_t n,
-                      float scale, float* __restrict__ d, float* __restrict__ loss) {
+                      float scale, const float* __restrict__ d_loss, float* __restrict__ d,
+                      float* __restrict__ loss) {
   float acc = 0.0f;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t n4 = n / 4;
+  const float s2 = 2.0f * scale;
+  const float g = (GRAD && d_loss) ? __ldg(d_loss) : 1.0f;
   const bool vec = ((((uintptr_t)p) | ((uintptr_t)t) | ((uintptr_t)d)) & 15) == 0;
   int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (vec) {
@@ -190,22 +194,23 @@ __global__ void k_mse(const float* __restrict__ p, const float* __restrict__ t, 
       float4 a = ldg4(p + 4 * i), b = ldg4(t + 4 * i);
       float4 r;
       r.x = a.x - b.x; r.y = a.y - b.y; r.z = a.z - b.z; r.w = a.w - b.w;
-      acc += r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
-      float s2 = 2.0f * scale;
-      reinterpret_cast<float4*>(d)[i] = make_float4(s2 * r.x, s2 * r.y, s2 * r.z, s2 * r.w);
+      if (LOSS) acc += r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
+      if (GRAD)
+        reinterpret_cast<float4*>(d)[i] = make_float4((s2 * r.x) * g, (s2 * r.y) * g, (s2 * r.z) * g, (s2 * r.w) * g);
     }
     for (int64_t i = 4 * n4 + i0; i < n; i += stride) {
       float r = p[i] - t[i];
-      acc += r * r;
-      d[i] = 2.0f * scale * r;
+      if (LOSS) acc += r * r;
+      if (GRAD) d[i] = (s2 * r) * g;
     }
   } else {
     for (int64_t i = i0; i < n; i += stride) {
       float r = p[i] - t[i];
-      acc += r * r;
-      d[i] = 2.0f * scale * r;
+      if (LOSS) acc += r * r;
+      if (GRAD) d[i] = (s2 * r) * g;
     }
   }
+  if (!LOSS) return;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   __shared__ float ws[32];
@@ -342,13 +347,28 @@ size_t dr_ctx_workspace_bytes(const dr_ctx* ctx) {
 dr_status dr_mse_fwd_bwd(dr_ctx* ctx, const float* pred, const float* target, int64_t n,
                          float scale, float* d_pred, float* loss, int zero_loss) {
   DR_ENTER(ctx);
-  DR_REQUIRE(ctx, n >= 0 && pred && target && d_pred && loss, "mse: null pointer or n < 0");
+  DR_REQUIRE(ctx, n >= 0 && pred && target && loss, "mse: null pointer or n < 0");
   if (zero_loss) DR_CUDA(ctx, cudaMemsetAsync(loss, 0, sizeof(float), ctx->stream), "mse memset");
   if (n == 0) return DR_OK;
   int blocks = (int)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)ctx->num_sms * 8);
   DR_TB(ctx);
-  k_mse<<<blocks, 256, 0, ctx->stream>>>(pred, target, n, scale, d_pred, loss);
+  if (d_pred)
+    k_mse<true, true><<<blocks, 256, 0, ctx->stream>>>(pred, target, n, scale, nullptr, d_pred, loss);
+  else
+    k_mse<true, false><<<blocks, 256, 0, ctx->stream>>>(pred, target, n, scale, nullptr, nullptr, loss);
   DR_LAUNCHED(ctx, "mse");
+  return DR_OK;
+}
+
+dr_status dr_mse_bwd(dr_ctx* ctx, const float* pred, const float* target, int64_t n, float scale,
+                     const float* d_loss, float* d_pred) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, n >= 0 && pred && target && d_pred, "mse_bwd: null pointer or n < 0");
+  if (n == 0) return DR_OK;
+  int blocks = (int)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)ctx->num_sms * 8);
+  DR_TB(ctx);
+  k_mse<false, true><<<blocks, 256, 0, ctx->stream>>>(pred, target, n, scale, d_loss, d_pred, nullptr);
+  DR_LAUNCHED(ctx, "mse_bwd");
   return DR_OK;
 }
 

@@ -117,6 +117,7 @@ def _ctx(t: torch.Tensor):
 class _Rasterize(torch.autograd.Function):
     @staticmethod
     def forward(ctx, pos, tri, ranges, peel, H, W, grad_db):
+        ctx.set_materialize_grads(False)  # outputs off the loss path get None, not zeros
         posc = _f32(pos, "pos")
         if ranges is not None:
             N, V = ranges.shape[0], posc.shape[0]
@@ -138,6 +139,8 @@ class _Rasterize(torch.autograd.Function):
     def backward(ctx, d_rast, d_db):
         posc, tri, ranges, rast = ctx.saved_tensors
         N, V, T, H, W, grad_db = ctx.dims
+        if d_rast is None and (d_db is None or not grad_db):
+            return None, None, None, None, None, None, None
         if d_rast is None:
             d_rast = torch.zeros_like(rast)
         d_rast = d_rast.contiguous().float()
@@ -182,6 +185,7 @@ def rasterize(pos: torch.Tensor, tri: torch.Tensor, resolution, grad_db: bool = 
 class _RasterizeLayers(torch.autograd.Function):
     @staticmethod
     def forward(ctx, pos, xform, tri, ranges, H, W, grad_db, nl):
+        ctx.set_materialize_grads(False)  # outputs off the loss path get None, not zeros
         import ctypes
         posc = _f32(pos, "pos")
         xf = _f32(xform, "xform") if xform is not None else None
@@ -222,6 +226,12 @@ class _RasterizeLayers(torch.autograd.Function):
         N, V, T, H, W, grad_db, nl = ctx.dims
         d_r = [g.contiguous().float() if g is not None else None for g in grads[0::2]]
         d_d = [g.contiguous().float() if (grad_db and g is not None) else None for g in grads[1::2]]
+        # A layer whose rast_db reaches the loss but whose rast does not still
+        # needs a (zero) rast cotangent; a layer reaching it by neither is skipped.
+        d_r = [torch.zeros_like(rasts[l]) if (d_r[l] is None and d_d[l] is not None) else d_r[l]
+               for l in range(nl)]
+        if all(g is None for g in d_r):
+            return None, None, None, None, None, None, None, None
         d_pos = torch.empty_like(posc)
         rp = ctypes.cast((ctypes.c_void_p * nl)(*[r.data_ptr() for r in rasts]), ctypes.c_void_p)
         gp = ctypes.cast((ctypes.c_void_p * nl)(*[(g.data_ptr() if g is not None else None) for g in d_r]),
@@ -272,6 +282,7 @@ def rasterize_layers(pos: torch.Tensor, tri: torch.Tensor, resolution, num_layer
 class _Interpolate(torch.autograd.Function):
     @staticmethod
     def forward(ctx, attr, rast, rast_db, tri, idx, K):
+        ctx.set_materialize_grads(False)  # outputs off the loss path get None, not zeros
         attr_c = _f32(attr, "attr")
         a3 = attr_c if attr_c.dim() == 3 else attr_c.unsqueeze(0)
         rast_c = _f32(rast, "rast")
@@ -295,6 +306,8 @@ class _Interpolate(torch.autograd.Function):
         idx, K, attr_shape = ctx.meta
         N, H, W = rast_c.shape[:3]
         Na, V, A = a3.shape
+        if d_out is None and (d_out_da is None or K == 0):
+            return None, None, None, None, None, None
         d_out = torch.zeros((N, H, W, A), device=rast_c.device) if d_out is None else d_out.contiguous().float()
         if K > 0 and d_out_da is None:
             # out_da did not reach the loss: its cotangent is zero, so the DA
@@ -377,6 +390,7 @@ def _build_pyramid(tex_c: torch.Tensor, max_level: int):
 class _Texture(torch.autograd.Function):
     @staticmethod
     def forward(ctx, tex, uv, uv_da, bias_map, filt, bnd, bias):
+        ctx.set_materialize_grads(False)  # outputs off the loss path get None, not zeros
         tex_c = _f32(tex, "tex")
         uv_c = _f32(uv, "uv")
         da_c = _f32(uv_da, "uvDA") if uv_da is not None else None
@@ -404,6 +418,8 @@ class _Texture(torch.autograd.Function):
     def backward(ctx, d_out):
         tex_c, uv_c, da_c, map_c, pyr = ctx.saved_tensors
         filt, bnd, bias, (Nt, Ht, Wt, C, N, Hi, Wi), map_shape = ctx.meta
+        if d_out is None:
+            return None, None, None, None, None, None, None
         d_out = d_out.contiguous().float()
         d_tex = torch.empty_like(tex_c)
         d_uv = torch.empty_like(uv_c)
@@ -493,6 +509,7 @@ def antialias_construct_topology_hash(tri: torch.Tensor) -> torch.Tensor:
 class _Antialias(torch.autograd.Function):
     @staticmethod
     def forward(ctx, color, pos, xform, rast, tri, topo):
+        ctx.set_materialize_grads(False)  # outputs off the loss path get None, not zeros
         color_c = _f32(color, "color")
         pos_c = _f32(pos, "pos")
         xf = _f32(xform, "xform") if xform is not None else None
@@ -518,6 +535,8 @@ class _Antialias(torch.autograd.Function):
     @staticmethod
     def backward(ctx, d_out):
         color_c, pos_c, xf, rast_c, tri, topo, work = ctx.saved_tensors
+        if d_out is None:
+            return None, None, None, None, None, None
         N, H, W, C = color_c.shape
         V, T = (pos_c.shape[0] if xf is not None else pos_c.shape[1]), tri.shape[0]
         d_out = d_out.contiguous().float()
@@ -568,18 +587,25 @@ class _MSE(torch.autograd.Function):
         p = _f32(pred, "pred")
         t = _f32(target, "target")
         n = p.numel()
-        d = torch.empty_like(p)
         loss = torch.empty((), device=p.device, dtype=torch.float32)
         c = _ctx(p)
-        L.check(L.lib().dr_mse_fwd_bwd(c, _ptr(p), _ptr(t), n, 1.0 / max(n, 1), _ptr(d), _ptr(loss), 1),
-                c, "mse")
-        ctx.save_for_backward(d)
+        # Loss only; the gradient is formed in backward, scaled there by the
+        # incoming cotangent read on the device (no extra pass over d_pred).
+        L.check(L.lib().dr_mse_fwd_bwd(c, _ptr(p), _ptr(t), n, 1.0 / max(n, 1), None, _ptr(loss), 1), c, "mse")
+        ctx.save_for_backward(p, t)
         return loss
 
     @staticmethod
     def backward(ctx, g):
-        (d,) = ctx.saved_tensors
-        return d * g, None
+        p, t = ctx.saved_tensors
+        if g is None:
+            return None, None
+        g = g.contiguous().float()
+        d = torch.empty_like(p)
+        c = _ctx(p)
+        L.check(L.lib().dr_mse_bwd(c, _ptr(p), _ptr(t), p.numel(), 1.0 / max(p.numel(), 1), _ptr(g), _ptr(d)),
+                c, "mse_bwd")
+        return d, None
 
 
 def mse_loss(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
