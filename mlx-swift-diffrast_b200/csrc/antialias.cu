@@ -17,6 +17,7 @@
 //   pixel adds its own g*(1 - sum beta) and the beta*g its four neighbours
 //   would have scattered toward it — so it needs no atomics and is
 //   deterministic; only d_pos uses (float) atomics.
+#include <climits>
 #include <mutex>
 
 #include "common.cuh"
@@ -220,6 +221,37 @@ __device__ SilDir sil_dir(const float4* __restrict__ rast, const float* __restri
   return s;
 }
 
+// Directions of pixel (pn, ph, pw) that can hold a silhouette: exactly the
+// pairs sil_dir does not reject before its edge search (neighbour inside the
+// image, different ids, not both empty, and — both covered — the neighbour
+// listed in tri_p's topology row).  All neighbour ids and the topology row
+// are loaded up front, independently, so the common case (no candidate) costs
+// one round of loads instead of four dependent chains.
+__device__ __forceinline__ unsigned sil_candidates(const float4* __restrict__ rast,
+                                                   const int32_t* __restrict__ topo, int H, int W, int T,
+                                                   int pn, int ph, int pw, int tri_p, unsigned* err) {
+  int tn[4];
+#pragma unroll
+  for (int d = 0; d < 4; ++d) {
+    const int nh = ph + (d == 1 ? 1 : (d == 3 ? -1 : 0)), nw = pw + (d == 0 ? 1 : (d == 2 ? -1 : 0));
+    tn[d] = (nh < 0 || nh >= H || nw < 0 || nw >= W) ? INT_MIN
+                                                     : rast_tri(rast, ((int64_t)pn * H + nh) * W + nw, T, err);
+  }
+  int n0 = INT_MIN, n1 = INT_MIN, n2 = INT_MIN;
+  if (tri_p >= 0) {
+    n0 = __ldg(topo + 3 * tri_p); n1 = __ldg(topo + 3 * tri_p + 1); n2 = __ldg(topo + 3 * tri_p + 2);
+  }
+  unsigned m = 0;
+#pragma unroll
+  for (int d = 0; d < 4; ++d) {
+    const int t = tn[d];
+    if (t == INT_MIN || t == tri_p || (tri_p < 0 && t < 0)) continue;
+    if (tri_p >= 0 && t >= 0 && !(n0 == t || n1 == t || n2 == t)) continue;
+    m |= 1u << d;
+  }
+  return m;
+}
+
 // The forward's per-pixel record for the VJP (the optional `aa_work` buffer):
 // beta[P] float4 (one beta per direction, 0 where inactive), then code[P]
 // bytes, 2 bits per direction: 0 inactive, else the selected edge kk + 1.
@@ -258,38 +290,71 @@ __device__ __forceinline__ int64_t nbr_pix(int pn, int ph, int pw, int dir, int 
   return ((int64_t)pn * H + (ph + dh)) * W + (pw + dw);
 }
 
+// Forward, one pixel per thread, in three block phases so the silhouette
+// search never runs with a few lanes of a warp active: (1) every pixel finds
+// its candidate directions (sil_candidates) and queues (pixel, direction)
+// entries in shared memory; (2) the block evaluates the queue with dense
+// lanes (sil_dir, unchanged); (3) every pixel blends its colour from the
+// shared betas and, with WORK, writes its record for the VJP.
 template <bool XF, bool WORK>
-__global__ void k_aa_fwd(const float* __restrict__ color, int N, int H, int W, int C,
-                         const float4* __restrict__ rast, const float* __restrict__ pos,
-                         const float* __restrict__ xform, int V,
-                         const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
-                         float* __restrict__ out, float4* __restrict__ work_beta,
-                         uint8_t* __restrict__ work_code, unsigned* err) {
-  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= (int64_t)N * H * W) return;
-  const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
-  const int tri_p = rast_tri(rast, pix, T, err);
-  Mat4 M;
-  if (XF) M = load_mat4(xform + (int64_t)pn * 16);
-  float beta[4];
-  int64_t nb[4];
-  bool any = false;
-  unsigned code = 0;
+__global__ void __launch_bounds__(256) k_aa_fwd(const float* __restrict__ color, int N, int H, int W, int C,
+                                                const float4* __restrict__ rast, const float* __restrict__ pos,
+                                                const float* __restrict__ xform, int V,
+                                                const int32_t* __restrict__ tri, int T,
+                                                const int32_t* __restrict__ topo, float* __restrict__ out,
+                                                float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
+                                                unsigned* err) {
+  __shared__ float4 s_beta[256];
+  __shared__ unsigned s_code[256];
+  __shared__ uint16_t s_q[4 * 256];
+  __shared__ int s_qn;
+  const int lt = threadIdx.x;
+  const int64_t P = (int64_t)N * H * W;
+  const int64_t blk0 = (int64_t)blockIdx.x * 256;
+  const int64_t pix = blk0 + lt;
+  const bool valid = pix < P;
+  if (lt == 0) s_qn = 0;
+  s_beta[lt] = make_float4(0.f, 0.f, 0.f, 0.f);
+  s_code[lt] = 0u;
+  __syncthreads();
+  if (valid) {
+    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    const int tri_p = rast_tri(rast, pix, T, err);
+    const unsigned cand = sil_candidates(rast, topo, H, W, T, pn, ph, pw, tri_p, err);
+    if (cand) {
+      int q = atomicAdd(&s_qn, __popc(cand));
 #pragma unroll
-  for (int d = 0; d < 4; ++d) {
-    const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, d, err);
-    beta[d] = s.active ? s.beta : 0.0f;
-    nb[d] = s.active ? nbr_pix(pn, ph, pw, d, H, W) : -1;
-    any |= s.active;
-    if (s.active) code |= (unsigned)(s.kk + 1) << (2 * d);
+      for (int d = 0; d < 4; ++d)
+        if ((cand >> d) & 1u) s_q[q++] = (uint16_t)((lt << 2) | d);
+    }
   }
+  __syncthreads();
+  const int qn = s_qn;
+  for (int e = lt; e < qn; e += 256) {
+    const int lp = s_q[e] >> 2, d = s_q[e] & 3;
+    const int64_t qp = blk0 + lp;
+    const int pw = (int)(qp % W), ph = (int)((qp / W) % H), pn = (int)(qp / ((int64_t)H * W));
+    Mat4 M;
+    if (XF) M = load_mat4(xform + (int64_t)pn * 16);
+    const SilDir sd = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, rast_tri(rast, qp, T, err), d,
+                                  err);
+    if (sd.active) {
+      reinterpret_cast<float*>(&s_beta[lp])[d] = sd.beta;
+      atomicOr(&s_code[lp], (unsigned)(sd.kk + 1) << (2 * d));
+    }
+  }
+  __syncthreads();
+  if (!valid) return;
+  const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+  const float4 b4 = s_beta[lt];
+  const float beta[4] = {b4.x, b4.y, b4.z, b4.w};
   if (WORK) {
-    work_beta[pix] = make_float4(beta[0], beta[1], beta[2], beta[3]);
-    work_code[pix] = (uint8_t)code;
+    work_beta[pix] = b4;
+    work_code[pix] = (uint8_t)s_code[lt];
   }
   const float* cp = color + pix * C;
   float* o = out + pix * C;
-  if (!any) {
+  if (s_code[lt] == 0u) {
     if ((C & 3) == 0 && ((((uintptr_t)color) | ((uintptr_t)out)) & 15) == 0) {
       for (int c = 0; c < C; c += 4) *reinterpret_cast<float4*>(o + c) = ldg4(cp + c);
     } else {
@@ -297,6 +362,9 @@ __global__ void k_aa_fwd(const float* __restrict__ color, int N, int H, int W, i
     }
     return;
   }
+  int64_t nb[4];
+#pragma unroll
+  for (int d = 0; d < 4; ++d) nb[d] = beta[d] > 0.0f ? nbr_pix(pn, ph, pw, d, H, W) : -1;
   for (int c = 0; c < C; ++c) {
     const float p = __ldg(cp + c);
     float acc = p;
@@ -320,115 +388,63 @@ __device__ __forceinline__ void add_pos(float* p, const Mat4& M, float x, float 
   }
 }
 
-// WORK: the forward's record supplies every beta and each active direction's
-// edge, so no silhouette search runs (neighbour betas are plain loads).
-template <bool VEC, bool XF, bool WORK>
-__global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd(const float* __restrict__ color, int N, int H, int W, int C,
-                         const float4* __restrict__ rast, const float* __restrict__ pos,
-                         const float* __restrict__ xform, int V,
-                         const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
-                         const float* __restrict__ d_out, float* __restrict__ d_color, float* __restrict__ d_pos,
-                         const float4* __restrict__ work_beta, const uint8_t* __restrict__ work_code,
-                         unsigned* err) {
-  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= (int64_t)N * H * W) return;
-  const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
-  const int tri_p = rast_tri(rast, pix, T, err);
-  Mat4 M;
-  if (XF) M = load_mat4(xform + (int64_t)pn * 16);
-  const float* g = d_out + pix * C;
+// d_pos contribution of one active silhouette direction of pixel (pn, ph, pw)
+// (Antialias.swift:405-495): d_alpha = sum_c g (c_n - c_p); skipped outside
+// beta in (0, 1) or for d_alpha == 0.
+template <bool VEC, bool XF>
+__device__ __forceinline__ void aa_dir_dpos(const SilDir& s, const float* __restrict__ color, int C,
+                                            const float* __restrict__ g, int64_t pix, int64_t nb,
+                                            const float* __restrict__ pos, const Mat4& M, int V, int pn, int ph,
+                                            int pw, int H, int W, float* __restrict__ d_pos) {
+  if (s.beta <= 0.0f || s.beta >= 1.0f) return;
   const float halfW = (float)W * 0.5f, halfH = (float)H * 0.5f;
-  float alpha_sum = 0.0f;
-  // Own silhouettes: the (1 - sum beta) factor and d_pos (Antialias.swift:405-495).
-  unsigned code = 0;
-  if (WORK) code = __ldg(work_code + pix);
-#pragma unroll 1
-  for (int dir = 0; dir < 4; ++dir) {
-    SilDir s;
-    if (WORK) {
-      const int kk = (int)((code >> (2 * dir)) & 3u) - 1;
-      if (kk < 0) continue;
-      s = sil_replay<XF>(rast, pos, M, tri, H, W, V, T, pn, ph, pw, tri_p, dir, kk, err);
-    } else {
-      s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, dir, err);
-    }
-    if (!s.active) continue;
-    alpha_sum += s.beta;
-    if (s.beta <= 0.0f || s.beta >= 1.0f) continue;
-    const int64_t nb = nbr_pix(pn, ph, pw, dir, H, W);
-    float d_alpha = 0.0f;
-    for (int c = 0; c < C; ++c) {
-      const float cp = __ldg(color + pix * C + c), cn = __ldg(color + nb * C + c);
-      d_alpha += __ldg(g + c) * (cn - cp);
-    }
-    if (d_alpha == 0.0f) continue;
-    float dade0x, dade0y, dade1x, dade1y;
-    const float inv_denom_sq = 1.0f / (s.denom * s.denom);
-    if (s.horiz) {
-      const float row_y = (float)ph + 0.5f;
-      const float ex_diff = s.e1x - s.e0x;
-      dade0x = s.dbeta * (1.0f - s.t);
-      dade1x = s.dbeta * s.t;
-      dade0y = s.dbeta * ex_diff * (row_y - s.e1y) * inv_denom_sq;
-      dade1y = s.dbeta * (-ex_diff) * (row_y - s.e0y) * inv_denom_sq;
-    } else {
-      const float col_x = (float)pw + 0.5f;
-      const float ey_diff = s.e1y - s.e0y;
-      dade0y = s.dbeta * (1.0f - s.t);
-      dade1y = s.dbeta * s.t;
-      dade0x = s.dbeta * ey_diff * (col_x - s.e1x) * inv_denom_sq;
-      dade1x = s.dbeta * (-ey_diff) * (col_x - s.e0x) * inv_denom_sq;
-    }
-    const int64_t pb = XF ? 0 : (int64_t)pn * V * 4;
-    {
-      const float4 pv = vpos<XF>(pos, M, V, pn, s.ie0);
-      const float inv_w = 1.0f / pv.w;
-      const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
-      add_pos<VEC, XF>(d_pos + pb + (int64_t)s.ie0 * 4, M, d_alpha * dade0x * halfW * inv_w,
-                       d_alpha * dade0y * (-halfH) * inv_w,
-                       d_alpha * (dade0x * (-halfW * nd_x) + dade0y * (halfH * nd_y)) * inv_w);
-    }
-    {
-      const float4 pv = vpos<XF>(pos, M, V, pn, s.ie1);
-      const float inv_w = 1.0f / pv.w;
-      const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
-      add_pos<VEC, XF>(d_pos + pb + (int64_t)s.ie1 * 4, M, d_alpha * dade1x * halfW * inv_w,
-                       d_alpha * dade1y * (-halfH) * inv_w,
-                       d_alpha * (dade1x * (-halfW * nd_x) + dade1y * (halfH * nd_y)) * inv_w);
-    }
+  float d_alpha = 0.0f;
+  for (int c = 0; c < C; ++c) {
+    const float cp = __ldg(color + pix * C + c), cn = __ldg(color + nb * C + c);
+    d_alpha += __ldg(g + c) * (cn - cp);
   }
-  // Neighbours' betas toward this pixel: neighbour p = q - dir_d sees q in
-  // direction d.
-  float nbeta[4];
-  int64_t nsrc[4];
-  if (WORK) {
-#pragma unroll
-    for (int d = 0; d < 4; ++d) {
-      nbeta[d] = 0.0f;
-      nsrc[d] = -1;
-      const int sw = pw - (d == 0 ? 1 : (d == 2 ? -1 : 0));
-      const int sh = ph - (d == 1 ? 1 : (d == 3 ? -1 : 0));
-      if (sw < 0 || sw >= W || sh < 0 || sh >= H) continue;
-      const int64_t p = ((int64_t)pn * H + sh) * W + sw;
-      const float b = __ldg(reinterpret_cast<const float*>(work_beta + p) + d);
-      if (b > 0.0f) { nbeta[d] = b; nsrc[d] = p; }
-    }
+  if (d_alpha == 0.0f) return;
+  float dade0x, dade0y, dade1x, dade1y;
+  const float inv_denom_sq = 1.0f / (s.denom * s.denom);
+  if (s.horiz) {
+    const float row_y = (float)ph + 0.5f;
+    const float ex_diff = s.e1x - s.e0x;
+    dade0x = s.dbeta * (1.0f - s.t);
+    dade1x = s.dbeta * s.t;
+    dade0y = s.dbeta * ex_diff * (row_y - s.e1y) * inv_denom_sq;
+    dade1y = s.dbeta * (-ex_diff) * (row_y - s.e0y) * inv_denom_sq;
   } else {
-#pragma unroll 1
-    for (int d = 0; d < 4; ++d) {
-      nbeta[d] = 0.0f;
-      nsrc[d] = -1;
-      const int sw = pw - (d == 0 ? 1 : (d == 2 ? -1 : 0));
-      const int sh = ph - (d == 1 ? 1 : (d == 3 ? -1 : 0));
-      if (sw < 0 || sw >= W || sh < 0 || sh >= H) continue;
-      const int64_t p = ((int64_t)pn * H + sh) * W + sw;
-      const int tri_s = rast_tri(rast, p, T, err);
-      if (tri_s == tri_p) continue;  // no silhouette between equal ids
-      const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
-      if (s.active) { nbeta[d] = s.beta; nsrc[d] = p; }
-    }
+    const float col_x = (float)pw + 0.5f;
+    const float ey_diff = s.e1y - s.e0y;
+    dade0y = s.dbeta * (1.0f - s.t);
+    dade1y = s.dbeta * s.t;
+    dade0x = s.dbeta * ey_diff * (col_x - s.e1x) * inv_denom_sq;
+    dade1x = s.dbeta * (-ey_diff) * (col_x - s.e0x) * inv_denom_sq;
   }
-  const float keep = 1.0f - alpha_sum;
+  const int64_t pb = XF ? 0 : (int64_t)pn * V * 4;
+  {
+    const float4 pv = vpos<XF>(pos, M, V, pn, s.ie0);
+    const float inv_w = 1.0f / pv.w;
+    const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
+    add_pos<VEC, XF>(d_pos + pb + (int64_t)s.ie0 * 4, M, d_alpha * dade0x * halfW * inv_w,
+                     d_alpha * dade0y * (-halfH) * inv_w,
+                     d_alpha * (dade0x * (-halfW * nd_x) + dade0y * (halfH * nd_y)) * inv_w);
+  }
+  {
+    const float4 pv = vpos<XF>(pos, M, V, pn, s.ie1);
+    const float inv_w = 1.0f / pv.w;
+    const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
+    add_pos<VEC, XF>(d_pos + pb + (int64_t)s.ie1 * 4, M, d_alpha * dade1x * halfW * inv_w,
+                     d_alpha * dade1y * (-halfH) * inv_w,
+                     d_alpha * (dade1x * (-halfW * nd_x) + dade1y * (halfH * nd_y)) * inv_w);
+  }
+}
+
+// d_color in gather form: g (1 - sum of own betas) plus beta * g of every
+// neighbour whose silhouette points at this pixel.
+__device__ __forceinline__ void aa_dcolor(const float* __restrict__ d_out, float* __restrict__ d_color, int C,
+                                          int64_t pix, float keep, const float nbeta[4], const int64_t nsrc[4]) {
+  const float* g = d_out + pix * C;
   if ((C & 3) == 0 && ((((uintptr_t)d_out) | ((uintptr_t)d_color)) & 15) == 0) {
     for (int c = 0; c < C; c += 4) {
       const float4 gs = ldg4(g + c);
@@ -451,6 +467,117 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd(const float* __r
       if (nsrc[d] >= 0) v += __ldg(d_out + nsrc[d] * C + c) * nbeta[d];
     d_color[pix * C + c] = v;
   }
+}
+
+// VJP from the forward's record: (1) every pixel forms d_color from its own
+// and its neighbours' recorded betas and queues its active directions; (2)
+// the block replays the queued directions with dense lanes for d_pos.
+template <bool VEC, bool XF>
+__global__ void __launch_bounds__(256) k_aa_bwd_work(const float* __restrict__ color, int N, int H, int W, int C,
+                                                     const float4* __restrict__ rast, const float* __restrict__ pos,
+                                                     const float* __restrict__ xform, int V,
+                                                     const int32_t* __restrict__ tri, int T,
+                                                     const float* __restrict__ d_out, float* __restrict__ d_color,
+                                                     float* __restrict__ d_pos, const float4* __restrict__ work_beta,
+                                                     const uint8_t* __restrict__ work_code, unsigned* err) {
+  __shared__ uint16_t s_q[4 * 256];
+  __shared__ int s_qn;
+  const int lt = threadIdx.x;
+  const int64_t P = (int64_t)N * H * W;
+  const int64_t blk0 = (int64_t)blockIdx.x * 256;
+  const int64_t pix = blk0 + lt;
+  const bool valid = pix < P;
+  if (lt == 0) s_qn = 0;
+  __syncthreads();
+  if (valid) {
+    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    const unsigned code = __ldg(work_code + pix);
+    const float4 b4 = __ldg(work_beta + pix);
+    // The same sum the search path forms: 0 + the active betas in direction order.
+    const float keep = 1.0f - ((((0.0f + b4.x) + b4.y) + b4.z) + b4.w);
+    float nbeta[4];
+    int64_t nsrc[4];
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+      nbeta[d] = 0.0f;
+      nsrc[d] = -1;
+      const int sw = pw - (d == 0 ? 1 : (d == 2 ? -1 : 0));
+      const int sh = ph - (d == 1 ? 1 : (d == 3 ? -1 : 0));
+      if (sw < 0 || sw >= W || sh < 0 || sh >= H) continue;
+      const int64_t p = ((int64_t)pn * H + sh) * W + sw;
+      const float b = __ldg(reinterpret_cast<const float*>(work_beta + p) + d);
+      if (b > 0.0f) { nbeta[d] = b; nsrc[d] = p; }
+    }
+    aa_dcolor(d_out, d_color, C, pix, keep, nbeta, nsrc);
+    unsigned act = 0;
+#pragma unroll
+    for (int d = 0; d < 4; ++d)
+      if ((code >> (2 * d)) & 3u) act |= 1u << d;
+    if (act) {
+      int q = atomicAdd(&s_qn, __popc(act));
+#pragma unroll
+      for (int d = 0; d < 4; ++d)
+        if ((act >> d) & 1u) s_q[q++] = (uint16_t)((lt << 2) | d);
+    }
+  }
+  __syncthreads();
+  const int qn = s_qn;
+  for (int e = lt; e < qn; e += 256) {
+    const int lp = s_q[e] >> 2, d = s_q[e] & 3;
+    const int64_t qp = blk0 + lp;
+    const int pw = (int)(qp % W), ph = (int)((qp / W) % H), pn = (int)(qp / ((int64_t)H * W));
+    Mat4 M;
+    if (XF) M = load_mat4(xform + (int64_t)pn * 16);
+    const int kk = (int)((__ldg(work_code + qp) >> (2 * d)) & 3u) - 1;
+    const SilDir sd = sil_replay<XF>(rast, pos, M, tri, H, W, V, T, pn, ph, pw, rast_tri(rast, qp, T, err), d, kk,
+                                     err);
+    if (!sd.active) continue;
+    aa_dir_dpos<VEC, XF>(sd, color, C, d_out + qp * C, qp, nbr_pix(pn, ph, pw, d, H, W), pos, M, V, pn, ph, pw, H,
+                         W, d_pos);
+  }
+}
+
+// VJP that searches the silhouettes again (no forward record), as the
+// reference does: own directions for (1 - sum beta) and d_pos, and each
+// neighbour's direction toward this pixel for the gathered d_color.
+template <bool VEC, bool XF>
+__global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd(const float* __restrict__ color, int N, int H, int W, int C,
+                         const float4* __restrict__ rast, const float* __restrict__ pos,
+                         const float* __restrict__ xform, int V,
+                         const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
+                         const float* __restrict__ d_out, float* __restrict__ d_color, float* __restrict__ d_pos,
+                         unsigned* err) {
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= (int64_t)N * H * W) return;
+  const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+  const int tri_p = rast_tri(rast, pix, T, err);
+  Mat4 M;
+  if (XF) M = load_mat4(xform + (int64_t)pn * 16);
+  float alpha_sum = 0.0f;
+#pragma unroll 1
+  for (int dir = 0; dir < 4; ++dir) {
+    const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, dir, err);
+    if (!s.active) continue;
+    alpha_sum += s.beta;
+    aa_dir_dpos<VEC, XF>(s, color, C, d_out + pix * C, pix, nbr_pix(pn, ph, pw, dir, H, W), pos, M, V, pn, ph, pw,
+                         H, W, d_pos);
+  }
+  float nbeta[4];
+  int64_t nsrc[4];
+#pragma unroll 1
+  for (int d = 0; d < 4; ++d) {
+    nbeta[d] = 0.0f;
+    nsrc[d] = -1;
+    const int sw = pw - (d == 0 ? 1 : (d == 2 ? -1 : 0));
+    const int sh = ph - (d == 1 ? 1 : (d == 3 ? -1 : 0));
+    if (sw < 0 || sw >= W || sh < 0 || sh >= H) continue;
+    const int64_t p = ((int64_t)pn * H + sh) * W + sw;
+    const int tri_s = rast_tri(rast, p, T, err);
+    if (tri_s == tri_p) continue;  // no silhouette between equal ids
+    const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
+    if (s.active) { nbeta[d] = s.beta; nsrc[d] = p; }
+  }
+  aa_dcolor(d_out, d_color, C, pix, 1.0f - alpha_sum, nbeta, nsrc);
 }
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
@@ -538,16 +665,22 @@ dr_status aa_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, co
   const uint8_t* wc = work ? reinterpret_cast<const uint8_t*>(work) + (size_t)P * 16 : nullptr;
   if (xform) DR_REQUIRE(ctx, aligned16(d_pos), "antialias_xf_bwd: d_verts must be 16-byte aligned");
   DR_TB(ctx);
-#define DR_AB(VECV, XFV, WV, XP)                                                                             \
-  k_aa_bwd<VECV, XFV, WV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T, \
-                                                                     topo, d_out, d_color, d_pos, wb, wc,        \
-                                                                     ctx->d_err)
+#define DR_AB(VECV, XFV, XP)                                                                                  \
+  do {                                                                                                         \
+    if (work)                                                                                                  \
+      k_aa_bwd_work<VECV, XFV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, \
+                                                                          T, d_out, d_color, d_pos, wb, wc,      \
+                                                                          ctx->d_err);                           \
+    else                                                                                                       \
+      k_aa_bwd<VECV, XFV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T,   \
+                                                                     topo, d_out, d_color, d_pos, ctx->d_err);   \
+  } while (0)
   if (xform) {
-    if (work) DR_AB(true, true, true, xform); else DR_AB(true, true, false, xform);
+    DR_AB(true, true, xform);
   } else if (aligned16(d_pos)) {
-    if (work) DR_AB(true, false, true, nullptr); else DR_AB(true, false, false, nullptr);
+    DR_AB(true, false, nullptr);
   } else {
-    if (work) DR_AB(false, false, true, nullptr); else DR_AB(false, false, false, nullptr);
+    DR_AB(false, false, nullptr);
   }
 #undef DR_AB
   DR_LAUNCHED(ctx, "aa_bwd");
