@@ -327,6 +327,19 @@ DR_API dr_status dr_mse_bwd(dr_ctx* ctx, const float* pred, const float* target,
                      int64_t n, float scale, const float* d_loss, float* d_pred);
 
 
+/* ---- optimizer step of the reference's examples ----------------------- */
+
+/* One Adam step in place (MLXDiffRastExamples/Adam.swift:36-43), fused:
+ *   g = grad (* mask when mask != NULL); m = beta1 m + (1 - beta1) g;
+ *   v = beta2 v + (1 - beta2) g^2;
+ *   param -= (lr * m / bias_c1) / (sqrt(v / bias_c2) + eps)
+ * with bias_c1 = 1 - beta1^t and bias_c2 = 1 - beta2^t for step t >= 1,
+ * formed by the caller in float.  n elements; m and v start at zero. */
+DR_API dr_status dr_adam_step(dr_ctx* ctx, float* param, const float* grad,
+                       const float* mask, float* m, float* v, int64_t n,
+                       float lr, float beta1, float beta2, float eps,
+                       float bias_c1, float bias_c2);
+
 #ifdef __cplusplus
 }
 #endif

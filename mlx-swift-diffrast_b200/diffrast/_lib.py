@@ -58,6 +58,7 @@ SIGNATURES = {
     "dr_antialias_xf_bwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P, P, P]),
     "dr_mse_fwd_bwd": (I, [P, P, P, I64, F, P, P, I]),
     "dr_mse_bwd": (I, [P, P, P, I64, F, P, P]),
+    "dr_adam_step": (I, [P, P, P, P, P, P, I64, F, F, F, F, F, F]),
 }
 
 _lib = None

@@ -276,3 +276,24 @@ def xf_vertex_grad(d_pos, xform):
     d_verts[v] = sum_n M_n^T d_pos[n, v] (float64 accumulation)."""
     return np.einsum("nri,nvr->vi", np.asarray(xform, np.float64),
                      np.asarray(d_pos, np.float64)).astype(np.float32)
+
+
+# ------------------------------------------------------- optimizer (examples)
+
+def adam_step(param, grad, m, v, t, lr, beta1=0.9, beta2=0.999, eps=1e-8, mask=None):
+    """Adam.swift:36-43 in float32, one IEEE operation at a time in the
+    reference's order: returns (param, m, v) after step t (t >= 1).  `mask`
+    multiplies the gradient first, as the PoseFit / MeshFit examples do."""
+    f = np.float32
+    g = np.asarray(grad, f)
+    if mask is not None:
+        g = (g * np.asarray(mask, f)).astype(f)
+    b1, b2, lr, eps = f(beta1), f(beta2), f(lr), f(eps)
+    m = (b1 * np.asarray(m, f) + (f(1) - b1) * g).astype(f)
+    v = (b2 * np.asarray(v, f) + (f(1) - b2) * (g * g)).astype(f)
+    c1 = f(1) - np.power(b1, f(t))
+    c2 = f(1) - np.power(b2, f(t))
+    m_hat = (m / c1).astype(f)
+    v_hat = (v / c2).astype(f)
+    p = (np.asarray(param, f) - (lr * m_hat) / (np.sqrt(v_hat) + eps)).astype(f)
+    return p, m, v
