@@ -473,7 +473,7 @@ __device__ __forceinline__ void aa_dcolor(const float* __restrict__ d_out, float
 // and its neighbours' recorded betas and queues its active directions; (2)
 // the block replays the queued directions with dense lanes for d_pos.
 template <bool VEC, bool XF>
-__global__ void __launch_bounds__(256) k_aa_bwd_work(const float* __restrict__ color, int N, int H, int W, int C,
+__global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_work(const float* __restrict__ color, int N, int H, int W, int C,
                                                      const float4* __restrict__ rast, const float* __restrict__ pos,
                                                      const float* __restrict__ xform, int V,
                                                      const int32_t* __restrict__ tri, int T,

@@ -35,6 +35,9 @@ __global__ void k_interp_fwd(const float* __restrict__ attr, bool attr_shared, i
   int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (pix >= P) return;
   const float4 r = __ldg(rast + pix);
+  // rast_db is independent of the triangle gathers: issue it with rast.
+  float4 db = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (DA) db = __ldg(rast_db + pix);
   int t = (int)r.w - 1;
   float* o = out + pix * A;
   float* od = DA ? out_da + pix * 2 * K : nullptr;
@@ -66,8 +69,9 @@ __global__ void k_interp_fwd(const float* __restrict__ attr, bool attr_shared, i
   const float* a2p = an + (int64_t)i2 * A;
   if (VEC4 && DA && !IDX) {
     // .all with A % 4 == 0: out and out_da from the same float4 gathers;
-    // out_da rows are 2A floats, so every store is a float4.
-    const float4 db = __ldg(rast_db + pix);
+    // out_da rows are 2A floats, so every store is a float4.  Unrolled by two
+    // so the gathers of consecutive channel groups are in flight together.
+#pragma unroll 2
     for (int a = 0; a < A; a += 4) {
       const float4 x0 = ldg4(a0p + a), x1 = ldg4(a1p + a), x2 = ldg4(a2p + a);
       float4 y;
@@ -88,6 +92,7 @@ __global__ void k_interp_fwd(const float* __restrict__ attr, bool attr_shared, i
     return;
   }
   if (VEC4) {
+#pragma unroll 2
     for (int a = 0; a < A; a += 4) {
       const float4 x0 = ldg4(a0p + a), x1 = ldg4(a1p + a), x2 = ldg4(a2p + a);
       float4 y;
@@ -101,7 +106,6 @@ __global__ void k_interp_fwd(const float* __restrict__ attr, bool attr_shared, i
     for (int a = 0; a < A; ++a) o[a] = bw * __ldg(a0p + a) + u * __ldg(a1p + a) + v * __ldg(a2p + a);
   }
   if (DA) {
-    const float4 db = __ldg(rast_db + pix);
     for (int k = 0; k < K; ++k) {
       const int a = IDX ? idx.k[k] : k;
       const float x0 = __ldg(a0p + a), x1 = __ldg(a1p + a), x2 = __ldg(a2p + a);
