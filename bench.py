@@ -113,6 +113,21 @@ class ClockSampler:
 
 # --------------------------------------------------- algorithmic bytes
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per pixel of one
+# layer for a kernel, from one ncu --set full capture of the 2-view cfg4 case
+# (2 x 1024^2 pixels per layer; the two-layer raster launch covers both
+# layers).  A full launch's traffic is this times its pixels: every per-pixel
+# stream scales with pixels, and the per-triangle records and tile lists with
+# views, i.e. also with pixels at a fixed resolution.
+NCU_DRAM_BYTES_PER_PIXEL = {
+    ("cfg4", "raster_tiles"): (120.805120e6 + 99.294464e6) / (2 * 1024 * 1024),
+    ("cfg4", "interp_fwd"): (146.003456e6 + 151.024640e6) / (2 * 1024 * 1024),
+    ("cfg4", "interp_bwd"): (244.021760e6 + 54.654464e6) / (2 * 1024 * 1024),
+    ("cfg4", "raster_bwd"): (145.058048e6 + 10.691072e6) / (2 * 1024 * 1024),
+    ("cfg4", "aa_fwd"): (124.246016e6 + 69.550336e6) / (2 * 1024 * 1024),
+}
+
+
 def algorithmic_bytes(cfg: str, chain) -> dict:
     """Compulsory HBM bytes per step for each library kernel (each input read
     once, each output written once; intermediates such as setup records, tile
@@ -385,15 +400,23 @@ def main():
     for name, (cnt, tot_ms) in sorted(report.items(), key=lambda kv: -kv[1][1]):
         b = algo.get(name, 0) * args.steps
         ach = b / (tot_ms * 1e-3) / 1e9 if (b and tot_ms > 0) else None
+        per_px = NCU_DRAM_BYTES_PER_PIXEL.get((cfg, name))
         kernels[name] = {"launches": cnt, "ms_per_launch": tot_ms / cnt, "share": tot_ms / (ms * args.steps),
                          "algo_bytes_per_launch": (b / cnt) if b else 0,
-                         "gbs": ach, "frac": (ach / peak) if ach else None}
+                         "gbs": ach, "frac": (ach / peak) if ach else None,
+                         "ncu_dram_bytes_per_launch": per_px * chain.info.pixels if per_px else None}
     dom = next((n for n in kernels if kernels[n]["gbs"]), None)
     roof = None
     if dom:
         kd = kernels[dom]
+        per_px = NCU_DRAM_BYTES_PER_PIXEL.get((cfg, dom))
+        traffic = per_px * chain.info.pixels if per_px else None
         roof = {"kernel": dom, "bound": "hbm", "achieved": kd["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": kd["frac"], "peak_source": f"{peak_kind} hbm_gbs", "traffic": None}
+                "frac": kd["frac"], "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic,
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel on a 2-view "
+                                   "capture of the same workload, per pixel, times this launch's pixels")
+                if per_px else None,
+                "algo_bytes_per_launch": kd["algo_bytes_per_launch"]}
 
     e2e = None
     if not args.no_e2e:
