@@ -290,88 +290,110 @@ __device__ __forceinline__ int64_t nbr_pix(int pn, int ph, int pw, int dir, int 
   return ((int64_t)pn * H + (ph + dh)) * W + (pw + dw);
 }
 
-// Forward, one pixel per thread, in three block phases so the silhouette
-// search never runs with a few lanes of a warp active: (1) every pixel finds
-// its candidate directions (sil_candidates) and queues (pixel, direction)
-// entries in shared memory; (2) the block evaluates the queue with dense
-// lanes (sil_dir, unchanged); (3) every pixel blends its colour from the
-// shared betas and, with WORK, writes its record for the VJP.
-template <bool XF, bool WORK>
-__global__ void __launch_bounds__(256) k_aa_fwd(const float* __restrict__ color, int N, int H, int W, int C,
-                                                const float4* __restrict__ rast, const float* __restrict__ pos,
-                                                const float* __restrict__ xform, int V,
-                                                const int32_t* __restrict__ tri, int T,
-                                                const int32_t* __restrict__ topo, float* __restrict__ out,
-                                                float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
-                                                unsigned* err) {
-  __shared__ float4 s_beta[256];
-  __shared__ unsigned s_code[256];
-  __shared__ uint16_t s_q[4 * 256];
-  __shared__ int s_qn;
-  const int lt = threadIdx.x;
-  const int64_t P = (int64_t)N * H * W;
-  const int64_t blk0 = (int64_t)blockIdx.x * 256;
-  const int64_t pix = blk0 + lt;
-  const bool valid = pix < P;
-  if (lt == 0) s_qn = 0;
-  s_beta[lt] = make_float4(0.f, 0.f, 0.f, 0.f);
-  s_code[lt] = 0u;
-  __syncthreads();
-  if (valid) {
-    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
-    const int tri_p = rast_tri(rast, pix, T, err);
-    const unsigned cand = sil_candidates(rast, topo, H, W, T, pn, ph, pw, tri_p, err);
-    if (cand) {
-      int q = atomicAdd(&s_qn, __popc(cand));
-#pragma unroll
-      for (int d = 0; d < 4; ++d)
-        if ((cand >> d) & 1u) s_q[q++] = (uint16_t)((lt << 2) | d);
-    }
-  }
-  __syncthreads();
-  const int qn = s_qn;
-  for (int e = lt; e < qn; e += 256) {
-    const int lp = s_q[e] >> 2, d = s_q[e] & 3;
-    const int64_t qp = blk0 + lp;
-    const int pw = (int)(qp % W), ph = (int)((qp / W) % H), pn = (int)(qp / ((int64_t)H * W));
-    Mat4 M;
-    if (XF) M = load_mat4(xform + (int64_t)pn * 16);
-    const SilDir sd = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, rast_tri(rast, qp, T, err), d,
-                                  err);
-    if (sd.active) {
-      reinterpret_cast<float*>(&s_beta[lp])[d] = sd.beta;
-      atomicOr(&s_code[lp], (unsigned)(sd.kk + 1) << (2 * d));
-    }
-  }
-  __syncthreads();
-  if (!valid) return;
-  const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
-  const float4 b4 = s_beta[lt];
-  const float beta[4] = {b4.x, b4.y, b4.z, b4.w};
-  if (WORK) {
-    work_beta[pix] = b4;
-    work_code[pix] = (uint8_t)s_code[lt];
-  }
+// Forward in two passes, so the rare silhouette search runs at full occupancy
+// instead of holding up whole warps and blocks:
+//   k_aa_fwd_scan   every pixel finds its candidate directions with one round
+//                   of independent loads (sil_candidates); pixels with none
+//                   are finished there (colour copied, empty record), the rest
+//                   are appended to a list as (pixel << 4 | candidate bits);
+//   k_aa_fwd_edges  a grid-stride pass over the list: sil_dir for each
+//                   candidate direction, then the record and the blend.
+template <bool WORK>
+__global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ color, int N, int H, int W, int C,
+                                                     const float4* __restrict__ rast, int T,
+                                                     const int32_t* __restrict__ topo, float* __restrict__ out,
+                                                     float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
+                                                     unsigned long long* __restrict__ list,
+                                                     unsigned long long* __restrict__ count, unsigned* err) {
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool valid = pix < (int64_t)N * H * W;
   const float* cp = color + pix * C;
   float* o = out + pix * C;
-  if (s_code[lt] == 0u) {
-    if ((C & 3) == 0 && ((((uintptr_t)color) | ((uintptr_t)out)) & 15) == 0) {
-      for (int c = 0; c < C; c += 4) *reinterpret_cast<float4*>(o + c) = ldg4(cp + c);
-    } else {
-      for (int c = 0; c < C; ++c) o[c] = __ldg(cp + c);
-    }
+  // The common case (no candidate, C == 8, aligned) copies the colour row:
+  // load it first so it overlaps the topology gather.
+  const bool vec8 = C == 8 && ((((uintptr_t)color) | ((uintptr_t)out)) & 15) == 0;
+  float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0;
+  if (valid && vec8) { c0 = ldg4(cp); c1 = ldg4(cp + 4); }
+  unsigned cand = 0;
+  if (valid) {
+    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    cand = sil_candidates(rast, topo, H, W, T, pn, ph, pw, rast_tri(rast, pix, T, err), err);
+  }
+  const unsigned m = __ballot_sync(0xffffffffu, cand != 0u);
+  if (m) {
+    const int lane = threadIdx.x & 31, leader = __ffs(m) - 1;
+    unsigned long long base = 0;
+    if (lane == leader) base = atomicAdd(count, (unsigned long long)__popc(m));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (cand) list[base + __popc(m & ((1u << lane) - 1u))] = ((unsigned long long)pix << 4) | cand;
+  }
+  if (!valid || cand) return;
+  if (WORK) {
+    work_beta[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
+    work_code[pix] = 0;
+  }
+  if (vec8) {
+    *reinterpret_cast<float4*>(o) = c0;
+    *reinterpret_cast<float4*>(o + 4) = c1;
     return;
   }
-  int64_t nb[4];
+  if ((C & 3) == 0 && ((((uintptr_t)color) | ((uintptr_t)out)) & 15) == 0) {
+    for (int c = 0; c < C; c += 4) *reinterpret_cast<float4*>(o + c) = ldg4(cp + c);
+  } else {
+    for (int c = 0; c < C; ++c) o[c] = __ldg(cp + c);
+  }
+}
+
+template <bool XF, bool WORK>
+__global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ color, int N, int H, int W, int C,
+                                                      const float4* __restrict__ rast, const float* __restrict__ pos,
+                                                      const float* __restrict__ xform, int V,
+                                                      const int32_t* __restrict__ tri, int T,
+                                                      const int32_t* __restrict__ topo, float* __restrict__ out,
+                                                      float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
+                                                      const unsigned long long* __restrict__ list,
+                                                      const unsigned long long* __restrict__ count, unsigned* err) {
+  const unsigned long long n = *count;
+  const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+  for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const unsigned long long e = list[i];
+    const int64_t pix = (int64_t)(e >> 4);
+    const unsigned cand = (unsigned)(e & 15u);
+    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    const int tri_p = rast_tri(rast, pix, T, err);
+    Mat4 M;
+    if (XF) M = load_mat4(xform + (int64_t)pn * 16);
+    float beta[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    unsigned code = 0;
 #pragma unroll
-  for (int d = 0; d < 4; ++d) nb[d] = beta[d] > 0.0f ? nbr_pix(pn, ph, pw, d, H, W) : -1;
-  for (int c = 0; c < C; ++c) {
-    const float p = __ldg(cp + c);
-    float acc = p;
+    for (int d = 0; d < 4; ++d) {
+      if (!((cand >> d) & 1u)) continue;
+      const SilDir sd = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, d, err);
+      if (!sd.active) continue;
+      beta[d] = sd.beta;
+      code |= (unsigned)(sd.kk + 1) << (2 * d);
+    }
+    if (WORK) {
+      work_beta[pix] = make_float4(beta[0], beta[1], beta[2], beta[3]);
+      work_code[pix] = (uint8_t)code;
+    }
+    const float* cp = color + pix * C;
+    float* o = out + pix * C;
+    if (code == 0u) {
+      for (int c = 0; c < C; ++c) o[c] = __ldg(cp + c);
+      continue;
+    }
+    int64_t nb[4];
 #pragma unroll
-    for (int d = 0; d < 4; ++d)
-      if (nb[d] >= 0) acc += beta[d] * (__ldg(color + nb[d] * C + c) - p);
-    o[c] = acc;
+    for (int d = 0; d < 4; ++d) nb[d] = beta[d] > 0.0f ? nbr_pix(pn, ph, pw, d, H, W) : -1;
+    for (int c = 0; c < C; ++c) {
+      const float p = __ldg(cp + c);
+      float acc = p;
+#pragma unroll
+      for (int d = 0; d < 4; ++d)
+        if (nb[d] >= 0) acc += beta[d] * (__ldg(color + nb[d] * C + c) - p);
+      o[c] = acc;
+    }
   }
 }
 
@@ -469,29 +491,23 @@ __device__ __forceinline__ void aa_dcolor(const float* __restrict__ d_out, float
   }
 }
 
-// VJP from the forward's record: (1) every pixel forms d_color from its own
-// and its neighbours' recorded betas and queues its active directions; (2)
-// the block replays the queued directions with dense lanes for d_pos.
-template <bool VEC, bool XF>
-__global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_work(const float* __restrict__ color, int N, int H, int W, int C,
-                                                     const float4* __restrict__ rast, const float* __restrict__ pos,
-                                                     const float* __restrict__ xform, int V,
-                                                     const int32_t* __restrict__ tri, int T,
-                                                     const float* __restrict__ d_out, float* __restrict__ d_color,
-                                                     float* __restrict__ d_pos, const float4* __restrict__ work_beta,
-                                                     const uint8_t* __restrict__ work_code, unsigned* err) {
-  __shared__ uint16_t s_q[4 * 256];
-  __shared__ int s_qn;
-  const int lt = threadIdx.x;
-  const int64_t P = (int64_t)N * H * W;
-  const int64_t blk0 = (int64_t)blockIdx.x * 256;
-  const int64_t pix = blk0 + lt;
-  const bool valid = pix < P;
-  if (lt == 0) s_qn = 0;
-  __syncthreads();
+// VJP from the forward's record, in two passes: k_aa_bwd_gather forms every
+// pixel's d_color from its own and its neighbours' recorded betas and appends
+// pixels with active directions to a list as (pixel << 8 | record code);
+// k_aa_bwd_edges replays those edges (a grid-stride pass, full occupancy)
+// for the d_pos atomics.
+__global__ void __launch_bounds__(256) k_aa_bwd_gather(int N, int H, int W, int C,
+                                                       const float* __restrict__ d_out, float* __restrict__ d_color,
+                                                       const float4* __restrict__ work_beta,
+                                                       const uint8_t* __restrict__ work_code,
+                                                       unsigned long long* __restrict__ list,
+                                                       unsigned long long* __restrict__ count) {
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool valid = pix < (int64_t)N * H * W;
+  unsigned code = 0;
   if (valid) {
     const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
-    const unsigned code = __ldg(work_code + pix);
+    code = __ldg(work_code + pix);
     const float4 b4 = __ldg(work_beta + pix);
     // The same sum the search path forms: 0 + the active betas in direction order.
     const float keep = 1.0f - ((((0.0f + b4.x) + b4.y) + b4.z) + b4.w);
@@ -509,31 +525,42 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_work(const float
       if (b > 0.0f) { nbeta[d] = b; nsrc[d] = p; }
     }
     aa_dcolor(d_out, d_color, C, pix, keep, nbeta, nsrc);
-    unsigned act = 0;
-#pragma unroll
-    for (int d = 0; d < 4; ++d)
-      if ((code >> (2 * d)) & 3u) act |= 1u << d;
-    if (act) {
-      int q = atomicAdd(&s_qn, __popc(act));
-#pragma unroll
-      for (int d = 0; d < 4; ++d)
-        if ((act >> d) & 1u) s_q[q++] = (uint16_t)((lt << 2) | d);
-    }
   }
-  __syncthreads();
-  const int qn = s_qn;
-  for (int e = lt; e < qn; e += 256) {
-    const int lp = s_q[e] >> 2, d = s_q[e] & 3;
-    const int64_t qp = blk0 + lp;
-    const int pw = (int)(qp % W), ph = (int)((qp / W) % H), pn = (int)(qp / ((int64_t)H * W));
+  const unsigned m = __ballot_sync(0xffffffffu, code != 0u);
+  if (m) {
+    const int lane = threadIdx.x & 31, leader = __ffs(m) - 1;
+    unsigned long long base = 0;
+    if (lane == leader) base = atomicAdd(count, (unsigned long long)__popc(m));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (code) list[base + __popc(m & ((1u << lane) - 1u))] = ((unsigned long long)pix << 8) | code;
+  }
+}
+
+template <bool VEC, bool XF>
+__global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_edges(
+    const float* __restrict__ color, int N, int H, int W, int C, const float4* __restrict__ rast,
+    const float* __restrict__ pos, const float* __restrict__ xform, int V, const int32_t* __restrict__ tri, int T,
+    const float* __restrict__ d_out, float* __restrict__ d_pos, const unsigned long long* __restrict__ list,
+    const unsigned long long* __restrict__ count, unsigned* err) {
+  const unsigned long long n = *count;
+  const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+  for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const unsigned long long e = list[i];
+    const int64_t pix = (int64_t)(e >> 8);
+    const unsigned code = (unsigned)(e & 255u);
+    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    const int tri_p = rast_tri(rast, pix, T, err);
     Mat4 M;
     if (XF) M = load_mat4(xform + (int64_t)pn * 16);
-    const int kk = (int)((__ldg(work_code + qp) >> (2 * d)) & 3u) - 1;
-    const SilDir sd = sil_replay<XF>(rast, pos, M, tri, H, W, V, T, pn, ph, pw, rast_tri(rast, qp, T, err), d, kk,
-                                     err);
-    if (!sd.active) continue;
-    aa_dir_dpos<VEC, XF>(sd, color, C, d_out + qp * C, qp, nbr_pix(pn, ph, pw, d, H, W), pos, M, V, pn, ph, pw, H,
-                         W, d_pos);
+#pragma unroll 1
+    for (int d = 0; d < 4; ++d) {
+      const int kk = (int)((code >> (2 * d)) & 3u) - 1;
+      if (kk < 0) continue;
+      const SilDir sd = sil_replay<XF>(rast, pos, M, tri, H, W, V, T, pn, ph, pw, tri_p, d, kk, err);
+      if (!sd.active) continue;
+      aa_dir_dpos<VEC, XF>(sd, color, C, d_out + pix * C, pix, nbr_pix(pn, ph, pw, d, H, W), pos, M, V, pn, ph, pw,
+                           H, W, d_pos);
+    }
   }
 }
 
@@ -625,6 +652,22 @@ extern "C" dr_status dr_antialias_construct_topology_hash(dr_ctx* ctx, const int
 
 namespace {
 
+// Candidate list in the WS_AA slot: a 64-bit count, then one 64-bit entry per
+// listed pixel (at most one per pixel).
+dr_status aa_list(dr_ctx* ctx, int64_t P, unsigned long long** count, unsigned long long** list) {
+  char* w = (char*)ws_get(ctx, WS_AA, 16 + sizeof(unsigned long long) * (size_t)P);
+  if (!w) return DR_ENOMEM;
+  *count = reinterpret_cast<unsigned long long*>(w);
+  *list = reinterpret_cast<unsigned long long*>(w + 16);
+  DR_CUDA(ctx, cudaMemsetAsync(w, 0, sizeof(unsigned long long), ctx->stream), "antialias list");
+  return DR_OK;
+}
+
+// Grid of a grid-stride pass over a device-counted list (about 8 blocks per SM).
+inline unsigned list_grid(dr_ctx* ctx, int64_t P) {
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>((P + 255) / 256, (int64_t)ctx->num_sms * 8));
+}
+
 dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
                  const float* pos, const float* xform, int V, const int32_t* tri, int T, const int32_t* topo,
                  float* out, void* work) {
@@ -636,17 +679,27 @@ dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, co
   const float4* r4 = reinterpret_cast<const float4*>(rast);
   float4* wb = reinterpret_cast<float4*>(work);
   uint8_t* wc = work ? reinterpret_cast<uint8_t*>(work) + (size_t)P * 16 : nullptr;
+  unsigned long long *cnt = nullptr, *list = nullptr;
+  if ((st = aa_list(ctx, P, &cnt, &list)) != DR_OK) return st;
   DR_TB(ctx);
-#define DR_AF(XFV, WV, XP)                                                                                   \
-  k_aa_fwd<XFV, WV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T, topo, \
-                                                               out, wb, wc, ctx->d_err)
+  if (work)
+    k_aa_fwd_scan<true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, T, topo, out, wb, wc,
+                                                                    list, cnt, ctx->d_err);
+  else
+    k_aa_fwd_scan<false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, T, topo, out, wb, wc,
+                                                                     list, cnt, ctx->d_err);
+  DR_LAUNCHED(ctx, "aa_fwd");
+  DR_TB(ctx);
+#define DR_AF(XFV, WV, XP)                                                                                       \
+  k_aa_fwd_edges<XFV, WV><<<list_grid(ctx, P), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T,  \
+                                                                      topo, out, wb, wc, list, cnt, ctx->d_err)
   if (xform) {
     if (work) DR_AF(true, true, xform); else DR_AF(true, false, xform);
   } else {
     if (work) DR_AF(false, true, nullptr); else DR_AF(false, false, nullptr);
   }
 #undef DR_AF
-  DR_LAUNCHED(ctx, "aa_fwd");
+  DR_LAUNCHED(ctx, "aa_fwd_edges");
   return DR_OK;
 }
 
@@ -664,24 +717,31 @@ dr_status aa_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, co
   const float4* wb = reinterpret_cast<const float4*>(work);
   const uint8_t* wc = work ? reinterpret_cast<const uint8_t*>(work) + (size_t)P * 16 : nullptr;
   if (xform) DR_REQUIRE(ctx, aligned16(d_pos), "antialias_xf_bwd: d_verts must be 16-byte aligned");
-  DR_TB(ctx);
-#define DR_AB(VECV, XFV, XP)                                                                                  \
-  do {                                                                                                         \
-    if (work)                                                                                                  \
-      k_aa_bwd_work<VECV, XFV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, \
-                                                                          T, d_out, d_color, d_pos, wb, wc,      \
-                                                                          ctx->d_err);                           \
-    else                                                                                                       \
-      k_aa_bwd<VECV, XFV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T,   \
-                                                                     topo, d_out, d_color, d_pos, ctx->d_err);   \
-  } while (0)
-  if (xform) {
-    DR_AB(true, true, xform);
-  } else if (aligned16(d_pos)) {
-    DR_AB(true, false, nullptr);
-  } else {
-    DR_AB(false, false, nullptr);
+  const bool vec = xform || aligned16(d_pos);
+  if (work) {
+    unsigned long long *cnt = nullptr, *list = nullptr;
+    if ((st = aa_list(ctx, P, &cnt, &list)) != DR_OK) return st;
+    DR_TB(ctx);
+    k_aa_bwd_gather<<<grid_for(P, 256), 256, 0, ctx->stream>>>(N, H, W, C, d_out, d_color, wb, wc, list, cnt);
+    DR_LAUNCHED(ctx, "aa_bwd");
+    DR_TB(ctx);
+#define DR_AE(VECV, XFV, XP)                                                                                     \
+  k_aa_bwd_edges<VECV, XFV><<<list_grid(ctx, P), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T, \
+                                                                        d_out, d_pos, list, cnt, ctx->d_err)
+    if (xform) DR_AE(true, true, xform);
+    else if (vec) DR_AE(true, false, nullptr);
+    else DR_AE(false, false, nullptr);
+#undef DR_AE
+    DR_LAUNCHED(ctx, "aa_bwd_edges");
+    return DR_OK;
   }
+  DR_TB(ctx);
+#define DR_AB(VECV, XFV, XP)                                                                                     \
+  k_aa_bwd<VECV, XFV><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T, topo,  \
+                                                                 d_out, d_color, d_pos, ctx->d_err)
+  if (xform) DR_AB(true, true, xform);
+  else if (vec) DR_AB(true, false, nullptr);
+  else DR_AB(false, false, nullptr);
 #undef DR_AB
   DR_LAUNCHED(ctx, "aa_bwd");
   return DR_OK;
