@@ -102,6 +102,34 @@ __device__ __forceinline__ float sample4(const float* __restrict__ b, const Taps
   return q.w00 * t00 + q.w10 * t10 + q.w01 * t01 + q.w11 * t11;
 }
 
+// d_tex scatter of one tap: adds w * (g[c] * gscale) to p[c] (c < C) for
+// every lane.  Lanes of a warp that hit the same texel (runs of neighbouring
+// pixels: a magnified texture, or background pixels that all sample one
+// texel) are summed first with a segmented warp reduction, so each run issues
+// one atomic per channel instead of one per pixel; a zero contribution issues
+// none (d_tex starts at +0, and adding +-0 to +0 leaves +0).  All 32 lanes of
+// the warp must call it; lanes with on == false add nothing.
+__device__ __forceinline__ void scatter_tap(float* p, float w, const float* __restrict__ g, float gscale, int C,
+                                            bool on, int lane) {
+  const long long key = on ? (long long)(uintptr_t)p : -1ll - (long long)lane;
+  bool head;
+  const int seg_end = warp_runs(key, lane, head);
+  const int span = warp_max_run(lane, seg_end, head);
+  if (span == 1) {
+    if (on)
+      for (int c = 0; c < C; ++c) {
+        const float v = w * (__ldg(g + c) * gscale);
+        if (v != 0.0f) atomicAdd(p + c, v);
+      }
+    return;
+  }
+  for (int c = 0; c < C; ++c) {
+    float v = on ? w * (__ldg(g + c) * gscale) : 0.0f;
+    v = warp_seg_sum(v, lane, seg_end, span);
+    if (on && head && v != 0.0f) atomicAdd(p + c, v);
+  }
+}
+
 // ---------------------------------------------------------------- bilinear
 
 template <int MODE>
@@ -123,25 +151,29 @@ __global__ void k_tex_linear_bwd(const float* __restrict__ tex, bool tex_shared,
                                  const float2* __restrict__ uv, int64_t P, int64_t HWi,
                                  const float* __restrict__ d_out, float* __restrict__ d_tex,
                                  float2* __restrict__ d_uv) {
-  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= P) return;
+  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool on = pix0 < P;
+  const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
+  const int lane = threadIdx.x & 31;
   const float2 t = __ldg(uv + pix);
   const Taps q = bilin_taps<MODE>(t.x, t.y, Wt, Ht);
   const int64_t base = tex_shared ? 0 : (pix / HWi) * Ht * Wt * C;
   const float* b = tex + base;
   float* db = d_tex + base;
+  const float* g = d_out + pix * C;
+  scatter_tap(db + q.a00 * C, q.w00, g, 1.0f, C, on, lane);
+  scatter_tap(db + q.a10 * C, q.w10, g, 1.0f, C, on, lane);
+  scatter_tap(db + q.a01 * C, q.w01, g, 1.0f, C, on, lane);
+  scatter_tap(db + q.a11 * C, q.w11, g, 1.0f, C, on, lane);
+  if (!on) return;
   const float fx = q.fx, fy = q.fy;
   float dfx_sum = 0.0f, dfy_sum = 0.0f;
   for (int c = 0; c < C; ++c) {
-    const float g = __ldg(d_out + pix * C + c);
-    atomicAdd(db + q.a00 * C + c, q.w00 * g);
-    atomicAdd(db + q.a10 * C + c, q.w10 * g);
-    atomicAdd(db + q.a01 * C + c, q.w01 * g);
-    atomicAdd(db + q.a11 * C + c, q.w11 * g);
+    const float gc = __ldg(g + c);
     const float t00 = __ldg(b + q.a00 * C + c) * q.m00, t10 = __ldg(b + q.a10 * C + c) * q.m10;
     const float t01 = __ldg(b + q.a01 * C + c) * q.m01, t11 = __ldg(b + q.a11 * C + c) * q.m11;
-    dfx_sum += g * ((1.0f - fy) * (t10 - t00) + fy * (t11 - t01));
-    dfy_sum += g * ((1.0f - fx) * (t01 - t00) + fx * (t11 - t10));
+    dfx_sum += gc * ((1.0f - fy) * (t10 - t00) + fy * (t11 - t01));
+    dfy_sum += gc * ((1.0f - fx) * (t01 - t00) + fx * (t11 - t10));
   }
   d_uv[pix] = make_float2(dfx_sum * (float)Wt, dfy_sum * (float)Ht);
 }
@@ -153,8 +185,10 @@ __global__ void k_tex_nearest(const float* __restrict__ tex, bool tex_shared, in
                               const float2* __restrict__ uv, int64_t P, int64_t HWi,
                               float* __restrict__ out, const float* __restrict__ d_out,
                               float* __restrict__ d_tex, float2* __restrict__ d_uv) {
-  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= P) return;
+  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (out && pix0 >= P) return;  // the forward has no warp collectives
+  const bool on = pix0 < P;
+  const int64_t pix = on ? pix0 : P - 1;
   const float2 t = __ldg(uv + pix);
   const int tx = dr_floor_i(t.x * (float)Wt), ty = dr_floor_i(t.y * (float)Ht);
   float ox, oy;
@@ -164,8 +198,9 @@ __global__ void k_tex_nearest(const float* __restrict__ tex, bool tex_shared, in
   if (out) {
     for (int c = 0; c < C; ++c) out[pix * C + c] = __ldg(tex + base + c) * mask;
   } else {
-    for (int c = 0; c < C; ++c) atomicAdd(d_tex + base + c, __ldg(d_out + pix * C + c) * mask);
-    d_uv[pix] = make_float2(0.0f, 0.0f);
+    // d_tex += g * mask: the tap weight is the mask (Texture.swift:576-605).
+    scatter_tap(d_tex + base, mask, d_out + pix * C, 1.0f, C, on, threadIdx.x & 31);
+    if (on) d_uv[pix] = make_float2(0.0f, 0.0f);
   }
 }
 
@@ -194,8 +229,10 @@ __global__ void k_tex_cube(const float* __restrict__ tex, bool tex_shared, int H
                            const float* __restrict__ dir, int64_t P, int64_t HWi, float* __restrict__ out,
                            const float* __restrict__ d_out, float* __restrict__ d_tex,
                            float* __restrict__ d_dir) {
-  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= P) return;
+  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (out && pix0 >= P) return;  // the forward has no warp collectives
+  const bool on = pix0 < P;
+  const int64_t pix = on ? pix0 : P - 1;
   const float x = __ldg(dir + 3 * pix), y = __ldg(dir + 3 * pix + 1), z = __ldg(dir + 3 * pix + 2);
   int face;
   float u, v;
@@ -213,15 +250,14 @@ __global__ void k_tex_cube(const float* __restrict__ tex, bool tex_shared, int H
       out[pix * C + c] = w00 * t00 + w10 * t10 + w01 * t01 + w11 * t11;
     }
   } else {
-    for (int c = 0; c < C; ++c) {
-      const float g = __ldg(d_out + pix * C + c);
-      atomicAdd(d_tex + fb + q.a00 * C + c, w00 * g);
-      atomicAdd(d_tex + fb + q.a10 * C + c, w10 * g);
-      atomicAdd(d_tex + fb + q.a01 * C + c, w01 * g);
-      atomicAdd(d_tex + fb + q.a11 * C + c, w11 * g);
-    }
+    const int lane = threadIdx.x & 31;
+    const float* g = d_out + pix * C;
+    scatter_tap(d_tex + fb + q.a00 * C, w00, g, 1.0f, C, on, lane);
+    scatter_tap(d_tex + fb + q.a10 * C, w10, g, 1.0f, C, on, lane);
+    scatter_tap(d_tex + fb + q.a01 * C, w01, g, 1.0f, C, on, lane);
+    scatter_tap(d_tex + fb + q.a11 * C, w11, g, 1.0f, C, on, lane);
     // d_dir is identically zero in the reference (Texture.swift:196-197).
-    d_dir[3 * pix] = 0.0f; d_dir[3 * pix + 1] = 0.0f; d_dir[3 * pix + 2] = 0.0f;
+    if (on) { d_dir[3 * pix] = 0.0f; d_dir[3 * pix + 1] = 0.0f; d_dir[3 * pix + 2] = 0.0f; }
   }
 }
 
@@ -308,8 +344,10 @@ __global__ void k_tex_mip_fwd(const float* __restrict__ tex, const float* __rest
                               bool tex_shared, int C, const float2* __restrict__ uv,
                               const float4* __restrict__ uv_da, float bias, const float* __restrict__ bias_map,
                               int64_t P, int64_t HWi, float* __restrict__ out) {
-  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= P) return;
+  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool on = pix0 < P;
+  const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
+  const int lane = threadIdx.x & 31;
   const int64_t nt = tex_shared ? 0 : pix / HWi;
   float s;
   const float4 e = effective_da(__ldg(uv_da + pix), pix, bias, bias_map, s);
@@ -336,8 +374,10 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
                               int64_t P, int64_t HWi, const float* __restrict__ d_out,
                               float* __restrict__ d_tex, float* __restrict__ d_pyr, float2* __restrict__ d_uv,
                               float4* __restrict__ d_uv_da, float* __restrict__ d_bias_map) {
-  int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= P) return;
+  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool on = pix0 < P;
+  const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
+  const int lane = threadIdx.x & 31;
   const int64_t nt = tex_shared ? 0 : pix / HWi;
   float s;
   const float4 e = effective_da(__ldg(uv_da + pix), pix, bias, bias_map, s);
@@ -355,14 +395,13 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
     float* db = (k == 0 ? d_tex : d_pyr + m.off[k]) + nt * (int64_t)m.h[k] * m.w[k] * C;
     float dfx = 0.0f, dfy = 0.0f;
     const float fx = q.fx, fy = q.fy;
+    const bool tap_on = on && scale != 0.0f;
+    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, tap_on, lane);
+    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, tap_on, lane);
+    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, tap_on, lane);
+    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, tap_on, lane);
     for (int c = 0; c < C; ++c) {
       const float gc = __ldg(g + c) * scale;
-      if (gc != 0.0f) {
-        atomicAdd(db + q.a00 * C + c, q.w00 * gc);
-        atomicAdd(db + q.a10 * C + c, q.w10 * gc);
-        atomicAdd(db + q.a01 * C + c, q.w01 * gc);
-        atomicAdd(db + q.a11 * C + c, q.w11 * gc);
-      }
       const float t00 = __ldg(b + q.a00 * C + c) * q.m00, t10 = __ldg(b + q.a10 * C + c) * q.m10;
       const float t01 = __ldg(b + q.a01 * C + c) * q.m01, t11 = __ldg(b + q.a11 * C + c) * q.m11;
       dfx += gc * ((1.0f - fy) * (t10 - t00) + fy * (t11 - t01));
@@ -371,6 +410,7 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
     dfx_total += dfx * (float)m.w[k];
     dfy_total += dfy * (float)m.h[k];
   }
+  if (!on) return;
   d_uv[pix] = make_float2(dfx_total, dfy_total);
 
   if (!d_uv_da && !d_bias_map) return;
