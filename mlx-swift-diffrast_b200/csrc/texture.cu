@@ -102,15 +102,49 @@ __device__ __forceinline__ float sample4(const float* __restrict__ b, const Taps
   return q.w00 * t00 + q.w10 * t10 + q.w01 * t01 + q.w11 * t11;
 }
 
+// Per-CTA cache of "hot" texels for the d_tex scatter: a warp whose 32 lanes
+// all hit one texel (typically background pixels that share one sample
+// point) adds its sum here instead of to global memory, so the many warps of
+// a CTA that hit the same texel issue one global atomic per channel between
+// them.  8 direct-mapped slots keyed by the destination address, C <= 4.
+constexpr int kHotSlots = 8, kHotC = 4;
+struct HotCache {
+  unsigned long long key[kHotSlots];
+  float val[kHotSlots][kHotC];
+};
+
+__device__ __forceinline__ void hot_init(HotCache* hc) {
+  if (threadIdx.x < kHotSlots) {
+    hc->key[threadIdx.x] = 0ull;
+#pragma unroll
+    for (int c = 0; c < kHotC; ++c) hc->val[threadIdx.x][c] = 0.0f;
+  }
+}
+
+// After every warp's last scatter_tap (a CTA barrier first): one atomic per
+// cached texel and channel.
+__device__ __forceinline__ void hot_flush(HotCache* hc, int C) {
+  __syncthreads();
+  if (threadIdx.x < kHotSlots && hc->key[threadIdx.x] != 0ull) {
+    float* p = reinterpret_cast<float*>(hc->key[threadIdx.x]);
+    for (int c = 0; c < C && c < kHotC; ++c) {
+      const float v = hc->val[threadIdx.x][c];
+      if (v != 0.0f) atomicAdd(p + c, v);
+    }
+  }
+}
+
 // d_tex scatter of one tap: adds w * (g[c] * gscale) to p[c] (c < C) for
 // every lane.  Lanes of a warp that hit the same texel (runs of neighbouring
 // pixels: a magnified texture, or background pixels that all sample one
 // texel) are summed first with a segmented warp reduction, so each run issues
-// one atomic per channel instead of one per pixel; a zero contribution issues
-// none (d_tex starts at +0, and adding +-0 to +0 leaves +0).  All 32 lanes of
-// the warp must call it; lanes with on == false add nothing.
+// one atomic per channel instead of one per pixel; a run covering the whole
+// warp goes to the CTA's hot cache when one is given (C <= 4); a zero
+// contribution issues no atomic (d_tex starts at +0, and adding +-0 to +0
+// leaves +0).  All 32 lanes of the warp must call it; lanes with on == false
+// add nothing.
 __device__ __forceinline__ void scatter_tap(float* p, float w, const float* __restrict__ g, float gscale, int C,
-                                            bool on, int lane) {
+                                            bool on, int lane, HotCache* hc = nullptr) {
   const long long key = on ? (long long)(uintptr_t)p : -1ll - (long long)lane;
   bool head;
   const int seg_end = warp_runs(key, lane, head);
@@ -121,6 +155,30 @@ __device__ __forceinline__ void scatter_tap(float* p, float w, const float* __re
         const float v = w * (__ldg(g + c) * gscale);
         if (v != 0.0f) atomicAdd(p + c, v);
       }
+    return;
+  }
+  if (hc && span == 32 && C <= kHotC) {
+    // One run spans the warp: all 32 lanes are on and share p.
+    float sum[kHotC];
+#pragma unroll
+    for (int c = 0; c < kHotC; ++c) {
+      float v = c < C ? w * (__ldg(g + c) * gscale) : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      sum[c] = v;
+    }
+    if (lane == 0) {
+      const unsigned long long k = (unsigned long long)(uintptr_t)p;
+      const int slot = (int)((k >> 4) % kHotSlots);
+      const unsigned long long prev = atomicCAS(&hc->key[slot], 0ull, k);
+      if (prev == 0ull || prev == k) {
+        for (int c = 0; c < C; ++c)
+          if (sum[c] != 0.0f) atomicAdd(&hc->val[slot][c], sum[c]);
+      } else {
+        for (int c = 0; c < C; ++c)
+          if (sum[c] != 0.0f) atomicAdd(p + c, sum[c]);
+      }
+    }
     return;
   }
   for (int c = 0; c < C; ++c) {
@@ -161,10 +219,14 @@ __global__ void k_tex_linear_bwd(const float* __restrict__ tex, bool tex_shared,
   const float* b = tex + base;
   float* db = d_tex + base;
   const float* g = d_out + pix * C;
-  scatter_tap(db + q.a00 * C, q.w00, g, 1.0f, C, on, lane);
-  scatter_tap(db + q.a10 * C, q.w10, g, 1.0f, C, on, lane);
-  scatter_tap(db + q.a01 * C, q.w01, g, 1.0f, C, on, lane);
-  scatter_tap(db + q.a11 * C, q.w11, g, 1.0f, C, on, lane);
+  __shared__ HotCache hc;
+  hot_init(&hc);
+  __syncthreads();
+  scatter_tap(db + q.a00 * C, q.w00, g, 1.0f, C, on, lane, &hc);
+  scatter_tap(db + q.a10 * C, q.w10, g, 1.0f, C, on, lane, &hc);
+  scatter_tap(db + q.a01 * C, q.w01, g, 1.0f, C, on, lane, &hc);
+  scatter_tap(db + q.a11 * C, q.w11, g, 1.0f, C, on, lane, &hc);
+  hot_flush(&hc, C);
   if (!on) return;
   const float fx = q.fx, fy = q.fy;
   float dfx_sum = 0.0f, dfy_sum = 0.0f;
@@ -252,10 +314,14 @@ __global__ void k_tex_cube(const float* __restrict__ tex, bool tex_shared, int H
   } else {
     const int lane = threadIdx.x & 31;
     const float* g = d_out + pix * C;
-    scatter_tap(d_tex + fb + q.a00 * C, w00, g, 1.0f, C, on, lane);
-    scatter_tap(d_tex + fb + q.a10 * C, w10, g, 1.0f, C, on, lane);
-    scatter_tap(d_tex + fb + q.a01 * C, w01, g, 1.0f, C, on, lane);
-    scatter_tap(d_tex + fb + q.a11 * C, w11, g, 1.0f, C, on, lane);
+    __shared__ HotCache hc;
+    hot_init(&hc);
+    __syncthreads();
+    scatter_tap(d_tex + fb + q.a00 * C, w00, g, 1.0f, C, on, lane, &hc);
+    scatter_tap(d_tex + fb + q.a10 * C, w10, g, 1.0f, C, on, lane, &hc);
+    scatter_tap(d_tex + fb + q.a01 * C, w01, g, 1.0f, C, on, lane, &hc);
+    scatter_tap(d_tex + fb + q.a11 * C, w11, g, 1.0f, C, on, lane, &hc);
+    hot_flush(&hc, C);
     // d_dir is identically zero in the reference (Texture.swift:196-197).
     if (on) { d_dir[3 * pix] = 0.0f; d_dir[3 * pix + 1] = 0.0f; d_dir[3 * pix + 2] = 0.0f; }
   }
@@ -386,6 +452,9 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
   const float2 t = __ldg(uv + pix);
   const float* g = d_out + pix * C;
   float dfx_total = 0.0f, dfy_total = 0.0f;
+  __shared__ HotCache hc;
+  hot_init(&hc);
+  __syncthreads();
 #pragma unroll
   for (int li = 0; li < 2; ++li) {
     const int k = li == 0 ? ls.k0 : ls.k1;
@@ -396,10 +465,10 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
     float dfx = 0.0f, dfy = 0.0f;
     const float fx = q.fx, fy = q.fy;
     const bool tap_on = on && scale != 0.0f;
-    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, tap_on, lane);
-    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, tap_on, lane);
-    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, tap_on, lane);
-    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, tap_on, lane);
+    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, tap_on, lane, &hc);
+    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, tap_on, lane, &hc);
+    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, tap_on, lane, &hc);
+    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, tap_on, lane, &hc);
     for (int c = 0; c < C; ++c) {
       const float gc = __ldg(g + c) * scale;
       const float t00 = __ldg(b + q.a00 * C + c) * q.m00, t10 = __ldg(b + q.a10 * C + c) * q.m10;
@@ -410,6 +479,7 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
     dfx_total += dfx * (float)m.w[k];
     dfy_total += dfy * (float)m.h[k];
   }
+  hot_flush(&hc, C);
   if (!on) return;
   d_uv[pix] = make_float2(dfx_total, dfy_total);
 
