@@ -522,22 +522,22 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
 
 // d_tex[level 0] += sum_k d_pyr_k[y >> k, x >> k] / 4^k: the adjoint of the
 // 2x2 mean pyramid, evaluated in one pass over level 0.
-__global__ void k_mip_fold(float* __restrict__ d_tex, const float* __restrict__ d_pyr, const MipDesc m, int C,
-                           int64_t n0) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n0) return;
-  const int c = (int)(i % C);
-  const int x = (int)((i / C) % m.w[0]);
-  const int64_t ny = i / ((int64_t)C * m.w[0]);
-  const int y = (int)(ny % m.h[0]);
-  const int64_t n = ny / m.h[0];
-  float acc = 0.0f, w = 1.0f;
-  for (int k = 1; k < m.L; ++k) {
-    w *= 0.25f;
-    const float* lk = d_pyr + m.off[k] + n * (int64_t)m.h[k] * m.w[k] * C;
-    acc += w * __ldg(lk + ((int64_t)(y >> k) * m.w[k] + (x >> k)) * C + c);
+__global__ void k_mip_fold(float* __restrict__ d_tex, const float* __restrict__ d_pyr, const MipDesc m, int C) {
+  // Grid (x blocks, y = level-0 row, z = texture): one thread per level-0
+  // texel, all channels, 32-bit indexing within a level.
+  const int x = blockIdx.x * blockDim.x + threadIdx.x;
+  if (x >= m.w[0]) return;
+  const int y = blockIdx.y, n = blockIdx.z;
+  float* dst = d_tex + (((int64_t)n * m.h[0] + y) * m.w[0] + x) * C;
+  for (int c = 0; c < C; ++c) {
+    float acc = 0.0f, w = 1.0f;
+    for (int k = 1; k < m.L; ++k) {
+      w *= 0.25f;
+      const float* lk = d_pyr + m.off[k] + (int64_t)n * m.h[k] * m.w[k] * C;
+      acc += w * __ldg(lk + ((y >> k) * m.w[k] + (x >> k)) * C + c);
+    }
+    dst[c] += acc;
   }
-  d_tex[i] += acc;
 }
 
 inline bool aligned(const void* p, unsigned a) { return ((uintptr_t)p & (a - 1)) == 0; }
@@ -745,9 +745,9 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   }
   DR_LAUNCHED(ctx, "tex_mip_bwd");
   if (a.m.L > 1) {
-    const int64_t n0 = (int64_t)Nt * Ht * Wt * C;
+    DR_REQUIRE(ctx, Ht <= 65535 && Nt <= 65535, "texture_bwd: mip fold supports H, N <= 65535");
     DR_TB(ctx);
-    k_mip_fold<<<grid_for(n0, 256), 256, 0, ctx->stream>>>(d_tex, dpyr, a.m, C, n0);
+    k_mip_fold<<<dim3(grid_for(Wt, 256), Ht, Nt), 256, 0, ctx->stream>>>(d_tex, dpyr, a.m, C);
     DR_LAUNCHED(ctx, "mip_fold");
   }
   return DR_OK;
