@@ -37,6 +37,7 @@ public enum DiffRast {
     public final class Context {
         let raw: OpaquePointer
         public init(device: Int32 = 0) {
+            precondition(dr_abi_version() == DR_ABI_VERSION, "libdiffrast ABI \(dr_abi_version()) != header \(DR_ABI_VERSION)")
             var p: OpaquePointer? = nil
             let st = dr_ctx_create(device, &p)
             precondition(st == DR_OK, "dr_ctx_create failed (\(st))")
@@ -174,25 +175,38 @@ public enum DiffRast {
         return topo
     }
 
+    /// Bytes of the optional per-pixel silhouette record (`antialiasWork`)
+    /// for N views of H x W pixels.
+    public static func antialiasWorkBytes(views: Int, height: Int, width: Int) -> Int {
+        Int(dr_antialias_work_bytes(Int32(views), Int32(height), Int32(width)))
+    }
+
+    /// DiffRast.antialias (Antialias.swift:90-131).  With `work` (a buffer of
+    /// `antialiasWorkBytes` bytes) the forward also records each pixel's
+    /// silhouettes, which `antialiasVJP` then replays instead of searching
+    /// again; in an MLX CustomFunction it is a hidden second output of Forward.
     public static func antialias(_ ctx: Context, _ alloc: DeviceAllocator, color: DeviceTensor, rast: DeviceTensor,
-                                 pos: DeviceTensor, tri: DeviceTensor, topologyHash: DeviceTensor? = nil) -> DeviceTensor {
+                                 pos: DeviceTensor, tri: DeviceTensor, topologyHash: DeviceTensor? = nil,
+                                 work: UnsafeMutableRawPointer? = nil) -> DeviceTensor {
         let topo = topologyHash ?? antialiasConstructTopologyHash(ctx, alloc, tri)
         let N = color.shape[0], H = color.shape[1], W = color.shape[2], C = color.shape[3]
         let out = DeviceTensor(pointer: alloc.allocate(bytes: color.count * 4), shape: color.shape)
         ctx.check(dr_antialias_fwd(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f, pos.f,
-                                   Int32(pos.shape[1]), tri.i, Int32(tri.shape[0]), topo.i, out.f), "antialias")
+                                   Int32(pos.shape[1]), tri.i, Int32(tri.shape[0]), topo.i, out.f, work),
+                  "antialias")
         return out
     }
 
     public static func antialiasVJP(_ ctx: Context, _ alloc: DeviceAllocator, color: DeviceTensor, rast: DeviceTensor,
                                     pos: DeviceTensor, tri: DeviceTensor, topologyHash: DeviceTensor,
-                                    dOut: DeviceTensor) -> (dColor: DeviceTensor, dPos: DeviceTensor) {
+                                    dOut: DeviceTensor,
+                                    work: UnsafeRawPointer? = nil) -> (dColor: DeviceTensor, dPos: DeviceTensor) {
         let N = color.shape[0], H = color.shape[1], W = color.shape[2], C = color.shape[3]
         let dColor = DeviceTensor(pointer: alloc.allocate(bytes: color.count * 4), shape: color.shape)
         let dPos = DeviceTensor(pointer: alloc.allocate(bytes: pos.count * 4), shape: pos.shape)
         ctx.check(dr_antialias_bwd(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f, pos.f,
                                    Int32(pos.shape[1]), tri.i, Int32(tri.shape[0]), topologyHash.i, dOut.f,
-                                   dColor.f, dPos.f), "antialias VJP")
+                                   dColor.f, dPos.f, work), "antialias VJP")
         return (dColor, dPos)
     }
 }
