@@ -146,6 +146,29 @@ public enum DiffRast {
         return out
     }
 
+    /// DiffRast.textureConstructMip (Texture.swift:144-161): level 0 is `tex`
+    /// itself; levels 1... are views into one pyramid buffer built on the GPU.
+    public static func textureConstructMip(_ ctx: Context, _ alloc: DeviceAllocator, _ tex: DeviceTensor,
+                                           maxLevel: Int? = nil) -> [DeviceTensor] {
+        let Nt = tex.shape[0], Ht = tex.shape[1], Wt = tex.shape[2], C = tex.shape[3]
+        let ml = Int32(maxLevel ?? -1)
+        var n: Int32 = 0, total: Int64 = 0
+        var off = [Int64](repeating: 0, count: Int(DR_MAX_MIP_LEVELS))
+        var hh = [Int32](repeating: 0, count: Int(DR_MAX_MIP_LEVELS))
+        var ww = [Int32](repeating: 0, count: Int(DR_MAX_MIP_LEVELS))
+        ctx.check(dr_texture_mip_layout(Int32(Nt), Int32(Ht), Int32(Wt), Int32(C), ml, &n, &off, &hh, &ww, &total),
+                  "textureConstructMip")
+        var levels = [tex]
+        if n <= 1 { return levels }
+        let pyr = alloc.allocate(bytes: Int(total) * 4)
+        ctx.check(dr_texture_construct_mip(ctx.raw, tex.f, Int32(Nt), Int32(Ht), Int32(Wt), Int32(C), ml,
+                                           pyr.assumingMemoryBound(to: Float.self)), "textureConstructMip")
+        for k in 1..<Int(n) {
+            levels.append(DeviceTensor(pointer: pyr + Int(off[k]) * 4, shape: [Nt, Int(hh[k]), Int(ww[k]), C]))
+        }
+        return levels
+    }
+
     public static func textureVJP(_ ctx: Context, _ alloc: DeviceAllocator, _ tex: DeviceTensor, uv: DeviceTensor,
                                   uvDA: DeviceTensor?, filterMode: FilterMode, boundaryMode: BoundaryMode,
                                   mipLevelBias: Float, mipLevelBiasMap: DeviceTensor?, dOut: DeviceTensor)
