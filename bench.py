@@ -350,9 +350,13 @@ def main():
     chain = chains.CHAINS[cfg](dev, **kw)
     torch.cuda.synchronize()
 
+    # Shared-parameter gradients are summed across ranks by all-reduces that
+    # the backward launches as each gradient becomes final (overlapping the
+    # rest of the backward); the step waits for them at its end.
+    sync = D.GradSync(chain.shared_params())
+
     def allreduce():
-        if ws > 1:
-            D.allreduce_grads(chain.shared_grads())
+        sync.finish()
 
     def one_step():
         chain.zero_grad()

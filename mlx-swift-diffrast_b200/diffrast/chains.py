@@ -42,8 +42,13 @@ class Chain:
     def params(self) -> List[torch.Tensor]:
         raise NotImplementedError
 
+    def shared_params(self) -> List[torch.Tensor]:
+        """Parameters every rank holds a replica of (their gradients are summed
+        across ranks)."""
+        return self.params()
+
     def shared_grads(self) -> List[torch.Tensor]:
-        return [p for p in self.params() if p.grad is not None]
+        return [p.grad for p in self.shared_params() if p.grad is not None]
 
     def zero_grad(self):
         for p in self.params():
@@ -105,8 +110,8 @@ class Cfg2(Chain):
     def params(self):
         return [self.pos, self.rgb, self.uv, self.tex]
 
-    def shared_grads(self):
-        return [p.grad for p in (self.rgb, self.uv, self.tex) if p.grad is not None]
+    def shared_params(self):
+        return [self.rgb, self.uv, self.tex]
 
     def step(self):
         rast, _ = ops.rasterize(self.pos, self.tri, self.res, grad_db=False)
@@ -141,8 +146,8 @@ class Cfg3(Chain):
     def params(self):
         return [self.pos, self.uv, self.tex]
 
-    def shared_grads(self):
-        return [p.grad for p in (self.uv, self.tex) if p.grad is not None]
+    def shared_params(self):
+        return [self.uv, self.tex]
 
     def step(self):
         rast, db = ops.rasterize(self.pos, self.tri, self.res, grad_db=True)
@@ -187,8 +192,8 @@ class Cfg4(Chain):
     def params(self):
         return [self.base, self.attr]
 
-    def shared_grads(self):
-        return [p.grad for p in (self.base, self.attr) if p.grad is not None]
+    def shared_params(self):
+        return [self.base, self.attr]
 
     def positions(self):
         return torch.einsum("nij,vj->nvi", self.sim, self.base)
@@ -234,8 +239,8 @@ class Cfg5(Chain):
     def params(self):
         return [self.verts, self.cube]
 
-    def shared_grads(self):
-        return [p.grad for p in (self.verts, self.cube) if p.grad is not None]
+    def shared_params(self):
+        return [self.verts, self.cube]
 
     def step(self):
         n = self.mvp.shape[0]

@@ -44,6 +44,32 @@ def allreduce_grads(grads: Sequence[torch.Tensor], group=None) -> None:
         g.copy_(f)
 
 
+class GradSync:
+    """All-reduce (sum) of shared-parameter gradients overlapped with the rest
+    of the backward: a post-accumulate hook on each parameter launches an
+    asynchronous all-reduce as soon as that gradient is final (e.g. the
+    attribute table's, while the rasterizer's VJP still runs), and `finish`
+    makes the current stream wait for all of them.  Every rank runs the same
+    graph, so the hooks fire — and the collectives are issued — in the same
+    order everywhere.  A no-op on one rank."""
+
+    def __init__(self, params: Sequence[torch.Tensor], group=None):
+        self.group = group
+        self.handles = []
+        self.active = dist.is_initialized() and dist.get_world_size(group) > 1
+        if self.active:
+            for p in params:
+                p.register_post_accumulate_grad_hook(self._launch)
+
+    def _launch(self, p: torch.Tensor) -> None:
+        self.handles.append(dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+
+    def finish(self) -> None:
+        for h in self.handles:
+            h.wait()
+        self.handles.clear()
+
+
 def init_from_env(timeout_s: float = 300.0) -> Tuple[int, int, int]:
     """Initialise the process group from torchrun's environment; returns
     (world, rank, local_rank).  NCCL when CUDA is present, gloo otherwise."""

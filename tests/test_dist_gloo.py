@@ -46,6 +46,30 @@ def _worker_allreduce(rank, world, port, q):
         q.put((rank, "error", repr(e)))
 
 
+def _worker_gradsync(rank, world, port, q):
+    import sys
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "mlx-swift-diffrast_b200"))
+    from diffrast import dist as D
+    try:
+        _init(rank, world, port)
+        a = torch.ones(4, requires_grad=True)
+        b = torch.full((3,), 2.0, requires_grad=True)
+        sync = D.GradSync([a, b])
+        for step in range(2):  # the hooks stay registered across steps
+            a.grad = None
+            b.grad = None
+            loss = (a * (rank + 1)).sum() + (b * b * (rank + 1)).sum()
+            loss.backward()
+            sync.finish()
+        q.put((rank, a.grad.tolist(), b.grad.tolist()))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, "error", repr(e)))
+
+
 def _worker_dead_peer(rank, world, port, q):
     import time
     import torch
@@ -112,3 +136,12 @@ def test_view_range_rejects_uneven_strong_split():
     from diffrast import dist as D
     with pytest.raises(ValueError):
         D.view_range(10, 0, 3, weak=False)
+
+
+def test_gradsync_sums_gradients_as_they_finish():
+    res = _run(_worker_gradsync)
+    for r in res:
+        assert r[1] != "error", r
+    # d/da = rank + 1 summed over ranks = 3; d/db = 2 b (rank + 1) summed = 4 * 3 = 12
+    assert res[0][1] == res[1][1] == [3.0] * 4
+    assert res[0][2] == res[1][2] == [12.0] * 3
