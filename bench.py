@@ -444,7 +444,7 @@ def main():
                            "l2": "inputs larger than L2 (per-step tensors are GBs; no flush needed)"},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "gpu_launches_per_step": launches / args.steps, "clocks": clk, "kernels": kernels,
-                "loss": float(loss)}
+                "loss": float(loss.detach())}
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

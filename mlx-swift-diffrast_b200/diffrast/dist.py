@@ -77,10 +77,12 @@ def init_from_env(timeout_s: float = 300.0) -> Tuple[int, int, int]:
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1 and not dist.is_initialized():
-        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        kw = {}
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
+            kw["device_id"] = torch.device("cuda", local)
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo",
+                                timeout=datetime.timedelta(seconds=timeout_s), **kw)
     return world, rank, local
 
 
