@@ -290,6 +290,53 @@ __device__ __forceinline__ int64_t nbr_pix(int pn, int ph, int pw, int dir, int 
   return ((int64_t)pn * H + (ph + dh)) * W + (pw + dw);
 }
 
+// A device list of pixels for the two-pass kernels below.  Appends are
+// warp-aggregated, and the list is split into kListShards shards by block
+// index so the append counters are not all one contended address: block b
+// appends to shard b % kListShards, whose region holds every pixel of its
+// blocks (cap entries).  count[s] is shard s's length.
+constexpr int kListShards = 64;
+
+struct PixList {
+  unsigned long long* count;
+  unsigned long long* list;
+  int64_t cap;
+};
+
+__device__ __forceinline__ void list_append(const PixList& L, bool want, unsigned long long entry) {
+  const unsigned m = __ballot_sync(0xffffffffu, want);
+  if (!m) return;
+  const int lane = threadIdx.x & 31, leader = __ffs(m) - 1;
+  const int sh = (int)(blockIdx.x % kListShards);
+  unsigned long long base = 0;
+  if (lane == leader) base = atomicAdd(L.count + sh, (unsigned long long)__popc(m));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (want) L.list[sh * L.cap + (int64_t)base + __popc(m & ((1u << lane) - 1u))] = entry;
+}
+
+// Consumer side: the shards' exclusive prefix in shared memory (all threads
+// of the block call it); returns the total.
+__device__ __forceinline__ unsigned long long list_prefix(const PixList& L, unsigned long long* s_pre) {
+  if (threadIdx.x == 0) {
+    unsigned long long acc = 0;
+    for (int sh = 0; sh < kListShards; ++sh) { s_pre[sh] = acc; acc += L.count[sh]; }
+    s_pre[kListShards] = acc;
+  }
+  __syncthreads();
+  return s_pre[kListShards];
+}
+
+// Entry i of the concatenated shards.
+__device__ __forceinline__ unsigned long long list_get(const PixList& L, const unsigned long long* s_pre,
+                                                       unsigned long long i) {
+  int lo = 0, hi = kListShards - 1;  // the last shard with s_pre[sh] <= i
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_pre[mid] <= i) lo = mid; else hi = mid - 1;
+  }
+  return L.list[lo * L.cap + (int64_t)(i - s_pre[lo])];
+}
+
 // Forward in two passes, so the rare silhouette search runs at full occupancy
 // instead of holding up whole warps and blocks:
 //   k_aa_fwd_scan   every pixel finds its candidate directions with one round
@@ -303,8 +350,7 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
                                                      const float4* __restrict__ rast, int T,
                                                      const int32_t* __restrict__ topo, float* __restrict__ out,
                                                      float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
-                                                     unsigned long long* __restrict__ list,
-                                                     unsigned long long* __restrict__ count, unsigned* err) {
+                                                     const PixList L, unsigned* err) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = pix < (int64_t)N * H * W;
   const float* cp = color + pix * C;
@@ -319,14 +365,7 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
     const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
     cand = sil_candidates(rast, topo, H, W, T, pn, ph, pw, rast_tri(rast, pix, T, err), err);
   }
-  const unsigned m = __ballot_sync(0xffffffffu, cand != 0u);
-  if (m) {
-    const int lane = threadIdx.x & 31, leader = __ffs(m) - 1;
-    unsigned long long base = 0;
-    if (lane == leader) base = atomicAdd(count, (unsigned long long)__popc(m));
-    base = __shfl_sync(0xffffffffu, base, leader);
-    if (cand) list[base + __popc(m & ((1u << lane) - 1u))] = ((unsigned long long)pix << 4) | cand;
-  }
+  list_append(L, cand != 0u, ((unsigned long long)pix << 4) | cand);
   if (!valid || cand) return;
   if (WORK) {
     work_beta[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -351,12 +390,12 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
                                                       const int32_t* __restrict__ tri, int T,
                                                       const int32_t* __restrict__ topo, float* __restrict__ out,
                                                       float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
-                                                      const unsigned long long* __restrict__ list,
-                                                      const unsigned long long* __restrict__ count, unsigned* err) {
-  const unsigned long long n = *count;
+                                                      const PixList L, unsigned* err) {
+  __shared__ unsigned long long s_pre[kListShards + 1];
+  const unsigned long long n = list_prefix(L, s_pre);
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const unsigned long long e = list[i];
+    const unsigned long long e = list_get(L, s_pre, i);
     const int64_t pix = (int64_t)(e >> 4);
     const unsigned cand = (unsigned)(e & 15u);
     const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
@@ -499,9 +538,7 @@ __device__ __forceinline__ void aa_dcolor(const float* __restrict__ d_out, float
 __global__ void __launch_bounds__(256) k_aa_bwd_gather(int N, int H, int W, int C,
                                                        const float* __restrict__ d_out, float* __restrict__ d_color,
                                                        const float4* __restrict__ work_beta,
-                                                       const uint8_t* __restrict__ work_code,
-                                                       unsigned long long* __restrict__ list,
-                                                       unsigned long long* __restrict__ count) {
+                                                       const uint8_t* __restrict__ work_code, const PixList L) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = pix < (int64_t)N * H * W;
   unsigned code = 0;
@@ -526,26 +563,19 @@ __global__ void __launch_bounds__(256) k_aa_bwd_gather(int N, int H, int W, int 
     }
     aa_dcolor(d_out, d_color, C, pix, keep, nbeta, nsrc);
   }
-  const unsigned m = __ballot_sync(0xffffffffu, code != 0u);
-  if (m) {
-    const int lane = threadIdx.x & 31, leader = __ffs(m) - 1;
-    unsigned long long base = 0;
-    if (lane == leader) base = atomicAdd(count, (unsigned long long)__popc(m));
-    base = __shfl_sync(0xffffffffu, base, leader);
-    if (code) list[base + __popc(m & ((1u << lane) - 1u))] = ((unsigned long long)pix << 8) | code;
-  }
+  list_append(L, code != 0u, ((unsigned long long)pix << 8) | code);
 }
 
 template <bool VEC, bool XF>
 __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_edges(
     const float* __restrict__ color, int N, int H, int W, int C, const float4* __restrict__ rast,
     const float* __restrict__ pos, const float* __restrict__ xform, int V, const int32_t* __restrict__ tri, int T,
-    const float* __restrict__ d_out, float* __restrict__ d_pos, const unsigned long long* __restrict__ list,
-    const unsigned long long* __restrict__ count, unsigned* err) {
-  const unsigned long long n = *count;
+    const float* __restrict__ d_out, float* __restrict__ d_pos, const PixList L, unsigned* err) {
+  __shared__ unsigned long long s_pre[kListShards + 1];
+  const unsigned long long n = list_prefix(L, s_pre);
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const unsigned long long e = list[i];
+    const unsigned long long e = list_get(L, s_pre, i);
     const int64_t pix = (int64_t)(e >> 8);
     const unsigned code = (unsigned)(e & 255u);
     const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
@@ -652,14 +682,18 @@ extern "C" dr_status dr_antialias_construct_topology_hash(dr_ctx* ctx, const int
 
 namespace {
 
-// Candidate list in the WS_AA slot: a 64-bit count, then one 64-bit entry per
-// listed pixel (at most one per pixel).
-dr_status aa_list(dr_ctx* ctx, int64_t P, unsigned long long** count, unsigned long long** list) {
-  char* w = (char*)ws_get(ctx, WS_AA, 16 + sizeof(unsigned long long) * (size_t)P);
+// Pixel list in the WS_AA slot: kListShards 64-bit counts, then the shards,
+// each with room for every pixel of its blocks (see PixList).
+dr_status aa_list(dr_ctx* ctx, int64_t P, PixList* L) {
+  const int64_t nblocks = (P + 255) / 256;
+  const int64_t cap = (nblocks + kListShards - 1) / kListShards * 256;
+  const size_t head = sizeof(unsigned long long) * kListShards;
+  char* w = (char*)ws_get(ctx, WS_AA, head + sizeof(unsigned long long) * (size_t)(cap * kListShards));
   if (!w) return DR_ENOMEM;
-  *count = reinterpret_cast<unsigned long long*>(w);
-  *list = reinterpret_cast<unsigned long long*>(w + 16);
-  DR_CUDA(ctx, cudaMemsetAsync(w, 0, sizeof(unsigned long long), ctx->stream), "antialias list");
+  L->count = reinterpret_cast<unsigned long long*>(w);
+  L->list = reinterpret_cast<unsigned long long*>(w + head);
+  L->cap = cap;
+  DR_CUDA(ctx, cudaMemsetAsync(w, 0, head, ctx->stream), "antialias list");
   return DR_OK;
 }
 
@@ -679,20 +713,20 @@ dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, co
   const float4* r4 = reinterpret_cast<const float4*>(rast);
   float4* wb = reinterpret_cast<float4*>(work);
   uint8_t* wc = work ? reinterpret_cast<uint8_t*>(work) + (size_t)P * 16 : nullptr;
-  unsigned long long *cnt = nullptr, *list = nullptr;
-  if ((st = aa_list(ctx, P, &cnt, &list)) != DR_OK) return st;
+  PixList L;
+  if ((st = aa_list(ctx, P, &L)) != DR_OK) return st;
   DR_TB(ctx);
   if (work)
-    k_aa_fwd_scan<true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, T, topo, out, wb, wc,
-                                                                    list, cnt, ctx->d_err);
+    k_aa_fwd_scan<true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, T, topo, out, wb, wc, L,
+                                                                    ctx->d_err);
   else
-    k_aa_fwd_scan<false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, T, topo, out, wb, wc,
-                                                                     list, cnt, ctx->d_err);
+    k_aa_fwd_scan<false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, T, topo, out, wb, wc, L,
+                                                                     ctx->d_err);
   DR_LAUNCHED(ctx, "aa_fwd");
   DR_TB(ctx);
 #define DR_AF(XFV, WV, XP)                                                                                       \
   k_aa_fwd_edges<XFV, WV><<<list_grid(ctx, P), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T,  \
-                                                                      topo, out, wb, wc, list, cnt, ctx->d_err)
+                                                                      topo, out, wb, wc, L, ctx->d_err)
   if (xform) {
     if (work) DR_AF(true, true, xform); else DR_AF(true, false, xform);
   } else {
@@ -719,15 +753,15 @@ dr_status aa_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, co
   if (xform) DR_REQUIRE(ctx, aligned16(d_pos), "antialias_xf_bwd: d_verts must be 16-byte aligned");
   const bool vec = xform || aligned16(d_pos);
   if (work) {
-    unsigned long long *cnt = nullptr, *list = nullptr;
-    if ((st = aa_list(ctx, P, &cnt, &list)) != DR_OK) return st;
+    PixList L;
+    if ((st = aa_list(ctx, P, &L)) != DR_OK) return st;
     DR_TB(ctx);
-    k_aa_bwd_gather<<<grid_for(P, 256), 256, 0, ctx->stream>>>(N, H, W, C, d_out, d_color, wb, wc, list, cnt);
+    k_aa_bwd_gather<<<grid_for(P, 256), 256, 0, ctx->stream>>>(N, H, W, C, d_out, d_color, wb, wc, L);
     DR_LAUNCHED(ctx, "aa_bwd");
     DR_TB(ctx);
 #define DR_AE(VECV, XFV, XP)                                                                                     \
   k_aa_bwd_edges<VECV, XFV><<<list_grid(ctx, P), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T, \
-                                                                        d_out, d_pos, list, cnt, ctx->d_err)
+                                                                        d_out, d_pos, L, ctx->d_err)
     if (xform) DR_AE(true, true, xform);
     else if (vec) DR_AE(true, false, nullptr);
     else DR_AE(false, false, nullptr);
