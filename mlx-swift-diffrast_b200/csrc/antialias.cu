@@ -314,29 +314,6 @@ __device__ __forceinline__ void list_append(const PixList& L, bool want, unsigne
   if (want) L.list[sh * L.cap + (int64_t)base + __popc(m & ((1u << lane) - 1u))] = entry;
 }
 
-// Consumer side: the shards' exclusive prefix in shared memory (all threads
-// of the block call it); returns the total.
-__device__ __forceinline__ unsigned long long list_prefix(const PixList& L, unsigned long long* s_pre) {
-  if (threadIdx.x == 0) {
-    unsigned long long acc = 0;
-    for (int sh = 0; sh < kListShards; ++sh) { s_pre[sh] = acc; acc += L.count[sh]; }
-    s_pre[kListShards] = acc;
-  }
-  __syncthreads();
-  return s_pre[kListShards];
-}
-
-// Entry i of the concatenated shards.
-__device__ __forceinline__ unsigned long long list_get(const PixList& L, const unsigned long long* s_pre,
-                                                       unsigned long long i) {
-  int lo = 0, hi = kListShards - 1;  // the last shard with s_pre[sh] <= i
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s_pre[mid] <= i) lo = mid; else hi = mid - 1;
-  }
-  return L.list[lo * L.cap + (int64_t)(i - s_pre[lo])];
-}
-
 // Forward in two passes, so the rare silhouette search runs at full occupancy
 // instead of holding up whole warps and blocks:
 //   k_aa_fwd_scan   every pixel finds its candidate directions with one round
@@ -391,11 +368,12 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
                                                       const int32_t* __restrict__ topo, float* __restrict__ out,
                                                       float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
                                                       const PixList L, unsigned* err) {
-  __shared__ unsigned long long s_pre[kListShards + 1];
-  const unsigned long long n = list_prefix(L, s_pre);
+  // Grid (x, shard): the blocks of row y walk shard y.
+  const unsigned long long n = L.count[blockIdx.y];
+  const unsigned long long* sl = L.list + (int64_t)blockIdx.y * L.cap;
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const unsigned long long e = list_get(L, s_pre, i);
+    const unsigned long long e = sl[i];
     const int64_t pix = (int64_t)(e >> 4);
     const unsigned cand = (unsigned)(e & 15u);
     const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
@@ -571,11 +549,12 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_edges(
     const float* __restrict__ color, int N, int H, int W, int C, const float4* __restrict__ rast,
     const float* __restrict__ pos, const float* __restrict__ xform, int V, const int32_t* __restrict__ tri, int T,
     const float* __restrict__ d_out, float* __restrict__ d_pos, const PixList L, unsigned* err) {
-  __shared__ unsigned long long s_pre[kListShards + 1];
-  const unsigned long long n = list_prefix(L, s_pre);
+  // Grid (x, shard): the blocks of row y walk shard y.
+  const unsigned long long n = L.count[blockIdx.y];
+  const unsigned long long* sl = L.list + (int64_t)blockIdx.y * L.cap;
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const unsigned long long e = list_get(L, s_pre, i);
+    const unsigned long long e = sl[i];
     const int64_t pix = (int64_t)(e >> 8);
     const unsigned code = (unsigned)(e & 255u);
     const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
@@ -697,9 +676,11 @@ dr_status aa_list(dr_ctx* ctx, int64_t P, PixList* L) {
   return DR_OK;
 }
 
-// Grid of a grid-stride pass over a device-counted list (about 8 blocks per SM).
-inline unsigned list_grid(dr_ctx* ctx, int64_t P) {
-  return (unsigned)std::max<int64_t>(1, std::min<int64_t>((P + 255) / 256, (int64_t)ctx->num_sms * 8));
+// Grid of a grid-stride pass over a sharded list: one row of blocks per shard,
+// about 8 blocks per SM in total.
+inline dim3 list_grid(dr_ctx* ctx, int64_t P) {
+  const int64_t total = std::max<int64_t>(1, std::min<int64_t>((P + 255) / 256, (int64_t)ctx->num_sms * 8));
+  return dim3((unsigned)std::max<int64_t>(1, (total + kListShards - 1) / kListShards), kListShards);
 }
 
 dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,

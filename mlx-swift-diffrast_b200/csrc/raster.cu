@@ -37,12 +37,20 @@ constexpr int TILE_PIX = TILE * TILE;
 #define FS(a, b) __fsub_rn((a), (b))
 #define FD(a, b) __fdiv_rn((a), (b))
 
+// a / d for the image sizes d of the NDC conversions.  For a power of two
+// d = 2^k the quotient is a * 2^-k exactly (a >= 1 here, so no underflow),
+// which saves the IEEE division; otherwise the division itself.
+__device__ __forceinline__ float div_by_size(float a, int d) {
+  if ((d & (d - 1)) == 0) return FM(a, __int_as_float((127 - (__ffs(d) - 1)) << 23));
+  return FD(a, (float)d);
+}
+
 // Pixel-centre NDC exactly as Rasterize.swift:381-382 computes it.
 __device__ __forceinline__ float ndc_x_of(int pw, int W) {
-  return FS(FD(FM(2.0f, FA((float)pw, 0.5f)), (float)W), 1.0f);
+  return FS(div_by_size(FM(2.0f, FA((float)pw, 0.5f)), W), 1.0f);
 }
 __device__ __forceinline__ float ndc_y_of(int ph, int H) {
-  return FS(1.0f, FD(FM(2.0f, FA((float)ph, 0.5f)), (float)H));
+  return FS(1.0f, div_by_size(FM(2.0f, FA((float)ph, 0.5f)), H));
 }
 
 // Setup record: 48 bytes.
