@@ -457,3 +457,53 @@ def test_unused_outputs_get_no_materialised_cotangent(cu, soup):
     (o2 * w).sum().backward()
     assert torch.equal(r1, r2) and torch.equal(o1, o2)
     assert rel_l2(p1.grad.cpu().numpy(), p2.grad.cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("C", [1, 4, 5])
+@pytest.mark.parametrize("filt", ["linear", "linear-mipmap-linear", "cube"])
+def test_texture_bwd_hot_texels_and_runs(cu, filt, C):
+    # Whole warps sampling one texel (the constant-uv "background" block),
+    # long runs of neighbours sharing texels (a magnified texture) and random
+    # samples, with C = 1, 4 (the per-CTA hot-texel cache) and 5 (above it),
+    # on a pixel count that is not a multiple of the block size.
+    g = np.random.default_rng(40 + C)
+    N, H, W = 2, 67, 93
+    if filt == "cube":
+        tex = g.random((1, 6, 16, 16, C)).astype(np.float32)
+        d = g.normal(size=(N, H, W, 3)).astype(np.float32)
+        d[:, :30] = np.array([0.2, -0.1, 1.0], np.float32)            # one texel of the +z face
+        d[:, 30:50, :, 0] = np.linspace(-1, 1, W, dtype=np.float32)  # slow sweep: long runs
+        d[:, 30:50, :, 1:] = np.array([0.1, 1.0], np.float32)
+        kw = dict(boundary_mode="cube")
+        uv = d
+    else:
+        tex = g.random((1, 32, 48, C)).astype(np.float32)
+        uv = g.uniform(0, 1, size=(N, H, W, 2)).astype(np.float32)
+        uv[:, :30] = 0.0                                              # background: one sample point
+        uv[:, 30:50, :, 0] = np.linspace(0.2, 0.3, W, dtype=np.float32)  # magnified: runs of 20+ pixels
+        uv[:, 30:50, :, 1] = 0.6
+        mip = filt.startswith("linear-mipmap")
+        da = (g.normal(size=(N, H, W, 4)) * 0.01).astype(np.float32)
+        kw = dict(uv_da=da if mip else None, filter_mode=filt, boundary_mode="wrap")
+    d_out = g.normal(size=(N, H, W, C)).astype(np.float32)
+    ga = cu.texture_bwd(tex, uv, d_out, **kw)
+    gb = O.texture_bwd(tex, uv, d_out, **kw)
+    assert rel_l2(ga[0], gb[0]) < 1e-4
+
+
+def test_antialias_ragged_pixel_count(cu, soup):
+    # P = 3 * 37 * 53 is not a multiple of the block size: the last block's
+    # lanes past the end take part in the warp-aggregated list appends without
+    # adding entries.
+    pos, tri = soup
+    rast, _ = O.rasterize(pos, tri, (37, 53), grad_db=False)
+    g = np.random.default_rng(41)
+    color = g.normal(size=(3, 37, 53, 3)).astype(np.float32)
+    topo = O.topology_hash(tri)
+    a = cu.antialias(color, rast, pos, tri, topo)
+    b = O.antialias(color, rast, pos, tri, topo)
+    assert _rel_max(a, b) <= 1e-5
+    d_out = g.normal(size=a.shape).astype(np.float32)
+    ga = cu.antialias_bwd(color, rast, pos, tri, d_out, topo)
+    gb = O.antialias_bwd(color, rast, pos, tri, d_out, topo)
+    assert rel_l2(ga[0], gb[0]) < 1e-5 and rel_l2(ga[1], gb[1]) < 1e-4
