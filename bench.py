@@ -120,11 +120,12 @@ class ClockSampler:
 # stream scales with pixels, and the per-triangle records and tile lists with
 # views, i.e. also with pixels at a fixed resolution.
 NCU_DRAM_BYTES_PER_PIXEL = {
-    ("cfg4", "raster_tiles"): (120.805120e6 + 99.294464e6) / (2 * 1024 * 1024),
-    ("cfg4", "interp_fwd"): (146.003456e6 + 151.024640e6) / (2 * 1024 * 1024),
-    ("cfg4", "interp_bwd"): (244.021760e6 + 54.654464e6) / (2 * 1024 * 1024),
-    ("cfg4", "raster_bwd"): (145.058048e6 + 10.691072e6) / (2 * 1024 * 1024),
-    ("cfg4", "aa_fwd"): (124.246016e6 + 69.550336e6) / (2 * 1024 * 1024),
+    ("cfg4", "raster_tiles"): (120.786176e6 + 99.920896e6) / (2 * 1024 * 1024),
+    ("cfg4", "interp_fwd"): (151.143424e6 + 152.051968e6) / (2 * 1024 * 1024),
+    ("cfg4", "interp_bwd"): (244.010496e6 + 55.546880e6) / (2 * 1024 * 1024),
+    ("cfg4", "raster_bwd"): (145.191168e6 + 11.467264e6) / (2 * 1024 * 1024),
+    ("cfg4", "aa_fwd"): (121.620224e6 + 61.306368e6) / (2 * 1024 * 1024),
+    ("cfg4", "aa_bwd"): (102.782208e6 + 35.914240e6) / (2 * 1024 * 1024),
 }
 
 
