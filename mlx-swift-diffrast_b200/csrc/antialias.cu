@@ -444,7 +444,7 @@ __device__ __forceinline__ void aa_dir_dpos(const SilDir& s, const float* __rest
   }
   if (d_alpha == 0.0f) return;
   float dade0x, dade0y, dade1x, dade1y;
-  const float inv_denom_sq = 1.0f / (s.denom * s.denom);
+  const float inv_denom_sq = __fdividef(1.0f, s.denom * s.denom);  // gradient only: fast reciprocal
   if (s.horiz) {
     const float row_y = (float)ph + 0.5f;
     const float ex_diff = s.e1x - s.e0x;
@@ -463,7 +463,7 @@ __device__ __forceinline__ void aa_dir_dpos(const SilDir& s, const float* __rest
   const int64_t pb = XF ? 0 : (int64_t)pn * V * 4;
   {
     const float4 pv = vpos<XF>(pos, M, V, pn, s.ie0);
-    const float inv_w = 1.0f / pv.w;
+    const float inv_w = __fdividef(1.0f, pv.w);
     const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
     add_pos<VEC, XF>(d_pos + pb + (int64_t)s.ie0 * 4, M, d_alpha * dade0x * halfW * inv_w,
                      d_alpha * dade0y * (-halfH) * inv_w,
@@ -471,7 +471,7 @@ __device__ __forceinline__ void aa_dir_dpos(const SilDir& s, const float* __rest
   }
   {
     const float4 pv = vpos<XF>(pos, M, V, pn, s.ie1);
-    const float inv_w = 1.0f / pv.w;
+    const float inv_w = __fdividef(1.0f, pv.w);
     const float nd_x = pv.x * inv_w, nd_y = pv.y * inv_w;
     add_pos<VEC, XF>(d_pos + pb + (int64_t)s.ie1 * 4, M, d_alpha * dade1x * halfW * inv_w,
                      d_alpha * dade1y * (-halfH) * inv_w,

@@ -537,8 +537,8 @@ __global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const fl
       const float4 gd = __ldg(d_rast_db + pix);
       d_db0 = gd.x; d_db1 = gd.y; d_db2 = gd.z; d_db3 = gd.w;
     }
-    const float Px = 2.0f * ((float)pw + 0.5f) / (float)W - 1.0f;
-    const float Py = 1.0f - 2.0f * ((float)ph + 0.5f) / (float)H;
+    const float Px = __fdividef(2.0f * ((float)pw + 0.5f), (float)W) - 1.0f;
+    const float Py = 1.0f - __fdividef(2.0f * ((float)ph + 0.5f), (float)H);
     float4 q0 = ldg4(pos + pos_n_base + (int64_t)i0 * 4);
     float4 q1 = ldg4(pos + pos_n_base + (int64_t)i1 * 4);
     float4 q2 = ldg4(pos + pos_n_base + (int64_t)i2 * 4);
@@ -547,12 +547,14 @@ __global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const fl
       q1 = mat4_apply(M, q1);
       q2 = mat4_apply(M, q2);
     }
-    const float w0 = q0.w, w1 = q1.w, w2 = q2.w;
-    const float sx0 = q0.x / w0, sy0 = q0.y / w0, sz0 = q0.z / w0;
-    const float sx1 = q1.x / w1, sy1 = q1.y / w1, sz1 = q1.z / w1;
-    const float sx2 = q2.x / w2, sy2 = q2.y / w2, sz2 = q2.z / w2;
+    // Gradient-only arithmetic (compared within tolerance, not bit for bit):
+    // one fast reciprocal per w instead of IEEE divisions.
+    const float inv_w0 = __fdividef(1.0f, q0.w), inv_w1 = __fdividef(1.0f, q1.w), inv_w2 = __fdividef(1.0f, q2.w);
+    const float sx0 = q0.x * inv_w0, sy0 = q0.y * inv_w0, sz0 = q0.z * inv_w0;
+    const float sx1 = q1.x * inv_w1, sy1 = q1.y * inv_w1, sz1 = q1.z * inv_w1;
+    const float sx2 = q2.x * inv_w2, sy2 = q2.y * inv_w2, sz2 = q2.z * inv_w2;
     const float area = (sx1 - sx0) * (sy2 - sy0) - (sx2 - sx0) * (sy1 - sy0);
-    const float inv_area = 1.0f / area;
+    const float inv_area = __fdividef(1.0f, area);
     const float dadsx0 = sy1 - sy2, dadsx1 = sy2 - sy0, dadsx2 = sy0 - sy1;
     const float dadsy0 = sx2 - sx1, dadsy1 = sx0 - sx2, dadsy2 = sx1 - sx0;
     const float de1dsx0 = Py - sy2, de1dsx2 = sy0 - Py, de1dsy0 = sx2 - Px, de1dsy2 = Px - sx0;
@@ -599,7 +601,6 @@ __global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const fl
       dsx0 += d_db3 * (-Ky) * inv_area;
       dsx1 += d_db3 * (Ky) * inv_area;
     }
-    const float inv_w0 = 1.0f / w0, inv_w1 = 1.0f / w1, inv_w2 = 1.0f / w2;
     g0 = make_float4(dsx0 * inv_w0, dsy0 * inv_w0, dsz0_s * inv_w0,
                      -(sx0 * dsx0 + sy0 * dsy0 + sz0 * dsz0_s) * inv_w0);
     g1 = make_float4(dsx1 * inv_w1, dsy1 * inv_w1, dsz1_s * inv_w1,
@@ -610,12 +611,13 @@ __global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const fl
   bool head;
   const long long key = hit ? (long long)pn * T + t : -1ll - (long long)lane;
   const int seg_end = warp_runs(key, lane, head);
-  g0.x = warp_seg_sum(g0.x, lane, seg_end); g0.y = warp_seg_sum(g0.y, lane, seg_end);
-  g0.z = warp_seg_sum(g0.z, lane, seg_end); g0.w = warp_seg_sum(g0.w, lane, seg_end);
-  g1.x = warp_seg_sum(g1.x, lane, seg_end); g1.y = warp_seg_sum(g1.y, lane, seg_end);
-  g1.z = warp_seg_sum(g1.z, lane, seg_end); g1.w = warp_seg_sum(g1.w, lane, seg_end);
-  g2.x = warp_seg_sum(g2.x, lane, seg_end); g2.y = warp_seg_sum(g2.y, lane, seg_end);
-  g2.z = warp_seg_sum(g2.z, lane, seg_end); g2.w = warp_seg_sum(g2.w, lane, seg_end);
+  const int span = warp_max_run(lane, seg_end, head);
+  g0.x = warp_seg_sum(g0.x, lane, seg_end, span); g0.y = warp_seg_sum(g0.y, lane, seg_end, span);
+  g0.z = warp_seg_sum(g0.z, lane, seg_end, span); g0.w = warp_seg_sum(g0.w, lane, seg_end, span);
+  g1.x = warp_seg_sum(g1.x, lane, seg_end, span); g1.y = warp_seg_sum(g1.y, lane, seg_end, span);
+  g1.z = warp_seg_sum(g1.z, lane, seg_end, span); g1.w = warp_seg_sum(g1.w, lane, seg_end, span);
+  g2.x = warp_seg_sum(g2.x, lane, seg_end, span); g2.y = warp_seg_sum(g2.y, lane, seg_end, span);
+  g2.z = warp_seg_sum(g2.z, lane, seg_end, span); g2.w = warp_seg_sum(g2.w, lane, seg_end, span);
   if (!(hit && head)) return;
   if (XF) {
     g0 = mat4_apply_t(M, g0);
