@@ -78,6 +78,27 @@ def build(force: bool = False, jobs: int = 0, verbose_ptxas: bool = False) -> st
     return LIB
 
 
+DRIVER_SRC = os.path.join(PKG, "cdriver", "dr_check.cpp")
+DRIVER = os.path.join(PKG, "cdriver", "dr_check")
+
+
+def build_driver(force: bool = False) -> str:
+    """The C++ caller of the ABI (cdriver/dr_check.cpp): host compiler only,
+    linked against libdiffrast.so and the CUDA runtime."""
+    lib = build()
+    if not force and os.path.exists(DRIVER) and os.path.getmtime(DRIVER) >= max(
+            os.path.getmtime(DRIVER_SRC), os.path.getmtime(lib), *[os.path.getmtime(h) for h in _headers()]):
+        return DRIVER
+    cuda = os.path.dirname(os.path.dirname(nvcc()))
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-I" + INCLUDE, "-I" + os.path.join(cuda, "include"),
+           DRIVER_SRC, "-o", DRIVER, "-L" + os.path.dirname(lib), "-ldiffrast", "-L" + os.path.join(cuda, "lib64"),
+           "-lcudart", "-Wl,-rpath," + os.path.dirname(lib), "-Wl,-rpath,$ORIGIN/../diffrast"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"driver build failed:\n{r.stdout}\n{r.stderr}")
+    return DRIVER
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -85,3 +106,4 @@ if __name__ == "__main__":
     ap.add_argument("--ptxas-v", action="store_true", help="print register/smem usage")
     a = ap.parse_args()
     print(build(a.force, a.jobs, a.ptxas_v))
+    print(build_driver(a.force))
