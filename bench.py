@@ -37,8 +37,9 @@ WORKLOADS = {
             "mip bias, MSE; bwd d_tex(all levels)/d_uv/d_uvDA->d_pos",
     "cfg4": "1M-triangle soup (20% in edge-sharing strips), 32 views/GPU at 1024^2, 2 depth-peeled layers with rast_db, "
             "interpolate A=8 diffAttrs=.all, antialias+topology hash, MSE; bwd d_pos(->shared verts)/d_attr",
-    "cfg5": "geodesic sphere 499,280 tris, 256 views 2048^2 sharded over GPUs, cube 6x1024^2x3 (.linear), antialias, "
-            "MSE; bwd d_verts/d_tex",
+    "cfg5": "geodesic sphere 499,280 tris, 256 views 2048^2 sharded over GPUs, rast_db, normals diffAttrs=.all, "
+            "trilinear cube 6x1024^2x3 (face pyramids, LOD from the normals' derivatives), antialias, MSE; "
+            "bwd d_verts/d_tex(all levels)",
 }
 # Configurations whose per-GPU work is fixed as N grows (each rank renders the
 # configuration's full view count); cfg5 splits its 256 views over the ranks.
@@ -204,12 +205,23 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         S = 6 * 1024 * 1024 * 3 * 4
         micro = -(-n // chain.micro)
         add("raster_setup", n * V * 16 + micro * T * 12)
-        add("raster_tiles", P * 16)
-        add("interp_fwd", micro * (V * 12 + T * 12) + P * (16 + 12))
-        add("interp_bwd", micro * (2 * V * 12 + T * 12) + P * (32 + 12))
-        add("tex_cube_fwd", micro * S + P * (12 + 12))
-        add("tex_cube_bwd", micro * 2 * S + P * (12 + 12 + 12))
-        add("raster_bwd", 2 * n * V * 16 + micro * T * 12 + P * 32)
+        if chain.filter_mode == 1:  # the reference's .linear cube
+            add("raster_tiles", P * 16)
+            add("interp_fwd", micro * (V * 12 + T * 12) + P * (16 + 12))
+            add("interp_bwd", micro * (2 * V * 12 + T * 12) + P * (32 + 12))
+            add("tex_cube_fwd", micro * S + P * (12 + 12))
+            add("tex_cube_bwd", micro * 2 * S + P * (12 + 12 + 12))
+            add("raster_bwd", 2 * n * V * 16 + micro * T * 12 + P * 32)
+        else:  # trilinear: rast_db, dirDA (6 floats / px), the faces' pyramids
+            S_all = S * 4 // 3
+            add("raster_tiles", P * 32)
+            add("interp_fwd", micro * (V * 12 + T * 12) + P * (32 + 12 + 24))
+            add("interp_bwd", micro * (2 * V * 12 + T * 12) + P * (32 + 12 + 24 + 32))
+            add("mip_down", micro * (S + S // 3))
+            add("tex_cube_mip_fwd", micro * S_all + P * (12 + 24 + 12))
+            add("tex_cube_mip_bwd", micro * 2 * S_all + P * (12 + 24 + 12 + 12 + 24))
+            add("mip_fold", micro * (S_all + S))
+            add("raster_bwd", 2 * n * V * 16 + micro * T * 12 + P * (32 + 16))
         add("aa_fwd", P * (8 * 3 + 16) + n * V * 16 + micro * 2 * T * 12)
         add("aa_bwd", P * (12 * 3 + 16) + 2 * n * V * 16 + micro * 2 * T * 12)
         add("mse", P * 8 * 3)  # loss: read pred and target

@@ -215,11 +215,18 @@ DR_API dr_status dr_texture_construct_mip(dr_ctx* ctx, const float* tex, int Nt,
 /* Forward.  Replaces DiffRast.texture (Texture.swift:62-131) and kernels
  * diffrast_texture_fwd / _nearest_fwd / _cube_fwd / _trilinear_fwd.
  *   tex: [Nt, Ht, Wt, C] (Nt == 1 broadcasts) or, for DR_BOUNDARY_CUBE,
- *        [Nt, 6, Ht, Wt, C] (cube requires DR_FILTER_LINEAR, as the reference).
- *   pyramid: mip levels >= 1 from dr_texture_construct_mip, or NULL to build
- *        them internally (mipmap filters only).  max_level as in the layout.
+ *        [Nt, 6, Ht, Wt, C].  Cube takes DR_FILTER_LINEAR as the reference;
+ *        the two mipmap filters on a cube are an extension (the reference
+ *        rejects them): the pyramid is that of the Nt * 6 faces, the LOD
+ *        comes from the derivatives of the face coordinates.
+ *   pyramid: mip levels >= 1 from dr_texture_construct_mip (for a cube, of
+ *        the [Nt * 6, Ht, Wt, C] faces), or NULL to build them internally
+ *        (mipmap filters only).  max_level as in the layout.
  *   uv: [N, Hi, Wi, 2] ([N, Hi, Wi, 3] direction for cube).
- *   uv_da: [N, Hi, Wi, 4], required for the mipmap filters.
+ *   uv_da: [N, Hi, Wi, 4], required for the mipmap filters; for a cube the
+ *        direction's derivatives [N, Hi, Wi, 6] = (dx/dX, dx/dY, dy/dX,
+ *        dy/dY, dz/dX, dz/dY), interpolate's diff_attrs layout, 8-byte
+ *        aligned.
  *   mip_level_bias / mip_level_bias_map ([N, Hi, Wi] or NULL): scale uv_da by
  *        2^bias * 2^map before the LOD, as Texture.swift:104-126.
  *   out: [N, Hi, Wi, C]. */
@@ -237,7 +244,7 @@ DR_API dr_status dr_texture_fwd(dr_ctx* ctx, int filter, int boundary,
  *   d_tex: out, same shape as tex (pyramid gradients folded in).
  *   d_uv: out, shape of uv (zero for nearest; zero d_dir for cube, as
  *         Texture.swift:196-197).
- *   d_uv_da: out [N, Hi, Wi, 4] for mipmap filters, or NULL.
+ *   d_uv_da: out, shape of uv_da, for mipmap filters, or NULL.
  *   d_bias_map: out [N, Hi, Wi] gradient of the bias map, or NULL. */
 DR_API dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary,
                          const float* tex, int Nt, int Ht, int Wt, int C,

@@ -405,15 +405,50 @@ __device__ __forceinline__ const float* level_ptr(const float* tex, const float*
   return b + nt * (int64_t)m.h[k] * m.w[k] * C;
 }
 
+// K22 (Texture.swift:1011-1102): d(loss)/d(eff) of the effective uvDA through
+// the LOD, independent of MIP_LINEAR.  `img` selects the image in each level
+// (texture batch entry, or batch * 6 + face for a cube).
+template <int MODE>
+__device__ __forceinline__ float4 lod_vjp(const float4 e, const MipDesc& m, const float* __restrict__ tex,
+                                          const float* __restrict__ pyr, int64_t img, int C, float u, float v,
+                                          const float* __restrict__ g) {
+  const int Ht = m.h[0], Wt = m.w[0], L = m.L;
+  const float sx = e.x * (float)Wt, sy = e.y * (float)Wt;
+  const float tx_ = e.z * (float)Ht, ty_ = e.w * (float)Ht;
+  const float Asq = sx * sx + tx_ * tx_, Bsq = sy * sy + ty_ * ty_;
+  const float rho_sq = fmaxf(Asq, Bsq);
+  const float lod_raw = 0.5f * log2_rn(fmaxf(rho_sq, 1e-20f));
+  float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (lod_raw <= 0.0f || lod_raw >= (float)(L - 1)) return g4;
+  const int k0 = dr_floor_i(lod_raw);
+  int k1 = k0 + 1;
+  if (k1 >= L) k1 = L - 1;
+  float d_lod = 0.0f;
+  for (int li = 0; li < 2; ++li) {
+    const int k = li == 0 ? k0 : k1;
+    const float sign = li == 0 ? -1.0f : 1.0f;
+    const Taps q = bilin_taps<MODE>(u, v, m.w[k], m.h[k]);
+    const float* b = level_ptr(tex, pyr, m, k, img, C);
+    for (int c = 0; c < C; ++c) d_lod += sign * sample4(b, q, C, c) * __ldg(g + c);
+  }
+  const float ln2 = 0.6931471805599453f;
+  const float dlod_drho_sq = 1.0f / (2.0f * rho_sq * ln2);
+  const float A_is_max = (Asq >= Bsq) ? 1.0f : 0.0f;
+  const float B_is_max = 1.0f - A_is_max;
+  g4.x = d_lod * dlod_drho_sq * A_is_max * 2.0f * sx * (float)Wt;
+  g4.y = d_lod * dlod_drho_sq * B_is_max * 2.0f * sy * (float)Wt;
+  g4.z = d_lod * dlod_drho_sq * A_is_max * 2.0f * tx_ * (float)Ht;
+  g4.w = d_lod * dlod_drho_sq * B_is_max * 2.0f * ty_ * (float)Ht;
+  return g4;
+}
+
 template <int MODE, bool MIP_LINEAR>
 __global__ void k_tex_mip_fwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
                               bool tex_shared, int C, const float2* __restrict__ uv,
                               const float4* __restrict__ uv_da, float bias, const float* __restrict__ bias_map,
                               int64_t P, int64_t HWi, float* __restrict__ out) {
-  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const bool on = pix0 < P;
-  const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
-  const int lane = threadIdx.x & 31;
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= P) return;  // no warp collectives
   const int64_t nt = tex_shared ? 0 : pix / HWi;
   float s;
   const float4 e = effective_da(__ldg(uv_da + pix), pix, bias, bias_map, s);
@@ -484,36 +519,159 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
   d_uv[pix] = make_float2(dfx_total, dfy_total);
 
   if (!d_uv_da && !d_bias_map) return;
-  // K22 (Texture.swift:1011-1102): independent of MIP_LINEAR.
-  const float sx = e.x * (float)Wt, sy = e.y * (float)Wt;
-  const float tx_ = e.z * (float)Ht, ty_ = e.w * (float)Ht;
-  const float Asq = sx * sx + tx_ * tx_, Bsq = sy * sy + ty_ * ty_;
-  const float rho_sq = fmaxf(Asq, Bsq);
-  const float lod_raw = 0.5f * log2_rn(fmaxf(rho_sq, 1e-20f));
-  float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (!(lod_raw <= 0.0f || lod_raw >= (float)(L - 1))) {
-    const int k0 = dr_floor_i(lod_raw);
-    int k1 = k0 + 1;
-    if (k1 >= L) k1 = L - 1;
-    float d_lod = 0.0f;
-    for (int li = 0; li < 2; ++li) {
-      const int k = li == 0 ? k0 : k1;
-      const float sign = li == 0 ? -1.0f : 1.0f;
-      const Taps q = bilin_taps<MODE>(t.x, t.y, m.w[k], m.h[k]);
-      const float* b = level_ptr(tex, pyr, m, k, nt, C);
-      for (int c = 0; c < C; ++c) d_lod += sign * sample4(b, q, C, c) * __ldg(g + c);
-    }
-    const float ln2 = 0.6931471805599453f;
-    const float dlod_drho_sq = 1.0f / (2.0f * rho_sq * ln2);
-    const float A_is_max = (Asq >= Bsq) ? 1.0f : 0.0f;
-    const float B_is_max = 1.0f - A_is_max;
-    g4.x = d_lod * dlod_drho_sq * A_is_max * 2.0f * sx * (float)Wt;
-    g4.y = d_lod * dlod_drho_sq * B_is_max * 2.0f * sy * (float)Wt;
-    g4.z = d_lod * dlod_drho_sq * A_is_max * 2.0f * tx_ * (float)Ht;
-    g4.w = d_lod * dlod_drho_sq * B_is_max * 2.0f * ty_ * (float)Ht;
-  }
+  const float4 g4 = lod_vjp<MODE>(e, m, tex, pyr, nt, C, t.x, t.y, g);
   // Backward of eff = uvDA * s: d_uvDA = g * s, d_map = ln2 * sum(g * eff).
   if (d_uv_da) d_uv_da[pix] = make_float4(g4.x * s, g4.y * s, g4.z * s, g4.w * s);
+  if (d_bias_map) {
+    const float acc = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
+    d_bias_map[pix] = bias_map ? acc * 0.6931471805599453f : 0.0f;
+  }
+}
+
+// ------------------------------------------------------- mip-mapped cube
+// Extension (the reference's cube path samples level 0 with .linear only):
+// the pyramid of the Nt * 6 faces, LOD from the screen-space derivatives of
+// the face coordinates, per-level per-face clamp bilinear.  d_dir = 0 as the
+// reference's cube VJP; dirDA gets the LOD gradient.
+
+// Face of a direction with its (s, t, major) axes and signs, chosen as
+// cube_project chooses them: sc = ss * d[sa], tc = ts * d[ta], ma = ms * d[ma].
+struct CubeFrame {
+  int face, sa, ta, ma;
+  float ss, ts, ms, sc, tc, inv_ma, u, v;
+};
+
+__device__ __forceinline__ float pick3(int a, float x, float y, float z) { return a == 0 ? x : (a == 1 ? y : z); }
+
+__device__ __forceinline__ CubeFrame cube_frame(float x, float y, float z) {
+  CubeFrame f;
+  cube_project(x, y, z, f.face, f.u, f.v);
+  // Faces +X,-X,+Y,-Y,+Z,-Z: sc = (-z, z, x, x, x, -x), tc = (-y, -y, z, -z, -y, -y).
+  switch (f.face) {
+    case 0: f.sa = 2; f.ta = 1; f.ma = 0; f.ss = -1.f; f.ts = -1.f; f.ms = 1.f; break;
+    case 1: f.sa = 2; f.ta = 1; f.ma = 0; f.ss = 1.f; f.ts = -1.f; f.ms = -1.f; break;
+    case 2: f.sa = 0; f.ta = 2; f.ma = 1; f.ss = 1.f; f.ts = 1.f; f.ms = 1.f; break;
+    case 3: f.sa = 0; f.ta = 2; f.ma = 1; f.ss = 1.f; f.ts = -1.f; f.ms = -1.f; break;
+    case 4: f.sa = 0; f.ta = 1; f.ma = 2; f.ss = 1.f; f.ts = -1.f; f.ms = 1.f; break;
+    default: f.sa = 0; f.ta = 1; f.ma = 2; f.ss = -1.f; f.ts = -1.f; f.ms = -1.f; break;
+  }
+  f.sc = f.ss * pick3(f.sa, x, y, z);
+  f.tc = f.ts * pick3(f.ta, x, y, z);
+  f.inv_ma = 1.0f / (f.ms * pick3(f.ma, x, y, z));
+  return f;
+}
+
+// Per-pixel direction derivatives, interpolate's interleaved layout:
+// [dx/dX, dx/dY, dy/dX, dy/dY, dz/dX, dz/dY].
+struct DirDA {
+  float2 a[3];  // a[axis] = (d/dX, d/dY)
+};
+
+__device__ __forceinline__ float2 pick_axis(const DirDA& d, int a) {
+  return a == 0 ? d.a[0] : (a == 1 ? d.a[1] : d.a[2]);
+}
+
+// (du/dX, du/dY, dv/dX, dv/dY) of the face coordinates:
+//   u = (sc / ma + 1) / 2  =>  du = (dsc - (sc / ma) dma) / (2 ma).
+__device__ __forceinline__ float4 cube_uv_da(const CubeFrame& f, const DirDA& d) {
+  const float h = 0.5f * f.inv_ma;
+  const float ks = (f.sc * f.inv_ma) * f.ms, kt = (f.tc * f.inv_ma) * f.ms;
+  const float2 ds = pick_axis(d, f.sa), dt = pick_axis(d, f.ta), dm = pick_axis(d, f.ma);
+  return make_float4(h * (f.ss * ds.x - ks * dm.x), h * (f.ss * ds.y - ks * dm.y),
+                     h * (f.ts * dt.x - kt * dm.x), h * (f.ts * dt.y - kt * dm.y));
+}
+
+// Transpose of cube_uv_da.
+__device__ __forceinline__ DirDA cube_uv_da_vjp(const CubeFrame& f, const float4 g) {
+  const float h = 0.5f * f.inv_ma;
+  const float ks = (f.sc * f.inv_ma) * f.ms, kt = (f.tc * f.inv_ma) * f.ms;
+  const float2 gs = make_float2(g.x * (h * f.ss), g.y * (h * f.ss));
+  const float2 gt = make_float2(g.z * (h * f.ts), g.w * (h * f.ts));
+  const float2 gm = make_float2(-(g.x * (h * ks) + g.z * (h * kt)), -(g.y * (h * ks) + g.w * (h * kt)));
+  DirDA r;
+#pragma unroll
+  for (int a = 0; a < 3; ++a) r.a[a] = a == f.sa ? gs : (a == f.ta ? gt : gm);
+  return r;
+}
+
+__device__ __forceinline__ DirDA load_dir_da(const float2* __restrict__ p, int64_t pix) {
+  DirDA d;
+  d.a[0] = __ldg(p + 3 * pix);
+  d.a[1] = __ldg(p + 3 * pix + 1);
+  d.a[2] = __ldg(p + 3 * pix + 2);
+  return d;
+}
+
+template <bool MIP_LINEAR>
+__global__ void k_tex_cube_mip_fwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+                                   bool tex_shared, int C, const float* __restrict__ dir,
+                                   const float2* __restrict__ dir_da, float bias,
+                                   const float* __restrict__ bias_map, int64_t P, int64_t HWi,
+                                   float* __restrict__ out) {
+  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= P) return;  // no warp collectives
+  const CubeFrame f = cube_frame(__ldg(dir + 3 * pix), __ldg(dir + 3 * pix + 1), __ldg(dir + 3 * pix + 2));
+  const int64_t img = (tex_shared ? 0 : pix / HWi) * 6 + f.face;
+  float s;
+  const float4 e = effective_da(cube_uv_da(f, load_dir_da(dir_da, pix)), pix, bias, bias_map, s);
+  const LodSel ls = lod_select<MIP_LINEAR>(e, m.h[0], m.w[0], m.L);
+  const Taps q0 = bilin_taps<1>(f.u, f.v, m.w[ls.k0], m.h[ls.k0]);
+  const Taps q1 = bilin_taps<1>(f.u, f.v, m.w[ls.k1], m.h[ls.k1]);
+  const float* b0 = level_ptr(tex, pyr, m, ls.k0, img, C);
+  const float* b1 = level_ptr(tex, pyr, m, ls.k1, img, C);
+  float* o = out + pix * C;
+  for (int c = 0; c < C; ++c) {
+    const float o0 = (1.0f - ls.frac) * sample4(b0, q0, C, c);
+    o[c] = o0 + ls.frac * sample4(b1, q1, C, c);
+  }
+}
+
+template <bool MIP_LINEAR>
+__global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+                                   bool tex_shared, int C, const float* __restrict__ dir,
+                                   const float2* __restrict__ dir_da, float bias,
+                                   const float* __restrict__ bias_map, int64_t P, int64_t HWi,
+                                   const float* __restrict__ d_out, float* __restrict__ d_tex,
+                                   float* __restrict__ d_pyr, float* __restrict__ d_dir,
+                                   float2* __restrict__ d_dir_da, float* __restrict__ d_bias_map) {
+  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool on = pix0 < P;
+  const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
+  const int lane = threadIdx.x & 31;
+  const CubeFrame f = cube_frame(__ldg(dir + 3 * pix), __ldg(dir + 3 * pix + 1), __ldg(dir + 3 * pix + 2));
+  const int64_t img = (tex_shared ? 0 : pix / HWi) * 6 + f.face;
+  float s;
+  const float4 e = effective_da(cube_uv_da(f, load_dir_da(dir_da, pix)), pix, bias, bias_map, s);
+  const LodSel ls = lod_select<MIP_LINEAR>(e, m.h[0], m.w[0], m.L);
+  const float* g = d_out + pix * C;
+  __shared__ HotCache hc;
+  hot_init(&hc);
+  __syncthreads();
+#pragma unroll
+  for (int li = 0; li < 2; ++li) {
+    const int k = li == 0 ? ls.k0 : ls.k1;
+    const float scale = li == 0 ? (1.0f - ls.frac) : ls.frac;
+    const Taps q = bilin_taps<1>(f.u, f.v, m.w[k], m.h[k]);
+    float* db = (k == 0 ? d_tex : d_pyr + m.off[k]) + img * (int64_t)m.h[k] * m.w[k] * C;
+    const bool tap_on = on && scale != 0.0f;
+    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, tap_on, lane, &hc);
+    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, tap_on, lane, &hc);
+    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, tap_on, lane, &hc);
+    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, tap_on, lane, &hc);
+  }
+  hot_flush(&hc, C);
+  if (!on) return;
+  d_dir[3 * pix] = 0.0f;
+  d_dir[3 * pix + 1] = 0.0f;
+  d_dir[3 * pix + 2] = 0.0f;
+  if (!d_dir_da && !d_bias_map) return;
+  const float4 g4 = lod_vjp<1>(e, m, tex, pyr, img, C, f.u, f.v, g);
+  if (d_dir_da) {
+    const DirDA r = cube_uv_da_vjp(f, make_float4(g4.x * s, g4.y * s, g4.z * s, g4.w * s));
+    d_dir_da[3 * pix] = r.a[0];
+    d_dir_da[3 * pix + 1] = r.a[1];
+    d_dir_da[3 * pix + 2] = r.a[2];
+  }
   if (d_bias_map) {
     const float acc = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
     d_bias_map[pix] = bias_map ? acc * 0.6931471805599453f : 0.0f;
@@ -557,6 +715,7 @@ dr_status build_pyramid(dr_ctx* ctx, const float* tex, int Nt, int C, const MipD
 struct TexArgs {
   bool cube, mip, mip_linear;
   int64_t P, HWi;
+  int64_t nimg;  // images per level: Nt, or Nt * 6 faces for a cube
   MipDesc m;
   int64_t pyr_floats;
 };
@@ -570,17 +729,20 @@ dr_status check_tex(dr_ctx* ctx, int filter, int boundary, const float* tex, int
   DR_REQUIRE(ctx, Nt == 1 || Nt == N, "texture: tex batch dim %d incompatible with uv batch %d", Nt, N);
   a.cube = boundary == DR_BOUNDARY_CUBE;
   if (a.cube)
-    DR_REQUIRE(ctx, filter == DR_FILTER_LINEAR, "texture: cube textures currently support filterMode .linear only");
+    DR_REQUIRE(ctx, filter != DR_FILTER_NEAREST, "texture: cube textures support the linear and mipmap filterModes");
   a.mip = filter == DR_FILTER_LINEAR_MIPMAP_NEAREST || filter == DR_FILTER_LINEAR_MIPMAP_LINEAR;
   a.mip_linear = filter == DR_FILTER_LINEAR_MIPMAP_LINEAR;
   if (a.mip) {
     DR_REQUIRE(ctx, uv_da != nullptr, "texture: mipmap filterModes require uvDA");
-    DR_REQUIRE(ctx, aligned(uv_da, 16), "texture: uvDA must be 16-byte aligned");
+    // [.., 4] uvDA loads as float4; a cube's [.., 6] dirDA as three float2.
+    DR_REQUIRE(ctx, aligned(uv_da, a.cube ? 8 : 16), "texture: uvDA must be %d-byte aligned", a.cube ? 8 : 16);
   }
   if (!a.cube) DR_REQUIRE(ctx, aligned(uv, 8), "texture: uv must be 8-byte aligned");
   a.P = (int64_t)N * Hi * Wi;
   a.HWi = (int64_t)Hi * Wi;
-  a.m = mip_desc(Nt, Ht, Wt, C, a.mip ? max_level : 0, &a.pyr_floats);
+  a.nimg = a.cube ? 6 * (int64_t)Nt : Nt;
+  DR_REQUIRE(ctx, a.nimg <= INT32_MAX, "texture: too many texture images");
+  a.m = mip_desc((int)a.nimg, Ht, Wt, C, a.mip ? max_level : 0, &a.pyr_floats);
   return DR_OK;
 }
 
@@ -632,7 +794,7 @@ extern "C" dr_status dr_texture_fwd(dr_ctx* ctx, int filter, int boundary, const
   DR_REQUIRE(ctx, out, "texture: out required");
   const unsigned grid = grid_for(a.P, 256);
   const bool shared = Nt == 1;
-  if (a.cube) {
+  if (a.cube && !a.mip) {
     DR_TB(ctx);
     k_tex_cube<<<grid, 256, 0, ctx->stream>>>(tex, shared, Ht, Wt, C, uv, a.P, a.HWi, out, nullptr, nullptr,
                                               nullptr);
@@ -658,9 +820,21 @@ extern "C" dr_status dr_texture_fwd(dr_ctx* ctx, int filter, int boundary, const
   if (!pyr && a.m.L > 1) {
     float* w = (float*)ws_get(ctx, WS_MIP, sizeof(float) * (size_t)a.pyr_floats);
     if (!w) return DR_ENOMEM;
-    st = build_pyramid(ctx, tex, Nt, C, a.m, w);
+    st = build_pyramid(ctx, tex, (int)a.nimg, C, a.m, w);
     if (st != DR_OK) return st;
     pyr = w;
+  }
+  if (a.cube) {
+    const float2* dda = reinterpret_cast<const float2*>(uv_da);
+    DR_TB(ctx);
+    if (a.mip_linear)
+      k_tex_cube_mip_fwd<true><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,
+                                                              mip_level_bias_map, a.P, a.HWi, out);
+    else
+      k_tex_cube_mip_fwd<false><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,
+                                                               mip_level_bias_map, a.P, a.HWi, out);
+    DR_LAUNCHED(ctx, "tex_cube_mip_fwd");
+    return DR_OK;
   }
   const float4* da4 = reinterpret_cast<const float4*>(uv_da);
   DR_TB(ctx);
@@ -687,12 +861,14 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   dr_status st = check_tex(ctx, filter, boundary, tex, Nt, Ht, Wt, C, max_level, uv, uv_da, N, Hi, Wi, a);
   if (st != DR_OK) return st;
   DR_REQUIRE(ctx, d_out && d_tex && d_uv, "texture_bwd: d_out, d_tex and d_uv are required");
-  if (d_uv_da) DR_REQUIRE(ctx, aligned(d_uv_da, 16), "texture_bwd: d_uv_da must be 16-byte aligned");
+  if (d_uv_da)
+    DR_REQUIRE(ctx, aligned(d_uv_da, a.cube ? 8 : 16), "texture_bwd: d_uv_da must be %d-byte aligned",
+               a.cube ? 8 : 16);
   const unsigned grid = grid_for(a.P, 256);
   const bool shared = Nt == 1;
   const int64_t n_tex = (int64_t)Nt * (a.cube ? 6 : 1) * Ht * Wt * C;
   DR_CUDA(ctx, cudaMemsetAsync(d_tex, 0, sizeof(float) * (size_t)n_tex, ctx->stream), "texture_bwd memset");
-  if (a.cube) {
+  if (a.cube && !a.mip) {
     DR_TB(ctx);
     k_tex_cube<<<grid, 256, 0, ctx->stream>>>(tex, shared, Ht, Wt, C, uv, a.P, a.HWi, nullptr, d_out, d_tex,
                                               d_uv);
@@ -701,7 +877,7 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   }
   const float2* uv2 = reinterpret_cast<const float2*>(uv);
   float2* duv2 = reinterpret_cast<float2*>(d_uv);
-  DR_REQUIRE(ctx, aligned(d_uv, 8), "texture_bwd: d_uv must be 8-byte aligned");
+  if (!a.cube) DR_REQUIRE(ctx, aligned(d_uv, 8), "texture_bwd: d_uv must be 8-byte aligned");
   if (filter == DR_FILTER_NEAREST) {
     DR_TB(ctx);
     DR_MODE_SWITCH(boundary, (k_tex_nearest<MODE><<<grid, 256, 0, ctx->stream>>>(
@@ -720,7 +896,7 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   if (!pyr && a.m.L > 1) {
     float* w = (float*)ws_get(ctx, WS_MIP, sizeof(float) * (size_t)a.pyr_floats);
     if (!w) return DR_ENOMEM;
-    st = build_pyramid(ctx, tex, Nt, C, a.m, w);
+    st = build_pyramid(ctx, tex, (int)a.nimg, C, a.m, w);
     if (st != DR_OK) return st;
     pyr = w;
   }
@@ -731,6 +907,20 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
     DR_CUDA(ctx, cudaMemsetAsync(dpyr, 0, sizeof(float) * (size_t)a.pyr_floats, ctx->stream),
             "texture_bwd memset");
   }
+  if (a.cube) {
+    const float2* dda = reinterpret_cast<const float2*>(uv_da);
+    float2* ddda = reinterpret_cast<float2*>(d_uv_da);
+    DR_TB(ctx);
+    if (a.mip_linear)
+      k_tex_cube_mip_bwd<true><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,
+                                                              mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr,
+                                                              d_uv, ddda, d_bias_map);
+    else
+      k_tex_cube_mip_bwd<false><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,
+                                                               mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr,
+                                                               d_uv, ddda, d_bias_map);
+    DR_LAUNCHED(ctx, "tex_cube_mip_bwd");
+  } else {
   const float4* da4 = reinterpret_cast<const float4*>(uv_da);
   float4* dda4 = reinterpret_cast<float4*>(d_uv_da);
   DR_TB(ctx);
@@ -744,10 +934,11 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
                                  a.HWi, d_out, d_tex, dpyr, duv2, dda4, d_bias_map)));
   }
   DR_LAUNCHED(ctx, "tex_mip_bwd");
+  }
   if (a.m.L > 1) {
-    DR_REQUIRE(ctx, Ht <= 65535 && Nt <= 65535, "texture_bwd: mip fold supports H, N <= 65535");
+    DR_REQUIRE(ctx, Ht <= 65535 && a.nimg <= 65535, "texture_bwd: mip fold supports H, images <= 65535");
     DR_TB(ctx);
-    k_mip_fold<<<dim3(grid_for(Wt, 256), Ht, Nt), 256, 0, ctx->stream>>>(d_tex, dpyr, a.m, C);
+    k_mip_fold<<<dim3(grid_for(Wt, 256), Ht, (unsigned)a.nimg), 256, 0, ctx->stream>>>(d_tex, dpyr, a.m, C);
     DR_LAUNCHED(ctx, "mip_fold");
   }
   return DR_OK;

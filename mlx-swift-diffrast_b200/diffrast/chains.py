@@ -213,11 +213,14 @@ class Cfg4(Chain):
 
 class Cfg5(Chain):
     """Geodesic sphere (f=158: 499,280 triangles), views at 2048^2: interpolate
-    per-vertex normals as cube directions, cube texture 6x1024^2x3 (.linear: the
-    reference's cube mode), antialias, MSE; backward d_verts and d_tex.  The
-    rank's views run as micro-batches with gradient accumulation."""
+    per-vertex normals as cube directions, cube texture 6x1024^2x3 sampled
+    trilinearly (the normals' screen-space derivatives give the LOD; the
+    reference's own cube mode, .linear, with filter_mode=FilterMode.linear),
+    antialias, MSE; backward d_verts and d_tex.  The rank's views run as
+    micro-batches with gradient accumulation."""
 
-    def __init__(self, dev, view_lo=0, view_hi=256, micro=16, res=2048, freq=158, cube=1024):
+    def __init__(self, dev, view_lo=0, view_hi=256, micro=16, res=2048, freq=158, cube=1024,
+                 filter_mode=ops.FilterMode.linearMipmapLinear):
         s = scenes.scene_cfg5(n_views=view_hi, res=res, freq=freq, cube=cube)
         self.verts = _t(np.concatenate([s["verts"], np.ones((s["verts"].shape[0], 1), np.float32)], 1),
                         dev, True)
@@ -234,6 +237,7 @@ class Cfg5(Chain):
         self.topo = ops.antialias_construct_topology_hash(self.tri)
         self.bg_dir = torch.tensor([0.0, 0.0, 1.0], device=dev)
         self.micro = micro
+        self.filter_mode = ops.FilterMode(filter_mode)
         self.info = ChainInfo("cfg5", n, self.res, n * H * W)
 
     def params(self):
@@ -248,12 +252,14 @@ class Cfg5(Chain):
         for a in range(0, n, self.micro):
             b = min(n, a + self.micro)
             xf = self.mvp[a:b]
-            ((rast, _),) = ops.rasterize_layers(self.verts, self.tri, self.res, 1, grad_db=False, xform=xf)
-            nrm, _ = ops.interpolate(self.nrm, rast, self.tri)
+            mip = self.filter_mode != ops.FilterMode.linear
+            ((rast, db),) = ops.rasterize_layers(self.verts, self.tri, self.res, 1, grad_db=mip, xform=xf)
+            nrm, nrm_da = ops.interpolate(self.nrm, rast, self.tri, db if mip else None,
+                                          ops.DiffAttrs.all if mip else None)
             # Background pixels interpolate a zero normal, which has no cube face
             # (the projection divides by max|dir| = 0): look them up along +z.
             nrm = nrm + (rast[..., 3:] == 0).float() * self.bg_dir
-            col = ops.texture(self.cube, nrm, boundary_mode=ops.BoundaryMode.cube)
+            col = ops.texture(self.cube, nrm, nrm_da if mip else None, self.filter_mode, ops.BoundaryMode.cube)
             aa = ops.antialias(col, rast, self.verts, self.tri, self.topo, xform=xf)
             loss = ops.mse_loss(aa, self.target[a:b]) * ((b - a) / n)
             loss.backward()

@@ -403,8 +403,8 @@ class _Texture(torch.autograd.Function):
         N, Hi, Wi = uv_c.shape[:3]
         mip = filt in (FilterMode.linearMipmapNearest, FilterMode.linearMipmapLinear)
         pyr = None
-        if mip:
-            pyr, _ = _build_pyramid(tex_c, -1)
+        if mip:  # a cube's pyramid is that of its Nt * 6 faces
+            pyr, _ = _build_pyramid(tex_c.view(-1, Ht, Wt, C) if cube else tex_c, -1)
         out = torch.empty((N, Hi, Wi, C), device=uv_c.device, dtype=torch.float32)
         c = _ctx(uv_c)
         L.check(L.lib().dr_texture_fwd(c, int(filt), int(bnd), _ptr(tex_c), Nt, Ht, Wt, C, _ptr(pyr), -1,
@@ -443,8 +443,11 @@ def texture(tex: torch.Tensor, uv: torch.Tensor, uv_da: Optional[torch.Tensor] =
     """DiffRast.texture (Texture.swift:62-131)."""
     filt, bnd = FilterMode(filter_mode), BoundaryMode(boundary_mode)
     if bnd == BoundaryMode.cube:
-        if filt != FilterMode.linear:
-            raise ValueError("texture: cube textures currently support filterMode .linear only")
+        # .linear as the reference; the mipmap filters are an extension that
+        # takes the direction's derivatives dirDA [N, H_img, W_img, 6]
+        # (interpolate's diff_attrs layout for a 3-component direction).
+        if filt == FilterMode.nearest:
+            raise ValueError("texture: cube textures support the linear and mipmap filterModes")
         if tex.dim() != 5 or tex.shape[1] != 6:
             raise ValueError(f"texture: cube tex must be [N, 6, H, W, C] (got {tuple(tex.shape)})")
         if uv.dim() != 4 or uv.shape[3] != 3:
@@ -452,7 +455,14 @@ def texture(tex: torch.Tensor, uv: torch.Tensor, uv_da: Optional[torch.Tensor] =
                              f"(got {tuple(uv.shape)})")
         if tex.shape[0] not in (1, uv.shape[0]):
             raise ValueError("texture: tex batch dim incompatible with uv batch")
-        return _Texture.apply(tex, uv, None, None, filt, bnd, 0.0)
+        if filt == FilterMode.linear:
+            return _Texture.apply(tex, uv, None, None, filt, bnd, 0.0)
+        if uv_da is None:
+            raise ValueError("texture: mipmap filterModes require uvDA")
+        if tuple(uv_da.shape) != tuple(uv.shape[:3]) + (6,):
+            raise ValueError(f"texture: cube uvDA must be [N, H_img, W_img, 6] (got {tuple(uv_da.shape)})")
+        _check_bias_map(mip_level_bias_map, uv)
+        return _Texture.apply(tex, uv, uv_da, mip_level_bias_map, filt, bnd, float(mip_level_bias))
     if tex.dim() != 4:
         raise ValueError(f"texture: tex must be [N, H_tex, W_tex, C] (got {tuple(tex.shape)})")
     if uv.dim() != 4 or uv.shape[3] != 2:
@@ -465,12 +475,15 @@ def texture(tex: torch.Tensor, uv: torch.Tensor, uv_da: Optional[torch.Tensor] =
         raise ValueError("texture: mipmap filterModes require uvDA")
     if tuple(uv_da.shape) != tuple(uv.shape[:3]) + (4,):
         raise ValueError(f"texture: uvDA must be [N, H_img, W_img, 4] (got {tuple(uv_da.shape)})")
-    if mip_level_bias_map is not None:
-        m = mip_level_bias_map
+    _check_bias_map(mip_level_bias_map, uv)
+    return _Texture.apply(tex, uv, uv_da, mip_level_bias_map, filt, bnd, float(mip_level_bias))
+
+
+def _check_bias_map(m, uv):
+    if m is not None:
         if tuple(m.shape[:3]) != tuple(uv.shape[:3]) or not (m.dim() == 3 or (m.dim() == 4 and m.shape[3] == 1)):
             raise ValueError("texture: mipLevelBiasMap must be [N, H_img, W_img] or [N, H_img, W_img, 1] "
                              f"(got {tuple(m.shape)})")
-    return _Texture.apply(tex, uv, uv_da, mip_level_bias_map, filt, bnd, float(mip_level_bias))
 
 
 def texture_construct_mip(tex: torch.Tensor, max_level: Optional[int] = None):

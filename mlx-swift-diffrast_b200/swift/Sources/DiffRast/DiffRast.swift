@@ -180,7 +180,10 @@ public enum DiffRast {
         let dTex = DeviceTensor(pointer: alloc.allocate(bytes: tex.count * 4), shape: tex.shape)
         let dUV = DeviceTensor(pointer: alloc.allocate(bytes: uv.count * 4), shape: uv.shape)
         let mip = filterMode == .linearMipmapLinear || filterMode == .linearMipmapNearest
-        let dDA = mip ? DeviceTensor(pointer: alloc.allocate(bytes: N * Hi * Wi * 16), shape: [N, Hi, Wi, 4]) : nil
+        // uvDA is [N, Hi, Wi, 4]; a mip-mapped cube's direction derivatives are [N, Hi, Wi, 6].
+        let nDA = cube ? 6 : 4
+        let dDA = mip ? DeviceTensor(pointer: alloc.allocate(bytes: N * Hi * Wi * nDA * 4), shape: [N, Hi, Wi, nDA])
+                      : nil
         ctx.check(dr_texture_bwd(ctx.raw, filterMode.rawValue, boundaryMode.rawValue, tex.f, Int32(Nt), Int32(Ht),
                                  Int32(Wt), Int32(C), nil, -1, uv.f, uvDA?.f, mipLevelBias, mipLevelBiasMap?.f,
                                  Int32(N), Int32(Hi), Int32(Wi), dOut.f, dTex.f, dUV.f, dDA?.f, nil),

@@ -201,7 +201,7 @@ def texture_bwd(tex, uv, d_out, uv_da=None, filter_mode="linear", boundary_mode=
     d_tex = np.zeros(tex.shape, np.float32)
     d_uv = np.zeros(uv.shape, np.float32)
     mip = filter_mode.startswith("linear-mipmap")
-    d_uv_da = np.zeros((N, Hi, Wi, 4), np.float32) if mip else None
+    d_uv_da = np.zeros((N, Hi, Wi, 6 if boundary_mode == "cube" else 4), np.float32) if mip else None
     d_map = np.zeros((N, Hi, Wi), np.float32) if mip else None
     rc = lib().orc_texture_bwd(FILTERS[filter_mode], BOUNDARIES[boundary_mode], _p(tex), Nt, Ht,
                                Wt, C, max_level, _p(uv), _p(uv_da), ctypes.c_float(mip_level_bias),

@@ -85,17 +85,27 @@ def cfg4(pos, tri, attr, tgt0, tgt1, res, topo=None, nthreads=0):
     return l0 + l1, {"pos": d_pos, "attr": d_attr0 + d_attr1}
 
 
-def cfg5(pos, tri, nrm, cube, target, res, topo=None, nthreads=0):
+def cfg5(pos, tri, nrm, cube, target, res, topo=None, nthreads=0, filter_mode="linear-mipmap-linear"):
+    """filter_mode "linear" is the reference's cube mode; the mipmap filters
+    take the normals' screen-space derivatives (rast_db, diff_attrs all)."""
     topo = topology_hash(tri) if topo is None else topo
-    rast, _ = rasterize(pos, tri, res, grad_db=False, nthreads=nthreads)
-    d, _ = interpolate(nrm, rast, tri, nthreads=nthreads)
+    mip = filter_mode != "linear"
+    rast, db = rasterize(pos, tri, res, grad_db=mip, nthreads=nthreads)
+    d, dda = interpolate(nrm, rast, tri, rast_db=db if mip else None, diff_attrs="all" if mip else None,
+                         nthreads=nthreads)
     # background pixels have a zero normal: look them up along +z
     d = (d + (rast[..., 3:] == 0).astype(np.float32) * np.array([0, 0, 1], np.float32)).astype(np.float32)
-    col = texture(cube, d, boundary_mode="cube", nthreads=nthreads)
+    col = texture(cube, d, dda if mip else None, filter_mode, "cube", nthreads=nthreads)
     aa = antialias(col, rast, pos, tri, topo, nthreads=nthreads)
     loss, d_aa = _mse(aa, target, nthreads)
     d_col, d_pos_aa = antialias_bwd(col, rast, pos, tri, d_aa, topo, nthreads=nthreads)
-    d_cube, d_dir, _, _ = texture_bwd(cube, d, d_col, boundary_mode="cube", nthreads=nthreads)
-    d_nrm, d_rast, _ = interpolate_bwd(nrm, rast, tri, d_dir, nthreads=nthreads)
-    d_pos = rasterize_bwd(pos, tri, rast, d_rast, nthreads=nthreads) + d_pos_aa
+    d_cube, d_dir, d_dda, _ = texture_bwd(cube, d, d_col, dda if mip else None, filter_mode, "cube",
+                                          nthreads=nthreads)
+    if mip:
+        d_nrm, d_rast, d_db = interpolate_bwd(nrm, rast, tri, d_dir, rast_db=db, diff_attrs="all", d_out_da=d_dda,
+                                              nthreads=nthreads)
+        d_pos = rasterize_bwd(pos, tri, rast, d_rast, d_db, nthreads=nthreads) + d_pos_aa
+    else:
+        d_nrm, d_rast, _ = interpolate_bwd(nrm, rast, tri, d_dir, nthreads=nthreads)
+        d_pos = rasterize_bwd(pos, tri, rast, d_rast, nthreads=nthreads) + d_pos_aa
     return loss, {"pos": d_pos, "cube": d_cube}

@@ -614,7 +614,7 @@ inline Lod lod_of(const float* da, int Ht, int Wt, int L, bool mip_linear) {
 
 // Effective uvDA with the mipLevelBias / mipLevelBiasMap fold
 // (Texture.swift:104-126): uvDA * 2^map * 2^bias.
-inline void effective_da(const float* uv_da, int64_t pix, float bias, const float* bias_map,
+inline void effective_da(const float* da4, int64_t pix, float bias, const float* bias_map,
                          float* eff, float* scale_out) {
   float s = 1.0f;
   bool scaled = false;
@@ -626,7 +626,7 @@ inline void effective_da(const float* uv_da, int64_t pix, float bias, const floa
     s = exp2_rn(bias);
     scaled = true;
   }
-  for (int c = 0; c < 4; ++c) eff[c] = scaled ? uv_da[pix * 4 + c] * s : uv_da[pix * 4 + c];
+  for (int c = 0; c < 4; ++c) eff[c] = scaled ? da4[c] * s : da4[c];
   *scale_out = s;
 }
 
@@ -647,6 +647,55 @@ inline void cube_project(float x, float y, float z, int& face, float& u, float& 
   float inv_ma = 1.0f / ma;
   u = (sc * inv_ma + 1.0f) * 0.5f;
   v = (tc * inv_ma + 1.0f) * 0.5f;
+}
+
+// Cube frame of a direction: the face and its (s, t, major) axes with their
+// signs, as cube_project selects them, so that sc = s_sign * d[s_axis] etc.
+struct CubeFrame {
+  int face, sa, ta, ma;
+  float ss, ts, ms, sc, tc, inv_ma;
+  float u, v;  // face coordinates, exactly as cube_project returns them
+};
+inline CubeFrame cube_frame(const float* d) {
+  static const int kAxes[6][3] = {{2, 1, 0}, {2, 1, 0}, {0, 2, 1}, {0, 2, 1}, {0, 1, 2}, {0, 1, 2}};
+  static const float kSigns[6][3] = {{-1.f, -1.f, 1.f}, {1.f, -1.f, -1.f}, {1.f, 1.f, 1.f},
+                                     {1.f, -1.f, -1.f}, {1.f, -1.f, 1.f}, {-1.f, -1.f, -1.f}};
+  CubeFrame f;
+  cube_project(d[0], d[1], d[2], f.face, f.u, f.v);
+  f.sa = kAxes[f.face][0]; f.ta = kAxes[f.face][1]; f.ma = kAxes[f.face][2];
+  f.ss = kSigns[f.face][0]; f.ts = kSigns[f.face][1]; f.ms = kSigns[f.face][2];
+  f.sc = f.ss * d[f.sa];
+  f.tc = f.ts * d[f.ta];
+  f.inv_ma = 1.0f / (f.ms * d[f.ma]);
+  return f;
+}
+
+// Screen-space derivatives of the face coordinates (u, v) from the
+// direction's derivatives dd = [dx/dX, dx/dY, dy/dX, dy/dY, dz/dX, dz/dY]
+// (interpolate's interleaved attribute-derivative layout):
+//   u = (sc / ma + 1) / 2  =>  du = (dsc - (sc / ma) dma) / (2 ma).
+// Output order matches uvDA: (du/dX, du/dY, dv/dX, dv/dY).  Extension (the
+// reference's cube path samples level 0 only).
+inline void cube_uv_da(const CubeFrame& f, const float* dd, float* e) {
+  const float h = 0.5f * f.inv_ma;
+  const float ks = (f.sc * f.inv_ma) * f.ms, kt = (f.tc * f.inv_ma) * f.ms;
+  e[0] = h * (f.ss * dd[2 * f.sa] - ks * dd[2 * f.ma]);
+  e[1] = h * (f.ss * dd[2 * f.sa + 1] - ks * dd[2 * f.ma + 1]);
+  e[2] = h * (f.ts * dd[2 * f.ta] - kt * dd[2 * f.ma]);
+  e[3] = h * (f.ts * dd[2 * f.ta + 1] - kt * dd[2 * f.ma + 1]);
+}
+
+// Transpose of cube_uv_da: g = d(loss)/d(du/dX, du/dY, dv/dX, dv/dY) ->
+// d(loss)/d(dd).
+inline void cube_uv_da_vjp(const CubeFrame& f, const float* g, float* dd) {
+  const float h = 0.5f * f.inv_ma;
+  const float ks = (f.sc * f.inv_ma) * f.ms, kt = (f.tc * f.inv_ma) * f.ms;
+  dd[2 * f.sa] = g[0] * (h * f.ss);
+  dd[2 * f.sa + 1] = g[1] * (h * f.ss);
+  dd[2 * f.ta] = g[2] * (h * f.ts);
+  dd[2 * f.ta + 1] = g[3] * (h * f.ts);
+  dd[2 * f.ma] = -(g[0] * (h * ks) + g[2] * (h * kt));
+  dd[2 * f.ma + 1] = -(g[1] * (h * ks) + g[3] * (h * kt));
 }
 
 void build_pyramid(const float* tex, int Nt, int C, const MipLayout& m, float* pyr, int nthreads) {
@@ -670,6 +719,71 @@ void build_pyramid(const float* tex, int Nt, int C, const MipLayout& m, float* p
         dst[i] = ((a + bb) + (cc + d)) * 0.25f;
       }
     });
+  }
+}
+
+
+// K22 (Texture.swift:1011-1102): d(loss)/d(eff) for the effective uvDA `eff`
+// through the LOD, independent of MIP_LINEAR.  `img` selects the image (the
+// texture batch entry, or batch * 6 + face for a cube) in every level.
+void lod_vjp(const float* eff, const MipLayout& m, const float* tex, const float* pyr, int64_t img, int C,
+             float u, float v, int boundary, const float* g, float* g4) {
+  const int Ht = m.h[0], Wt = m.w[0];
+  float du_dx = eff[0], du_dy = eff[1], dv_dx = eff[2], dv_dy = eff[3];
+  float sx = du_dx * (float)Wt, sy = du_dy * (float)Wt;
+  float tx_ = dv_dx * (float)Ht, ty_ = dv_dy * (float)Ht;
+  float Asq = sx * sx + tx_ * tx_, Bsq = sy * sy + ty_ * ty_;
+  float rho_sq = std::fmax(Asq, Bsq);
+  float lod_raw = 0.5f * log2_rn(std::fmax(rho_sq, 1e-20f));
+  for (int c = 0; c < 4; ++c) g4[c] = 0.0f;
+  if (lod_raw <= 0.0f || lod_raw >= (float)(m.L - 1)) return;
+  int k0 = floor_to_int(lod_raw);
+  int k1 = k0 + 1;
+  if (k1 >= m.L) k1 = m.L - 1;
+  float d_lod = 0.0f;
+  for (int li = 0; li < 2; ++li) {
+    int k = li == 0 ? k0 : k1;
+    float sign = li == 0 ? -1.0f : 1.0f;
+    int Hk = m.h[k], Wk = m.w[k];
+    const float* lb = (k == 0 ? tex : pyr + m.off[k]) + img * Hk * Wk * C;
+    Bilin bl = bilin(u, v, Wk, Hk, boundary);
+    for (int c = 0; c < C; ++c) {
+      float t00 = lb[((int64_t)bl.iy0 * Wk + bl.ix0) * C + c];
+      float t10 = lb[((int64_t)bl.iy0 * Wk + bl.ix1) * C + c];
+      float t01 = lb[((int64_t)bl.iy1 * Wk + bl.ix0) * C + c];
+      float t11 = lb[((int64_t)bl.iy1 * Wk + bl.ix1) * C + c];
+      float sample = bl.w00 * t00 + bl.w10 * t10 + bl.w01 * t01 + bl.w11 * t11;
+      d_lod += sign * sample * g[c];
+    }
+  }
+  float ln2 = 0.6931471805599453f;
+  float dlod_drho_sq = 1.0f / (2.0f * rho_sq * ln2);
+  float A_is_max = (Asq >= Bsq) ? 1.0f : 0.0f;
+  float B_is_max = 1.0f - A_is_max;
+  g4[0] = d_lod * dlod_drho_sq * A_is_max * 2.0f * sx * (float)Wt;
+  g4[1] = d_lod * dlod_drho_sq * B_is_max * 2.0f * sy * (float)Wt;
+  g4[2] = d_lod * dlod_drho_sq * A_is_max * 2.0f * tx_ * (float)Ht;
+  g4[3] = d_lod * dlod_drho_sq * B_is_max * 2.0f * ty_ * (float)Ht;
+}
+
+// Adjoint of the pyramid build: fold level gradients into level 0,
+// d_{k-1} += upsample(d_k) / 4, coarsest first.  dall = [level 0 | levels >= 1].
+void fold_pyramid(float* dall, int64_t l0, const MipLayout& m, int Nimg, int C) {
+  for (int k = m.L - 1; k >= 1; --k) {
+    float* dk = dall + l0 + m.off[k];
+    float* dp = (k == 1) ? dall : dall + l0 + m.off[k - 1];
+    int Hd = m.h[k], Wd = m.w[k], Ws = m.w[k - 1];
+    for (int n = 0; n < Nimg; ++n)
+      for (int y = 0; y < Hd; ++y)
+        for (int x = 0; x < Wd; ++x)
+          for (int c = 0; c < C; ++c) {
+            float g = dk[(((int64_t)n * Hd + y) * Wd + x) * C + c] * 0.25f;
+            int64_t pb = (int64_t)n * m.h[k - 1] * Ws;
+            dp[(pb + (int64_t)(2 * y) * Ws + 2 * x) * C + c] += g;
+            dp[(pb + (int64_t)(2 * y) * Ws + 2 * x + 1) * C + c] += g;
+            dp[(pb + (int64_t)(2 * y + 1) * Ws + 2 * x) * C + c] += g;
+            dp[(pb + (int64_t)(2 * y + 1) * Ws + 2 * x + 1) * C + c] += g;
+          }
   }
 }
 
@@ -706,6 +820,42 @@ extern "C" int orc_texture_fwd(int filter, int boundary, const float* tex, int N
                                const float* uv_da, float bias, const float* bias_map, int N,
                                int Hi, int Wi, float* out, int nthreads) {
   int64_t P = (int64_t)N * Hi * Wi;
+  if (boundary == 3 && (filter == 2 || filter == 3)) {
+    // Mipmapped cube (extension): the pyramid of the Nt * 6 faces, LOD from
+    // the face-coordinate derivatives, per-level per-face clamp bilinear.
+    if (!uv_da) return 1;
+    MipLayout m = mip_layout(Nt * 6, Ht, Wt, C, max_level);
+    std::vector<float> pyr((size_t)std::max<int64_t>(m.total, 1));
+    build_pyramid(tex, Nt * 6, C, m, pyr.data(), nthreads);
+    bool mip_linear = (filter == 3);
+    parallel_for(P, nthreads, [&](int64_t b, int64_t e, int) {
+      for (int64_t pix = b; pix < e; ++pix) {
+        int pn = (int)(pix / ((int64_t)Hi * Wi));
+        CubeFrame f = cube_frame(uv + pix * 3);
+        int64_t img = (int64_t)(Nt == 1 ? 0 : pn) * 6 + f.face;
+        float da4[4], eff[4], s;
+        cube_uv_da(f, uv_da + pix * 6, da4);
+        effective_da(da4, pix, bias, bias_map, eff, &s);
+        Lod ld = lod_of(eff, Ht, Wt, m.L, mip_linear);
+        for (int li = 0; li < 2; ++li) {
+          int k = li == 0 ? ld.k0 : ld.k1;
+          int Hk = m.h[k], Wk = m.w[k];
+          const float* lb = (k == 0 ? tex : pyr.data() + m.off[k]) + img * Hk * Wk * C;
+          Bilin bl = bilin(f.u, f.v, Wk, Hk, 1);
+          for (int c = 0; c < C; ++c) {
+            float t00 = lb[((int64_t)bl.iy0 * Wk + bl.ix0) * C + c];
+            float t10 = lb[((int64_t)bl.iy0 * Wk + bl.ix1) * C + c];
+            float t01 = lb[((int64_t)bl.iy1 * Wk + bl.ix0) * C + c];
+            float t11 = lb[((int64_t)bl.iy1 * Wk + bl.ix1) * C + c];
+            float sample = bl.w00 * t00 + bl.w10 * t10 + bl.w01 * t01 + bl.w11 * t11;
+            if (li == 0) out[pix * C + c] = (1.0f - ld.frac) * sample;
+            else out[pix * C + c] += ld.frac * sample;
+          }
+        }
+      }
+    });
+    return 0;
+  }
   if (boundary == 3) {
     if (filter != 1) return 1;
     parallel_for(P, nthreads, [&](int64_t b, int64_t e, int) {
@@ -772,7 +922,7 @@ extern "C" int orc_texture_fwd(int filter, int boundary, const float* tex, int N
       int pn = (int)(pix / ((int64_t)Hi * Wi));
       int nt = (Nt == 1 ? 0 : pn);
       float eff[4], s;
-      effective_da(uv_da, pix, bias, bias_map, eff, &s);
+      effective_da(uv_da + pix * 4, pix, bias, bias_map, eff, &s);
       Lod ld = lod_of(eff, Ht, Wt, m.L, mip_linear);
       float u = uv[pix * 2], v = uv[pix * 2 + 1];
       for (int li = 0; li < 2; ++li) {
@@ -803,6 +953,63 @@ extern "C" int orc_texture_bwd(int filter, int boundary, const float* tex, int N
                                int Hi, int Wi, const float* d_out, float* d_tex, float* d_uv,
                                float* d_uv_da, float* d_bias_map, int nthreads) {
   int64_t P = (int64_t)N * Hi * Wi;
+  if (boundary == 3 && (filter == 2 || filter == 3)) {
+    // Mipmapped cube VJP (extension): d_tex through the pyramid of the
+    // Nt * 6 faces, d_dir = 0 as the reference's cube VJP, d_dirDA through
+    // the LOD (K22's d(eff) mapped back through cube_uv_da).
+    if (!uv_da) return 1;
+    const int Nf = Nt * 6;
+    MipLayout m = mip_layout(Nf, Ht, Wt, C, max_level);
+    std::vector<float> pyr((size_t)std::max<int64_t>(m.total, 1));
+    build_pyramid(tex, Nf, C, m, pyr.data(), nthreads);
+    bool mip_linear = (filter == 3);
+    int64_t l0 = (int64_t)Nf * Ht * Wt * C;
+    Accum acc(nthreads, (size_t)(l0 + m.total));
+    parallel_for(P, nthreads, [&](int64_t b, int64_t e, int tid) {
+      double* dt = acc.get(tid);
+      for (int64_t pix = b; pix < e; ++pix) {
+        int pn = (int)(pix / ((int64_t)Hi * Wi));
+        CubeFrame f = cube_frame(uv + pix * 3);
+        int64_t img = (int64_t)(Nt == 1 ? 0 : pn) * 6 + f.face;
+        float da4[4], eff[4], s;
+        cube_uv_da(f, uv_da + pix * 6, da4);
+        effective_da(da4, pix, bias, bias_map, eff, &s);
+        Lod ld = lod_of(eff, Ht, Wt, m.L, mip_linear);
+        for (int li = 0; li < 2; ++li) {
+          int k = li == 0 ? ld.k0 : ld.k1;
+          float scale = li == 0 ? (1.0f - ld.frac) : ld.frac;
+          int Hk = m.h[k], Wk = m.w[k];
+          int64_t lvl_off = (k == 0 ? 0 : l0 + m.off[k]) + img * Hk * Wk * C;
+          Bilin bl = bilin(f.u, f.v, Wk, Hk, 1);
+          for (int c = 0; c < C; ++c) {
+            float g = d_out[pix * C + c] * scale;
+            dt[lvl_off + ((int64_t)bl.iy0 * Wk + bl.ix0) * C + c] += (double)(bl.w00 * g);
+            dt[lvl_off + ((int64_t)bl.iy0 * Wk + bl.ix1) * C + c] += (double)(bl.w10 * g);
+            dt[lvl_off + ((int64_t)bl.iy1 * Wk + bl.ix0) * C + c] += (double)(bl.w01 * g);
+            dt[lvl_off + ((int64_t)bl.iy1 * Wk + bl.ix1) * C + c] += (double)(bl.w11 * g);
+          }
+        }
+        for (int c = 0; c < 3; ++c) d_uv[pix * 3 + c] = 0.0f;
+        float g4[4];
+        lod_vjp(eff, m, tex, pyr.data(), img, C, f.u, f.v, 1, d_out + pix * C, g4);
+        if (d_uv_da) {
+          float gs[4] = {g4[0] * s, g4[1] * s, g4[2] * s, g4[3] * s};
+          cube_uv_da_vjp(f, gs, d_uv_da + pix * 6);
+        }
+        if (d_bias_map) {
+          float acc_m = 0.0f;
+          for (int c = 0; c < 4; ++c) acc_m += g4[c] * eff[c];
+          d_bias_map[pix] = bias_map ? acc_m * 0.6931471805599453f : 0.0f;
+        }
+      }
+    });
+    size_t tot = (size_t)(l0 + m.total);
+    std::vector<float> dall(tot);
+    acc.reduce_to(dall.data());
+    fold_pyramid(dall.data(), l0, m, Nf, C);
+    std::memcpy(d_tex, dall.data(), sizeof(float) * (size_t)l0);
+    return 0;
+  }
   if (boundary == 3) {
     if (filter != 1) return 1;
     Accum acc(nthreads, (size_t)Nt * 6 * Ht * Wt * C);
@@ -896,7 +1103,7 @@ extern "C" int orc_texture_bwd(int filter, int boundary, const float* tex, int N
       int pn = (int)(pix / ((int64_t)Hi * Wi));
       int nt = (Nt == 1 ? 0 : pn);
       float eff[4], s;
-      effective_da(uv_da, pix, bias, bias_map, eff, &s);
+      effective_da(uv_da + pix * 4, pix, bias, bias_map, eff, &s);
       Lod ld = lod_of(eff, Ht, Wt, m.L, mip_linear);
       float u = uv[pix * 2], v = uv[pix * 2 + 1];
       float dfx_sum_total = 0.0f, dfy_sum_total = 0.0f;
@@ -930,42 +1137,8 @@ extern "C" int orc_texture_bwd(int filter, int boundary, const float* tex, int N
       d_uv[pix * 2 + 1] = dfy_sum_total;
 
       // K22 d_uvDA (Texture.swift:1011-1102): independent of MIP_LINEAR.
-      float du_dx = eff[0], du_dy = eff[1], dv_dx = eff[2], dv_dy = eff[3];
-      float sx = du_dx * (float)Wt, sy = du_dy * (float)Wt;
-      float tx_ = dv_dx * (float)Ht, ty_ = dv_dy * (float)Ht;
-      float Asq = sx * sx + tx_ * tx_, Bsq = sy * sy + ty_ * ty_;
-      float rho_sq = std::fmax(Asq, Bsq);
-      float lod_raw = 0.5f * log2_rn(std::fmax(rho_sq, 1e-20f));
-      float g4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      if (!(lod_raw <= 0.0f || lod_raw >= (float)(m.L - 1))) {
-        int k0 = floor_to_int(lod_raw);
-        int k1 = k0 + 1;
-        if (k1 >= m.L) k1 = m.L - 1;
-        float d_lod = 0.0f;
-        for (int li = 0; li < 2; ++li) {
-          int k = li == 0 ? k0 : k1;
-          float sign = li == 0 ? -1.0f : 1.0f;
-          int Hk = m.h[k], Wk = m.w[k];
-          const float* lb = (k == 0 ? tex : pyr.data() + m.off[k]) + (int64_t)nt * Hk * Wk * C;
-          Bilin bl = bilin(u, v, Wk, Hk, boundary);
-          for (int c = 0; c < C; ++c) {
-            float t00 = lb[((int64_t)bl.iy0 * Wk + bl.ix0) * C + c];
-            float t10 = lb[((int64_t)bl.iy0 * Wk + bl.ix1) * C + c];
-            float t01 = lb[((int64_t)bl.iy1 * Wk + bl.ix0) * C + c];
-            float t11 = lb[((int64_t)bl.iy1 * Wk + bl.ix1) * C + c];
-            float sample = bl.w00 * t00 + bl.w10 * t10 + bl.w01 * t01 + bl.w11 * t11;
-            d_lod += sign * sample * d_out[pix * C + c];
-          }
-        }
-        float ln2 = 0.6931471805599453f;
-        float dlod_drho_sq = 1.0f / (2.0f * rho_sq * ln2);
-        float A_is_max = (Asq >= Bsq) ? 1.0f : 0.0f;
-        float B_is_max = 1.0f - A_is_max;
-        g4[0] = d_lod * dlod_drho_sq * A_is_max * 2.0f * sx * (float)Wt;
-        g4[1] = d_lod * dlod_drho_sq * B_is_max * 2.0f * sy * (float)Wt;
-        g4[2] = d_lod * dlod_drho_sq * A_is_max * 2.0f * tx_ * (float)Ht;
-        g4[3] = d_lod * dlod_drho_sq * B_is_max * 2.0f * ty_ * (float)Ht;
-      }
+      float g4[4];
+      lod_vjp(eff, m, tex, pyr.data(), nt, C, u, v, boundary, d_out + pix * C, g4);
       // Backward of eff = uvDA * s: d_uvDA = g * s; d_map = ln2 * sum(g * eff).
       if (d_uv_da)
         for (int c = 0; c < 4; ++c) d_uv_da[pix * 4 + c] = g4[c] * s;
@@ -976,26 +1149,10 @@ extern "C" int orc_texture_bwd(int filter, int boundary, const float* tex, int N
       }
     }
   });
-  // Fold pyramid gradients into level 0: d_{k-1} += upsample(d_k) / 4.
   size_t tot = (size_t)(l0 + m.total);
   std::vector<float> dall(tot);
   acc.reduce_to(dall.data());
-  for (int k = m.L - 1; k >= 1; --k) {
-    float* dk = dall.data() + l0 + m.off[k];
-    float* dp = (k == 1) ? dall.data() : dall.data() + l0 + m.off[k - 1];
-    int Hd = m.h[k], Wd = m.w[k], Ws = m.w[k - 1];
-    for (int n = 0; n < Nt; ++n)
-      for (int y = 0; y < Hd; ++y)
-        for (int x = 0; x < Wd; ++x)
-          for (int c = 0; c < C; ++c) {
-            float g = dk[(((int64_t)n * Hd + y) * Wd + x) * C + c] * 0.25f;
-            int64_t pb = (int64_t)n * m.h[k - 1] * Ws;
-            dp[(pb + (int64_t)(2 * y) * Ws + 2 * x) * C + c] += g;
-            dp[(pb + (int64_t)(2 * y) * Ws + 2 * x + 1) * C + c] += g;
-            dp[(pb + (int64_t)(2 * y + 1) * Ws + 2 * x) * C + c] += g;
-            dp[(pb + (int64_t)(2 * y + 1) * Ws + 2 * x + 1) * C + c] += g;
-          }
-  }
+  fold_pyramid(dall.data(), l0, m, Nt, C);
   std::memcpy(d_tex, dall.data(), sizeof(float) * (size_t)l0);
   return 0;
 }

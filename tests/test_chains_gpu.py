@@ -69,16 +69,18 @@ def test_cfg4_chain_per_view_transform(dev):
     _check(loss.detach(), got, ref_loss, ref)
 
 
-def test_cfg5_chain_microbatched_cube(dev):
+@pytest.mark.parametrize("filt", ["linear", "linear-mipmap-linear"])
+def test_cfg5_chain_microbatched_cube(dev, filt):
     import oracle
     import oracle.chains as OC
-    from diffrast import chains
-    c = chains.Cfg5(dev, 0, 3, micro=2, res=128, freq=8, cube=32)
+    from diffrast import chains, ops
+    fm = ops.FilterMode.linear if filt == "linear" else ops.FilterMode.linearMipmapLinear
+    c = chains.Cfg5(dev, 0, 3, micro=2, res=128, freq=8, cube=32, filter_mode=fm)
     loss = c.step()
     verts, mvp = c.verts.detach().cpu().numpy(), c.mvp.cpu().numpy()
     pos = oracle.xf_positions(verts, mvp)
     ref_loss, ref = OC.cfg5(pos, c.tri.cpu().numpy(), c.nrm.cpu().numpy(), c.cube.detach().cpu().numpy(),
-                            c.target.cpu().numpy(), c.res)
+                            c.target.cpu().numpy(), c.res, filter_mode=filt)
     ref = {"verts": oracle.xf_vertex_grad(ref["pos"], mvp), "cube": ref["cube"]}
     got = {"verts": c.verts.grad.cpu().numpy(), "cube": c.cube.grad.cpu().numpy()}
     _check(loss, got, ref_loss, ref)

@@ -203,3 +203,91 @@ def test_batch1_texture_gradient_sums_over_views(backend):
     d1, _, _, _ = backend.texture_bwd(tex, uv, d, boundary_mode="clamp")
     d3, _, _, _ = backend.texture_bwd(np.repeat(tex, 3, 0), uv, d, boundary_mode="clamp")
     np.testing.assert_allclose(d1[0], d3.sum(0), atol=1e-5)
+
+
+# ---- mip-mapped cube textures (extension: the reference's cube path samples
+# level 0 with filterMode .linear only).  The LOD comes from the derivatives of
+# the face coordinates, obtained from the direction's screen-space derivatives
+# dirDA = [dx/dX, dx/dY, dy/dX, dy/dY, dz/dX, dz/dY] through the cube
+# projection u = (sc / ma + 1) / 2.
+
+def _cube_fixture(seed=0xC0BE, Ht=8, C=2):
+    g = np.random.default_rng(seed)
+    tex = g.normal(size=(1, 6, Ht, Ht, C)).astype(np.float32)
+    d = np.array([[0.9, 0.2, -0.3], [-0.8, 0.35, 0.1], [0.15, 1.1, -0.4], [0.3, -0.7, 0.2],
+                  [-0.25, 0.3, 0.95], [0.2, -0.1, -1.2]], np.float32).reshape(1, 2, 3, 3)
+    dd = g.uniform(0.35, 0.7, size=(1, 2, 3, 6)).astype(np.float32)
+    w = np.array([(1 + i % 5) * 0.1 for i in range(6 * C)], np.float32).reshape(1, 2, 3, C)
+    return tex, d, dd, w
+
+
+def test_cube_mip_matches_cube_linear_at_lod0(backend):
+    tex, d, _, _ = _cube_fixture()
+    dd = np.full((1, 2, 3, 6), 1e-6, np.float32)
+    lin = backend.texture(tex, d, boundary_mode="cube")
+    for f in ("linear-mipmap-linear", "linear-mipmap-nearest"):
+        mip = backend.texture(tex, d, dd, filter_mode=f, boundary_mode="cube")
+        assert np.array_equal(lin, mip), f
+
+
+def test_cube_mip_constant_faces_any_lod(backend):
+    tex = np.broadcast_to(np.arange(1, 7, dtype=np.float32).reshape(1, 6, 1, 1, 1), (1, 6, 8, 8, 1)).copy()
+    _, d, dd, _ = _cube_fixture()
+    for scale in (0.01, 1.0, 100.0):
+        out = backend.texture(tex, d, dd * scale, filter_mode="linear-mipmap-linear", boundary_mode="cube")
+        np.testing.assert_allclose(out.reshape(-1), [1.0, 2.0, 3.0, 4.0, 5.0, 6.0], rtol=1e-6)
+
+
+@pytest.mark.parametrize("f", ["linear-mipmap-linear", "linear-mipmap-nearest"])
+def test_cube_mip_pz_face_equals_2d_mip(backend, f):
+    # On +Z with z = 1 and dz = 0: u = (x + 1) / 2, v = (1 - y) / 2, so the
+    # cube sample is the 2D clamp-mode sample of face 4 with
+    # uvDA = (dx/dX, dx/dY, -dy/dX, -dy/dY) / 2 — bit for bit.
+    tex, _, _, w = _cube_fixture()
+    g = np.random.default_rng(5)
+    xy = g.uniform(-0.9, 0.9, size=(1, 3, 4, 2)).astype(np.float32)
+    d = np.concatenate([xy, np.ones((1, 3, 4, 1), np.float32)], -1)
+    dxy = g.uniform(0.05, 0.8, size=(1, 3, 4, 4)).astype(np.float32)
+    dd = np.concatenate([dxy, np.zeros((1, 3, 4, 2), np.float32)], -1)
+    uv = np.stack([(xy[..., 0] + 1.0) * 0.5, (-xy[..., 1] + 1.0) * 0.5], -1).astype(np.float32)
+    uv_da = np.stack([0.5 * dxy[..., 0], 0.5 * dxy[..., 1], -0.5 * dxy[..., 2], -0.5 * dxy[..., 3]],
+                     -1).astype(np.float32)
+    face = np.ascontiguousarray(tex[:, 4])
+    cube = backend.texture(tex, d, dd, filter_mode=f, boundary_mode="cube")
+    flat = backend.texture(face, uv, uv_da, filter_mode=f, boundary_mode="clamp")
+    assert np.array_equal(cube, flat)
+    wc = np.resize(w, cube.shape).astype(np.float32)
+    dt_c, d_dir, d_dd, _ = backend.texture_bwd(tex, d, wc, dd, filter_mode=f, boundary_mode="cube")
+    dt_f, _, d_uvda, _ = backend.texture_bwd(face, uv, wc, uv_da, filter_mode=f, boundary_mode="clamp")
+    np.testing.assert_allclose(dt_c[:, 4], dt_f, rtol=1e-5, atol=1e-6)
+    assert np.all(np.delete(dt_c, 4, axis=1) == 0)
+    assert np.all(d_dir == 0)
+    np.testing.assert_allclose(d_dd[..., 0], 0.5 * d_uvda[..., 0], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(d_dd[..., 1], 0.5 * d_uvda[..., 1], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(d_dd[..., 2], -0.5 * d_uvda[..., 2], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(d_dd[..., 3], -0.5 * d_uvda[..., 3], rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("perturb", ["tex", "dirDA"])
+def test_gradcheck_cube_trilinear(backend, perturb):
+    tex, d, dd, w = _cube_fixture()
+    f = "linear-mipmap-linear"
+    d_tex, d_dir, d_dd, _ = backend.texture_bwd(tex, d, w, dd, filter_mode=f, boundary_mode="cube")
+    assert d_dd.shape == dd.shape and np.all(d_dir == 0)
+    if perturb == "tex":
+        num = fd_grad(lambda x: wsum(backend.texture(x, d, dd, filter_mode=f, boundary_mode="cube"), w), tex)
+        np.testing.assert_allclose(d_tex, num, atol=8e-3)
+    else:
+        num = fd_grad(lambda x: wsum(backend.texture(tex, d, x, filter_mode=f, boundary_mode="cube"), w), dd)
+        assert np.abs(num).max() > 1e-2  # the fixture's LODs are interior
+        np.testing.assert_allclose(d_dd, num, atol=8e-3)
+
+
+def test_gradcheck_cube_bias_map(backend):
+    tex, d, dd, w = _cube_fixture()
+    bmap = np.array([0.1, -0.2, 0.15, -0.05, 0.3, -0.1], np.float32).reshape(1, 2, 3)
+    f = "linear-mipmap-linear"
+    _, _, _, d_map = backend.texture_bwd(tex, d, w, dd, filter_mode=f, boundary_mode="cube", bias_map=bmap)
+    num = fd_grad(lambda x: wsum(backend.texture(tex, d, dd, filter_mode=f, boundary_mode="cube", bias_map=x),
+                                 w), bmap)
+    np.testing.assert_allclose(d_map, num, atol=8e-3)
