@@ -70,6 +70,13 @@ typedef enum dr_boundary {
   DR_BOUNDARY_CUBE = 3
 } dr_boundary;
 
+/* Flag bit OR'ed into the `boundary` argument of dr_texture_bwd (ignored by
+ * dr_texture_fwd).  Extension, cube textures only: d_uv receives d(loss)/d(dir)
+ * through the face projection u = (sc/ma + 1)/2, v = (tc/ma + 1)/2 — and, for
+ * the mipmap filters, through the LOD — instead of the reference's zero
+ * (Texture.swift:196-197). */
+#define DR_TEXTURE_CUBE_DIR_GRAD 0x100
+
 typedef struct dr_ctx dr_ctx;
 
 /* ---- context ----------------------------------------------------------- */
@@ -243,7 +250,7 @@ DR_API dr_status dr_texture_fwd(dr_ctx* ctx, int filter, int boundary,
  * MLX autograd of the pyramid build (folded into level 0 here).
  *   d_tex: out, same shape as tex (pyramid gradients folded in).
  *   d_uv: out, shape of uv (zero for nearest; zero d_dir for cube, as
- *         Texture.swift:196-197).
+ *         Texture.swift:196-197, unless boundary has DR_TEXTURE_CUBE_DIR_GRAD).
  *   d_uv_da: out, shape of uv_da, for mipmap filters, or NULL.
  *   d_bias_map: out [N, Hi, Wi] gradient of the bias map, or NULL. */
 DR_API dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary,

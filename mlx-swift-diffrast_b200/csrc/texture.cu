@@ -287,20 +287,126 @@ __device__ __forceinline__ void cube_project(float x, float y, float z, int& fac
   v = (tc * inv_ma + 1.0f) * 0.5f;
 }
 
+// Face of a direction with its (s, t, major) axes and signs, chosen as
+// cube_project chooses them: sc = ss * d[sa], tc = ts * d[ta], ma = ms * d[ma].
+struct CubeFrame {
+  int face, sa, ta, ma;
+  float ss, ts, ms, sc, tc, inv_ma, u, v;
+};
+
+__device__ __forceinline__ float pick3(int a, float x, float y, float z) { return a == 0 ? x : (a == 1 ? y : z); }
+
+__device__ __forceinline__ CubeFrame cube_frame(float x, float y, float z) {
+  CubeFrame f;
+  cube_project(x, y, z, f.face, f.u, f.v);
+  // Faces +X,-X,+Y,-Y,+Z,-Z: sc = (-z, z, x, x, x, -x), tc = (-y, -y, z, -z, -y, -y).
+  switch (f.face) {
+    case 0: f.sa = 2; f.ta = 1; f.ma = 0; f.ss = -1.f; f.ts = -1.f; f.ms = 1.f; break;
+    case 1: f.sa = 2; f.ta = 1; f.ma = 0; f.ss = 1.f; f.ts = -1.f; f.ms = -1.f; break;
+    case 2: f.sa = 0; f.ta = 2; f.ma = 1; f.ss = 1.f; f.ts = 1.f; f.ms = 1.f; break;
+    case 3: f.sa = 0; f.ta = 2; f.ma = 1; f.ss = 1.f; f.ts = -1.f; f.ms = -1.f; break;
+    case 4: f.sa = 0; f.ta = 1; f.ma = 2; f.ss = 1.f; f.ts = -1.f; f.ms = 1.f; break;
+    default: f.sa = 0; f.ta = 1; f.ma = 2; f.ss = -1.f; f.ts = -1.f; f.ms = -1.f; break;
+  }
+  f.sc = f.ss * pick3(f.sa, x, y, z);
+  f.tc = f.ts * pick3(f.ta, x, y, z);
+  f.inv_ma = 1.0f / (f.ms * pick3(f.ma, x, y, z));
+  return f;
+}
+
+// Per-pixel direction derivatives, interpolate's interleaved layout:
+// [dx/dX, dx/dY, dy/dX, dy/dY, dz/dX, dz/dY].
+struct DirDA {
+  float2 a[3];  // a[axis] = (d/dX, d/dY)
+};
+
+__device__ __forceinline__ float2 pick_axis(const DirDA& d, int a) {
+  return a == 0 ? d.a[0] : (a == 1 ? d.a[1] : d.a[2]);
+}
+
+// (du/dX, du/dY, dv/dX, dv/dY) of the face coordinates:
+//   u = (sc / ma + 1) / 2  =>  du = (dsc - (sc / ma) dma) / (2 ma).
+__device__ __forceinline__ float4 cube_uv_da(const CubeFrame& f, const DirDA& d) {
+  const float h = 0.5f * f.inv_ma;
+  const float ks = (f.sc * f.inv_ma) * f.ms, kt = (f.tc * f.inv_ma) * f.ms;
+  const float2 ds = pick_axis(d, f.sa), dt = pick_axis(d, f.ta), dm = pick_axis(d, f.ma);
+  return make_float4(h * (f.ss * ds.x - ks * dm.x), h * (f.ss * ds.y - ks * dm.y),
+                     h * (f.ts * dt.x - kt * dm.x), h * (f.ts * dt.y - kt * dm.y));
+}
+
+// Transpose of cube_uv_da.
+__device__ __forceinline__ DirDA cube_uv_da_vjp(const CubeFrame& f, const float4 g) {
+  const float h = 0.5f * f.inv_ma;
+  const float ks = (f.sc * f.inv_ma) * f.ms, kt = (f.tc * f.inv_ma) * f.ms;
+  const float2 gs = make_float2(g.x * (h * f.ss), g.y * (h * f.ss));
+  const float2 gt = make_float2(g.z * (h * f.ts), g.w * (h * f.ts));
+  const float2 gm = make_float2(-(g.x * (h * ks) + g.z * (h * kt)), -(g.y * (h * ks) + g.w * (h * kt)));
+  DirDA r;
+#pragma unroll
+  for (int a = 0; a < 3; ++a) r.a[a] = a == f.sa ? gs : (a == f.ta ? gt : gm);
+  return r;
+}
+
+// d(loss)/d(dir) (extension; the reference returns zero, Texture.swift:196-197)
+// from d(loss)/d(u, v) through u = (sc/ma + 1)/2, v alike, as per-axis values
+// (s axis, t axis, major axis).
+struct AxisGrad {
+  float s, t, m;
+};
+
+__device__ __forceinline__ AxisGrad cube_dir_vjp(const CubeFrame& f, float d_u, float d_v) {
+  const float h = 0.5f * f.inv_ma;
+  AxisGrad r;
+  r.s = d_u * (h * f.ss);
+  r.t = d_v * (h * f.ts);
+  r.m = -((d_u * f.sc + d_v * f.tc) * (h * f.inv_ma)) * f.ms;
+  return r;
+}
+
+// The LOD's dependence on the direction: with G = d(loss)/d(eff) * s, add
+// the Jacobian of cube_uv_da with respect to sc, tc and ma, transposed.
+__device__ __forceinline__ void cube_dir_lod_vjp(const CubeFrame& f, const DirDA& d, const float4 G,
+                                                 AxisGrad& r) {
+  const float a = f.inv_ma, a2 = a * a;
+  const float2 ds = pick_axis(d, f.sa), dt = pick_axis(d, f.ta), dm = pick_axis(d, f.ma);
+  const float gsm = G.x * dm.x + G.y * dm.y, gtm = G.z * dm.x + G.w * dm.y;
+  const float gss = G.x * ds.x + G.y * ds.y, gtt = G.z * dt.x + G.w * dt.y;
+  const float hm = (0.5f * a2) * f.ms;
+  r.s += -(hm * f.ss) * gsm;
+  r.t += -(hm * f.ts) * gtm;
+  r.m += -(hm * (f.ss * gss + f.ts * gtt)) + (a2 * a) * (f.sc * gsm + f.tc * gtm);
+}
+
+__device__ __forceinline__ void store_dir_grad(float* __restrict__ d_dir, int64_t pix, const CubeFrame& f,
+                                               const AxisGrad& r) {
+  float v[3];
+#pragma unroll
+  for (int a = 0; a < 3; ++a) v[a] = a == f.sa ? r.s : (a == f.ta ? r.t : r.m);
+  d_dir[3 * pix] = v[0];
+  d_dir[3 * pix + 1] = v[1];
+  d_dir[3 * pix + 2] = v[2];
+}
+
+__device__ __forceinline__ DirDA load_dir_da(const float2* __restrict__ p, int64_t pix) {
+  DirDA d;
+  d.a[0] = __ldg(p + 3 * pix);
+  d.a[1] = __ldg(p + 3 * pix + 1);
+  d.a[2] = __ldg(p + 3 * pix + 2);
+  return d;
+}
+
 __global__ void k_tex_cube(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
                            const float* __restrict__ dir, int64_t P, int64_t HWi, float* __restrict__ out,
                            const float* __restrict__ d_out, float* __restrict__ d_tex,
-                           float* __restrict__ d_dir) {
+                           float* __restrict__ d_dir, bool dir_grad) {
   const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (out && pix0 >= P) return;  // the forward has no warp collectives
   const bool on = pix0 < P;
   const int64_t pix = on ? pix0 : P - 1;
-  const float x = __ldg(dir + 3 * pix), y = __ldg(dir + 3 * pix + 1), z = __ldg(dir + 3 * pix + 2);
-  int face;
-  float u, v;
-  cube_project(x, y, z, face, u, v);
+  const CubeFrame f = cube_frame(__ldg(dir + 3 * pix), __ldg(dir + 3 * pix + 1), __ldg(dir + 3 * pix + 2));
+  const int face = f.face;
   // Per-face clamp bilinear (Texture.swift:656-672): weights carry no OOB mask.
-  Taps q = bilin_taps<1>(u, v, Wt, Ht);
+  Taps q = bilin_taps<1>(f.u, f.v, Wt, Ht);
   const float fx = q.fx, fy = q.fy;
   const float w00 = (1.0f - fx) * (1.0f - fy), w10 = fx * (1.0f - fy);
   const float w01 = (1.0f - fx) * fy, w11 = fx * fy;
@@ -322,8 +428,22 @@ __global__ void k_tex_cube(const float* __restrict__ tex, bool tex_shared, int H
     scatter_tap(d_tex + fb + q.a01 * C, w01, g, 1.0f, C, on, lane, &hc);
     scatter_tap(d_tex + fb + q.a11 * C, w11, g, 1.0f, C, on, lane, &hc);
     hot_flush(&hc, C);
-    // d_dir is identically zero in the reference (Texture.swift:196-197).
-    if (on) { d_dir[3 * pix] = 0.0f; d_dir[3 * pix + 1] = 0.0f; d_dir[3 * pix + 2] = 0.0f; }
+    if (!on) return;
+    // d_dir is identically zero in the reference (Texture.swift:196-197); the
+    // chain rule through the projection is an opt-in extension.
+    AxisGrad ag = {0.0f, 0.0f, 0.0f};
+    if (dir_grad) {
+      float dfx = 0.0f, dfy = 0.0f;
+      for (int c = 0; c < C; ++c) {
+        const float gc = __ldg(g + c);
+        const float t00 = __ldg(tex + fb + q.a00 * C + c), t10 = __ldg(tex + fb + q.a10 * C + c);
+        const float t01 = __ldg(tex + fb + q.a01 * C + c), t11 = __ldg(tex + fb + q.a11 * C + c);
+        dfx += gc * ((1.0f - fy) * (t10 - t00) + fy * (t11 - t01));
+        dfy += gc * ((1.0f - fx) * (t01 - t00) + fx * (t11 - t10));
+      }
+      ag = cube_dir_vjp(f, dfx * (float)Wt, dfy * (float)Ht);
+    }
+    store_dir_grad(d_dir, pix, f, ag);
   }
 }
 
@@ -534,74 +654,6 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
 // the face coordinates, per-level per-face clamp bilinear.  d_dir = 0 as the
 // reference's cube VJP; dirDA gets the LOD gradient.
 
-// Face of a direction with its (s, t, major) axes and signs, chosen as
-// cube_project chooses them: sc = ss * d[sa], tc = ts * d[ta], ma = ms * d[ma].
-struct CubeFrame {
-  int face, sa, ta, ma;
-  float ss, ts, ms, sc, tc, inv_ma, u, v;
-};
-
-__device__ __forceinline__ float pick3(int a, float x, float y, float z) { return a == 0 ? x : (a == 1 ? y : z); }
-
-__device__ __forceinline__ CubeFrame cube_frame(float x, float y, float z) {
-  CubeFrame f;
-  cube_project(x, y, z, f.face, f.u, f.v);
-  // Faces +X,-X,+Y,-Y,+Z,-Z: sc = (-z, z, x, x, x, -x), tc = (-y, -y, z, -z, -y, -y).
-  switch (f.face) {
-    case 0: f.sa = 2; f.ta = 1; f.ma = 0; f.ss = -1.f; f.ts = -1.f; f.ms = 1.f; break;
-    case 1: f.sa = 2; f.ta = 1; f.ma = 0; f.ss = 1.f; f.ts = -1.f; f.ms = -1.f; break;
-    case 2: f.sa = 0; f.ta = 2; f.ma = 1; f.ss = 1.f; f.ts = 1.f; f.ms = 1.f; break;
-    case 3: f.sa = 0; f.ta = 2; f.ma = 1; f.ss = 1.f; f.ts = -1.f; f.ms = -1.f; break;
-    case 4: f.sa = 0; f.ta = 1; f.ma = 2; f.ss = 1.f; f.ts = -1.f; f.ms = 1.f; break;
-    default: f.sa = 0; f.ta = 1; f.ma = 2; f.ss = -1.f; f.ts = -1.f; f.ms = -1.f; break;
-  }
-  f.sc = f.ss * pick3(f.sa, x, y, z);
-  f.tc = f.ts * pick3(f.ta, x, y, z);
-  f.inv_ma = 1.0f / (f.ms * pick3(f.ma, x, y, z));
-  return f;
-}
-
-// Per-pixel direction derivatives, interpolate's interleaved layout:
-// [dx/dX, dx/dY, dy/dX, dy/dY, dz/dX, dz/dY].
-struct DirDA {
-  float2 a[3];  // a[axis] = (d/dX, d/dY)
-};
-
-__device__ __forceinline__ float2 pick_axis(const DirDA& d, int a) {
-  return a == 0 ? d.a[0] : (a == 1 ? d.a[1] : d.a[2]);
-}
-
-// (du/dX, du/dY, dv/dX, dv/dY) of the face coordinates:
-//   u = (sc / ma + 1) / 2  =>  du = (dsc - (sc / ma) dma) / (2 ma).
-__device__ __forceinline__ float4 cube_uv_da(const CubeFrame& f, const DirDA& d) {
-  const float h = 0.5f * f.inv_ma;
-  const float ks = (f.sc * f.inv_ma) * f.ms, kt = (f.tc * f.inv_ma) * f.ms;
-  const float2 ds = pick_axis(d, f.sa), dt = pick_axis(d, f.ta), dm = pick_axis(d, f.ma);
-  return make_float4(h * (f.ss * ds.x - ks * dm.x), h * (f.ss * ds.y - ks * dm.y),
-                     h * (f.ts * dt.x - kt * dm.x), h * (f.ts * dt.y - kt * dm.y));
-}
-
-// Transpose of cube_uv_da.
-__device__ __forceinline__ DirDA cube_uv_da_vjp(const CubeFrame& f, const float4 g) {
-  const float h = 0.5f * f.inv_ma;
-  const float ks = (f.sc * f.inv_ma) * f.ms, kt = (f.tc * f.inv_ma) * f.ms;
-  const float2 gs = make_float2(g.x * (h * f.ss), g.y * (h * f.ss));
-  const float2 gt = make_float2(g.z * (h * f.ts), g.w * (h * f.ts));
-  const float2 gm = make_float2(-(g.x * (h * ks) + g.z * (h * kt)), -(g.y * (h * ks) + g.w * (h * kt)));
-  DirDA r;
-#pragma unroll
-  for (int a = 0; a < 3; ++a) r.a[a] = a == f.sa ? gs : (a == f.ta ? gt : gm);
-  return r;
-}
-
-__device__ __forceinline__ DirDA load_dir_da(const float2* __restrict__ p, int64_t pix) {
-  DirDA d;
-  d.a[0] = __ldg(p + 3 * pix);
-  d.a[1] = __ldg(p + 3 * pix + 1);
-  d.a[2] = __ldg(p + 3 * pix + 2);
-  return d;
-}
-
 template <bool MIP_LINEAR>
 __global__ void k_tex_cube_mip_fwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
                                    bool tex_shared, int C, const float* __restrict__ dir,
@@ -633,7 +685,8 @@ __global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* _
                                    const float* __restrict__ bias_map, int64_t P, int64_t HWi,
                                    const float* __restrict__ d_out, float* __restrict__ d_tex,
                                    float* __restrict__ d_pyr, float* __restrict__ d_dir,
-                                   float2* __restrict__ d_dir_da, float* __restrict__ d_bias_map) {
+                                   float2* __restrict__ d_dir_da, float* __restrict__ d_bias_map,
+                                   bool dir_grad) {
   const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool on = pix0 < P;
   const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
@@ -641,9 +694,11 @@ __global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* _
   const CubeFrame f = cube_frame(__ldg(dir + 3 * pix), __ldg(dir + 3 * pix + 1), __ldg(dir + 3 * pix + 2));
   const int64_t img = (tex_shared ? 0 : pix / HWi) * 6 + f.face;
   float s;
-  const float4 e = effective_da(cube_uv_da(f, load_dir_da(dir_da, pix)), pix, bias, bias_map, s);
+  const DirDA dda = load_dir_da(dir_da, pix);
+  const float4 e = effective_da(cube_uv_da(f, dda), pix, bias, bias_map, s);
   const LodSel ls = lod_select<MIP_LINEAR>(e, m.h[0], m.w[0], m.L);
   const float* g = d_out + pix * C;
+  float d_u = 0.0f, d_v = 0.0f;
   __shared__ HotCache hc;
   hot_init(&hc);
   __syncthreads();
@@ -658,16 +713,34 @@ __global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* _
     scatter_tap(db + q.a10 * C, q.w10, g, scale, C, tap_on, lane, &hc);
     scatter_tap(db + q.a01 * C, q.w01, g, scale, C, tap_on, lane, &hc);
     scatter_tap(db + q.a11 * C, q.w11, g, scale, C, tap_on, lane, &hc);
+    if (dir_grad) {
+      const float* b = level_ptr(tex, pyr, m, k, img, C);
+      float dfx = 0.0f, dfy = 0.0f;
+      for (int c = 0; c < C; ++c) {
+        const float gc = __ldg(g + c) * scale;
+        const float t00 = __ldg(b + q.a00 * C + c), t10 = __ldg(b + q.a10 * C + c);
+        const float t01 = __ldg(b + q.a01 * C + c), t11 = __ldg(b + q.a11 * C + c);
+        dfx += gc * ((1.0f - q.fy) * (t10 - t00) + q.fy * (t11 - t01));
+        dfy += gc * ((1.0f - q.fx) * (t01 - t00) + q.fx * (t11 - t10));
+      }
+      d_u += dfx * (float)m.w[k];
+      d_v += dfy * (float)m.h[k];
+    }
   }
   hot_flush(&hc, C);
   if (!on) return;
-  d_dir[3 * pix] = 0.0f;
-  d_dir[3 * pix + 1] = 0.0f;
-  d_dir[3 * pix + 2] = 0.0f;
-  if (!d_dir_da && !d_bias_map) return;
+  AxisGrad ag = {0.0f, 0.0f, 0.0f};
+  if (dir_grad) ag = cube_dir_vjp(f, d_u, d_v);
+  if (!d_dir_da && !d_bias_map && !dir_grad) {
+    store_dir_grad(d_dir, pix, f, ag);
+    return;
+  }
   const float4 g4 = lod_vjp<1>(e, m, tex, pyr, img, C, f.u, f.v, g);
+  const float4 gs = make_float4(g4.x * s, g4.y * s, g4.z * s, g4.w * s);
+  if (dir_grad) cube_dir_lod_vjp(f, dda, gs, ag);
+  store_dir_grad(d_dir, pix, f, ag);
   if (d_dir_da) {
-    const DirDA r = cube_uv_da_vjp(f, make_float4(g4.x * s, g4.y * s, g4.z * s, g4.w * s));
+    const DirDA r = cube_uv_da_vjp(f, gs);
     d_dir_da[3 * pix] = r.a[0];
     d_dir_da[3 * pix + 1] = r.a[1];
     d_dir_da[3 * pix + 2] = r.a[2];
@@ -714,14 +787,23 @@ dr_status build_pyramid(dr_ctx* ctx, const float* tex, int Nt, int C, const MipD
 
 struct TexArgs {
   bool cube, mip, mip_linear;
+  bool dir_grad;  // d_dir through the cube projection (extension)
   int64_t P, HWi;
   int64_t nimg;  // images per level: Nt, or Nt * 6 faces for a cube
   MipDesc m;
   int64_t pyr_floats;
 };
 
-dr_status check_tex(dr_ctx* ctx, int filter, int boundary, const float* tex, int Nt, int Ht, int Wt, int C,
+// `boundary` carries the boundary mode in its low byte and flag bits above it
+// (DR_TEXTURE_CUBE_DIR_GRAD); check_tex strips the flags into `a`.
+dr_status check_tex(dr_ctx* ctx, int filter, int& boundary, const float* tex, int Nt, int Ht, int Wt, int C,
                     int max_level, const float* uv, const float* uv_da, int N, int Hi, int Wi, TexArgs& a) {
+  const int flags = boundary & ~0xff;
+  boundary &= 0xff;
+  DR_REQUIRE(ctx, (flags & ~DR_TEXTURE_CUBE_DIR_GRAD) == 0, "texture: unknown flag bits 0x%x", flags);
+  a.dir_grad = (flags & DR_TEXTURE_CUBE_DIR_GRAD) != 0;
+  DR_REQUIRE(ctx, !a.dir_grad || boundary == DR_BOUNDARY_CUBE,
+             "texture: DR_TEXTURE_CUBE_DIR_GRAD applies to cube textures only");
   DR_REQUIRE(ctx, tex && uv, "texture: tex and uv are required");
   DR_REQUIRE(ctx, filter >= 0 && filter <= 3, "texture: bad filter mode %d", filter);
   DR_REQUIRE(ctx, boundary >= 0 && boundary <= 3, "texture: bad boundary mode %d", boundary);
@@ -797,7 +879,7 @@ extern "C" dr_status dr_texture_fwd(dr_ctx* ctx, int filter, int boundary, const
   if (a.cube && !a.mip) {
     DR_TB(ctx);
     k_tex_cube<<<grid, 256, 0, ctx->stream>>>(tex, shared, Ht, Wt, C, uv, a.P, a.HWi, out, nullptr, nullptr,
-                                              nullptr);
+                                              nullptr, false);
     DR_LAUNCHED(ctx, "tex_cube_fwd");
     return DR_OK;
   }
@@ -871,7 +953,7 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   if (a.cube && !a.mip) {
     DR_TB(ctx);
     k_tex_cube<<<grid, 256, 0, ctx->stream>>>(tex, shared, Ht, Wt, C, uv, a.P, a.HWi, nullptr, d_out, d_tex,
-                                              d_uv);
+                                              d_uv, a.dir_grad);
     DR_LAUNCHED(ctx, "tex_cube_bwd");
     return DR_OK;
   }
@@ -914,11 +996,11 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
     if (a.mip_linear)
       k_tex_cube_mip_bwd<true><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,
                                                               mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr,
-                                                              d_uv, ddda, d_bias_map);
+                                                              d_uv, ddda, d_bias_map, a.dir_grad);
     else
       k_tex_cube_mip_bwd<false><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,
                                                                mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr,
-                                                               d_uv, ddda, d_bias_map);
+                                                               d_uv, ddda, d_bias_map, a.dir_grad);
     DR_LAUNCHED(ctx, "tex_cube_mip_bwd");
   } else {
   const float4* da4 = reinterpret_cast<const float4*>(uv_da);

@@ -31,6 +31,10 @@ class BoundaryMode(enum.IntEnum):
     cube = 3
 
 
+# Flag bit of the boundary argument of dr_texture_bwd (DR_TEXTURE_CUBE_DIR_GRAD).
+CUBE_DIR_GRAD = 0x100
+
+
 class FilterMode(enum.IntEnum):
     """DiffRast.FilterMode (Texture.swift:35-40)."""
     nearest = 0
@@ -389,7 +393,7 @@ def _build_pyramid(tex_c: torch.Tensor, max_level: int):
 
 class _Texture(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, tex, uv, uv_da, bias_map, filt, bnd, bias):
+    def forward(ctx, tex, uv, uv_da, bias_map, filt, bnd, bias, dir_grad=False):
         ctx.set_materialize_grads(False)  # outputs off the loss path get None, not zeros
         tex_c = _f32(tex, "tex")
         uv_c = _f32(uv, "uv")
@@ -411,7 +415,8 @@ class _Texture(torch.autograd.Function):
                                        _ptr(uv_c), _ptr(da_c), float(bias), _ptr(map_c), N, Hi, Wi,
                                        _ptr(out)), c, "texture")
         ctx.save_for_backward(tex_c, uv_c, da_c, map_c, pyr)
-        ctx.meta = (int(filt), int(bnd), float(bias), (Nt, Ht, Wt, C, N, Hi, Wi), tuple(map_c.shape) if map_c is not None else None)
+        ctx.meta = (int(filt), int(bnd) | (CUBE_DIR_GRAD if dir_grad else 0), float(bias), (Nt, Ht, Wt, C, N, Hi, Wi),
+                    tuple(map_c.shape) if map_c is not None else None)
         return out
 
     @staticmethod
@@ -419,11 +424,11 @@ class _Texture(torch.autograd.Function):
         tex_c, uv_c, da_c, map_c, pyr = ctx.saved_tensors
         filt, bnd, bias, (Nt, Ht, Wt, C, N, Hi, Wi), map_shape = ctx.meta
         if d_out is None:
-            return None, None, None, None, None, None, None
+            return None, None, None, None, None, None, None, None
         d_out = d_out.contiguous().float()
         d_tex = torch.empty_like(tex_c)
         d_uv = torch.empty_like(uv_c)
-        mip = filt in (2, 3)
+        mip = filt in (FilterMode.linearMipmapNearest, FilterMode.linearMipmapLinear)
         d_da = torch.empty_like(da_c) if (mip and ctx.needs_input_grad[2]) else None
         d_map = (torch.empty((N, Hi, Wi), device=uv_c.device, dtype=torch.float32)
                  if (mip and map_c is not None and ctx.needs_input_grad[3]) else None)
@@ -434,14 +439,22 @@ class _Texture(torch.autograd.Function):
                 c, "texture_bwd")
         if d_map is not None:
             d_map = d_map.reshape(map_shape)
-        return d_tex, d_uv, d_da, d_map, None, None, None
+        return d_tex, d_uv, d_da, d_map, None, None, None, None
 
 
 def texture(tex: torch.Tensor, uv: torch.Tensor, uv_da: Optional[torch.Tensor] = None,
             filter_mode: FilterMode = FilterMode.linear, boundary_mode: BoundaryMode = BoundaryMode.wrap,
-            mip_level_bias: float = 0.0, mip_level_bias_map: Optional[torch.Tensor] = None):
-    """DiffRast.texture (Texture.swift:62-131)."""
+            mip_level_bias: float = 0.0, mip_level_bias_map: Optional[torch.Tensor] = None, *,
+            cube_dir_grad: bool = False):
+    """DiffRast.texture (Texture.swift:62-131).
+
+    cube_dir_grad (extension, cube textures only): the direction receives the
+    chain rule through the face projection (and, for the mipmap filters, the
+    LOD) instead of the reference's zero gradient (Texture.swift:196-197).
+    """
     filt, bnd = FilterMode(filter_mode), BoundaryMode(boundary_mode)
+    if cube_dir_grad and bnd != BoundaryMode.cube:
+        raise ValueError("texture: cube_dir_grad applies to cube textures only")
     if bnd == BoundaryMode.cube:
         # .linear as the reference; the mipmap filters are an extension that
         # takes the direction's derivatives dirDA [N, H_img, W_img, 6]
@@ -456,13 +469,13 @@ def texture(tex: torch.Tensor, uv: torch.Tensor, uv_da: Optional[torch.Tensor] =
         if tex.shape[0] not in (1, uv.shape[0]):
             raise ValueError("texture: tex batch dim incompatible with uv batch")
         if filt == FilterMode.linear:
-            return _Texture.apply(tex, uv, None, None, filt, bnd, 0.0)
+            return _Texture.apply(tex, uv, None, None, filt, bnd, 0.0, cube_dir_grad)
         if uv_da is None:
             raise ValueError("texture: mipmap filterModes require uvDA")
         if tuple(uv_da.shape) != tuple(uv.shape[:3]) + (6,):
             raise ValueError(f"texture: cube uvDA must be [N, H_img, W_img, 6] (got {tuple(uv_da.shape)})")
         _check_bias_map(mip_level_bias_map, uv)
-        return _Texture.apply(tex, uv, uv_da, mip_level_bias_map, filt, bnd, float(mip_level_bias))
+        return _Texture.apply(tex, uv, uv_da, mip_level_bias_map, filt, bnd, float(mip_level_bias), cube_dir_grad)
     if tex.dim() != 4:
         raise ValueError(f"texture: tex must be [N, H_tex, W_tex, C] (got {tuple(tex.shape)})")
     if uv.dim() != 4 or uv.shape[3] != 2:

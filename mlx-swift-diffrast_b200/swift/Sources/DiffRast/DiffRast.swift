@@ -169,9 +169,12 @@ public enum DiffRast {
         return levels
     }
 
+    /// `cubeDirGrad` (extension, cube textures only): the direction receives the
+    /// chain rule through the face projection instead of the reference's zero.
     public static func textureVJP(_ ctx: Context, _ alloc: DeviceAllocator, _ tex: DeviceTensor, uv: DeviceTensor,
                                   uvDA: DeviceTensor?, filterMode: FilterMode, boundaryMode: BoundaryMode,
-                                  mipLevelBias: Float, mipLevelBiasMap: DeviceTensor?, dOut: DeviceTensor)
+                                  mipLevelBias: Float, mipLevelBiasMap: DeviceTensor?, dOut: DeviceTensor,
+                                  cubeDirGrad: Bool = false)
         -> (dTex: DeviceTensor, dUV: DeviceTensor, dUVDA: DeviceTensor?) {
         let cube = boundaryMode == .cube
         let Nt = tex.shape[0], Ht = tex.shape[cube ? 2 : 1], Wt = tex.shape[cube ? 3 : 2]
@@ -184,7 +187,8 @@ public enum DiffRast {
         let nDA = cube ? 6 : 4
         let dDA = mip ? DeviceTensor(pointer: alloc.allocate(bytes: N * Hi * Wi * nDA * 4), shape: [N, Hi, Wi, nDA])
                       : nil
-        ctx.check(dr_texture_bwd(ctx.raw, filterMode.rawValue, boundaryMode.rawValue, tex.f, Int32(Nt), Int32(Ht),
+        let bnd = boundaryMode.rawValue | (cube && cubeDirGrad ? Int32(DR_TEXTURE_CUBE_DIR_GRAD) : 0)
+        ctx.check(dr_texture_bwd(ctx.raw, filterMode.rawValue, bnd, tex.f, Int32(Nt), Int32(Ht),
                                  Int32(Wt), Int32(C), nil, -1, uv.f, uvDA?.f, mipLevelBias, mipLevelBiasMap?.f,
                                  Int32(N), Int32(Hi), Int32(Wi), dOut.f, dTex.f, dUV.f, dDA?.f, nil),
                   "texture VJP")

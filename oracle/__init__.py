@@ -194,7 +194,9 @@ def texture(tex, uv, uv_da=None, filter_mode="linear", boundary_mode="wrap",
 
 
 def texture_bwd(tex, uv, d_out, uv_da=None, filter_mode="linear", boundary_mode="wrap",
-                mip_level_bias=0.0, mip_level_bias_map=None, max_level=-1, nthreads=0):
+                mip_level_bias=0.0, mip_level_bias_map=None, max_level=-1, nthreads=0, cube_dir_grad=False):
+    """cube_dir_grad: the d_dir chain rule through the cube projection
+    (extension, flag bit 0x100 of the boundary code; the reference returns 0)."""
     tex, uv, uv_da, bmap, d_out = _f32(tex), _f32(uv), _f32(uv_da), _f32(mip_level_bias_map), _f32(d_out)
     Nt, Ht, Wt, C = _tex_dims(tex, boundary_mode)
     N, Hi, Wi = uv.shape[:3]
@@ -203,7 +205,8 @@ def texture_bwd(tex, uv, d_out, uv_da=None, filter_mode="linear", boundary_mode=
     mip = filter_mode.startswith("linear-mipmap")
     d_uv_da = np.zeros((N, Hi, Wi, 6 if boundary_mode == "cube" else 4), np.float32) if mip else None
     d_map = np.zeros((N, Hi, Wi), np.float32) if mip else None
-    rc = lib().orc_texture_bwd(FILTERS[filter_mode], BOUNDARIES[boundary_mode], _p(tex), Nt, Ht,
+    rc = lib().orc_texture_bwd(FILTERS[filter_mode], BOUNDARIES[boundary_mode] | (0x100 if cube_dir_grad else 0),
+                               _p(tex), Nt, Ht,
                                Wt, C, max_level, _p(uv), _p(uv_da), ctypes.c_float(mip_level_bias),
                                _p(bmap), N, Hi, Wi, _p(d_out), _p(d_tex), _p(d_uv), _p(d_uv_da),
                                _p(d_map), _nt(nthreads))

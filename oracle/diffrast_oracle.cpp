@@ -698,6 +698,32 @@ inline void cube_uv_da_vjp(const CubeFrame& f, const float* g, float* dd) {
   dd[2 * f.ma + 1] = -(g[1] * (h * ks) + g[3] * (h * kt));
 }
 
+// d(loss)/d(dir) through the face coordinates (extension; the reference's
+// cube VJP returns zero, Texture.swift:196-197): u = (sc/ma + 1)/2, v alike,
+// sc = ss d[sa], tc = ts d[ta], ma = ms d[ma].  d_u, d_v: d(loss)/d(u, v).
+inline void cube_dir_vjp(const CubeFrame& f, float d_u, float d_v, float* dd) {
+  const float h = 0.5f * f.inv_ma;
+  dd[f.sa] = d_u * (h * f.ss);
+  dd[f.ta] = d_v * (h * f.ts);
+  dd[f.ma] = -((d_u * f.sc + d_v * f.tc) * (h * f.inv_ma)) * f.ms;
+}
+
+// The LOD's dependence on the direction: eff = s * cube_uv_da(dir, dirDA), so
+// with G = d(loss)/d(eff) * s, add d(loss)/d(dir) of the four derivatives
+// (Jacobian of cube_uv_da with respect to sc, tc and ma).
+inline void cube_dir_lod_vjp(const CubeFrame& f, const float* dda, const float* G, float* dd) {
+  const float a = f.inv_ma, a2 = a * a;
+  const float Dsx = dda[2 * f.sa], Dsy = dda[2 * f.sa + 1];
+  const float Dtx = dda[2 * f.ta], Dty = dda[2 * f.ta + 1];
+  const float Dmx = dda[2 * f.ma], Dmy = dda[2 * f.ma + 1];
+  const float gsm = G[0] * Dmx + G[1] * Dmy, gtm = G[2] * Dmx + G[3] * Dmy;
+  const float gss = G[0] * Dsx + G[1] * Dsy, gtt = G[2] * Dtx + G[3] * Dty;
+  const float hm = (0.5f * a2) * f.ms;
+  dd[f.sa] += -(hm * f.ss) * gsm;
+  dd[f.ta] += -(hm * f.ts) * gtm;
+  dd[f.ma] += -(hm * (f.ss * gss + f.ts * gtt)) + (a2 * a) * (f.sc * gsm + f.tc * gtm);
+}
+
 void build_pyramid(const float* tex, int Nt, int C, const MipLayout& m, float* pyr, int nthreads) {
   for (int k = 1; k < m.L; ++k) {
     const float* src = (k == 1) ? tex : pyr + m.off[k - 1];
@@ -953,6 +979,12 @@ extern "C" int orc_texture_bwd(int filter, int boundary, const float* tex, int N
                                int Hi, int Wi, const float* d_out, float* d_tex, float* d_uv,
                                float* d_uv_da, float* d_bias_map, int nthreads) {
   int64_t P = (int64_t)N * Hi * Wi;
+  // Flag bits above the boundary mode: 0x100 = the d_dir chain rule for cube
+  // textures (extension; the reference returns d_dir = 0).
+  const int flags = boundary & ~0xff;
+  boundary &= 0xff;
+  const bool dir_grad = (flags & 0x100) != 0;
+  if ((flags & ~0x100) != 0 || (dir_grad && boundary != 3)) return 1;
   if (boundary == 3 && (filter == 2 || filter == 3)) {
     // Mipmapped cube VJP (extension): d_tex through the pyramid of the
     // Nt * 6 faces, d_dir = 0 as the reference's cube VJP, d_dirDA through
@@ -975,27 +1007,39 @@ extern "C" int orc_texture_bwd(int filter, int boundary, const float* tex, int N
         cube_uv_da(f, uv_da + pix * 6, da4);
         effective_da(da4, pix, bias, bias_map, eff, &s);
         Lod ld = lod_of(eff, Ht, Wt, m.L, mip_linear);
+        float d_u = 0.0f, d_v = 0.0f;
         for (int li = 0; li < 2; ++li) {
           int k = li == 0 ? ld.k0 : ld.k1;
           float scale = li == 0 ? (1.0f - ld.frac) : ld.frac;
           int Hk = m.h[k], Wk = m.w[k];
           int64_t lvl_off = (k == 0 ? 0 : l0 + m.off[k]) + img * Hk * Wk * C;
+          const float* lb = (k == 0 ? tex : pyr.data() + m.off[k]) + img * Hk * Wk * C;
           Bilin bl = bilin(f.u, f.v, Wk, Hk, 1);
+          float dfx = 0.0f, dfy = 0.0f;
           for (int c = 0; c < C; ++c) {
             float g = d_out[pix * C + c] * scale;
-            dt[lvl_off + ((int64_t)bl.iy0 * Wk + bl.ix0) * C + c] += (double)(bl.w00 * g);
-            dt[lvl_off + ((int64_t)bl.iy0 * Wk + bl.ix1) * C + c] += (double)(bl.w10 * g);
-            dt[lvl_off + ((int64_t)bl.iy1 * Wk + bl.ix0) * C + c] += (double)(bl.w01 * g);
-            dt[lvl_off + ((int64_t)bl.iy1 * Wk + bl.ix1) * C + c] += (double)(bl.w11 * g);
+            int64_t a00 = ((int64_t)bl.iy0 * Wk + bl.ix0) * C + c, a10 = ((int64_t)bl.iy0 * Wk + bl.ix1) * C + c;
+            int64_t a01 = ((int64_t)bl.iy1 * Wk + bl.ix0) * C + c, a11 = ((int64_t)bl.iy1 * Wk + bl.ix1) * C + c;
+            dt[lvl_off + a00] += (double)(bl.w00 * g);
+            dt[lvl_off + a10] += (double)(bl.w10 * g);
+            dt[lvl_off + a01] += (double)(bl.w01 * g);
+            dt[lvl_off + a11] += (double)(bl.w11 * g);
+            if (dir_grad) {
+              dfx += g * ((1.0f - bl.fy) * (lb[a10] - lb[a00]) + bl.fy * (lb[a11] - lb[a01]));
+              dfy += g * ((1.0f - bl.fx) * (lb[a01] - lb[a00]) + bl.fx * (lb[a11] - lb[a10]));
+            }
           }
+          d_u += dfx * (float)Wk;
+          d_v += dfy * (float)Hk;
         }
-        for (int c = 0; c < 3; ++c) d_uv[pix * 3 + c] = 0.0f;
+        float* dd = d_uv + pix * 3;
+        if (dir_grad) cube_dir_vjp(f, d_u, d_v, dd);
+        else for (int c = 0; c < 3; ++c) dd[c] = 0.0f;
         float g4[4];
         lod_vjp(eff, m, tex, pyr.data(), img, C, f.u, f.v, 1, d_out + pix * C, g4);
-        if (d_uv_da) {
-          float gs[4] = {g4[0] * s, g4[1] * s, g4[2] * s, g4[3] * s};
-          cube_uv_da_vjp(f, gs, d_uv_da + pix * 6);
-        }
+        float gs[4] = {g4[0] * s, g4[1] * s, g4[2] * s, g4[3] * s};
+        if (dir_grad) cube_dir_lod_vjp(f, uv_da + pix * 6, gs, dd);
+        if (d_uv_da) cube_uv_da_vjp(f, gs, d_uv_da + pix * 6);
         if (d_bias_map) {
           float acc_m = 0.0f;
           for (int c = 0; c < 4; ++c) acc_m += g4[c] * eff[c];
@@ -1018,20 +1062,29 @@ extern "C" int orc_texture_bwd(int filter, int boundary, const float* tex, int N
       for (int64_t pix = b; pix < e; ++pix) {
         int pn = (int)(pix / ((int64_t)Hi * Wi));
         const float* d = uv + pix * 3;
-        int face; float u, v;
-        cube_project(d[0], d[1], d[2], face, u, v);
-        Bilin bl = bilin(u, v, Wt, Ht, 1);
+        CubeFrame f = cube_frame(d);
+        Bilin bl = bilin(f.u, f.v, Wt, Ht, 1);
         float w00 = (1.0f - bl.fx) * (1.0f - bl.fy), w10 = bl.fx * (1.0f - bl.fy);
         float w01 = (1.0f - bl.fx) * bl.fy, w11 = bl.fx * bl.fy;
-        double* fb = dt + ((int64_t)(Nt == 1 ? 0 : pn) * 6 + face) * Ht * Wt * C;
+        const int64_t fo = ((int64_t)(Nt == 1 ? 0 : pn) * 6 + f.face) * Ht * Wt * C;
+        double* fb = dt + fo;
+        const float* tb = tex + fo;
+        float dfx = 0.0f, dfy = 0.0f;
         for (int c = 0; c < C; ++c) {
           float g = d_out[pix * C + c];
-          fb[((int64_t)bl.iy0 * Wt + bl.ix0) * C + c] += (double)(w00 * g);
-          fb[((int64_t)bl.iy0 * Wt + bl.ix1) * C + c] += (double)(w10 * g);
-          fb[((int64_t)bl.iy1 * Wt + bl.ix0) * C + c] += (double)(w01 * g);
-          fb[((int64_t)bl.iy1 * Wt + bl.ix1) * C + c] += (double)(w11 * g);
+          int64_t a00 = ((int64_t)bl.iy0 * Wt + bl.ix0) * C + c, a10 = ((int64_t)bl.iy0 * Wt + bl.ix1) * C + c;
+          int64_t a01 = ((int64_t)bl.iy1 * Wt + bl.ix0) * C + c, a11 = ((int64_t)bl.iy1 * Wt + bl.ix1) * C + c;
+          fb[a00] += (double)(w00 * g);
+          fb[a10] += (double)(w10 * g);
+          fb[a01] += (double)(w01 * g);
+          fb[a11] += (double)(w11 * g);
+          if (dir_grad) {
+            dfx += g * ((1.0f - bl.fy) * (tb[a10] - tb[a00]) + bl.fy * (tb[a11] - tb[a01]));
+            dfy += g * ((1.0f - bl.fx) * (tb[a01] - tb[a00]) + bl.fx * (tb[a11] - tb[a10]));
+          }
         }
-        for (int c = 0; c < 3; ++c) d_uv[pix * 3 + c] = 0.0f;
+        if (dir_grad) cube_dir_vjp(f, dfx * (float)Wt, dfy * (float)Ht, d_uv + pix * 3);
+        else for (int c = 0; c < 3; ++c) d_uv[pix * 3 + c] = 0.0f;
       }
     });
     acc.reduce_to(d_tex);

@@ -36,8 +36,9 @@ class OracleBackend:
         return O.texture(tex, uv, uv_da, filter_mode, boundary_mode, bias, bias_map)
 
     def texture_bwd(self, tex, uv, d_out, uv_da=None, filter_mode="linear", boundary_mode="wrap",
-                    bias=0.0, bias_map=None):
-        return O.texture_bwd(tex, uv, d_out, uv_da, filter_mode, boundary_mode, bias, bias_map)
+                    bias=0.0, bias_map=None, cube_dir_grad=False):
+        return O.texture_bwd(tex, uv, d_out, uv_da, filter_mode, boundary_mode, bias, bias_map,
+                             cube_dir_grad=cube_dir_grad)
 
     def construct_mip(self, tex, max_level=None):
         return O.texture_construct_mip(tex, max_level)
@@ -117,13 +118,14 @@ class CudaBackend:
         return self._n(out)
 
     def texture_bwd(self, tex, uv, d_out, uv_da=None, filter_mode="linear", boundary_mode="wrap",
-                    bias=0.0, bias_map=None):
+                    bias=0.0, bias_map=None, cube_dir_grad=False):
         t = self._t(tex, grad=True)
         u = self._t(uv, grad=True)
         mip = filter_mode.startswith("linear-mipmap")
         da = self._t(uv_da, grad=mip) if uv_da is not None else None
         bm = self._t(bias_map, grad=mip) if bias_map is not None else None
-        out = self.dr.texture(t, u, da, _FILT[filter_mode], _BND[boundary_mode], bias, bm)
+        out = self.dr.texture(t, u, da, _FILT[filter_mode], _BND[boundary_mode], bias, bm,
+                              cube_dir_grad=cube_dir_grad)
         (out * self._t(d_out)).sum().backward()
         d_da = self._n(da.grad) if (mip and da is not None) else None
         d_bm = (self._n(bm.grad) if bm is not None else

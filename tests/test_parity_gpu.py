@@ -157,6 +157,10 @@ def test_texture_cube_matches_oracle(cu):
     ga = cu.texture_bwd(tex, d, d_out, boundary_mode="cube")
     gb = O.texture_bwd(tex, d, d_out, boundary_mode="cube")
     assert rel_l2(ga[0], gb[0]) < 1e-4 and np.all(ga[1] == 0)
+    # d_dir through the projection (extension, opt-in)
+    ga = cu.texture_bwd(tex, d, d_out, boundary_mode="cube", cube_dir_grad=True)
+    gb = O.texture_bwd(tex, d, d_out, boundary_mode="cube", cube_dir_grad=True)
+    assert rel_l2(ga[0], gb[0]) < 1e-4 and rel_l2(ga[1], gb[1]) < 1e-4
 
 
 @pytest.mark.parametrize("nt", [1, 2])
@@ -179,6 +183,9 @@ def test_texture_cube_mip_matches_oracle(cu, filt, nt):
     assert rel_l2(ga[0], gb[0]) < 1e-4 and np.all(ga[1] == 0)
     assert ga[2].shape == dd.shape and rel_l2(ga[2], gb[2]) < 1e-4
     assert rel_l2(ga[3], gb[3]) < 1e-4
+    ga = cu.texture_bwd(tex, d, d_out, cube_dir_grad=True, **kw)
+    gb = O.texture_bwd(tex, d, d_out, cube_dir_grad=True, **kw)
+    assert rel_l2(ga[1], gb[1]) < 1e-4 and rel_l2(ga[2], gb[2]) < 1e-4
 
 
 def test_texture_mip_large_pyramid(cu):

@@ -214,7 +214,7 @@ def test_batch1_texture_gradient_sums_over_views(backend):
 def _cube_fixture(seed=0xC0BE, Ht=8, C=2):
     g = np.random.default_rng(seed)
     tex = g.normal(size=(1, 6, Ht, Ht, C)).astype(np.float32)
-    d = np.array([[0.9, 0.2, -0.3], [-0.8, 0.35, 0.1], [0.15, 1.1, -0.4], [0.3, -0.7, 0.2],
+    d = np.array([[0.9, 0.2, -0.3], [-0.8, 0.35, 0.13], [0.15, 1.1, -0.4], [0.3, -0.7, 0.2],
                   [-0.25, 0.3, 0.95], [0.2, -0.1, -1.2]], np.float32).reshape(1, 2, 3, 3)
     dd = g.uniform(0.35, 0.7, size=(1, 2, 3, 6)).astype(np.float32)
     w = np.array([(1 + i % 5) * 0.1 for i in range(6 * C)], np.float32).reshape(1, 2, 3, C)
@@ -291,3 +291,37 @@ def test_gradcheck_cube_bias_map(backend):
     num = fd_grad(lambda x: wsum(backend.texture(tex, d, dd, filter_mode=f, boundary_mode="cube", bias_map=x),
                                  w), bmap)
     np.testing.assert_allclose(d_map, num, atol=8e-3)
+
+
+# ---- d_dir through the cube projection (extension: the reference's cube VJP
+# returns d_dir = 0, Texture.swift:196-197; opt-in with cube_dir_grad).
+
+@pytest.mark.parametrize("f", ["linear", "linear-mipmap-linear"])
+def test_gradcheck_cube_dir(backend, f):
+    tex, d, dd, w = _cube_fixture()
+    mip = f != "linear"
+    da = dd if mip else None
+    _, d_dir0, _, _ = backend.texture_bwd(tex, d, w, da, filter_mode=f, boundary_mode="cube")
+    assert np.all(d_dir0 == 0)  # the reference's behaviour stays the default
+    _, d_dir, _, _ = backend.texture_bwd(tex, d, w, da, filter_mode=f, boundary_mode="cube", cube_dir_grad=True)
+    num = fd_grad(lambda x: wsum(backend.texture(tex, x, da, filter_mode=f, boundary_mode="cube"), w), d)
+    assert np.abs(num).max() > 1e-1
+    np.testing.assert_allclose(d_dir, num, atol=8e-3)
+
+
+def test_cube_dir_grad_pz_face_matches_uv_grad(backend):
+    # On +Z with z = 1: u = (x + 1) / 2, v = (1 - y) / 2, so d_x = d_u / 2,
+    # d_y = -d_v / 2 and d_z = -(x d_u - y d_v) / 2 (d_u, d_v from the 2D path).
+    tex, _, _, _ = _cube_fixture()
+    g = np.random.default_rng(9)
+    xy = g.uniform(-0.9, 0.9, size=(1, 3, 4, 2)).astype(np.float32)
+    d = np.concatenate([xy, np.ones((1, 3, 4, 1), np.float32)], -1)
+    uv = np.stack([(xy[..., 0] + 1.0) * 0.5, (-xy[..., 1] + 1.0) * 0.5], -1).astype(np.float32)
+    w = g.normal(size=(1, 3, 4, 2)).astype(np.float32)
+    face = np.ascontiguousarray(tex[:, 4])
+    _, d_dir, _, _ = backend.texture_bwd(tex, d, w, boundary_mode="cube", cube_dir_grad=True)
+    _, d_uv, _, _ = backend.texture_bwd(face, uv, w, boundary_mode="clamp")
+    np.testing.assert_allclose(d_dir[..., 0], 0.5 * d_uv[..., 0], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(d_dir[..., 1], -0.5 * d_uv[..., 1], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(d_dir[..., 2], -0.5 * (xy[..., 0] * d_uv[..., 0] - xy[..., 1] * d_uv[..., 1]),
+                               rtol=1e-4, atol=1e-5)
