@@ -38,9 +38,17 @@ WORKLOADS = {
     "cfg4": "1M-triangle soup (20% in edge-sharing strips), 32 views/GPU at 1024^2, 2 depth-peeled layers with rast_db, "
             "interpolate A=8 diffAttrs=.all, antialias+topology hash, MSE; bwd d_pos(->shared verts)/d_attr",
     "cfg5": "geodesic sphere 499,280 tris, 256 views 2048^2 sharded over GPUs, rast_db, normals diffAttrs=.all, "
-            "trilinear cube 6x1024^2x3 (face pyramids, LOD from the normals' derivatives), antialias, MSE; "
-            "bwd d_verts/d_tex(all levels)",
+            "trilinear cube 6x1024^2x3 (an extension of the reference: face pyramids, LOD from the normals' "
+            "derivatives), antialias, MSE; bwd d_verts/d_tex(all levels)",
 }
+CFG5_LINEAR = ("geodesic sphere 499,280 tris, 256 views 2048^2 sharded over GPUs, cube 6x1024^2x3 in the reference's "
+               ".linear mode, antialias, MSE; bwd d_verts/d_tex")
+def workload_text(args) -> str:
+    if args.config == "cfg5" and args.cube_filter == "linear":
+        return CFG5_LINEAR
+    return WORKLOADS[args.config]
+
+
 # Configurations whose per-GPU work is fixed as N grows (each rank renders the
 # configuration's full view count); cfg5 splits its 256 views over the ranks.
 WEAK = {"cfg1", "cfg2", "cfg3", "cfg4"}
@@ -231,7 +239,7 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
 
 # --------------------------------------------------------- CPU baseline
 
-def cpu_chain_sample(cfg: str, nthreads: int):
+def cpu_chain_sample(cfg: str, nthreads: int, cube_filter: str = "trilinear"):
     """Build a bounded sample of the configuration for the CPU oracle chain.
     Returns (callable, pixels, description)."""
     import numpy as np
@@ -271,13 +279,14 @@ def cpu_chain_sample(cfg: str, nthreads: int):
     g = np.random.default_rng(16)
     tgt = g.random((1,) + s["res"] + (3,)).astype(np.float32)
     topo = oracle.topology_hash(s["tri"])
-    f = lambda: OC.cfg5(pos, s["tri"], s["unit"], s["cube"], tgt, s["res"], topo, nthreads)  # noqa: E731
-    return f, s["res"][0] * s["res"][1], "1 of 256 views of cfg5"
+    fm = "linear" if cube_filter == "linear" else "linear-mipmap-linear"
+    f = lambda: OC.cfg5(pos, s["tri"], s["unit"], s["cube"], tgt, s["res"], topo, nthreads, fm)  # noqa: E731
+    return f, s["res"][0] * s["res"][1], f"1 of 256 views of cfg5 ({cube_filter} cube)"
 
 
-def time_cpu(cfg: str, reps: int = 2):
+def time_cpu(cfg: str, reps: int = 2, cube_filter: str = "trilinear"):
     nthreads = os.cpu_count() or 1
-    f, pixels, desc = cpu_chain_sample(cfg, nthreads)
+    f, pixels, desc = cpu_chain_sample(cfg, nthreads, cube_filter)
     f()  # warm-up (oracle scratch pool, page faults)
     ts = []
     for _ in range(reps):
@@ -303,7 +312,7 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     nthreads = os.cpu_count() or 1
-    f, pixels, desc = cpu_chain_sample(args.config, nthreads)
+    f, pixels, desc = cpu_chain_sample(args.config, nthreads, args.cube_filter)
     for _ in range(args.warmup):
         f()
     t0 = time.perf_counter()
@@ -315,7 +324,7 @@ def run_reference(args, ws, rank):
             "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
             "scaling": "weak" if args.config in WEAK else "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded PCG64 scenes)", "impl": "reference",
-            "config": {"workload": f"{args.config}: {WORKLOADS[args.config]}", "sample_per_step": desc},
+            "config": {"workload": f"{args.config}: {workload_text(args)}", "sample_per_step": desc},
             "cpu_baseline": {"value": v, "unit": "Mpx/s", "cores": nthreads, "kind": "port",
                              "sample": desc + " per step; CPU oracle restatement of the reference kernels"},
             "e2e": {"value": v, "unit": "Mpx/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -332,6 +341,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--views", type=int, default=0, help="override views per GPU (profiling runs)")
+    ap.add_argument("--cube-filter", default="trilinear", choices=["trilinear", "linear"],
+                    help="cfg5: trilinear cube (the configuration's text; an extension of the reference) or the "
+                         "reference's own .linear cube mode")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
 
@@ -360,6 +372,8 @@ def main():
         kw = dict(view_lo=lo, view_hi=hi, total_views=tot)
     elif cfg != "cfg1":
         kw = dict(view_lo=lo, view_hi=hi)
+    if cfg == "cfg5" and args.cube_filter == "linear":
+        kw["filter_mode"] = diffrast.FilterMode.linear
     chain = chains.CHAINS[cfg](dev, **kw)
     torch.cuda.synchronize()
 
@@ -442,7 +456,7 @@ def main():
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         try:
-            cpu = time_cpu(cfg)
+            cpu = time_cpu(cfg, cube_filter=args.cube_filter)
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"error": str(ex)[:200]}
 
@@ -451,7 +465,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
                 "scaling": "weak" if cfg in WEAK else "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded PCG64 scenes, seeded torch targets)",
-                "config": {"workload": f"{cfg}: {WORKLOADS[cfg]}", "views_per_gpu": chain.info.n_views,
+                "config": {"workload": f"{cfg}: {workload_text(args)}", "views_per_gpu": chain.info.n_views,
                            "resolution": list(chain.info.res), "pixels_per_step": pixels_all,
                            "parallelism": f"dp{ws} (views sharded, grads all-reduced)" if ws > 1 else "single GPU",
                            "l2": "inputs larger than L2 (per-step tensors are GBs; no flush needed)"},

@@ -31,6 +31,17 @@ enum : unsigned {
 #ifndef DR_MINB_AA_BWD
 #define DR_MINB_AA_BWD 5
 #endif
+// Texture VJPs (scatter-bound: latency of the float atomics) and the mipmap
+// forwards (dependent gathers): four resident CTAs (64 registers) measured
+// faster than three without spills, and than five or six with more spills
+// (cfg3 / cfg5).  A bound of one CTA lets the compiler take more registers
+// and is slower still.
+#ifndef DR_MINB_TEX_BWD
+#define DR_MINB_TEX_BWD 4
+#endif
+#ifndef DR_MINB_TEX_FWD
+#define DR_MINB_TEX_FWD 4
+#endif
 
 // Workspace slots: each is an independent grow-only device buffer.
 enum WsSlot {

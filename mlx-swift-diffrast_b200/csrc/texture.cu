@@ -134,61 +134,148 @@ __device__ __forceinline__ void hot_flush(HotCache* hc, int C) {
   }
 }
 
-// d_tex scatter of one tap: adds w * (g[c] * gscale) to p[c] (c < C) for
+// Global float atomics of one texel's C <= 4 channel sums, as wide as the
+// address allows: one float4 (16-byte aligned C == 4), else float2 pairs on
+// 8-byte boundaries and scalars around them.  All-zero groups issue nothing
+// (d_tex starts at +0 and adding +-0 leaves every value unchanged).
+__device__ __forceinline__ void red_add(float* p, float a) {
+  if (a != 0.0f) atomicAdd(p, a);
+}
+__device__ __forceinline__ void red_add2(float* p, float a, float b) {
+  if (a != 0.0f || b != 0.0f) atomicAdd(reinterpret_cast<float2*>(p), make_float2(a, b));
+}
+__device__ __forceinline__ void red_add_texel(float* p, int C, float v0, float v1, float v2, float v3) {
+  const uintptr_t ad = (uintptr_t)p;
+  const bool a8 = (ad & 7) == 0;
+  switch (C) {
+    case 1:
+      red_add(p, v0);
+      return;
+    case 2:
+      if (a8) {
+        red_add2(p, v0, v1);
+      } else {
+        red_add(p, v0);
+        red_add(p + 1, v1);
+      }
+      return;
+    case 3: {
+      // Texels of 12 bytes alternate between 8-byte aligned and not: every
+      // lane issues one float2 (channels 0-1 or 1-2) and one scalar (2 or 0)
+      // with per-lane addresses, so the warp runs two atomics, not two paths.
+      red_add2(a8 ? p : p + 1, a8 ? v0 : v1, a8 ? v1 : v2);
+      red_add(a8 ? p + 2 : p, a8 ? v2 : v0);
+      return;
+    }
+    default:  // 4
+      if ((ad & 15) == 0) {
+        if (v0 != 0.0f || v1 != 0.0f || v2 != 0.0f || v3 != 0.0f)
+          atomicAdd(reinterpret_cast<float4*>(p), make_float4(v0, v1, v2, v3));
+      } else if (a8) {
+        red_add2(p, v0, v1);
+        red_add2(p + 2, v2, v3);
+      } else {
+        red_add(p, v0);
+        red_add2(p + 1, v1, v2);
+        red_add(p + 3, v3);
+      }
+      return;
+  }
+}
+
+// d_tex scatter of one tap for C <= 4: adds v.{x,y,z,w}[c] (c < C) to p[c] for
 // every lane.  Lanes of a warp that hit the same texel (runs of neighbouring
 // pixels: a magnified texture, or background pixels that all sample one
 // texel) are summed first with a segmented warp reduction, so each run issues
-// one atomic per channel instead of one per pixel; a run covering the whole
-// warp goes to the CTA's hot cache when one is given (C <= 4); a zero
-// contribution issues no atomic (d_tex starts at +0, and adding +-0 to +0
-// leaves +0).  All 32 lanes of the warp must call it; lanes with on == false
-// add nothing.
-__device__ __forceinline__ void scatter_tap(float* p, float w, const float* __restrict__ g, float gscale, int C,
-                                            bool on, int lane, HotCache* hc = nullptr) {
+// one (vector) atomic instead of one per pixel; a run covering the whole warp
+// goes to the CTA's hot cache when one is given.  All 32 lanes of the warp
+// must call it; lanes with on == false add nothing.
+__device__ __forceinline__ void scatter_tap4(float* p, float4 v, int C, bool on, int lane, HotCache* hc) {
   const long long key = on ? (long long)(uintptr_t)p : -1ll - (long long)lane;
   bool head;
   const int seg_end = warp_runs(key, lane, head);
   const int span = warp_max_run(lane, seg_end, head);
-  if (span == 1) {
-    if (on)
-      for (int c = 0; c < C; ++c) {
-        const float v = w * (__ldg(g + c) * gscale);
-        if (v != 0.0f) atomicAdd(p + c, v);
-      }
-    return;
-  }
-  if (hc && span == 32 && C <= kHotC) {
+  if (!on) v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (hc && span == 32) {
     // One run spans the warp: all 32 lanes are on and share p.
-    float sum[kHotC];
+    float sum[kHotC] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int c = 0; c < kHotC; ++c) {
-      float v = c < C ? w * (__ldg(g + c) * gscale) : 0.0f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      sum[c] = v;
+      for (int o = 16; o > 0; o >>= 1) sum[c] += __shfl_xor_sync(0xffffffffu, sum[c], o);
     }
     if (lane == 0) {
       const unsigned long long k = (unsigned long long)(uintptr_t)p;
       const int slot = (int)((k >> 4) % kHotSlots);
       const unsigned long long prev = atomicCAS(&hc->key[slot], 0ull, k);
       if (prev == 0ull || prev == k) {
-        for (int c = 0; c < C; ++c)
-          if (sum[c] != 0.0f) atomicAdd(&hc->val[slot][c], sum[c]);
+#pragma unroll
+        for (int c = 0; c < kHotC; ++c)
+          if (c < C && sum[c] != 0.0f) atomicAdd(&hc->val[slot][c], sum[c]);
       } else {
-        for (int c = 0; c < C; ++c)
-          if (sum[c] != 0.0f) atomicAdd(p + c, sum[c]);
+        red_add_texel(p, C, sum[0], sum[1], sum[2], sum[3]);
       }
     }
     return;
   }
+  if (span > 1) {
+    v.x = warp_seg_sum(v.x, lane, seg_end, span);
+    if (C > 1) v.y = warp_seg_sum(v.y, lane, seg_end, span);
+    if (C > 2) v.z = warp_seg_sum(v.z, lane, seg_end, span);
+    if (C > 3) v.w = warp_seg_sum(v.w, lane, seg_end, span);
+  }
+  if (on && head) red_add_texel(p, C, v.x, v.y, v.z, v.w);
+}
+
+// Contribution w * (g[c] * gscale) of one tap, C <= 4 (unused channels 0).
+__device__ __forceinline__ float4 tap_contrib(float w, const float4 g, float gscale) {
+  return make_float4(w * (g.x * gscale), w * (g.y * gscale), w * (g.z * gscale), w * (g.w * gscale));
+}
+
+__device__ __forceinline__ float4 load_cot(const float* __restrict__ g, int C, bool vec4) {
+  if (vec4) return ldg4(g);
+  return make_float4(__ldg(g), C > 1 ? __ldg(g + 1) : 0.f, C > 2 ? __ldg(g + 2) : 0.f, C > 3 ? __ldg(g + 3) : 0.f);
+}
+
+// d_tex scatter of one tap: adds w * (g[c] * gscale) to p[c] (c < C).  As
+// scatter_tap4 for C <= 4; wider texels sum each channel over the runs and
+// issue scalar atomics from the run heads.  A zero contribution issues no
+// atomic (d_tex starts at +0, and adding +-0 to +0 leaves +0).
+__device__ __forceinline__ void scatter_tap(float* p, float w, const float* __restrict__ g, float gscale, int C,
+                                            bool on, int lane, HotCache* hc = nullptr) {
+  if (C <= 4) {
+    const float4 gv = on ? load_cot(g, C, false) : make_float4(0.f, 0.f, 0.f, 0.f);
+    scatter_tap4(p, tap_contrib(w, gv, gscale), C, on, lane, hc);
+    return;
+  }
+  const long long key = on ? (long long)(uintptr_t)p : -1ll - (long long)lane;
+  bool head;
+  const int seg_end = warp_runs(key, lane, head);
+  const int span = warp_max_run(lane, seg_end, head);
   for (int c = 0; c < C; ++c) {
     float v = on ? w * (__ldg(g + c) * gscale) : 0.0f;
-    v = warp_seg_sum(v, lane, seg_end, span);
+    if (span > 1) v = warp_seg_sum(v, lane, seg_end, span);
     if (on && head && v != 0.0f) atomicAdd(p + c, v);
   }
 }
 
-// ---------------------------------------------------------------- bilinear
+// The four taps of one bilinear sample (weights q.w**, clamp / wrap / zero
+// masks included): the pixel's cotangent g (C channels; gv = its first four)
+// times `scale` and each tap's weight.
+__device__ __forceinline__ void scatter_bilin(float* db, const Taps& q, const float* __restrict__ g, float4 gv,
+                                              float scale, int C, bool on, int lane, HotCache* hc) {
+  if (C <= 4) {
+    scatter_tap4(db + q.a00 * C, tap_contrib(q.w00, gv, scale), C, on, lane, hc);
+    scatter_tap4(db + q.a10 * C, tap_contrib(q.w10, gv, scale), C, on, lane, hc);
+    scatter_tap4(db + q.a01 * C, tap_contrib(q.w01, gv, scale), C, on, lane, hc);
+    scatter_tap4(db + q.a11 * C, tap_contrib(q.w11, gv, scale), C, on, lane, hc);
+  } else {
+    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, on, lane, hc);
+    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, on, lane, hc);
+    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, on, lane, hc);
+    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, on, lane, hc);
+  }
+}
 
 template <int MODE>
 __global__ void k_tex_linear_fwd(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
@@ -205,7 +292,7 @@ __global__ void k_tex_linear_fwd(const float* __restrict__ tex, bool tex_shared,
 
 // d_tex scatter (Texture.swift:407-459) and d_uv (472-521) in one pass.
 template <int MODE>
-__global__ void k_tex_linear_bwd(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
+__global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_linear_bwd(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
                                  const float2* __restrict__ uv, int64_t P, int64_t HWi,
                                  const float* __restrict__ d_out, float* __restrict__ d_tex,
                                  float2* __restrict__ d_uv) {
@@ -219,13 +306,11 @@ __global__ void k_tex_linear_bwd(const float* __restrict__ tex, bool tex_shared,
   const float* b = tex + base;
   float* db = d_tex + base;
   const float* g = d_out + pix * C;
+  const float4 gv = (on && C <= 4) ? load_cot(g, C, false) : make_float4(0.f, 0.f, 0.f, 0.f);
   __shared__ HotCache hc;
   hot_init(&hc);
   __syncthreads();
-  scatter_tap(db + q.a00 * C, q.w00, g, 1.0f, C, on, lane, &hc);
-  scatter_tap(db + q.a10 * C, q.w10, g, 1.0f, C, on, lane, &hc);
-  scatter_tap(db + q.a01 * C, q.w01, g, 1.0f, C, on, lane, &hc);
-  scatter_tap(db + q.a11 * C, q.w11, g, 1.0f, C, on, lane, &hc);
+  scatter_bilin(db, q, g, gv, 1.0f, C, on, lane, &hc);
   hot_flush(&hc, C);
   if (!on) return;
   const float fx = q.fx, fy = q.fy;
@@ -395,7 +480,7 @@ __device__ __forceinline__ DirDA load_dir_da(const float2* __restrict__ p, int64
   return d;
 }
 
-__global__ void k_tex_cube(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
+__global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube(const float* __restrict__ tex, bool tex_shared, int Ht, int Wt, int C,
                            const float* __restrict__ dir, int64_t P, int64_t HWi, float* __restrict__ out,
                            const float* __restrict__ d_out, float* __restrict__ d_tex,
                            float* __restrict__ d_dir, bool dir_grad) {
@@ -420,13 +505,12 @@ __global__ void k_tex_cube(const float* __restrict__ tex, bool tex_shared, int H
   } else {
     const int lane = threadIdx.x & 31;
     const float* g = d_out + pix * C;
+    const float4 gv = (on && C <= 4) ? load_cot(g, C, false) : make_float4(0.f, 0.f, 0.f, 0.f);
     __shared__ HotCache hc;
     hot_init(&hc);
     __syncthreads();
-    scatter_tap(d_tex + fb + q.a00 * C, w00, g, 1.0f, C, on, lane, &hc);
-    scatter_tap(d_tex + fb + q.a10 * C, w10, g, 1.0f, C, on, lane, &hc);
-    scatter_tap(d_tex + fb + q.a01 * C, w01, g, 1.0f, C, on, lane, &hc);
-    scatter_tap(d_tex + fb + q.a11 * C, w11, g, 1.0f, C, on, lane, &hc);
+    // q.w** equal w** here: clamp taps carry no OOB mask.
+    scatter_bilin(d_tex + fb, q, g, gv, 1.0f, C, on, lane, &hc);
     hot_flush(&hc, C);
     if (!on) return;
     // d_dir is identically zero in the reference (Texture.swift:196-197); the
@@ -494,6 +578,7 @@ __device__ __forceinline__ float4 effective_da(const float4 da, int64_t pix, flo
 struct LodSel {
   int k0, k1;
   float frac;
+  float raw;  // the unclamped LOD (K22 uses it)
 };
 
 // Texture.swift:764-790.
@@ -503,8 +588,9 @@ __device__ __forceinline__ LodSel lod_select(const float4 e, int Ht, int Wt, int
   const float tx = e.z * (float)Ht, ty = e.w * (float)Ht;
   const float rho_sq = fmaxf(sx * sx + tx * tx, sy * sy + ty * ty);
   float lod = 0.5f * log2_rn(fmaxf(rho_sq, 1e-20f));
-  lod = fmaxf(0.0f, fminf((float)(L - 1), lod));
   LodSel s;
+  s.raw = lod;
+  lod = fmaxf(0.0f, fminf((float)(L - 1), lod));
   if (MIP_LINEAR) {
     s.k0 = dr_floor_i(lod);
     s.k1 = s.k0 + 1;
@@ -526,20 +612,39 @@ __device__ __forceinline__ const float* level_ptr(const float* tex, const float*
 }
 
 // K22 (Texture.swift:1011-1102): d(loss)/d(eff) of the effective uvDA through
-// the LOD, independent of MIP_LINEAR.  `img` selects the image in each level
-// (texture batch entry, or batch * 6 + face for a cube).
-template <int MODE>
-__device__ __forceinline__ float4 lod_vjp(const float4 e, const MipDesc& m, const float* __restrict__ tex,
-                                          const float* __restrict__ pyr, int64_t img, int C, float u, float v,
-                                          const float* __restrict__ g) {
-  const int Ht = m.h[0], Wt = m.w[0], L = m.L;
+// the LOD, independent of MIP_LINEAR.  lod_interior: whether the unclamped
+// LOD has a gradient; lod_grad: the gradient given
+// d_lod = sum over the two levels floor(lod), floor(lod) + 1 of
+// (-1, +1) * sample_c * g_c, accumulated level by level, channel by channel.
+__device__ __forceinline__ bool lod_interior(float lod_raw, int L) {
+  return !(lod_raw <= 0.0f || lod_raw >= (float)(L - 1));
+}
+
+__device__ __forceinline__ float4 lod_grad(const float4 e, int Ht, int Wt, float d_lod) {
   const float sx = e.x * (float)Wt, sy = e.y * (float)Wt;
   const float tx_ = e.z * (float)Ht, ty_ = e.w * (float)Ht;
   const float Asq = sx * sx + tx_ * tx_, Bsq = sy * sy + ty_ * ty_;
   const float rho_sq = fmaxf(Asq, Bsq);
-  const float lod_raw = 0.5f * log2_rn(fmaxf(rho_sq, 1e-20f));
-  float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (lod_raw <= 0.0f || lod_raw >= (float)(L - 1)) return g4;
+  const float ln2 = 0.6931471805599453f;
+  const float dlod_drho_sq = 1.0f / (2.0f * rho_sq * ln2);
+  const float A_is_max = (Asq >= Bsq) ? 1.0f : 0.0f;
+  const float B_is_max = 1.0f - A_is_max;
+  return make_float4(d_lod * dlod_drho_sq * A_is_max * 2.0f * sx * (float)Wt,
+                     d_lod * dlod_drho_sq * B_is_max * 2.0f * sy * (float)Wt,
+                     d_lod * dlod_drho_sq * A_is_max * 2.0f * tx_ * (float)Ht,
+                     d_lod * dlod_drho_sq * B_is_max * 2.0f * ty_ * (float)Ht);
+}
+
+// The same, sampling the two levels itself (mip-nearest, whose sampled level
+// is not floor(lod), and callers that did not keep the samples).  `img`
+// selects the image in each level (texture batch entry, or batch * 6 + face
+// for a cube).
+template <int MODE>
+__device__ __forceinline__ float4 lod_vjp(const float4 e, const MipDesc& m, const float* __restrict__ tex,
+                                          const float* __restrict__ pyr, int64_t img, int C, float u, float v,
+                                          float lod_raw, const float* __restrict__ g) {
+  const int L = m.L;
+  if (!lod_interior(lod_raw, L)) return make_float4(0.f, 0.f, 0.f, 0.f);
   const int k0 = dr_floor_i(lod_raw);
   int k1 = k0 + 1;
   if (k1 >= L) k1 = L - 1;
@@ -551,19 +656,23 @@ __device__ __forceinline__ float4 lod_vjp(const float4 e, const MipDesc& m, cons
     const float* b = level_ptr(tex, pyr, m, k, img, C);
     for (int c = 0; c < C; ++c) d_lod += sign * sample4(b, q, C, c) * __ldg(g + c);
   }
-  const float ln2 = 0.6931471805599453f;
-  const float dlod_drho_sq = 1.0f / (2.0f * rho_sq * ln2);
-  const float A_is_max = (Asq >= Bsq) ? 1.0f : 0.0f;
-  const float B_is_max = 1.0f - A_is_max;
-  g4.x = d_lod * dlod_drho_sq * A_is_max * 2.0f * sx * (float)Wt;
-  g4.y = d_lod * dlod_drho_sq * B_is_max * 2.0f * sy * (float)Wt;
-  g4.z = d_lod * dlod_drho_sq * A_is_max * 2.0f * tx_ * (float)Ht;
-  g4.w = d_lod * dlod_drho_sq * B_is_max * 2.0f * ty_ * (float)Ht;
-  return g4;
+  return lod_grad(e, m.h[0], m.w[0], d_lod);
 }
 
-template <int MODE, bool MIP_LINEAR>
-__global__ void k_tex_mip_fwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+// Bilinear sample of all four channels of a C == 4 level (16-byte texels),
+// per channel the same arithmetic as sample4.
+__device__ __forceinline__ float4 sample4v(const float* __restrict__ b, const Taps& q) {
+  const float4 t00 = ldg4(b + q.a00 * 4), t10 = ldg4(b + q.a10 * 4);
+  const float4 t01 = ldg4(b + q.a01 * 4), t11 = ldg4(b + q.a11 * 4);
+  return make_float4(q.w00 * t00.x + q.w10 * t10.x + q.w01 * t01.x + q.w11 * t11.x,
+                     q.w00 * t00.y + q.w10 * t10.y + q.w01 * t01.y + q.w11 * t11.y,
+                     q.w00 * t00.z + q.w10 * t10.z + q.w01 * t01.z + q.w11 * t11.z,
+                     q.w00 * t00.w + q.w10 * t10.w + q.w01 * t01.w + q.w11 * t11.w);
+}
+
+// VEC4: C == 4 with 16-byte aligned texture, pyramid and output.
+template <int MODE, bool MIP_LINEAR, bool VEC4>
+__global__ void __launch_bounds__(256, DR_MINB_TEX_FWD) k_tex_mip_fwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
                               bool tex_shared, int C, const float2* __restrict__ uv,
                               const float4* __restrict__ uv_da, float bias, const float* __restrict__ bias_map,
                               int64_t P, int64_t HWi, float* __restrict__ out) {
@@ -579,17 +688,39 @@ __global__ void k_tex_mip_fwd(const float* __restrict__ tex, const float* __rest
   const float* b0 = level_ptr(tex, pyr, m, ls.k0, nt, C);
   const float* b1 = level_ptr(tex, pyr, m, ls.k1, nt, C);
   float* o = out + pix * C;
-  for (int c = 0; c < C; ++c) {
-    // out = (1-frac)*s0, then += frac*s1 (Texture.swift:853-859)
-    const float o0 = (1.0f - ls.frac) * sample4(b0, q0, C, c);
-    o[c] = o0 + ls.frac * sample4(b1, q1, C, c);
+  // out = (1-frac)*s0, then += frac*s1 (Texture.swift:853-859)
+  const float a = 1.0f - ls.frac, f = ls.frac;
+  if constexpr (VEC4) {
+    const float4 s0 = sample4v(b0, q0), s1 = sample4v(b1, q1);
+    *reinterpret_cast<float4*>(o) =
+        make_float4(a * s0.x + f * s1.x, a * s0.y + f * s1.y, a * s0.z + f * s1.z, a * s0.w + f * s1.w);
+  } else {
+    for (int c = 0; c < C; ++c) {
+      const float o0 = a * sample4(b0, q0, C, c);
+      o[c] = o0 + f * sample4(b1, q1, C, c);
+    }
   }
 }
 
+// One channel of the mipmap VJP's per-level texel pass: d(out)/d(u, v)
+// (with the OOB masks) and, when `acc`, the K22 term sign * sample * g.
+__device__ __forceinline__ void mip_texel_terms(const Taps& q, float r00, float r10, float r01, float r11, float gv,
+                                               float scale, float sign, bool acc, float& dfx, float& dfy,
+                                               float& d_lod) {
+  const float gc = gv * scale;
+  if (acc) d_lod += sign * (q.w00 * r00 + q.w10 * r10 + q.w01 * r01 + q.w11 * r11) * gv;
+  const float t00 = r00 * q.m00, t10 = r10 * q.m10, t01 = r01 * q.m01, t11 = r11 * q.m11;
+  dfx += gc * ((1.0f - q.fy) * (t10 - t00) + q.fy * (t11 - t01));
+  dfy += gc * ((1.0f - q.fx) * (t01 - t00) + q.fx * (t11 - t10));
+}
+
 // Fused mipmap VJP: d_tex / d_pyramid scatter (K20), d_uv (K21), d_uvDA (K22)
-// and the optional gradient of the bias map.
-template <int MODE, bool MIP_LINEAR>
-__global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+// and the optional gradient of the bias map.  For MIP_LINEAR the K22 samples
+// are those of the two levels already read for d_uv (the unclamped LOD's
+// floor and floor + 1 are the sampled levels whenever K22 is non-zero).
+// VEC4: C == 4 with 16-byte aligned texture, pyramid and cotangent.
+template <int MODE, bool MIP_LINEAR, bool VEC4>
+__global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
                               bool tex_shared, int C, const float2* __restrict__ uv,
                               const float4* __restrict__ uv_da, float bias, const float* __restrict__ bias_map,
                               int64_t P, int64_t HWi, const float* __restrict__ d_out,
@@ -606,7 +737,10 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
   const LodSel ls = lod_select<MIP_LINEAR>(e, Ht, Wt, L);
   const float2 t = __ldg(uv + pix);
   const float* g = d_out + pix * C;
-  float dfx_total = 0.0f, dfy_total = 0.0f;
+  const bool want_lod = d_uv_da || d_bias_map;
+  const bool acc = MIP_LINEAR && want_lod && lod_interior(ls.raw, L);
+  const float4 gv = C <= 4 ? load_cot(g, C, VEC4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float dfx_total = 0.0f, dfy_total = 0.0f, d_lod = 0.0f;
   __shared__ HotCache hc;
   hot_init(&hc);
   __syncthreads();
@@ -614,22 +748,23 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
   for (int li = 0; li < 2; ++li) {
     const int k = li == 0 ? ls.k0 : ls.k1;
     const float scale = li == 0 ? (1.0f - ls.frac) : ls.frac;
+    const float sign = li == 0 ? -1.0f : 1.0f;
     const Taps q = bilin_taps<MODE>(t.x, t.y, m.w[k], m.h[k]);
     const float* b = level_ptr(tex, pyr, m, k, nt, C);
     float* db = (k == 0 ? d_tex : d_pyr + m.off[k]) + nt * (int64_t)m.h[k] * m.w[k] * C;
     float dfx = 0.0f, dfy = 0.0f;
-    const float fx = q.fx, fy = q.fy;
-    const bool tap_on = on && scale != 0.0f;
-    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, tap_on, lane, &hc);
-    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, tap_on, lane, &hc);
-    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, tap_on, lane, &hc);
-    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, tap_on, lane, &hc);
-    for (int c = 0; c < C; ++c) {
-      const float gc = __ldg(g + c) * scale;
-      const float t00 = __ldg(b + q.a00 * C + c) * q.m00, t10 = __ldg(b + q.a10 * C + c) * q.m10;
-      const float t01 = __ldg(b + q.a01 * C + c) * q.m01, t11 = __ldg(b + q.a11 * C + c) * q.m11;
-      dfx += gc * ((1.0f - fy) * (t10 - t00) + fy * (t11 - t01));
-      dfy += gc * ((1.0f - fx) * (t01 - t00) + fx * (t11 - t10));
+    scatter_bilin(db, q, g, gv, scale, C, on && scale != 0.0f, lane, &hc);
+    if constexpr (VEC4) {
+      const float4 T00 = ldg4(b + q.a00 * 4), T10 = ldg4(b + q.a10 * 4);
+      const float4 T01 = ldg4(b + q.a01 * 4), T11 = ldg4(b + q.a11 * 4);
+      mip_texel_terms(q, T00.x, T10.x, T01.x, T11.x, gv.x, scale, sign, acc, dfx, dfy, d_lod);
+      mip_texel_terms(q, T00.y, T10.y, T01.y, T11.y, gv.y, scale, sign, acc, dfx, dfy, d_lod);
+      mip_texel_terms(q, T00.z, T10.z, T01.z, T11.z, gv.z, scale, sign, acc, dfx, dfy, d_lod);
+      mip_texel_terms(q, T00.w, T10.w, T01.w, T11.w, gv.w, scale, sign, acc, dfx, dfy, d_lod);
+    } else {
+      for (int c = 0; c < C; ++c)
+        mip_texel_terms(q, __ldg(b + q.a00 * C + c), __ldg(b + q.a10 * C + c), __ldg(b + q.a01 * C + c),
+                        __ldg(b + q.a11 * C + c), __ldg(g + c), scale, sign, acc, dfx, dfy, d_lod);
     }
     dfx_total += dfx * (float)m.w[k];
     dfy_total += dfy * (float)m.h[k];
@@ -638,13 +773,15 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
   if (!on) return;
   d_uv[pix] = make_float2(dfx_total, dfy_total);
 
-  if (!d_uv_da && !d_bias_map) return;
-  const float4 g4 = lod_vjp<MODE>(e, m, tex, pyr, nt, C, t.x, t.y, g);
+  if (!want_lod) return;
+  float4 g4;
+  if (MIP_LINEAR) g4 = acc ? lod_grad(e, Ht, Wt, d_lod) : make_float4(0.f, 0.f, 0.f, 0.f);
+  else g4 = lod_vjp<MODE>(e, m, tex, pyr, nt, C, t.x, t.y, ls.raw, g);
   // Backward of eff = uvDA * s: d_uvDA = g * s, d_map = ln2 * sum(g * eff).
   if (d_uv_da) d_uv_da[pix] = make_float4(g4.x * s, g4.y * s, g4.z * s, g4.w * s);
   if (d_bias_map) {
-    const float acc = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
-    d_bias_map[pix] = bias_map ? acc * 0.6931471805599453f : 0.0f;
+    const float acc_m = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
+    d_bias_map[pix] = bias_map ? acc_m * 0.6931471805599453f : 0.0f;
   }
 }
 
@@ -655,7 +792,7 @@ __global__ void k_tex_mip_bwd(const float* __restrict__ tex, const float* __rest
 // reference's cube VJP; dirDA gets the LOD gradient.
 
 template <bool MIP_LINEAR>
-__global__ void k_tex_cube_mip_fwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+__global__ void __launch_bounds__(256, DR_MINB_TEX_FWD) k_tex_cube_mip_fwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
                                    bool tex_shared, int C, const float* __restrict__ dir,
                                    const float2* __restrict__ dir_da, float bias,
                                    const float* __restrict__ bias_map, int64_t P, int64_t HWi,
@@ -678,15 +815,14 @@ __global__ void k_tex_cube_mip_fwd(const float* __restrict__ tex, const float* _
   }
 }
 
-template <bool MIP_LINEAR>
-__global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+template <bool MIP_LINEAR, bool DIR_GRAD>
+__global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
                                    bool tex_shared, int C, const float* __restrict__ dir,
                                    const float2* __restrict__ dir_da, float bias,
                                    const float* __restrict__ bias_map, int64_t P, int64_t HWi,
                                    const float* __restrict__ d_out, float* __restrict__ d_tex,
                                    float* __restrict__ d_pyr, float* __restrict__ d_dir,
-                                   float2* __restrict__ d_dir_da, float* __restrict__ d_bias_map,
-                                   bool dir_grad) {
+                                   float2* __restrict__ d_dir_da, float* __restrict__ d_bias_map) {
   const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool on = pix0 < P;
   const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
@@ -698,7 +834,11 @@ __global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* _
   const float4 e = effective_da(cube_uv_da(f, dda), pix, bias, bias_map, s);
   const LodSel ls = lod_select<MIP_LINEAR>(e, m.h[0], m.w[0], m.L);
   const float* g = d_out + pix * C;
-  float d_u = 0.0f, d_v = 0.0f;
+  const bool want_lod = d_dir_da || d_bias_map || DIR_GRAD;
+  // MIP_LINEAR: the K22 samples are those of the two levels read here.
+  const bool acc = MIP_LINEAR && want_lod && lod_interior(ls.raw, m.L);
+  const float4 gv = C <= 4 ? load_cot(g, C, false) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float d_u = 0.0f, d_v = 0.0f, d_lod = 0.0f;
   __shared__ HotCache hc;
   hot_init(&hc);
   __syncthreads();
@@ -706,23 +846,16 @@ __global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* _
   for (int li = 0; li < 2; ++li) {
     const int k = li == 0 ? ls.k0 : ls.k1;
     const float scale = li == 0 ? (1.0f - ls.frac) : ls.frac;
+    const float sign = li == 0 ? -1.0f : 1.0f;
     const Taps q = bilin_taps<1>(f.u, f.v, m.w[k], m.h[k]);
     float* db = (k == 0 ? d_tex : d_pyr + m.off[k]) + img * (int64_t)m.h[k] * m.w[k] * C;
-    const bool tap_on = on && scale != 0.0f;
-    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, tap_on, lane, &hc);
-    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, tap_on, lane, &hc);
-    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, tap_on, lane, &hc);
-    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, tap_on, lane, &hc);
-    if (dir_grad) {
+    scatter_bilin(db, q, g, gv, scale, C, on && scale != 0.0f, lane, &hc);
+    if (DIR_GRAD || acc) {
       const float* b = level_ptr(tex, pyr, m, k, img, C);
       float dfx = 0.0f, dfy = 0.0f;
-      for (int c = 0; c < C; ++c) {
-        const float gc = __ldg(g + c) * scale;
-        const float t00 = __ldg(b + q.a00 * C + c), t10 = __ldg(b + q.a10 * C + c);
-        const float t01 = __ldg(b + q.a01 * C + c), t11 = __ldg(b + q.a11 * C + c);
-        dfx += gc * ((1.0f - q.fy) * (t10 - t00) + q.fy * (t11 - t01));
-        dfy += gc * ((1.0f - q.fx) * (t01 - t00) + q.fx * (t11 - t10));
-      }
+      for (int c = 0; c < C; ++c)
+        mip_texel_terms(q, __ldg(b + q.a00 * C + c), __ldg(b + q.a10 * C + c), __ldg(b + q.a01 * C + c),
+                        __ldg(b + q.a11 * C + c), __ldg(g + c), scale, sign, acc, dfx, dfy, d_lod);
       d_u += dfx * (float)m.w[k];
       d_v += dfy * (float)m.h[k];
     }
@@ -730,14 +863,16 @@ __global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* _
   hot_flush(&hc, C);
   if (!on) return;
   AxisGrad ag = {0.0f, 0.0f, 0.0f};
-  if (dir_grad) ag = cube_dir_vjp(f, d_u, d_v);
-  if (!d_dir_da && !d_bias_map && !dir_grad) {
+  if (DIR_GRAD) ag = cube_dir_vjp(f, d_u, d_v);
+  if (!want_lod) {
     store_dir_grad(d_dir, pix, f, ag);
     return;
   }
-  const float4 g4 = lod_vjp<1>(e, m, tex, pyr, img, C, f.u, f.v, g);
+  float4 g4;
+  if (MIP_LINEAR) g4 = acc ? lod_grad(e, m.h[0], m.w[0], d_lod) : make_float4(0.f, 0.f, 0.f, 0.f);
+  else g4 = lod_vjp<1>(e, m, tex, pyr, img, C, f.u, f.v, ls.raw, g);
   const float4 gs = make_float4(g4.x * s, g4.y * s, g4.z * s, g4.w * s);
-  if (dir_grad) cube_dir_lod_vjp(f, dda, gs, ag);
+  if (DIR_GRAD) cube_dir_lod_vjp(f, dda, gs, ag);
   store_dir_grad(d_dir, pix, f, ag);
   if (d_dir_da) {
     const DirDA r = cube_uv_da_vjp(f, gs);
@@ -746,8 +881,8 @@ __global__ void k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* _
     d_dir_da[3 * pix + 2] = r.a[2];
   }
   if (d_bias_map) {
-    const float acc = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
-    d_bias_map[pix] = bias_map ? acc * 0.6931471805599453f : 0.0f;
+    const float acc_m = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
+    d_bias_map[pix] = bias_map ? acc_m * 0.6931471805599453f : 0.0f;
   }
 }
 
@@ -919,16 +1054,18 @@ extern "C" dr_status dr_texture_fwd(dr_ctx* ctx, int filter, int boundary, const
     return DR_OK;
   }
   const float4* da4 = reinterpret_cast<const float4*>(uv_da);
+  const bool vec4 = C == 4 && aligned(tex, 16) && aligned(pyr, 16) && aligned(out, 16);
   DR_TB(ctx);
+#define DR_MIP_FWD(ML, V4)                                                                                          \
+  DR_MODE_SWITCH(boundary, (k_tex_mip_fwd<MODE, ML, V4><<<grid, 256, 0, ctx->stream>>>(                               \
+                               tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P, a.HWi, \
+                               out)))
   if (a.mip_linear) {
-    DR_MODE_SWITCH(boundary, (k_tex_mip_fwd<MODE, true><<<grid, 256, 0, ctx->stream>>>(
-                                 tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P,
-                                 a.HWi, out)));
+    if (vec4) { DR_MIP_FWD(true, true); } else { DR_MIP_FWD(true, false); }
   } else {
-    DR_MODE_SWITCH(boundary, (k_tex_mip_fwd<MODE, false><<<grid, 256, 0, ctx->stream>>>(
-                                 tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P,
-                                 a.HWi, out)));
+    if (vec4) { DR_MIP_FWD(false, true); } else { DR_MIP_FWD(false, false); }
   }
+#undef DR_MIP_FWD
   DR_LAUNCHED(ctx, "tex_mip_fwd");
   return DR_OK;
 }
@@ -993,28 +1130,32 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
     const float2* dda = reinterpret_cast<const float2*>(uv_da);
     float2* ddda = reinterpret_cast<float2*>(d_uv_da);
     DR_TB(ctx);
-    if (a.mip_linear)
-      k_tex_cube_mip_bwd<true><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,
-                                                              mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr,
-                                                              d_uv, ddda, d_bias_map, a.dir_grad);
-    else
-      k_tex_cube_mip_bwd<false><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,
-                                                               mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr,
-                                                               d_uv, ddda, d_bias_map, a.dir_grad);
+#define DR_CUBE_MIP_BWD(ML, DG)                                                                                     \
+  k_tex_cube_mip_bwd<ML, DG><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,       \
+                                                            mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr, d_uv, \
+                                                            ddda, d_bias_map)
+    if (a.mip_linear) {
+      if (a.dir_grad) DR_CUBE_MIP_BWD(true, true); else DR_CUBE_MIP_BWD(true, false);
+    } else {
+      if (a.dir_grad) DR_CUBE_MIP_BWD(false, true); else DR_CUBE_MIP_BWD(false, false);
+    }
+#undef DR_CUBE_MIP_BWD
     DR_LAUNCHED(ctx, "tex_cube_mip_bwd");
   } else {
   const float4* da4 = reinterpret_cast<const float4*>(uv_da);
   float4* dda4 = reinterpret_cast<float4*>(d_uv_da);
+  const bool vec4 = C == 4 && aligned(tex, 16) && aligned(pyr, 16) && aligned(d_out, 16);
   DR_TB(ctx);
+#define DR_MIP_BWD(ML, V4)                                                                                          \
+  DR_MODE_SWITCH(boundary, (k_tex_mip_bwd<MODE, ML, V4><<<grid, 256, 0, ctx->stream>>>(                               \
+                               tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P, a.HWi, \
+                               d_out, d_tex, dpyr, duv2, dda4, d_bias_map)))
   if (a.mip_linear) {
-    DR_MODE_SWITCH(boundary, (k_tex_mip_bwd<MODE, true><<<grid, 256, 0, ctx->stream>>>(
-                                 tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P,
-                                 a.HWi, d_out, d_tex, dpyr, duv2, dda4, d_bias_map)));
+    if (vec4) { DR_MIP_BWD(true, true); } else { DR_MIP_BWD(true, false); }
   } else {
-    DR_MODE_SWITCH(boundary, (k_tex_mip_bwd<MODE, false><<<grid, 256, 0, ctx->stream>>>(
-                                 tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P,
-                                 a.HWi, d_out, d_tex, dpyr, duv2, dda4, d_bias_map)));
+    if (vec4) { DR_MIP_BWD(false, true); } else { DR_MIP_BWD(false, false); }
   }
+#undef DR_MIP_BWD
   DR_LAUNCHED(ctx, "tex_mip_bwd");
   }
   if (a.m.L > 1) {
