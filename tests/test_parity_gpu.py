@@ -122,11 +122,14 @@ def test_interpolate_matches_oracle(cu, ico, A, diff, shared):
         np.testing.assert_allclose(ga[2], gb[2], rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("C", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("boundary", ["wrap", "clamp", "zero"])
 @pytest.mark.parametrize("filt", ["nearest", "linear", "linear-mipmap-nearest", "linear-mipmap-linear"])
-def test_texture_matches_oracle(cu, filt, boundary):
+def test_texture_matches_oracle(cu, filt, boundary, C):
+    # C = 4 takes the float4 texel path, C <= 4 the vector-atomic scatter
+    # (float2 pairs for C = 2, 3), C = 5 the per-channel fallback.
     g = np.random.default_rng(11)
-    tex = g.random((1, 64, 128, 3)).astype(np.float32)
+    tex = g.random((1, 64, 128, C)).astype(np.float32)
     uv = g.uniform(-0.3, 1.3, size=(2, 48, 40, 2)).astype(np.float32)
     da = (g.normal(size=(2, 48, 40, 4)) * 0.02).astype(np.float32)
     bmap = g.uniform(-1, 1, size=(2, 48, 40)).astype(np.float32)
@@ -163,13 +166,14 @@ def test_texture_cube_matches_oracle(cu):
     assert rel_l2(ga[0], gb[0]) < 1e-4 and rel_l2(ga[1], gb[1]) < 1e-4
 
 
+@pytest.mark.parametrize("C", [1, 3, 4])
 @pytest.mark.parametrize("nt", [1, 2])
 @pytest.mark.parametrize("filt", ["linear-mipmap-nearest", "linear-mipmap-linear"])
-def test_texture_cube_mip_matches_oracle(cu, filt, nt):
+def test_texture_cube_mip_matches_oracle(cu, filt, nt, C):
     # Mip-mapped cube (extension): LOD from the direction derivatives through
     # the cube projection, per-face pyramids, bias and bias map.
     g = np.random.default_rng(21)
-    tex = g.random((nt, 6, 64, 64, 3)).astype(np.float32)
+    tex = g.random((nt, 6, 64, 64, C)).astype(np.float32)
     d = g.normal(size=(2, 40, 24, 3)).astype(np.float32)
     dd = (np.exp(g.uniform(-7, 0, size=(2, 40, 24, 1))) * g.normal(size=(2, 40, 24, 6))).astype(np.float32)
     bmap = g.uniform(-1, 1, size=(2, 40, 24)).astype(np.float32)
