@@ -537,6 +537,26 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube(const float* 
 
 // ------------------------------------------------------------------ mipmap
 
+// 2x2 box filter of one level, 4 channels per thread (C == 4, 16-byte
+// aligned): the same ((t00 + t01) + (t10 + t11)) / 4 per channel.  n_out
+// counts output texels.
+__global__ void k_mip_down4(const float4* __restrict__ src, int Hs, int Ws, float4* __restrict__ dst, int Hd,
+                            int Wd, int64_t n_out) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_out) return;
+  const int x = (int)(i % Wd);
+  const int64_t ny = i / Wd;  // n * Hd + y
+  const int y = (int)(ny % Hd);
+  const int64_t n = ny / Hd;
+  const float4* s = src + n * Hs * Ws;
+  const float4 a = __ldg(s + (int64_t)(2 * y) * Ws + 2 * x);
+  const float4 b = __ldg(s + (int64_t)(2 * y) * Ws + 2 * x + 1);
+  const float4 c = __ldg(s + (int64_t)(2 * y + 1) * Ws + 2 * x);
+  const float4 d = __ldg(s + (int64_t)(2 * y + 1) * Ws + 2 * x + 1);
+  dst[i] = make_float4(((a.x + b.x) + (c.x + d.x)) * 0.25f, ((a.y + b.y) + (c.y + d.y)) * 0.25f,
+                       ((a.z + b.z) + (c.z + d.z)) * 0.25f, ((a.w + b.w) + (c.w + d.w)) * 0.25f);
+}
+
 // 2x2 box filter of one level: ((t00 + t01) + (t10 + t11)) / 4.
 __global__ void k_mip_down(const float* __restrict__ src, int Hs, int Ws, float* __restrict__ dst, int Hd,
                            int Wd, int C, int64_t n_out) {
@@ -892,33 +912,57 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube_mip_bwd(const
 
 // d_tex[level 0] += sum_k d_pyr_k[y >> k, x >> k] / 4^k: the adjoint of the
 // 2x2 mean pyramid, evaluated in one pass over level 0.
+template <bool VEC4>
 __global__ void k_mip_fold(float* __restrict__ d_tex, const float* __restrict__ d_pyr, const MipDesc m, int C) {
   // Grid (x blocks, y = level-0 row, z = texture): one thread per level-0
-  // texel, all channels, 32-bit indexing within a level.
+  // texel, all channels, 32-bit indexing within a level.  VEC4: C == 4 with
+  // 16-byte aligned buffers, one float4 per texel and level (the same sums).
   const int x = blockIdx.x * blockDim.x + threadIdx.x;
   if (x >= m.w[0]) return;
   const int y = blockIdx.y, n = blockIdx.z;
   float* dst = d_tex + (((int64_t)n * m.h[0] + y) * m.w[0] + x) * C;
-  for (int c = 0; c < C; ++c) {
-    float acc = 0.0f, w = 1.0f;
+  if constexpr (VEC4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float w = 1.0f;
     for (int k = 1; k < m.L; ++k) {
       w *= 0.25f;
-      const float* lk = d_pyr + m.off[k] + (int64_t)n * m.h[k] * m.w[k] * C;
-      acc += w * __ldg(lk + ((y >> k) * m.w[k] + (x >> k)) * C + c);
+      const float* lk = d_pyr + m.off[k] + (int64_t)n * m.h[k] * m.w[k] * 4;
+      const float4 v = ldg4(lk + ((y >> k) * m.w[k] + (x >> k)) * 4);
+      acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
     }
-    dst[c] += acc;
+    float4 d = *reinterpret_cast<float4*>(dst);
+    d.x += acc.x; d.y += acc.y; d.z += acc.z; d.w += acc.w;
+    *reinterpret_cast<float4*>(dst) = d;
+  } else {
+    for (int c = 0; c < C; ++c) {
+      float acc = 0.0f, w = 1.0f;
+      for (int k = 1; k < m.L; ++k) {
+        w *= 0.25f;
+        const float* lk = d_pyr + m.off[k] + (int64_t)n * m.h[k] * m.w[k] * C;
+        acc += w * __ldg(lk + ((y >> k) * m.w[k] + (x >> k)) * C + c);
+      }
+      dst[c] += acc;
+    }
   }
 }
 
 inline bool aligned(const void* p, unsigned a) { return ((uintptr_t)p & (a - 1)) == 0; }
 
 dr_status build_pyramid(dr_ctx* ctx, const float* tex, int Nt, int C, const MipDesc& m, float* pyr) {
+  const bool vec4 = C == 4 && aligned(tex, 16) && aligned(pyr, 16);
   for (int k = 1; k < m.L; ++k) {
     const float* src = (k == 1) ? tex : pyr + m.off[k - 1];
-    const int64_t n_out = (int64_t)Nt * m.h[k] * m.w[k] * C;
     DR_TB(ctx);
-    k_mip_down<<<grid_for(n_out, 256), 256, 0, ctx->stream>>>(src, m.h[k - 1], m.w[k - 1], pyr + m.off[k],
-                                                               m.h[k], m.w[k], C, n_out);
+    if (vec4) {
+      const int64_t n_out = (int64_t)Nt * m.h[k] * m.w[k];
+      k_mip_down4<<<grid_for(n_out, 256), 256, 0, ctx->stream>>>(
+          reinterpret_cast<const float4*>(src), m.h[k - 1], m.w[k - 1], reinterpret_cast<float4*>(pyr + m.off[k]),
+          m.h[k], m.w[k], n_out);
+    } else {
+      const int64_t n_out = (int64_t)Nt * m.h[k] * m.w[k] * C;
+      k_mip_down<<<grid_for(n_out, 256), 256, 0, ctx->stream>>>(src, m.h[k - 1], m.w[k - 1], pyr + m.off[k],
+                                                                 m.h[k], m.w[k], C, n_out);
+    }
     DR_LAUNCHED(ctx, "mip_down");
   }
   return DR_OK;
@@ -1165,7 +1209,11 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   if (a.m.L > 1) {
     DR_REQUIRE(ctx, Ht <= 65535 && a.nimg <= 65535, "texture_bwd: mip fold supports H, images <= 65535");
     DR_TB(ctx);
-    k_mip_fold<<<dim3(grid_for(Wt, 256), Ht, (unsigned)a.nimg), 256, 0, ctx->stream>>>(d_tex, dpyr, a.m, C);
+    const dim3 fg(grid_for(Wt, 256), Ht, (unsigned)a.nimg);
+    if (C == 4 && aligned(d_tex, 16) && aligned(dpyr, 16))
+      k_mip_fold<true><<<fg, 256, 0, ctx->stream>>>(d_tex, dpyr, a.m, C);
+    else
+      k_mip_fold<false><<<fg, 256, 0, ctx->stream>>>(d_tex, dpyr, a.m, C);
     DR_LAUNCHED(ctx, "mip_fold");
   }
   return DR_OK;
