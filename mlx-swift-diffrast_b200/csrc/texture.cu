@@ -7,8 +7,12 @@
 //   cube           _cube_fwd / _cube_grad_tex                   (616-738)
 //   mipmap         _trilinear_fwd / _grad_pyramid / _grad_uv / _grad_uvda
 //                  (764-1102), pyramid = textureConstructMip (144-161)
+//   mip-mapped cube and the cube d_dir chain rule: extensions (the reference
+//                  takes .linear only for cube maps and returns d_dir = 0)
 // Each backward here is ONE kernel (d_tex scatter + d_uv + d_uvDA together)
-// instead of the reference's two or three passes.  A texture with batch 1 is
+// instead of the reference's two or three passes; its d_tex scatter sums the
+// pixels of a warp that hit the same texel first and issues float2 / float4
+// atomics.  A texture with batch 1 is
 // sampled directly (the reference broadcasts it to N copies and builds N
 // pyramids, Texture.swift:282-285); gradients accumulate into the one copy.
 // Pyramid gradients of levels >= 1 are folded into d_tex level 0 by one kernel,
