@@ -341,6 +341,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--views", type=int, default=0, help="override views per GPU (profiling runs)")
+    ap.add_argument("--graph", action="store_true",
+                    help="single GPU: capture one step in a CUDA graph (fixed tile-list capacity, no host readback) "
+                         "and time its replays; the per-kernel breakdown comes from an eager pass")
+    ap.add_argument("--list-capacity", type=int, default=1 << 26,
+                    help="tile-list capacity in (tile, triangle) pairs for --graph")
     ap.add_argument("--cube-filter", default="trilinear", choices=["trilinear", "linear"],
                     help="cfg5: trilinear cube (the configuration's text; an extension of the reference) or the "
                          "reference's own .linear cube mode")
@@ -398,29 +403,69 @@ def main():
     if ws > 1:
         dist.barrier()
 
+    graph = None
+    if args.graph:
+        if ws > 1:
+            raise SystemExit("--graph is single-GPU only")
+        # Fixed list capacity: rasterize reads nothing back, so the whole step
+        # (forward, every VJP) can be captured.  Warm up on a side stream (all
+        # workspaces reach their size), then capture one step.
+        diffrast.set_raster_list_capacity(args.list_capacity, local)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                one_step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        chain.zero_grad()
+        graph = torch.cuda.CUDAGraph()
+        n0 = diffrast.launch_count(local)
+        with torch.cuda.graph(graph):
+            static_loss = one_step()
+        graph_launches = diffrast.launch_count(local) - n0
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+
+    def timed(step, timing):
+        """CUDA-event time per step over args.steps steps (barriers and
+        synchronisation on both sides), launches, per-kernel report."""
+        if timing:
+            _lib.set_timing(True, local)
+        launches0 = diffrast.launch_count(local)
+        stream = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            out = step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        rep = None
+        if timing:
+            rep = _lib.timing_report(local)
+            _lib.set_timing(False, local)
+        return e0.elapsed_time(e1) / args.steps, diffrast.launch_count(local) - launches0, rep, out
+
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.4)
-    _lib.set_timing(True, local)
-    launches0 = diffrast.launch_count(local)
-    stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(args.steps):
-        loss = one_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    launches = diffrast.launch_count(local) - launches0
-    report = _lib.timing_report(local)
-    _lib.set_timing(False, local)
+    if graph is not None:
+        def replay():
+            graph.replay()
+            return static_loss
+        ms, _, _, loss = timed(replay, False)
+        launches = graph_launches * args.steps
+        ms_eager, _, report, _ = timed(one_step, True)
+    else:
+        ms, launches, report, loss = timed(one_step, True)
     clk = clocks.stop()
     ms_max = D.max_over_ranks(ms, device=dev)
     diffrast.sync(local)
+    overflow_tiles = diffrast.raster_overflow(local) if graph is not None else None
 
     pixels_all = chain.info.pixels * ws
     value = pixels_all / (ms_max * 1e-3) / 1e6
@@ -432,7 +477,8 @@ def main():
         b = algo.get(name, 0) * args.steps
         ach = b / (tot_ms * 1e-3) / 1e9 if (b and tot_ms > 0) else None
         per_px = NCU_DRAM_BYTES_PER_PIXEL.get((cfg, name))
-        kernels[name] = {"launches": cnt, "ms_per_launch": tot_ms / cnt, "share": tot_ms / (ms * args.steps),
+        kernels[name] = {"launches": cnt, "ms_per_launch": tot_ms / cnt,
+                         "share": tot_ms / ((ms_eager if graph is not None else ms) * args.steps),
                          "algo_bytes_per_launch": (b / cnt) if b else 0,
                          "gbs": ach, "frac": (ach / peak) if ach else None,
                          "ncu_dram_bytes_per_launch": per_px * chain.info.pixels if per_px else None}
@@ -468,10 +514,15 @@ def main():
                 "config": {"workload": f"{cfg}: {workload_text(args)}", "views_per_gpu": chain.info.n_views,
                            "resolution": list(chain.info.res), "pixels_per_step": pixels_all,
                            "parallelism": f"dp{ws} (views sharded, grads all-reduced)" if ws > 1 else "single GPU",
-                           "l2": "inputs larger than L2 (per-step tensors are GBs; no flush needed)"},
+                           "l2": ("inputs larger than L2 (per-step tensors are GBs; no flush needed)"
+                                  if chain.info.pixels * 64 > 126e6 else
+                                  "working set smaller than L2 and not flushed (a small configuration)")},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "gpu_launches_per_step": launches / args.steps, "clocks": clk, "kernels": kernels,
                 "loss": float(loss.detach())}
+        if graph is not None:
+            line["execution"] = {"cuda_graph": True, "list_capacity": args.list_capacity,
+                                 "overflow_tiles": overflow_tiles, "eager_ms_per_step": ms_eager}
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

@@ -107,6 +107,22 @@ DR_API size_t dr_ctx_workspace_bytes(const dr_ctx* ctx);
 DR_API dr_status dr_ctx_set_timing(dr_ctx* ctx, int enable);
 DR_API dr_status dr_ctx_timing_report(dr_ctx* ctx, char* buf, size_t n);
 
+/* Graph-safe binning (no counterpart in the reference, whose bins hold 128
+ * entries and drop the rest).  By default every rasterize call sizes its
+ * (tile, triangle) list exactly, which takes one small device-to-host read of
+ * the list length — a synchronisation that a CUDA graph capture cannot hold.
+ * With pairs > 0 the list buffer holds `pairs` entries (allocated here, so
+ * call this before a capture) and rasterize reads nothing back: a tile whose
+ * list would run past the buffer tests every triangle of its view instead —
+ * the same result, slower — and is counted.  pairs = 0 restores exact sizing.
+ * dr_ctx_raster_overflow synchronizes the stream and returns (and resets) the
+ * number of tiles that took that path.  A captured graph holds the context's
+ * workspace pointers: replay it with the shapes it was captured with, and do
+ * not change the capacity (or grow a workspace with larger calls) while it
+ * lives. */
+DR_API dr_status dr_ctx_set_raster_list_capacity(dr_ctx* ctx, int64_t pairs);
+DR_API dr_status dr_ctx_raster_overflow(dr_ctx* ctx, int64_t* tiles);
+
 /* ---- rasterize (Rasterize.swift:44-144) -------------------------------- */
 
 /* Forward.  Replaces DiffRast.rasterize (Rasterize.swift:44) and its kernels

@@ -64,7 +64,11 @@ struct dr_ctx {
   void* ws[WS_NUM_SLOTS] = {};
   size_t ws_bytes[WS_NUM_SLOTS] = {};
   unsigned* d_err = nullptr;      // device error word
+  unsigned* d_overflow = nullptr; // tiles that took the full-scan path (fixed list capacity)
   int* h_pinned = nullptr;        // pinned host scratch for small readbacks
+  // Fixed tile-list capacity in (tile, triangle) pairs (dr_ctx_set_raster_list_capacity);
+  // 0 = size the list exactly from one readback per rasterize call.
+  int64_t list_cap = 0;
   int num_sms = 148;
   // Per-launch CUDA-event timing (dr_ctx_set_timing): events recorded on the
   // launching stream around every kernel, summed per kernel name on report.

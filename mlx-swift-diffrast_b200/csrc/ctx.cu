@@ -247,8 +247,15 @@ dr_status dr_ctx_create(int device, dr_ctx** out) {
   cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
   if (cudaMalloc(&c->d_err, sizeof(unsigned)) != cudaSuccess) { delete c; return DR_ENOMEM; }
   cudaMemset(c->d_err, 0, sizeof(unsigned));
+  if (cudaMalloc(&c->d_overflow, sizeof(unsigned)) != cudaSuccess) {
+    cudaFree(c->d_err);
+    delete c;
+    return DR_ENOMEM;
+  }
+  cudaMemset(c->d_overflow, 0, sizeof(unsigned));
   if (cudaMallocHost(&c->h_pinned, 64) != cudaSuccess) {
     cudaFree(c->d_err);
+    cudaFree(c->d_overflow);
     delete c;
     return DR_ENOMEM;
   }
@@ -265,8 +272,30 @@ void dr_ctx_destroy(dr_ctx* ctx) {
   for (int i = 0; i < WS_NUM_SLOTS; ++i)
     if (ctx->ws[i]) cudaFree(ctx->ws[i]);
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->d_overflow) cudaFree(ctx->d_overflow);
   if (ctx->h_pinned) cudaFreeHost(ctx->h_pinned);
   delete ctx;
+}
+
+dr_status dr_ctx_set_raster_list_capacity(dr_ctx* ctx, int64_t pairs) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, pairs >= 0 && pairs < (int64_t)UINT32_MAX, "raster list capacity %lld out of range",
+             (long long)pairs);
+  if (pairs > 0 && !ws_get(ctx, WS_TILE_LIST, sizeof(int32_t) * (size_t)(pairs + 1))) return DR_ENOMEM;
+  ctx->list_cap = pairs;
+  return DR_OK;
+}
+
+dr_status dr_ctx_raster_overflow(dr_ctx* ctx, int64_t* tiles) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, tiles != nullptr, "raster_overflow: tiles is required");
+  cudaError_t e = cudaMemcpyAsync(ctx->h_pinned, ctx->d_overflow, sizeof(unsigned), cudaMemcpyDeviceToHost,
+                                  ctx->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_overflow, 0, sizeof(unsigned), ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return fail(ctx, DR_ECUDA, "raster_overflow: %s", cudaGetErrorString(e));
+  *tiles = (int64_t)(unsigned)ctx->h_pinned[0];
+  return DR_OK;
 }
 
 dr_status dr_ctx_set_stream(dr_ctx* ctx, void* stream) {

@@ -205,7 +205,7 @@ k_raster_setup_binned(const float* __restrict__ pos, const float* __restrict__ x
 // segment start comes from the scan, and slots within it from shared atomics.
 __global__ void __launch_bounds__(256)
 k_raster_scatter_binned(const float4* __restrict__ rec, int T, int ntx, int nty, int chunk, int cpv,
-                        const uint32_t* __restrict__ off, int32_t* __restrict__ list) {
+                        const uint32_t* __restrict__ off, int32_t* __restrict__ list, uint32_t cap) {
   extern __shared__ uint32_t s_base[];
   const int c = blockIdx.x, n = blockIdx.y;
   const int ntiles = ntx * nty;
@@ -219,7 +219,10 @@ k_raster_scatter_binned(const float4* __restrict__ rec, int T, int ntx, int nty,
     const unsigned xs = __float_as_uint(r2.z), ys = __float_as_uint(r2.w);
     const int x0 = (int)(xs & 0xffffu), x1 = (int)(xs >> 16), y0 = (int)(ys & 0xffffu), y1 = (int)(ys >> 16);
     for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
-      for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) list[atomicAdd(&s_base[ty * ntx + tx], 1u)] = t;
+      for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) {
+        const uint32_t slot = atomicAdd(&s_base[ty * ntx + tx], 1u);
+        if (slot < cap) list[slot] = t;  // past a fixed capacity: the tile scans instead
+      }
   }
 }
 
@@ -244,7 +247,7 @@ __global__ void k_raster_setup(const float* __restrict__ pos, const float* __res
 // Scatter every valid (view, triangle) into the lists of the tiles it touches.
 // tile_cur starts as the exclusive offsets; atomicAdd hands out list slots.
 __global__ void k_raster_scatter(const float4* __restrict__ rec, int N, int T, int ntx, int nty,
-                                 uint32_t* __restrict__ tile_cur, int32_t* __restrict__ list) {
+                                 uint32_t* __restrict__ tile_cur, int32_t* __restrict__ list, uint32_t cap) {
   int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)N * T) return;
   float4 c = __ldg(rec + 3 * idx + 2);
@@ -257,7 +260,7 @@ __global__ void k_raster_scatter(const float4* __restrict__ rec, int N, int T, i
   for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
     for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) {
       uint32_t slot = atomicAdd(tc + ty * ntx + tx, 1u);
-      list[slot] = t;
+      if (slot < cap) list[slot] = t;
     }
 }
 
@@ -336,13 +339,17 @@ __device__ __forceinline__ void write_pixel(const float4* __restrict__ rec, int6
 constexpr int WARPS = TILE_PIX / 32;
 constexpr int SSTRIDE = 5;  // float4 per staged candidate (80 B)
 
-template <int MODE, bool DB>
+// CAPPED: the list buffer holds `cap` entries (fixed capacity, no readback);
+// a tile whose list runs past it stages every triangle of its view instead,
+// giving those without pixels in the tile no work items.
+template <int MODE, bool DB, bool CAPPED>
 __global__ void __launch_bounds__(TILE_PIX, 4)
 k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int nty,
                const uint32_t* __restrict__ tile_off, int off_stride,
                const int32_t* __restrict__ list, const float* __restrict__ peel,
                float4* __restrict__ rast, float4* __restrict__ rast_db,
-               float4* __restrict__ rast1, float4* __restrict__ rast_db1, unsigned* err) {
+               float4* __restrict__ rast1, float4* __restrict__ rast_db1, unsigned* err,
+               uint32_t cap, unsigned* overflow) {
   constexpr bool PEEL = MODE == 1, TWO = MODE == 2;
   __shared__ unsigned long long s_k0[TILE_PIX], s_k1[TWO ? TILE_PIX : 1];
   __shared__ float s_peel[PEEL ? TILE_PIX : 1];
@@ -375,7 +382,13 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
 
   const uint32_t gt = (uint32_t)blockIdx.x;
   const uint32_t begin = __ldg(tile_off + (int64_t)gt * off_stride);
-  const uint32_t cnt = __ldg(tile_off + (int64_t)(gt + 1) * off_stride) - begin;
+  const uint32_t end = __ldg(tile_off + (int64_t)(gt + 1) * off_stride);
+  bool scan_all = false;  // CAPPED only: the tile's list did not fit
+  if (CAPPED && end > cap) {
+    scan_all = true;
+    if (tid == 0) atomicAdd(overflow, 1u);
+  }
+  const uint32_t cnt = scan_all ? (uint32_t)T : end - begin;
   const int64_t rec_view = (int64_t)n * T;
   const int warp = tid >> 5, lane = tid & 31;
 
@@ -413,7 +426,7 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
     const uint32_t i = base + tid;
     int n_items = 0;
     if (i < cnt) {
-      const int t = __ldg(list + begin + i);
+      const int t = scan_all ? (int)i : __ldg(list + begin + i);
       const float4 a = __ldg(rec + 3 * (rec_view + t) + 0);
       const float4 bb = __ldg(rec + 3 * (rec_view + t) + 1);
       const float4 c = __ldg(rec + 3 * (rec_view + t) + 2);
@@ -423,6 +436,7 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
       // A listed candidate's rectangle always meets its tile (it was binned by it).
       const int wc = max(cx1 - cx0 + 1, 1), hc = max(cy1 - cy0 + 1, 1);
       n_items = wc * hc;
+      if (CAPPED && scan_all && (c.y == 0.0f || cx0 > cx1 || cy0 > cy1)) n_items = 0;
       const int pk = (cx0 - tx0) | ((cy0 - ty0) << 4) | (wc << 8) | (hc << 16);
       s_stage[tid * SSTRIDE + 0] = a;
       s_stage[tid * SSTRIDE + 1] = bb;
@@ -475,6 +489,10 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
         if (++row == hc && r + 1 < nmine) {
           row = 0;
           ++j;
+          // Scanned tiles stage candidates without items: skip them (an item
+          // of this thread's range lies ahead, so the loop ends).
+          if (CAPPED)
+            while (s_excl[j + 1] == s_excl[j]) ++j;
           f0 = s_stage[j * SSTRIDE + 0];
           f1 = s_stage[j * SSTRIDE + 1];
           f2 = s_stage[j * SSTRIDE + 2];
@@ -653,6 +671,8 @@ struct Prepared {
   const int32_t* list;
   int ntx, nty;
   int64_t ntiles_all;
+  uint32_t cap;  // list entries held; UINT32_MAX when sized exactly
+  bool capped;   // fixed capacity: tiles past it scan every triangle
 };
 
 // Largest per-view tile count whose histogram (4 B per tile) the binned
@@ -723,25 +743,36 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
   // off[ncnt] = total closes the last tile's range.
   DR_CUDA(ctx, cudaMemcpyAsync(off + ncnt, total, sizeof(uint32_t), cudaMemcpyDeviceToDevice, ctx->stream),
           "rasterize copy");
-  // The list length is data dependent: read it back (one small sync) and size
-  // the list buffer exactly, so no candidate is ever dropped.
-  DR_CUDA(ctx, cudaMemcpyAsync(ctx->h_pinned, total, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream),
-          "rasterize readback");
   if (!binned)
     DR_CUDA(ctx, cudaMemcpyAsync(cur, off, sizeof(uint32_t) * (size_t)ntiles_all, cudaMemcpyDeviceToDevice,
                                  ctx->stream), "rasterize copy");
-  cudaError_t e = cudaStreamSynchronize(ctx->stream);
-  if (e != cudaSuccess) return fail(ctx, DR_ECUDA, "rasterize: %s", cudaGetErrorString(e));
-  const uint32_t n_pairs = (uint32_t)ctx->h_pinned[0];
-  int32_t* list = (int32_t*)ws_get(ctx, WS_TILE_LIST, sizeof(int32_t) * (size_t)(n_pairs + 1));
+  int32_t* list;
+  uint32_t cap;
+  bool launch_scatter = NT > 0;
+  if (ctx->list_cap > 0) {
+    // Fixed capacity (dr_ctx_set_raster_list_capacity): nothing is read back.
+    cap = (uint32_t)ctx->list_cap;
+    list = (int32_t*)ws_get(ctx, WS_TILE_LIST, sizeof(int32_t) * (size_t)(cap + 1));
+  } else {
+    // The list length is data dependent: read it back (one small sync) and
+    // size the list buffer exactly, so no candidate is ever dropped.
+    DR_CUDA(ctx, cudaMemcpyAsync(ctx->h_pinned, total, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream),
+            "rasterize readback");
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return fail(ctx, DR_ECUDA, "rasterize: %s", cudaGetErrorString(e));
+    const uint32_t n_pairs = (uint32_t)ctx->h_pinned[0];
+    list = (int32_t*)ws_get(ctx, WS_TILE_LIST, sizeof(int32_t) * (size_t)(n_pairs + 1));
+    cap = UINT32_MAX;
+    launch_scatter = launch_scatter && n_pairs > 0;
+  }
   if (!list) return DR_ENOMEM;
-  if (NT > 0 && n_pairs > 0) {
+  if (launch_scatter) {
     DR_TB(ctx);
     if (binned)
       k_raster_scatter_binned<<<dim3(cpv, N), 256, hist_bytes, ctx->stream>>>(rec, T, ntx, nty, chunk, cpv, off,
-                                                                              list);
+                                                                              list, cap);
     else
-      k_raster_scatter<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(rec, N, T, ntx, nty, cur, list);
+      k_raster_scatter<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(rec, N, T, ntx, nty, cur, list, cap);
     DR_LAUNCHED(ctx, "raster_scatter");
   }
   pr.rec = rec;
@@ -751,6 +782,8 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
   pr.ntx = ntx;
   pr.nty = nty;
   pr.ntiles_all = ntiles_all;
+  pr.cap = cap;
+  pr.capped = ctx->list_cap > 0;
   return DR_OK;
 }
 
@@ -770,9 +803,16 @@ dr_status raster_layer(dr_ctx* ctx, const Prepared& pr, int T, int H, int W, con
   const int ntx = pr.ntx, nty = pr.nty;
   DR_TB(ctx);
 #define DR_RT(MODEV, DBV, PEELP)                                                                               \
-  k_raster_tiles<MODEV, DBV><<<grid, TILE_PIX, 0, ctx->stream>>>(pr.rec, T, H, W, ntx, nty, pr.tile_off,        \
-                                                                 pr.off_stride, pr.list, PEELP, r4, d4, r41, d41,  \
-                                                                 ctx->d_err)
+  do {                                                                                                         \
+    if (pr.capped)                                                                                             \
+      k_raster_tiles<MODEV, DBV, true><<<grid, TILE_PIX, 0, ctx->stream>>>(                                    \
+          pr.rec, T, H, W, ntx, nty, pr.tile_off, pr.off_stride, pr.list, PEELP, r4, d4, r41, d41, ctx->d_err, \
+          pr.cap, ctx->d_overflow);                                                                            \
+    else                                                                                                       \
+      k_raster_tiles<MODEV, DBV, false><<<grid, TILE_PIX, 0, ctx->stream>>>(                                   \
+          pr.rec, T, H, W, ntx, nty, pr.tile_off, pr.off_stride, pr.list, PEELP, r4, d4, r41, d41, ctx->d_err, \
+          pr.cap, ctx->d_overflow);                                                                            \
+  } while (0)
   if (rast1) {
     if (rast_db) DR_RT(2, true, nullptr); else DR_RT(2, false, nullptr);
   } else if (peel_layer) {

@@ -5,7 +5,14 @@ mlx-swift-diffrast's `DiffRast.*` operators.
 All compute runs in libdiffrast.so (hand-written sm_100a CUDA behind the C ABI
 of include/diffrast.h); this package binds it for torch tensors.
 """
-from ._lib import DiffRastError, launch_count, sync, workspace_bytes  # noqa: F401
+from ._lib import (  # noqa: F401
+    DiffRastError,
+    launch_count,
+    raster_overflow,
+    set_raster_list_capacity,
+    sync,
+    workspace_bytes,
+)
 from .ops import (  # noqa: F401
     BoundaryMode,
     DiffAttrs,
@@ -26,5 +33,5 @@ __all__ = [
     "BoundaryMode", "DiffAttrs", "FilterMode", "DiffRastError",
     "rasterize", "rasterize_layers", "interpolate", "texture", "texture_construct_mip", "textureConstructMip",
     "antialias_construct_topology_hash", "antialiasConstructTopologyHash", "antialias",
-    "mse_loss", "launch_count", "sync", "workspace_bytes",
+    "mse_loss", "launch_count", "sync", "workspace_bytes", "set_raster_list_capacity", "raster_overflow",
 ]

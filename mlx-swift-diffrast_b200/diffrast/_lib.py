@@ -36,6 +36,8 @@ SIGNATURES = {
     "dr_ctx_workspace_bytes": (ctypes.c_size_t, [P]),
     "dr_ctx_set_timing": (I, [P, I]),
     "dr_ctx_timing_report": (I, [P, ctypes.c_char_p, ctypes.c_size_t]),
+    "dr_ctx_set_raster_list_capacity": (I, [P, I64]),
+    "dr_ctx_raster_overflow": (I, [P, ctypes.POINTER(I64)]),
     "dr_rasterize_fwd": (I, [P, P, I, P, I, P, I, I, I, P, P, P]),
     "dr_rasterize_bwd": (I, [P, P, I, P, I, P, I, I, I, P, P, P, P]),
     "dr_rasterize_layers_fwd": (I, [P, P, I, P, I, P, I, I, I, I, P, P]),
@@ -142,3 +144,22 @@ def timing_report(device_index: int = 0) -> dict:
 def sync(device_index: int = 0):
     c = ctx_for(device_index)
     check(lib().dr_ctx_sync(c), c, "dr_ctx_sync")
+
+
+def set_raster_list_capacity(pairs: int, device_index: int = 0):
+    """Fixed (tile, triangle) list capacity for rasterize (0 = exact sizing).
+
+    With a capacity, rasterize reads nothing back to the host, so a whole
+    training step can be captured in a CUDA graph; tiles whose list would not
+    fit test every triangle of their view instead (same result, slower) and
+    are counted by raster_overflow().  Call it before capturing."""
+    c = ctx_for(device_index)
+    check(lib().dr_ctx_set_raster_list_capacity(c, int(pairs)), c, "dr_ctx_set_raster_list_capacity")
+
+
+def raster_overflow(device_index: int = 0) -> int:
+    """Tiles that scanned every triangle since the last call (synchronizes)."""
+    c = ctx_for(device_index)
+    n = I64(0)
+    check(lib().dr_ctx_raster_overflow(c, ctypes.byref(n)), c, "dr_ctx_raster_overflow")
+    return int(n.value)

@@ -45,6 +45,17 @@ public enum DiffRast {
         }
         deinit { dr_ctx_destroy(raw) }
         public func setStream(_ s: UnsafeMutableRawPointer?) { _ = dr_ctx_set_stream(raw, s) }
+        /// Fixed tile-list capacity (0 = exact sizing with one readback per
+        /// rasterize): with a capacity a whole step can be captured in a CUDA graph.
+        public func setRasterListCapacity(_ pairs: Int64) {
+            check(dr_ctx_set_raster_list_capacity(raw, pairs), "setRasterListCapacity")
+        }
+        /// Tiles that scanned every triangle since the last call (synchronizes).
+        public func rasterOverflow() -> Int64 {
+            var n: Int64 = 0
+            check(dr_ctx_raster_overflow(raw, &n), "rasterOverflow")
+            return n
+        }
         func check(_ st: dr_status, _ what: String) {
             // The reference crashes on misuse with `precondition`; keep that.
             precondition(st == DR_OK, "\(what): \(String(cString: dr_last_error(raw)))")
