@@ -75,6 +75,9 @@ def test_null_context_is_an_error_not_a_crash():
     assert L.dr_last_error(None) == b"null context"
     assert L.dr_rasterize_fwd(None, None, 0, None, 0, None, 0, 0, 0, None, None, None) == _lib.DR_EINVAL
     assert L.dr_ctx_create(0, None) == _lib.DR_EINVAL
+    n = ctypes.c_int64(0)
+    assert L.dr_ctx_set_raster_list_capacity(None, 10) == _lib.DR_EINVAL
+    assert L.dr_ctx_raster_overflow(None, ctypes.byref(n)) == _lib.DR_EINVAL
 
 
 def test_ctx_create_without_gpu_reports_status():
