@@ -56,6 +56,11 @@ public enum DiffRast {
             check(dr_ctx_raster_overflow(raw, &n), "rasterOverflow")
             return n
         }
+        /// Synchronizes the stream; crashes (as the reference's preconditions)
+        /// if a kernel met an out-of-range index since the last sync.
+        public func sync() { check(dr_ctx_sync(raw), "sync") }
+        public var launchCount: UInt64 { dr_ctx_launch_count(raw) }
+        public var workspaceBytes: Int { Int(dr_ctx_workspace_bytes(raw)) }
         func check(_ st: dr_status, _ what: String) {
             // The reference crashes on misuse with `precondition`; keep that.
             precondition(st == DR_OK, "\(what): \(String(cString: dr_last_error(raw)))")
@@ -249,5 +254,164 @@ public enum DiffRast {
                                    Int32(pos.shape[1]), tri.i, Int32(tri.shape[0]), topologyHash.i, dOut.f,
                                    dColor.f, dPos.f, work), "antialias VJP")
         return (dColor, dPos)
+    }
+
+    // MARK: extensions (no counterpart in the reference's surface)
+
+    /// Depth peeling of `numLayers` layers in one call, identical to chained
+    /// rasterize(peelLayer:) calls; setup and tile binning run once.
+    public static func rasterizeLayers(_ ctx: Context, _ alloc: DeviceAllocator, _ pos: DeviceTensor,
+                                       tri: DeviceTensor, resolution: (height: Int, width: Int), numLayers: Int,
+                                       gradDB: Bool = true, ranges: DeviceTensor? = nil)
+        -> [(rast: DeviceTensor, rastDB: DeviceTensor?)] {
+        let (N, V) = ranges != nil ? (ranges!.shape[0], pos.shape[0]) : (pos.shape[0], pos.shape[1])
+        let H = resolution.height, W = resolution.width
+        let layers: [(rast: DeviceTensor, rastDB: DeviceTensor?)] = (0..<numLayers).map { _ in
+            (DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * 16), shape: [N, H, W, 4]),
+             gradDB ? DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * 16), shape: [N, H, W, 4]) : nil)
+        }
+        let r: [UnsafeMutablePointer<Float>?] = layers.map { $0.rast.f }
+        let d: [UnsafeMutablePointer<Float>?] = layers.map { $0.rastDB?.f }
+        let st: dr_status = r.withUnsafeBufferPointer { rb in
+            d.withUnsafeBufferPointer { db in
+                dr_rasterize_layers_fwd(ctx.raw, pos.f, Int32(V), tri.i, Int32(tri.shape[0]), ranges?.i, Int32(N),
+                                        Int32(H), Int32(W), Int32(numLayers), rb.baseAddress,
+                                        gradDB ? db.baseAddress : nil)
+            }
+        }
+        ctx.check(st, "rasterizeLayers")
+        return layers
+    }
+
+    /// VJP of rasterizeLayers: d_pos summed over the layers (a layer without
+    /// a cotangent contributes nothing).
+    public static func rasterizeLayersVJP(_ ctx: Context, _ alloc: DeviceAllocator, _ pos: DeviceTensor,
+                                          tri: DeviceTensor, ranges: DeviceTensor?, rast: [DeviceTensor],
+                                          dRast: [DeviceTensor?], dRastDB: [DeviceTensor?]) -> DeviceTensor {
+        let N = rast[0].shape[0], H = rast[0].shape[1], W = rast[0].shape[2]
+        let V = ranges != nil ? pos.shape[0] : pos.shape[1]
+        let dPos = DeviceTensor(pointer: alloc.allocate(bytes: pos.count * 4), shape: pos.shape)
+        let r: [UnsafePointer<Float>?] = rast.map { UnsafePointer($0.f) }
+        let g: [UnsafePointer<Float>?] = dRast.map { $0.map { UnsafePointer($0.f) } }
+        let gd: [UnsafePointer<Float>?] = dRastDB.map { $0.map { UnsafePointer($0.f) } }
+        let st: dr_status = r.withUnsafeBufferPointer { rb in
+            g.withUnsafeBufferPointer { gb in
+                gd.withUnsafeBufferPointer { gdb in
+                    dr_rasterize_layers_bwd(ctx.raw, pos.f, Int32(V), tri.i, Int32(tri.shape[0]), ranges?.i,
+                                            Int32(N), Int32(H), Int32(W), Int32(rast.count), rb.baseAddress,
+                                            gb.baseAddress, gdb.baseAddress, dPos.f)
+                }
+            }
+        }
+        ctx.check(st, "rasterizeLayers VJP")
+        return dPos
+    }
+
+    /// Layers of the views M_n · verts (xform [N, 4, 4] row-major, verts
+    /// [V, 4]) without materialising the [N, V, 4] clip positions.
+    public static func rasterizeXF(_ ctx: Context, _ alloc: DeviceAllocator, verts: DeviceTensor,
+                                   xform: DeviceTensor, tri: DeviceTensor, resolution: (height: Int, width: Int),
+                                   numLayers: Int = 1, gradDB: Bool = true)
+        -> [(rast: DeviceTensor, rastDB: DeviceTensor?)] {
+        let N = xform.shape[0], V = verts.shape[0], H = resolution.height, W = resolution.width
+        let layers: [(rast: DeviceTensor, rastDB: DeviceTensor?)] = (0..<numLayers).map { _ in
+            (DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * 16), shape: [N, H, W, 4]),
+             gradDB ? DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * 16), shape: [N, H, W, 4]) : nil)
+        }
+        let r: [UnsafeMutablePointer<Float>?] = layers.map { $0.rast.f }
+        let d: [UnsafeMutablePointer<Float>?] = layers.map { $0.rastDB?.f }
+        let st: dr_status = r.withUnsafeBufferPointer { rb in
+            d.withUnsafeBufferPointer { db in
+                dr_rasterize_xf_fwd(ctx.raw, verts.f, Int32(V), xform.f, tri.i, Int32(tri.shape[0]), Int32(N),
+                                    Int32(H), Int32(W), Int32(numLayers), rb.baseAddress,
+                                    gradDB ? db.baseAddress : nil)
+            }
+        }
+        ctx.check(st, "rasterizeXF")
+        return layers
+    }
+
+    /// VJP of rasterizeXF: d_verts [V, 4], summed over views (M_n^T applied).
+    public static func rasterizeXFVJP(_ ctx: Context, _ alloc: DeviceAllocator, verts: DeviceTensor,
+                                      xform: DeviceTensor, tri: DeviceTensor, rast: [DeviceTensor],
+                                      dRast: [DeviceTensor?], dRastDB: [DeviceTensor?]) -> DeviceTensor {
+        let N = xform.shape[0], V = verts.shape[0], H = rast[0].shape[1], W = rast[0].shape[2]
+        let dVerts = DeviceTensor(pointer: alloc.allocate(bytes: verts.count * 4), shape: verts.shape)
+        let r: [UnsafePointer<Float>?] = rast.map { UnsafePointer($0.f) }
+        let g: [UnsafePointer<Float>?] = dRast.map { $0.map { UnsafePointer($0.f) } }
+        let gd: [UnsafePointer<Float>?] = dRastDB.map { $0.map { UnsafePointer($0.f) } }
+        let st: dr_status = r.withUnsafeBufferPointer { rb in
+            g.withUnsafeBufferPointer { gb in
+                gd.withUnsafeBufferPointer { gdb in
+                    dr_rasterize_xf_bwd(ctx.raw, verts.f, Int32(V), xform.f, tri.i, Int32(tri.shape[0]), Int32(N),
+                                        Int32(H), Int32(W), Int32(rast.count), rb.baseAddress, gb.baseAddress,
+                                        gdb.baseAddress, dVerts.f)
+                }
+            }
+        }
+        ctx.check(st, "rasterizeXF VJP")
+        return dVerts
+    }
+
+    /// antialias over the views M_n · verts (see rasterizeXF).
+    public static func antialiasXF(_ ctx: Context, _ alloc: DeviceAllocator, color: DeviceTensor, rast: DeviceTensor,
+                                   verts: DeviceTensor, xform: DeviceTensor, tri: DeviceTensor,
+                                   topologyHash: DeviceTensor, work: UnsafeMutableRawPointer? = nil) -> DeviceTensor {
+        let N = color.shape[0], H = color.shape[1], W = color.shape[2], C = color.shape[3]
+        let out = DeviceTensor(pointer: alloc.allocate(bytes: color.count * 4), shape: color.shape)
+        ctx.check(dr_antialias_xf_fwd(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f, verts.f,
+                                      Int32(verts.shape[0]), xform.f, tri.i, Int32(tri.shape[0]), topologyHash.i,
+                                      out.f, work), "antialiasXF")
+        return out
+    }
+
+    public static func antialiasXFVJP(_ ctx: Context, _ alloc: DeviceAllocator, color: DeviceTensor,
+                                      rast: DeviceTensor, verts: DeviceTensor, xform: DeviceTensor,
+                                      tri: DeviceTensor, topologyHash: DeviceTensor, dOut: DeviceTensor,
+                                      work: UnsafeRawPointer? = nil) -> (dColor: DeviceTensor, dVerts: DeviceTensor) {
+        let N = color.shape[0], H = color.shape[1], W = color.shape[2], C = color.shape[3]
+        let dColor = DeviceTensor(pointer: alloc.allocate(bytes: color.count * 4), shape: color.shape)
+        let dVerts = DeviceTensor(pointer: alloc.allocate(bytes: verts.count * 4), shape: verts.shape)
+        ctx.check(dr_antialias_xf_bwd(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f, verts.f,
+                                      Int32(verts.shape[0]), xform.f, tri.i, Int32(tri.shape[0]), topologyHash.i,
+                                      dOut.f, dColor.f, dVerts.f, work), "antialiasXF VJP")
+        return (dColor, dVerts)
+    }
+
+    /// The examples' loss `((pred - target)^2).mean()` into a device scalar
+    /// (a [1] tensor); with `dPred` also its gradient for a cotangent of 1.
+    public static func mseLoss(_ ctx: Context, _ alloc: DeviceAllocator, pred: DeviceTensor, target: DeviceTensor,
+                               dPred: DeviceTensor? = nil) -> DeviceTensor {
+        let loss = DeviceTensor(pointer: alloc.allocate(bytes: 4), shape: [1])
+        ctx.check(dr_mse_fwd_bwd(ctx.raw, pred.f, target.f, Int64(pred.count), 1.0 / Float(pred.count), dPred?.f,
+                                 loss.f, 1), "mseLoss")
+        return loss
+    }
+
+    /// VJP of mseLoss for the cotangent dLoss (a device scalar; nil means 1).
+    public static func mseVJP(_ ctx: Context, _ alloc: DeviceAllocator, pred: DeviceTensor, target: DeviceTensor,
+                              dLoss: DeviceTensor? = nil) -> DeviceTensor {
+        let dPred = DeviceTensor(pointer: alloc.allocate(bytes: pred.count * 4), shape: pred.shape)
+        ctx.check(dr_mse_bwd(ctx.raw, pred.f, target.f, Int64(pred.count), 1.0 / Float(pred.count), dLoss?.f,
+                             dPred.f), "mse VJP")
+        return dPred
+    }
+
+    /// One fused Adam step in place (MLXDiffRastExamples/Adam.swift:36-43):
+    /// `step` counts from 1; m and v start at zero.
+    public static func adamStep(_ ctx: Context, param: DeviceTensor, grad: DeviceTensor, m: DeviceTensor,
+                                v: DeviceTensor, step: Int, lr: Float, beta1: Float = 0.9, beta2: Float = 0.999,
+                                eps: Float = 1e-8, mask: DeviceTensor? = nil) {
+        let c1 = 1 - pow(beta1, Float(step)), c2 = 1 - pow(beta2, Float(step))
+        ctx.check(dr_adam_step(ctx.raw, param.f, grad.f, mask?.f, m.f, v.f, Int64(param.count), lr, beta1, beta2,
+                               eps, c1, c2), "adamStep")
+    }
+
+    /// Allocation-free topology hash (fixed table in the library, at most
+    /// DR_STATIC_TOPO_MAX_TRIS triangles): writes `topo` [T, 3].
+    public static func antialiasConstructTopologyHashStatic(tri: DeviceTensor, topo: DeviceTensor,
+                                                            stream: UnsafeMutableRawPointer?) {
+        let st = dr_antialias_construct_topology_hash_static(tri.i, Int32(tri.shape[0]), topo.i, stream)
+        precondition(st == DR_OK, "antialiasConstructTopologyHashStatic failed (\(st))")
     }
 }
