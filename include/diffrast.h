@@ -132,7 +132,10 @@ DR_API dr_status dr_ctx_raster_overflow(dr_ctx* ctx, int64_t* tiles);
  *   peel_layer: NULL, or a previous rast [N, H, W, 4] to peel through.
  *   rast: [N, H, W, 4] out.  rast_db: [N, H, W, 4] out, or NULL (gradDB=false).
  * Unlike the reference (MAX_PER_TILE=128, overflow dropped) no triangle is ever
- * dropped, and depth ties resolve to the lowest triangle index. */
+ * dropped, and depth ties resolve to the lowest triangle index.
+ * Limits: T < 2^24 (tri_id + 1 is stored as a float), H, W <= 32768, and the
+ * (16x16 tile, triangle) pairs of one call (summed over its views) below 2^32
+ * (the tile lists are offset by a 32-bit prefix sum). */
 DR_API dr_status dr_rasterize_fwd(dr_ctx* ctx, const float* pos, int V,
                            const int32_t* tri, int T, const int32_t* ranges,
                            int N, int H, int W, const float* peel_layer,
