@@ -60,3 +60,50 @@ def test_bench_options():
     assert r.returncode == 0
     for opt in ("--gpus", "--steps", "--warmup", "--config", "--impl", "--graph", "--cube-filter"):
         assert opt in r.stdout
+
+
+def _launched_names():
+    import glob
+    import re
+    names = set()
+    for f in glob.glob(os.path.join(ROOT, "mlx-swift-diffrast_b200", "csrc", "*.cu")):
+        names |= set(re.findall(r'DR_LAUNCHED\(ctx, "([a-z_0-9]+)"\)', open(f).read()))
+    return names
+
+
+def test_algorithmic_bytes_name_launched_kernels():
+    # The roofline of every bench line divides these bytes by the CUDA-event
+    # time of the kernel of the same name: every key must be a launched
+    # kernel's name, every value positive, and each configuration's main
+    # kernels present.
+    from types import SimpleNamespace as NS
+
+    import numpy as np
+
+    import bench
+    launched = _launched_names()
+
+    def info(n, h, w):
+        return NS(n_views=n, res=(h, w), pixels=n * h * w)
+
+    z = np.zeros
+    chains = {
+        "cfg1": NS(info=info(1, 256, 256)),
+        "cfg2": NS(info=info(8, 512, 512), pos=z((8, 2562, 4)), tri=z((5120, 3))),
+        "cfg3": NS(info=info(16, 1024, 1024), pos=z((16, 2562, 4)), tri=z((5120, 3))),
+        "cfg4": NS(info=info(32, 1024, 1024), base=z((2600000, 4)), tri=z((1000000, 3))),
+        "cfg5": NS(info=info(256, 2048, 2048), verts=z((249642, 4)), tri=z((499280, 3)), micro=16, filter_mode=3),
+        "cfg5-linear": NS(info=info(256, 2048, 2048), verts=z((249642, 4)), tri=z((499280, 3)), micro=16,
+                          filter_mode=1),
+    }
+    main = {"cfg1": {"raster_tiles", "interp_fwd", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd", "mse"},
+            "cfg2": {"tex_linear_fwd", "tex_linear_bwd", "interp_bwd", "aa_bwd"},
+            "cfg3": {"tex_mip_fwd", "tex_mip_bwd", "mip_down", "mip_fold", "interp_bwd"},
+            "cfg4": {"raster_tiles", "interp_fwd", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd", "mse", "mse_bwd"},
+            "cfg5": {"tex_cube_mip_fwd", "tex_cube_mip_bwd", "mip_down", "mip_fold", "aa_bwd"},
+            "cfg5-linear": {"tex_cube_fwd", "tex_cube_bwd", "aa_bwd"}}
+    for name, ch in chains.items():
+        b = bench.algorithmic_bytes(name.split("-")[0], ch)
+        assert set(b) <= launched, (name, set(b) - launched)
+        assert all(v > 0 for v in b.values()), name
+        assert main[name] <= set(b), (name, main[name] - set(b))
