@@ -2,7 +2,7 @@
  * diffrast.h — C ABI of the B200-native differentiable rasterization chain.
  *
  * This is the drop-in boundary under the Swift `DiffRast.*` operator surface of
- * mlx-swift-diffrast (Sources/MLXDiffRast/*.swift).  Every forward op is paired
+ * mlx-swift-diffrast (the .swift files of Sources/MLXDiffRast).  Every forward op is paired
  * with an explicit VJP ("_bwd") entry point; the Swift wrapper (or any other
  * host language) owns autograd and calls these two halves.
  *

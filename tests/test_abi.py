@@ -109,3 +109,12 @@ def test_first_call_path_does_not_deadlock():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stderr
     assert r.stdout.startswith(("ctx", "err"))
+
+
+@pytest.mark.parametrize("lang,std", [("c", "-std=c99"), ("c++", "-std=c++11")])
+def test_header_compiles_cleanly(lang, std):
+    # A C or C++ host includes the header alone: no warnings, no extensions.
+    cc = "gcc" if lang == "c" else "g++"
+    r = subprocess.run([cc, "-x", lang, std, "-fsyntax-only", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                        os.path.join(ROOT, "include", "diffrast.h")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
