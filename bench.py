@@ -386,6 +386,7 @@ def main():
     # the backward launches as each gradient becomes final (overlapping the
     # rest of the backward); the step waits for them at its end.
     sync = D.GradSync(chain.shared_params())
+    chain.grad_sync = sync
 
     def allreduce():
         sync.finish()

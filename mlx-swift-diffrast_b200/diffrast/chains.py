@@ -38,6 +38,14 @@ def _t(a, dev, grad=False):
 
 class Chain:
     info: ChainInfo
+    # Set by a multi-rank driver to its dist.GradSync: chains that run several
+    # backward calls per step tell it which one is the last.
+    grad_sync = None
+
+    def backward(self, loss: torch.Tensor, last: bool = True) -> None:
+        if self.grad_sync is not None:
+            self.grad_sync.arm(last)
+        loss.backward()
 
     def params(self) -> List[torch.Tensor]:
         raise NotImplementedError
@@ -262,7 +270,7 @@ class Cfg5(Chain):
             col = ops.texture(self.cube, nrm, nrm_da if mip else None, self.filter_mode, ops.BoundaryMode.cube)
             aa = ops.antialias(col, rast, self.verts, self.tri, self.topo, xform=xf)
             loss = ops.mse_loss(aa, self.target[a:b]) * ((b - a) / n)
-            loss.backward()
+            self.backward(loss, last=b == n)
             tot = loss.detach() if tot is None else tot + loss.detach()
         return tot
 

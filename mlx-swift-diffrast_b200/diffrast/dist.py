@@ -51,23 +51,39 @@ class GradSync:
     attribute table's, while the rasterizer's VJP still runs), and `finish`
     makes the current stream wait for all of them.  Every rank runs the same
     graph, so the hooks fire — and the collectives are issued — in the same
-    order everywhere.  A no-op on one rank."""
+    order everywhere.  A no-op on one rank.
+
+    A step that accumulates gradients over several backward calls
+    (micro-batches) calls `arm(last)` before each of them: only the last
+    backward's hooks launch all-reduces.  A gradient is final only then, and
+    an all-reduce launched earlier would both be summed again by the next one
+    and race with the next backward's in-place accumulation into the same
+    buffer.  `finish` re-arms, so single-backward steps need no call."""
 
     def __init__(self, params: Sequence[torch.Tensor], group=None):
         self.group = group
         self.handles = []
+        self.armed = True
         self.active = dist.is_initialized() and dist.get_world_size(group) > 1
         if self.active:
             for p in params:
                 p.register_post_accumulate_grad_hook(self._launch)
 
+    def arm(self, last: bool) -> None:
+        """Before a backward: launch the all-reduces from it only if it is the
+        step's last one."""
+        self.armed = bool(last)
+
     def _launch(self, p: torch.Tensor) -> None:
+        if not self.armed:
+            return
         self.handles.append(dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
 
     def finish(self) -> None:
         for h in self.handles:
             h.wait()
         self.handles.clear()
+        self.armed = True
 
 
 def init_from_env(timeout_s: float = 300.0) -> Tuple[int, int, int]:

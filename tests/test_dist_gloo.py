@@ -70,6 +70,37 @@ def _worker_gradsync(rank, world, port, q):
         q.put((rank, "error", repr(e)))
 
 
+def _worker_gradsync_micro(rank, world, port, q):
+    """Two backward calls per step (micro-batches), as the sharded cfg5 chain
+    runs them: the all-reduce must start once, after the last backward."""
+    import sys
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "mlx-swift-diffrast_b200"))
+    from diffrast import dist as D
+    try:
+        _init(rank, world, port)
+        a = torch.ones(4, requires_grad=True)
+        b = torch.full((3,), 2.0, requires_grad=True)
+        sync = D.GradSync([a, b])
+        launched = []
+        for step in range(2):
+            a.grad = None
+            b.grad = None
+            for micro in range(2):
+                sync.arm(micro == 1)
+                # micro-batch k contributes (k + 1) * (rank + 1) to d/da
+                loss = (a * (micro + 1) * (rank + 1)).sum() + (b * b * (rank + 1)).sum()
+                loss.backward()
+                launched.append(len(sync.handles))
+            sync.finish()
+        q.put((rank, a.grad.tolist(), b.grad.tolist(), launched))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, "error", repr(e)))
+
+
 def _worker_dead_peer(rank, world, port, q):
     import time
     import torch
@@ -145,3 +176,16 @@ def test_gradsync_sums_gradients_as_they_finish():
     # d/da = rank + 1 summed over ranks = 3; d/db = 2 b (rank + 1) summed = 4 * 3 = 12
     assert res[0][1] == res[1][1] == [3.0] * 4
     assert res[0][2] == res[1][2] == [12.0] * 3
+
+
+def test_gradsync_reduces_once_after_the_last_micro_batch():
+    res = _run(_worker_gradsync_micro)
+    for r in res:
+        assert r[1] != "error", r
+    # d/da per rank = (1 + 2)(rank + 1), summed over ranks = 3 * 3 = 9 exactly;
+    # reducing after the first micro-batch too would give 3 + 2 * 3 * ... != 9.
+    assert res[0][1] == res[1][1] == [9.0] * 4
+    # d/db per rank = 2 * (2 b)(rank + 1) = 8 (rank + 1), summed = 24
+    assert res[0][2] == res[1][2] == [24.0] * 3
+    # no all-reduce is in flight after the first micro-batch; two after the last
+    assert res[0][3] == res[1][3] == [0, 2, 0, 2]
