@@ -873,8 +873,14 @@ extern "C" dr_status dr_antialias_construct_topology_hash_static(const int32_t* 
   int32_t* rb = ra + kStaticCap;
   uint32_t* rs = reinterpret_cast<uint32_t*>(rb + kStaticCap);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // An error already pending on this thread belongs to the caller's earlier
+  // work: report it without launching, and leave it in place for the caller.
+  if (cudaPeekAtLastError() != cudaSuccess) return DR_ECUDA;
   k_topo_init<<<dr::grid_for((int64_t)cap, 256), 256, 0, s>>>(keys, cnt, cap);
+  if (cudaGetLastError() != cudaSuccess) return DR_ECUDA;
   k_topo_insert<<<dr::grid_for(E, 256), 256, 0, s>>>(tri, T, keys, cnt, ra, rb, rs, cap - 1, nullptr);
+  if (cudaGetLastError() != cudaSuccess) return DR_ECUDA;
   k_topo_classify<<<dr::grid_for(E, 256), 256, 0, s>>>(T, cnt, ra, rb, rs, topo);
-  return cudaGetLastError() == cudaSuccess ? DR_OK : DR_ECUDA;
+  if (cudaGetLastError() != cudaSuccess) return DR_ECUDA;
+  return DR_OK;
 }

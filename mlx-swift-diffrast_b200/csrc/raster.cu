@@ -152,8 +152,11 @@ __device__ __forceinline__ bool setup_one(const float* __restrict__ pos, const f
   float sx1 = FD(p1.x, p1.w), sy1 = FD(p1.y, p1.w), sz1 = FD(p1.z, p1.w);
   float sx2 = FD(p2.x, p2.w), sy2 = FD(p2.y, p2.w), sz2 = FD(p2.z, p2.w);
   float area = FS(FM(FS(sx1, sx0), FS(sy2, sy0)), FM(FS(sx2, sx0), FS(sy1, sy0)));
+  // |area| < 2^-128 (finite, non-zero) has 1/area = inf: every pixel test of
+  // the record yields an infinite or NaN depth, which is never a fragment, so
+  // the record is invalid (the oracle's setup applies the same rule).
   ok = finite3(sx0, sy0, sz0) && finite3(sx1, sy1, sz1) && finite3(sx2, sy2, sz2) &&
-       isfinite(area) && area != 0.0f;
+       isfinite(area) && area != 0.0f && isfinite(FD(1.0f, area));
   x0 = 0; x1 = -1; y0 = 0; y1 = -1;
   if (ok) {
     float minx = fminf(sx0, fminf(sx1, sx2)), maxx = fmaxf(sx0, fmaxf(sx1, sx2));
@@ -407,7 +410,10 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
     if (FM(e0, area) < 0.0f || FM(e1, area) < 0.0f || FM(e2, area) < 0.0f) return false;
     const float bw = FM(e0, f2.z), u = FM(e1, f2.z), v = FM(e2, f2.z);
     const float z = FA(FA(FM(bw, f0.z), FM(u, f1.y)), FM(v, f2.x));
-    // NaN never wins in the reference (its strict z < best_z is false).
+    // A NaN depth is never a fragment.  The reference stores one (every
+    // comparison it makes is false) and lets the next candidate in its bin
+    // order replace it; rejecting it keeps the winner independent of order,
+    // and the oracle applies the same rule.
     if (!(z >= -1.0f && z <= 1.0f)) return false;
     p = ly * TILE + lx;
     if (PEEL && z <= s_peel[p]) return false;
@@ -466,8 +472,12 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
     float4 f0 = make_float4(0.f, 0.f, 0.f, 0.f), f1 = f0, f2 = f0;
     int j = 0, pk = 0, wc = 1, hc = 1, row = 0, col = 0;
     if (nmine > 0) {
-      // The candidate holding item lo: the last j with s_excl[j] <= lo (every
-      // candidate owns >= 1 item, so s_excl is strictly increasing over [0, nc)).
+      // The candidate holding item lo: the last j with s_excl[j] <= lo.  A
+      // listed candidate owns >= 1 item, so s_excl is strictly increasing over
+      // [0, nc); in the CAPPED scan-all mode candidates may own none and s_excl
+      // is only non-decreasing, but the last j with s_excl[j] <= lo < total is
+      // still the one whose range [s_excl[j], s_excl[j+1]) holds item lo, so it
+      // owns items.
       int jh = nc - 1;
       while (j < jh) {
         const int mid = (j + jh + 1) >> 1;

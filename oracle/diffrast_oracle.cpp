@@ -128,6 +128,11 @@ void raster_setup(const float* pos, int64_t pos_n_base, const int32_t* tri,
   float v[10] = {sx0, sy0, sz0, sx1, sy1, sz1, sx2, sy2, sz2, area};
   for (int k = 0; k < 10; ++k)
     if (!finitef(v[k])) return;
+  // A finite, non-zero but tiny area (|area| < 2^-128) has 1/area = inf: every
+  // pixel of such a record gets bw/u/v of +-inf or NaN (0 * inf), hence a depth
+  // that is infinite or NaN and never a fragment (see the z test in the pixel
+  // loop).  Marking it invalid here changes no output and skips the work.
+  if (!finitef(1.0f / area)) return;
   for (int k = 0; k < 10; ++k) rec[k] = v[k];
 }
 
@@ -228,6 +233,13 @@ extern "C" int orc_rasterize_fwd(const float* pos, int V, const int32_t* tri, in
               float v = e2 * inv_area;
               float z_pix = bw * sz0 + u * sz1 + v * sz2;
               if (z_pix < -1.0f || z_pix > 1.0f) continue;
+              // Deviation from Rasterize.swift:455-458: there a NaN depth
+              // (e.g. e = inf - inf for vertices near w = 0, or 0 * inf) passes
+              // every comparison, is stored as best_z, and is then replaced by
+              // whichever candidate comes next, so the result depends on the
+              // bin's atomic append order.  Here a NaN depth is never a
+              // fragment, which keeps the winner order independent.
+              if (std::isnan(z_pix)) continue;
               if (z_pix <= peel_z) continue;
               if (z_pix >= best_z) continue;
               best_z = z_pix; best_t = t; best_u = u; best_v = v;

@@ -24,8 +24,9 @@ Remaps (our = this library, nv = nvdiffrast; all image tensors flipped on H):
   in both libraries; d_color differs by algorithm and is not used.
   texture: convention-free (same uv input), stored unchanged.
 
-Usage (in a checkout that has the reference next to it):
-    python tests/golden/make_golden.py [path/to/diffrast_fixtures.safetensors]
+Usage (the fixture is the reference checkout's
+Tests/MLXDiffRastTests/Fixtures/diffrast_fixtures.safetensors):
+    python tests/golden/make_golden.py path/to/diffrast_fixtures.safetensors
 """
 from __future__ import annotations
 
@@ -35,9 +36,6 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_SRC = os.path.join(
-    os.sep, "root", "reference", "Tests", "MLXDiffRastTests", "Fixtures",
-    "diffrast_fixtures.safetensors")
 
 
 def fixture_inputs():
@@ -118,7 +116,9 @@ def convert(src):
 
 
 def main():
-    src = sys.argv[1] if len(sys.argv) > 1 else DEFAULT_SRC
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py path/to/diffrast_fixtures.safetensors")
+    src = sys.argv[1]
     g = convert(src)
     out = os.path.join(HERE, "nvdiffrast_fixture.npz")
     np.savez_compressed(out, **g)

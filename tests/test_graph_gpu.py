@@ -117,3 +117,40 @@ def test_cuda_graph_captures_a_training_step():
             ga, gb = a.grad.double(), b.double()
             assert float((ga - gb).norm() / gb.norm().clamp_min(1e-30)) < 1e-5
         del g
+
+
+def test_capped_scan_all_batches_with_itemless_candidates():
+    # Every tile scans the whole triangle list (capacity 1).  In tile (0, 0)
+    # the staged batch of 256 candidates holds covering triangles interleaved
+    # with triangles elsewhere (no items in that tile), and its last 56
+    # candidates own no item at all: the walk must skip item-less candidates
+    # in the middle and never step past the batch's last item.
+    import oracle as O
+    import diffrast
+    res = (64, 64)
+    g = np.random.default_rng(5)
+    verts, tris = [], []
+    for i in range(256):
+        in_tile0 = i < 200 and i % 3 != 1
+        cx, cy = ((-0.85, 0.85) if in_tile0 else (0.6, -0.6))
+        cx += g.uniform(-0.1, 0.1); cy += g.uniform(-0.1, 0.1)
+        z = g.uniform(-0.9, 0.9)
+        r = g.uniform(0.05, 0.3)
+        a = g.uniform(0, 2 * np.pi)
+        for k in range(3):
+            verts.append([cx + r * np.cos(a + 2.1 * k), cy + r * np.sin(a + 2.1 * k), z, 1.0])
+        tris.append([3 * i, 3 * i + 1, 3 * i + 2])
+    pos = np.array([verts], np.float32)
+    tri = np.array(tris, np.int32)
+    ref = _layers(pos, tri, res, 2, True)
+    with _capped(1):
+        got = _layers(pos, tri, res, 2, True)
+        over = diffrast.raster_overflow()
+    assert over > 0
+    r_prev = None
+    for l in range(2):
+        assert np.array_equal(got[l][0], ref[l][0]) and np.array_equal(got[l][1], ref[l][1])
+        r_o, d_o = O.rasterize(pos, tri, res, peel=r_prev)
+        assert np.array_equal(got[l][0], r_o) and np.array_equal(got[l][1], d_o)
+        r_prev = r_o
+    assert (got[0][0][0, :16, :16, 3] > 0).mean() > 0.5  # tile (0, 0) is mostly covered

@@ -364,6 +364,38 @@ def test_layers_fused_pass_depth_ties(cu, soup):
     assert ids0.max() <= tri.shape[0]  # ties resolve to the first copy
 
 
+def test_subnormal_area_slivers_bit_exact(cu, soup):
+    # Slivers of area 2^-129 (1/area = inf, NaN depth along the row y = 0)
+    # spliced into the soup before and after full-screen triangles: CUDA and the
+    # oracle agree bit for bit in one layer, in the fused two-layer pass and in
+    # a peeled third layer.
+    import torch
+
+    import diffrast
+    pos, tri = soup
+    V = pos.shape[1]
+    N = pos.shape[0]
+    tiny = np.float32(2.0 ** -130)
+    extra = np.array([[-1, 0, -0.5, 1], [1, 0, -0.5, 1], [1, tiny, -0.5, 1],
+                      [-4, -4, 0.95, 1], [4, -4, 0.95, 1], [0, 4, 0.95, 1],
+                      [-0.5, 0, -0.9, 1], [0.7, 0, -0.9, 1], [0.7, tiny, -0.9, 1]], np.float32)
+    p = np.concatenate([pos, np.broadcast_to(extra, (N,) + extra.shape)], axis=1).copy()
+    e = np.arange(9, dtype=np.int32).reshape(3, 3) + V
+    t = np.concatenate([e[:1], tri[: len(tri) // 2], e[1:2], tri[len(tri) // 2:], e[2:]]).astype(np.int32)
+    res = (161, 144)  # odd height: the centre row is y = 0 exactly
+    r_c, d_c = cu.rasterize(p, t, res)
+    r_o, d_o = O.rasterize(p, t, res)
+    assert np.array_equal(r_c, r_o) and np.array_equal(d_c, d_o)
+    assert np.all(np.isfinite(r_c)) and np.all(np.isfinite(d_c))
+    layers = diffrast.rasterize_layers(torch.from_numpy(p).cuda(), torch.from_numpy(t).cuda(), res, 3)
+    r_prev = None
+    for l in range(3):
+        r_o, d_o = O.rasterize(p, t, res, peel=r_prev)
+        assert np.array_equal(layers[l][0].cpu().numpy(), r_o), l
+        assert np.array_equal(layers[l][1].cpu().numpy(), d_o), l
+        r_prev = r_o
+
+
 def test_layers_full_size_soup_two_views(cu):
     # Both depth layers of two full 1024^2 cfg4 views from the fused pass.
     import torch

@@ -163,3 +163,31 @@ def test_no_triangle_dropped_in_a_dense_tile(backend):
     assert ids.max() == float(n)
     covered = ids > 0
     assert np.all(ids[covered] == n)
+
+
+def _sliver_scene(sliver_first):
+    # A sliver with a finite, non-zero area of 2^-129: 1/area = inf, so at the
+    # pixels of row 2 of a 5-row image (centre y = 0 exactly) its barycentrics
+    # are inf or 0 * inf = NaN and its depth is NaN.  The reference would store
+    # that NaN (every comparison is false) and let its next candidate replace
+    # it; this library and its oracle never take a NaN depth, so the full-screen
+    # triangle at z = 0.5 wins everywhere whatever the order.
+    tiny = np.float32(2.0 ** -130)
+    sliver = [[-1, 0, -0.5, 1], [1, 0, -0.5, 1], [1, tiny, -0.5, 1]]
+    full = [[-4, -4, 0.5, 1], [4, -4, 0.5, 1], [0, 4, 0.5, 1]]
+    verts = sliver + full if sliver_first else full + sliver
+    pos = np.array([verts], np.float32)
+    tri = np.array([[0, 1, 2], [3, 4, 5]], np.int32)
+    return pos, tri, (2.0 if sliver_first else 1.0)
+
+
+def test_subnormal_area_sliver_never_wins(backend):
+    pos, tri, full_id = _sliver_scene(True)
+    rast, db = backend.rasterize(pos[:, :3], tri[:1], (5, 8))
+    assert np.all(rast == 0) and np.all(db == 0)  # alone: no fragment, no NaN
+    for first in (True, False):
+        pos, tri, full_id = _sliver_scene(first)
+        rast, db = backend.rasterize(pos, tri, (5, 8))
+        assert np.all(np.isfinite(rast)) and np.all(np.isfinite(db))
+        assert np.all(rast[..., 3] == full_id), first
+        assert np.all(rast[..., 2] == np.float32(0.5))

@@ -51,6 +51,30 @@ def test_static_topology_hash_matches_allocating_entry_point():
         assert (out >= 0).any() and (out == -1).any() and (out == -2).any()
 
 
+def test_static_topology_hash_large_then_small_mesh():
+    # A mesh near the table's limit fills slots far above a small mesh's range;
+    # the small mesh that follows must not see them (each call clears and
+    # probes only its own range).
+    import torch
+
+    import diffrast
+    from diffrast import _lib
+
+    fn = _lib.lib().dr_antialias_construct_topology_hash_static
+    stream = torch.cuda.current_stream().cuda_stream
+    big = _mesh(33, 50000, 1500)[: MAX_TRIS - 16]
+    small = np.array([[0, 1, 2], [2, 1, 3], [3, 1, 4], [0, 2, 5], [6, 7, 8]], np.int32)
+    for tri_np in (big, small):
+        tri = torch.from_numpy(np.ascontiguousarray(tri_np)).cuda()
+        ref = diffrast.antialias_construct_topology_hash(tri)
+        out = torch.full_like(tri, 7)
+        st = fn(ctypes.c_void_p(tri.data_ptr()), tri.shape[0], ctypes.c_void_p(out.data_ptr()),
+                ctypes.c_void_p(stream))
+        assert st == _lib.DR_OK
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), tri_np.shape
+
+
 def test_static_topology_hash_rejects_meshes_above_its_limit():
     import torch
 
