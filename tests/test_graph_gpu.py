@@ -150,7 +150,7 @@ def test_capped_scan_all_batches_with_itemless_candidates():
     r_prev = None
     for l in range(2):
         assert np.array_equal(got[l][0], ref[l][0]) and np.array_equal(got[l][1], ref[l][1])
-        r_o, d_o = O.rasterize(pos, tri, res, peel=r_prev)
+        r_o, d_o = O.rasterize(pos, tri, res, peel_layer=r_prev)
         assert np.array_equal(got[l][0], r_o) and np.array_equal(got[l][1], d_o)
         r_prev = r_o
     assert (got[0][0][0, :16, :16, 3] > 0).mean() > 0.5  # tile (0, 0) is mostly covered
