@@ -330,17 +330,114 @@ __device__ __forceinline__ void write_pixel(const float4* __restrict__ rec, int6
   }
 }
 
+// Conservative column spans of one candidate, per tile row.
+//
+// The exact pixel test (inclusive edges, Rasterize.swift:442-447) stays the
+// only authority on coverage; a span only drops pixels it provably rejects,
+// so results are bit-identical, and about half of the pixels of a small
+// triangle's rectangle are never tested (cfg4: 36.5 M -> 16.7 M tests per
+// view for 16.65 M covered pixels).
+//
+// Edge i runs from a = vertex i+1 to b = vertex i+2; its exact edge function
+// at a pixel centre p, e(p) = (a_x - p_x)(b_y - p_y) - (b_x - p_x)(a_y - p_y),
+// is affine in p_x with slope g = a_y - b_y, and zero at the root
+// x*(y) = a_x + (b_x - a_x)(y - a_y) / (b_y - a_y).  For pixels inside the
+// candidate's bounding box (|p - vertex| <= Wb, Hb per axis), the float
+// evaluation ê of the test differs from e by at most
+//   D = 8u Wb Hb + 2^-149 (1 + 1/|area|)      (u = 2^-24)
+// (three roundings of the products, one of the difference, subnormal
+// products, and an e * area product that underflows to -0 and passes).  A
+// pixel that passes has sign(area) * ê >= 0, so sign(area) * g (p_x - x*) >=
+// -D: p_x >= x* - D/|g| when sign(area) g > 0 (a lower bound), else p_x <=
+// x* + D/|g| (an upper bound).  The root is evaluated as fma(B, y, A) with
+// B = (b_x - a_x) / (b_y - a_y) and A = a_x - B a_y; its error, that of
+// folding the margin into A, of the pixel centres' own NDC rounding and of
+// the conversion to a column index stay below
+//   u (10|a_x| + 2|B||a_y| + 9|B| Hb + 42) + 4u Wb Hb / |g|.
+// The margin used is twice the sum of both bounds; an edge with g = 0, a
+// non-finite B or A, or a margin of 8 or more constrains nothing.  (Checked on
+// the CPU against the exact test on full cfg4 views and on adversarial
+// slivers, axis-aligned and near-degenerate edges, sub-pixel and huge
+// triangles at several resolutions: no accepted pixel outside its span.)
+//
+// Every triangle has at most two lower-bound and two upper-bound edges (the
+// exact slopes g of its three edges sum to zero and a correctly rounded
+// difference keeps its sign), so each row's span is
+//   [max of the two lower roots, min of the two upper roots],
+// unused slots holding (B, A) = (0, -inf) or (0, +inf).
+// Writes one byte per tile row of [ly0, ly1] with a non-empty span (first
+// column | last column << 4, tile-local), returns the number of pixels and
+// sets n_rows to the number of non-empty rows.
+__device__ __forceinline__ int stage_spans(const float4& f0, const float4& f1, float area, float inv_area,
+                                           int lx0, int lx1, int ly0, int ly1, int tx0, int W,
+                                           const float* __restrict__ s_ndcy, unsigned char* __restrict__ span,
+                                           int& n_rows) {
+  constexpr float kU = 5.9604645e-08f;     // 2^-24
+  constexpr float kTiny = 1.4012985e-45f;  // 2^-149
+  const float sx[3] = {f0.x, f0.w, f1.z}, sy[3] = {f0.y, f1.x, f1.w};
+  const float Wb = FS(fmaxf(sx[0], fmaxf(sx[1], sx[2])), fminf(sx[0], fminf(sx[1], sx[2])));
+  const float Hb = FS(fmaxf(sy[0], fmaxf(sy[1], sy[2])), fminf(sy[0], fminf(sy[1], sy[2])));
+  const float dnum = FA(FM(12.1f * kU, FM(Wb, Hb)), FM(kTiny, FA(1.0f, fabsf(inv_area))));
+  float lb0 = 0.0f, la0 = -INFINITY, lb1 = 0.0f, la1 = -INFINITY;
+  float hb0 = 0.0f, ha0 = INFINITY, hb1 = 0.0f, ha1 = INFINITY;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int ia = (i + 1) % 3, ib = (i + 2) % 3;
+    const float ax = sx[ia], ay = sy[ia], bx = sx[ib], by = sy[ib];
+    const float g = FS(ay, by);
+    const float inv = __frcp_rn(FS(by, ay));
+    const float B = FM(FS(bx, ax), inv);
+    const float A = FS(ax, FM(B, ay));
+    const float aB = fabsf(B);
+    const float m = FM(2.0f, FA(FM(dnum, fabsf(inv)),
+                                FM(kU, FA(FA(FA(FM(10.0f, fabsf(ax)), FM(FM(2.0f, aB), fabsf(ay))),
+                                             FM(FM(9.0f, aB), Hb)), 42.0f))));
+    if (g != 0.0f && isfinite(B) && isfinite(A) && m < 8.0f) {
+      if ((area > 0.0f) == (g > 0.0f)) {  // a lower bound on the column
+        const float a = FS(A, m);
+        if (la0 == -INFINITY) { lb0 = B; la0 = a; } else { lb1 = B; la1 = a; }
+      } else {
+        const float a = FA(A, m);
+        if (ha0 == INFINITY) { hb0 = B; ha0 = a; } else { hb1 = B; ha1 = a; }
+      }
+    }
+  }
+  const float half = (float)W * 0.5f;  // exact: W <= 32768
+  const float off = half - 0.5f;
+  const float clo_min = (float)(lx0 + tx0), chi_max = (float)(lx1 + tx0);
+  int n = 0, rows = 0;
+  for (int ly = ly0; ly <= ly1; ++ly) {
+    const float y = s_ndcy[ly];
+    const float lo = fmaxf(__fmaf_rn(lb0, y, la0), __fmaf_rn(lb1, y, la1));
+    const float hi = fminf(__fmaf_rn(hb0, y, ha0), __fmaf_rn(hb1, y, ha1));
+    const float cl = fmaxf(ceilf(__fmaf_rn(lo, half, off)), clo_min);
+    const float ch = fminf(floorf(__fmaf_rn(hi, half, off)), chi_max);
+    if (cl <= ch) {
+      const int c0 = (int)cl - tx0, c1 = (int)ch - tx0;
+      span[ly] = (unsigned char)(c0 | (c1 << 4));
+      n += c1 - c0 + 1;
+      ++rows;
+    }
+  }
+  n_rows = rows;
+  return n;
+}
+
 // Per-tile fine raster.  The CTA stages up to 256 candidates at a time (one per
-// thread) in shared memory and block-scans their work-item counts (the pixels
-// of each candidate's rectangle inside the tile).  Every thread then takes an
-// equal contiguous range of the batch's items, finds the candidate holding its
-// first item by binary search, and walks (row, col) of that rectangle
-// incrementally, reloading a staged record only when its range crosses into
-// the next candidate.  Work is balanced to within one item per thread, and
-// the per-item cost is the reference's pixel test plus a counter step.
+// thread): each thread loads its candidate's record, computes its per-row
+// column spans inside the tile (stage_spans) and counts its pixels and
+// non-empty rows.  One block scan of both counts gives every non-empty
+// (candidate, row) span its slot in a shared list of spans and the index of
+// its first pixel in the batch's item space, so the list is ordered by item
+// and its start indices increase strictly.  Each warp then takes a contiguous
+// range of items, 32 consecutive items per step, one per lane: a lane finds
+// the span holding its item by counting the span starts among the next 32
+// that do not exceed it (one shared load, an OR-reduction of one bit per
+// start, a population count), so the walk has no per-lane loop.  Work is
+// balanced to within one step per warp whatever the triangle sizes.
 // MODE: 0 = one layer, 1 = one layer peeled at `peel`, 2 = layers 0 and 1 at once.
 constexpr int WARPS = TILE_PIX / 32;
-constexpr int SSTRIDE = 5;  // float4 per staged candidate (80 B)
+constexpr int MAX_SPANS = TILE_PIX * TILE;  // every staged candidate non-empty on every row
 
 // CAPPED: the list buffer holds `cap` entries (fixed capacity, no readback);
 // a tile whose list runs past it stages every triangle of its view instead,
@@ -357,8 +454,10 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   __shared__ unsigned long long s_k0[TILE_PIX], s_k1[TWO ? TILE_PIX : 1];
   __shared__ float s_peel[PEEL ? TILE_PIX : 1];
   __shared__ float s_ndcx[TILE], s_ndcy[TILE];
-  __shared__ float4 s_stage[TILE_PIX * SSTRIDE];
-  __shared__ int s_excl[TILE_PIX + 1];
+  __shared__ float4 s_rec[TILE_PIX * 3];        // staged records, by staging thread
+  __shared__ uint4 s_rowspan[TILE_PIX];         // per staging thread: one span byte per tile row
+  __shared__ int s_start[MAX_SPANS + 33];       // first item of each span (+ 33 entries past the last)
+  __shared__ unsigned short s_info[MAX_SPANS];  // staging thread | row << 8 | first column << 12
   __shared__ int s_wsum[WARPS];
 
   const int ntiles = ntx * nty;
@@ -430,7 +529,8 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   for (uint32_t base = 0; base < cnt; base += TILE_PIX) {
     __syncthreads();  // the previous batch's readers are done with the stage
     const uint32_t i = base + tid;
-    int n_items = 0;
+    int n_items = 0, n_rows = 0, ly0 = 0, ly1 = -1;
+    unsigned char* span = reinterpret_cast<unsigned char*>(&s_rowspan[tid]);
     if (i < cnt) {
       const int t = scan_all ? (int)i : __ldg(list + begin + i);
       const float4 a = __ldg(rec + 3 * (rec_view + t) + 0);
@@ -439,18 +539,24 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
       const unsigned xs = __float_as_uint(c.z), ys = __float_as_uint(c.w);
       const int cx0 = max((int)(xs & 0xffffu), tx0), cx1 = min((int)(xs >> 16), tx0 + TILE - 1);
       const int cy0 = max((int)(ys & 0xffffu), ty0), cy1 = min((int)(ys >> 16), ty0 + TILE - 1);
-      // A listed candidate's rectangle always meets its tile (it was binned by it).
-      const int wc = max(cx1 - cx0 + 1, 1), hc = max(cy1 - cy0 + 1, 1);
-      n_items = wc * hc;
-      if (CAPPED && scan_all && (c.y == 0.0f || cx0 > cx1 || cy0 > cy1)) n_items = 0;
-      const int pk = (cx0 - tx0) | ((cy0 - ty0) << 4) | (wc << 8) | (hc << 16);
-      s_stage[tid * SSTRIDE + 0] = a;
-      s_stage[tid * SSTRIDE + 1] = bb;
-      s_stage[tid * SSTRIDE + 2] = make_float4(c.x, c.y, FD(1.0f, c.y), __int_as_float(t));
-      s_stage[tid * SSTRIDE + 3] = make_float4(__int_as_float(pk), 0.f, 0.f, 0.f);
+      // The correctly rounded reciprocal: identical to the reference's 1.0f / area.
+      const float inv_area = __frcp_rn(c.y);
+      s_rowspan[tid] = make_uint4(0x0F0F0F0Fu, 0x0F0F0F0Fu, 0x0F0F0F0Fu, 0x0F0F0F0Fu);  // every row empty
+      // A listed candidate's rectangle always meets its tile (it was binned by
+      // it); a scanned one may not, and an invalid record (area 0) has none.
+      if (c.y != 0.0f && cx0 <= cx1 && cy0 <= cy1) {
+        ly0 = cy0 - ty0;
+        ly1 = cy1 - ty0;
+        n_items = stage_spans(a, bb, c.y, inv_area, cx0 - tx0, cx1 - tx0, ly0, ly1, tx0, W, s_ndcy, span, n_rows);
+      }
+      s_rec[3 * tid + 0] = a;
+      s_rec[3 * tid + 1] = bb;
+      s_rec[3 * tid + 2] = make_float4(c.x, c.y, inv_area, __int_as_float(t));
     }
-    // Block exclusive scan of the item counts.
-    int incl = n_items;
+    // Block exclusive scan of (pixels, non-empty rows), packed: a batch holds
+    // at most 256 * 256 pixels (17 bits) and 256 * 16 rows (13 bits).
+    const int mine = n_items | (n_rows << 17);
+    int incl = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -458,57 +564,60 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
     }
     if (lane == 31) s_wsum[warp] = incl;
     __syncthreads();
-    int before = 0;
+    int before = 0, all = 0;
 #pragma unroll
-    for (int w = 0; w < WARPS; ++w)
-      if (w < warp) before += s_wsum[w];
-    s_excl[tid] = before + incl - n_items;
-    if (tid == TILE_PIX - 1) s_excl[TILE_PIX] = before + incl;
-    __syncthreads();
-    const int total = s_excl[TILE_PIX];
-    const int nc = (int)min(cnt - base, (uint32_t)TILE_PIX);
-    const int lo = (int)(((long long)tid * total) / TILE_PIX);
-    const int nmine = (int)(((long long)(tid + 1) * total) / TILE_PIX) - lo;
-    float4 f0 = make_float4(0.f, 0.f, 0.f, 0.f), f1 = f0, f2 = f0;
-    int j = 0, pk = 0, wc = 1, hc = 1, row = 0, col = 0;
-    if (nmine > 0) {
-      // The candidate holding item lo: the last j with s_excl[j] <= lo.  A
-      // listed candidate owns >= 1 item, so s_excl is strictly increasing over
-      // [0, nc); in the CAPPED scan-all mode candidates may own none and s_excl
-      // is only non-decreasing, but the last j with s_excl[j] <= lo < total is
-      // still the one whose range [s_excl[j], s_excl[j+1]) holds item lo, so it
-      // owns items.
-      int jh = nc - 1;
-      while (j < jh) {
-        const int mid = (j + jh + 1) >> 1;
-        if (s_excl[mid] <= lo) j = mid; else jh = mid - 1;
-      }
-      f0 = s_stage[j * SSTRIDE + 0]; f1 = s_stage[j * SSTRIDE + 1]; f2 = s_stage[j * SSTRIDE + 2];
-      pk = __float_as_int(s_stage[j * SSTRIDE + 3].x);
-      wc = (pk >> 8) & 31; hc = (pk >> 16) & 31;
-      const int k = lo - s_excl[j];
-      row = k / wc;
-      col = k - row * wc;
+    for (int w = 0; w < WARPS; ++w) {
+      const int ws = s_wsum[w];
+      if (w < warp) before += ws;
+      all += ws;
     }
-    for (int r = 0; r < nmine; ++r) {
-      unsigned long long key = 0;
-      int p = 0;
-      if (test(f0, f1, f2, (pk & 15) + col, ((pk >> 4) & 15) + row, key, p)) fold(key, p);
-      if (++col == wc) {
-        col = 0;
-        if (++row == hc && r + 1 < nmine) {
-          row = 0;
-          ++j;
-          // Scanned tiles stage candidates without items: skip them (an item
-          // of this thread's range lies ahead, so the loop ends).
-          if (CAPPED)
-            while (s_excl[j + 1] == s_excl[j]) ++j;
-          f0 = s_stage[j * SSTRIDE + 0];
-          f1 = s_stage[j * SSTRIDE + 1];
-          f2 = s_stage[j * SSTRIDE + 2];
-          pk = __float_as_int(s_stage[j * SSTRIDE + 3].x);
-          wc = (pk >> 8) & 31;
-          hc = (pk >> 16) & 31;
+    const int n_total = all & 0x1FFFF, n_spans = all >> 17;
+    if (n_rows > 0) {
+      // This candidate's non-empty rows, in item order, into the span list
+      // (stage_spans wrote only the rows in [ly0, ly1] with a span).
+      const int excl = before + incl - mine;
+      int item = excl & 0x1FFFF, slot = excl >> 17;
+      for (int ly = ly0; ly <= ly1; ++ly) {
+        const unsigned sp = span[ly];
+        const int c0 = (int)(sp & 15u), c1 = (int)(sp >> 4);
+        if (c1 >= c0) {
+          s_start[slot] = item;
+          s_info[slot] = (unsigned short)(tid | (ly << 8) | (c0 << 12));
+          ++slot;
+          item += c1 - c0 + 1;
+        }
+      }
+    }
+    if (tid < 33) s_start[n_spans + tid] = INT_MAX;  // no start past the last span
+    __syncthreads();
+    // Warp w tests items [wlo, whi), 32 consecutive items per step.
+    const int wlo = (int)(((long long)warp * n_total) / WARPS);
+    const int whi = (int)(((long long)(warp + 1) * n_total) / WARPS);
+    if (wlo < whi) {
+      // The span holding item wlo: the last s with s_start[s] <= wlo (starts
+      // increase strictly, every span owning at least one item).
+      int s0 = 0, sh = n_spans - 1;
+      while (s0 < sh) {
+        const int mid = (s0 + sh + 1) >> 1;
+        if (s_start[mid] <= wlo) s0 = mid; else sh = mid - 1;
+      }
+      for (int b0 = wlo; b0 < whi; b0 += 32) {
+        // s0 holds item b0, so the starts after it are >= b0 and at most 32
+        // of them (one per later item of the step) can fall inside the step:
+        // the span of item b0 + lane is s0 plus the number of starts among
+        // s_start[s0 + 1 .. s0 + 32] that are <= b0 + lane.
+        const int d = s_start[s0 + 1 + lane] - b0;
+        const unsigned M = __reduce_or_sync(0xffffffffu, d < 32 ? (1u << d) : 0u);
+        const int s = s0 + __popc(M & (0xffffffffu >> (31 - lane)));
+        s0 = __shfl_sync(0xffffffffu, s, 31);
+        const int item = b0 + lane;
+        if (item < whi) {
+          const unsigned info = s_info[s];
+          const int j = (int)(info & 255u), ly = (int)((info >> 8) & 15u);
+          const int lx = (int)(info >> 12) + (item - s_start[s]);
+          unsigned long long key = 0;
+          int p = 0;
+          if (test(s_rec[3 * j], s_rec[3 * j + 1], s_rec[3 * j + 2], lx, ly, key, p)) fold(key, p);
         }
       }
     }
