@@ -152,6 +152,15 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
     def add(name, b):
         k[name] = k.get(name, 0) + b
 
+    def add_aa(C, V, T, nv):
+        """Antialias fused with its MSE: the forward reads colour, rast and the
+        target and writes out plus the 17 B/px silhouette record; the VJP reads
+        the record, out and the target (the loss's cotangent is formed from
+        them) and writes d_color.  nv: vertex batches read (1 with per-view
+        transforms of one shared buffer)."""
+        add("aa_fwd", P * (12 * C + 16 + 17) + nv * V * 16 + 2 * T * 12)
+        add("aa_bwd", P * (12 * C + 17) + 2 * nv * V * 16 + 2 * T * 12)
+
     if cfg == "cfg4":
         V, T, A = chain.base.shape[0], chain.tri.shape[0], 8
         # Vertices are the shared [V, 4] soup (Nv = 1) transformed per view in-kernel.
@@ -159,15 +168,14 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         # One tile pass writes both layers (rast + rast_db each); layer 0 is never re-read.
         add("raster_tiles", 2 * (P * 16 + P * 16))
         for layer in (0, 1):
-            add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A))
+            # Layer 1's interpolation also reads its MSE target (the fused loss).
+            add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A) + (P * 4 * A if layer else 0))
             # out_da never reaches the loss: the VJP runs without the DA terms.
-            add("interp_bwd", 2 * V * A * 4 + T * 12 + P * (16 + 16 + 4 * A))
+            # Layer 0 reads d_out; layer 1 forms it from its output and target.
+            add("interp_bwd", 2 * V * A * 4 + T * 12 + P * (16 + 16 + 4 * A) + (P * 4 * A if layer else 0))
             # rast_db's cotangent is zero (out_da is off the loss path): not read.
             add("raster_bwd", 2 * V * 16 + T * 12 + P * 32)
-        add("aa_fwd", P * (8 * A + 16) + V * 16 + 2 * T * 12)
-        add("aa_bwd", P * (12 * A + 16) + 2 * V * 16 + 2 * T * 12)
-        add("mse", 2 * P * 8 * A)  # loss: read pred and target
-        add("mse_bwd", 2 * P * 12 * A)  # read pred and target, write d_pred
+        add_aa(A, V, T, 1)
     elif cfg == "cfg1":
         V, T, C = 3, 1, 3
         add("raster_setup", V * 16 + T * 12)
@@ -175,10 +183,7 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         add("interp_fwd", V * C * 4 + T * 12 + P * (16 + 4 * C))
         add("interp_bwd", 2 * V * C * 4 + T * 12 + P * (32 + 4 * C))
         add("raster_bwd", 2 * V * 16 + T * 12 + P * 32)
-        add("aa_fwd", P * (8 * C + 16) + V * 16 + 2 * T * 12)
-        add("aa_bwd", P * (12 * C + 16) + 2 * V * 16 + 2 * T * 12)
-        add("mse", P * 8 * C)  # loss: read pred and target
-        add("mse_bwd", P * 12 * C)  # read pred and target, write d_pred
+        add_aa(C, V, T, 1)
     elif cfg == "cfg2":
         V, T = chain.pos.shape[1], chain.tri.shape[0]
         S = 512 * 512 * 3 * 4
@@ -189,10 +194,7 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         add("tex_linear_fwd", S + P * (8 + 12))
         add("tex_linear_bwd", 2 * S + P * (16 + 12))
         add("raster_bwd", 2 * n * V * 16 + T * 12 + P * 32)
-        add("aa_fwd", P * (8 * 3 + 16) + n * V * 16 + 2 * T * 12)
-        add("aa_bwd", P * (12 * 3 + 16) + 2 * n * V * 16 + 2 * T * 12)
-        add("mse", P * 8 * 3)  # loss: read pred and target
-        add("mse_bwd", P * 12 * 3)  # read pred and target, write d_pred
+        add_aa(3, V, T, n)
     elif cfg == "cfg3":
         V, T = chain.pos.shape[1], chain.tri.shape[0]
         S0 = 2048 * 2048 * 4 * 4
@@ -230,10 +232,7 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
             add("tex_cube_mip_bwd", micro * 2 * S_all + P * (12 + 24 + 12 + 12 + 24))
             add("mip_fold", micro * (S_all + S))
             add("raster_bwd", 2 * n * V * 16 + micro * T * 12 + P * (32 + 16))
-        add("aa_fwd", P * (8 * 3 + 16) + n * V * 16 + micro * 2 * T * 12)
-        add("aa_bwd", P * (12 * 3 + 16) + 2 * n * V * 16 + micro * 2 * T * 12)
-        add("mse", P * 8 * 3)  # loss: read pred and target
-        add("mse_bwd", P * 12 * 3)  # read pred and target, write d_pred
+        add_aa(3, V, micro * T, micro)  # per-view transforms of the shared vertices
     return k
 
 

@@ -220,6 +220,32 @@ DR_API dr_status dr_interpolate_bwd(dr_ctx* ctx, const float* attr, int attr_bat
                              int K, const float* d_out, const float* d_out_da,
                              float* d_attr, float* d_rast, float* d_rast_db);
 
+/* Interpolate followed by a mean-squared-error loss of `out` against `target`
+ * ([N, H, W, A]) in the same pass: the loss the reference's examples compute
+ * after the op (`mean((out - target)^2)`, ColorFitExample/main.swift:57-60,
+ * PoseFitExample/main.swift:89-92), fused here; no counterpart in the
+ * reference's operator surface.  The forward writes out / out_da as
+ * dr_interpolate_fwd and writes scale * sum((out - target)^2) to the device
+ * scalar *loss (scale = 1 / numel for a mean).  The
+ * VJP takes out (the forward's output), target, scale and d_loss (a device
+ * scalar, the loss's cotangent) in place of d_out and forms out's cotangent
+ * 2 * scale * (out - target) * (*d_loss) where it reads it; d_out_da is
+ * out_da's cotangent as in dr_interpolate_bwd. */
+DR_API dr_status dr_interpolate_fwd_mse(dr_ctx* ctx, const float* attr, int attr_batch,
+                                 int V, int A, const float* rast, int N, int H,
+                                 int W, const int32_t* tri, int T,
+                                 const float* rast_db, const int32_t* diff_idx,
+                                 int K, float* out, float* out_da,
+                                 const float* target, float scale, float* loss);
+DR_API dr_status dr_interpolate_bwd_mse(dr_ctx* ctx, const float* attr, int attr_batch,
+                                 int V, int A, const float* rast, int N, int H,
+                                 int W, const int32_t* tri, int T,
+                                 const float* rast_db, const int32_t* diff_idx,
+                                 int K, const float* out, const float* target,
+                                 float scale, const float* d_loss,
+                                 const float* d_out_da, float* d_attr,
+                                 float* d_rast, float* d_rast_db);
+
 /* ---- texture (Texture.swift:62-1313) ----------------------------------- */
 
 /* Host-only: the mip pyramid layout textureConstructMip (Texture.swift:144-161)
@@ -344,6 +370,37 @@ DR_API dr_status dr_antialias_xf_bwd(dr_ctx* ctx, const float* color, int N, int
                               int V, const float* xform, const int32_t* tri, int T,
                               const int32_t* topo, const float* d_out,
                               float* d_color, float* d_verts, const void* aa_work);
+
+/* Antialias followed by a mean-squared-error loss of `out` against `target`
+ * ([N, H, W, C]) in the same passes, as dr_interpolate_fwd_mse: the forward
+ * also writes scale * sum((out - target)^2) to the device scalar *loss; the
+ * VJP takes out, target, scale and d_loss in place of
+ * d_out.  No counterpart in the reference's operator surface (its examples
+ * compute the loss after the op, ColorFitExample/main.swift:57-60). */
+DR_API dr_status dr_antialias_fwd_mse(dr_ctx* ctx, const float* color, int N, int H,
+                               int W, int C, const float* rast, const float* pos,
+                               int V, const int32_t* tri, int T,
+                               const int32_t* topo, float* out, void* aa_work,
+                               const float* target, float scale, float* loss);
+DR_API dr_status dr_antialias_bwd_mse(dr_ctx* ctx, const float* color, int N, int H,
+                               int W, int C, const float* rast, const float* pos,
+                               int V, const int32_t* tri, int T,
+                               const int32_t* topo, const float* out,
+                               const float* target, float scale,
+                               const float* d_loss, float* d_color, float* d_pos,
+                               const void* aa_work);
+DR_API dr_status dr_antialias_xf_fwd_mse(dr_ctx* ctx, const float* color, int N, int H,
+                                  int W, int C, const float* rast, const float* verts,
+                                  int V, const float* xform, const int32_t* tri, int T,
+                                  const int32_t* topo, float* out, void* aa_work,
+                                  const float* target, float scale, float* loss);
+DR_API dr_status dr_antialias_xf_bwd_mse(dr_ctx* ctx, const float* color, int N, int H,
+                                  int W, int C, const float* rast, const float* verts,
+                                  int V, const float* xform, const int32_t* tri, int T,
+                                  const int32_t* topo, const float* out,
+                                  const float* target, float scale,
+                                  const float* d_loss, float* d_color, float* d_verts,
+                                  const void* aa_work);
 
 /* ---- loss helper (the MSE of the reference's examples) ------------------ */
 

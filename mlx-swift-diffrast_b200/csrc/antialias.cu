@@ -327,7 +327,8 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
                                                      const float4* __restrict__ rast, int T,
                                                      const int32_t* __restrict__ topo, float* __restrict__ out,
                                                      float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
-                                                     const PixList L, unsigned* err) {
+                                                     const PixList L, const float* __restrict__ tgt, float lscale,
+                                                     float* __restrict__ part, unsigned* err) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = pix < (int64_t)N * H * W;
   const float* cp = color + pix * C;
@@ -343,21 +344,34 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
     cand = sil_candidates(rast, topo, H, W, T, pn, ph, pw, rast_tri(rast, pix, T, err), err);
   }
   list_append(L, cand != 0u, ((unsigned long long)pix << 4) | cand);
-  if (!valid || cand) return;
-  if (WORK) {
-    work_beta[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
-    work_code[pix] = 0;
+  // Pixels without a candidate keep their colour (and add their share of a
+  // fused loss: out == colour).
+  float l = 0.0f;
+  if (valid && !cand) {
+    if (WORK) {
+      work_beta[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
+      work_code[pix] = 0;
+    }
+    const float* tp = tgt ? tgt + pix * C : nullptr;
+    if (vec8) {
+      *reinterpret_cast<float4*>(o) = c0;
+      *reinterpret_cast<float4*>(o + 4) = c1;
+      if (tp) l = sq_diff4(c0, ldg4(tp)) + sq_diff4(c1, ldg4(tp + 4));
+    } else if ((C & 3) == 0 && ((((uintptr_t)color) | ((uintptr_t)out) | ((uintptr_t)tgt)) & 15) == 0) {
+      for (int c = 0; c < C; c += 4) {
+        const float4 x = ldg4(cp + c);
+        *reinterpret_cast<float4*>(o + c) = x;
+        if (tp) l += sq_diff4(x, ldg4(tp + c));
+      }
+    } else {
+      for (int c = 0; c < C; ++c) {
+        const float x = __ldg(cp + c);
+        o[c] = x;
+        if (tp) { const float r = x - __ldg(tp + c); l += r * r; }
+      }
+    }
   }
-  if (vec8) {
-    *reinterpret_cast<float4*>(o) = c0;
-    *reinterpret_cast<float4*>(o + 4) = c1;
-    return;
-  }
-  if ((C & 3) == 0 && ((((uintptr_t)color) | ((uintptr_t)out)) & 15) == 0) {
-    for (int c = 0; c < C; c += 4) *reinterpret_cast<float4*>(o + c) = ldg4(cp + c);
-  } else {
-    for (int c = 0; c < C; ++c) o[c] = __ldg(cp + c);
-  }
+  if (part) block_loss_add(l, lscale, part);
 }
 
 template <bool XF, bool WORK>
@@ -367,9 +381,11 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
                                                       const int32_t* __restrict__ tri, int T,
                                                       const int32_t* __restrict__ topo, float* __restrict__ out,
                                                       float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
-                                                      const PixList L, unsigned* err) {
+                                                      const PixList L, const float* __restrict__ tgt, float lscale,
+                                                      float* __restrict__ part, unsigned* err) {
   // Grid (x, shard): the blocks of row y walk shard y.
   const unsigned long long n = L.count[blockIdx.y];
+  float l = 0.0f;
   const unsigned long long* sl = L.list + (int64_t)blockIdx.y * L.cap;
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -396,8 +412,13 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
     }
     const float* cp = color + pix * C;
     float* o = out + pix * C;
+    const float* tp = tgt ? tgt + pix * C : nullptr;
     if (code == 0u) {
-      for (int c = 0; c < C; ++c) o[c] = __ldg(cp + c);
+      for (int c = 0; c < C; ++c) {
+        const float x = __ldg(cp + c);
+        o[c] = x;
+        if (tp) { const float r = x - __ldg(tp + c); l += r * r; }
+      }
       continue;
     }
     int64_t nb[4];
@@ -410,8 +431,10 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
       for (int d = 0; d < 4; ++d)
         if (nb[d] >= 0) acc += beta[d] * (__ldg(color + nb[d] * C + c) - p);
       o[c] = acc;
+      if (tp) { const float r = acc - __ldg(tp + c); l += r * r; }
     }
   }
+  if (part) block_loss_add(l, lscale, part);
 }
 
 template <bool VEC, bool XF>
@@ -432,7 +455,7 @@ __device__ __forceinline__ void add_pos(float* p, const Mat4& M, float x, float 
 // beta in (0, 1) or for d_alpha == 0.
 template <bool VEC, bool XF>
 __device__ __forceinline__ void aa_dir_dpos(const SilDir& s, const float* __restrict__ color, int C,
-                                            const float* __restrict__ g, int64_t pix, int64_t nb,
+                                            const Cot& cot, float gl, int64_t pix, int64_t nb,
                                             const float* __restrict__ pos, const Mat4& M, int V, int pn, int ph,
                                             int pw, int H, int W, float* __restrict__ d_pos) {
   if (s.beta <= 0.0f || s.beta >= 1.0f) return;
@@ -440,7 +463,7 @@ __device__ __forceinline__ void aa_dir_dpos(const SilDir& s, const float* __rest
   float d_alpha = 0.0f;
   for (int c = 0; c < C; ++c) {
     const float cp = __ldg(color + pix * C + c), cn = __ldg(color + nb * C + c);
-    d_alpha += __ldg(g + c) * (cn - cp);
+    d_alpha += cot_at(cot, gl, pix * C + c) * (cn - cp);
   }
   if (d_alpha == 0.0f) return;
   float dade0x, dade0y, dade1x, dade1y;
@@ -481,17 +504,17 @@ __device__ __forceinline__ void aa_dir_dpos(const SilDir& s, const float* __rest
 
 // d_color in gather form: g (1 - sum of own betas) plus beta * g of every
 // neighbour whose silhouette points at this pixel.
-__device__ __forceinline__ void aa_dcolor(const float* __restrict__ d_out, float* __restrict__ d_color, int C,
+__device__ __forceinline__ void aa_dcolor(const Cot& cot, float gl, float* __restrict__ d_color, int C,
                                           int64_t pix, float keep, const float nbeta[4], const int64_t nsrc[4]) {
-  const float* g = d_out + pix * C;
-  if ((C & 3) == 0 && ((((uintptr_t)d_out) | ((uintptr_t)d_color)) & 15) == 0) {
+  if ((C & 3) == 0 &&
+      ((((uintptr_t)cot.d) | ((uintptr_t)cot.pred) | ((uintptr_t)cot.target) | ((uintptr_t)d_color)) & 15) == 0) {
     for (int c = 0; c < C; c += 4) {
-      const float4 gs = ldg4(g + c);
+      const float4 gs = cot_at4(cot, gl, pix * C + c);
       float4 v = make_float4(gs.x * keep, gs.y * keep, gs.z * keep, gs.w * keep);
 #pragma unroll
       for (int d = 0; d < 4; ++d)
         if (nsrc[d] >= 0) {
-          const float4 gn = ldg4(d_out + nsrc[d] * C + c);
+          const float4 gn = cot_at4(cot, gl, nsrc[d] * C + c);
           const float b = nbeta[d];
           v.x += gn.x * b; v.y += gn.y * b; v.z += gn.z * b; v.w += gn.w * b;
         }
@@ -500,10 +523,10 @@ __device__ __forceinline__ void aa_dcolor(const float* __restrict__ d_out, float
     return;
   }
   for (int c = 0; c < C; ++c) {
-    float v = __ldg(g + c) * keep;
+    float v = cot_at(cot, gl, pix * C + c) * keep;
 #pragma unroll
     for (int d = 0; d < 4; ++d)
-      if (nsrc[d] >= 0) v += __ldg(d_out + nsrc[d] * C + c) * nbeta[d];
+      if (nsrc[d] >= 0) v += cot_at(cot, gl, nsrc[d] * C + c) * nbeta[d];
     d_color[pix * C + c] = v;
   }
 }
@@ -514,7 +537,7 @@ __device__ __forceinline__ void aa_dcolor(const float* __restrict__ d_out, float
 // k_aa_bwd_edges replays those edges (a grid-stride pass, full occupancy)
 // for the d_pos atomics.
 __global__ void __launch_bounds__(256) k_aa_bwd_gather(int N, int H, int W, int C,
-                                                       const float* __restrict__ d_out, float* __restrict__ d_color,
+                                                       const Cot cot, float* __restrict__ d_color,
                                                        const float4* __restrict__ work_beta,
                                                        const uint8_t* __restrict__ work_code, const PixList L) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -539,7 +562,7 @@ __global__ void __launch_bounds__(256) k_aa_bwd_gather(int N, int H, int W, int 
       const float b = __ldg(reinterpret_cast<const float*>(work_beta + p) + d);
       if (b > 0.0f) { nbeta[d] = b; nsrc[d] = p; }
     }
-    aa_dcolor(d_out, d_color, C, pix, keep, nbeta, nsrc);
+    aa_dcolor(cot, cot_g(cot), d_color, C, pix, keep, nbeta, nsrc);
   }
   list_append(L, code != 0u, ((unsigned long long)pix << 8) | code);
 }
@@ -548,8 +571,9 @@ template <bool VEC, bool XF>
 __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_edges(
     const float* __restrict__ color, int N, int H, int W, int C, const float4* __restrict__ rast,
     const float* __restrict__ pos, const float* __restrict__ xform, int V, const int32_t* __restrict__ tri, int T,
-    const float* __restrict__ d_out, float* __restrict__ d_pos, const PixList L, unsigned* err) {
+    const Cot cot, float* __restrict__ d_pos, const PixList L, unsigned* err) {
   // Grid (x, shard): the blocks of row y walk shard y.
+  const float gl = cot_g(cot);
   const unsigned long long n = L.count[blockIdx.y];
   const unsigned long long* sl = L.list + (int64_t)blockIdx.y * L.cap;
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
@@ -567,8 +591,8 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_edges(
       if (kk < 0) continue;
       const SilDir sd = sil_replay<XF>(rast, pos, M, tri, H, W, V, T, pn, ph, pw, tri_p, d, kk, err);
       if (!sd.active) continue;
-      aa_dir_dpos<VEC, XF>(sd, color, C, d_out + pix * C, pix, nbr_pix(pn, ph, pw, d, H, W), pos, M, V, pn, ph, pw,
-                           H, W, d_pos);
+      aa_dir_dpos<VEC, XF>(sd, color, C, cot, gl, pix, nbr_pix(pn, ph, pw, d, H, W), pos, M, V, pn, ph, pw, H, W,
+                           d_pos);
     }
   }
 }
@@ -581,10 +605,11 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd(const float* __r
                          const float4* __restrict__ rast, const float* __restrict__ pos,
                          const float* __restrict__ xform, int V,
                          const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ topo,
-                         const float* __restrict__ d_out, float* __restrict__ d_color, float* __restrict__ d_pos,
+                         const Cot cot, float* __restrict__ d_color, float* __restrict__ d_pos,
                          unsigned* err) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (pix >= (int64_t)N * H * W) return;
+  const float gl = cot_g(cot);
   const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
   const int tri_p = rast_tri(rast, pix, T, err);
   Mat4 M;
@@ -595,8 +620,8 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd(const float* __r
     const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, dir, err);
     if (!s.active) continue;
     alpha_sum += s.beta;
-    aa_dir_dpos<VEC, XF>(s, color, C, d_out + pix * C, pix, nbr_pix(pn, ph, pw, dir, H, W), pos, M, V, pn, ph, pw,
-                         H, W, d_pos);
+    aa_dir_dpos<VEC, XF>(s, color, C, cot, gl, pix, nbr_pix(pn, ph, pw, dir, H, W), pos, M, V, pn, ph, pw, H, W,
+                         d_pos);
   }
   float nbeta[4];
   int64_t nsrc[4];
@@ -613,7 +638,7 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd(const float* __r
     const SilDir s = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, sh, sw, tri_s, d, err);
     if (s.active) { nbeta[d] = s.beta; nsrc[d] = p; }
   }
-  aa_dcolor(d_out, d_color, C, pix, 1.0f - alpha_sum, nbeta, nsrc);
+  aa_dcolor(cot, gl, d_color, C, pix, 1.0f - alpha_sum, nbeta, nsrc);
 }
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
@@ -683,9 +708,12 @@ inline dim3 list_grid(dr_ctx* ctx, int64_t P) {
   return dim3((unsigned)std::max<int64_t>(1, (total + kListShards - 1) / kListShards), kListShards);
 }
 
+// With a target, also writes lscale * sum((out - target)^2) to the device
+// scalar *loss (the fused MSE of the *_mse entry points).
 dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
                  const float* pos, const float* xform, int V, const int32_t* tri, int T, const int32_t* topo,
-                 float* out, void* work) {
+                 float* out, void* work, const float* target = nullptr, float lscale = 0.0f,
+                 float* loss = nullptr) {
   dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
   if (st != DR_OK) return st;
   DR_REQUIRE(ctx, out, "antialias: out required");
@@ -696,18 +724,24 @@ dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, co
   uint8_t* wc = work ? reinterpret_cast<uint8_t*>(work) + (size_t)P * 16 : nullptr;
   PixList L;
   if ((st = aa_list(ctx, P, &L)) != DR_OK) return st;
+  float* part = nullptr;
+  if (target) {
+    DR_REQUIRE(ctx, loss, "antialias_mse: loss required");
+    if ((st = loss_begin(ctx, &part)) != DR_OK) return st;
+  }
   DR_TB(ctx);
   if (work)
     k_aa_fwd_scan<true><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, T, topo, out, wb, wc, L,
-                                                                    ctx->d_err);
+                                                                    target, lscale, part, ctx->d_err);
   else
     k_aa_fwd_scan<false><<<grid_for(P, 256), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, T, topo, out, wb, wc, L,
-                                                                     ctx->d_err);
+                                                                     target, lscale, part, ctx->d_err);
   DR_LAUNCHED(ctx, "aa_fwd");
   DR_TB(ctx);
 #define DR_AF(XFV, WV, XP)                                                                                       \
   k_aa_fwd_edges<XFV, WV><<<list_grid(ctx, P), 256, 0, ctx->stream>>>(color, N, H, W, C, r4, pos, XP, V, tri, T,  \
-                                                                      topo, out, wb, wc, L, ctx->d_err)
+                                                                      topo, out, wb, wc, L, target, lscale, part, \
+                                                                      ctx->d_err)
   if (xform) {
     if (work) DR_AF(true, true, xform); else DR_AF(true, false, xform);
   } else {
@@ -715,15 +749,17 @@ dr_status aa_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, co
   }
 #undef DR_AF
   DR_LAUNCHED(ctx, "aa_fwd_edges");
+  if (part) return loss_end(ctx, part, loss);
   return DR_OK;
 }
 
 dr_status aa_bwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C, const float* rast,
                  const float* pos, const float* xform, int V, const int32_t* tri, int T, const int32_t* topo,
-                 const float* d_out, float* d_color, float* d_pos, const void* work) {
+                 const Cot& d_out, float* d_color, float* d_pos, const void* work) {
   dr_status st = check_aa(ctx, color, N, H, W, C, rast, pos, V, tri, T, topo);
   if (st != DR_OK) return st;
-  DR_REQUIRE(ctx, d_out && d_color && d_pos, "antialias_bwd: d_out, d_color, d_pos required");
+  DR_REQUIRE(ctx, (d_out.d || (d_out.pred && d_out.target && d_out.d_loss)) && d_color && d_pos,
+             "antialias_bwd: d_out (or out, target and d_loss), d_color, d_pos required");
   DR_REQUIRE(ctx, !work || aligned16(work), "antialias_bwd: aa_work must be 16-byte aligned");
   const size_t npos = (size_t)(xform ? 1 : N) * V * 4;
   DR_CUDA(ctx, cudaMemsetAsync(d_pos, 0, sizeof(float) * npos, ctx->stream), "antialias_bwd memset");
@@ -781,7 +817,8 @@ extern "C" dr_status dr_antialias_bwd(dr_ctx* ctx, const float* color, int N, in
                                       const int32_t* topo, const float* d_out, float* d_color, float* d_pos,
                                       const void* aa_work) {
   DR_ENTER(ctx);
-  return aa_bwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, d_out, d_color, d_pos, aa_work);
+  return aa_bwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, Cot{d_out, nullptr, nullptr, 0.0f, nullptr},
+                d_color, d_pos, aa_work);
 }
 
 extern "C" dr_status dr_antialias_xf_fwd(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
@@ -799,7 +836,53 @@ extern "C" dr_status dr_antialias_xf_bwd(dr_ctx* ctx, const float* color, int N,
                                          float* d_color, float* d_verts, const void* aa_work) {
   DR_ENTER(ctx);
   DR_REQUIRE(ctx, xform && aligned16(xform), "antialias_xf_bwd: xform [N,4,4] must be given and 16-byte aligned");
-  return aa_bwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, d_out, d_color, d_verts, aa_work);
+  return aa_bwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo,
+                Cot{d_out, nullptr, nullptr, 0.0f, nullptr}, d_color, d_verts, aa_work);
+}
+
+// Antialias with a fused mean-squared-error loss against `target` (same shape
+// as out): the forward also writes scale * sum((out - target)^2) to the device
+// scalar *loss, and the VJP forms its cotangent 2 * scale * (out - target) *
+// (*d_loss) where it reads it, so no separate loss pass or d_out tensor runs.
+extern "C" dr_status dr_antialias_fwd_mse(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                          const float* rast, const float* pos, int V, const int32_t* tri, int T,
+                                          const int32_t* topo, float* out, void* aa_work, const float* target,
+                                          float scale, float* loss) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, target && loss, "antialias_mse: target and loss required");
+  return aa_fwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo, out, aa_work, target, scale, loss);
+}
+
+extern "C" dr_status dr_antialias_bwd_mse(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                          const float* rast, const float* pos, int V, const int32_t* tri, int T,
+                                          const int32_t* topo, const float* out, const float* target, float scale,
+                                          const float* d_loss, float* d_color, float* d_pos, const void* aa_work) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, out && target && d_loss, "antialias_bwd_mse: out, target and d_loss required");
+  return aa_bwd(ctx, color, N, H, W, C, rast, pos, nullptr, V, tri, T, topo,
+                Cot{nullptr, out, target, 2.0f * scale, d_loss}, d_color, d_pos, aa_work);
+}
+
+extern "C" dr_status dr_antialias_xf_fwd_mse(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                             const float* rast, const float* verts, int V, const float* xform,
+                                             const int32_t* tri, int T, const int32_t* topo, float* out,
+                                             void* aa_work, const float* target, float scale, float* loss) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, xform && aligned16(xform), "antialias_xf: xform [N,4,4] must be given and 16-byte aligned");
+  DR_REQUIRE(ctx, target && loss, "antialias_mse: target and loss required");
+  return aa_fwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo, out, aa_work, target, scale, loss);
+}
+
+extern "C" dr_status dr_antialias_xf_bwd_mse(dr_ctx* ctx, const float* color, int N, int H, int W, int C,
+                                             const float* rast, const float* verts, int V, const float* xform,
+                                             const int32_t* tri, int T, const int32_t* topo, const float* out,
+                                             const float* target, float scale, const float* d_loss,
+                                             float* d_color, float* d_verts, const void* aa_work) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, xform && aligned16(xform), "antialias_xf_bwd: xform [N,4,4] must be given and 16-byte aligned");
+  DR_REQUIRE(ctx, out && target && d_loss, "antialias_bwd_mse: out, target and d_loss required");
+  return aa_bwd(ctx, color, N, H, W, C, rast, verts, xform, V, tri, T, topo,
+                Cot{nullptr, out, target, 2.0f * scale, d_loss}, d_color, d_verts, aa_work);
 }
 
 // ---------------------------------------------------------------------------

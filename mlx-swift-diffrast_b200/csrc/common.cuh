@@ -53,6 +53,7 @@ enum WsSlot {
   WS_DMIP,             // pyramid gradients before the fold into level 0
   WS_HASH,             // topology hash table
   WS_AA,               // antialias scratch
+  WS_LOSS,             // partial sums of a fused loss
   WS_NUM_SLOTS
 };
 
@@ -207,3 +208,71 @@ __device__ __forceinline__ int warp_runs(long long key, int lane, bool& head) {
 __device__ __forceinline__ int warp_max_run(int lane, int seg_end, bool head) {
   return (int)__reduce_max_sync(0xffffffffu, head ? (unsigned)(seg_end - lane) : 0u);
 }
+
+// ---------------------------------------------------------------------------
+// Fused mean-squared-error loss (the *_mse entry points).
+//
+// Cotangent of an op's output: the given tensor d, or, when the output feeds
+// only a fused loss scale * sum((pred - target)^2), that loss's gradient
+// (2 * scale * (pred - target)) * d_loss formed where it is read, with the
+// arithmetic of the stand-alone MSE VJP (so the two agree bit for bit).
+struct Cot {
+  const float* d;       // given cotangent, or nullptr for the fused loss
+  const float* pred;    // the forward output
+  const float* target;
+  float s2;             // 2 * scale
+  const float* d_loss;  // device scalar: the loss's cotangent
+};
+
+// Per-thread factor of the fused form: *d_loss (1 when d is given).
+__device__ __forceinline__ float cot_g(const Cot& c) { return c.d ? 1.0f : __ldg(c.d_loss); }
+
+__device__ __forceinline__ float cot_at(const Cot& c, float g, int64_t i) {
+  if (c.d) return __ldg(c.d + i);
+  const float r = __ldg(c.pred + i) - __ldg(c.target + i);
+  return (c.s2 * r) * g;
+}
+
+// Four consecutive elements from a 16-byte aligned index.
+__device__ __forceinline__ float4 cot_at4(const Cot& c, float g, int64_t i) {
+  if (c.d) return ldg4(c.d + i);
+  const float4 p = ldg4(c.pred + i), t = ldg4(c.target + i);
+  return make_float4((c.s2 * (p.x - t.x)) * g, (c.s2 * (p.y - t.y)) * g, (c.s2 * (p.z - t.z)) * g,
+                     (c.s2 * (p.w - t.w)) * g);
+}
+
+// Sum of squared differences of four elements (the fused loss's terms).
+__device__ __forceinline__ float sq_diff4(float4 a, float4 b) {
+  const float x = a.x - b.x, y = a.y - b.y, z = a.z - b.z, w = a.w - b.w;
+  return x * x + y * y + z * z + w * w;
+}
+
+// The forward's loss is summed per block and added to one of kLossSlots
+// partial sums (spreading the atomics over several addresses); dr::loss_end
+// writes their total to the caller's loss.
+constexpr int kLossSlots = 32;
+
+// Adds v summed over the block, times scale, to part[blockIdx.x % kLossSlots].
+// Every thread of the block must call it (it synchronises the block).
+__device__ __forceinline__ void block_loss_add(float v, float scale, float* part) {
+  __shared__ float s_warp[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) s_warp[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    float w = lane < nw ? s_warp[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+    if (lane == 0) atomicAdd(part + (blockIdx.x % kLossSlots), scale * w);
+  }
+}
+
+namespace dr {
+// Zeroed partial sums for a fused loss (a workspace slot), and their total
+// written to the caller's device scalar `loss` (one small launch).
+dr_status loss_begin(dr_ctx* ctx, float** part);
+dr_status loss_end(dr_ctx* ctx, const float* part, float* loss);
+}  // namespace dr

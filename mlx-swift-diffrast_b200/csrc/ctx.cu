@@ -225,6 +225,29 @@ __global__ void k_mse(const float* __restrict__ p, const float* __restrict__ t, 
   }
 }
 
+// loss = the kLossSlots partial sums of a fused loss, added in slot order.
+__global__ void k_loss_finish(const float* __restrict__ part, float* __restrict__ loss) {
+  if (threadIdx.x != 0) return;
+  float s = 0.0f;
+  for (int i = 0; i < kLossSlots; ++i) s += part[i];
+  *loss = s;
+}
+
+dr_status loss_begin(dr_ctx* ctx, float** part) {
+  float* p = (float*)ws_get(ctx, WS_LOSS, sizeof(float) * kLossSlots);
+  if (!p) return DR_ENOMEM;
+  DR_CUDA(ctx, cudaMemsetAsync(p, 0, sizeof(float) * kLossSlots, ctx->stream), "loss memset");
+  *part = p;
+  return DR_OK;
+}
+
+dr_status loss_end(dr_ctx* ctx, const float* part, float* loss) {
+  DR_TB(ctx);
+  k_loss_finish<<<1, 32, 0, ctx->stream>>>(part, loss);
+  DR_LAUNCHED(ctx, "loss_finish");
+  return DR_OK;
+}
+
 }  // namespace dr
 
 using namespace dr;

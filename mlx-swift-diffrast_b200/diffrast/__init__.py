@@ -19,8 +19,10 @@ from .ops import (  # noqa: F401
     FilterMode,
     antialias,
     antialias_construct_topology_hash,
+    antialias_mse,
     antialiasConstructTopologyHash,
     interpolate,
+    interpolate_mse,
     mse_loss,
     rasterize,
     rasterize_layers,
@@ -33,5 +35,5 @@ __all__ = [
     "BoundaryMode", "DiffAttrs", "FilterMode", "DiffRastError",
     "rasterize", "rasterize_layers", "interpolate", "texture", "texture_construct_mip", "textureConstructMip",
     "antialias_construct_topology_hash", "antialiasConstructTopologyHash", "antialias",
-    "mse_loss", "launch_count", "sync", "workspace_bytes", "set_raster_list_capacity", "raster_overflow",
+    "mse_loss", "antialias_mse", "interpolate_mse", "launch_count", "sync", "workspace_bytes", "set_raster_list_capacity", "raster_overflow",
 ]

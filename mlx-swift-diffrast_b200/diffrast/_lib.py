@@ -58,6 +58,12 @@ SIGNATURES = {
     "dr_antialias_work_bytes": (ctypes.c_size_t, [I, I, I]),
     "dr_antialias_xf_fwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P]),
     "dr_antialias_xf_bwd": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P, P, P]),
+    "dr_antialias_fwd_mse": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P, P, P, F, P]),
+    "dr_antialias_bwd_mse": (I, [P, P, I, I, I, I, P, P, I, P, I, P, P, P, F, P, P, P, P]),
+    "dr_antialias_xf_fwd_mse": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P, P, F, P]),
+    "dr_antialias_xf_bwd_mse": (I, [P, P, I, I, I, I, P, P, I, P, P, I, P, P, P, F, P, P, P, P]),
+    "dr_interpolate_fwd_mse": (I, [P, P, I, I, I, P, I, I, I, P, I, P, P, I, P, P, P, F, P]),
+    "dr_interpolate_bwd_mse": (I, [P, P, I, I, I, P, I, I, I, P, I, P, P, I, P, P, F, P, P, P, P, P]),
     "dr_mse_fwd_bwd": (I, [P, P, P, I64, F, P, P, I]),
     "dr_mse_bwd": (I, [P, P, P, I64, F, P, P]),
     "dr_adam_step": (I, [P, P, P, P, P, P, I64, F, F, F, F, F, F]),

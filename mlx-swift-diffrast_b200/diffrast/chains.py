@@ -90,8 +90,7 @@ class Cfg1(Chain):
     def step(self):
         rast, _ = ops.rasterize(self.pos, self.tri, self.res, grad_db=False)
         col, _ = ops.interpolate(self.rgb, rast, self.tri)
-        aa = ops.antialias(col, rast, self.pos, self.tri, self.topo)
-        loss = ops.mse_loss(aa, self.target)
+        loss, _ = ops.antialias_mse(col, rast, self.pos, self.tri, self.target, self.topo)
         loss.backward()
         return loss
 
@@ -126,8 +125,7 @@ class Cfg2(Chain):
         rgb, _ = ops.interpolate(self.rgb, rast, self.tri)
         uv, _ = ops.interpolate(self.uv, rast, self.tri)
         tc = ops.texture(self.tex, uv, filter_mode=ops.FilterMode.linear, boundary_mode=ops.BoundaryMode.clamp)
-        aa = ops.antialias(rgb * tc, rast, self.pos, self.tri, self.topo)
-        loss = ops.mse_loss(aa, self.target)
+        loss, _ = ops.antialias_mse(rgb * tc, rast, self.pos, self.tri, self.target, self.topo)
         loss.backward()
         return loss
 
@@ -210,9 +208,11 @@ class Cfg4(Chain):
         (rast0, db0), (rast1, db1) = ops.rasterize_layers(self.base, self.tri, self.res, 2, grad_db=True,
                                                           xform=self.sim)
         out0, _ = ops.interpolate(self.attr, rast0, self.tri, db0, ops.DiffAttrs.all)
-        out1, _ = ops.interpolate(self.attr, rast1, self.tri, db1, ops.DiffAttrs.all)
-        aa0 = ops.antialias(out0, rast0, self.base, self.tri, self.topo, xform=self.sim)
-        loss = ops.mse_loss(aa0, self.tgt0) + ops.mse_loss(out1, self.tgt1)
+        # Layer 1's interpolation and layer 0's antialias each compute their MSE
+        # term in their own kernels (the *_mse ops).
+        loss1, _, _ = ops.interpolate_mse(self.attr, rast1, self.tri, self.tgt1, db1, ops.DiffAttrs.all)
+        loss0, _ = ops.antialias_mse(out0, rast0, self.base, self.tri, self.tgt0, self.topo, xform=self.sim)
+        loss = loss0 + loss1
         loss.backward()
         return loss
 
@@ -268,8 +268,8 @@ class Cfg5(Chain):
             # (the projection divides by max|dir| = 0): look them up along +z.
             nrm = nrm + (rast[..., 3:] == 0).float() * self.bg_dir
             col = ops.texture(self.cube, nrm, nrm_da if mip else None, self.filter_mode, ops.BoundaryMode.cube)
-            aa = ops.antialias(col, rast, self.verts, self.tri, self.topo, xform=xf)
-            loss = ops.mse_loss(aa, self.target[a:b]) * ((b - a) / n)
+            mse, _ = ops.antialias_mse(col, rast, self.verts, self.tri, self.target[a:b], self.topo, xform=xf)
+            loss = mse * ((b - a) / n)
             self.backward(loss, last=b == n)
             tot = loss.detach() if tot is None else tot + loss.detach()
         return tot

@@ -639,6 +639,176 @@ def mse_loss(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
     return _MSE.apply(pred, target)
 
 
+# ------------------------------------------------- ops fused with the loss
+#
+# The reference's examples render and then take mean((image - target)^2)
+# (ColorFitExample/main.swift:57-60).  When an op's output feeds only that
+# loss, the *_mse ops compute it in the op's own kernels: the forward adds the
+# loss while it writes the output, and the VJP forms the output's cotangent
+# 2 (out - target) / numel * d_loss where it reads it, so neither a separate
+# loss pass nor a materialised d_out runs.  The output is returned for
+# inspection and is not differentiable: gradients flow through the loss only.
+
+def _check_target(target: torch.Tensor, like: torch.Tensor, name: str) -> torch.Tensor:
+    if tuple(target.shape) != tuple(like.shape):
+        raise ValueError(f"{name}: target must have the output's shape {tuple(like.shape)} "
+                         f"(got {tuple(target.shape)})")
+    return _f32(target, "target")
+
+
+class _AntialiasMSE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, color, pos, xform, rast, tri, topo, target):
+        ctx.set_materialize_grads(False)
+        color_c = _f32(color, "color")
+        pos_c = _f32(pos, "pos")
+        xf = _f32(xform, "xform") if xform is not None else None
+        rast_c = _f32(rast, "rast")
+        tgt = _check_target(target, color_c, "antialias_mse")
+        N, H, W, C = color_c.shape
+        V, T = (pos_c.shape[0] if xf is not None else pos_c.shape[1]), tri.shape[0]
+        out = torch.empty_like(color_c)
+        loss = torch.empty((), device=color_c.device, dtype=torch.float32)
+        scale = 1.0 / max(out.numel(), 1)
+        c = _ctx(color_c)
+        work = None
+        if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
+            work = torch.empty(L.lib().dr_antialias_work_bytes(N, H, W), dtype=torch.uint8, device=color_c.device)
+        if xf is not None:
+            L.check(L.lib().dr_antialias_xf_fwd_mse(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V,
+                                                    _ptr(xf), _ptr(tri), T, _ptr(topo), _ptr(out), _ptr(work),
+                                                    _ptr(tgt), scale, _ptr(loss)), c, "antialias_xf_mse")
+        else:
+            L.check(L.lib().dr_antialias_fwd_mse(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V,
+                                                 _ptr(tri), T, _ptr(topo), _ptr(out), _ptr(work), _ptr(tgt), scale,
+                                                 _ptr(loss)), c, "antialias_mse")
+        ctx.save_for_backward(color_c, pos_c, xf, rast_c, tri, topo, work, out, tgt)
+        ctx.scale = scale
+        ctx.mark_non_differentiable(out)
+        return loss, out
+
+    @staticmethod
+    def backward(ctx, d_loss, _d_out):
+        color_c, pos_c, xf, rast_c, tri, topo, work, out, tgt = ctx.saved_tensors
+        if d_loss is None:
+            return None, None, None, None, None, None, None
+        N, H, W, C = color_c.shape
+        V, T = (pos_c.shape[0] if xf is not None else pos_c.shape[1]), tri.shape[0]
+        g = d_loss.contiguous().float()
+        d_color = torch.empty_like(color_c)
+        d_pos = torch.empty_like(pos_c)
+        c = _ctx(color_c)
+        if xf is not None:
+            L.check(L.lib().dr_antialias_xf_bwd_mse(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V,
+                                                    _ptr(xf), _ptr(tri), T, _ptr(topo), _ptr(out), _ptr(tgt),
+                                                    ctx.scale, _ptr(g), _ptr(d_color), _ptr(d_pos), _ptr(work)),
+                    c, "antialias_xf_bwd_mse")
+        else:
+            L.check(L.lib().dr_antialias_bwd_mse(c, _ptr(color_c), N, H, W, C, _ptr(rast_c), _ptr(pos_c), V,
+                                                 _ptr(tri), T, _ptr(topo), _ptr(out), _ptr(tgt), ctx.scale, _ptr(g),
+                                                 _ptr(d_color), _ptr(d_pos), _ptr(work)), c, "antialias_bwd_mse")
+        return d_color, d_pos, None, None, None, None, None
+
+
+def antialias_mse(color: torch.Tensor, rast: torch.Tensor, pos: torch.Tensor, tri: torch.Tensor,
+                  target: torch.Tensor, topology_hash: Optional[torch.Tensor] = None,
+                  xform: Optional[torch.Tensor] = None):
+    """mean((antialias(color, rast, pos, tri) - target)^2) computed inside the
+    antialias kernels -> (loss, out).  Arguments as antialias(); the loss is
+    differentiable w.r.t. color and pos, out is not."""
+    if color.dim() != 4:
+        raise ValueError(f"antialias: color must be [N, H, W, C] (got {tuple(color.shape)})")
+    if rast.dim() != 4 or rast.shape[3] != 4 or tuple(rast.shape[:3]) != tuple(color.shape[:3]):
+        raise ValueError("antialias: rast must match color in [N, H, W] and have 4 channels")
+    if xform is not None:
+        if pos.dim() != 2 or pos.shape[1] != 4 or tuple(xform.shape) != (color.shape[0], 4, 4):
+            raise ValueError("antialias: with `xform` [N, 4, 4], pos must be [V, 4]")
+    elif pos.dim() != 3 or pos.shape[2] != 4 or pos.shape[0] != color.shape[0]:
+        raise ValueError(f"antialias: pos must be [N, V, 4] (got {tuple(pos.shape)})")
+    if tri.dim() != 2 or tri.shape[1] != 3:
+        raise ValueError(f"antialias: tri must be [T, 3] (got {tuple(tri.shape)})")
+    tri_c = _i32(tri, "tri")
+    topo = antialias_construct_topology_hash(tri_c) if topology_hash is None else _i32(topology_hash, "topologyHash")
+    return _AntialiasMSE.apply(color, pos, xform, rast.detach(), tri_c, topo, target)
+
+
+class _InterpolateMSE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, attr, rast, rast_db, tri, idx, K, target):
+        ctx.set_materialize_grads(False)
+        attr_c = _f32(attr, "attr")
+        a3 = attr_c if attr_c.dim() == 3 else attr_c.unsqueeze(0)
+        rast_c = _f32(rast, "rast")
+        db_c = _f32(rast_db, "rast_db") if K > 0 else None
+        N, H, W = rast_c.shape[:3]
+        Na, V, A = a3.shape
+        out = torch.empty((N, H, W, A), device=rast_c.device, dtype=torch.float32)
+        out_da = torch.empty((N, H, W, 2 * K), device=rast_c.device, dtype=torch.float32)
+        tgt = _check_target(target, out, "interpolate_mse")
+        loss = torch.empty((), device=rast_c.device, dtype=torch.float32)
+        scale = 1.0 / max(out.numel(), 1)
+        arr = (ctypes_int_array(idx) if idx is not None else None)
+        c = _ctx(rast_c)
+        L.check(L.lib().dr_interpolate_fwd_mse(c, _ptr(a3), Na, V, A, _ptr(rast_c), N, H, W, _ptr(tri),
+                                               tri.shape[0], _ptr(db_c), arr, K, _ptr(out),
+                                               _ptr(out_da) if K > 0 else None, _ptr(tgt), scale, _ptr(loss)),
+                c, "interpolate_mse")
+        ctx.save_for_backward(a3, rast_c, db_c, tri, out, tgt)
+        ctx.meta = (idx, K, tuple(attr.shape), scale)
+        ctx.mark_non_differentiable(out)
+        return loss, out, out_da
+
+    @staticmethod
+    def backward(ctx, d_loss, _d_out, d_out_da):
+        a3, rast_c, db_c, tri, out, tgt = ctx.saved_tensors
+        idx, K, attr_shape, scale = ctx.meta
+        N, H, W = rast_c.shape[:3]
+        Na, V, A = a3.shape
+        if d_loss is None and (d_out_da is None or K == 0):
+            return None, None, None, None, None, None, None
+        g = torch.zeros((), device=rast_c.device) if d_loss is None else d_loss.contiguous().float()
+        if K > 0 and d_out_da is None:
+            K, idx = 0, None  # out_da is off the loss path: no DA terms
+        d_out_da = d_out_da.contiguous().float() if K > 0 else None
+        d_attr = torch.empty_like(a3)
+        d_rast = torch.empty_like(rast_c)
+        d_db = torch.empty_like(rast_c) if K > 0 else None
+        arr = (ctypes_int_array(idx) if idx is not None else None)
+        c = _ctx(rast_c)
+        L.check(L.lib().dr_interpolate_bwd_mse(c, _ptr(a3), Na, V, A, _ptr(rast_c), N, H, W, _ptr(tri),
+                                               tri.shape[0], _ptr(db_c), arr, K, _ptr(out), _ptr(tgt), scale,
+                                               _ptr(g), _ptr(d_out_da), _ptr(d_attr), _ptr(d_rast), _ptr(d_db)),
+                c, "interpolate_bwd_mse")
+        return d_attr.reshape(attr_shape), d_rast, d_db, None, None, None, None
+
+
+def interpolate_mse(attr: torch.Tensor, rast: torch.Tensor, tri: torch.Tensor, target: torch.Tensor,
+                    rast_db: Optional[torch.Tensor] = None,
+                    diff_attrs: Union[None, DiffAttrs, str, Sequence[int]] = None):
+    """mean((interpolate(attr, rast, tri, ...).out - target)^2) computed inside
+    the interpolate kernels -> (loss, out, out_da).  Arguments as
+    interpolate(); the loss and out_da are differentiable, out is not."""
+    if rast.dim() != 4 or rast.shape[3] != 4:
+        raise ValueError(f"interpolate: rast must be [N, H, W, 4] (got {tuple(rast.shape)})")
+    if tri.dim() != 2 or tri.shape[1] != 3:
+        raise ValueError(f"interpolate: tri must be [T, 3] (got {tuple(tri.shape)})")
+    if attr.dim() not in (2, 3):
+        raise ValueError(f"interpolate: attr must be [V, A] or [N, V, A] (got {tuple(attr.shape)})")
+    diff = _as_diff(diff_attrs)
+    N = rast.shape[0]
+    Na = 1 if attr.dim() == 2 else attr.shape[0]
+    if Na != 1 and Na != N:
+        raise ValueError(f"interpolate: attr batch dim {Na} incompatible with rast batch {N}")
+    A = attr.shape[-1]
+    if diff is not None:
+        if rast_db is None:
+            raise ValueError("interpolate: rastDB is required when diffAttrs is set")
+        idx, K = diff.resolve(A)
+    else:
+        idx, K, rast_db = None, 0, None
+    return _InterpolateMSE.apply(attr, rast, rast_db, _i32(tri, "tri"), idx, K, target)
+
+
 # Swift-style aliases of the reference's names.
 textureConstructMip = texture_construct_mip
 antialiasConstructTopologyHash = antialias_construct_topology_hash
