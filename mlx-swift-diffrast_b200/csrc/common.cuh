@@ -148,6 +148,13 @@ __device__ __forceinline__ float4 ldg4(const float* p) {
   return __ldg(reinterpret_cast<const float4*>(p));
 }
 
+// Per-pixel streams read or written once (rast, cotangents, outputs) use the
+// streaming cache operator (evict first), so they pass through L2 without
+// evicting the small tables the same kernel gathers from (attribute rows,
+// vertices, texels) — a per-instruction hint, not a device setting.
+__device__ __forceinline__ float4 ldcs4(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ void stcs4(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
+
 // Per-view vertex transform (the "xf" entry points): clip position of vertex v
 // in view n is M_n v with M_n a row-major 4x4, evaluated in this fixed order
 // (each product and sum rounded separately):
@@ -227,16 +234,20 @@ struct Cot {
 // Per-thread factor of the fused form: *d_loss (1 when d is given).
 __device__ __forceinline__ float cot_g(const Cot& c) { return c.d ? 1.0f : __ldg(c.d_loss); }
 
+// STREAM: a per-pixel stream read once (the streaming cache operator);
+// otherwise a read that neighbouring pixels repeat.
+template <bool STREAM = false>
 __device__ __forceinline__ float cot_at(const Cot& c, float g, int64_t i) {
-  if (c.d) return __ldg(c.d + i);
-  const float r = __ldg(c.pred + i) - __ldg(c.target + i);
+  if (c.d) return STREAM ? __ldcs(c.d + i) : __ldg(c.d + i);
+  const float r = STREAM ? __ldcs(c.pred + i) - __ldcs(c.target + i) : __ldg(c.pred + i) - __ldg(c.target + i);
   return (c.s2 * r) * g;
 }
 
 // Four consecutive elements from a 16-byte aligned index.
+template <bool STREAM = false>
 __device__ __forceinline__ float4 cot_at4(const Cot& c, float g, int64_t i) {
-  if (c.d) return ldg4(c.d + i);
-  const float4 p = ldg4(c.pred + i), t = ldg4(c.target + i);
+  if (c.d) return STREAM ? ldcs4(c.d + i) : ldg4(c.d + i);
+  const float4 p = STREAM ? ldcs4(c.pred + i) : ldg4(c.pred + i), t = STREAM ? ldcs4(c.target + i) : ldg4(c.target + i);
   return make_float4((c.s2 * (p.x - t.x)) * g, (c.s2 * (p.y - t.y)) * g, (c.s2 * (p.z - t.z)) * g,
                      (c.s2 * (p.w - t.w)) * g);
 }

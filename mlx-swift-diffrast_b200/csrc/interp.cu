@@ -22,10 +22,10 @@ __device__ __forceinline__ void interp_fwd_pixel(const float* __restrict__ attr,
                                                  const float4* __restrict__ rast_db, const DiffIdx& idx, int K,
                                                  float* __restrict__ out, float* __restrict__ out_da,
                                                  const float* __restrict__ tgt, float& lsum, unsigned* err) {
-  const float4 r = __ldg(rast + pix);
+  const float4 r = __ldcs(rast + pix);
   // rast_db is independent of the triangle gathers: issue it with rast.
   float4 db = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (DA) db = __ldg(rast_db + pix);
+  if (DA) db = __ldcs(rast_db + pix);
   int t = (int)r.w - 1;
   float* o = out + pix * A;
   float* od = DA ? out_da + pix * 2 * K : nullptr;
@@ -37,20 +37,20 @@ __device__ __forceinline__ void interp_fwd_pixel(const float* __restrict__ attr,
   if (!hit) {
     if (VEC4) {
       for (int a = 0; a < A; a += 4) {
-        *reinterpret_cast<float4*>(o + a) = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (tp) lsum += sq_diff4(make_float4(0.f, 0.f, 0.f, 0.f), ldg4(tp + a));
+        stcs4(o + a, make_float4(0.f, 0.f, 0.f, 0.f));
+        if (tp) lsum += sq_diff4(make_float4(0.f, 0.f, 0.f, 0.f), ldcs4(tp + a));
       }
     } else {
       for (int a = 0; a < A; ++a) {
-        o[a] = 0.0f;
-        if (tp) { const float d = 0.0f - __ldg(tp + a); lsum += d * d; }
+        __stcs(o + a, 0.0f);
+        if (tp) { const float d = 0.0f - __ldcs(tp + a); lsum += d * d; }
       }
     }
     if (DA) {
       if (VEC4 && !IDX) {
-        for (int k = 0; k < 2 * K; k += 4) *reinterpret_cast<float4*>(od + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < 2 * K; k += 4) stcs4(od + k, make_float4(0.f, 0.f, 0.f, 0.f));
       } else {
-        for (int k = 0; k < 2 * K; ++k) od[k] = 0.0f;
+        for (int k = 0; k < 2 * K; ++k) __stcs(od + k, 0.0f);
       }
     }
     return;
@@ -74,16 +74,14 @@ __device__ __forceinline__ void interp_fwd_pixel(const float* __restrict__ attr,
       y.y = bw * x0.y + u * x1.y + v * x2.y;
       y.z = bw * x0.z + u * x1.z + v * x2.z;
       y.w = bw * x0.w + u * x1.w + v * x2.w;
-      *reinterpret_cast<float4*>(o + a) = y;
-      if (tp) lsum += sq_diff4(y, ldg4(tp + a));
+      stcs4(o + a, y);
+      if (tp) lsum += sq_diff4(y, ldcs4(tp + a));
       const float4 d01 = make_float4(x1.x - x0.x, x1.y - x0.y, x1.z - x0.z, x1.w - x0.w);
       const float4 d02 = make_float4(x2.x - x0.x, x2.y - x0.y, x2.z - x0.z, x2.w - x0.w);
-      *reinterpret_cast<float4*>(od + 2 * a) =
-          make_float4(d01.x * db.x + d02.x * db.z, d01.x * db.y + d02.x * db.w,
-                      d01.y * db.x + d02.y * db.z, d01.y * db.y + d02.y * db.w);
-      *reinterpret_cast<float4*>(od + 2 * a + 4) =
-          make_float4(d01.z * db.x + d02.z * db.z, d01.z * db.y + d02.z * db.w,
-                      d01.w * db.x + d02.w * db.z, d01.w * db.y + d02.w * db.w);
+      stcs4(od + 2 * a, make_float4(d01.x * db.x + d02.x * db.z, d01.x * db.y + d02.x * db.w,
+                                    d01.y * db.x + d02.y * db.z, d01.y * db.y + d02.y * db.w));
+      stcs4(od + 2 * a + 4, make_float4(d01.z * db.x + d02.z * db.z, d01.z * db.y + d02.z * db.w,
+                                        d01.w * db.x + d02.w * db.z, d01.w * db.y + d02.w * db.w));
     }
     return;
   }
@@ -96,14 +94,14 @@ __device__ __forceinline__ void interp_fwd_pixel(const float* __restrict__ attr,
       y.y = bw * x0.y + u * x1.y + v * x2.y;
       y.z = bw * x0.z + u * x1.z + v * x2.z;
       y.w = bw * x0.w + u * x1.w + v * x2.w;
-      *reinterpret_cast<float4*>(o + a) = y;
-      if (tp) lsum += sq_diff4(y, ldg4(tp + a));
+      stcs4(o + a, y);
+      if (tp) lsum += sq_diff4(y, ldcs4(tp + a));
     }
   } else {
     for (int a = 0; a < A; ++a) {
       const float y = bw * __ldg(a0p + a) + u * __ldg(a1p + a) + v * __ldg(a2p + a);
-      o[a] = y;
-      if (tp) { const float d = y - __ldg(tp + a); lsum += d * d; }
+      __stcs(o + a, y);
+      if (tp) { const float d = y - __ldcs(tp + a); lsum += d * d; }
     }
   }
   if (DA) {
@@ -111,8 +109,8 @@ __device__ __forceinline__ void interp_fwd_pixel(const float* __restrict__ attr,
       const int a = IDX ? idx.k[k] : k;
       const float x0 = __ldg(a0p + a), x1 = __ldg(a1p + a), x2 = __ldg(a2p + a);
       const float d01 = x1 - x0, d02 = x2 - x0;
-      od[2 * k + 0] = d01 * db.x + d02 * db.z;
-      od[2 * k + 1] = d01 * db.y + d02 * db.w;
+      __stcs(od + 2 * k + 0, d01 * db.x + d02 * db.z);
+      __stcs(od + 2 * k + 1, d01 * db.y + d02 * db.w);
     }
   }
 }

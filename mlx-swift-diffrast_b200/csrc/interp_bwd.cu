@@ -22,7 +22,7 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
   const int lane = threadIdx.x & 31;
   const bool in = pix < P;
   float4 r = make_float4(0.f, 0.f, 0.f, -1.f);
-  if (in) r = __ldg(rast + pix);
+  if (in) r = __ldcs(rast + pix);
   int t = (int)r.w - 1;
   int i0 = 0, i1 = 0, i2 = 0;
   bool hit = in && t >= 0;
@@ -48,7 +48,7 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
   const float gl = cot_g(d_out);
   const float* gd = DA ? d_out_da + pix * 2 * K : nullptr;
   float4 db = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (DA && hit) db = __ldg(rast_db + pix);
+  if (DA && hit) db = __ldcs(rast_db + pix);
   float du = 0.0f, dv = 0.0f;
   float d_udx = 0.0f, d_udy = 0.0f, d_vdx = 0.0f, d_vdy = 0.0f;
   for (int a = 0; a < A; a += 4) {
@@ -56,7 +56,7 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
     if (hit) {
       float ga[4], x0[4], x1[4], x2[4];
       if (VEC4) {
-        const float4 q = cot_at4(d_out, gl, g + a), p0 = ldg4(a0p + a), p1 = ldg4(a1p + a), p2 = ldg4(a2p + a);
+        const float4 q = cot_at4<true>(d_out, gl, g + a), p0 = ldg4(a0p + a), p1 = ldg4(a1p + a), p2 = ldg4(a2p + a);
         ga[0] = q.x; ga[1] = q.y; ga[2] = q.z; ga[3] = q.w;
         x0[0] = p0.x; x0[1] = p0.y; x0[2] = p0.z; x0[3] = p0.w;
         x1[0] = p1.x; x1[1] = p1.y; x1[2] = p1.z; x1[3] = p1.w;
@@ -65,7 +65,7 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const bool ok = a + j < A;
-          ga[j] = ok ? cot_at(d_out, gl, g + a + j) : 0.f;
+          ga[j] = ok ? cot_at<true>(d_out, gl, g + a + j) : 0.f;
           x0[j] = ok ? __ldg(a0p + a + j) : 0.f;
           x1[j] = ok ? __ldg(a1p + a + j) : 0.f;
           x2[j] = ok ? __ldg(a2p + a + j) : 0.f;
@@ -84,7 +84,7 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (!VEC4 && a + j >= A) break;
-          const float gx = __ldg(gd + 2 * (a + j)), gy = __ldg(gd + 2 * (a + j) + 1);
+          const float gx = __ldcs(gd + 2 * (a + j)), gy = __ldcs(gd + 2 * (a + j) + 1);
           const float u_term = gx * db.x + gy * db.y;
           const float v_term = gx * db.z + gy * db.w;
           c0[j] += -u_term - v_term;
@@ -122,17 +122,17 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
   }
   if (!in) return;
   if (!hit) {
-    d_rast[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (DA) d_rast_db[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __stcs(d_rast + pix, make_float4(0.f, 0.f, 0.f, 0.f));
+    if (DA) __stcs(d_rast_db + pix, make_float4(0.f, 0.f, 0.f, 0.f));
     return;
   }
-  d_rast[pix] = make_float4(du, dv, 0.0f, 0.0f);
+  __stcs(d_rast + pix, make_float4(du, dv, 0.0f, 0.0f));
   if (DA) {
     if (IDX) {
       // .indices: arbitrary (possibly repeated) attribute indices.
       for (int k = 0; k < K; ++k) {
         const int a = idx.k[k];
-        const float gx = __ldg(gd + 2 * k), gy = __ldg(gd + 2 * k + 1);
+        const float gx = __ldcs(gd + 2 * k), gy = __ldcs(gd + 2 * k + 1);
         const float u_term = gx * db.x + gy * db.y;
         const float v_term = gx * db.z + gy * db.w;
         atomicAdd(g0p + a, -u_term - v_term);
@@ -146,7 +146,7 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
         d_vdy += d02 * gy;
       }
     }
-    d_rast_db[pix] = make_float4(d_udx, d_udy, d_vdx, d_vdy);
+    __stcs(d_rast_db + pix, make_float4(d_udx, d_udy, d_vdx, d_vdy));
   }
 }
 

@@ -216,16 +216,30 @@ k_raster_scatter_binned(const float4* __restrict__ rec, int T, int ntx, int nty,
   for (int i = threadIdx.x; i < ntiles; i += blockDim.x) s_base[i] = __ldg(col + (int64_t)i * cpv);
   __syncthreads();
   const int t0 = c * chunk, t1 = min(T, t0 + chunk);
-  for (int t = t0 + (int)threadIdx.x; t < t1; t += blockDim.x) {
-    const float4 r2 = __ldg(rec + 3 * ((int64_t)n * T + t) + 2);
-    if (r2.y == 0.0f) continue;  // area == 0: invalid
-    const unsigned xs = __float_as_uint(r2.z), ys = __float_as_uint(r2.w);
-    const int x0 = (int)(xs & 0xffffu), x1 = (int)(xs >> 16), y0 = (int)(ys & 0xffffu), y1 = (int)(ys >> 16);
-    for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
-      for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) {
-        const uint32_t slot = atomicAdd(&s_base[ty * ntx + tx], 1u);
-        if (slot < cap) list[slot] = t;  // past a fixed capacity: the tile scans instead
-      }
+  // Four records per thread per round, loaded before any is used, so four
+  // independent loads are in flight (the loop is otherwise one load latency
+  // per triangle).
+  constexpr int R = 4;
+  const float4* rv = rec + 3 * (int64_t)n * T + 2;
+  for (int tb = t0 + (int)threadIdx.x; tb < t1; tb += R * blockDim.x) {
+    float4 r2[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int t = tb + k * (int)blockDim.x;
+      r2[k] = t < t1 ? __ldg(rv + 3 * (int64_t)t) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      if (r2[k].y == 0.0f) continue;  // area == 0: invalid (or past the chunk)
+      const int t = tb + k * (int)blockDim.x;
+      const unsigned xs = __float_as_uint(r2[k].z), ys = __float_as_uint(r2[k].w);
+      const int x0 = (int)(xs & 0xffffu), x1 = (int)(xs >> 16), y0 = (int)(ys & 0xffffu), y1 = (int)(ys >> 16);
+      for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
+        for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) {
+          const uint32_t slot = atomicAdd(&s_base[ty * ntx + tx], 1u);
+          if (slot < cap) list[slot] = t;  // past a fixed capacity: the tile scans instead
+        }
+    }
   }
 }
 

@@ -23,7 +23,7 @@ __global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const fl
   const int64_t P = (int64_t)N * H * W;
   const bool in = pix < P;
   float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (in) r = __ldg(rast + pix);
+  if (in) r = __ldcs(rast + pix);
   const int t = (int)r.w - 1;
   bool hit = in && t >= 0;
   if (hit && t >= T) { dr_flag(err, DR_DEVERR_TRI_ID); hit = false; }
@@ -45,11 +45,11 @@ __global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const fl
     const int ph = (int)((pix / W) % H);
     const float u_val = r.x, v_val = r.y;
     const float bw_val = 1.0f - u_val - v_val;
-    const float4 g = __ldg(d_rast + pix);
+    const float4 g = __ldcs(d_rast + pix);
     const float d_u = g.x, d_v = g.y, d_z = g.z;
     float d_db0 = 0.f, d_db1 = 0.f, d_db2 = 0.f, d_db3 = 0.f;
     if (DB) {
-      const float4 gd = __ldg(d_rast_db + pix);
+      const float4 gd = __ldcs(d_rast_db + pix);
       d_db0 = gd.x; d_db1 = gd.y; d_db2 = gd.z; d_db3 = gd.w;
     }
     const float Px = __fdividef(2.0f * ((float)pw + 0.5f), (float)W) - 1.0f;
