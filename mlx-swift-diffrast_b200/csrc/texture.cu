@@ -194,13 +194,20 @@ __device__ __forceinline__ void red_add_texel(float* p, int C, float v0, float v
 // one (vector) atomic instead of one per pixel; a run covering the whole warp
 // goes to the CTA's hot cache when one is given.  All 32 lanes of the warp
 // must call it; lanes with on == false add nothing.
-__device__ __forceinline__ void scatter_tap4(float* p, float4 v, int C, bool on, int lane, HotCache* hc) {
+// so >= 0: the tap's texel is held at s_small[so .. so + C) (the CTA's shared
+// copy of the small levels, see SmallLevels below) instead of at p.
+__device__ __forceinline__ void scatter_tap4(float* p, float4 v, int C, bool on, int lane, HotCache* hc,
+                                             float* s_small = nullptr, int so = -1) {
+  const bool smem = so >= 0;
+  float* sp = s_small + so;
   const long long key = on ? (long long)(uintptr_t)p : -1ll - (long long)lane;
   bool head;
   const int seg_end = warp_runs(key, lane, head);
   const int span = warp_max_run(lane, seg_end, head);
   if (!on) v = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (hc && span == 32) {
+  // A run spanning the warp has one key, so all 32 lanes are on and share p
+  // (or all share sp: the small levels are already reduced per CTA).
+  if (hc && span == 32 && !smem) {
     // One run spans the warp: all 32 lanes are on and share p.
     float sum[kHotC] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -228,7 +235,17 @@ __device__ __forceinline__ void scatter_tap4(float* p, float4 v, int C, bool on,
     if (C > 2) v.z = warp_seg_sum(v.z, lane, seg_end, span);
     if (C > 3) v.w = warp_seg_sum(v.w, lane, seg_end, span);
   }
-  if (on && head) red_add_texel(p, C, v.x, v.y, v.z, v.w);
+  if (on && head) {
+    if (smem) {
+      // The CTA's shared copy of the small levels: scalar shared atomics.
+      if (v.x != 0.0f) atomicAdd(sp, v.x);
+      if (C > 1 && v.y != 0.0f) atomicAdd(sp + 1, v.y);
+      if (C > 2 && v.z != 0.0f) atomicAdd(sp + 2, v.z);
+      if (C > 3 && v.w != 0.0f) atomicAdd(sp + 3, v.w);
+    } else {
+      red_add_texel(p, C, v.x, v.y, v.z, v.w);
+    }
+  }
 }
 
 // Contribution w * (g[c] * gscale) of one tap, C <= 4 (unused channels 0).
@@ -246,12 +263,14 @@ __device__ __forceinline__ float4 load_cot(const float* __restrict__ g, int C, b
 // issue scalar atomics from the run heads.  A zero contribution issues no
 // atomic (d_tex starts at +0, and adding +-0 to +0 leaves +0).
 __device__ __forceinline__ void scatter_tap(float* p, float w, const float* __restrict__ g, float gscale, int C,
-                                            bool on, int lane, HotCache* hc = nullptr) {
+                                            bool on, int lane, HotCache* hc = nullptr, float* s_small = nullptr,
+                                            int so = -1) {
   if (C <= 4) {
     const float4 gv = on ? load_cot(g, C, false) : make_float4(0.f, 0.f, 0.f, 0.f);
-    scatter_tap4(p, tap_contrib(w, gv, gscale), C, on, lane, hc);
+    scatter_tap4(p, tap_contrib(w, gv, gscale), C, on, lane, hc, s_small, so);
     return;
   }
+  const bool smem = so >= 0;
   const long long key = on ? (long long)(uintptr_t)p : -1ll - (long long)lane;
   bool head;
   const int seg_end = warp_runs(key, lane, head);
@@ -259,15 +278,21 @@ __device__ __forceinline__ void scatter_tap(float* p, float w, const float* __re
   for (int c = 0; c < C; ++c) {
     float v = on ? w * (__ldg(g + c) * gscale) : 0.0f;
     if (span > 1) v = warp_seg_sum(v, lane, seg_end, span);
-    if (on && head && v != 0.0f) atomicAdd(p + c, v);
+    if (on && head && v != 0.0f) {
+      if (smem) atomicAdd(s_small + so + c, v);
+      else atomicAdd(p + c, v);
+    }
   }
 }
 
 // The four taps of one bilinear sample (weights q.w**, clamp / wrap / zero
 // masks included): the pixel's cotangent g (C channels; gv = its first four)
 // times `scale` and each tap's weight.
+// slev >= 0: the level is held in the CTA's shared copy of the small levels,
+// starting at s_small[slev]; its taps go there.
 __device__ __forceinline__ void scatter_bilin(float* db, const Taps& q, const float* __restrict__ g, float4 gv,
-                                              float scale, int C, bool on, int lane, HotCache* hc) {
+                                              float scale, int C, bool on, int lane, HotCache* hc,
+                                              float* s_small = nullptr, int slev = -1) {
   if (C <= 4) {
     // A rolled loop: one copy of the scatter code (the unrolled four copies
     // measured slower, instruction-fetch bound).
@@ -275,13 +300,41 @@ __device__ __forceinline__ void scatter_bilin(float* db, const Taps& q, const fl
     for (int tp = 0; tp < 4; ++tp) {
       const int64_t a = tp == 0 ? q.a00 : (tp == 1 ? q.a10 : (tp == 2 ? q.a01 : q.a11));
       const float w = tp == 0 ? q.w00 : (tp == 1 ? q.w10 : (tp == 2 ? q.w01 : q.w11));
-      scatter_tap4(db + a * C, tap_contrib(w, gv, scale), C, on, lane, hc);
+      scatter_tap4(db + a * C, tap_contrib(w, gv, scale), C, on, lane, hc, s_small,
+                   slev >= 0 ? slev + (int)a * C : -1);
     }
   } else {
-    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, on, lane, hc);
-    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, on, lane, hc);
-    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, on, lane, hc);
-    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, on, lane, hc);
+    scatter_tap(db + q.a00 * C, q.w00, g, scale, C, on, lane, hc, s_small, slev >= 0 ? slev + (int)q.a00 * C : -1);
+    scatter_tap(db + q.a10 * C, q.w10, g, scale, C, on, lane, hc, s_small, slev >= 0 ? slev + (int)q.a10 * C : -1);
+    scatter_tap(db + q.a01 * C, q.w01, g, scale, C, on, lane, hc, s_small, slev >= 0 ? slev + (int)q.a01 * C : -1);
+    scatter_tap(db + q.a11 * C, q.w11, g, scale, C, on, lane, hc, s_small, slev >= 0 ? slev + (int)q.a11 * C : -1);
+  }
+}
+
+// Shared-memory reduction of the pyramid's smallest levels.  Every pixel whose
+// LOD reaches a level of a few texels scatters into the same handful of
+// addresses; the mip VJPs keep the gradient of the levels [ks, L) of a shared
+// texture (the tail of the pyramid gradient buffer, contiguous from
+// base = off[ks]) in shared memory and add it to global memory once per CTA,
+// one atomic per non-zero float.  ks == L (n == 0) holds nothing.
+// 4 KB: the shared copy is carved out of the L1 the texel gathers use, so it
+// holds only the top levels, where the contention is (a few texels per level).
+constexpr int kSmallCap = 1024;  // floats
+struct SmallLevels {
+  int ks;
+  int n;
+  int64_t base;
+};
+
+__device__ __forceinline__ void small_init(float* s, const SmallLevels& sl) {
+  for (int i = threadIdx.x; i < sl.n; i += blockDim.x) s[i] = 0.0f;
+}
+
+// After a CTA barrier: the CTA's sums into the pyramid gradient.
+__device__ __forceinline__ void small_flush(const float* s, const SmallLevels& sl, float* __restrict__ d_pyr) {
+  for (int i = threadIdx.x; i < sl.n; i += blockDim.x) {
+    const float v = s[i];
+    if (v != 0.0f) atomicAdd(d_pyr + sl.base + i, v);
   }
 }
 
@@ -748,13 +801,15 @@ __device__ __forceinline__ void mip_texel_terms(const Taps& q, float r00, float 
 // floor and floor + 1 are the sampled levels whenever K22 is non-zero).
 // VEC4: C == 4 with 16-byte aligned texture, pyramid and cotangent.
 template <int MODE, bool MIP_LINEAR, bool VEC4>
-__global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
-                              bool tex_shared, int C, const float2* __restrict__ uv,
-                              const float4* __restrict__ uv_da, float bias, const float* __restrict__ bias_map,
-                              int64_t P, int64_t HWi, const float* __restrict__ d_out,
-                              float* __restrict__ d_tex, float* __restrict__ d_pyr, float2* __restrict__ d_uv,
-                              float4* __restrict__ d_uv_da, float* __restrict__ d_bias_map) {
-  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void mip_bwd_pixel(const int64_t pix0, const float* __restrict__ tex,
+                                              const float* __restrict__ pyr, const MipDesc& m, bool tex_shared,
+                                              int C, const float2* __restrict__ uv,
+                                              const float4* __restrict__ uv_da, float bias,
+                                              const float* __restrict__ bias_map, int64_t P, int64_t HWi,
+                                              const float* __restrict__ d_out, float* __restrict__ d_tex,
+                                              float* __restrict__ d_pyr, float2* __restrict__ d_uv,
+                                              float4* __restrict__ d_uv_da, float* __restrict__ d_bias_map,
+                                              HotCache* hc, float* s_small, const SmallLevels& sl) {
   const bool on = pix0 < P;
   const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
   const int lane = threadIdx.x & 31;
@@ -769,9 +824,6 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_mip_bwd(const floa
   const bool acc = MIP_LINEAR && want_lod && lod_interior(ls.raw, L);
   const float4 gv = C <= 4 ? load_cot(g, C, VEC4) : make_float4(0.f, 0.f, 0.f, 0.f);
   float dfx_total = 0.0f, dfy_total = 0.0f, d_lod = 0.0f;
-  __shared__ HotCache hc;
-  hot_init(&hc);
-  __syncthreads();
 #pragma unroll
   for (int li = 0; li < 2; ++li) {
     const int k = li == 0 ? ls.k0 : ls.k1;
@@ -781,7 +833,8 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_mip_bwd(const floa
     const float* b = level_ptr(tex, pyr, m, k, nt, C);
     float* db = (k == 0 ? d_tex : d_pyr + m.off[k]) + nt * (int64_t)m.h[k] * m.w[k] * C;
     float dfx = 0.0f, dfy = 0.0f;
-    scatter_bilin(db, q, g, gv, scale, C, on && scale != 0.0f, lane, &hc);
+    scatter_bilin(db, q, g, gv, scale, C, on && scale != 0.0f, lane, hc, s_small,
+                  k >= sl.ks ? (int)(m.off[k] - sl.base) : -1);  // a small level: shared texture, nt == 0
     if constexpr (VEC4) {
       const float4 T00 = ldg4(b + q.a00 * 4), T10 = ldg4(b + q.a10 * 4);
       const float4 T01 = ldg4(b + q.a01 * 4), T11 = ldg4(b + q.a11 * 4);
@@ -797,7 +850,6 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_mip_bwd(const floa
     dfx_total += dfx * (float)m.w[k];
     dfy_total += dfy * (float)m.h[k];
   }
-  hot_flush(&hc, C);
   if (!on) return;
   d_uv[pix] = make_float2(dfx_total, dfy_total);
 
@@ -811,6 +863,27 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_mip_bwd(const floa
     const float acc_m = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
     d_bias_map[pix] = bias_map ? acc_m * 0.6931471805599453f : 0.0f;
   }
+}
+
+// Mip-mapped VJP: d_tex / pyramid gradient, d_uv, d_uvDA (and the bias map's
+// gradient), one pixel per thread.
+template <int MODE, bool MIP_LINEAR, bool VEC4>
+__global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+                              bool tex_shared, int C, const float2* __restrict__ uv,
+                              const float4* __restrict__ uv_da, float bias, const float* __restrict__ bias_map,
+                              int64_t P, int64_t HWi, const float* __restrict__ d_out,
+                              float* __restrict__ d_tex, float* __restrict__ d_pyr, float2* __restrict__ d_uv,
+                              float4* __restrict__ d_uv_da, float* __restrict__ d_bias_map, const SmallLevels sl) {
+  __shared__ HotCache hc;
+  __shared__ float s_small[kSmallCap];
+  hot_init(&hc);
+  small_init(s_small, sl);
+  __syncthreads();
+  mip_bwd_pixel<MODE, MIP_LINEAR, VEC4>((int64_t)blockIdx.x * blockDim.x + threadIdx.x, tex, pyr, m, tex_shared, C,
+                                        uv, uv_da, bias, bias_map, P, HWi, d_out, d_tex, d_pyr, d_uv, d_uv_da,
+                                        d_bias_map, &hc, s_small, sl);
+  hot_flush(&hc, C);  // a CTA barrier first
+  small_flush(s_small, sl, d_pyr);
 }
 
 // ------------------------------------------------------- mip-mapped cube
@@ -844,14 +917,15 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_FWD) k_tex_cube_mip_fwd(const
 }
 
 template <bool MIP_LINEAR, bool DIR_GRAD>
-__global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
-                                   bool tex_shared, int C, const float* __restrict__ dir,
-                                   const float2* __restrict__ dir_da, float bias,
-                                   const float* __restrict__ bias_map, int64_t P, int64_t HWi,
-                                   const float* __restrict__ d_out, float* __restrict__ d_tex,
-                                   float* __restrict__ d_pyr, float* __restrict__ d_dir,
-                                   float2* __restrict__ d_dir_da, float* __restrict__ d_bias_map) {
-  const int64_t pix0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void cube_mip_bwd_pixel(const int64_t pix0, const float* __restrict__ tex,
+                                                   const float* __restrict__ pyr, const MipDesc& m, bool tex_shared,
+                                                   int C, const float* __restrict__ dir,
+                                                   const float2* __restrict__ dir_da, float bias,
+                                                   const float* __restrict__ bias_map, int64_t P, int64_t HWi,
+                                                   const float* __restrict__ d_out, float* __restrict__ d_tex,
+                                                   float* __restrict__ d_pyr, float* __restrict__ d_dir,
+                                                   float2* __restrict__ d_dir_da, float* __restrict__ d_bias_map,
+                                                   HotCache* hc, float* s_small, const SmallLevels& sl) {
   const bool on = pix0 < P;
   const int64_t pix = on ? pix0 : P - 1;  // out-of-range lanes follow a valid pixel, adding nothing
   const int lane = threadIdx.x & 31;
@@ -867,9 +941,6 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube_mip_bwd(const
   const bool acc = MIP_LINEAR && want_lod && lod_interior(ls.raw, m.L);
   const float4 gv = C <= 4 ? load_cot(g, C, false) : make_float4(0.f, 0.f, 0.f, 0.f);
   float d_u = 0.0f, d_v = 0.0f, d_lod = 0.0f;
-  __shared__ HotCache hc;
-  hot_init(&hc);
-  __syncthreads();
 #pragma unroll
   for (int li = 0; li < 2; ++li) {
     const int k = li == 0 ? ls.k0 : ls.k1;
@@ -877,7 +948,8 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube_mip_bwd(const
     const float sign = li == 0 ? -1.0f : 1.0f;
     const Taps q = bilin_taps<1>(f.u, f.v, m.w[k], m.h[k]);
     float* db = (k == 0 ? d_tex : d_pyr + m.off[k]) + img * (int64_t)m.h[k] * m.w[k] * C;
-    scatter_bilin(db, q, g, gv, scale, C, on && scale != 0.0f, lane, &hc);
+    scatter_bilin(db, q, g, gv, scale, C, on && scale != 0.0f, lane, hc, s_small,
+                  k >= sl.ks ? (int)(m.off[k] - sl.base + img * (int64_t)m.h[k] * m.w[k] * C) : -1);
     if (DIR_GRAD || acc) {
       const float* b = level_ptr(tex, pyr, m, k, img, C);
       float dfx = 0.0f, dfy = 0.0f;
@@ -888,7 +960,6 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube_mip_bwd(const
       d_v += dfy * (float)m.h[k];
     }
   }
-  hot_flush(&hc, C);
   if (!on) return;
   AxisGrad ag = {0.0f, 0.0f, 0.0f};
   if (DIR_GRAD) ag = cube_dir_vjp(f, d_u, d_v);
@@ -912,6 +983,27 @@ __global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube_mip_bwd(const
     const float acc_m = g4.x * e.x + g4.y * e.y + g4.z * e.z + g4.w * e.w;
     d_bias_map[pix] = bias_map ? acc_m * 0.6931471805599453f : 0.0f;
   }
+}
+
+template <bool MIP_LINEAR, bool DIR_GRAD>
+__global__ void __launch_bounds__(256, DR_MINB_TEX_BWD) k_tex_cube_mip_bwd(const float* __restrict__ tex, const float* __restrict__ pyr, const MipDesc m,
+                                   bool tex_shared, int C, const float* __restrict__ dir,
+                                   const float2* __restrict__ dir_da, float bias,
+                                   const float* __restrict__ bias_map, int64_t P, int64_t HWi,
+                                   const float* __restrict__ d_out, float* __restrict__ d_tex,
+                                   float* __restrict__ d_pyr, float* __restrict__ d_dir,
+                                   float2* __restrict__ d_dir_da, float* __restrict__ d_bias_map,
+                                   const SmallLevels sl) {
+  __shared__ HotCache hc;
+  __shared__ float s_small[kSmallCap];
+  hot_init(&hc);
+  small_init(s_small, sl);
+  __syncthreads();
+  cube_mip_bwd_pixel<MIP_LINEAR, DIR_GRAD>((int64_t)blockIdx.x * blockDim.x + threadIdx.x, tex, pyr, m, tex_shared,
+                                           C, dir, dir_da, bias, bias_map, P, HWi, d_out, d_tex, d_pyr, d_dir,
+                                           d_dir_da, d_bias_map, &hc, s_small, sl);
+  hot_flush(&hc, C);  // a CTA barrier first
+  small_flush(s_small, sl, d_pyr);
 }
 
 // d_tex[level 0] += sum_k d_pyr_k[y >> k, x >> k] / 4^k: the adjoint of the
@@ -1178,14 +1270,25 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
     DR_CUDA(ctx, cudaMemsetAsync(dpyr, 0, sizeof(float) * (size_t)a.pyr_floats, ctx->stream),
             "texture_bwd memset");
   }
+  // The smallest levels of a shared texture (all of them that fit together in
+  // kSmallCap floats) are reduced in shared memory per CTA.
+  SmallLevels sl{a.m.L, 0, 0};
+  if (shared && a.m.L > 1) {
+    for (int k = 1; k < a.m.L; ++k)
+      if (a.pyr_floats - a.m.off[k] <= kSmallCap) {
+        sl = SmallLevels{k, (int)(a.pyr_floats - a.m.off[k]), a.m.off[k]};
+        break;
+      }
+  }
+  const unsigned mgrid = grid;
   if (a.cube) {
     const float2* dda = reinterpret_cast<const float2*>(uv_da);
     float2* ddda = reinterpret_cast<float2*>(d_uv_da);
     DR_TB(ctx);
 #define DR_CUBE_MIP_BWD(ML, DG)                                                                                     \
-  k_tex_cube_mip_bwd<ML, DG><<<grid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,       \
-                                                            mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr, d_uv, \
-                                                            ddda, d_bias_map)
+  k_tex_cube_mip_bwd<ML, DG><<<mgrid, 256, 0, ctx->stream>>>(tex, pyr, a.m, shared, C, uv, dda, mip_level_bias,      \
+                                                             mip_level_bias_map, a.P, a.HWi, d_out, d_tex, dpyr,     \
+                                                             d_uv, ddda, d_bias_map, sl)
     if (a.mip_linear) {
       if (a.dir_grad) DR_CUBE_MIP_BWD(true, true); else DR_CUBE_MIP_BWD(true, false);
     } else {
@@ -1199,9 +1302,9 @@ extern "C" dr_status dr_texture_bwd(dr_ctx* ctx, int filter, int boundary, const
   const bool vec4 = C == 4 && aligned(tex, 16) && aligned(pyr, 16) && aligned(d_out, 16);
   DR_TB(ctx);
 #define DR_MIP_BWD(ML, V4)                                                                                          \
-  DR_MODE_SWITCH(boundary, (k_tex_mip_bwd<MODE, ML, V4><<<grid, 256, 0, ctx->stream>>>(                               \
+  DR_MODE_SWITCH(boundary, (k_tex_mip_bwd<MODE, ML, V4><<<mgrid, 256, 0, ctx->stream>>>(                              \
                                tex, pyr, a.m, shared, C, uv2, da4, mip_level_bias, mip_level_bias_map, a.P, a.HWi, \
-                               d_out, d_tex, dpyr, duv2, dda4, d_bias_map)))
+                               d_out, d_tex, dpyr, duv2, dda4, d_bias_map, sl)))
   if (a.mip_linear) {
     if (vec4) { DR_MIP_BWD(true, true); } else { DR_MIP_BWD(true, false); }
   } else {

@@ -192,6 +192,28 @@ def test_texture_cube_mip_matches_oracle(cu, filt, nt, C):
     assert rel_l2(ga[1], gb[1]) < 1e-4 and rel_l2(ga[2], gb[2]) < 1e-4
 
 
+@pytest.mark.parametrize("C", [1, 3, 4, 5])
+@pytest.mark.parametrize("filt", ["linear-mipmap-nearest", "linear-mipmap-linear"])
+def test_texture_bwd_small_levels_reduced_in_shared_memory(cu, filt, C):
+    # A bias of +6 sends most LODs to the pyramid's top levels (4x4 .. 1x1 of
+    # a 256^2 texture), which the VJP accumulates in shared memory per CTA and
+    # adds to the pyramid gradient once per CTA: many pixels per texel.
+    g = np.random.default_rng(31)
+    tex = g.random((1, 256, 256, C)).astype(np.float32)
+    uv = g.uniform(0, 1, size=(3, 96, 80, 2)).astype(np.float32)
+    da = (g.normal(size=(3, 96, 80, 4)) * 0.01).astype(np.float32)
+    bmap = g.uniform(-1, 1, size=(3, 96, 80)).astype(np.float32)
+    kw = dict(uv_da=da, filter_mode=filt, boundary_mode="wrap", bias=6.0, bias_map=bmap)
+    a = cu.texture(tex, uv, **kw)
+    b = O.texture(tex, uv, **kw)
+    assert _rel_max(a, b) <= 1e-5
+    d_out = g.normal(size=a.shape).astype(np.float32)
+    ga = cu.texture_bwd(tex, uv, d_out, **kw)
+    gb = O.texture_bwd(tex, uv, d_out, **kw)
+    for x, y in zip(ga, gb):
+        assert rel_l2(x, y) < 1e-4
+
+
 def test_texture_mip_large_pyramid(cu):
     # A 1024^2 x 4 texture (11 levels) sampled at mixed LODs.
     g = np.random.default_rng(13)
