@@ -388,6 +388,103 @@ public enum DiffRast {
         return loss
     }
 
+    /// antialias followed by the examples' loss `((out - target)^2).mean()`,
+    /// computed in the antialias kernels: returns the loss (a device scalar)
+    /// and out.  `verts` / `xform` select the per-view transform form (as
+    /// antialiasXF); otherwise `pos` is [N, V, 4].
+    public static func antialiasMSE(_ ctx: Context, _ alloc: DeviceAllocator, color: DeviceTensor,
+                                    rast: DeviceTensor, pos: DeviceTensor, xform: DeviceTensor? = nil,
+                                    tri: DeviceTensor, topologyHash: DeviceTensor, target: DeviceTensor,
+                                    work: UnsafeMutableRawPointer? = nil) -> (loss: DeviceTensor, out: DeviceTensor) {
+        let N = color.shape[0], H = color.shape[1], W = color.shape[2], C = color.shape[3]
+        let out = DeviceTensor(pointer: alloc.allocate(bytes: color.count * 4), shape: color.shape)
+        let loss = DeviceTensor(pointer: alloc.allocate(bytes: 4), shape: [1])
+        let scale = 1.0 / Float(color.count)
+        if let xf = xform {
+            ctx.check(dr_antialias_xf_fwd_mse(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f,
+                                              pos.f, Int32(pos.shape[0]), xf.f, tri.i, Int32(tri.shape[0]),
+                                              topologyHash.i, out.f, work, target.f, scale, loss.f),
+                      "antialiasMSE")
+        } else {
+            ctx.check(dr_antialias_fwd_mse(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f, pos.f,
+                                           Int32(pos.shape[1]), tri.i, Int32(tri.shape[0]), topologyHash.i, out.f,
+                                           work, target.f, scale, loss.f), "antialiasMSE")
+        }
+        return (loss, out)
+    }
+
+    /// VJP of antialiasMSE for the loss's cotangent dLoss (a device scalar);
+    /// `out` is the forward's output.
+    public static func antialiasMSEVJP(_ ctx: Context, _ alloc: DeviceAllocator, color: DeviceTensor,
+                                       rast: DeviceTensor, pos: DeviceTensor, xform: DeviceTensor? = nil,
+                                       tri: DeviceTensor, topologyHash: DeviceTensor, out: DeviceTensor,
+                                       target: DeviceTensor, dLoss: DeviceTensor,
+                                       work: UnsafeRawPointer? = nil) -> (dColor: DeviceTensor, dPos: DeviceTensor) {
+        let N = color.shape[0], H = color.shape[1], W = color.shape[2], C = color.shape[3]
+        let dColor = DeviceTensor(pointer: alloc.allocate(bytes: color.count * 4), shape: color.shape)
+        let dPos = DeviceTensor(pointer: alloc.allocate(bytes: pos.count * 4), shape: pos.shape)
+        let scale = 1.0 / Float(color.count)
+        if let xf = xform {
+            ctx.check(dr_antialias_xf_bwd_mse(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f,
+                                              pos.f, Int32(pos.shape[0]), xf.f, tri.i, Int32(tri.shape[0]),
+                                              topologyHash.i, out.f, target.f, scale, dLoss.f, dColor.f, dPos.f,
+                                              work), "antialiasMSE VJP")
+        } else {
+            ctx.check(dr_antialias_bwd_mse(ctx.raw, color.f, Int32(N), Int32(H), Int32(W), Int32(C), rast.f, pos.f,
+                                           Int32(pos.shape[1]), tri.i, Int32(tri.shape[0]), topologyHash.i, out.f,
+                                           target.f, scale, dLoss.f, dColor.f, dPos.f, work), "antialiasMSE VJP")
+        }
+        return (dColor, dPos)
+    }
+
+    /// interpolate followed by `((out - target)^2).mean()` in the same kernel:
+    /// returns the loss (a device scalar), out and outDA.
+    public static func interpolateMSE(_ ctx: Context, _ alloc: DeviceAllocator, _ attr: DeviceTensor,
+                                      rast: DeviceTensor, tri: DeviceTensor, target: DeviceTensor,
+                                      rastDB: DeviceTensor? = nil, diffAttrs: DiffAttrs? = nil)
+        -> (loss: DeviceTensor, out: DeviceTensor, outDA: DeviceTensor) {
+        let N = rast.shape[0], H = rast.shape[1], W = rast.shape[2]
+        let Na = attr.shape.count == 2 ? 1 : attr.shape[0]
+        let V = attr.shape[attr.shape.count - 2], A = attr.shape[attr.shape.count - 1]
+        let (idx, K) = resolve(diffAttrs, A)
+        let out = DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * A * 4), shape: [N, H, W, A])
+        let oda = DeviceTensor(pointer: alloc.allocate(bytes: max(16, N * H * W * 2 * K * 4)), shape: [N, H, W, 2 * K])
+        let loss = DeviceTensor(pointer: alloc.allocate(bytes: 4), shape: [1])
+        let st: dr_status = (idx ?? []).withUnsafeBufferPointer { ib in
+            dr_interpolate_fwd_mse(ctx.raw, attr.f, Int32(Na), Int32(V), Int32(A), rast.f, Int32(N), Int32(H),
+                                   Int32(W), tri.i, Int32(tri.shape[0]), rastDB?.f,
+                                   idx == nil ? nil : ib.baseAddress, Int32(K), out.f, K > 0 ? oda.f : nil,
+                                   target.f, 1.0 / Float(out.count), loss.f)
+        }
+        ctx.check(st, "interpolateMSE")
+        return (loss, out, oda)
+    }
+
+    /// VJP of interpolateMSE: dLoss is the loss's cotangent (a device scalar),
+    /// dOutDA outDA's (nil when it does not reach a loss).
+    public static func interpolateMSEVJP(_ ctx: Context, _ alloc: DeviceAllocator, _ attr: DeviceTensor,
+                                         rast: DeviceTensor, tri: DeviceTensor, rastDB: DeviceTensor?,
+                                         diffAttrs: DiffAttrs?, out: DeviceTensor, target: DeviceTensor,
+                                         dLoss: DeviceTensor, dOutDA: DeviceTensor?)
+        -> (dAttr: DeviceTensor, dRast: DeviceTensor, dRastDB: DeviceTensor?) {
+        let N = rast.shape[0], H = rast.shape[1], W = rast.shape[2]
+        let Na = attr.shape.count == 2 ? 1 : attr.shape[0]
+        let V = attr.shape[attr.shape.count - 2], A = attr.shape[attr.shape.count - 1]
+        let (idx, K0) = resolve(diffAttrs, A)
+        let K = dOutDA == nil ? 0 : K0  // outDA off the loss path: no DA terms
+        let dAttr = DeviceTensor(pointer: alloc.allocate(bytes: attr.count * 4), shape: attr.shape)
+        let dRast = DeviceTensor(pointer: alloc.allocate(bytes: rast.count * 4), shape: rast.shape)
+        let dDB = K > 0 ? DeviceTensor(pointer: alloc.allocate(bytes: rast.count * 4), shape: rast.shape) : nil
+        let st: dr_status = (K > 0 ? (idx ?? []) : []).withUnsafeBufferPointer { ib in
+            dr_interpolate_bwd_mse(ctx.raw, attr.f, Int32(Na), Int32(V), Int32(A), rast.f, Int32(N), Int32(H),
+                                   Int32(W), tri.i, Int32(tri.shape[0]), rastDB?.f,
+                                   (K > 0 && idx != nil) ? ib.baseAddress : nil, Int32(K), out.f, target.f,
+                                   1.0 / Float(out.count), dLoss.f, dOutDA?.f, dAttr.f, dRast.f, dDB?.f)
+        }
+        ctx.check(st, "interpolateMSE VJP")
+        return (dAttr, dRast, dDB)
+    }
+
     /// VJP of mseLoss for the cotangent dLoss (a device scalar; nil means 1).
     public static func mseVJP(_ ctx: Context, _ alloc: DeviceAllocator, pred: DeviceTensor, target: DeviceTensor,
                               dLoss: DeviceTensor? = nil) -> DeviceTensor {
