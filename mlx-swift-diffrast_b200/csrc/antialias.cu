@@ -333,9 +333,10 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
   const bool valid = pix < (int64_t)N * H * W;
   const float* cp = color + pix * C;
   float* o = out + pix * C;
-  // The common case (no candidate, C == 8, aligned) copies the colour row:
-  // load it first so it overlaps the topology gather.
-  const bool vec8 = C == 8 && ((((uintptr_t)color) | ((uintptr_t)out)) & 15) == 0;
+  // The common case (no candidate, C == 8, colour, out and target 16-byte
+  // aligned) copies the colour row: load it first so it overlaps the
+  // topology gather.
+  const bool vec8 = C == 8 && ((((uintptr_t)color) | ((uintptr_t)out) | ((uintptr_t)tgt)) & 15) == 0;
   float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0;
   if (valid && vec8) { c0 = ldg4(cp); c1 = ldg4(cp + 4); }
   unsigned cand = 0;
@@ -371,7 +372,7 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
       }
     }
   }
-  if (part) block_loss_add(l, lscale, part);
+  if (part) warp_loss_add(l, lscale, part);
 }
 
 template <bool XF, bool WORK>
@@ -434,7 +435,7 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
       if (tp) { const float r = acc - __ldg(tp + c); l += r * r; }
     }
   }
-  if (part) block_loss_add(l, lscale, part);
+  if (part) warp_loss_add(l, lscale, part);
 }
 
 template <bool VEC, bool XF>

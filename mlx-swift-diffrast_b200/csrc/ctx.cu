@@ -225,12 +225,14 @@ __global__ void k_mse(const float* __restrict__ p, const float* __restrict__ t, 
   }
 }
 
-// loss = the kLossSlots partial sums of a fused loss, added in slot order.
+// loss = the kLossSlots partial sums of a fused loss (one warp: strided
+// partial sums, then a shuffle reduction).
 __global__ void k_loss_finish(const float* __restrict__ part, float* __restrict__ loss) {
-  if (threadIdx.x != 0) return;
   float s = 0.0f;
-  for (int i = 0; i < kLossSlots; ++i) s += part[i];
-  *loss = s;
+  for (int i = threadIdx.x; i < kLossSlots; i += 32) s += part[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (threadIdx.x == 0) *loss = s;
 }
 
 dr_status loss_begin(dr_ctx* ctx, float** part) {

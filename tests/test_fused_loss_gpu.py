@@ -8,6 +8,8 @@ same inputs:
   MSE VJP's arithmetic)
   atomically accumulated gradients (d_pos, d_attr): <= 1e-4 relative L2
 The loss's cotangent is scaled (0.7) so the device-side d_loss is exercised.
+A target that starts 4 bytes past a 16-byte boundary takes the kernels'
+scalar paths (their float4 loads need 16-byte alignment).
 """
 import numpy as np
 import pytest
@@ -30,9 +32,18 @@ def _leaf(t):
     return t.detach().clone().requires_grad_(True)
 
 
-@pytest.mark.parametrize("xf", [False, True])
-@pytest.mark.parametrize("C", [8, 3])
-def test_antialias_mse_matches_op_then_mse(soup, xf, C):
+def _offset(t):
+    """A contiguous copy of t whose data starts one float past t's alignment."""
+    import torch
+    buf = torch.empty(t.numel() + 1, device=t.device, dtype=t.dtype)
+    v = buf[1:].view(t.shape)
+    v.copy_(t)
+    return v
+
+
+@pytest.mark.parametrize("xf,C,odd_target", [(False, 8, False), (True, 8, False), (False, 3, False),
+                                              (True, 3, False), (False, 8, True), (True, 4, True)])
+def test_antialias_mse_matches_op_then_mse(soup, xf, C, odd_target):
     import torch
 
     import diffrast
@@ -44,6 +55,9 @@ def test_antialias_mse_matches_op_then_mse(soup, xf, C):
     g.manual_seed(7 + C)
     color = torch.rand((3,) + res + (C,), generator=g, device="cuda")
     target = torch.rand((3,) + res + (C,), generator=g, device="cuda")
+    if odd_target:
+        target = _offset(target)
+        assert target.data_ptr() % 16 == 4
     topo = diffrast.antialias_construct_topology_hash(tri)
     grads = []
     for fused in (False, True):
@@ -64,9 +78,10 @@ def test_antialias_mse_matches_op_then_mse(soup, xf, C):
     assert rel_l2(dp1, dp0) < 1e-4 and np.abs(dp0).sum() > 0
 
 
-@pytest.mark.parametrize("diff,da_loss", [(None, False), ("all", False), ("all", True), ([2, 0], True)])
+@pytest.mark.parametrize("diff,da_loss,odd_target", [(None, False, False), ("all", False, False), ("all", True, False),
+                                                     ([2, 0], True, False), ("all", True, True)])
 @pytest.mark.parametrize("shared", [True, False])
-def test_interpolate_mse_matches_op_then_mse(soup, diff, da_loss, shared):
+def test_interpolate_mse_matches_op_then_mse(soup, diff, da_loss, odd_target, shared):
     import torch
 
     import diffrast
@@ -78,6 +93,8 @@ def test_interpolate_mse_matches_op_then_mse(soup, diff, da_loss, shared):
     g.manual_seed(11)
     attr = torch.randn(((V, A) if shared else (3, V, A)), generator=g, device="cuda")
     target = torch.randn((3,) + res + (A,), generator=g, device="cuda")
+    if odd_target:
+        target = _offset(target)
     K = 0 if diff is None else (A if diff == "all" else len(diff))
     w_da = torch.randn((3,) + res + (2 * K,), generator=g, device="cuda") if K else None
     grads = []
