@@ -122,19 +122,31 @@ class ClockSampler:
 
 # --------------------------------------------------- algorithmic bytes
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per pixel of one
-# layer for a kernel, from one ncu --set full capture of the 2-view cfg4 case
-# (2 x 1024^2 pixels per layer; the two-layer raster launch covers both
-# layers).  A full launch's traffic is this times its pixels: every per-pixel
-# stream scales with pixels, and the per-triangle records and tile lists with
-# views, i.e. also with pixels at a fixed resolution.
+# Measured DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of each
+# library kernel in one full-size cfg4 step (32 views x 1024^2 = P4 pixels per
+# layer), summed over the kernel's launches in the step, per pixel.  They come
+# from NCU_CAPTURE: ncu collects these three metrics in one pass, so the
+# capture replays nothing and sees the step's real cache state (the attribute
+# and vertex tables that the interpolate and raster VJPs gather from miss L2
+# once per view, which a smaller capture understates).  Scaled by the pixels
+# of a run with other view counts.
+P4 = 32 * 1024 * 1024
+NCU_CAPTURE = {
+    "commit": "97c2e20",
+    "command": ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum "
+                "--clock-control none -c 200 --csv python -u bench.py --steps 1 --warmup 3 --no-e2e --no-cpu"),
+}
 NCU_DRAM_BYTES_PER_PIXEL = {
-    ("cfg4", "raster_tiles"): (120.786176e6 + 99.920896e6) / (2 * 1024 * 1024),
-    ("cfg4", "interp_fwd"): (151.143424e6 + 152.051968e6) / (2 * 1024 * 1024),
-    ("cfg4", "interp_bwd"): (244.010496e6 + 55.546880e6) / (2 * 1024 * 1024),
-    ("cfg4", "raster_bwd"): (145.191168e6 + 11.467264e6) / (2 * 1024 * 1024),
-    ("cfg4", "aa_fwd"): (121.620224e6 + 61.306368e6) / (2 * 1024 * 1024),
-    ("cfg4", "aa_bwd"): (102.782208e6 + 35.914240e6) / (2 * 1024 * 1024),
+    ("cfg4", "raster_setup"): 1632472064 / P4,
+    ("cfg4", "raster_scatter"): 3432289792 / P4,
+    ("cfg4", "raster_tiles"): 4051083008 / P4,
+    ("cfg4", "interp_fwd"): 11966521344 / P4,  # two launches
+    ("cfg4", "aa_fwd"): 4543445504 / P4,
+    ("cfg4", "aa_fwd_edges"): 1184014080 / P4,
+    ("cfg4", "aa_bwd"): 3781019136 / P4,
+    ("cfg4", "aa_bwd_edges"): 937977344 / P4,
+    ("cfg4", "interp_bwd"): 10366702592 / P4,  # two launches
+    ("cfg4", "raster_bwd"): 3279653632 / P4,  # two launches
 }
 
 
@@ -477,22 +489,27 @@ def main():
         b = algo.get(name, 0) * args.steps
         ach = b / (tot_ms * 1e-3) / 1e9 if (b and tot_ms > 0) else None
         per_px = NCU_DRAM_BYTES_PER_PIXEL.get((cfg, name))
+        # Measured bytes over the same CUDA-event time: the rate the kernel
+        # really drives HBM at (>= the algorithmic rate when it re-reads).
+        nb = per_px * chain.info.pixels * args.steps if per_px else None
+        ncu_gbs = nb / (tot_ms * 1e-3) / 1e9 if (nb and tot_ms > 0) else None
         kernels[name] = {"launches": cnt, "ms_per_launch": tot_ms / cnt,
                          "share": tot_ms / ((ms_eager if graph is not None else ms) * args.steps),
                          "algo_bytes_per_launch": (b / cnt) if b else 0,
                          "gbs": ach, "frac": (ach / peak) if ach else None,
-                         "ncu_dram_bytes_per_launch": per_px * chain.info.pixels if per_px else None}
+                         "ncu_dram_bytes_per_launch": (nb / cnt) if nb else None,
+                         "ncu_gbs": ncu_gbs, "ncu_frac": (ncu_gbs / peak) if ncu_gbs else None}
     dom = next((n for n in kernels if kernels[n]["gbs"]), None)
     roof = None
     if dom:
         kd = kernels[dom]
-        per_px = NCU_DRAM_BYTES_PER_PIXEL.get((cfg, dom))
-        traffic = per_px * chain.info.pixels if per_px else None
         roof = {"kernel": dom, "bound": "hbm", "achieved": kd["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": kd["frac"], "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic,
-                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel on a 2-view "
-                                   "capture of the same workload, per pixel, times this launch's pixels")
-                if per_px else None,
+                "frac": kd["frac"], "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": kd["ncu_dram_bytes_per_launch"],
+                "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel in a full-size "
+                                   f"cfg4 step, build {NCU_CAPTURE['commit']}, per pixel times this launch's pixels "
+                                   f"({NCU_CAPTURE['command']})") if kd["ncu_dram_bytes_per_launch"] else None,
+                "traffic_gbs": kd["ncu_gbs"], "traffic_frac": kd["ncu_frac"],
                 "algo_bytes_per_launch": kd["algo_bytes_per_launch"]}
 
     e2e = None

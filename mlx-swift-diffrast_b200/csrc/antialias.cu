@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
       }
     }
   }
-  if (part) warp_loss_add(l, lscale, part);
+  if (part) block_loss_add(l, lscale, part);
 }
 
 template <bool XF, bool WORK>
@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
       if (tp) { const float r = acc - __ldg(tp + c); l += r * r; }
     }
   }
-  if (part) warp_loss_add(l, lscale, part);
+  if (part) block_loss_add(l, lscale, part);
 }
 
 template <bool VEC, bool XF>

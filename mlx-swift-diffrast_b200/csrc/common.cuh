@@ -258,20 +258,26 @@ __device__ __forceinline__ float sq_diff4(float4 a, float4 b) {
   return x * x + y * y + z * z + w * w;
 }
 
-// The forward's loss is summed per warp and added to one of kLossSlots
-// partial sums (spreading the atomics over many addresses, and no block
-// barrier in the producing kernel); dr::loss_end writes their total to the
-// caller's loss.
-constexpr int kLossSlots = 256;
+// The forward's loss is summed per block and added to one of kLossSlots
+// partial sums (spreading the atomics over several addresses); dr::loss_end
+// writes their total to the caller's loss.
+constexpr int kLossSlots = 32;
 
-// Adds v summed over the warp, times scale, to one of the partial sums.
-// Every lane of the warp must call it.
-__device__ __forceinline__ void warp_loss_add(float v, float scale, float* part) {
+// Adds v summed over the block, times scale, to part[blockIdx.x % kLossSlots].
+// Every thread of the block must call it (it synchronises the block).
+__device__ __forceinline__ void block_loss_add(float v, float scale, float* part) {
+  __shared__ float s_warp[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  if ((threadIdx.x & 31) == 0 && v != 0.0f) {
-    const unsigned w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    atomicAdd(part + (w % kLossSlots), scale * v);
+  if (lane == 0) s_warp[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    float w = lane < nw ? s_warp[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+    if (lane == 0) atomicAdd(part + (blockIdx.x % kLossSlots), scale * w);
   }
 }
 

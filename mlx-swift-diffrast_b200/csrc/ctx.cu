@@ -225,8 +225,8 @@ __global__ void k_mse(const float* __restrict__ p, const float* __restrict__ t, 
   }
 }
 
-// loss = the kLossSlots partial sums of a fused loss (one warp: strided
-// partial sums, then a shuffle reduction).
+// loss = the kLossSlots partial sums of a fused loss (one warp, a shuffle
+// reduction).
 __global__ void k_loss_finish(const float* __restrict__ part, float* __restrict__ loss) {
   float s = 0.0f;
   for (int i = threadIdx.x; i < kLossSlots; i += 32) s += part[i];

@@ -115,7 +115,7 @@ __device__ __forceinline__ void interp_fwd_pixel(const float* __restrict__ attr,
   }
 }
 
-// One thread per pixel; with a fused loss (LOSS) every warp adds lscale * its
+// One thread per pixel; with a fused loss (LOSS) every block adds lscale * its
 // sum of squared differences to a partial sum.  The loss is a separate
 // instance so the plain forward keeps its register count; both are held to
 // four resident blocks per SM (the dependent gathers need the occupancy).
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(256, 4) k_interp_fwd(const float* __restrict__
   if (pix < P)
     interp_fwd_pixel<VEC4, DA, IDX>(attr, attr_shared, V, A, rast, pix, HW, tri, T, rast_db, idx, K, out, out_da,
                                     LOSS ? tgt : nullptr, lsum, err);
-  if (LOSS) warp_loss_add(lsum, lscale, part);
+  if (LOSS) block_loss_add(lsum, lscale, part);
 }
 
 template <bool LOSS>
