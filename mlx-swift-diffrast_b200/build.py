@@ -34,7 +34,7 @@ NVCC_FLAGS = ARCH + [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
     "-I" + INCLUDE, "-I" + CSRC,
 ]
-FMA_SOURCES = {"raster_bwd.cu"}
+FMA_SOURCES = {"raster_bwd.cu", "texture_bwd.cu"}
 
 
 def fmad_flag(src: str) -> str:
