@@ -123,6 +123,33 @@ DR_API dr_status dr_ctx_timing_report(dr_ctx* ctx, char* buf, size_t n);
 DR_API dr_status dr_ctx_set_raster_list_capacity(dr_ctx* ctx, int64_t pairs);
 DR_API dr_status dr_ctx_raster_overflow(dr_ctx* ctx, int64_t* tiles);
 
+/* Tile order (no counterpart in the reference, whose kernels run one thread
+ * per pixel in image order).  Every view of a multi-view batch shows about
+ * the same triangles, so interpolate (which gathers attribute rows by vertex
+ * and, in its VJP, adds into a gradient table of the same shape) sweeps the
+ * whole table once per view; when the table and its gradient do not fit L2,
+ * each view misses on them again.  dr_tile_order writes a processing order of
+ * the batch's 32 x 8 pixel tiles (dr_tile_count(N, H, W) int32 entries, a
+ * permutation of 0 .. count-1, tile = view * tiles per view + tile row *
+ * tiles per row + tile column) grouped by the world region each tile shows:
+ * a few coarse regions, the views in order inside each, tiles that show
+ * nothing last.  The region comes from the triangle the layer `rast`
+ * ([N, H, W, 4]) shows at the tile's centre, through vertex 0 of tri ([T, 3])
+ * in `pos` ([V, 4], one fixed frame for all views: the shared vertices of the
+ * per-view transform mode, or one view's clip-space positions; x/w and y/w
+ * are used).  dr_ctx_set_tile_order makes the interpolate forward and VJP
+ * entry points (the _mse ones included) process batches of exactly
+ * N x H x W pixels tile by tile in `order` (a permutation from dr_tile_order,
+ * which must stay valid and unchanged while it is set); order = NULL restores
+ * image order.  Outputs are the same in either order; gradients summed with
+ * atomics differ only in their summation order, as between any two runs. */
+DR_API int64_t dr_tile_count(int N, int H, int W);
+DR_API dr_status dr_tile_order(dr_ctx* ctx, const float* rast, int N, int H, int W,
+                               const int32_t* tri, int T, const float* pos, int V,
+                               int32_t* order);
+DR_API dr_status dr_ctx_set_tile_order(dr_ctx* ctx, const int32_t* order, int N, int H,
+                                       int W);
+
 /* ---- rasterize (Rasterize.swift:44-144) -------------------------------- */
 
 /* Forward.  Replaces DiffRast.rasterize (Rasterize.swift:44) and its kernels

@@ -54,6 +54,7 @@ enum WsSlot {
   WS_HASH,             // topology hash table
   WS_AA,               // antialias scratch
   WS_LOSS,             // partial sums of a fused loss
+  WS_ORDER,            // tile-order construction (box, bin counts, offsets)
   WS_NUM_SLOTS
 };
 
@@ -78,6 +79,10 @@ struct dr_ctx {
   size_t ev_next = 0;
   long pending_start = -1;
   std::vector<std::pair<const char*, size_t>> trecs;
+  // Tile order of the per-pixel kernels (dr_ctx_set_tile_order) for batches of
+  // exactly order_n x order_h x order_w pixels; nullptr = image order.
+  const int32_t* tile_order = nullptr;
+  int order_n = 0, order_h = 0, order_w = 0;
 };
 
 namespace dr {
@@ -99,6 +104,43 @@ dr_status scan_u32(dr_ctx* ctx, const uint32_t* in, uint32_t* out, int64_t n,
 
 inline unsigned grid_for(int64_t n, int block) {
   return (unsigned)((n + block - 1) / block);
+}
+
+// Pixel order of a per-pixel kernel launched with 256-thread blocks: image
+// order (order == nullptr: pixel = block * 256 + thread), or one
+// kOrderTileW x kOrderTileH tile per block, tile order[block] (tile = view *
+// tiles per view + tile row * tiles per row + tile column; pixels past the
+// image's edge are idle).  Wide tiles keep each block's reads of the per-pixel
+// streams in long contiguous rows.
+constexpr int kOrderTileW = 32, kOrderTileH = 8;
+static_assert(kOrderTileW * kOrderTileH == 256, "one 256-thread block per tile");
+struct PixOrder {
+  const int32_t* order = nullptr;
+  int H = 0, W = 0, ntx = 0, ntiles = 0;  // ntiles: tiles per view
+  int64_t n_tiles = 0;
+};
+
+// The PixOrder and grid of a launch over an N x H x W batch: tiles when the
+// context's tile order was set for exactly these sizes, else image order.
+PixOrder pix_order(const dr_ctx* ctx, int N, int H, int W, unsigned& grid);
+
+__device__ __forceinline__ int64_t pix_of(const PixOrder& o, int64_t P, bool& in) {
+  if (!o.order) {
+    const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    in = pix < P;
+    return pix;
+  }
+  const int tile = __ldg(o.order + blockIdx.x);
+  if (tile < 0 || (int64_t)tile >= o.n_tiles) {  // not an order from dr_tile_order: touch nothing
+    in = false;
+    return 0;
+  }
+  const int n = tile / o.ntiles, t = tile - n * o.ntiles;
+  const int ty = t / o.ntx, tx = t - ty * o.ntx;
+  const int px = tx * kOrderTileW + (int)(threadIdx.x % kOrderTileW);
+  const int py = ty * kOrderTileH + (int)(threadIdx.x / kOrderTileW);
+  in = px < o.W && py < o.H;
+  return ((int64_t)n * o.H + py) * o.W + px;
 }
 
 }  // namespace dr

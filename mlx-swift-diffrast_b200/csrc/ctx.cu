@@ -235,6 +235,22 @@ __global__ void k_loss_finish(const float* __restrict__ part, float* __restrict_
   if (threadIdx.x == 0) *loss = s;
 }
 
+PixOrder pix_order(const dr_ctx* ctx, int N, int H, int W, unsigned& grid) {
+  PixOrder o;
+  if (ctx->tile_order && ctx->order_n == N && ctx->order_h == H && ctx->order_w == W) {
+    o.order = ctx->tile_order;
+    o.H = H;
+    o.W = W;
+    o.ntx = (W + kOrderTileW - 1) / kOrderTileW;
+    o.ntiles = o.ntx * ((H + kOrderTileH - 1) / kOrderTileH);
+    o.n_tiles = (int64_t)N * o.ntiles;
+    grid = (unsigned)o.n_tiles;
+  } else {
+    grid = grid_for((int64_t)N * H * W, 256);
+  }
+  return o;
+}
+
 dr_status loss_begin(dr_ctx* ctx, float** part) {
   float* p = (float*)ws_get(ctx, WS_LOSS, sizeof(float) * kLossSlots);
   if (!p) return DR_ENOMEM;

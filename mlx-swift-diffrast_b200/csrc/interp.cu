@@ -125,10 +125,11 @@ __global__ void __launch_bounds__(256, 4) k_interp_fwd(const float* __restrict__
                              const int32_t* __restrict__ tri, int T,
                              const float4* __restrict__ rast_db, const DiffIdx idx, int K,
                              float* __restrict__ out, float* __restrict__ out_da, const float* __restrict__ tgt,
-                             float lscale, float* __restrict__ part, unsigned* err) {
-  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+                             float lscale, float* __restrict__ part, const PixOrder po, unsigned* err) {
+  bool in;
+  const int64_t pix = pix_of(po, P, in);
   float lsum = 0.0f;
-  if (pix < P)
+  if (in)
     interp_fwd_pixel<VEC4, DA, IDX>(attr, attr_shared, V, A, rast, pix, HW, tri, T, rast_db, idx, K, out, out_da,
                                     LOSS ? tgt : nullptr, lsum, err);
   if (LOSS) block_loss_add(lsum, lscale, part);
@@ -140,9 +141,9 @@ struct InterpFwd {
   static __host__ void launch(unsigned grid, cudaStream_t s, const float* attr, bool attr_shared, int V, int A,
                               const float4* rast, int64_t P, int64_t HW, const int32_t* tri, int T,
                               const float4* rast_db, const DiffIdx& idx, int K, float* out, float* out_da,
-                              const float* tgt, float lscale, float* part, unsigned* err) {
+                              const float* tgt, float lscale, float* part, const PixOrder& po, unsigned* err) {
     k_interp_fwd<VEC4, DA, IDX, LOSS><<<grid, 256, 0, s>>>(attr, attr_shared, V, A, rast, P, HW, tri, T, rast_db, idx,
-                                                           K, out, out_da, tgt, lscale, part, err);
+                                                           K, out, out_da, tgt, lscale, part, po, err);
   }
 };
 
@@ -166,7 +167,8 @@ dr_status interp_fwd(dr_ctx* ctx, const float* attr, int attr_batch, int V, int 
   const int64_t P = (int64_t)N * H * W;
   const bool vec = (A % 4 == 0) && aligned16(attr) && aligned16(out) && aligned16(target);
   const bool use_idx = diff_idx != nullptr;
-  const unsigned grid = grid_for(P, 256);
+  unsigned grid;
+  const PixOrder po = pix_order(ctx, N, H, W, grid);
   const float4* r4 = reinterpret_cast<const float4*>(rast);
   const float4* db4 = reinterpret_cast<const float4*>(rast_db);
   float* part = nullptr;
@@ -180,11 +182,11 @@ dr_status interp_fwd(dr_ctx* ctx, const float* attr, int attr_batch, int V, int 
     if (part)                                                                                                   \
       InterpFwd<true>::launch<VEC4V, DAV, IDXV>(grid, ctx->stream, attr, attr_batch == 1, V, A, r4, P,          \
                                                 (int64_t)H * W, tri, T, db4, idx, K, out, out_da, target,       \
-                                                lscale, part, ctx->d_err);                                      \
+                                                lscale, part, po, ctx->d_err);                                  \
     else                                                                                                        \
       InterpFwd<false>::launch<VEC4V, DAV, IDXV>(grid, ctx->stream, attr, attr_batch == 1, V, A, r4, P,         \
                                                  (int64_t)H * W, tri, T, db4, idx, K, out, out_da, nullptr,     \
-                                                 0.0f, nullptr, ctx->d_err);                                    \
+                                                 0.0f, nullptr, po, ctx->d_err);                                \
   } while (0)
   if (vec) {
     if (K == 0) DR_IF(true, false, false);

@@ -17,10 +17,10 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
                              const float4* __restrict__ rast_db, const DiffIdx idx, int K,
                              const Cot d_out, const float* __restrict__ d_out_da,
                              float* __restrict__ d_attr, float4* __restrict__ d_rast,
-                             float4* __restrict__ d_rast_db, unsigned* err) {
-  const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+                             float4* __restrict__ d_rast_db, const PixOrder po, unsigned* err) {
+  bool in;
+  const int64_t pix = pix_of(po, P, in);
   const int lane = threadIdx.x & 31;
-  const bool in = pix < P;
   float4 r = make_float4(0.f, 0.f, 0.f, -1.f);
   if (in) r = __ldcs(rast + pix);
   int t = (int)r.w - 1;
@@ -174,14 +174,15 @@ dr_status interp_bwd(dr_ctx* ctx, const float* attr, int attr_batch, int V, int 
   const bool vec = (A % 4 == 0) && aligned16(attr) && aligned16(d_out.d) && aligned16(d_out.pred) &&
                    aligned16(d_out.target) && aligned16(d_attr);
   const bool use_idx = diff_idx != nullptr;
-  const unsigned grid = grid_for(P, 256);
+  unsigned grid;
+  const PixOrder po = pix_order(ctx, N, H, W, grid);
   const float4* r4 = reinterpret_cast<const float4*>(rast);
   const float4* db4 = reinterpret_cast<const float4*>(rast_db);
   float4* dr4 = reinterpret_cast<float4*>(d_rast);
   float4* ddb4 = reinterpret_cast<float4*>(d_rast_db);
   DR_TB(ctx);
   DR_INTERP_DISPATCH(k_interp_bwd, attr, attr_batch == 1, V, A, r4, P, (int64_t)H * W, tri, T, db4, idx, K, d_out,
-                     d_out_da, d_attr, dr4, ddb4, ctx->d_err);
+                     d_out_da, d_attr, dr4, ddb4, po, ctx->d_err);
   DR_LAUNCHED(ctx, "interp_bwd");
   return DR_OK;
 }

@@ -4,6 +4,10 @@
 
 #include "common.cuh"
 
+using dr::PixOrder;
+using dr::pix_of;
+using dr::pix_order;
+
 namespace {
 
 struct DiffIdx {

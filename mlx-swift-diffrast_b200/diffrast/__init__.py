@@ -26,9 +26,12 @@ from .ops import (  # noqa: F401
     mse_loss,
     rasterize,
     rasterize_layers,
+    set_tile_order,
     texture,
     texture_construct_mip,
     textureConstructMip,
+    tile_order,
+    tile_order_scope,
 )
 
 __all__ = [
@@ -36,4 +39,5 @@ __all__ = [
     "rasterize", "rasterize_layers", "interpolate", "texture", "texture_construct_mip", "textureConstructMip",
     "antialias_construct_topology_hash", "antialiasConstructTopologyHash", "antialias",
     "mse_loss", "antialias_mse", "interpolate_mse", "launch_count", "sync", "workspace_bytes", "set_raster_list_capacity", "raster_overflow",
+    "tile_order", "set_tile_order", "tile_order_scope",
 ]

@@ -38,6 +38,9 @@ SIGNATURES = {
     "dr_ctx_timing_report": (I, [P, ctypes.c_char_p, ctypes.c_size_t]),
     "dr_ctx_set_raster_list_capacity": (I, [P, I64]),
     "dr_ctx_raster_overflow": (I, [P, ctypes.POINTER(I64)]),
+    "dr_tile_count": (I64, [I, I, I]),
+    "dr_tile_order": (I, [P, P, I, I, I, P, I, P, I, P]),
+    "dr_ctx_set_tile_order": (I, [P, P, I, I, I]),
     "dr_rasterize_fwd": (I, [P, P, I, P, I, P, I, I, I, P, P, P]),
     "dr_rasterize_bwd": (I, [P, P, I, P, I, P, I, I, I, P, P, P, P]),
     "dr_rasterize_layers_fwd": (I, [P, P, I, P, I, P, I, I, I, I, P, P]),

@@ -15,6 +15,7 @@ Two small differences from the reference's host glue, both about avoiding work:
 """
 from __future__ import annotations
 
+import contextlib
 import enum
 from typing import Optional, Sequence, Union
 
@@ -114,6 +115,77 @@ def _ctx(t: torch.Tensor):
     c = L.ctx_for(dev)
     L.lib().dr_ctx_set_stream(c, torch.cuda.current_stream(dev).cuda_stream)
     return c
+
+
+# -------------------------------------------------------------- tile order
+#
+# No counterpart in the reference.  Interpolate gathers attribute rows by
+# vertex and its VJP adds into a gradient table of the same shape; every view
+# of a batch shows about the same triangles, so in image order each view
+# sweeps both tables once, missing L2 on them again when they do not fit it
+# together.  A tile order groups the batch's 32 x 8 tiles by the world region
+# they show (a few regions, the views in order inside each), so one region's
+# slice of the tables stays in L2 while every view passes over it.  Outputs
+# do not depend on the order.
+
+_TILE_ORDERS = {}  # device index -> (order tensor, (N, H, W)) the context holds
+
+
+def tile_order(rast: torch.Tensor, pos: torch.Tensor, tri: torch.Tensor) -> torch.Tensor:
+    """Processing order of rast's [N, H, W] batch of 32 x 8 pixel tiles grouped
+    by the world region each shows (dr_tile_order): int32 [count], a
+    permutation of the tile indices.  pos: [V, 4] vertices in one frame shared
+    by all views (the per-view transform mode's shared vertices, or one view's
+    clip-space positions); tri: [T, 3]."""
+    rast_c = _f32(rast, "rast")
+    pos_c = _f32(pos, "pos")
+    tri_c = _i32(tri, "tri")
+    if rast_c.dim() != 4 or rast_c.shape[3] != 4:
+        raise ValueError(f"tile_order: rast must be [N, H, W, 4] (got {tuple(rast_c.shape)})")
+    if pos_c.dim() != 2 or pos_c.shape[1] != 4:
+        raise ValueError(f"tile_order: pos must be [V, 4] (got {tuple(pos_c.shape)})")
+    N, H, W, _ = rast_c.shape
+    order = torch.empty(int(L.lib().dr_tile_count(N, H, W)), dtype=torch.int32, device=rast_c.device)
+    c = _ctx(rast_c)
+    L.check(L.lib().dr_tile_order(c, _ptr(rast_c), N, H, W, _ptr(tri_c), tri_c.shape[0], _ptr(pos_c),
+                                  pos_c.shape[0], _ptr(order)), c, "tile_order")
+    return order
+
+
+def set_tile_order(order: Optional[torch.Tensor], shape=None, device=None):
+    """Make interpolate (forward and VJP, the _mse forms included) process
+    batches of exactly shape = (N, H, W) pixels tile by tile in `order` (from
+    tile_order); order=None restores image order on `device` (default: the
+    current device).  The tensor is kept alive while it is set."""
+    if order is None:
+        dev = device if device is not None else torch.cuda.current_device()
+        dev = dev.index if isinstance(dev, torch.device) else int(dev)
+        c = L.ctx_for(dev)
+        L.check(L.lib().dr_ctx_set_tile_order(c, None, 0, 0, 0), c, "set_tile_order")
+        _TILE_ORDERS.pop(dev, None)
+        return
+    if shape is None or len(shape) != 3:
+        raise ValueError("set_tile_order: shape must be (N, H, W)")
+    N, H, W = (int(x) for x in shape)
+    if order.dtype != torch.int32 or not order.is_cuda or not order.is_contiguous():
+        raise ValueError("set_tile_order: order must be a contiguous int32 CUDA tensor from tile_order")
+    if order.numel() != int(L.lib().dr_tile_count(N, H, W)):
+        raise ValueError(f"set_tile_order: order has {order.numel()} entries, the batch has "
+                         f"{int(L.lib().dr_tile_count(N, H, W))} tiles")
+    c = _ctx(order)
+    L.check(L.lib().dr_ctx_set_tile_order(c, _ptr(order), N, H, W), c, "set_tile_order")
+    _TILE_ORDERS[order.device.index] = (order, (N, H, W))
+
+
+@contextlib.contextmanager
+def tile_order_scope(order: torch.Tensor, shape):
+    """set_tile_order(order, shape) for the body of a with-statement (the
+    backward passes run inside it too), image order again after it."""
+    set_tile_order(order, shape)
+    try:
+        yield
+    finally:
+        set_tile_order(None, device=order.device)
 
 
 # --------------------------------------------------------------- rasterize

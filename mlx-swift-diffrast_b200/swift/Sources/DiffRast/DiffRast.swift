@@ -56,6 +56,12 @@ public enum DiffRast {
             check(dr_ctx_raster_overflow(raw, &n), "rasterOverflow")
             return n
         }
+        /// Interpolate (forward and VJP) walks [N, H, W] batches tile by tile in
+        /// `order` (from `DiffRast.tileOrder`); nil restores image order.  The
+        /// buffer must stay valid and unchanged while it is set.
+        public func setTileOrder(_ order: DeviceTensor?, n: Int = 0, h: Int = 0, w: Int = 0) {
+            check(dr_ctx_set_tile_order(raw, order?.i, Int32(n), Int32(h), Int32(w)), "setTileOrder")
+        }
         /// Synchronizes the stream; crashes (as the reference's preconditions)
         /// if a kernel met an out-of-range index since the last sync.
         public func sync() { check(dr_ctx_sync(raw), "sync") }
@@ -105,6 +111,19 @@ public enum DiffRast {
             precondition(!idx.isEmpty, "interpolate: diffAttrs.indices must be non-empty")
             return (idx, idx.count)
         }
+    }
+
+    /// Processing order of rast's 32 x 8 tiles grouped by the world region each
+    /// shows (positions `pos` [V, 4] in one frame shared by all views), for
+    /// `Context.setTileOrder`: Int32 [dr_tile_count(N, H, W)].
+    public static func tileOrder(_ ctx: Context, _ alloc: DeviceAllocator, rast: DeviceTensor, pos: DeviceTensor,
+                                 tri: DeviceTensor) -> DeviceTensor {
+        let N = rast.shape[0], H = rast.shape[1], W = rast.shape[2]
+        let n = Int(dr_tile_count(Int32(N), Int32(H), Int32(W)))
+        let order = DeviceTensor(pointer: alloc.allocate(bytes: max(16, n * 4)), shape: [n])
+        ctx.check(dr_tile_order(ctx.raw, rast.f, Int32(N), Int32(H), Int32(W), tri.i, Int32(tri.shape[0]), pos.f,
+                                Int32(pos.shape[0]), order.i), "tileOrder")
+        return order
     }
 
     public static func interpolate(_ ctx: Context, _ alloc: DeviceAllocator, _ attr: DeviceTensor,

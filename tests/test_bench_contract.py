@@ -66,7 +66,8 @@ def _launched_names():
     import glob
     import re
     names = set()
-    for f in glob.glob(os.path.join(ROOT, "mlx-swift-diffrast_b200", "csrc", "*.cu")):
+    csrc = os.path.join(ROOT, "mlx-swift-diffrast_b200", "csrc")
+    for f in glob.glob(os.path.join(csrc, "*.cu")) + glob.glob(os.path.join(csrc, "*.cuh")):
         names |= set(re.findall(r'DR_LAUNCHED\(ctx, "([a-z_0-9]+)"\)', open(f).read()))
     return names
 
