@@ -399,8 +399,20 @@ def main():
     sync = D.GradSync(chain.shared_params())
     chain.grad_sync = sync
 
+    # With several ranks, the time the stream waits at the end of a step for
+    # the gradient all-reduces still in flight (CUDA events around the wait,
+    # recorded during the timed steps).
+    exposed = {"on": False, "events": []}
+
     def allreduce():
-        sync.finish()
+        if exposed["on"]:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            sync.finish()
+            b.record()
+            exposed["events"].append((a, b))
+        else:
+            sync.finish()
 
     def one_step():
         chain.zero_grad()
@@ -473,8 +485,14 @@ def main():
         launches = graph_launches * args.steps
         ms_eager, _, report, _ = timed(one_step, True)
     else:
+        exposed["on"] = ws > 1
         ms, launches, report, loss = timed(one_step, True)
+        exposed["on"] = False
     clk = clocks.stop()
+    exposed_ms = None
+    if exposed["events"]:
+        exposed_ms = D.max_over_ranks(sum(a.elapsed_time(b) for a, b in exposed["events"]) / len(exposed["events"]),
+                                      device=dev)
     ms_max = D.max_over_ranks(ms, device=dev)
     diffrast.sync(local)
     overflow_tiles = diffrast.raster_overflow(local) if graph is not None else None
@@ -536,6 +554,7 @@ def main():
                                   "working set smaller than L2 and not flushed (a small configuration)")},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "gpu_launches_per_step": launches / args.steps, "clocks": clk, "kernels": kernels,
+                "allreduce_exposed_ms": exposed_ms,
                 "loss": float(loss.detach())}
         if graph is not None:
             line["execution"] = {"cuda_graph": True, "list_capacity": args.list_capacity,
