@@ -536,16 +536,28 @@ __device__ __forceinline__ void aa_dcolor(const Cot& cot, float gl, float* __res
 // pixel's d_color from its own and its neighbours' recorded betas and appends
 // pixels with active directions to a list as (pixel << 8 | record code);
 // k_aa_bwd_edges replays those edges (a grid-stride pass, full occupancy)
-// for the d_pos atomics.
-__global__ void __launch_bounds__(256) k_aa_bwd_gather(int N, int H, int W, int C,
+// for the d_pos atomics.  The gather is a stream of independent loads held to
+// five resident blocks per SM (48 registers) for more loads in flight.
+__global__ void __launch_bounds__(256, 5) k_aa_bwd_gather(int N, int H, int W, int C,
                                                        const Cot cot, float* __restrict__ d_color,
                                                        const float4* __restrict__ work_beta,
                                                        const uint8_t* __restrict__ work_code, const PixList L) {
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = pix < (int64_t)N * H * W;
+  // C == 8 with 16-byte aligned streams: the pixel's own cotangent is loaded
+  // together with its record, ahead of the neighbours' betas, so all of the
+  // pixel's loads are in flight at once (the same arithmetic as aa_dcolor).
+  const bool vec8 = C == 8 && ((((uintptr_t)cot.d) | ((uintptr_t)cot.pred) | ((uintptr_t)cot.target) |
+                                ((uintptr_t)d_color)) & 15) == 0;
   unsigned code = 0;
   if (valid) {
     const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    const float gl = cot_g(cot);
+    float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
+    if (vec8) {
+      g0 = cot_at4<true>(cot, gl, pix * 8);
+      g1 = cot_at4<true>(cot, gl, pix * 8 + 4);
+    }
     code = __ldg(work_code + pix);
     const float4 b4 = __ldg(work_beta + pix);
     // The same sum the search path forms: 0 + the active betas in direction order.
@@ -563,7 +575,22 @@ __global__ void __launch_bounds__(256) k_aa_bwd_gather(int N, int H, int W, int 
       const float b = __ldg(reinterpret_cast<const float*>(work_beta + p) + d);
       if (b > 0.0f) { nbeta[d] = b; nsrc[d] = p; }
     }
-    aa_dcolor(cot, cot_g(cot), d_color, C, pix, keep, nbeta, nsrc);
+    if (vec8) {
+      float4 v0 = make_float4(g0.x * keep, g0.y * keep, g0.z * keep, g0.w * keep);
+      float4 v1 = make_float4(g1.x * keep, g1.y * keep, g1.z * keep, g1.w * keep);
+#pragma unroll
+      for (int d = 0; d < 4; ++d)
+        if (nsrc[d] >= 0) {
+          const float4 n0 = cot_at4(cot, gl, nsrc[d] * 8), n1 = cot_at4(cot, gl, nsrc[d] * 8 + 4);
+          const float b = nbeta[d];
+          v0.x += n0.x * b; v0.y += n0.y * b; v0.z += n0.z * b; v0.w += n0.w * b;
+          v1.x += n1.x * b; v1.y += n1.y * b; v1.z += n1.z * b; v1.w += n1.w * b;
+        }
+      stcs4(d_color + pix * 8, v0);
+      stcs4(d_color + pix * 8 + 4, v1);
+    } else {
+      aa_dcolor(cot, gl, d_color, C, pix, keep, nbeta, nsrc);
+    }
   }
   list_append(L, code != 0u, ((unsigned long long)pix << 8) | code);
 }
