@@ -180,11 +180,16 @@ __device__ __forceinline__ bool setup_one(const float* __restrict__ pos, const f
 // counts their tiles in a shared-memory histogram of the view's tiles, then
 // writes the histogram to cnt[(n*ntiles + tile)*cpv + c].  The exclusive scan
 // of cnt (tile-major, chunk-minor) gives every (tile, chunk) its list segment,
-// so neither this kernel nor the scatter issues a global atomic.
+// so neither this kernel nor the scatter issues a global atomic.  Each
+// triangle's pixel rectangle also goes to box[n*T + t] (the record's last two
+// words, kInvalidBox for a record that covers nothing): the scatter reads
+// those 8 bytes instead of a 32-byte sector of the record.
+constexpr unsigned kInvalidBox = 0xFFFFFFFFu;
+
 __global__ void __launch_bounds__(256)
 k_raster_setup_binned(const float* __restrict__ pos, const float* __restrict__ xform, int V,
                       const int32_t* __restrict__ tri, int T, const int32_t* __restrict__ ranges, int H, int W,
-                      int ntx, int nty, int chunk, int cpv, float4* __restrict__ rec,
+                      int ntx, int nty, int chunk, int cpv, float4* __restrict__ rec, uint2* __restrict__ box,
                       uint32_t* __restrict__ cnt, unsigned* err) {
   extern __shared__ uint32_t s_hist[];
   const int c = blockIdx.x, n = blockIdx.y;
@@ -194,8 +199,12 @@ k_raster_setup_binned(const float* __restrict__ pos, const float* __restrict__ x
   const int t0 = c * chunk, t1 = min(T, t0 + chunk);
   for (int t = t0 + (int)threadIdx.x; t < t1; t += blockDim.x) {
     int x0, x1, y0, y1;
-    if (!setup_one(pos, xform, V, tri, T, ranges, H, W, n, t, rec + 3 * ((int64_t)n * T + t), x0, x1, y0, y1, err))
+    if (!setup_one(pos, xform, V, tri, T, ranges, H, W, n, t, rec + 3 * ((int64_t)n * T + t), x0, x1, y0, y1,
+                   err)) {
+      box[(int64_t)n * T + t] = make_uint2(kInvalidBox, kInvalidBox);
       continue;
+    }
+    box[(int64_t)n * T + t] = make_uint2((unsigned)x0 | ((unsigned)x1 << 16), (unsigned)y0 | ((unsigned)y1 << 16));
     for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
       for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) atomicAdd(&s_hist[ty * ntx + tx], 1u);
   }
@@ -204,41 +213,51 @@ k_raster_setup_binned(const float* __restrict__ pos, const float* __restrict__ x
   for (int i = threadIdx.x; i < ntiles; i += blockDim.x) col[(int64_t)i * cpv] = s_hist[i];
 }
 
-// Binned scatter: the same CTA-to-chunk map as the setup; each (tile, chunk)
-// segment start comes from the scan, and slots within it from shared atomics.
-__global__ void __launch_bounds__(256)
-k_raster_scatter_binned(const float4* __restrict__ rec, int T, int ntx, int nty, int chunk, int cpv,
+// Binned scatter: CTA k walks the (view, chunk) pairs [k*per, (k+1)*per) of
+// the setup's map (view-major) one after the other; each pair's (tile, chunk)
+// segment starts come from the scan, and slots within them from shared
+// atomics.  One wave of large CTAs keeps few pairs in flight: every pair
+// appends to all of its view's tiles at once, and the partly written list
+// sectors of all pairs in flight must stay in L2 until they fill (with one
+// pair per 256-thread CTA they did not: about 1 GB of write-backs re-read).
+constexpr int kScatterBlock = 1024;
+
+__global__ void __launch_bounds__(kScatterBlock)
+k_raster_scatter_binned(const uint2* __restrict__ box, int N, int T, int ntx, int nty, int chunk, int cpv, int per,
                         const uint32_t* __restrict__ off, int32_t* __restrict__ list, uint32_t cap) {
   extern __shared__ uint32_t s_base[];
-  const int c = blockIdx.x, n = blockIdx.y;
   const int ntiles = ntx * nty;
-  const uint32_t* col = off + (int64_t)n * ntiles * cpv + c;
-  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) s_base[i] = __ldg(col + (int64_t)i * cpv);
-  __syncthreads();
-  const int t0 = c * chunk, t1 = min(T, t0 + chunk);
-  // Four records per thread per round, loaded before any is used, so four
-  // independent loads are in flight (the loop is otherwise one load latency
-  // per triangle).
-  constexpr int R = 4;
-  const float4* rv = rec + 3 * (int64_t)n * T + 2;
-  for (int tb = t0 + (int)threadIdx.x; tb < t1; tb += R * blockDim.x) {
-    float4 r2[R];
+  const int64_t pairs = (int64_t)N * cpv;
+  for (int64_t q = (int64_t)blockIdx.x * per, qe = min(pairs, q + per); q < qe; ++q) {
+    const int n = (int)(q / cpv), c = (int)(q - (int64_t)n * cpv);
+    const uint32_t* col = off + (int64_t)n * ntiles * cpv + c;
+    __syncthreads();  // the previous pair's appends are done with s_base
+    for (int i = threadIdx.x; i < ntiles; i += blockDim.x) s_base[i] = __ldg(col + (int64_t)i * cpv);
+    __syncthreads();
+    const int t0 = c * chunk, t1 = min(T, t0 + chunk);
+    // Four rectangles per thread per round, loaded before any is used, so
+    // four independent loads are in flight.
+    constexpr int R = 4;
+    const uint2* bv = box + (int64_t)n * T;
+    for (int tb = t0 + (int)threadIdx.x; tb < t1; tb += R * blockDim.x) {
+      uint2 r2[R];
 #pragma unroll
-    for (int k = 0; k < R; ++k) {
-      const int t = tb + k * (int)blockDim.x;
-      r2[k] = t < t1 ? __ldg(rv + 3 * (int64_t)t) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+      for (int k = 0; k < R; ++k) {
+        const int t = tb + k * (int)blockDim.x;
+        r2[k] = t < t1 ? __ldcs(bv + t) : make_uint2(kInvalidBox, kInvalidBox);
+      }
 #pragma unroll
-    for (int k = 0; k < R; ++k) {
-      if (r2[k].y == 0.0f) continue;  // area == 0: invalid (or past the chunk)
-      const int t = tb + k * (int)blockDim.x;
-      const unsigned xs = __float_as_uint(r2[k].z), ys = __float_as_uint(r2[k].w);
-      const int x0 = (int)(xs & 0xffffu), x1 = (int)(xs >> 16), y0 = (int)(ys & 0xffffu), y1 = (int)(ys >> 16);
-      for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
-        for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) {
-          const uint32_t slot = atomicAdd(&s_base[ty * ntx + tx], 1u);
-          if (slot < cap) list[slot] = t;  // past a fixed capacity: the tile scans instead
-        }
+      for (int k = 0; k < R; ++k) {
+        if (r2[k].x == kInvalidBox) continue;  // covers no pixel (or past the chunk)
+        const int t = tb + k * (int)blockDim.x;
+        const unsigned xs = r2[k].x, ys = r2[k].y;
+        const int x0 = (int)(xs & 0xffffu), x1 = (int)(xs >> 16), y0 = (int)(ys & 0xffffu), y1 = (int)(ys >> 16);
+        for (int ty = y0 / TILE; ty <= y1 / TILE; ++ty)
+          for (int tx = x0 / TILE; tx <= x1 / TILE; ++tx) {
+            const uint32_t slot = atomicAdd(&s_base[ty * ntx + tx], 1u);
+            if (slot < cap) list[slot] = t;  // past a fixed capacity: the tile scans instead
+          }
+      }
     }
   }
 }
@@ -697,7 +716,9 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
   const int64_t ncnt = ntiles_all * cpv;
   DR_REQUIRE(ctx, ncnt < (1ll << 31), "rasterize: too many tile segments");
 
-  float4* rec = (float4*)ws_get(ctx, WS_RASTER_REC, sizeof(float4) * 3 * (size_t)(NT > 0 ? NT : 1));
+  // Records (48 B) then, binned, the pixel rectangles (8 B) of every (view, triangle).
+  float4* rec = (float4*)ws_get(ctx, WS_RASTER_REC, (sizeof(float4) * 3 + sizeof(uint2)) * (size_t)(NT > 0 ? NT : 1));
+  uint2* box = rec ? reinterpret_cast<uint2*>(rec + 3 * (NT > 0 ? NT : 1)) : nullptr;
   // cnt[ncnt] | off[ncnt + 1] | cur[ntiles_all] (unbinned only) | total
   uint32_t* tc = (uint32_t*)ws_get(ctx, WS_TILE_COUNT, sizeof(uint32_t) * (size_t)(2 * ncnt + ntiles_all + 4));
   if (!rec || !tc) return DR_ENOMEM;
@@ -716,7 +737,8 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
     }
     DR_TB(ctx);
     k_raster_setup_binned<<<dim3(cpv, N), 256, hist_bytes, ctx->stream>>>(pos, xform, V, tri, T, ranges, H, W, ntx,
-                                                                         nty, chunk, cpv, rec, cnt, ctx->d_err);
+                                                                         nty, chunk, cpv, rec, box, cnt,
+                                                                         ctx->d_err);
     DR_LAUNCHED(ctx, "raster_setup");
   } else {
     DR_CUDA(ctx, cudaMemsetAsync(cnt, 0, sizeof(uint32_t) * (size_t)ncnt, ctx->stream), "rasterize memset");
@@ -757,10 +779,17 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
   if (!list) return DR_ENOMEM;
   if (launch_scatter) {
     DR_TB(ctx);
-    if (binned)
-      k_raster_scatter_binned<<<dim3(cpv, N), 256, hist_bytes, ctx->stream>>>(rec, T, ntx, nty, chunk, cpv, off,
-                                                                              list, cap);
-    else
+    if (binned) {
+      // One wave: as many pairs per CTA as fill the resident CTAs once.
+      const int per_sm = (int)std::max<size_t>(1, std::min<size_t>(2048 / kScatterBlock,
+                                                                   (227 * 1024) / (hist_bytes + 1024)));
+      const int64_t pairs = (int64_t)N * cpv;
+      const int64_t slots = (int64_t)per_sm * ctx->num_sms;
+      const int per = (int)((pairs + slots - 1) / slots);
+      const unsigned grid = (unsigned)((pairs + per - 1) / per);
+      k_raster_scatter_binned<<<grid, kScatterBlock, hist_bytes, ctx->stream>>>(box, N, T, ntx, nty, chunk, cpv,
+                                                                                per, off, list, cap);
+    } else
       k_raster_scatter<<<grid_for(NT, 256), 256, 0, ctx->stream>>>(rec, N, T, ntx, nty, cur, list, cap);
     DR_LAUNCHED(ctx, "raster_scatter");
   }
