@@ -445,12 +445,13 @@ __device__ __forceinline__ int stage_spans(const float4& f0, const float4& f1, f
     const float hi = fminf(__fmaf_rn(hb0, y, ha0), __fmaf_rn(hb1, y, ha1));
     const float cl = fmaxf(ceilf(__fmaf_rn(lo, half, off)), clo_min);
     const float ch = fminf(floorf(__fmaf_rn(hi, half, off)), chi_max);
-    if (cl <= ch) {
-      const int c0 = (int)cl - tx0, c1 = (int)ch - tx0;
-      span[ly] = (unsigned char)(c0 | (c1 << 4));
-      n += c1 - c0 + 1;
-      ++rows;
-    }
+    // Branch-free: an empty row keeps the empty code 0x0F (first column 15,
+    // last 0).  cl and ch lie in [clo_min, chi_max] whenever cl <= ch.
+    const bool on = cl <= ch;
+    const int c0 = (int)cl - tx0, c1 = (int)ch - tx0;
+    span[ly] = on ? (unsigned char)(c0 | (c1 << 4)) : (unsigned char)0x0F;
+    n += on ? c1 - c0 + 1 : 0;
+    rows += on ? 1 : 0;
   }
   n_rows = rows;
   return n;
@@ -541,25 +542,27 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
     const float e1 = FS(FM(dx2, dy0), FM(dx0, dy2));
     const float e2 = FS(FM(dx0, dy1), FM(dx1, dy0));
     const float area = f2.y;
-    if (FM(e0, area) < 0.0f || FM(e1, area) < 0.0f || FM(e2, area) < 0.0f) return false;
+    // Straight-line code: nearly every tested item covers its pixel (the
+    // spans leave few misses), so the barycentrics and depth are computed
+    // for all and the conditions combined into one predicate.
     const float bw = FM(e0, f2.z), u = FM(e1, f2.z), v = FM(e2, f2.z);
     const float z = FA(FA(FM(bw, f0.z), FM(u, f1.y)), FM(v, f2.x));
     // A NaN depth is never a fragment.  The reference stores one (every
     // comparison it makes is false) and lets the next candidate in its bin
     // order replace it; rejecting it keeps the winner independent of order,
     // and the oracle applies the same rule.
-    if (!(z >= -1.0f && z <= 1.0f)) return false;
     p = ly * TILE + lx;
-    if (PEEL && z <= s_peel[p]) return false;
+    bool ok = !(FM(e0, area) < 0.0f) & !(FM(e1, area) < 0.0f) & !(FM(e2, area) < 0.0f) & (z >= -1.0f) &
+              (z <= 1.0f);
+    if (PEEL) ok &= !(z <= s_peel[p]);
     key = pack_key(z, __float_as_int(f2.w));
-    return TWO ? key < s_k1[p] : key < s_k0[p];
+    return ok & (TWO ? key < s_k1[p] : key < s_k0[p]);
   };
+  // The test's read of the key is the filter; the atomics are correct for
+  // any key, so a key lowered by another thread in between costs nothing.
   auto fold = [&](unsigned long long key, int p) {
-    if (TWO) {
-      if (key < s_k1[p]) fold_two(&s_k0[p], &s_k1[p], key);
-    } else if (key < s_k0[p]) {
-      atomicMin(&s_k0[p], key);
-    }
+    if (TWO) fold_two(&s_k0[p], &s_k1[p], key);
+    else atomicMin(&s_k0[p], key);
   };
   for (uint32_t base = 0; base < cnt; base += TILE_PIX) {
     __syncthreads();  // the previous batch's readers are done with the stage
@@ -643,17 +646,17 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
         // s_start[s0 + 1 .. s0 + 32] that are <= b0 + lane.
         const int d = s_start[s0 + 1 + lane] - b0;
         const unsigned M = __reduce_or_sync(0xffffffffu, d < 32 ? (1u << d) : 0u);
-        const int s = s0 + __popc(M & (0xffffffffu >> (31 - lane)));
+        // Lanes past the warp's range (last step only) get a valid span and
+        // an in-tile column, test without effect and fold nothing: no branch.
+        const int s = min(s0 + __popc(M & (0xffffffffu >> (31 - lane))), n_spans - 1);
         s0 = __shfl_sync(0xffffffffu, s, 31);
         const int item = b0 + lane;
-        if (item < whi) {
-          const unsigned info = s_info[s];
-          const int j = (int)(info & 255u), ly = (int)((info >> 8) & 15u);
-          const int lx = (int)(info >> 12) + (item - s_start[s]);
-          unsigned long long key = 0;
-          int p = 0;
-          if (test(s_rec[3 * j], s_rec[3 * j + 1], s_rec[3 * j + 2], lx, ly, key, p)) fold(key, p);
-        }
+        const unsigned info = s_info[s];
+        const int j = (int)(info & 255u), ly = (int)((info >> 8) & 15u);
+        const int lx = ((int)(info >> 12) + (item - s_start[s])) & (TILE - 1);
+        unsigned long long key = 0;
+        int p = 0;
+        if (test(s_rec[3 * j], s_rec[3 * j + 1], s_rec[3 * j + 2], lx, ly, key, p) & (item < whi)) fold(key, p);
       }
     }
   }
