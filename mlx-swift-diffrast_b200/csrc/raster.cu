@@ -471,7 +471,11 @@ __device__ __forceinline__ int stage_spans(const float4& f0, const float4& f1, f
 // balanced to within one step per warp whatever the triangle sizes.
 // MODE: 0 = one layer, 1 = one layer peeled at `peel`, 2 = layers 0 and 1 at once.
 constexpr int WARPS = TILE_PIX / 32;
-constexpr int MAX_SPANS = TILE_PIX * TILE;  // every staged candidate non-empty on every row
+// A batch stages at most 255 candidates, so its items (at most 255 * 256)
+// and span starts fit 16 bits with 0xFFFF left free as the end sentinel.
+constexpr int BATCH = TILE_PIX - 1;
+constexpr int MAX_SPANS = BATCH * TILE;  // every staged candidate non-empty on every row
+constexpr unsigned short kNoStart = 0xFFFF;
 
 // CAPPED: the list buffer holds `cap` entries (fixed capacity, no readback);
 // a tile whose list runs past it stages every triangle of its view instead,
@@ -492,8 +496,10 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
   __shared__ float s_ndcx[TILE], s_ndcy[TILE];
   __shared__ float4 s_rec[TILE_PIX * 3];        // staged records, by staging thread
   __shared__ uint4 s_rowspan[TILE_PIX];         // per staging thread: one span byte per tile row
-  __shared__ int s_start[MAX_SPANS + 33];       // first item of each span (+ 33 entries past the last)
-  __shared__ unsigned short s_info[MAX_SPANS];  // staging thread | row << 8 | first column << 12
+  __shared__ unsigned short s_start[MAX_SPANS + 33];  // first item of each span (+ 33 entries past the last)
+  // Staging thread | row << 8 | (first column - first item) << 12 (signed):
+  // an item's column is its index plus the high bits, with no second load.
+  __shared__ int s_info[MAX_SPANS];
   __shared__ int s_wsum[WARPS];
 
   const int ntiles = ntx * nty;
@@ -564,12 +570,12 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
     if (TWO) fold_two(&s_k0[p], &s_k1[p], key);
     else atomicMin(&s_k0[p], key);
   };
-  for (uint32_t base = 0; base < cnt; base += TILE_PIX) {
+  for (uint32_t base = 0; base < cnt; base += BATCH) {
     __syncthreads();  // the previous batch's readers are done with the stage
     const uint32_t i = base + tid;
     int n_items = 0, n_rows = 0, ly0 = 0, ly1 = -1;
     unsigned char* span = reinterpret_cast<unsigned char*>(&s_rowspan[tid]);
-    if (i < cnt) {
+    if (tid < BATCH && i < cnt) {
       const int t = scan_all ? (int)i : __ldg(list + begin + i);
       const float4 a = __ldg(rec + 3 * (rec_view + t) + 0);
       const float4 bb = __ldg(rec + 3 * (rec_view + t) + 1);
@@ -592,7 +598,7 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
       s_rec[3 * tid + 2] = make_float4(c.x, c.y, inv_area, __int_as_float(t));
     }
     // Block exclusive scan of (pixels, non-empty rows), packed: a batch holds
-    // at most 256 * 256 pixels (17 bits) and 256 * 16 rows (13 bits).
+    // at most 255 * 256 pixels (17 bits) and 255 * 16 rows (13 bits).
     const int mine = n_items | (n_rows << 17);
     int incl = mine;
 #pragma unroll
@@ -619,14 +625,14 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
         const unsigned sp = span[ly];
         const int c0 = (int)(sp & 15u), c1 = (int)(sp >> 4);
         if (c1 >= c0) {
-          s_start[slot] = item;
-          s_info[slot] = (unsigned short)(tid | (ly << 8) | (c0 << 12));
+          s_start[slot] = (unsigned short)item;
+          s_info[slot] = tid | (ly << 8) | (int)((unsigned)(c0 - item) << 12);
           ++slot;
           item += c1 - c0 + 1;
         }
       }
     }
-    if (tid < 33) s_start[n_spans + tid] = INT_MAX;  // no start past the last span
+    if (tid < 33) s_start[n_spans + tid] = kNoStart;  // no start past the last span
     __syncthreads();
     // Warp w tests items [wlo, whi), 32 consecutive items per step.
     const int wlo = (int)(((long long)warp * n_total) / WARPS);
@@ -644,16 +650,16 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
         // of them (one per later item of the step) can fall inside the step:
         // the span of item b0 + lane is s0 plus the number of starts among
         // s_start[s0 + 1 .. s0 + 32] that are <= b0 + lane.
-        const int d = s_start[s0 + 1 + lane] - b0;
+        const int d = (int)s_start[s0 + 1 + lane] - b0;
         const unsigned M = __reduce_or_sync(0xffffffffu, d < 32 ? (1u << d) : 0u);
         // Lanes past the warp's range (last step only) get a valid span and
         // an in-tile column, test without effect and fold nothing: no branch.
         const int s = min(s0 + __popc(M & (0xffffffffu >> (31 - lane))), n_spans - 1);
         s0 = __shfl_sync(0xffffffffu, s, 31);
         const int item = b0 + lane;
-        const unsigned info = s_info[s];
-        const int j = (int)(info & 255u), ly = (int)((info >> 8) & 15u);
-        const int lx = ((int)(info >> 12) + (item - s_start[s])) & (TILE - 1);
+        const int info = s_info[s];
+        const int j = info & 255, ly = (info >> 8) & 15;
+        const int lx = (item + (info >> 12)) & (TILE - 1);
         unsigned long long key = 0;
         int p = 0;
         if (test(s_rec[3 * j], s_rec[3 * j + 1], s_rec[3 * j + 2], lx, ly, key, p) & (item < whi)) fold(key, p);
