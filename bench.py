@@ -126,27 +126,27 @@ class ClockSampler:
 # library kernel in one full-size cfg4 step (32 views x 1024^2 = P4 pixels per
 # layer), summed over the kernel's launches in the step, per pixel.  They come
 # from NCU_CAPTURE: ncu collects these three metrics in one pass, so the
-# capture replays nothing and sees the step's real cache state (the attribute
-# and vertex tables that the interpolate and raster VJPs gather from miss L2
-# once per view, which a smaller capture understates).  Scaled by the pixels
-# of a run with other view counts.
+# capture replays nothing and sees the step's real cache state (tables that
+# a kernel gathers from and that miss L2 once per view, such as the raster
+# VJP's vertex rows, are understated by a smaller capture).  Scaled by the
+# pixels of a run with other view counts.
 P4 = 32 * 1024 * 1024
 NCU_CAPTURE = {
-    "commit": "97c2e20",
+    "commit": "cf26099",
     "command": ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum "
                 "--clock-control none -c 200 --csv python -u bench.py --steps 1 --warmup 3 --no-e2e --no-cpu"),
 }
 NCU_DRAM_BYTES_PER_PIXEL = {
-    ("cfg4", "raster_setup"): 1632472064 / P4,
-    ("cfg4", "raster_scatter"): 3432289792 / P4,
-    ("cfg4", "raster_tiles"): 4051083008 / P4,
-    ("cfg4", "interp_fwd"): 11966521344 / P4,  # two launches
-    ("cfg4", "aa_fwd"): 4543445504 / P4,
-    ("cfg4", "aa_fwd_edges"): 1184014080 / P4,
-    ("cfg4", "aa_bwd"): 3781019136 / P4,
-    ("cfg4", "aa_bwd_edges"): 937977344 / P4,
-    ("cfg4", "interp_bwd"): 10366702592 / P4,  # two launches
-    ("cfg4", "raster_bwd"): 3279653632 / P4,  # two launches
+    ("cfg4", "raster_setup"): 1900341504 / P4,
+    ("cfg4", "raster_scatter"): 1349818624 / P4,
+    ("cfg4", "raster_tiles"): 4061209856 / P4,
+    ("cfg4", "interp_fwd"): 10010063616 / P4,  # two launches
+    ("cfg4", "aa_fwd"): 4542756864 / P4,
+    ("cfg4", "aa_fwd_edges"): 1187073536 / P4,
+    ("cfg4", "aa_bwd"): 4026920704 / P4,
+    ("cfg4", "aa_bwd_edges"): 936102656 / P4,
+    ("cfg4", "interp_bwd"): 6096521984 / P4,  # two launches
+    ("cfg4", "raster_bwd"): 3296983296 / P4,  # two launches
 }
 
 
