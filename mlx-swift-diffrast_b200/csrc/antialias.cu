@@ -384,28 +384,70 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
                                                       float4* __restrict__ work_beta, uint8_t* __restrict__ work_code,
                                                       const PixList L, const float* __restrict__ tgt, float lscale,
                                                       float* __restrict__ part, unsigned* err) {
-  // Grid (x, shard): the blocks of row y walk shard y.
+  // Grid (x, shard): the blocks of row y walk shard y, a warp 32 listed
+  // pixels at a time.  The warp's (pixel, candidate direction) pairs are
+  // searched one per lane (a pixel has one to four, so a lane per pixel
+  // left most lanes idle), into per-warp shared slots; then every lane
+  // blends its own pixel.
+  constexpr int kWarps = 256 / 32;
+  __shared__ unsigned char s_item[kWarps][128];  // source lane | direction << 5
+  __shared__ float s_beta[kWarps][128];          // [source lane * 4 + direction]
+  __shared__ unsigned char s_kk[kWarps][128];    // selected edge + 1, 0 inactive
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned long long n = L.count[blockIdx.y];
   float l = 0.0f;
   const unsigned long long* sl = L.list + (int64_t)blockIdx.y * L.cap;
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
-  for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const unsigned long long e = sl[i];
+  for (unsigned long long wb = (unsigned long long)blockIdx.x * blockDim.x + (unsigned)(warp * 32); wb < n;
+       wb += stride) {
+    const bool has = wb + lane < n;
+    const unsigned long long e = has ? sl[wb + lane] : 0ull;
     const int64_t pix = (int64_t)(e >> 4);
     const unsigned cand = (unsigned)(e & 15u);
+    const int tri_p = has ? rast_tri(rast, pix, T, err) : -1;
+    // The warp's items, in lane order, and this lane's result slots cleared.
+    const int cnt = __popc(cand);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    int k = incl - cnt;
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+      if ((cand >> d) & 1u) s_item[warp][k++] = (unsigned char)(lane | (d << 5));
+      s_beta[warp][lane * 4 + d] = 0.0f;
+      s_kk[warp][lane * 4 + d] = 0;
+    }
+    __syncwarp();
+    for (int r = 0; r < total; r += 32) {
+      const bool act = r + lane < total;
+      const unsigned it = act ? s_item[warp][r + lane] : 0u;
+      const int src = (int)(it & 31u), d = (int)(it >> 5);
+      const int64_t spix = __shfl_sync(0xffffffffu, pix, src);
+      const int stri = __shfl_sync(0xffffffffu, tri_p, src);
+      if (act) {
+        const int pw = (int)(spix % W), ph = (int)((spix / W) % H), pn = (int)(spix / ((int64_t)H * W));
+        Mat4 M;
+        if (XF) M = load_mat4(xform + (int64_t)pn * 16);
+        const SilDir sd = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, stri, d, err);
+        if (sd.active) {
+          s_beta[warp][src * 4 + d] = sd.beta;
+          s_kk[warp][src * 4 + d] = (unsigned char)(sd.kk + 1);
+        }
+      }
+    }
+    __syncwarp();
+    if (!has) continue;
     const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
-    const int tri_p = rast_tri(rast, pix, T, err);
-    Mat4 M;
-    if (XF) M = load_mat4(xform + (int64_t)pn * 16);
-    float beta[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float beta[4];
     unsigned code = 0;
 #pragma unroll
     for (int d = 0; d < 4; ++d) {
-      if (!((cand >> d) & 1u)) continue;
-      const SilDir sd = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, tri_p, d, err);
-      if (!sd.active) continue;
-      beta[d] = sd.beta;
-      code |= (unsigned)(sd.kk + 1) << (2 * d);
+      beta[d] = s_beta[warp][lane * 4 + d];
+      code |= (unsigned)s_kk[warp][lane * 4 + d] << (2 * d);
     }
     if (WORK) {
       work_beta[pix] = make_float4(beta[0], beta[1], beta[2], beta[3]);
@@ -600,28 +642,57 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_edges(
     const float* __restrict__ color, int N, int H, int W, int C, const float4* __restrict__ rast,
     const float* __restrict__ pos, const float* __restrict__ xform, int V, const int32_t* __restrict__ tri, int T,
     const Cot cot, float* __restrict__ d_pos, const PixList L, unsigned* err) {
-  // Grid (x, shard): the blocks of row y walk shard y.
+  // Grid (x, shard): the blocks of row y walk shard y, a warp 32 listed
+  // pixels at a time; their recorded (pixel, direction) edges are replayed
+  // one per lane (a pixel has one to four).
+  constexpr int kWarps = 256 / 32;
+  __shared__ unsigned char s_item[kWarps][128];  // source lane | direction << 5
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float gl = cot_g(cot);
   const unsigned long long n = L.count[blockIdx.y];
   const unsigned long long* sl = L.list + (int64_t)blockIdx.y * L.cap;
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
-  for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const unsigned long long e = sl[i];
+  for (unsigned long long wb = (unsigned long long)blockIdx.x * blockDim.x + (unsigned)(warp * 32); wb < n;
+       wb += stride) {
+    const bool has = wb + lane < n;
+    const unsigned long long e = has ? sl[wb + lane] : 0ull;
     const int64_t pix = (int64_t)(e >> 8);
     const unsigned code = (unsigned)(e & 255u);
-    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
-    const int tri_p = rast_tri(rast, pix, T, err);
-    Mat4 M;
-    if (XF) M = load_mat4(xform + (int64_t)pn * 16);
-#pragma unroll 1
-    for (int d = 0; d < 4; ++d) {
-      const int kk = (int)((code >> (2 * d)) & 3u) - 1;
-      if (kk < 0) continue;
-      const SilDir sd = sil_replay<XF>(rast, pos, M, tri, H, W, V, T, pn, ph, pw, tri_p, d, kk, err);
+    const int tri_p = has ? rast_tri(rast, pix, T, err) : -1;
+    unsigned dirs = 0;
+#pragma unroll
+    for (int d = 0; d < 4; ++d) dirs |= (((code >> (2 * d)) & 3u) != 0u ? 1u : 0u) << d;
+    const int cnt = __popc(dirs);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    int k = incl - cnt;
+#pragma unroll
+    for (int d = 0; d < 4; ++d)
+      if ((dirs >> d) & 1u) s_item[warp][k++] = (unsigned char)(lane | (d << 5));
+    __syncwarp();
+    for (int r = 0; r < total; r += 32) {
+      const bool act = r + lane < total;
+      const unsigned it = act ? s_item[warp][r + lane] : 0u;
+      const int src = (int)(it & 31u), d = (int)(it >> 5);
+      const int64_t spix = __shfl_sync(0xffffffffu, pix, src);
+      const int stri = __shfl_sync(0xffffffffu, tri_p, src);
+      const unsigned scode = __shfl_sync(0xffffffffu, code, src);
+      if (!act) continue;
+      const int pw = (int)(spix % W), ph = (int)((spix / W) % H), pn = (int)(spix / ((int64_t)H * W));
+      const int kk = (int)((scode >> (2 * d)) & 3u) - 1;
+      Mat4 M;
+      if (XF) M = load_mat4(xform + (int64_t)pn * 16);
+      const SilDir sd = sil_replay<XF>(rast, pos, M, tri, H, W, V, T, pn, ph, pw, stri, d, kk, err);
       if (!sd.active) continue;
-      aa_dir_dpos<VEC, XF>(sd, color, C, cot, gl, pix, nbr_pix(pn, ph, pw, d, H, W), pos, M, V, pn, ph, pw, H, W,
+      aa_dir_dpos<VEC, XF>(sd, color, C, cot, gl, spix, nbr_pix(pn, ph, pw, d, H, W), pos, M, V, pn, ph, pw, H, W,
                            d_pos);
     }
+    __syncwarp();
   }
 }
 
