@@ -178,10 +178,15 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         # Vertices are the shared [V, 4] soup (Nv = 1) transformed per view in-kernel.
         add("raster_setup", V * 16 + T * 12)  # both layers share setup and tile lists
         # One tile pass writes both layers (rast + rast_db each); layer 0 is never re-read.
-        add("raster_tiles", 2 * (P * 16 + P * 16))
+        fused = getattr(chain, "fused", False)
+        add("raster_tiles_interp" if fused else "raster_tiles", 2 * (P * 16 + P * 16))
         for layer in (0, 1):
             # Layer 1's interpolation also reads its MSE target (the fused loss).
-            add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A) + (P * 4 * A if layer else 0))
+            # Fused into the tile pass, it reads no rast / rast_db back.
+            if fused:
+                add("raster_tiles_interp", V * A * 4 + T * 12 + P * (4 * A + 8 * A) + (P * 4 * A if layer else 0))
+            else:
+                add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A) + (P * 4 * A if layer else 0))
             # out_da never reaches the loss: the VJP runs without the DA terms.
             # Layer 0 reads d_out; layer 1 forms it from its output and target.
             add("interp_bwd", 2 * V * A * 4 + T * 12 + P * (16 + 16 + 4 * A) + (P * 4 * A if layer else 0))

@@ -216,6 +216,25 @@ DR_API dr_status dr_rasterize_xf_bwd(dr_ctx* ctx, const float* verts, int V,
                               int N, int H, int W, int num_layers,
                               const float* const* rast, const float* const* d_rast,
                               const float* const* d_rast_db, float* d_verts);
+/* Two depth layers of the xf mode with interpolate fused into the pass (no
+ * counterpart in the reference, where rasterize and interpolate are separate
+ * operators): writes, per layer l of 2, rast[l] and rast_db[l] exactly as
+ * dr_rasterize_xf_fwd(num_layers = 2) and out[l] [N, H, W, A] / out_da[l]
+ * [N, H, W, 2A] exactly as dr_interpolate_fwd(attr, rast[l], ..., rast_db[l],
+ * diff_idx = NULL, K = A), computed from each pixel's winner instead of by a
+ * second pass that reads rast back.  attr [attr_batch, V, A] shares verts'
+ * V, with A a multiple of 4 and attr / out / out_da 16-byte aligned.  With
+ * target[l] (and loss[l], both or neither; target may be NULL for no loss at
+ * all) the layer also writes scale * sum((out[l] - target[l])^2) to the
+ * device scalar *loss[l], as dr_interpolate_fwd_mse.  The VJPs are the
+ * separate ones: dr_interpolate_bwd(_mse) per layer, then dr_rasterize_xf_bwd. */
+DR_API dr_status dr_rasterize_xf_interp_fwd(dr_ctx* ctx, const float* verts, int V,
+                                     const float* xform, const int32_t* tri, int T,
+                                     int N, int H, int W, const float* attr,
+                                     int attr_batch, int A, float* const* rast,
+                                     float* const* rast_db, float* const* out,
+                                     float* const* out_da, const float* const* target,
+                                     float scale, float* const* loss);
 
 /* ---- interpolate (Interpolate.swift:43-132) ---------------------------- */
 

@@ -63,26 +63,8 @@ __device__ __forceinline__ void interp_fwd_pixel(const float* __restrict__ attr,
   const float* a1p = an + (int64_t)i1 * A;
   const float* a2p = an + (int64_t)i2 * A;
   if (VEC4 && DA && !IDX) {
-    // .all with A % 4 == 0: out and out_da from the same float4 gathers;
-    // out_da rows are 2A floats, so every store is a float4.  Unrolled by two
-    // so the gathers of consecutive channel groups are in flight together.
-#pragma unroll 2
-    for (int a = 0; a < A; a += 4) {
-      const float4 x0 = ldg4(a0p + a), x1 = ldg4(a1p + a), x2 = ldg4(a2p + a);
-      float4 y;
-      y.x = bw * x0.x + u * x1.x + v * x2.x;
-      y.y = bw * x0.y + u * x1.y + v * x2.y;
-      y.z = bw * x0.z + u * x1.z + v * x2.z;
-      y.w = bw * x0.w + u * x1.w + v * x2.w;
-      stcs4(o + a, y);
-      if (tp) lsum += sq_diff4(y, ldcs4(tp + a));
-      const float4 d01 = make_float4(x1.x - x0.x, x1.y - x0.y, x1.z - x0.z, x1.w - x0.w);
-      const float4 d02 = make_float4(x2.x - x0.x, x2.y - x0.y, x2.z - x0.z, x2.w - x0.w);
-      stcs4(od + 2 * a, make_float4(d01.x * db.x + d02.x * db.z, d01.x * db.y + d02.x * db.w,
-                                    d01.y * db.x + d02.y * db.z, d01.y * db.y + d02.y * db.w));
-      stcs4(od + 2 * a + 4, make_float4(d01.z * db.x + d02.z * db.z, d01.z * db.y + d02.z * db.w,
-                                        d01.w * db.x + d02.w * db.z, d01.w * db.y + d02.w * db.w));
-    }
+    // .all with A % 4 == 0: out and out_da from the same float4 gathers.
+    interp_row4_da(a0p, a1p, a2p, A, bw, u, v, db, o, od, tp, lsum);
     return;
   }
   if (VEC4) {

@@ -26,6 +26,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "interp_common.cuh"
 
 namespace {
 
@@ -330,17 +331,31 @@ __device__ __forceinline__ void fold_two(unsigned long long* k0, unsigned long l
   if (lose != ~0ull && (lose >> 32) > (win >> 32)) atomicMin(k1, lose);
 }
 
+// What write_pixel wrote: the winner (hit, triangle), its (u, v) and rast_db.
+struct PixOut {
+  bool hit;
+  int t;
+  float u, v;
+  float4 db;
+};
+
 // Recompute the winner's (u, v, z) and rast_db bit-identically from its record
 // and write one output pixel (zeros where the key is empty).
 template <bool DB>
-__device__ __forceinline__ void write_pixel(const float4* __restrict__ rec, int64_t rec_view,
-                                            unsigned long long key, float x, float y, int H, int W,
-                                            float4* __restrict__ rast, float4* __restrict__ rast_db, int64_t pix) {
+__device__ __forceinline__ PixOut write_pixel(const float4* __restrict__ rec, int64_t rec_view,
+                                              unsigned long long key, float x, float y, int H, int W,
+                                              float4* __restrict__ rast, float4* __restrict__ rast_db,
+                                              int64_t pix) {
+  PixOut po;
+  po.hit = false;
+  po.t = -1;
+  po.u = po.v = 0.0f;
+  po.db = make_float4(0.f, 0.f, 0.f, 0.f);
   if (key == ~0ull) {
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
     rast[pix] = z4;
     if (DB) rast_db[pix] = z4;
-    return;
+    return po;
   }
   const int t = (int)(unsigned)(key & 0xffffffffull);
   const Rec r = load_rec(rec, rec_view + t);
@@ -353,14 +368,53 @@ __device__ __forceinline__ void write_pixel(const float4* __restrict__ rec, int6
   const float bw = FM(e0, inv_area), u = FM(e1, inv_area), v = FM(e2, inv_area);
   const float z = FA(FA(FM(bw, r.sz0), FM(u, r.sz1)), FM(v, r.sz2));
   rast[pix] = make_float4(u, v, z, (float)(t + 1));
+  po.hit = true;
+  po.t = t;
+  po.u = u;
+  po.v = v;
   if (DB) {
     // Rasterize.swift:586-598
     const float k_x = FD(2.0f, (float)W), k_y = FD(-2.0f, (float)H);
-    rast_db[pix] = make_float4(FM(FM(FS(r.sy2, r.sy0), inv_area), k_x),
-                               FM(FM(FS(r.sx0, r.sx2), inv_area), k_y),
-                               FM(FM(FS(r.sy0, r.sy1), inv_area), k_x),
-                               FM(FM(FS(r.sx1, r.sx0), inv_area), k_y));
+    po.db = make_float4(FM(FM(FS(r.sy2, r.sy0), inv_area), k_x), FM(FM(FS(r.sx0, r.sx2), inv_area), k_y),
+                        FM(FM(FS(r.sy0, r.sy1), inv_area), k_x), FM(FM(FS(r.sx1, r.sx0), inv_area), k_y));
+    rast_db[pix] = po.db;
   }
+  return po;
+}
+
+// Interpolation fused into the two-layer pass (dr_rasterize_xf_interp_fwd):
+// per layer, interpolate's out / out_da (.all, A % 4 == 0) and, with a
+// target, its mean-squared-error loss, computed from the winner the pass
+// has just written instead of by a second kernel that reads rast back.
+struct InterpEpi {
+  const float* attr;  // [attr_batch, V, A]
+  int attr_shared;    // attr_batch == 1
+  int V, A;
+  const int32_t* tri;
+  float* out[2];
+  float* out_da[2];
+  const float* tgt[2];  // or nullptr
+  float lscale[2];
+  float* part[2];  // loss partial sums, or nullptr
+};
+
+__device__ __forceinline__ void epi_pixel(const InterpEpi& e, int l, const PixOut& p, int64_t pix, int n,
+                                          float& lsum, unsigned* err) {
+  float* o = e.out[l] + pix * e.A;
+  float* od = e.out_da[l] + pix * 2 * e.A;
+  const float* tp = e.tgt[l] ? e.tgt[l] + pix * e.A : nullptr;
+  int i0, i1, i2;
+  bool hit = p.hit;
+  if (hit && !tri_verts(e.tri, p.t, e.V, i0, i1, i2)) { dr_flag(err, DR_DEVERR_VERTEX); hit = false; }
+  if (!hit) {
+    interp_row4_da_miss(e.A, o, od, tp, lsum);
+    return;
+  }
+  // The interpolate forward's arithmetic on the rast it would read back.
+  const float bw = 1.0f - p.u - p.v;
+  const float* an = e.attr + (e.attr_shared ? 0 : (int64_t)n * e.V * e.A);
+  interp_row4_da<1>(an + (int64_t)i0 * e.A, an + (int64_t)i1 * e.A, an + (int64_t)i2 * e.A, e.A, bw, p.u, p.v,
+                    p.db, o, od, tp, lsum);
 }
 
 // Conservative column spans of one candidate, per tile row.
@@ -481,15 +535,18 @@ constexpr unsigned short kNoStart = 0xFFFF;
 // a tile whose list runs past it stages every triangle of its view instead,
 // giving those without pixels in the tile no work items.
 // Five resident CTAs per SM: 48 registers (the hot instances do not spill)
-// and about 44 KB of shared memory each.
-template <int MODE, bool DB, bool CAPPED>
-__global__ void __launch_bounds__(TILE_PIX, 5)
+// and about 44 KB of shared memory each; four with the interpolation
+// epilogue, whose gathers need the registers.
+// EPI (two layers with rast_db only): the interpolation epilogue (InterpEpi).
+template <int MODE, bool DB, bool CAPPED, bool EPI = false>
+__global__ void __launch_bounds__(TILE_PIX, EPI ? 4 : 5)
 k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int nty,
                const uint32_t* __restrict__ tile_off, int off_stride,
                const int32_t* __restrict__ list, const float* __restrict__ peel,
                float4* __restrict__ rast, float4* __restrict__ rast_db,
                float4* __restrict__ rast1, float4* __restrict__ rast_db1, unsigned* err,
-               uint32_t cap, unsigned* overflow) {
+               uint32_t cap, unsigned* overflow, const InterpEpi epi) {
+  static_assert(!EPI || (MODE == 2 && DB), "the interpolation epilogue runs on the two-layer pass with rast_db");
   constexpr bool PEEL = MODE == 1, TWO = MODE == 2;
   __shared__ unsigned long long s_k0[TILE_PIX], s_k1[TWO ? TILE_PIX : 1];
   __shared__ float s_peel[PEEL ? TILE_PIX : 1];
@@ -667,13 +724,26 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
     }
   }
   __syncthreads();
-  if (!inside_img) return;
-  const float x = s_ndcx[px - tx0], y = s_ndcy[py - ty0];
-  write_pixel<DB>(rec, rec_view, s_k0[tid], x, y, H, W, rast, rast_db, pix);
-  if (TWO) write_pixel<DB>(rec, rec_view, s_k1[tid], x, y, H, W, rast1, rast_db1, pix);
+  if (!EPI) {
+    if (!inside_img) return;
+    const float x = s_ndcx[px - tx0], y = s_ndcy[py - ty0];
+    write_pixel<DB>(rec, rec_view, s_k0[tid], x, y, H, W, rast, rast_db, pix);
+    if (TWO) write_pixel<DB>(rec, rec_view, s_k1[tid], x, y, H, W, rast1, rast_db1, pix);
+    return;
+  }
+  // Every thread stays for the block sums of the fused losses.
+  float l0 = 0.0f, l1 = 0.0f;
+  if (inside_img) {
+    const float x = s_ndcx[px - tx0], y = s_ndcy[py - ty0];
+    const PixOut p0 = write_pixel<DB>(rec, rec_view, s_k0[tid], x, y, H, W, rast, rast_db, pix);
+    epi_pixel(epi, 0, p0, pix, n, l0, err);
+    const PixOut p1 = write_pixel<DB>(rec, rec_view, s_k1[tid], x, y, H, W, rast1, rast_db1, pix);
+    epi_pixel(epi, 1, p1, pix, n, l1, err);
+  }
+  if (epi.part[0]) block_loss_add(l0, epi.lscale[0], epi.part[0]);
+  if (epi.part[0] && epi.part[1]) __syncthreads();  // block_loss_add's shared slots are reused
+  if (epi.part[1]) block_loss_add(l1, epi.lscale[1], epi.part[1]);
 }
-
-inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 }  // namespace
 
@@ -817,7 +887,8 @@ dr_status raster_prepare(dr_ctx* ctx, const float* pos, const float* xform, int 
 // One depth layer over prepared tile lists (peel: previous layer or NULL), or
 // layers 0 and 1 together when rast1 is given (then peel must be NULL).
 dr_status raster_layer(dr_ctx* ctx, const Prepared& pr, int T, int H, int W, const float* peel_layer,
-                       float* rast, float* rast_db, float* rast1 = nullptr, float* rast_db1 = nullptr) {
+                       float* rast, float* rast_db, float* rast1 = nullptr, float* rast_db1 = nullptr,
+                       const InterpEpi* epi = nullptr) {
   DR_REQUIRE(ctx, rast != nullptr, "rasterize: rast output is required");
   DR_REQUIRE(ctx, aligned16(rast) && (!rast_db || aligned16(rast_db)) && (!peel_layer || aligned16(peel_layer)) &&
                       (!rast1 || aligned16(rast1)) && (!rast_db1 || aligned16(rast_db1)),
@@ -829,16 +900,28 @@ dr_status raster_layer(dr_ctx* ctx, const Prepared& pr, int T, int H, int W, con
   float4* d41 = reinterpret_cast<float4*>(rast_db1);
   const int ntx = pr.ntx, nty = pr.nty;
   DR_TB(ctx);
+  if (epi) {  // two layers with rast_db and the interpolation epilogue
+    if (pr.capped)
+      k_raster_tiles<2, true, true, true><<<grid, TILE_PIX, 0, ctx->stream>>>(
+          pr.rec, T, H, W, ntx, nty, pr.tile_off, pr.off_stride, pr.list, nullptr, r4, d4, r41, d41, ctx->d_err,
+          pr.cap, ctx->d_overflow, *epi);
+    else
+      k_raster_tiles<2, true, false, true><<<grid, TILE_PIX, 0, ctx->stream>>>(
+          pr.rec, T, H, W, ntx, nty, pr.tile_off, pr.off_stride, pr.list, nullptr, r4, d4, r41, d41, ctx->d_err,
+          pr.cap, ctx->d_overflow, *epi);
+    DR_LAUNCHED(ctx, "raster_tiles_interp");
+    return DR_OK;
+  }
 #define DR_RT(MODEV, DBV, PEELP)                                                                               \
   do {                                                                                                         \
     if (pr.capped)                                                                                             \
       k_raster_tiles<MODEV, DBV, true><<<grid, TILE_PIX, 0, ctx->stream>>>(                                    \
           pr.rec, T, H, W, ntx, nty, pr.tile_off, pr.off_stride, pr.list, PEELP, r4, d4, r41, d41, ctx->d_err, \
-          pr.cap, ctx->d_overflow);                                                                            \
+          pr.cap, ctx->d_overflow, InterpEpi{});                                                               \
     else                                                                                                       \
       k_raster_tiles<MODEV, DBV, false><<<grid, TILE_PIX, 0, ctx->stream>>>(                                   \
           pr.rec, T, H, W, ntx, nty, pr.tile_off, pr.off_stride, pr.list, PEELP, r4, d4, r41, d41, ctx->d_err, \
-          pr.cap, ctx->d_overflow);                                                                            \
+          pr.cap, ctx->d_overflow, InterpEpi{});                                                               \
   } while (0)
   if (rast1) {
     if (rast_db) DR_RT(2, true, nullptr); else DR_RT(2, false, nullptr);
@@ -906,4 +989,54 @@ extern "C" dr_status dr_rasterize_xf_fwd(dr_ctx* ctx, const float* verts, int V,
   DR_REQUIRE(ctx, xform != nullptr && ((uintptr_t)xform & 15) == 0,
              "rasterize_xf: xform [N,4,4] must be given and 16-byte aligned");
   return layers_fwd(ctx, verts, xform, V, tri, T, nullptr, N, H, W, num_layers, rast, rast_db);
+}
+
+extern "C" dr_status dr_rasterize_xf_interp_fwd(dr_ctx* ctx, const float* verts, int V, const float* xform,
+                                                const int32_t* tri, int T, int N, int H, int W, const float* attr,
+                                                int attr_batch, int A, float* const* rast, float* const* rast_db,
+                                                float* const* out, float* const* out_da,
+                                                const float* const* target, float scale, float* const* loss) {
+  DR_ENTER(ctx);
+  DR_REQUIRE(ctx, xform != nullptr && ((uintptr_t)xform & 15) == 0,
+             "rasterize_interp: xform [N,4,4] must be given and 16-byte aligned");
+  DR_REQUIRE(ctx, rast && rast_db && out && out_da, "rasterize_interp: rast, rast_db, out and out_da are required");
+  DR_REQUIRE(ctx, attr && aligned16(attr) && A > 0 && A % 4 == 0,
+             "rasterize_interp: attr must be 16-byte aligned with A a multiple of 4 (A=%d)", A);
+  DR_REQUIRE(ctx, attr_batch == 1 || attr_batch == N,
+             "rasterize_interp: attr batch dim %d incompatible with %d views", attr_batch, N);
+  InterpEpi e{};
+  e.attr = attr;
+  e.attr_shared = attr_batch == 1;
+  e.V = V;
+  e.A = A;
+  e.tri = tri;
+  bool any_loss = false;
+  for (int l = 0; l < 2; ++l) {
+    DR_REQUIRE(ctx, rast[l] && rast_db[l] && out[l] && out_da[l], "rasterize_interp: layer %d output missing", l);
+    DR_REQUIRE(ctx, aligned16(out[l]) && aligned16(out_da[l]), "rasterize_interp: out / out_da must be 16-byte aligned");
+    const float* t = target ? target[l] : nullptr;
+    float* lo = loss ? loss[l] : nullptr;
+    DR_REQUIRE(ctx, (t == nullptr) == (lo == nullptr), "rasterize_interp: layer %d: target and loss go together", l);
+    DR_REQUIRE(ctx, !t || aligned16(t), "rasterize_interp: target must be 16-byte aligned");
+    e.out[l] = out[l];
+    e.out_da[l] = out_da[l];
+    e.tgt[l] = t;
+    e.lscale[l] = scale;
+    any_loss = any_loss || t;
+  }
+  Prepared pr;
+  dr_status st = raster_prepare(ctx, verts, xform, V, tri, T, nullptr, N, H, W, pr);
+  if (st != DR_OK) return st;
+  if (any_loss) {
+    // Both layers' partial sums, side by side in the fused-loss slot.
+    float* part = (float*)ws_get(ctx, WS_LOSS, sizeof(float) * 2 * kLossSlots);
+    if (!part) return DR_ENOMEM;
+    DR_CUDA(ctx, cudaMemsetAsync(part, 0, sizeof(float) * 2 * kLossSlots, ctx->stream), "loss memset");
+    for (int l = 0; l < 2; ++l) e.part[l] = e.tgt[l] ? part + l * kLossSlots : nullptr;
+  }
+  st = raster_layer(ctx, pr, T, H, W, nullptr, rast[0], rast_db[0], rast[1], rast_db[1], &e);
+  if (st != DR_OK) return st;
+  for (int l = 0; l < 2; ++l)
+    if (e.part[l] && (st = loss_end(ctx, e.part[l], loss[l])) != DR_OK) return st;
+  return DR_OK;
 }

@@ -25,6 +25,7 @@ from .ops import (  # noqa: F401
     interpolate_mse,
     mse_loss,
     rasterize,
+    rasterize_interpolate_layers,
     rasterize_layers,
     set_tile_order,
     texture,
@@ -36,7 +37,7 @@ from .ops import (  # noqa: F401
 
 __all__ = [
     "BoundaryMode", "DiffAttrs", "FilterMode", "DiffRastError",
-    "rasterize", "rasterize_layers", "interpolate", "texture", "texture_construct_mip", "textureConstructMip",
+    "rasterize", "rasterize_layers", "rasterize_interpolate_layers", "interpolate", "texture", "texture_construct_mip", "textureConstructMip",
     "antialias_construct_topology_hash", "antialiasConstructTopologyHash", "antialias",
     "mse_loss", "antialias_mse", "interpolate_mse", "launch_count", "sync", "workspace_bytes", "set_raster_list_capacity", "raster_overflow",
     "tile_order", "set_tile_order", "tile_order_scope",

@@ -180,8 +180,9 @@ class Cfg4(Chain):
     materialised and every view's gradient lands on the shared [V, 4] buffer."""
 
     def __init__(self, dev, view_lo=0, view_hi=32, total_views=32, res=1024, n_isolated=800_000,
-                 n_strips=20_000, use_tile_order=True):
+                 n_strips=20_000, use_tile_order=True, fused=True):
         self.use_tile_order = use_tile_order
+        self.fused = fused
         s = scenes.scene_cfg4(n_views=total_views, res=res, n_isolated=n_isolated, n_strips=n_strips)
         self.base = _t(s["base"], dev, True)
         self.tri = _t(s["tri"], dev)
@@ -207,17 +208,24 @@ class Cfg4(Chain):
         return torch.einsum("nij,vj->nvi", self.sim, self.base)
 
     def step(self):
-        (rast0, db0), (rast1, db1) = ops.rasterize_layers(self.base, self.tri, self.res, 2, grad_db=True,
-                                                          xform=self.sim)
-        # Interpolate (both layers, forward and VJP) walks the views' tiles
-        # grouped by soup region, so the attribute table and its gradient stay
-        # in L2 while every view passes over a region.
+        if self.fused:
+            # Both layers rasterized with interpolate in the same pass (layer
+            # 1's MSE included); the VJPs are the separate ones.
+            (rast0, _, out0, _, _), (_, _, _, _, loss1) = ops.rasterize_interpolate_layers(
+                self.base, self.tri, self.res, self.attr, self.sim, targets=(None, self.tgt1))
+        else:
+            (rast0, db0), (rast1, db1) = ops.rasterize_layers(self.base, self.tri, self.res, 2, grad_db=True,
+                                                              xform=self.sim)
+        # Interpolate (its VJPs, and the separate forward) walks the views'
+        # tiles grouped by soup region, so the attribute table and its
+        # gradient stay in L2 while every view passes over a region.
         order = ops.tile_order(rast0, self.base, self.tri) if self.use_tile_order else None
         with (ops.tile_order_scope(order, rast0.shape[:3]) if order is not None else contextlib.nullcontext()):
-            out0, _ = ops.interpolate(self.attr, rast0, self.tri, db0, ops.DiffAttrs.all)
-            # Layer 1's interpolation and layer 0's antialias each compute their
-            # MSE term in their own kernels (the *_mse ops).
-            loss1, _, _ = ops.interpolate_mse(self.attr, rast1, self.tri, self.tgt1, db1, ops.DiffAttrs.all)
+            if not self.fused:
+                out0, _ = ops.interpolate(self.attr, rast0, self.tri, db0, ops.DiffAttrs.all)
+                # Layer 1's interpolation and layer 0's antialias each compute
+                # their MSE term in their own kernels (the *_mse ops).
+                loss1, _, _ = ops.interpolate_mse(self.attr, rast1, self.tri, self.tgt1, db1, ops.DiffAttrs.all)
             loss0, _ = ops.antialias_mse(out0, rast0, self.base, self.tri, self.tgt0, self.topo, xform=self.sim)
             loss = loss0 + loss1
             loss.backward()

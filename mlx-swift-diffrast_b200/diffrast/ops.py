@@ -881,6 +881,142 @@ def interpolate_mse(attr: torch.Tensor, rast: torch.Tensor, tri: torch.Tensor, t
     return _InterpolateMSE.apply(attr, rast, rast_db, _i32(tri, "tri"), idx, K, target)
 
 
+# ------------------------------------ rasterize + interpolate, fused forward
+#
+# No counterpart in the reference (rasterize and interpolate are separate
+# operators there).  Two depth layers of the per-view transform mode with
+# interpolate (.all derivatives) run in one pass: the rasterizer interpolates
+# each pixel's winner as it writes it, so rast is not read back by a second
+# kernel.  The outputs equal rasterize_layers(...) followed by interpolate /
+# interpolate_mse on each layer, bit for bit; the VJPs are the same kernels.
+
+class _RasterizeInterpolateLayers(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, verts, attr, xform, tri, H, W, tgt0, tgt1):
+        ctx.set_materialize_grads(False)
+        import ctypes
+        vc = _f32(verts, "verts")
+        xf = _f32(xform, "xform")
+        attr_c = _f32(attr, "attr")
+        a3 = attr_c if attr_c.dim() == 3 else attr_c.unsqueeze(0)
+        N, V, T = xf.shape[0], vc.shape[0], tri.shape[0]
+        Na, Va, A = a3.shape
+        dev = vc.device
+        rasts = [torch.empty((N, H, W, 4), device=dev, dtype=torch.float32) for _ in range(2)]
+        dbs = [torch.empty((N, H, W, 4), device=dev, dtype=torch.float32) for _ in range(2)]
+        outs = [torch.empty((N, H, W, A), device=dev, dtype=torch.float32) for _ in range(2)]
+        odas = [torch.empty((N, H, W, 2 * A), device=dev, dtype=torch.float32) for _ in range(2)]
+        tgts = [_check_target(t, outs[l], "rasterize_interpolate_layers") if t is not None else None
+                for l, t in enumerate((tgt0, tgt1))]
+        losses = [torch.zeros((), device=dev, dtype=torch.float32) for _ in range(2)]
+        scale = 1.0 / max(outs[0].numel(), 1)
+
+        def arr(ts):
+            return ctypes.cast((ctypes.c_void_p * 2)(*[(t.data_ptr() if t is not None else None) for t in ts]),
+                               ctypes.c_void_p)
+        any_t = any(t is not None for t in tgts)
+        c = _ctx(vc)
+        L.check(L.lib().dr_rasterize_xf_interp_fwd(
+            c, _ptr(vc), V, _ptr(xf), _ptr(tri), T, N, H, W, _ptr(a3), Na, A, arr(rasts), arr(dbs), arr(outs),
+            arr(odas), arr(tgts) if any_t else None, scale,
+            arr([losses[l] if tgts[l] is not None else None for l in range(2)]) if any_t else None),
+            c, "rasterize_interpolate_layers")
+        ctx.save_for_backward(vc, xf, tri, a3, *rasts, *dbs, *outs,
+                              *[t if t is not None else torch.empty(0, device=dev) for t in tgts])
+        ctx.meta = (N, V, T, H, W, A, tuple(attr.shape), scale, [t is not None for t in tgts])
+        # A layer's out feeds its fused loss when it has a target; it is then
+        # not differentiable (as interpolate_mse's), and a loss without a
+        # target is a constant zero.
+        for l in range(2):
+            if tgts[l] is not None:
+                ctx.mark_non_differentiable(outs[l])
+            else:
+                ctx.mark_non_differentiable(losses[l])
+        return (rasts[0], dbs[0], outs[0], odas[0], rasts[1], dbs[1], outs[1], odas[1], losses[0], losses[1])
+
+    @staticmethod
+    def backward(ctx, g_r0, g_db0, g_o0, g_oda0, g_r1, g_db1, g_o1, g_oda1, g_l0, g_l1):
+        import ctypes
+        vc, xf, tri, a3, r0, r1, db0, db1, o0, o1, t0, t1 = ctx.saved_tensors
+        N, V, T, H, W, A, attr_shape, scale, has_t = ctx.meta
+        Na = a3.shape[0]
+        rasts, dbs, outs, tgts = (r0, r1), (db0, db1), (o0, o1), (t0, t1)
+        g_r, g_db, g_o, g_oda, g_l = (g_r0, g_r1), (g_db0, g_db1), (g_o0, g_o1), (g_oda0, g_oda1), (g_l0, g_l1)
+        c = _ctx(vc)
+        d_attr = None
+        d_rast, d_db = [None, None], [None, None]
+        for l in range(2):
+            mse = has_t[l] and g_l[l] is not None
+            plain = (not has_t[l]) and g_o[l] is not None
+            K = A if g_oda[l] is not None else 0
+            if not (mse or plain or K):
+                continue
+            da = torch.empty_like(a3)
+            dr_ = torch.empty_like(rasts[l])
+            ddb = torch.empty_like(rasts[l]) if K else None
+            oda = g_oda[l].contiguous().float() if K else None
+            if mse:
+                L.check(L.lib().dr_interpolate_bwd_mse(
+                    c, _ptr(a3), Na, V, A, _ptr(rasts[l]), N, H, W, _ptr(tri), T, _ptr(dbs[l]), None, K,
+                    _ptr(outs[l]), _ptr(tgts[l]), scale, _ptr(g_l[l].contiguous().float()), _ptr(oda), _ptr(da),
+                    _ptr(dr_), _ptr(ddb)), c, "interpolate_bwd_mse")
+            else:
+                d_out = (g_o[l].contiguous().float() if plain
+                         else torch.zeros((N, H, W, A), device=vc.device, dtype=torch.float32))
+                L.check(L.lib().dr_interpolate_bwd(
+                    c, _ptr(a3), Na, V, A, _ptr(rasts[l]), N, H, W, _ptr(tri), T, _ptr(dbs[l]), None, K,
+                    _ptr(d_out), _ptr(oda), _ptr(da), _ptr(dr_), _ptr(ddb)), c, "interpolate_bwd")
+            d_attr = da if d_attr is None else d_attr + da
+            d_rast[l], d_db[l] = dr_, ddb
+        for l in range(2):
+            if g_r[l] is not None:
+                d_rast[l] = g_r[l].float() if d_rast[l] is None else d_rast[l] + g_r[l]
+            if g_db[l] is not None:
+                d_db[l] = g_db[l].float() if d_db[l] is None else d_db[l] + g_db[l]
+            if d_rast[l] is None and d_db[l] is not None:
+                d_rast[l] = torch.zeros_like(rasts[l])
+        d_verts = None
+        if any(g is not None for g in d_rast):
+            d_verts = torch.empty_like(vc)
+            d_rast = [g.contiguous() if g is not None else None for g in d_rast]
+            d_db = [g.contiguous() if g is not None else None for g in d_db]
+
+            def arr(ts):
+                return ctypes.cast((ctypes.c_void_p * 2)(*[(t.data_ptr() if t is not None else None) for t in ts]),
+                                   ctypes.c_void_p)
+            L.check(L.lib().dr_rasterize_xf_bwd(c, _ptr(vc), V, _ptr(xf), _ptr(tri), T, N, H, W, 2, arr(rasts),
+                                                arr(d_rast), arr(d_db), _ptr(d_verts)), c, "rasterize_xf_bwd")
+        return (d_verts, d_attr.reshape(attr_shape) if d_attr is not None else None, None, None, None, None, None,
+                None)
+
+
+def rasterize_interpolate_layers(verts: torch.Tensor, tri: torch.Tensor, resolution, attr: torch.Tensor,
+                                 xform: torch.Tensor, targets=(None, None)):
+    """Two depth layers of the per-view transform mode (verts [V, 4], xform
+    [N, 4, 4]) with interpolate of attr ([V, A] or [N, V, A], A a multiple of
+    4; diffAttrs .all) fused into the rasterizer's pass.  targets: per layer
+    None or an [N, H, W, A] target of a fused mean-squared-error loss.
+    Returns [(rast, rast_db, out, out_da, loss), ...] for layers 0 and 1, the
+    same values as rasterize_layers(verts, tri, resolution, 2, xform=xform)
+    followed by interpolate(attr, rast, tri, rast_db, "all") (or
+    interpolate_mse with the layer's target); a layer's loss is a zero
+    constant when it has no target, and its out is not differentiable when it
+    has one."""
+    if tri.dim() != 2 or tri.shape[1] != 3:
+        raise ValueError(f"rasterize: tri must be [T, 3] (got {tuple(tri.shape)})")
+    if verts.dim() != 2 or verts.shape[1] != 4 or xform.dim() != 3 or tuple(xform.shape[1:]) != (4, 4):
+        raise ValueError("rasterize_interpolate_layers: verts must be [V, 4] and xform [N, 4, 4]")
+    if attr.dim() not in (2, 3) or attr.shape[-2] != verts.shape[0] or attr.shape[-1] % 4 != 0:
+        raise ValueError("rasterize_interpolate_layers: attr must be [V, A] or [N, V, A] with verts' V and A a "
+                         f"multiple of 4 (got {tuple(attr.shape)})")
+    if attr.dim() == 3 and attr.shape[0] not in (1, xform.shape[0]):
+        raise ValueError(f"interpolate: attr batch dim {attr.shape[0]} incompatible with rast batch {xform.shape[0]}")
+    H, W = int(resolution[0]), int(resolution[1])
+    t0, t1 = targets
+    o = _RasterizeInterpolateLayers.apply(verts, attr, xform, _i32(tri, "tri"), H, W, t0, t1)
+    return [(o[0], o[1], o[2], o[3], o[8]), (o[4], o[5], o[6], o[7], o[9])]
+
+
 # Swift-style aliases of the reference's names.
 textureConstructMip = texture_construct_mip
 antialiasConstructTopologyHash = antialias_construct_topology_hash

@@ -92,7 +92,8 @@ def test_algorithmic_bytes_name_launched_kernels():
         "cfg1": NS(info=info(1, 256, 256)),
         "cfg2": NS(info=info(8, 512, 512), pos=z((8, 2562, 4)), tri=z((5120, 3))),
         "cfg3": NS(info=info(16, 1024, 1024), pos=z((16, 2562, 4)), tri=z((5120, 3))),
-        "cfg4": NS(info=info(32, 1024, 1024), base=z((2600000, 4)), tri=z((1000000, 3))),
+        "cfg4": NS(info=info(32, 1024, 1024), base=z((2600000, 4)), tri=z((1000000, 3)), fused=True),
+        "cfg4-separate": NS(info=info(32, 1024, 1024), base=z((2600000, 4)), tri=z((1000000, 3)), fused=False),
         "cfg5": NS(info=info(256, 2048, 2048), verts=z((249642, 4)), tri=z((499280, 3)), micro=16, filter_mode=3),
         "cfg5-linear": NS(info=info(256, 2048, 2048), verts=z((249642, 4)), tri=z((499280, 3)), micro=16,
                           filter_mode=1),
@@ -102,7 +103,8 @@ def test_algorithmic_bytes_name_launched_kernels():
     main = {"cfg1": {"raster_tiles", "interp_fwd", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd"},
             "cfg2": {"tex_linear_fwd", "tex_linear_bwd", "interp_bwd", "aa_bwd"},
             "cfg3": {"tex_mip_fwd", "tex_mip_bwd", "mip_down", "mip_fold", "interp_bwd"},
-            "cfg4": {"raster_tiles", "interp_fwd", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd"},
+            "cfg4": {"raster_tiles_interp", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd"},
+            "cfg4-separate": {"raster_tiles", "interp_fwd", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd"},
             "cfg5": {"tex_cube_mip_fwd", "tex_cube_mip_bwd", "mip_down", "mip_fold", "aa_bwd"},
             "cfg5-linear": {"tex_cube_fwd", "tex_cube_bwd", "aa_bwd"}}
     for name, ch in chains.items():
