@@ -341,9 +341,10 @@ struct PixOut {
 
 // Recompute the winner's (u, v, z) and rast_db bit-identically from its record
 // and write one output pixel (zeros where the key is empty).
+// k_x = 2 / W and k_y = -2 / H (IEEE divisions, computed once per thread).
 template <bool DB>
 __device__ __forceinline__ PixOut write_pixel(const float4* __restrict__ rec, int64_t rec_view,
-                                              unsigned long long key, float x, float y, int H, int W,
+                                              unsigned long long key, float x, float y, float k_x, float k_y,
                                               float4* __restrict__ rast, float4* __restrict__ rast_db,
                                               int64_t pix) {
   PixOut po;
@@ -374,7 +375,6 @@ __device__ __forceinline__ PixOut write_pixel(const float4* __restrict__ rec, in
   po.v = v;
   if (DB) {
     // Rasterize.swift:586-598
-    const float k_x = FD(2.0f, (float)W), k_y = FD(-2.0f, (float)H);
     po.db = make_float4(FM(FM(FS(r.sy2, r.sy0), inv_area), k_x), FM(FM(FS(r.sx0, r.sx2), inv_area), k_y),
                         FM(FM(FS(r.sy0, r.sy1), inv_area), k_x), FM(FM(FS(r.sx1, r.sx0), inv_area), k_y));
     rast_db[pix] = po.db;
@@ -724,20 +724,21 @@ k_raster_tiles(const float4* __restrict__ rec, int T, int H, int W, int ntx, int
     }
   }
   __syncthreads();
+  const float k_x = DB ? FD(2.0f, (float)W) : 0.0f, k_y = DB ? FD(-2.0f, (float)H) : 0.0f;
   if (!EPI) {
     if (!inside_img) return;
     const float x = s_ndcx[px - tx0], y = s_ndcy[py - ty0];
-    write_pixel<DB>(rec, rec_view, s_k0[tid], x, y, H, W, rast, rast_db, pix);
-    if (TWO) write_pixel<DB>(rec, rec_view, s_k1[tid], x, y, H, W, rast1, rast_db1, pix);
+    write_pixel<DB>(rec, rec_view, s_k0[tid], x, y, k_x, k_y, rast, rast_db, pix);
+    if (TWO) write_pixel<DB>(rec, rec_view, s_k1[tid], x, y, k_x, k_y, rast1, rast_db1, pix);
     return;
   }
   // Every thread stays for the block sums of the fused losses.
   float l0 = 0.0f, l1 = 0.0f;
   if (inside_img) {
     const float x = s_ndcx[px - tx0], y = s_ndcy[py - ty0];
-    const PixOut p0 = write_pixel<DB>(rec, rec_view, s_k0[tid], x, y, H, W, rast, rast_db, pix);
+    const PixOut p0 = write_pixel<DB>(rec, rec_view, s_k0[tid], x, y, k_x, k_y, rast, rast_db, pix);
     epi_pixel(epi, 0, p0, pix, n, l0, err);
-    const PixOut p1 = write_pixel<DB>(rec, rec_view, s_k1[tid], x, y, H, W, rast1, rast_db1, pix);
+    const PixOut p1 = write_pixel<DB>(rec, rec_view, s_k1[tid], x, y, k_x, k_y, rast1, rast_db1, pix);
     epi_pixel(epi, 1, p1, pix, n, l1, err);
   }
   if (epi.part[0]) block_loss_add(l0, epi.lscale[0], epi.part[0]);

@@ -350,6 +350,47 @@ public enum DiffRast {
         return layers
     }
 
+    /// Two layers of rasterizeXF with interpolate (.all) fused into the pass:
+    /// per layer rast, rastDB, out [N, H, W, A], outDA [N, H, W, 2A] and, with a
+    /// target, its MSE loss (a device scalar).  The VJPs are interpolateVJP /
+    /// interpolateMSEVJP per layer, then rasterizeXFVJP.
+    public static func rasterizeInterpolateXF(_ ctx: Context, _ alloc: DeviceAllocator, verts: DeviceTensor,
+                                              xform: DeviceTensor, tri: DeviceTensor,
+                                              resolution: (height: Int, width: Int), attr: DeviceTensor,
+                                              targets: [DeviceTensor?] = [nil, nil])
+        -> [(rast: DeviceTensor, rastDB: DeviceTensor, out: DeviceTensor, outDA: DeviceTensor,
+             loss: DeviceTensor?)] {
+        let N = xform.shape[0], V = verts.shape[0], H = resolution.height, W = resolution.width
+        let Na = attr.shape.count == 2 ? 1 : attr.shape[0], A = attr.shape[attr.shape.count - 1]
+        let layers = (0..<2).map { l in
+            (rast: DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * 16), shape: [N, H, W, 4]),
+             rastDB: DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * 16), shape: [N, H, W, 4]),
+             out: DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * A * 4), shape: [N, H, W, A]),
+             outDA: DeviceTensor(pointer: alloc.allocate(bytes: N * H * W * 2 * A * 4), shape: [N, H, W, 2 * A]),
+             loss: targets[l] == nil ? nil : DeviceTensor(pointer: alloc.allocate(bytes: 16), shape: []))
+        }
+        let r: [UnsafeMutablePointer<Float>?] = layers.map { $0.rast.f }
+        let d: [UnsafeMutablePointer<Float>?] = layers.map { $0.rastDB.f }
+        let o: [UnsafeMutablePointer<Float>?] = layers.map { $0.out.f }
+        let od: [UnsafeMutablePointer<Float>?] = layers.map { $0.outDA.f }
+        let t: [UnsafePointer<Float>?] = targets.map { $0.map { UnsafePointer($0.f) } }
+        let lo: [UnsafeMutablePointer<Float>?] = layers.map { $0.loss?.f }
+        let anyTarget = targets.contains { $0 != nil }
+        let st: dr_status = r.withUnsafeBufferPointer { rb in d.withUnsafeBufferPointer { db in
+            o.withUnsafeBufferPointer { ob in od.withUnsafeBufferPointer { odb in
+                t.withUnsafeBufferPointer { tb in lo.withUnsafeBufferPointer { lb in
+                    dr_rasterize_xf_interp_fwd(ctx.raw, verts.f, Int32(V), xform.f, tri.i, Int32(tri.shape[0]),
+                                               Int32(N), Int32(H), Int32(W), attr.f, Int32(Na), Int32(A),
+                                               rb.baseAddress, db.baseAddress, ob.baseAddress, odb.baseAddress,
+                                               anyTarget ? tb.baseAddress : nil, 1.0 / Float(N * H * W * A),
+                                               anyTarget ? lb.baseAddress : nil)
+                } }
+            } }
+        } }
+        ctx.check(st, "rasterizeInterpolateXF")
+        return layers
+    }
+
     /// VJP of rasterizeXF: d_verts [V, 4], summed over views (M_n^T applied).
     public static func rasterizeXFVJP(_ ctx: Context, _ alloc: DeviceAllocator, verts: DeviceTensor,
                                       xform: DeviceTensor, tri: DeviceTensor, rast: [DeviceTensor],
