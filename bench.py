@@ -132,21 +132,20 @@ class ClockSampler:
 # pixels of a run with other view counts.
 P4 = 32 * 1024 * 1024
 NCU_CAPTURE = {
-    "commit": "cf26099",
+    "commit": "d9d362a",
     "command": ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum "
                 "--clock-control none -c 200 --csv python -u bench.py --steps 1 --warmup 3 --no-e2e --no-cpu"),
 }
 NCU_DRAM_BYTES_PER_PIXEL = {
-    ("cfg4", "raster_setup"): 1900341504 / P4,
-    ("cfg4", "raster_scatter"): 1349818624 / P4,
-    ("cfg4", "raster_tiles"): 4061209856 / P4,
-    ("cfg4", "interp_fwd"): 10010063616 / P4,  # two launches
-    ("cfg4", "aa_fwd"): 4542756864 / P4,
-    ("cfg4", "aa_fwd_edges"): 1187073536 / P4,
-    ("cfg4", "aa_bwd"): 4026920704 / P4,
-    ("cfg4", "aa_bwd_edges"): 936102656 / P4,
-    ("cfg4", "interp_bwd"): 6096521984 / P4,  # two launches
-    ("cfg4", "raster_bwd"): 3296983296 / P4,  # two launches
+    ("cfg4", "raster_setup"): 1898293760 / P4,
+    ("cfg4", "raster_scatter"): 1342349568 / P4,
+    ("cfg4", "raster_tiles_interp"): 14772614656 / P4,
+    ("cfg4", "aa_fwd"): 4542198272 / P4,
+    ("cfg4", "aa_fwd_edges"): 1170119680 / P4,
+    ("cfg4", "aa_bwd"): 4024747520 / P4,
+    ("cfg4", "aa_bwd_edges"): 970795520 / P4,
+    ("cfg4", "interp_bwd"): 6113848576 / P4,  # two launches
+    ("cfg4", "raster_bwd"): 3293293312 / P4,  # two launches
 }
 
 
