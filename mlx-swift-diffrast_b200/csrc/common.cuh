@@ -242,6 +242,23 @@ __device__ __forceinline__ float warp_seg_sum(float v, int lane, int seg_end, in
   return v;
 }
 
+// warp_seg_sum of N values at once: one step loop (and one span check per
+// step) for all of them; each value sees the same shuffles and additions in
+// the same order as warp_seg_sum alone.
+template <int N>
+__device__ __forceinline__ void warp_seg_sum_n(float (&v)[N], int lane, int seg_end, int span) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    if (o >= span) break;
+    const bool take = lane + o < seg_end;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const float y = __shfl_down_sync(0xffffffffu, v[i], o);
+      if (take) v[i] += y;
+    }
+  }
+}
+
 // Run structure of a per-lane key in a warp: returns seg_end and whether this
 // lane is the run's head.
 __device__ __forceinline__ int warp_runs(long long key, int lane, bool& head) {

@@ -98,11 +98,15 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
         }
       }
     }
+    {
+      float cv[12] = {c0[0], c0[1], c0[2], c0[3], c1[0], c1[1], c1[2], c1[3], c2[0], c2[1], c2[2], c2[3]};
+      warp_seg_sum_n<12>(cv, lane, seg_end, span);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      c0[j] = warp_seg_sum(c0[j], lane, seg_end, span);
-      c1[j] = warp_seg_sum(c1[j], lane, seg_end, span);
-      c2[j] = warp_seg_sum(c2[j], lane, seg_end, span);
+      for (int j = 0; j < 4; ++j) {
+        c0[j] = cv[j];
+        c1[j] = cv[4 + j];
+        c2[j] = cv[8 + j];
+      }
     }
     if (hit && head) {
       if (VEC4) {

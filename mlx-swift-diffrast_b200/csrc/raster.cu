@@ -157,7 +157,7 @@ __device__ __forceinline__ bool setup_one(const float* __restrict__ pos, const f
   // the record yields an infinite or NaN depth, which is never a fragment, so
   // the record is invalid (the oracle's setup applies the same rule).
   ok = finite3(sx0, sy0, sz0) && finite3(sx1, sy1, sz1) && finite3(sx2, sy2, sz2) &&
-       isfinite(area) && area != 0.0f && isfinite(FD(1.0f, area));
+       isfinite(area) && area != 0.0f && isfinite(__frcp_rn(area));
   x0 = 0; x1 = -1; y0 = 0; y1 = -1;
   if (ok) {
     float minx = fminf(sx0, fminf(sx1, sx2)), maxx = fmaxf(sx0, fmaxf(sx1, sx2));
@@ -360,7 +360,7 @@ __device__ __forceinline__ PixOut write_pixel(const float4* __restrict__ rec, in
   }
   const int t = (int)(unsigned)(key & 0xffffffffull);
   const Rec r = load_rec(rec, rec_view + t);
-  const float inv_area = FD(1.0f, r.area);
+  const float inv_area = __frcp_rn(r.area);  // correctly rounded: the same value as 1.0f / area
   const float dx0 = FS(r.sx0, x), dx1 = FS(r.sx1, x), dx2 = FS(r.sx2, x);
   const float dy0 = FS(r.sy0, y), dy1 = FS(r.sy1, y), dy2 = FS(r.sy2, y);
   const float e0 = FS(FM(dx1, dy2), FM(dx2, dy1));

@@ -127,12 +127,13 @@ __global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const fl
   const long long key = hit ? (long long)pn * T + t : -1ll - (long long)lane;
   const int seg_end = warp_runs(key, lane, head);
   const int span = warp_max_run(lane, seg_end, head);
-  g0.x = warp_seg_sum(g0.x, lane, seg_end, span); g0.y = warp_seg_sum(g0.y, lane, seg_end, span);
-  g0.z = warp_seg_sum(g0.z, lane, seg_end, span); g0.w = warp_seg_sum(g0.w, lane, seg_end, span);
-  g1.x = warp_seg_sum(g1.x, lane, seg_end, span); g1.y = warp_seg_sum(g1.y, lane, seg_end, span);
-  g1.z = warp_seg_sum(g1.z, lane, seg_end, span); g1.w = warp_seg_sum(g1.w, lane, seg_end, span);
-  g2.x = warp_seg_sum(g2.x, lane, seg_end, span); g2.y = warp_seg_sum(g2.y, lane, seg_end, span);
-  g2.z = warp_seg_sum(g2.z, lane, seg_end, span); g2.w = warp_seg_sum(g2.w, lane, seg_end, span);
+  {
+    float gv[12] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w, g2.x, g2.y, g2.z, g2.w};
+    warp_seg_sum_n<12>(gv, lane, seg_end, span);
+    g0 = make_float4(gv[0], gv[1], gv[2], gv[3]);
+    g1 = make_float4(gv[4], gv[5], gv[6], gv[7]);
+    g2 = make_float4(gv[8], gv[9], gv[10], gv[11]);
+  }
   if (!(hit && head)) return;
   if (XF) {
     g0 = mat4_apply_t(M, g0);
