@@ -238,10 +238,11 @@ __device__ __forceinline__ void scatter_tap4(float* p, float4 v, int C, bool on,
     return;
   }
   if (span > 1) {
-    v.x = warp_seg_sum(v.x, lane, seg_end, span);
-    if (C > 1) v.y = warp_seg_sum(v.y, lane, seg_end, span);
-    if (C > 2) v.z = warp_seg_sum(v.z, lane, seg_end, span);
-    if (C > 3) v.w = warp_seg_sum(v.w, lane, seg_end, span);
+    // All four lanes of the float4 in one step loop (channels past C are
+    // zero and never stored).
+    float vv[4] = {v.x, v.y, v.z, v.w};
+    warp_seg_sum_n<4>(vv, lane, seg_end, span);
+    v = make_float4(vv[0], vv[1], vv[2], vv[3]);
   }
   if (on && head) {
     if (smem) {
