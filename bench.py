@@ -132,20 +132,20 @@ class ClockSampler:
 # pixels of a run with other view counts.
 P4 = 32 * 1024 * 1024
 NCU_CAPTURE = {
-    "commit": "d9d362a",
+    "commit": "c46e38a",
     "command": ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum "
                 "--clock-control none -c 200 --csv python -u bench.py --steps 1 --warmup 3 --no-e2e --no-cpu"),
 }
 NCU_DRAM_BYTES_PER_PIXEL = {
-    ("cfg4", "raster_setup"): 1898293760 / P4,
-    ("cfg4", "raster_scatter"): 1342349568 / P4,
-    ("cfg4", "raster_tiles_interp"): 14772614656 / P4,
-    ("cfg4", "aa_fwd"): 4542198272 / P4,
-    ("cfg4", "aa_fwd_edges"): 1170119680 / P4,
-    ("cfg4", "aa_bwd"): 4024747520 / P4,
-    ("cfg4", "aa_bwd_edges"): 970795520 / P4,
-    ("cfg4", "interp_bwd"): 6113848576 / P4,  # two launches
-    ("cfg4", "raster_bwd"): 3293293312 / P4,  # two launches
+    ("cfg4", "raster_setup"): 1897623808 / P4,
+    ("cfg4", "raster_scatter"): 1345582080 / P4,
+    ("cfg4", "raster_tiles_interp"): 14770027008 / P4,
+    ("cfg4", "aa_fwd"): 4542665984 / P4,
+    ("cfg4", "aa_fwd_edges"): 1169305600 / P4,
+    ("cfg4", "aa_bwd"): 4023916800 / P4,
+    ("cfg4", "aa_bwd_edges"): 971402240 / P4,
+    ("cfg4", "interp_bwd"): 6013203200 / P4,  # two launches
+    ("cfg4", "raster_bwd"): 3300966912 / P4,  # two launches
 }
 
 
