@@ -226,8 +226,10 @@ DR_API dr_status dr_rasterize_xf_bwd(dr_ctx* ctx, const float* verts, int V,
  * V, with A a multiple of 4 and attr / out / out_da 16-byte aligned.  With
  * target[l] (and loss[l], both or neither; target may be NULL for no loss at
  * all) the layer also writes scale * sum((out[l] - target[l])^2) to the
- * device scalar *loss[l], as dr_interpolate_fwd_mse.  The VJPs are the
- * separate ones: dr_interpolate_bwd(_mse) per layer, then dr_rasterize_xf_bwd. */
+ * device scalar *loss[l], as dr_interpolate_fwd_mse.  Its VJP is
+ * dr_rasterize_xf_interp_bwd when only out reaches the loss (directly or
+ * through the fused loss); otherwise the separate ones,
+ * dr_interpolate_bwd(_mse) per layer and then dr_rasterize_xf_bwd. */
 DR_API dr_status dr_rasterize_xf_interp_fwd(dr_ctx* ctx, const float* verts, int V,
                                      const float* xform, const int32_t* tri, int T,
                                      int N, int H, int W, const float* attr,
@@ -235,6 +237,26 @@ DR_API dr_status dr_rasterize_xf_interp_fwd(dr_ctx* ctx, const float* verts, int
                                      float* const* rast_db, float* const* out,
                                      float* const* out_da, const float* const* target,
                                      float scale, float* const* loss);
+/* VJP of dr_rasterize_xf_interp_fwd when out_da, rast and rast_db take no
+ * cotangent (no counterpart in the reference): the interpolate VJP and the
+ * rasterize VJP of both layers in one pass, with each pixel's rast cotangent
+ * (d_u, d_v, 0) handed from the one to the other in registers.  The same
+ * values as dr_interpolate_bwd(_mse) per layer (diff_idx = NULL, K = 0)
+ * followed by dr_rasterize_xf_bwd, up to the order of the atomic sums.
+ * Per layer l of 2, out's cotangent is d_out[l] [N, H, W, A], or the fused
+ * loss's, 2 * scale * (out[l] - target[l]) * (*d_loss[l]) (out, target and
+ * d_loss together; not with d_out), or none (the layer adds nothing); any of
+ * the pointer arrays may be NULL.  Writes d_attr [attr_batch, V, A] and
+ * d_verts [V, 4] (both zeroed first).  rast, cotangent rows, attr, d_attr,
+ * verts, xform and d_verts 16-byte aligned; A a multiple of 4. */
+DR_API dr_status dr_rasterize_xf_interp_bwd(dr_ctx* ctx, const float* verts, int V,
+                                     const float* xform, const int32_t* tri, int T,
+                                     int N, int H, int W, const float* attr,
+                                     int attr_batch, int A, const float* const* rast,
+                                     const float* const* d_out, const float* const* out,
+                                     const float* const* target, float scale,
+                                     const float* const* d_loss, float* d_attr,
+                                     float* d_verts);
 
 /* ---- interpolate (Interpolate.swift:43-132) ---------------------------- */
 

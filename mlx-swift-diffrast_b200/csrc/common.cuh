@@ -31,6 +31,9 @@ enum : unsigned {
 #ifndef DR_MINB_AA_BWD
 #define DR_MINB_AA_BWD 5
 #endif
+#ifndef DR_MINB_INTERP_RASTER_BWD
+#define DR_MINB_INTERP_RASTER_BWD 4
+#endif
 // Texture VJPs (scatter-bound: latency of the float atomics) and the mipmap
 // forwards (dependent gathers): four resident CTAs (64 registers) measured
 // faster than three without spills, and than five or six with more spills

@@ -48,6 +48,7 @@ SIGNATURES = {
     "dr_rasterize_xf_fwd": (I, [P, P, I, P, P, I, I, I, I, I, P, P]),
     "dr_rasterize_xf_bwd": (I, [P, P, I, P, P, I, I, I, I, I, P, P, P, P]),
     "dr_rasterize_xf_interp_fwd": (I, [P, P, I, P, P, I, I, I, I, P, I, I, P, P, P, P, P, F, P]),
+    "dr_rasterize_xf_interp_bwd": (I, [P, P, I, P, P, I, I, I, I, P, I, I, P, P, P, P, F, P, P, P]),
     "dr_interpolate_fwd": (I, [P, P, I, I, I, P, I, I, I, P, I, P, P, I, P, P]),
     "dr_interpolate_bwd": (I, [P, P, I, I, I, P, I, I, I, P, I, P, P, I, P, P, P, P, P]),
     "dr_texture_mip_layout": (I, [I, I, I, I, I, ctypes.POINTER(I), ctypes.POINTER(I64),

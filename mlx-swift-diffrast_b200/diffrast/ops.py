@@ -888,7 +888,21 @@ def interpolate_mse(attr: torch.Tensor, rast: torch.Tensor, tri: torch.Tensor, t
 # interpolate (.all derivatives) run in one pass: the rasterizer interpolates
 # each pixel's winner as it writes it, so rast is not read back by a second
 # kernel.  The outputs equal rasterize_layers(...) followed by interpolate /
-# interpolate_mse on each layer, bit for bit; the VJPs are the same kernels.
+# interpolate_mse on each layer, bit for bit.  When only out reaches the loss
+# (directly or through its fused loss), the VJP is one pass for both layers'
+# interpolate and rasterize VJPs (dr_rasterize_xf_interp_bwd); otherwise the
+# separate VJP kernels.
+
+# False runs the separate VJPs in every case (to compare the two).
+FUSED_LAYERS_VJP = True
+
+
+def _ptr_pair(ts):
+    """A C array of two device pointers (NULL for None)."""
+    import ctypes
+    return ctypes.cast((ctypes.c_void_p * 2)(*[(t.data_ptr() if t is not None else None) for t in ts]),
+                       ctypes.c_void_p)
+
 
 class _RasterizeInterpolateLayers(torch.autograd.Function):
     @staticmethod
@@ -943,6 +957,24 @@ class _RasterizeInterpolateLayers(torch.autograd.Function):
         rasts, dbs, outs, tgts = (r0, r1), (db0, db1), (o0, o1), (t0, t1)
         g_r, g_db, g_o, g_oda, g_l = (g_r0, g_r1), (g_db0, g_db1), (g_o0, g_o1), (g_oda0, g_oda1), (g_l0, g_l1)
         c = _ctx(vc)
+        if FUSED_LAYERS_VJP and all(g is None for g in g_r + g_db + g_oda):
+            # Only out reaches the loss (directly or through its fused loss):
+            # both VJPs of both layers in one pass.
+            d_out, o_p, t_p, dl_p = [None, None], [None, None], [None, None], [None, None]
+            for l in range(2):
+                if has_t[l] and g_l[l] is not None:
+                    o_p[l], t_p[l], dl_p[l] = outs[l], tgts[l], g_l[l].contiguous().float()
+                elif not has_t[l] and g_o[l] is not None:
+                    d_out[l] = g_o[l].contiguous().float()
+            if all(x is None for x in d_out + o_p):
+                return (None,) * 8
+            d_attr = torch.empty_like(a3)
+            d_verts = torch.empty_like(vc)
+            L.check(L.lib().dr_rasterize_xf_interp_bwd(
+                c, _ptr(vc), V, _ptr(xf), _ptr(tri), T, N, H, W, _ptr(a3), Na, A, _ptr_pair(rasts),
+                _ptr_pair(d_out), _ptr_pair(o_p), _ptr_pair(t_p), scale, _ptr_pair(dl_p), _ptr(d_attr),
+                _ptr(d_verts)), c, "rasterize_interpolate_layers_bwd")
+            return (d_verts, d_attr.reshape(attr_shape), None, None, None, None, None, None)
         d_attr = None
         d_rast, d_db = [None, None], [None, None]
         for l in range(2):

@@ -76,3 +76,41 @@ def test_fused_rejects_a_channel_count_off_four(soup):
     base, tri, M = soup
     with pytest.raises(ValueError, match="multiple of 4"):
         diffrast.rasterize_interpolate_layers(base, tri, (32, 32), torch.zeros((base.shape[0], 3), device="cuda"), M)
+
+
+@pytest.mark.parametrize("shared", [True, False])
+@pytest.mark.parametrize("use_da", [False, True])
+def test_fused_vjp_matches_separate_vjps(soup, shared, use_da):
+    # The one-pass VJP (only out reaches the loss: a plain cotangent on layer 0,
+    # the fused loss on layer 1) against the separate VJP kernels on the same
+    # forward.  With out_da in the loss both runs take the separate VJPs.
+    import torch
+
+    import diffrast
+    from diffrast import ops
+    base, tri, M = soup
+    res = (100, 72)
+    N, V, A = M.shape[0], base.shape[0], 8
+    g = torch.Generator(device="cuda")
+    g.manual_seed(91)
+    attr = torch.randn(((V, A) if shared else (N, V, A)), generator=g, device="cuda")
+    tg1 = torch.randn((N,) + res + (A,), generator=g, device="cuda")
+    w0 = torch.randn((N,) + res + (A,), generator=g, device="cuda")
+    wd = torch.randn((N,) + res + (2 * A,), generator=g, device="cuda")
+    grads = []
+    for fused_vjp in (True, False):
+        ops.FUSED_LAYERS_VJP = fused_vjp
+        try:
+            b = base.clone().requires_grad_(True)
+            a = attr.clone().requires_grad_(True)
+            l0, l1 = diffrast.rasterize_interpolate_layers(b, tri, res, a, M, targets=(None, tg1))
+            total = (l0[2] * w0).sum() + 0.5 * l1[4]
+            if use_da:
+                total = total + (l0[3] * wd).sum()
+            total.backward()
+        finally:
+            ops.FUSED_LAYERS_VJP = True
+        grads.append((a.grad.cpu().numpy(), b.grad.cpu().numpy()))
+    (ga0, gb0), (ga1, gb1) = grads
+    assert rel_l2(ga0, ga1) < 1e-5 and np.abs(ga1).sum() > 0
+    assert rel_l2(gb0, gb1) < 1e-4 and np.abs(gb1).sum() > 0
