@@ -178,7 +178,13 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
         add("raster_setup", V * 16 + T * 12)  # both layers share setup and tile lists
         # One tile pass writes both layers (rast + rast_db each); layer 0 is never re-read.
         fused = getattr(chain, "fused", False)
+        from diffrast import ops
+        fused_vjp = fused and ops.FUSED_LAYERS_VJP
         add("raster_tiles_interp" if fused else "raster_tiles", 2 * (P * 16 + P * 16))
+        if fused_vjp:
+            # One launch for both layers' VJPs: attr and verts read, d_attr and
+            # d_verts written once; per layer its rast and out's cotangent.
+            add("interp_raster_bwd", 2 * V * A * 4 + 2 * V * 16 + T * 12)
         for layer in (0, 1):
             # Layer 1's interpolation also reads its MSE target (the fused loss).
             # Fused into the tile pass, it reads no rast / rast_db back.
@@ -188,6 +194,10 @@ def algorithmic_bytes(cfg: str, chain) -> dict:
                 add("interp_fwd", V * A * 4 + T * 12 + P * (16 + 16 + 4 * A + 8 * A) + (P * 4 * A if layer else 0))
             # out_da never reaches the loss: the VJP runs without the DA terms.
             # Layer 0 reads d_out; layer 1 forms it from its output and target.
+            if fused_vjp:
+                # rast once; d_rast stays in registers.
+                add("interp_raster_bwd", P * (16 + 4 * A) + (P * 4 * A if layer else 0))
+                continue
             add("interp_bwd", 2 * V * A * 4 + T * 12 + P * (16 + 16 + 4 * A) + (P * 4 * A if layer else 0))
             # rast_db's cotangent is zero (out_da is off the loss path): not read.
             add("raster_bwd", 2 * V * 16 + T * 12 + P * 32)

@@ -352,7 +352,8 @@ public enum DiffRast {
 
     /// Two layers of rasterizeXF with interpolate (.all) fused into the pass:
     /// per layer rast, rastDB, out [N, H, W, A], outDA [N, H, W, 2A] and, with a
-    /// target, its MSE loss (a device scalar).  The VJPs are interpolateVJP /
+    /// target, its MSE loss (a device scalar).  Its VJP is rasterizeInterpolateXFVJP when
+    /// only out reaches the loss; otherwise interpolateVJP /
     /// interpolateMSEVJP per layer, then rasterizeXFVJP.
     public static func rasterizeInterpolateXF(_ ctx: Context, _ alloc: DeviceAllocator, verts: DeviceTensor,
                                               xform: DeviceTensor, tri: DeviceTensor,
@@ -389,6 +390,39 @@ public enum DiffRast {
         } }
         ctx.check(st, "rasterizeInterpolateXF")
         return layers
+    }
+
+    /// VJP of rasterizeInterpolateXF when only out reaches the loss: both
+    /// layers' interpolate and rasterize VJPs in one pass.  Per layer, out's
+    /// cotangent is dOut[l], or the fused loss's (targets[l] with the loss's
+    /// cotangent dLoss[l], a device scalar), or none.  Returns (d_attr, d_verts).
+    public static func rasterizeInterpolateXFVJP(_ ctx: Context, _ alloc: DeviceAllocator, verts: DeviceTensor,
+                                                 xform: DeviceTensor, tri: DeviceTensor, attr: DeviceTensor,
+                                                 rast: [DeviceTensor], out: [DeviceTensor],
+                                                 dOut: [DeviceTensor?] = [nil, nil],
+                                                 targets: [DeviceTensor?] = [nil, nil],
+                                                 dLoss: [DeviceTensor?] = [nil, nil])
+        -> (dAttr: DeviceTensor, dVerts: DeviceTensor) {
+        let N = xform.shape[0], V = verts.shape[0], H = rast[0].shape[1], W = rast[0].shape[2]
+        let Na = attr.shape.count == 2 ? 1 : attr.shape[0], A = attr.shape[attr.shape.count - 1]
+        let dAttr = DeviceTensor(pointer: alloc.allocate(bytes: attr.count * 4), shape: attr.shape)
+        let dVerts = DeviceTensor(pointer: alloc.allocate(bytes: verts.count * 4), shape: verts.shape)
+        let r: [UnsafePointer<Float>?] = rast.map { UnsafePointer($0.f) }
+        let g: [UnsafePointer<Float>?] = dOut.map { $0.map { UnsafePointer($0.f) } }
+        let mse = (0..<2).map { targets[$0] != nil && dLoss[$0] != nil }
+        let o: [UnsafePointer<Float>?] = (0..<2).map { mse[$0] ? UnsafePointer(out[$0].f) : nil }
+        let t: [UnsafePointer<Float>?] = (0..<2).map { mse[$0] ? UnsafePointer(targets[$0]!.f) : nil }
+        let dl: [UnsafePointer<Float>?] = (0..<2).map { mse[$0] ? UnsafePointer(dLoss[$0]!.f) : nil }
+        let st: dr_status = r.withUnsafeBufferPointer { rb in g.withUnsafeBufferPointer { gb in
+            o.withUnsafeBufferPointer { ob in t.withUnsafeBufferPointer { tb in dl.withUnsafeBufferPointer { lb in
+                dr_rasterize_xf_interp_bwd(ctx.raw, verts.f, Int32(V), xform.f, tri.i, Int32(tri.shape[0]),
+                                           Int32(N), Int32(H), Int32(W), attr.f, Int32(Na), Int32(A),
+                                           rb.baseAddress, gb.baseAddress, ob.baseAddress, tb.baseAddress,
+                                           1.0 / Float(N * H * W * A), lb.baseAddress, dAttr.f, dVerts.f)
+            } } }
+        } }
+        ctx.check(st, "rasterizeInterpolateXF VJP")
+        return (dAttr, dVerts)
     }
 
     /// VJP of rasterizeXF: d_verts [V, 4], summed over views (M_n^T applied).
