@@ -103,7 +103,7 @@ def test_algorithmic_bytes_name_launched_kernels():
     main = {"cfg1": {"raster_tiles", "interp_fwd", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd"},
             "cfg2": {"tex_linear_fwd", "tex_linear_bwd", "interp_bwd", "aa_bwd"},
             "cfg3": {"tex_mip_fwd", "tex_mip_bwd", "mip_down", "mip_fold", "interp_bwd"},
-            "cfg4": {"raster_tiles_interp", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd"},
+            "cfg4": {"raster_tiles_interp", "interp_raster_bwd", "aa_fwd", "aa_bwd"},
             "cfg4-separate": {"raster_tiles", "interp_fwd", "interp_bwd", "raster_bwd", "aa_fwd", "aa_bwd"},
             "cfg5": {"tex_cube_mip_fwd", "tex_cube_mip_bwd", "mip_down", "mip_fold", "aa_bwd"},
             "cfg5-linear": {"tex_cube_fwd", "tex_cube_bwd", "aa_bwd"}}
