@@ -114,3 +114,48 @@ def test_fused_vjp_matches_separate_vjps(soup, shared, use_da):
     (ga0, gb0), (ga1, gb1) = grads
     assert rel_l2(ga0, ga1) < 1e-5 and np.abs(ga1).sum() > 0
     assert rel_l2(gb0, gb1) < 1e-4 and np.abs(gb1).sum() > 0
+
+
+def test_fused_vjp_abi_checks(soup):
+    # dr_rasterize_xf_interp_bwd's own argument checks (through the C ABI):
+    # inconsistent cotangents and misaligned or misshaped tables are
+    # DR_EINVAL with a message; no cotangent at all zeroes both outputs.
+    import ctypes
+
+    import torch
+
+    from diffrast import _lib
+    base, tri, M = soup
+    L = _lib.lib()
+    c = _lib.ctx_for(base.device.index or 0)
+    N, V, T, H, W, A = M.shape[0], base.shape[0], tri.shape[0], 16, 24, 8
+    attr = torch.randn((V, A), device="cuda")
+    rast = [torch.zeros((N, H, W, 4), device="cuda") for _ in range(2)]
+    out = [torch.zeros((N, H, W, A), device="cuda") for _ in range(2)]
+    tgt = torch.zeros((N, H, W, A), device="cuda")
+    dl = torch.ones((), device="cuda")
+    d_attr = torch.full((V, A), 7.0, device="cuda")
+    d_verts = torch.full((V, 4), 7.0, device="cuda")
+
+    def pair(a, b):
+        return ctypes.cast((ctypes.c_void_p * 2)(a.data_ptr() if a is not None else None,
+                                                  b.data_ptr() if b is not None else None), ctypes.c_void_p)
+
+    def call(A_=A, attr_=attr, d_out=None, o=None, t=None, d=None):
+        return L.dr_rasterize_xf_interp_bwd(c, base.data_ptr(), V, M.data_ptr(), tri.data_ptr(), T, N, H, W,
+                                            attr_.data_ptr(), 1, A_, pair(*rast), d_out, o, t, 1.0 / out[0].numel(),
+                                            d, d_attr.data_ptr(), d_verts.data_ptr())
+
+    st = call(o=pair(out[0], None), t=pair(None, None), d=pair(dl, None))
+    assert st == _lib.DR_EINVAL and b"go together" in L.dr_last_error(c)
+    st = call(d_out=pair(out[1], None), o=pair(out[0], None), t=pair(tgt, None), d=pair(dl, None))
+    assert st == _lib.DR_EINVAL and b"not both" in L.dr_last_error(c)
+    st = call(A_=6)
+    assert st == _lib.DR_EINVAL and b"multiple of 4" in L.dr_last_error(c)
+    flat = torch.zeros(V * A + 4, device="cuda")
+    st = call(attr_=flat[1:1 + V * A])
+    assert st == _lib.DR_EINVAL and b"16-byte aligned" in L.dr_last_error(c)
+    st = call()
+    torch.cuda.synchronize()
+    assert st == _lib.DR_OK
+    assert float(d_attr.abs().sum()) == 0.0 and float(d_verts.abs().sum()) == 0.0
