@@ -1,8 +1,12 @@
-// raster_bwd.cu — rasterize backward (d_pos), Rasterize.swift:637-812.
+// raster_bwd.cu — rasterize backward (d_pos), Rasterize.swift:637-812, and
+// the one-pass VJP of the fused two-layer raster + interpolate forward
+// (interpolate's VJP, Interpolate.swift:231-417, feeding the rasterize VJP in
+// registers).
 //
-// The gradient is compared with the CPU oracle within a relative L2 tolerance,
-// not bit for bit, so this translation unit is built with FMA contraction (the
-// forward, raster.cu, keeps every operation separately rounded).
+// The gradients are compared with the CPU oracle within a relative L2
+// tolerance, not bit for bit, so this translation unit is built with FMA
+// contraction (the forward, raster.cu, keeps every operation separately
+// rounded).
 #include "interp_common.cuh"
 
 namespace {
