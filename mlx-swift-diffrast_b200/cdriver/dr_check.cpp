@@ -7,6 +7,7 @@
 //   * interpolate: out = (1 - u - v) a0 + u a1 + v a2 recomputed on the host;
 //   * antialias: a constant colour is returned unchanged;
 //   * the VJPs run and leave finite gradients; dr_ctx_sync reports no error;
+//   * the fused two-layer pass's one-pass VJP equals the separate VJPs;
 //   * misuse returns DR_EINVAL with a message instead of crashing.
 // Exit status 0 when every check passes.
 #include <cuda_runtime.h>
@@ -139,6 +140,58 @@ int main() {
   for (int p = 0; p < H * W; ++p) covered += rast[4 * p + 3] > 0.0f;
   CHECK(std::fabs(wsum - (float)covered) <= 1e-3f * covered, "sum of d_attr[:,0] %g != covered pixels %d", wsum,
         covered);
+
+  // The fused two-layer pass (per-view transform mode, identity transform)
+  // and its one-pass VJP against the separate VJP entry points: layer 0's
+  // out takes a cotangent, layer 1 (empty for one triangle) none.
+  {
+    const int A4 = 4;
+    const std::vector<float> attr4 = {1, 0, 0, 2, 0, 1, 0, 3, 0, 0, 1, 4};
+    const std::vector<float> eye = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1};
+    const std::vector<float> z4(N * H * W * 4, 0.0f), zA(N * H * W * A4, 0.0f), zA2(N * H * W * 2 * A4, 0.0f);
+    float* d_attr4 = dev(attr4);
+    float* d_xf = dev(eye);
+    float* r[2] = {dev(z4), dev(z4)};
+    float* db[2] = {dev(z4), dev(z4)};
+    float* o[2] = {dev(zA), dev(zA)};
+    float* od[2] = {dev(zA2), dev(zA2)};
+    OK(dr_rasterize_xf_interp_fwd(ctx, d_posv, V, d_xf, d_tri, T, N, H, W, d_attr4, 1, A4, r, db, o, od, nullptr,
+                                  0.0f, nullptr));
+    std::vector<float> gh(N * H * W * A4);
+    for (size_t k = 0; k < gh.size(); ++k) gh[k] = 0.25f + 0.01f * (float)(k % 7);
+    float* dg = dev(gh);
+    const float* rc[2] = {r[0], r[1]};
+    const float* dout[2] = {dg, nullptr};
+    float* fa = dev(attr4);
+    float* fv = dev(dpos0);
+    OK(dr_rasterize_xf_interp_bwd(ctx, d_posv, V, d_xf, d_tri, T, N, H, W, d_attr4, 1, A4, rc, dout, nullptr,
+                                  nullptr, 0.0f, nullptr, fa, fv));
+    float* sa = dev(attr4);
+    float* sr = dev(z4);
+    float* sv = dev(dpos0);
+    OK(dr_interpolate_bwd(ctx, d_attr4, 1, V, A4, r[0], N, H, W, d_tri, T, nullptr, nullptr, 0, dg, nullptr, sa, sr,
+                          nullptr));
+    const float* drs[2] = {sr, nullptr};
+    OK(dr_rasterize_xf_bwd(ctx, d_posv, V, d_xf, d_tri, T, N, H, W, 2, rc, drs, nullptr, sv));
+    OK(dr_ctx_sync(ctx));
+    const std::vector<float> ha = host(fa, attr4.size()), hsa = host(sa, attr4.size());
+    const std::vector<float> hv = host(fv, dpos0.size()), hsv = host(sv, dpos0.size());
+    float ea = 0.0f, ma = 0.0f, ev = 0.0f, mv = 0.0f;
+    for (size_t k = 0; k < ha.size(); ++k) {
+      ea = std::fmax(ea, std::fabs(ha[k] - hsa[k]));
+      ma = std::fmax(ma, std::fabs(hsa[k]));
+    }
+    for (size_t k = 0; k < hv.size(); ++k) {
+      ev = std::fmax(ev, std::fabs(hv[k] - hsv[k]));
+      mv = std::fmax(mv, std::fabs(hsv[k]));
+    }
+    CHECK(ma > 0.0f && ea <= 1e-5f * ma, "fused VJP d_attr differs by %g (max %g)", ea, ma);
+    CHECK(mv > 0.0f && ev <= 1e-4f * mv, "fused VJP d_verts differs by %g (max %g)", ev, mv);
+    for (void* p : {(void*)d_attr4, (void*)d_xf, (void*)r[0], (void*)r[1], (void*)db[0], (void*)db[1], (void*)o[0],
+                    (void*)o[1], (void*)od[0], (void*)od[1], (void*)dg, (void*)fa, (void*)fv, (void*)sa, (void*)sr,
+                    (void*)sv})
+      cudaFree(p);
+  }
 
   // misuse is a status, not a crash
   const dr_status bad = dr_rasterize_fwd(ctx, nullptr, V, d_tri, T, nullptr, N, H, W, nullptr, d_rast, d_db);
