@@ -341,7 +341,8 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
   if (valid && vec8) { c0 = ldg4(cp); c1 = ldg4(cp + 4); }
   unsigned cand = 0;
   if (valid) {
-    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    int pn, ph, pw;
+    dr::pix_nyx(pix, (int64_t)N * H * W, H, W, pn, ph, pw);
     cand = sil_candidates(rast, topo, H, W, T, pn, ph, pw, rast_tri(rast, pix, T, err), err);
   }
   list_append(L, cand != 0u, ((unsigned long long)pix << 4) | cand);
@@ -376,7 +377,7 @@ __global__ void __launch_bounds__(256) k_aa_fwd_scan(const float* __restrict__ c
 }
 
 template <bool XF, bool WORK>
-__global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ color, int N, int H, int W, int C,
+__global__ void __launch_bounds__(256, 4) k_aa_fwd_edges(const float* __restrict__ color, int N, int H, int W, int C,
                                                       const float4* __restrict__ rast, const float* __restrict__ pos,
                                                       const float* __restrict__ xform, int V,
                                                       const int32_t* __restrict__ tri, int T,
@@ -429,7 +430,8 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
       const int64_t spix = __shfl_sync(0xffffffffu, pix, src);
       const int stri = __shfl_sync(0xffffffffu, tri_p, src);
       if (act) {
-        const int pw = (int)(spix % W), ph = (int)((spix / W) % H), pn = (int)(spix / ((int64_t)H * W));
+        int pn, ph, pw;
+        dr::pix_nyx(spix, (int64_t)N * H * W, H, W, pn, ph, pw);
         Mat4 M;
         if (XF) M = load_mat4(xform + (int64_t)pn * 16);
         const SilDir sd = sil_dir<XF>(rast, pos, M, tri, topo, H, W, V, T, pn, ph, pw, stri, d, err);
@@ -441,7 +443,8 @@ __global__ void __launch_bounds__(256) k_aa_fwd_edges(const float* __restrict__ 
     }
     __syncwarp();
     if (!has) continue;
-    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    int pn, ph, pw;
+    dr::pix_nyx(pix, (int64_t)N * H * W, H, W, pn, ph, pw);
     float beta[4];
     unsigned code = 0;
 #pragma unroll
@@ -593,7 +596,8 @@ __global__ void __launch_bounds__(256, 5) k_aa_bwd_gather(int N, int H, int W, i
                                 ((uintptr_t)d_color)) & 15) == 0;
   unsigned code = 0;
   if (valid) {
-    const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+    int pn, ph, pw;
+    dr::pix_nyx(pix, (int64_t)N * H * W, H, W, pn, ph, pw);
     const float gl = cot_g(cot);
     float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
     if (vec8) {
@@ -683,7 +687,8 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd_edges(
       const int stri = __shfl_sync(0xffffffffu, tri_p, src);
       const unsigned scode = __shfl_sync(0xffffffffu, code, src);
       if (!act) continue;
-      const int pw = (int)(spix % W), ph = (int)((spix / W) % H), pn = (int)(spix / ((int64_t)H * W));
+      int pn, ph, pw;
+      dr::pix_nyx(spix, (int64_t)N * H * W, H, W, pn, ph, pw);
       const int kk = (int)((scode >> (2 * d)) & 3u) - 1;
       Mat4 M;
       if (XF) M = load_mat4(xform + (int64_t)pn * 16);
@@ -709,7 +714,8 @@ __global__ void __launch_bounds__(256, DR_MINB_AA_BWD) k_aa_bwd(const float* __r
   const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (pix >= (int64_t)N * H * W) return;
   const float gl = cot_g(cot);
-  const int pw = (int)(pix % W), ph = (int)((pix / W) % H), pn = (int)(pix / ((int64_t)H * W));
+  int pn, ph, pw;
+  dr::pix_nyx(pix, (int64_t)N * H * W, H, W, pn, ph, pw);
   const int tri_p = rast_tri(rast, pix, T, err);
   Mat4 M;
   if (XF) M = load_mat4(xform + (int64_t)pn * 16);

@@ -146,6 +146,60 @@ __device__ __forceinline__ int64_t pix_of(const PixOrder& o, int64_t P, bool& in
   return ((int64_t)n * o.H + py) * o.W + px;
 }
 
+// View n, row y and column x of pixel pix (0 <= pix < P) of an N x H x W
+// batch of P pixels.  Divides in 32 bits when P allows (P is uniform over a
+// launch, so the branch is too): a 64-bit division is a long instruction
+// sequence, and the per-pixel kernels run it for every pixel.
+__device__ __forceinline__ void pix_nyx(int64_t pix, int64_t P, int H, int W, int& n, int& y, int& x) {
+  if (P <= 0xFFFFFFFFll) {
+    const unsigned p = (unsigned)pix, hw = (unsigned)H * (unsigned)W;
+    const unsigned nn = p / hw, q = p - nn * hw, yy = q / (unsigned)W;
+    n = (int)nn;
+    y = (int)yy;
+    x = (int)(q - yy * (unsigned)W);
+  } else {
+    const int64_t hw = (int64_t)H * W;
+    n = (int)(pix / hw);
+    const int64_t q = pix - (int64_t)n * hw;
+    y = (int)(q / W);
+    x = (int)(q - (int64_t)y * W);
+  }
+}
+
+// The view pix / HW of a pixel, in 32 bits when both fit.
+__device__ __forceinline__ int view_of(int64_t pix, int64_t HW) {
+  return ((unsigned long long)(pix | HW) >> 32) == 0ull ? (int)((unsigned)pix / (unsigned)HW) : (int)(pix / HW);
+}
+
+// pix_of, also giving the pixel's view n, row y and column x of the N x H x W
+// batch (all 0 when !in): the tile order has them already.
+__device__ __forceinline__ int64_t pix_of_nyx(const PixOrder& o, int64_t P, int H, int W, bool& in, int& n, int& y,
+                                              int& x) {
+  n = y = x = 0;
+  if (!o.order) {
+    const int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    in = pix < P;
+    if (in) pix_nyx(pix, P, H, W, n, y, x);
+    return pix;
+  }
+  const int tile = __ldg(o.order + blockIdx.x);
+  if (tile < 0 || (int64_t)tile >= o.n_tiles) {  // not an order from dr_tile_order: touch nothing
+    in = false;
+    return 0;
+  }
+  const int nn = tile / o.ntiles, t = tile - nn * o.ntiles;
+  const int ty = t / o.ntx, tx = t - ty * o.ntx;
+  const int px = tx * kOrderTileW + (int)(threadIdx.x % kOrderTileW);
+  const int py = ty * kOrderTileH + (int)(threadIdx.x / kOrderTileW);
+  in = px < o.W && py < o.H;
+  if (in) {
+    n = nn;
+    y = py;
+    x = px;
+  }
+  return ((int64_t)nn * o.H + py) * o.W + px;
+}
+
 }  // namespace dr
 
 #define DR_ENTER(ctx)                                   \

@@ -57,7 +57,7 @@ __device__ __forceinline__ void interp_fwd_pixel(const float* __restrict__ attr,
   }
   const float u = r.x, v = r.y;
   const float bw = 1.0f - u - v;
-  const int n = (int)(pix / HW);
+  const int n = attr_shared ? 0 : view_of(pix, HW);
   const float* an = attr + (attr_shared ? 0 : (int64_t)n * V * A);
   const float* a0p = an + (int64_t)i0 * A;
   const float* a1p = an + (int64_t)i1 * A;

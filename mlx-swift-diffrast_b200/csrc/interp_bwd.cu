@@ -28,7 +28,7 @@ __global__ void k_interp_bwd(const float* __restrict__ attr, bool attr_shared, i
   bool hit = in && t >= 0;
   if (hit && t >= T) { dr_flag(err, DR_DEVERR_TRI_ID); hit = false; }
   if (hit && !tri_verts(tri, t, V, i0, i1, i2)) { dr_flag(err, DR_DEVERR_VERTEX); hit = false; }
-  const int n = in ? (int)(pix / HW) : 0;
+  const int n = (in && !attr_shared) ? view_of(pix, HW) : 0;
   // Run key: the triangle, and the view when every view has its own attributes.
   const long long key = hit ? ((attr_shared ? 0ll : (long long)n * T) + t) : -1ll - (long long)lane;
   bool head;

@@ -7,6 +7,9 @@
 
 using dr::PixOrder;
 using dr::pix_of;
+using dr::pix_of_nyx;
+using dr::view_of;
+using dr::pix_nyx;
 using dr::pix_order;
 
 namespace {

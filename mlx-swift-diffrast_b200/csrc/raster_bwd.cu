@@ -110,14 +110,13 @@ __global__ void __launch_bounds__(256, DR_MINB_RASTER_BWD) k_raster_bwd(const fl
       hit = false;
     }
   }
-  const int pn = in ? (int)(pix / ((int64_t)H * W)) : 0;
+  int pn = 0, ph = 0, pw = 0;
+  if (in) pix_nyx(pix, P, H, W, pn, ph, pw);
   const int64_t pos_n_base = (shared_pos || XF) ? 0 : (int64_t)pn * V * 4;
   float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0, g2 = g0;
   Mat4 M;
   if (XF && hit) M = load_mat4(xform + (int64_t)pn * 16);
   if (hit) {
-    const int pw = (int)(pix % W);
-    const int ph = (int)((pix / W) % H);
     const float4 g = __ldcs(d_rast + pix);
     const float4 gd = DB ? __ldcs(d_rast_db + pix) : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 q0 = ldg4(pos + pos_n_base + (int64_t)i0 * 4);
@@ -190,7 +189,8 @@ __global__ void __launch_bounds__(256, DR_MINB_INTERP_RASTER_BWD)
   const float4* __restrict__ rast = second ? layers.rast[1] : layers.rast[0];
   const Cot cot = second ? layers.cot[1] : layers.cot[0];
   bool in;
-  const int64_t pix = pix_of(po, P, in);
+  int n, ph, pw;
+  const int64_t pix = pix_of_nyx(po, P, H, W, in, n, ph, pw);
   const int lane = threadIdx.x & 31;
   float4 r = make_float4(0.f, 0.f, 0.f, -1.f);
   if (in) r = __ldcs(rast + pix);
@@ -199,8 +199,6 @@ __global__ void __launch_bounds__(256, DR_MINB_INTERP_RASTER_BWD)
   bool hit = in && t >= 0;
   if (hit && t >= T) { dr_flag(err, DR_DEVERR_TRI_ID); hit = false; }
   if (hit && !tri_verts(tri, t, V, i0, i1, i2)) { dr_flag(err, DR_DEVERR_VERTEX); hit = false; }
-  const int64_t HW = (int64_t)H * W;
-  const int n = in ? (int)(pix / HW) : 0;
   // One run key for both scatters: the (view, triangle), since each view's
   // vertex gradient is mapped through its own transform.
   const long long key = hit ? (long long)n * T + t : -1ll - (long long)lane;
@@ -250,8 +248,6 @@ __global__ void __launch_bounds__(256, DR_MINB_INTERP_RASTER_BWD)
   Mat4 M;
   if (hit) {
     M = load_mat4(xform + (int64_t)n * 16);
-    const int64_t q = pix - (int64_t)n * HW;
-    const int ph = (int)(q / W), pw = (int)(q - (int64_t)ph * W);
     const float4 q0 = mat4_apply(M, ldg4(verts + (int64_t)i0 * 4));
     const float4 q1 = mat4_apply(M, ldg4(verts + (int64_t)i1 * 4));
     const float4 q2 = mat4_apply(M, ldg4(verts + (int64_t)i2 * 4));
