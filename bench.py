@@ -132,19 +132,19 @@ class ClockSampler:
 # pixels of a run with other view counts.
 P4 = 32 * 1024 * 1024
 NCU_CAPTURE = {
-    "commit": "4544c9a",
+    "commit": "66ceb2f",
     "command": ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum "
                 "--clock-control none -c 200 --csv python -u bench.py --steps 1 --warmup 3 --no-e2e --no-cpu"),
 }
 NCU_DRAM_BYTES_PER_PIXEL = {
-    ("cfg4", "raster_setup"): 1898371584 / P4,
-    ("cfg4", "raster_scatter"): 1359161344 / P4,
-    ("cfg4", "raster_tiles_interp"): 14770897664 / P4,
-    ("cfg4", "aa_fwd"): 4542272512 / P4,
-    ("cfg4", "aa_fwd_edges"): 1168429056 / P4,
-    ("cfg4", "aa_bwd"): 4025138944 / P4,
-    ("cfg4", "aa_bwd_edges"): 970782976 / P4,
-    ("cfg4", "interp_raster_bwd"): 5559963136 / P4,  # both layers, one launch
+    ("cfg4", "raster_setup"): 1901652736 / P4,
+    ("cfg4", "raster_scatter"): 1344560640 / P4,
+    ("cfg4", "raster_tiles_interp"): 14772549632 / P4,
+    ("cfg4", "aa_fwd"): 4542650880 / P4,
+    ("cfg4", "aa_fwd_edges"): 1170285312 / P4,
+    ("cfg4", "aa_bwd"): 3962484480 / P4,
+    ("cfg4", "aa_bwd_edges"): 964109056 / P4,
+    ("cfg4", "interp_raster_bwd"): 5654321664 / P4,  # both layers, one launch
 }
 
 
