@@ -22,8 +22,11 @@ enum : unsigned {
 };
 
 // Minimum resident 256-thread blocks per SM requested from the compiler for
-// two register-heavy per-pixel kernels (caps them at 65536 / (256 * n)
-// registers; measured faster than the uncapped build on cfg4).  The other
+// the register-heavy per-pixel kernels (caps them at 65536 / (256 * n)
+// registers): the raster and antialias VJPs at five (faster than the
+// uncapped build on cfg4), the fused raster + interpolate VJP at four (64
+// registers, no spills; at five it spills and measured no faster).  The
+// antialias edge pass is held at four in its own declaration; the other
 // per-pixel kernels measured fastest with no bound.
 #ifndef DR_MINB_RASTER_BWD
 #define DR_MINB_RASTER_BWD 5
